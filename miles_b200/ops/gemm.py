@@ -1,0 +1,203 @@
+"""bf16 GEMMs on the tcgen05 kernel (miles_b200/csrc/gemm_sm100.cu).
+
+`linear(x, w)` computes x @ w.T with an autograd backward that issues the data-grad as a
+(K-major, MN-major) product and the weight-grad as an (MN-major, MN-major) product, so no
+transposed copies are ever materialised. `grouped_linear` is the MoE expert form over tokens
+sorted by expert with 128-row padded segments.
+
+Reference roles replaced: TE linear layers (megatron_utils/model_provider.py:146-183),
+TEGroupedLinear (--moe-grouped-gemm) and fsdp_utils/kernels/fused_experts.py:15-170.
+"""
+from __future__ import annotations
+
+import torch
+
+from miles_b200.ops._lib import err_word, lib, use_native
+
+EPI_STORE_BF16, EPI_STORE_F32, EPI_ACC_BF16, EPI_ACC_F32 = 0, 1, 2, 3
+_NUM_SMS: dict[int, int] = {}
+
+
+def _num_sms(dev: torch.device) -> int:
+    i = dev.index or 0
+    if i not in _NUM_SMS:
+        _NUM_SMS[i] = torch.cuda.get_device_properties(dev).multi_processor_count
+    return _NUM_SMS[i]
+
+
+def _pick_bn(M: int, N: int, dev: torch.device, groups: int = 1) -> int:
+    """Widest N tile that still fills the machine. The N tile width never changes the
+    per-element reduction order, so the choice does not affect results."""
+    mt = (M + 127) // 128 * groups
+    sms = _num_sms(dev)
+    for bn in (256, 128):
+        if mt * ((N + bn - 1) // bn) >= sms:
+            return bn
+    return 64
+
+
+def gemm(a: torch.Tensor, a_mn: bool, b: torch.Tensor, b_mn: bool, out: torch.Tensor,
+         M: int, N: int, K: int, *, mode: int = 0, group_offsets: torch.Tensor | None = None,
+         num_groups: int = 1, b_rows_per_group: int = 0, c_group_stride: int = 0,
+         epi: int = EPI_STORE_BF16, alpha: float = 1.0, bn: int | None = None) -> torch.Tensor:
+    """Raw launcher: out[M,N] (=|+=) alpha * A[M,K] @ B[N,K]^T with stored operand layouts."""
+    if bn is None:
+        bn = _pick_bn(M, N, a.device, num_groups if mode == 2 else 1)
+    lib().gemm(a, a_mn, b, b_mn, out, M, N, K, mode, group_offsets, num_groups,
+               b_rows_per_group, c_group_stride, epi, alpha, bn, err_word(a.device))
+    return out
+
+
+def matmul_nt(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+              out_dtype: torch.dtype = torch.bfloat16, accumulate: bool = False) -> torch.Tensor:
+    """a[M,K] @ b[N,K]^T (both K-major)."""
+    M, K = a.shape
+    N = b.shape[0]
+    if not use_native(a):
+        r = (a.float() @ b.float().t())
+        if out is None:
+            return r.to(out_dtype)
+        if accumulate:
+            out.add_(r.to(out.dtype))
+        else:
+            out.copy_(r)
+        return out
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+    epi = (EPI_STORE_F32 if out.dtype == torch.float32 else EPI_STORE_BF16) | (2 if accumulate else 0)
+    return gemm(a, False, b, False, out, M, N, K, epi=epi)
+
+
+def matmul_nn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """a[M,K] @ b[K,N] (b stored row-major [K,N], i.e. MN-major)."""
+    M, K = a.shape
+    N = b.shape[1]
+    if not use_native(a):
+        r = a.float() @ b.float()
+        return r.to(torch.bfloat16) if out is None else out.copy_(r)
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+    return gemm(a, False, b, True, out, M, N, K)
+
+
+def matmul_tn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+              accumulate: bool = False) -> torch.Tensor:
+    """a[K,M]^T @ b[K,N]: the weight-grad product (both stored with the contraction outermost)."""
+    K, M = a.shape
+    N = b.shape[1]
+    if not use_native(a):
+        r = a.float().t() @ b.float()
+        if out is None:
+            return r.to(torch.bfloat16)
+        if accumulate:
+            out.add_(r.to(out.dtype))
+        else:
+            out.copy_(r)
+        return out
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+    epi = (EPI_STORE_F32 if out.dtype == torch.float32 else EPI_STORE_BF16) | (2 if accumulate else 0)
+    return gemm(a, True, b, True, out, M, N, K, epi=epi)
+
+
+def _accumulate_wgrad(w: torch.Tensor, dy2: torch.Tensor, x2: torch.Tensor) -> torch.Tensor | None:
+    """Weight-grad dW = dy^T x. When the parameter carries a persistent `main_grad` buffer
+    (the trainer's gradient bucket), accumulate into it in place and return None."""
+    main = getattr(w, "main_grad", None)
+    if main is not None:
+        matmul_tn(dy2, x2, out=main, accumulate=True)
+        return None
+    return matmul_tn(dy2, x2)
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w):
+        shp = x.shape
+        y = matmul_nt(x.reshape(-1, shp[-1]), w)
+        # Save the input itself, not a reshaped view of it: saving a view of a grad-requiring
+        # input crashed the CUDA autograd thread in this torch build.
+        ctx.save_for_backward(x, w)
+        return y.view(*shp[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        x2 = x.reshape(-1, x.shape[-1])
+        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = matmul_nn(dy2, w).view(x.shape)
+        if ctx.needs_input_grad[1]:
+            dw = _accumulate_wgrad(w, dy2, x2)
+        return dx, dw
+
+
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """y = x @ w.T  (w: [out, in], bf16)."""
+    if not use_native(x):
+        return torch.nn.functional.linear(x, w)
+    return _Linear.apply(x, w)
+
+
+# ------------------------------------------------------------------------------------------
+# Grouped (MoE) GEMMs
+# ------------------------------------------------------------------------------------------
+def grouped_nt(x: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-expert x_e @ w[e]^T. x: [R, K] sorted by expert with segments padded to 128 rows
+    (offsets: int32 [E+1], device); w: [E, N, K]. Returns [R, N]."""
+    R, K = x.shape
+    E, N, _ = w.shape
+    if out is None:
+        out = torch.empty(R, N, dtype=torch.bfloat16, device=x.device)
+    if not use_native(x):
+        off = offsets.tolist()
+        for e in range(E):
+            a, b = off[e], off[e + 1]
+            if b > a:
+                out[a:b] = (x[a:b].float() @ w[e].float().t()).to(out.dtype)
+        return out
+    return gemm(x, False, w.view(E * N, K), False, out, R, N, K, mode=1, group_offsets=offsets,
+                num_groups=E, b_rows_per_group=N, bn=_pick_bn(R, N, x.device))
+
+
+def grouped_nn(dy: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-expert dy_e @ w[e] (data-grad). dy: [R, N]; w: [E, N, K]. Returns [R, K]."""
+    R, N = dy.shape
+    E, _, K = w.shape
+    if out is None:
+        out = torch.empty(R, K, dtype=torch.bfloat16, device=dy.device)
+    if not use_native(dy):
+        off = offsets.tolist()
+        for e in range(E):
+            a, b = off[e], off[e + 1]
+            if b > a:
+                out[a:b] = (dy[a:b].float() @ w[e].float()).to(out.dtype)
+        return out
+    return gemm(dy, False, w.view(E * N, K), True, out, R, K, N, mode=1, group_offsets=offsets,
+                num_groups=E, b_rows_per_group=N, bn=_pick_bn(R, K, dy.device))
+
+
+def grouped_tn(dy: torch.Tensor, x: torch.Tensor, offsets: torch.Tensor, E: int,
+               out: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    """Per-expert dy_e^T @ x_e (weight-grad). dy: [R, N]; x: [R, K]. Returns [E, N, K]."""
+    R, N = dy.shape
+    K = x.shape[1]
+    if out is None:
+        out = torch.empty(E, N, K, dtype=torch.bfloat16, device=dy.device)
+        accumulate = False
+    if not use_native(dy):
+        off = offsets.tolist()
+        for e in range(E):
+            a, b = off[e], off[e + 1]
+            r = dy[a:b].float().t() @ x[a:b].float()
+            if accumulate:
+                out[e] += r.to(out.dtype)
+            else:
+                out[e] = r.to(out.dtype)
+        return out
+    epi = (EPI_STORE_F32 if out.dtype == torch.float32 else EPI_STORE_BF16) | (2 if accumulate else 0)
+    return gemm(dy, True, x, True, out, N, K, R, mode=2, group_offsets=offsets, num_groups=E,
+                c_group_stride=N * K, epi=epi)
