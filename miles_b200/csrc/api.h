@@ -16,3 +16,78 @@ int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, long long ld
 #ifdef __cplusplus
 }
 #endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+int mb_rmsnorm_fwd(const void* x, const void* res, const void* w, void* h_out, void* y, float* rstd,
+                   int rows, int H, float eps, cudaStream_t st);
+int mb_rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, const void* dres,
+                   void* dx, float* dw_part, int nparts, float* dw_f32, void* dw_bf16, int accumulate,
+                   int rows, int H, cudaStream_t st);
+int mb_qk_norm_rope_fwd(const void* qkv, long long ld_in, const void* qw, const void* kw,
+                        const int* pos, const float* cos_t, const float* sin_t, void* q_out,
+                        void* k_out, void* v_out, const long long* slot, long long ld_kv,
+                        float* rstd, int T, int nq, int nkv, float eps, int use_norm,
+                        cudaStream_t st);
+int mb_qk_norm_rope_bwd(const void* dq, const void* dk, const void* dv, const void* qkv,
+                        long long ld_in, const void* qw, const void* kw, const int* pos,
+                        const float* cos_t, const float* sin_t, const float* rstd, void* dqkv,
+                        float* dw_part, int nparts, float* dw_out, int T, int nq, int nkv,
+                        int use_norm, cudaStream_t st);
+int mb_swiglu_fwd(const void* gu, void* out, long long T, int I, cudaStream_t st);
+int mb_swiglu_bwd(const void* gu, const void* dout, void* dgu, long long T, int I, cudaStream_t st);
+int mb_router_fwd(const float* logits, const float* bias, const int* idx_in, int* idx_out,
+                  float* w_out, int T, int E, int k, int score_fn, int renorm, int n_group,
+                  int topk_group, float scale, cudaStream_t st);
+int mb_router_bwd(const float* logits, const int* idx, const float* dw, void* dlogits, int T, int E,
+                  int k, int score_fn, int renorm, float scale, cudaStream_t st);
+int mb_moe_permute_plan(const int* idx, int n, int E, int align, int* hist, int* chunk_base,
+                        int* counts, int* offsets, int* dest, cudaStream_t st);
+int mb_moe_zero_pad(const int* counts, const int* offsets, void* buf, int E, int H, cudaStream_t st);
+int mb_moe_gather(const void* x, const int* dest, int n, int k, int H, void* xs, cudaStream_t st);
+int mb_moe_gather_bwd(const void* dxs, const int* dest, int T, int k, int H, void* dx,
+                      cudaStream_t st);
+int mb_moe_combine(const void* ys, const int* dest, const float* w, const void* add, int T, int k,
+                   int H, void* y, cudaStream_t st);
+int mb_moe_combine_bwd(const void* dy, const void* ys, const int* dest, const float* w, int T,
+                       int k, int H, void* dys, float* dw, cudaStream_t st);
+int mb_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                const int* cu_seqlens, const int* blk_seq, const int* blk_idx, int nblocks,
+                long long q_stride, long long k_stride, long long v_stride, long long o_stride,
+                int nq, int nkv, int T, float softmax_scale, cudaStream_t st);
+int mb_attn_decode(const void* q, const void* kc, const void* vc, void* o, const int* page_table,
+                   const int* ctx_lens, int B, int max_pages, int nq, int nkv, float softmax_scale,
+                   cudaStream_t st);
+int mb_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                const float* lse, float* delta, void* dq, void* dk, void* dv,
+                const int* cu_seqlens, const int* blk_seq, const int* blk_idx, int nblocks,
+                long long q_stride, long long k_stride, long long v_stride, long long o_stride,
+                long long do_stride, long long dq_stride, long long dk_stride,
+                long long dv_stride, int nq, int nkv, int T, float softmax_scale, cudaStream_t st);
+int mb_logprob_fwd(const float* logits, long long ld, const int* target, int n, int V,
+                   float inv_temp, float* logp, float* ent, float* lse, cudaStream_t st);
+int mb_logprob_bwd(const float* logits, long long ld, const int* target, int n, int V,
+                   float inv_temp, const float* lse, const float* g_lp, const float* g_ent,
+                   const float* ent, void* dlogits, long long ldd, cudaStream_t st);
+int mb_sample(const float* logits, long long ld, int n, int V, const float* inv_temps,
+              const unsigned long long* seeds, const int* positions, int* tokens, float* logp,
+              cudaStream_t st);
+int mb_policy_loss(const float* logp, const float* old_logp, const float* adv, const float* weight,
+                   const float* rollout_logp, const float* ref_logp, float* dlogp, float* pg_out,
+                   float* part, float* metrics, int n, float eps, float eps_hi, float eps_c,
+                   float tis_lo, float tis_hi, float kl_coef, int kl_type, int use_tis,
+                   cudaStream_t st);
+int mb_gae(const float* rewards, const float* values, const int* cu, int B, float gamma, float lam,
+           float* adv, float* ret, cudaStream_t st);
+int mb_grpo_adv(const float* r, int ngroups, int gsize, int norm_std, float eps, float* adv,
+                cudaStream_t st);
+int mb_sqnorm(const void* x, long long n, int is_bf16, float* part, float* out, cudaStream_t st);
+int mb_nonfinite(const void* x, long long n, int is_bf16, float* flag, cudaStream_t st);
+int mb_adam(void* param, float* master, void* m, void* v, const void* grad, long long n,
+            int grad_bf16, int mv_bf16, float lr, float b1, float b2, float eps, float wd, int step,
+            const float* sqnorm, float max_norm, float inv_loss_scale, unsigned long long seed,
+            const float* skip, cudaStream_t st);
+#ifdef __cplusplus
+}
+#endif
