@@ -1,0 +1,175 @@
+"""Mixture-of-experts layer on the sm_100a kernels (csrc/moe.cu + grouped tcgen05 GEMMs).
+
+    logits = x @ Wr^T (fp32)            router_fwd  -> top-k experts / weights (or R3 replay)
+    plan: deterministic expert-sorted order, 128-row padded segments
+    xs = gather(x); gu = xs @ W1[e]^T; a = swiglu(gu); ys = a @ W2[e]^T; y = sum_j w_j ys
+
+The backward mirrors it with grouped data-grad (K, MN-major) and weight-grad (MN, MN-major)
+GEMMs; every reduction is fixed-order, so the layer is bitwise reproducible.
+
+Reference roles replaced: Megatron MoE layer with TEGroupedLinear and alltoall dispatcher,
+router with R3 replay (megatron.patch:514-541), fsdp_utils/kernels/fused_experts.py.
+"""
+from __future__ import annotations
+
+import torch
+
+from miles_b200.ops import gemm as G
+from miles_b200.ops._lib import lib, use_native
+from miles_b200.ops.norm import swiglu_ref
+
+ALIGN = 128
+
+
+class RouterCfg:
+    def __init__(self, num_experts: int, topk: int, score_fn: str = "softmax", renorm: bool = True,
+                 n_group: int = 1, topk_group: int = 1, scale: float = 1.0):
+        self.E = num_experts
+        self.k = topk
+        self.score_fn = 0 if score_fn == "softmax" else 1
+        self.renorm = renorm
+        self.n_group = n_group
+        self.topk_group = topk_group
+        self.scale = scale
+
+
+def route_ref(logits: torch.Tensor, cfg: RouterCfg, bias=None, replay_idx=None):
+    """fp32 reference router: returns (idx int32 [T,k], weights fp32 [T,k])."""
+    if cfg.score_fn == 0:
+        sc = logits.float().softmax(-1)
+        sel = sc
+    else:
+        sc = logits.float().sigmoid()
+        sel = sc + (bias.float() if bias is not None else 0)
+        if cfg.n_group > 1:
+            T = sel.shape[0]
+            g = sel.view(T, cfg.n_group, -1)
+            gs = g.topk(2, -1).values.sum(-1)
+            keep = gs.topk(cfg.topk_group, -1).indices
+            mask = torch.zeros_like(gs, dtype=torch.bool).scatter_(1, keep, True)
+            sel = sel.masked_fill(~mask.repeat_interleave(g.shape[-1], 1), float("-inf"))
+    if replay_idx is not None:
+        idx = replay_idx.long()
+    else:
+        idx = torch.sort(sel, dim=-1, descending=True, stable=True).indices[:, : cfg.k]
+    w = sc.gather(1, idx)
+    if cfg.renorm:
+        w = w / w.sum(-1, keepdim=True)
+    return idx.int(), (w * cfg.scale).float()
+
+
+def moe_ref(x, router_w, w1, w2, cfg: RouterCfg, bias=None, replay_idx=None):
+    """fp32 reference of the whole expert layer."""
+    logits = x.float() @ router_w.float().t()
+    idx, w = route_ref(logits, cfg, bias, replay_idx)
+    T, H = x.shape
+    y = torch.zeros(T, H, dtype=torch.float32, device=x.device)
+    for e in range(cfg.E):
+        tok, slot = (idx == e).nonzero(as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        gu = (x[tok].float() @ w1[e].float().t()).to(torch.bfloat16)
+        a = swiglu_ref(gu)
+        o = (a.float() @ w2[e].float().t()).to(torch.bfloat16)
+        y.index_add_(0, tok, w[tok, slot][:, None] * o.float())
+    return y.to(x.dtype), idx
+
+
+class MoEPlan:
+    """Device-side dispatch plan for one batch: dest rows, padded offsets and counts."""
+
+    def __init__(self, idx: torch.Tensor, E: int):
+        T, k = idx.shape
+        n = T * k
+        dev = idx.device
+        nchunks = max(1, (n + 1023) // 1024)
+        self.E, self.k, self.T = E, k, T
+        self.rows = ((n + E * (ALIGN - 1)) + ALIGN - 1) // ALIGN * ALIGN
+        hist = torch.empty(nchunks * E, dtype=torch.int32, device=dev)
+        base = torch.empty(nchunks * E, dtype=torch.int32, device=dev)
+        self.counts = torch.empty(E, dtype=torch.int32, device=dev)
+        self.offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        self.dest = torch.empty(n, dtype=torch.int32, device=dev)
+        lib().moe_permute_plan(idx.contiguous().view(-1), E, ALIGN, hist, base, self.counts,
+                               self.offsets, self.dest)
+
+    def gather(self, x: torch.Tensor) -> torch.Tensor:
+        xs = torch.empty(self.rows, x.shape[1], dtype=x.dtype, device=x.device)
+        lib().moe_gather(x, self.dest, self.k, xs)
+        lib().moe_zero_pad(self.counts, self.offsets, xs)
+        return xs
+
+
+def _accum_grouped_wgrad(w: torch.Tensor, dy: torch.Tensor, x: torch.Tensor, plan: MoEPlan):
+    main = getattr(w, "main_grad", None)
+    if main is not None:
+        G.grouped_tn(dy, x, plan.offsets, plan.E, out=main, accumulate=True)
+        return None
+    return G.grouped_tn(dy, x, plan.offsets, plan.E)
+
+
+def experts_forward(xs, w1, w2, plan: MoEPlan):
+    gu = G.grouped_nt(xs, w1, plan.offsets)
+    a = torch.empty(gu.shape[0], gu.shape[1] // 2, dtype=gu.dtype, device=gu.device)
+    lib().swiglu_fwd(gu, a)
+    ys = G.grouped_nt(a, w2, plan.offsets)
+    return gu, a, ys
+
+
+class _MoE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, router_w, w1, w2, bias, cfg: RouterCfg, replay_idx, record):
+        T, H = x.shape
+        x = x.contiguous()
+        logits = G.matmul_nt(x, router_w, out_dtype=torch.float32)
+        idx = torch.empty(T, cfg.k, dtype=torch.int32, device=x.device)
+        w = torch.empty(T, cfg.k, dtype=torch.float32, device=x.device)
+        lib().router_fwd(logits, bias, replay_idx, idx, w, cfg.k, cfg.score_fn, cfg.renorm,
+                         cfg.n_group, cfg.topk_group, cfg.scale)
+        if record is not None:
+            record(idx)
+        plan = MoEPlan(idx, cfg.E)
+        xs = plan.gather(x)
+        gu, a, ys = experts_forward(xs, w1, w2, plan)
+        y = torch.empty_like(x)
+        lib().moe_combine(ys, plan.dest, w, None, y)
+        ctx.save_for_backward(x, router_w, w1, w2, logits, idx, w, xs, gu, a, ys)
+        ctx.plan = plan
+        ctx.cfg = cfg
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, router_w, w1, w2, logits, idx, w, xs, gu, a, ys = ctx.saved_tensors
+        plan, cfg = ctx.plan, ctx.cfg
+        dy = dy.contiguous()
+        T, H = x.shape
+        dys = torch.empty_like(ys)
+        dw = torch.empty_like(w)
+        lib().moe_combine_bwd(dy, ys, plan.dest, w, dys, dw)
+        lib().moe_zero_pad(plan.counts, plan.offsets, dys)
+        da = G.grouped_nn(dys, w2, plan.offsets)
+        dw2 = _accum_grouped_wgrad(w2, dys, a, plan)
+        dgu = torch.empty_like(gu)
+        lib().swiglu_bwd(gu, da, dgu)
+        dxs = G.grouped_nn(dgu, w1, plan.offsets)
+        dw1 = _accum_grouped_wgrad(w1, dgu, xs, plan)
+        dx = torch.empty_like(x)
+        lib().moe_gather_bwd(dxs, plan.dest, plan.k, dx)
+        dlogits = torch.empty(T, cfg.E, dtype=torch.bfloat16, device=x.device)
+        lib().router_bwd(logits, idx, dw, dlogits, cfg.score_fn, cfg.renorm, cfg.scale)
+        dx.add_(G.matmul_nn(dlogits, router_w))
+        dwr = G._accumulate_wgrad(router_w, dlogits, x)
+        return dx, dwr, dw1, dw2, None, None, None, None
+
+
+def moe_experts(x, router_w, w1, w2, cfg: RouterCfg, bias=None, replay_idx=None, record=None):
+    """Routed-expert output for x [T,H]. w1 [E, 2I, H] ([gate|up]), w2 [E, H, I].
+    replay_idx: int32 [T,k] replays a recorded routing (R3); record(idx) receives the routing
+    actually used (R3 capture)."""
+    if not use_native(x):
+        y, idx = moe_ref(x, router_w, w1, w2, cfg, bias, replay_idx)
+        if record is not None:
+            record(idx)
+        return y
+    return _MoE.apply(x, router_w, w1, w2, bias, cfg, replay_idx, record)
