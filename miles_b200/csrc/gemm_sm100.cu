@@ -26,6 +26,7 @@
 // fused_moe_triton_backward_kernels.py:10-271).
 #include "common.cuh"
 #include <stdio.h>
+#include <stdlib.h>
 #include <mutex>
 #include <unordered_map>
 
@@ -435,13 +436,18 @@ extern "C" int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, l
                             int bn, int* err, cudaStream_t stream) {
   using namespace mb;
   if (a_mn && !b_mn) return -5;
+  // The driver's tensor-map encoder needs a current context in the calling thread; a thread
+  // that has not made a runtime call yet (e.g. the autograd worker) has none. cudaSetDevice
+  // makes the device's primary context current.
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) return -8;
   CUtensorMap ta, tb;
   const uint32_t a_box_rows = a_mn ? BK : BM;
   const uint32_t b_box_rows = b_mn ? BK : (uint32_t)bn;
-  if (make_map(&ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a_rows, a_cols, lda, 64, a_box_rows))
-    return -1;
-  if (make_map(&tb, b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b_rows, b_cols, ldb, 64, b_box_rows))
-    return -1;
+  int rc = make_map(&ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a_rows, a_cols, lda, 64, a_box_rows);
+  if (rc) return rc;
+  rc = make_map(&tb, b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b_rows, b_cols, ldb, 64, b_box_rows);
+  if (rc) return rc;
   GemmParams p;
   p.M = M; p.N = N; p.K = K;
   p.C = c; p.ldc = ldc; p.c_group_stride = c_group_stride;

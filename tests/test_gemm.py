@@ -96,7 +96,8 @@ def test_grouped():
     dy = torch.zeros(x.shape[0], N, device="cuda", dtype=torch.bfloat16)
     for e, c in enumerate(counts):
         a = off[e]
-        _close(y[a:a + c], x[a:a + c].float() @ w[e].float().t())
+        if c:
+            _close(y[a:a + c], x[a:a + c].float() @ w[e].float().t())
         dy[a:a + c] = torch.randn(c, N, device="cuda", dtype=torch.bfloat16)
     dx = G.grouped_nn(dy, w, offs)
     dw = G.grouped_tn(dy, x, offs, E)
@@ -109,3 +110,20 @@ def test_grouped():
             _close(dw[e], ref)
         else:
             assert dw[e].abs().max().item() == 0
+
+
+def test_worker_thread_and_error_path():
+    """A kernel first used on the main thread also runs from a fresh thread (the autograd
+    worker), and a rejected configuration raises instead of crashing."""
+    import threading
+    a = torch.randn(300, 768, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(768, 512, device="cuda", dtype=torch.bfloat16)
+    ref = G.matmul_nn(a, w)
+    out = {}
+    t = threading.Thread(target=lambda: out.setdefault("y", G.matmul_nn(a, w)))
+    t.start()
+    t.join()
+    assert torch.equal(out["y"], ref)
+    with pytest.raises(RuntimeError):
+        G.gemm(a, False, w, True, torch.empty(300, 512, device="cuda", dtype=torch.bfloat16),
+               300, 512, 768, bn=96)
