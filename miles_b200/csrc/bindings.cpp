@@ -12,14 +12,13 @@
 
 static cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
-static void check_rc(int rc, const char* what) {
-  TORCH_CHECK(rc == 0, what, " failed with code ", rc);
-}
+// Launchers return their C status code to Python (miles_b200/ops/_lib.py raises on non-zero)
+// instead of throwing from C++ once CUDA calls have run.
 
 // ------------------------------------------------------------------ GEMM
 // a: stored 2-D [a_rows, a_cols]; b: stored 2-D [b_rows, b_cols]; c: output buffer (any shape,
 // row stride ldc). See gemm_sm100.cu for the modes.
-void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor c, int64_t M,
+int64_t gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor c, int64_t M,
           int64_t N, int64_t K, int64_t mode, c10::optional<torch::Tensor> group_offsets,
           int64_t num_groups, int64_t b_rows_per_group, int64_t c_group_stride, int64_t epi,
           double alpha, int64_t bn, torch::Tensor err) {
@@ -47,7 +46,7 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
                         (int)K, (int)mode, go, (int)num_groups, (int)b_rows_per_group,
                         c_group_stride, (int)epi, (float)alpha, (int)bn, err.data_ptr<int>(),
                         cur_stream());
-  check_rc(rc, "mb_gemm_bf16");
+  return rc;
 }
 
 
@@ -60,208 +59,185 @@ static void* P(const torch::Tensor& t) { return t.data_ptr(); }
 template <typename T> static T* PT(const OT& t) { return t.has_value() ? (T*)t.value().data_ptr() : nullptr; }
 template <typename T> static T* PT(const torch::Tensor& t) { return (T*)t.data_ptr(); }
 
-void rmsnorm_fwd(torch::Tensor x, OT res, torch::Tensor w, OT h_out, torch::Tensor y, OT rstd,
+int64_t rmsnorm_fwd(torch::Tensor x, OT res, torch::Tensor w, OT h_out, torch::Tensor y, OT rstd,
                  double eps) {
   CHECK_CUDA(x); CHECK_DT(x, at::kBFloat16); TORCH_CHECK(x.is_contiguous());
   const int H = x.size(-1);
   const int rows = x.numel() / H;
-  check_rc(mb_rmsnorm_fwd(P(x), P(res), P(w), P(h_out), P(y), PT<float>(rstd), rows, H, (float)eps,
-                          cur_stream()), "rmsnorm_fwd");
+  return mb_rmsnorm_fwd(P(x), P(res), P(w), P(h_out), P(y), PT<float>(rstd), rows, H, (float)eps,
+                          cur_stream());
 }
 
-void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, OT dres,
+int64_t rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, OT dres,
                  torch::Tensor dx, torch::Tensor dw_part, OT dw_f32, OT dw_bf16, bool accumulate) {
   TORCH_CHECK(dy.is_contiguous() && x.is_contiguous());
   const int H = x.size(-1);
   const int rows = x.numel() / H;
   const int nparts = dw_part.size(0);
-  check_rc(mb_rmsnorm_bwd(P(dy), P(x), P(w), PT<float>(rstd), P(dres), P(dx), PT<float>(dw_part),
-                          nparts, PT<float>(dw_f32), P(dw_bf16), accumulate, rows, H, cur_stream()),
-           "rmsnorm_bwd");
+  return mb_rmsnorm_bwd(P(dy), P(x), P(w), PT<float>(rstd), P(dres), P(dx), PT<float>(dw_part),
+                          nparts, PT<float>(dw_f32), P(dw_bf16), accumulate, rows, H, cur_stream());
 }
 
-void qk_norm_rope_fwd(torch::Tensor qkv, OT qw, OT kw, torch::Tensor pos, torch::Tensor cos_t,
+int64_t qk_norm_rope_fwd(torch::Tensor qkv, OT qw, OT kw, torch::Tensor pos, torch::Tensor cos_t,
                       torch::Tensor sin_t, torch::Tensor q_out, torch::Tensor k_out,
                       torch::Tensor v_out, OT slot, int64_t ld_kv, OT rstd, int64_t nq,
                       int64_t nkv, double eps, bool use_norm) {
   TORCH_CHECK(qkv.stride(-1) == 1);
   const int T = qkv.size(0);
-  check_rc(mb_qk_norm_rope_fwd(P(qkv), qkv.stride(0), P(qw), P(kw), PT<int>(pos),
+  return mb_qk_norm_rope_fwd(P(qkv), qkv.stride(0), P(qw), P(kw), PT<int>(pos),
                                PT<float>(cos_t), PT<float>(sin_t), P(q_out), P(k_out), P(v_out),
                                PT<long long>(slot), ld_kv, PT<float>(rstd), T, nq, nkv,
-                               (float)eps, use_norm, cur_stream()),
-           "qk_norm_rope_fwd");
+                               (float)eps, use_norm, cur_stream());
 }
 
-void qk_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv,
+int64_t qk_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv,
                       OT qw, OT kw, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t,
                       OT rstd, torch::Tensor dqkv, torch::Tensor dw_part, torch::Tensor dw_out,
                       int64_t nq, int64_t nkv, bool use_norm) {
   TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous());
   const int T = qkv.size(0);
-  check_rc(mb_qk_norm_rope_bwd(P(dq), P(dk), P(dv), P(qkv), qkv.stride(0), P(qw), P(kw),
+  return mb_qk_norm_rope_bwd(P(dq), P(dk), P(dv), P(qkv), qkv.stride(0), P(qw), P(kw),
                                PT<int>(pos), PT<float>(cos_t), PT<float>(sin_t), PT<float>(rstd),
                                P(dqkv), PT<float>(dw_part), dw_part.size(0), PT<float>(dw_out), T,
-                               nq, nkv, use_norm, cur_stream()),
-           "qk_norm_rope_bwd");
+                               nq, nkv, use_norm, cur_stream());
 }
 
-void swiglu_fwd(torch::Tensor gu, torch::Tensor out) {
+int64_t swiglu_fwd(torch::Tensor gu, torch::Tensor out) {
   TORCH_CHECK(gu.is_contiguous() && out.is_contiguous());
   const int I = out.size(-1);
-  check_rc(mb_swiglu_fwd(P(gu), P(out), out.numel() / I, I, cur_stream()), "swiglu_fwd");
+  return mb_swiglu_fwd(P(gu), P(out), out.numel() / I, I, cur_stream());
 }
-void swiglu_bwd(torch::Tensor gu, torch::Tensor dout, torch::Tensor dgu) {
+int64_t swiglu_bwd(torch::Tensor gu, torch::Tensor dout, torch::Tensor dgu) {
   TORCH_CHECK(gu.is_contiguous() && dout.is_contiguous() && dgu.is_contiguous());
   const int I = dout.size(-1);
-  check_rc(mb_swiglu_bwd(P(gu), P(dout), P(dgu), dout.numel() / I, I, cur_stream()), "swiglu_bwd");
+  return mb_swiglu_bwd(P(gu), P(dout), P(dgu), dout.numel() / I, I, cur_stream());
 }
 
-void router_fwd(torch::Tensor logits, OT bias, OT idx_in, torch::Tensor idx_out,
+int64_t router_fwd(torch::Tensor logits, OT bias, OT idx_in, torch::Tensor idx_out,
                 torch::Tensor w_out, int64_t k, int64_t score_fn, bool renorm, int64_t n_group,
                 int64_t topk_group, double scale) {
   CHECK_DT(logits, at::kFloat); TORCH_CHECK(logits.is_contiguous());
-  check_rc(mb_router_fwd(PT<float>(logits), PT<float>(bias), PT<int>(idx_in), PT<int>(idx_out),
+  return mb_router_fwd(PT<float>(logits), PT<float>(bias), PT<int>(idx_in), PT<int>(idx_out),
                          PT<float>(w_out), logits.size(0), logits.size(1), k, score_fn, renorm,
-                         n_group, topk_group, (float)scale, cur_stream()),
-           "router_fwd");
+                         n_group, topk_group, (float)scale, cur_stream());
 }
-void router_bwd(torch::Tensor logits, torch::Tensor idx, torch::Tensor dw, torch::Tensor dlogits,
+int64_t router_bwd(torch::Tensor logits, torch::Tensor idx, torch::Tensor dw, torch::Tensor dlogits,
                 int64_t score_fn, bool renorm, double scale) {
-  check_rc(mb_router_bwd(PT<float>(logits), PT<int>(idx), PT<float>(dw), P(dlogits),
+  return mb_router_bwd(PT<float>(logits), PT<int>(idx), PT<float>(dw), P(dlogits),
                          logits.size(0), logits.size(1), idx.size(1), score_fn, renorm,
-                         (float)scale, cur_stream()),
-           "router_bwd");
+                         (float)scale, cur_stream());
 }
-void moe_permute_plan(torch::Tensor idx, int64_t E, int64_t align, torch::Tensor hist,
+int64_t moe_permute_plan(torch::Tensor idx, int64_t E, int64_t align, torch::Tensor hist,
                       torch::Tensor chunk_base, torch::Tensor counts, torch::Tensor offsets,
                       torch::Tensor dest) {
   CHECK_DT(idx, at::kInt);
-  check_rc(mb_moe_permute_plan(PT<int>(idx), idx.numel(), E, align, PT<int>(hist),
+  return mb_moe_permute_plan(PT<int>(idx), idx.numel(), E, align, PT<int>(hist),
                                PT<int>(chunk_base), PT<int>(counts), PT<int>(offsets),
-                               PT<int>(dest), cur_stream()),
-           "moe_permute_plan");
+                               PT<int>(dest), cur_stream());
 }
-void moe_zero_pad(torch::Tensor counts, torch::Tensor offsets, torch::Tensor buf) {
-  check_rc(mb_moe_zero_pad(PT<int>(counts), PT<int>(offsets), P(buf), counts.size(0), buf.size(1),
-                           cur_stream()),
-           "moe_zero_pad");
+int64_t moe_zero_pad(torch::Tensor counts, torch::Tensor offsets, torch::Tensor buf) {
+  return mb_moe_zero_pad(PT<int>(counts), PT<int>(offsets), P(buf), counts.size(0), buf.size(1),
+                           cur_stream());
 }
-void moe_gather(torch::Tensor x, torch::Tensor dest, int64_t k, torch::Tensor xs) {
-  check_rc(mb_moe_gather(P(x), PT<int>(dest), dest.numel(), k, x.size(1), P(xs), cur_stream()),
-           "moe_gather");
+int64_t moe_gather(torch::Tensor x, torch::Tensor dest, int64_t k, torch::Tensor xs) {
+  return mb_moe_gather(P(x), PT<int>(dest), dest.numel(), k, x.size(1), P(xs), cur_stream());
 }
-void moe_gather_bwd(torch::Tensor dxs, torch::Tensor dest, int64_t k, torch::Tensor dx) {
-  check_rc(mb_moe_gather_bwd(P(dxs), PT<int>(dest), dx.size(0), k, dx.size(1), P(dx), cur_stream()),
-           "moe_gather_bwd");
+int64_t moe_gather_bwd(torch::Tensor dxs, torch::Tensor dest, int64_t k, torch::Tensor dx) {
+  return mb_moe_gather_bwd(P(dxs), PT<int>(dest), dx.size(0), k, dx.size(1), P(dx), cur_stream());
 }
-void moe_combine(torch::Tensor ys, torch::Tensor dest, torch::Tensor w, OT add, torch::Tensor y) {
-  check_rc(mb_moe_combine(P(ys), PT<int>(dest), PT<float>(w), P(add), y.size(0), w.size(1),
-                          y.size(1), P(y), cur_stream()),
-           "moe_combine");
+int64_t moe_combine(torch::Tensor ys, torch::Tensor dest, torch::Tensor w, OT add, torch::Tensor y) {
+  return mb_moe_combine(P(ys), PT<int>(dest), PT<float>(w), P(add), y.size(0), w.size(1),
+                          y.size(1), P(y), cur_stream());
 }
-void moe_combine_bwd(torch::Tensor dy, torch::Tensor ys, torch::Tensor dest, torch::Tensor w,
+int64_t moe_combine_bwd(torch::Tensor dy, torch::Tensor ys, torch::Tensor dest, torch::Tensor w,
                      torch::Tensor dys, torch::Tensor dw) {
-  check_rc(mb_moe_combine_bwd(P(dy), P(ys), PT<int>(dest), PT<float>(w), dy.size(0), w.size(1),
-                              dy.size(1), P(dys), PT<float>(dw), cur_stream()),
-           "moe_combine_bwd");
+  return mb_moe_combine_bwd(P(dy), P(ys), PT<int>(dest), PT<float>(w), dy.size(0), w.size(1),
+                              dy.size(1), P(dys), PT<float>(dw), cur_stream());
 }
 
-void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, OT lse,
+int64_t attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, OT lse,
               torch::Tensor cu, torch::Tensor blk_seq, torch::Tensor blk_idx, int64_t nq,
               int64_t nkv, double scale) {
   TORCH_CHECK(q.stride(-1) == 1 && k.stride(-1) == 1 && v.stride(-1) == 1 && o.stride(-1) == 1);
-  check_rc(mb_attn_fwd(P(q), P(k), P(v), P(o), PT<float>(lse), PT<int>(cu), PT<int>(blk_seq),
+  return mb_attn_fwd(P(q), P(k), P(v), P(o), PT<float>(lse), PT<int>(cu), PT<int>(blk_seq),
                        PT<int>(blk_idx), blk_seq.numel(), q.stride(0), k.stride(0), v.stride(0),
-                       o.stride(0), nq, nkv, q.size(0), (float)scale, cur_stream()),
-           "attn_fwd");
+                       o.stride(0), nq, nkv, q.size(0), (float)scale, cur_stream());
 }
-void attn_decode(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor o,
+int64_t attn_decode(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor o,
                  torch::Tensor page_table, torch::Tensor ctx_lens, int64_t nq, int64_t nkv,
                  double scale) {
-  check_rc(mb_attn_decode(P(q), P(kc), P(vc), P(o), PT<int>(page_table), PT<int>(ctx_lens),
-                          q.size(0), page_table.size(1), nq, nkv, (float)scale, cur_stream()),
-           "attn_decode");
+  return mb_attn_decode(P(q), P(kc), P(vc), P(o), PT<int>(page_table), PT<int>(ctx_lens),
+                          q.size(0), page_table.size(1), nq, nkv, (float)scale, cur_stream());
 }
-void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
+int64_t attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
               torch::Tensor dout, torch::Tensor lse, torch::Tensor delta, torch::Tensor dq,
               torch::Tensor dk, torch::Tensor dv, torch::Tensor cu, torch::Tensor blk_seq,
               torch::Tensor blk_idx, int64_t nq, int64_t nkv, double scale) {
-  check_rc(mb_attn_bwd(P(q), P(k), P(v), P(o), P(dout), PT<float>(lse), PT<float>(delta), P(dq),
+  return mb_attn_bwd(P(q), P(k), P(v), P(o), P(dout), PT<float>(lse), PT<float>(delta), P(dq),
                        P(dk), P(dv), PT<int>(cu), PT<int>(blk_seq), PT<int>(blk_idx),
                        blk_seq.numel(), q.stride(0), k.stride(0), v.stride(0), o.stride(0),
                        dout.stride(0), dq.stride(0), dk.stride(0), dv.stride(0), nq, nkv,
-                       q.size(0), (float)scale, cur_stream()),
-           "attn_bwd");
+                       q.size(0), (float)scale, cur_stream());
 }
 
-void logprob_fwd(torch::Tensor logits, torch::Tensor target, double inv_temp, OT logp, OT ent,
+int64_t logprob_fwd(torch::Tensor logits, torch::Tensor target, double inv_temp, OT logp, OT ent,
                  OT lse) {
   CHECK_DT(logits, at::kFloat); TORCH_CHECK(logits.stride(-1) == 1);
-  check_rc(mb_logprob_fwd(PT<float>(logits), logits.stride(0), PT<int>(target), logits.size(0),
+  return mb_logprob_fwd(PT<float>(logits), logits.stride(0), PT<int>(target), logits.size(0),
                           logits.size(1), (float)inv_temp, PT<float>(logp), PT<float>(ent),
-                          PT<float>(lse), cur_stream()),
-           "logprob_fwd");
+                          PT<float>(lse), cur_stream());
 }
-void logprob_bwd(torch::Tensor logits, torch::Tensor target, double inv_temp, torch::Tensor lse,
+int64_t logprob_bwd(torch::Tensor logits, torch::Tensor target, double inv_temp, torch::Tensor lse,
                  OT g_lp, OT g_ent, OT ent, torch::Tensor dlogits) {
-  check_rc(mb_logprob_bwd(PT<float>(logits), logits.stride(0), PT<int>(target), logits.size(0),
+  return mb_logprob_bwd(PT<float>(logits), logits.stride(0), PT<int>(target), logits.size(0),
                           logits.size(1), (float)inv_temp, PT<float>(lse), PT<float>(g_lp),
                           PT<float>(g_ent), PT<float>(ent), P(dlogits), dlogits.stride(0),
-                          cur_stream()),
-           "logprob_bwd");
+                          cur_stream());
 }
-void sample(torch::Tensor logits, torch::Tensor inv_temps, torch::Tensor seeds,
+int64_t sample(torch::Tensor logits, torch::Tensor inv_temps, torch::Tensor seeds,
             torch::Tensor positions, torch::Tensor tokens, OT logp) {
   CHECK_DT(logits, at::kFloat);
-  check_rc(mb_sample(PT<float>(logits), logits.stride(0), logits.size(0), logits.size(1),
+  return mb_sample(PT<float>(logits), logits.stride(0), logits.size(0), logits.size(1),
                      PT<float>(inv_temps), PT<unsigned long long>(seeds), PT<int>(positions),
-                     PT<int>(tokens), PT<float>(logp), cur_stream()),
-           "sample");
+                     PT<int>(tokens), PT<float>(logp), cur_stream());
 }
-void policy_loss(torch::Tensor logp, torch::Tensor old_logp, torch::Tensor adv,
+int64_t policy_loss(torch::Tensor logp, torch::Tensor old_logp, torch::Tensor adv,
                  torch::Tensor weight, OT rollout_logp, OT ref_logp, torch::Tensor dlogp,
                  OT pg_out, torch::Tensor part, torch::Tensor metrics, double eps, double eps_hi,
                  double eps_c, double tis_lo, double tis_hi, double kl_coef, int64_t kl_type,
                  bool use_tis) {
-  check_rc(mb_policy_loss(PT<float>(logp), PT<float>(old_logp), PT<float>(adv), PT<float>(weight),
+  return mb_policy_loss(PT<float>(logp), PT<float>(old_logp), PT<float>(adv), PT<float>(weight),
                           PT<float>(rollout_logp), PT<float>(ref_logp), PT<float>(dlogp),
                           PT<float>(pg_out), PT<float>(part), PT<float>(metrics), logp.numel(),
                           eps, eps_hi, eps_c, tis_lo, tis_hi, kl_coef, kl_type, use_tis,
-                          cur_stream()),
-           "policy_loss");
+                          cur_stream());
 }
-void gae(torch::Tensor rewards, torch::Tensor values, torch::Tensor cu, double gamma, double lam,
+int64_t gae(torch::Tensor rewards, torch::Tensor values, torch::Tensor cu, double gamma, double lam,
          torch::Tensor adv, torch::Tensor ret) {
-  check_rc(mb_gae(PT<float>(rewards), PT<float>(values), PT<int>(cu), cu.numel() - 1, gamma, lam,
-                  PT<float>(adv), PT<float>(ret), cur_stream()),
-           "gae");
+  return mb_gae(PT<float>(rewards), PT<float>(values), PT<int>(cu), cu.numel() - 1, gamma, lam,
+                  PT<float>(adv), PT<float>(ret), cur_stream());
 }
-void grpo_adv(torch::Tensor r, int64_t gsize, bool norm_std, double eps, torch::Tensor adv) {
-  check_rc(mb_grpo_adv(PT<float>(r), r.numel() / gsize, gsize, norm_std, eps, PT<float>(adv),
-                       cur_stream()),
-           "grpo_adv");
+int64_t grpo_adv(torch::Tensor r, int64_t gsize, bool norm_std, double eps, torch::Tensor adv) {
+  return mb_grpo_adv(PT<float>(r), r.numel() / gsize, gsize, norm_std, eps, PT<float>(adv),
+                       cur_stream());
 }
-void sqnorm(torch::Tensor x, torch::Tensor part, torch::Tensor out) {
-  check_rc(mb_sqnorm(P(x), x.numel(), x.scalar_type() == at::kBFloat16, PT<float>(part),
-                     PT<float>(out), cur_stream()),
-           "sqnorm");
+int64_t sqnorm(torch::Tensor x, torch::Tensor part, torch::Tensor out) {
+  return mb_sqnorm(P(x), x.numel(), x.scalar_type() == at::kBFloat16, PT<float>(part),
+                     PT<float>(out), cur_stream());
 }
-void nonfinite(torch::Tensor x, torch::Tensor flag) {
-  check_rc(mb_nonfinite(P(x), x.numel(), x.scalar_type() == at::kBFloat16, PT<float>(flag),
-                        cur_stream()),
-           "nonfinite");
+int64_t nonfinite(torch::Tensor x, torch::Tensor flag) {
+  return mb_nonfinite(P(x), x.numel(), x.scalar_type() == at::kBFloat16, PT<float>(flag),
+                        cur_stream());
 }
-void adam(torch::Tensor param, OT master, torch::Tensor m, torch::Tensor v, torch::Tensor grad,
+int64_t adam(torch::Tensor param, OT master, torch::Tensor m, torch::Tensor v, torch::Tensor grad,
           double lr, double b1, double b2, double eps, double wd, int64_t step, OT sq,
           double max_norm, double inv_loss_scale, int64_t seed, OT skip) {
   CHECK_DT(param, at::kBFloat16);
   TORCH_CHECK(param.numel() == grad.numel() && m.numel() == param.numel() && v.numel() == param.numel());
-  check_rc(mb_adam(P(param), PT<float>(master), P(m), P(v), P(grad), param.numel(),
+  return mb_adam(P(param), PT<float>(master), P(m), P(v), P(grad), param.numel(),
                    grad.scalar_type() == at::kBFloat16, m.scalar_type() == at::kBFloat16, lr, b1,
                    b2, eps, wd, step, PT<float>(sq), max_norm, inv_loss_scale,
-                   (unsigned long long)seed, PT<float>(skip), cur_stream()),
-           "adam");
+                   (unsigned long long)seed, PT<float>(skip), cur_stream());
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

@@ -21,14 +21,47 @@ def native_available() -> bool:
     return _C is not None
 
 
+class KernelLaunchError(RuntimeError):
+    pass
+
+
+class _Checked:
+    """Proxy over the extension: every launcher returns a C status code (0 = ok); a non-zero
+    code is raised here as KernelLaunchError naming the entry point."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self._cache = {}
+
+    def __getattr__(self, name):
+        fn = self._cache.get(name)
+        if fn is None:
+            raw = getattr(self._mod, name)
+
+            def fn(*args, _raw=raw, _name=name):
+                rc = _raw(*args)
+                if isinstance(rc, int) and rc != 0:
+                    raise KernelLaunchError(f"{_name} failed with status {rc}")
+                return rc
+
+            self._cache[name] = fn
+        return fn
+
+
+_CHECKED = None
+
+
 def lib():
-    """Return the native module; raise loudly when it is missing on a GPU machine."""
+    """Return the (status-checked) native module; raise loudly when it is missing."""
+    global _CHECKED
     if _C is None:
         raise RuntimeError(
             "miles_b200._C is not built (run `python setup.py build_ext --inplace`): "
             f"{_IMPORT_ERROR!r}"
         )
-    return _C
+    if _CHECKED is None:
+        _CHECKED = _Checked(_C)
+    return _CHECKED
 
 
 def use_native(t: torch.Tensor) -> bool:
