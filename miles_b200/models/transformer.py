@@ -1,0 +1,307 @@
+"""Qwen3-family decoder (dense and MoE) on the sm_100a kernel library.
+
+One module serves both the trainer and the rollout engine:
+  * `forward_train`   packed variable-length micro-batch (thd layout), optional per-layer
+                      activation recompute, optional Rollout Routing Replay (R3)
+  * `forward_prefill` packed prompts, writes K/V into the paged cache
+  * `forward_decode`  one token per sequence against the paged cache
+All three run the same kernels with the same reduction orders, so the log-prob of a token
+computed in training is bitwise equal to the one the engine reported when it sampled it.
+
+Parameters live in ONE flat bf16 buffer (`self.flat`) with named views; gradients accumulate
+in a matching flat buffer (`main_grad` views) allocated by the trainer. The flat layout makes
+the optimizer a single fused launch, and offload / refit a handful of large copies.
+
+Reference: the GPT/MoE layer specs the reference builds through Megatron + TE
+(megatron_utils/model_provider.py:27-250) and HF Qwen3 / Qwen3-MoE modelling.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch.utils.checkpoint import checkpoint
+
+from miles_b200.models.config import ModelConfig
+from miles_b200.ops import gemm as G
+from miles_b200.ops.attention import PAGE, VarlenMeta, decode_attention, varlen_attention
+from miles_b200.ops.moe import RouterCfg, moe_experts
+from miles_b200.ops.norm import (add_rms_norm, qk_norm_rope, qk_norm_rope_to_cache, rms_norm,
+                                 rope_tables, swiglu)
+
+
+@dataclass
+class ParamSpec:
+    name: str
+    shape: tuple
+    init: str  # "normal" | "ones" | "zeros"
+    offset: int = 0
+
+    @property
+    def numel(self) -> int:
+        n = 1
+        for s in self.shape:
+            n *= s
+        return n
+
+
+def param_specs(cfg: ModelConfig) -> list[ParamSpec]:
+    H, D = cfg.hidden_size, cfg.head_dim
+    nq, nkv = cfg.num_heads, cfg.num_kv_heads
+    specs = [ParamSpec("embed_tokens.weight", (cfg.vocab_size, H), "normal")]
+    for i in range(cfg.num_layers):
+        p = f"layers.{i}."
+        specs += [
+            ParamSpec(p + "input_layernorm.weight", (H,), "ones"),
+            ParamSpec(p + "self_attn.qkv_proj.weight", ((nq + 2 * nkv) * D, H), "normal"),
+            ParamSpec(p + "self_attn.o_proj.weight", (H, nq * D), "normal"),
+            ParamSpec(p + "post_attention_layernorm.weight", (H,), "ones"),
+        ]
+        if cfg.qk_norm:
+            specs += [ParamSpec(p + "self_attn.q_norm.weight", (D,), "ones"),
+                      ParamSpec(p + "self_attn.k_norm.weight", (D,), "ones")]
+        if cfg.layer_is_moe(i):
+            E, I = cfg.num_experts, cfg.moe_intermediate_size
+            specs += [ParamSpec(p + "mlp.gate.weight", (E, H), "normal"),
+                      ParamSpec(p + "mlp.experts.w1", (E, 2 * I, H), "normal"),
+                      ParamSpec(p + "mlp.experts.w2", (E, H, I), "normal")]
+            if cfg.router_score == "sigmoid":
+                specs.append(ParamSpec(p + "mlp.gate.e_score_correction_bias", (E,), "zeros"))
+            if cfg.num_shared_experts:
+                Is = I * cfg.num_shared_experts
+                specs += [ParamSpec(p + "mlp.shared_experts.gate_up_proj.weight", (2 * Is, H), "normal"),
+                          ParamSpec(p + "mlp.shared_experts.down_proj.weight", (H, Is), "normal")]
+        else:
+            I = cfg.intermediate_size
+            specs += [ParamSpec(p + "mlp.gate_up_proj.weight", (2 * I, H), "normal"),
+                      ParamSpec(p + "mlp.down_proj.weight", (H, I), "normal")]
+    specs.append(ParamSpec("norm.weight", (H,), "ones"))
+    if not cfg.tie_embeddings:
+        specs.append(ParamSpec("lm_head.weight", (cfg.vocab_size, H), "normal"))
+    # Replicated (dense) parameters first, routed-expert parameters last: under expert
+    # parallelism the two regions reduce over different groups.
+    specs = [s for s in specs if not is_expert_param(s.name)] + [s for s in specs if is_expert_param(s.name)]
+    off = 0
+    for s in specs:
+        s.offset = off
+        off += (s.numel + 127) // 128 * 128  # 256-byte aligned views (TMA wants 16)
+    return specs
+
+
+def is_expert_param(name: str) -> bool:
+    return ".mlp.experts." in name
+
+
+class KVCache:
+    """Paged KV cache: per layer K and V of [num_pages * 64, nkv, 128] bf16."""
+
+    def __init__(self, cfg: ModelConfig, num_pages: int, device, dtype=torch.bfloat16):
+        self.num_pages = num_pages
+        slots = num_pages * PAGE
+        self.k = [torch.empty(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device)
+                  for _ in range(cfg.num_layers)]
+        self.v = [torch.empty(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device)
+                  for _ in range(cfg.num_layers)]
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.k + self.v)
+
+
+class Transformer(torch.nn.Module):
+    def __init__(self, cfg: ModelConfig, device="cuda", dtype=torch.bfloat16, seed: int = 0,
+                 init_std: float = 0.02, materialize: bool = True):
+        super().__init__()
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.specs = param_specs(cfg)
+        total = self.specs[-1].offset + self.specs[-1].numel
+        self.numel = total
+        ex = [sp.offset for sp in self.specs if is_expert_param(sp.name)]
+        self.dense_numel = ex[0] if ex else total
+        self.flat = torch.empty(total, dtype=dtype, device=self.device)
+        self.params: dict[str, torch.nn.Parameter] = {}
+        for s in self.specs:
+            p = torch.nn.Parameter(self.flat[s.offset:s.offset + s.numel].view(s.shape))
+            self.params[s.name] = p
+        if materialize:
+            self.init_weights(seed, init_std)
+        self.rope_cos, self.rope_sin = rope_tables(cfg.max_position, cfg.head_dim, cfg.rope_theta,
+                                                   self.device, cfg.rope_scaling)
+        self.router_cfgs = {}
+        if cfg.is_moe:
+            rc = RouterCfg(cfg.num_experts, cfg.topk, cfg.router_score, cfg.norm_topk_prob,
+                           cfg.n_group, cfg.topk_group, cfg.routed_scaling_factor)
+            for i in range(cfg.num_layers):
+                if cfg.layer_is_moe(i):
+                    self.router_cfgs[i] = rc
+        self.recompute = True
+        self.weight_version = 0
+
+    # -------------------------------------------------------------------------------- params
+    @torch.no_grad()
+    def init_weights(self, seed: int, std: float):
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        chunk = 1 << 26
+        for s in self.specs:
+            t = self.flat[s.offset:s.offset + s.numel]
+            if s.init == "ones":
+                t.fill_(1.0)
+            elif s.init == "zeros":
+                t.zero_()
+            else:
+                for a in range(0, s.numel, chunk):
+                    b = min(s.numel, a + chunk)
+                    t[a:b] = (torch.randn(b - a, generator=g, device=self.device) * std).to(self.dtype)
+
+    def named_flat_params(self):
+        return self.params.items()
+
+    def p(self, name: str) -> torch.Tensor:
+        return self.params[name]
+
+    def lm_head_weight(self) -> torch.Tensor:
+        return self.params["embed_tokens.weight" if self.cfg.tie_embeddings else "lm_head.weight"]
+
+    # -------------------------------------------------------------------------------- blocks
+    def _attn_train(self, i: int, x: torch.Tensor, meta: VarlenMeta) -> torch.Tensor:
+        cfg = self.cfg
+        pre = f"layers.{i}.self_attn."
+        qkv = G.linear(x, self.params[pre + "qkv_proj.weight"])
+        q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
+                               self.params.get(pre + "k_norm.weight"), meta.positions,
+                               self.rope_cos, self.rope_sin, cfg.num_heads, cfg.num_kv_heads,
+                               cfg.rms_eps, cfg.qk_norm)
+        o = varlen_attention(q, k, v, meta)
+        return G.linear(o.reshape(x.shape[0], -1), self.params[pre + "o_proj.weight"])
+
+    def _mlp(self, i: int, x: torch.Tensor, replay=None, record=None) -> torch.Tensor:
+        pre = f"layers.{i}.mlp."
+        if i in self.router_cfgs:
+            y = moe_experts(x, self.params[pre + "gate.weight"], self.params[pre + "experts.w1"],
+                            self.params[pre + "experts.w2"], self.router_cfgs[i],
+                            self.params.get(pre + "gate.e_score_correction_bias"), replay, record)
+            if self.cfg.num_shared_experts:
+                s = swiglu(G.linear(x, self.params[pre + "shared_experts.gate_up_proj.weight"]))
+                y = y + G.linear(s, self.params[pre + "shared_experts.down_proj.weight"])
+            return y
+        gu = G.linear(x, self.params[pre + "gate_up_proj.weight"])
+        return G.linear(swiglu(gu), self.params[pre + "down_proj.weight"])
+
+    def _layer_train(self, i, m_prev, r_prev, meta, replay):
+        cfg = self.cfg
+        ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
+        if m_prev is None:
+            x, r = rms_norm(r_prev, ln1, cfg.rms_eps), r_prev
+        else:
+            x, r = add_rms_norm(m_prev, r_prev, ln1, cfg.rms_eps)
+        a = self._attn_train(i, x, meta)
+        x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"],
+                             cfg.rms_eps)
+        m = self._mlp(i, x2, replay=replay)
+        return m, r
+
+    # -------------------------------------------------------------------------------- train
+    def forward_train(self, tokens: torch.Tensor, meta: VarlenMeta,
+                      replay_experts: torch.Tensor | None = None,
+                      record_experts: list | None = None) -> torch.Tensor:
+        """tokens int [T] packed; returns final hidden [T, H] (after the final norm).
+        replay_experts: int32 [T, L_moe, k] routing to replay (R3)."""
+        cfg = self.cfg
+        r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
+        m = None
+        moe_i = 0
+        for i in range(cfg.num_layers):
+            replay = None
+            if i in self.router_cfgs:
+                if replay_experts is not None:
+                    replay = replay_experts[:, moe_i].contiguous()
+                moe_i += 1
+            if self.recompute and torch.is_grad_enabled():
+                if m is None:
+                    m, r = checkpoint(lambda rr, i=i, rp=replay: self._layer_train(i, None, rr, meta, rp),
+                                      r, use_reentrant=False)
+                else:
+                    m, r = checkpoint(lambda mm, rr, i=i, rp=replay: self._layer_train(i, mm, rr, meta, rp),
+                                      m, r, use_reentrant=False)
+            else:
+                rec = None
+                if record_experts is not None and i in self.router_cfgs:
+                    rec = record_experts.append
+                if rec is not None:
+                    ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
+                    x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
+                    a = self._attn_train(i, x, meta)
+                    x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
+                    m = self._mlp(i, x2, replay=replay, record=rec)
+                else:
+                    m, r = self._layer_train(i, m, r, meta, replay)
+        y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
+        return y
+
+    # -------------------------------------------------------------------------------- inference
+    @torch.no_grad()
+    def forward_prefill(self, tokens: torch.Tensor, meta: VarlenMeta, cache: KVCache,
+                        slots: torch.Tensor, record: list | None = None) -> torch.Tensor:
+        """Packed prompt prefill. Writes K/V of every token to cache rows `slots` (int64 [T]).
+        Returns the final hidden of every token [T, H]."""
+        cfg = self.cfg
+        r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
+        m = None
+        for i in range(cfg.num_layers):
+            ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
+            x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
+            pre = f"layers.{i}.self_attn."
+            qkv = G.linear(x, self.params[pre + "qkv_proj.weight"])
+            q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
+                                   self.params.get(pre + "k_norm.weight"), meta.positions,
+                                   self.rope_cos, self.rope_sin, cfg.num_heads, cfg.num_kv_heads,
+                                   cfg.rms_eps, cfg.qk_norm)
+            cache.k[i].index_copy_(0, slots, k)
+            cache.v[i].index_copy_(0, slots, v)
+            o = varlen_attention(q, k, v, meta)
+            a = G.linear(o.reshape(x.shape[0], -1), self.params[pre + "o_proj.weight"])
+            x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"],
+                                 cfg.rms_eps)
+            rec = record.append if (record is not None and i in self.router_cfgs) else None
+            m = self._mlp(i, x2, record=rec)
+        y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
+        return y
+
+    @torch.no_grad()
+    def forward_decode(self, tokens: torch.Tensor, positions: torch.Tensor, cache: KVCache,
+                       page_table: torch.Tensor, ctx_lens: torch.Tensor, slots: torch.Tensor,
+                       record: list | None = None) -> torch.Tensor:
+        """One token per sequence. tokens int [B]; positions int32 [B]; slots int64 [B]
+        (cache row of the new token); ctx_lens int32 [B] = positions + 1. Returns hidden [B,H]."""
+        cfg = self.cfg
+        B = tokens.shape[0]
+        r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
+        m = None
+        for i in range(cfg.num_layers):
+            ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
+            x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
+            pre = f"layers.{i}.self_attn."
+            qkv = G.linear(x, self.params[pre + "qkv_proj.weight"])
+            q = qk_norm_rope_to_cache(qkv, self.params.get(pre + "q_norm.weight"),
+                                      self.params.get(pre + "k_norm.weight"), positions,
+                                      self.rope_cos, self.rope_sin, cfg.num_heads,
+                                      cfg.num_kv_heads, cache.k[i], cache.v[i], slots,
+                                      cfg.rms_eps, cfg.qk_norm)
+            o = decode_attention(q, cache.k[i], cache.v[i], page_table, ctx_lens)
+            a = G.linear(o.reshape(B, -1), self.params[pre + "o_proj.weight"])
+            x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"],
+                                 cfg.rms_eps)
+            rec = record.append if (record is not None and i in self.router_cfgs) else None
+            m = self._mlp(i, x2, record=rec)
+        y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
+        return y
+
+    def flops_per_token(self, ctx: float) -> float:
+        """Forward FLOPs per token (matmuls + attention at average context `ctx`)."""
+        c = self.cfg
+        attn = 4 * c.num_layers * c.num_heads * c.head_dim * ctx / 2  # causal: half the keys
+        return 2 * c.active_params() + attn

@@ -144,7 +144,8 @@ def rope_tables(max_pos: int, head_dim: int, theta: float, device, scaling: dict
 
 def qk_norm_rope_ref(qkv, qw, kw, pos, cos, sin, nq, nkv, eps, use_norm=True):
     T = qkv.shape[0]
-    D = 128
+    D = qkv.shape[1] // (nq + 2 * nkv)
+    half = D // 2
     x = qkv.view(T, nq + 2 * nkv, D)
     q, k, v = x[:, :nq], x[:, nq:nq + nkv], x[:, nq + nkv:]
 
@@ -153,13 +154,13 @@ def qk_norm_rope_ref(qkv, qw, kw, pos, cos, sin, nq, nkv, eps, use_norm=True):
             return t.float()
         tf = t.float()
         r = torch.rsqrt(tf.pow(2).mean(-1, keepdim=True) + eps)
-        return ((tf * r).to(torch.bfloat16).float() * w.float()).to(torch.bfloat16).float()
+        return ((tf * r).to(qkv.dtype).float() * w.float()).to(qkv.dtype).float()
 
     def rope(t):
         c = cos[pos.long()][:, None, :]
         s = sin[pos.long()][:, None, :]
-        a, b = t[..., :64], t[..., 64:]
-        return torch.cat([a * c - b * s, b * c + a * s], -1).to(torch.bfloat16)
+        a, b = t[..., :half], t[..., half:]
+        return torch.cat([a * c - b * s, b * c + a * s], -1).to(qkv.dtype)
 
     return rope(norm(q, qw)), rope(norm(k, kw)), v.contiguous()
 

@@ -1,0 +1,240 @@
+"""Training actor: packing, log-prob collection, advantage estimation and the policy update.
+
+One `Actor` per GPU process. Samples arrive with their prompt/response tokens, loss mask,
+reward-derived advantage and the rollout log-probs the engine recorded. A training step:
+
+  1. pack samples into micro-batches of at most `max_tokens_per_gpu` tokens (first-fit
+     decreasing, thd layout: no padding inside a micro-batch),
+  2. old log-probs: a no-grad forward (or the rollout log-probs with --use-rollout-logprobs);
+     with colocated weights they are bitwise equal to the engine's, which is checked,
+  3. per micro-batch: recompute-checkpointed forward (+ R3 routing replay), chunked LM-head
+     log-prob/entropy, fused clipped policy loss, backward into the flat gradient buffer,
+  4. data-parallel gradient reduction (when the world is larger than one) and the flat Adam.
+
+Reference: megatron_utils/actor.py (train_actor :367-466), training_utils/data.py
+(get_batch / DataIterator :86-418), training_utils/loss.py (policy_loss_function :500-716,
+loss scaling :828-927), megatron_utils/model.py (train_one_step :318-490).
+"""
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from miles_b200.models.transformer import Transformer
+from miles_b200.ops.attention import VarlenMeta
+from miles_b200.ops.logprob import lm_head_logprob
+from miles_b200.ops.rl import METRIC_NAMES, PolicyLossCfg, policy_loss
+from miles_b200.trainer.optimizer import FlatAdam
+
+
+@dataclass
+class TrainItem:
+    tokens: list[int]
+    prompt_len: int
+    advantage: float | list[float] = 0.0
+    loss_mask: list[int] | None = None          # over the response tokens
+    rollout_logp: list[float] | None = None
+    old_logp: list[float] | None = None
+    ref_logp: list[float] | None = None
+    routed_experts: np.ndarray | None = None    # [len(tokens)-1, L_moe, k] int32
+
+    @property
+    def resp_len(self) -> int:
+        return len(self.tokens) - self.prompt_len
+
+
+@dataclass
+class ActorConfig:
+    lr: float = 1e-6
+    betas: tuple = (0.9, 0.98)
+    weight_decay: float = 0.0
+    clip_grad: float = 1.0
+    max_tokens_per_gpu: int = 16384
+    loss: PolicyLossCfg = field(default_factory=PolicyLossCfg)
+    entropy_coef: float = 0.0
+    per_token_loss: bool = False
+    temperature: float = 1.0
+    use_rollout_logprobs: bool = False
+    use_routing_replay: bool = False
+    grad_dtype: torch.dtype = torch.bfloat16
+    optimizer_placement: str = "auto"
+    logprob_chunk: int = 4096
+
+
+def pack_microbatches(lengths: list[int], max_tokens: int) -> list[list[int]]:
+    """First-fit-decreasing bin packing of sample indices under a token budget."""
+    order = sorted(range(len(lengths)), key=lambda i: -lengths[i])
+    bins: list[list[int]] = []
+    loads: list[int] = []
+    for i in order:
+        L = lengths[i]
+        for b in range(len(bins)):
+            if loads[b] + L <= max_tokens:
+                bins[b].append(i)
+                loads[b] += L
+                break
+        else:
+            bins.append([i])
+            loads.append(L)
+    return [sorted(b) for b in bins]
+
+
+class Actor:
+    def __init__(self, model: Transformer, cfg: ActorConfig, dp_group=None):
+        self.model = model
+        self.cfg = cfg
+        self.dp_group = dp_group
+        self.dev = model.device
+        self.grad_flat: torch.Tensor | None = None
+        self.opt: FlatAdam | None = None
+        self.timers: dict[str, float] = {}
+
+    # ------------------------------------------------------------------ memory
+    def _ensure_grads(self):
+        if self.grad_flat is None:
+            self.grad_flat = torch.zeros(self.model.flat.numel(), dtype=self.cfg.grad_dtype,
+                                         device=self.dev)
+            for s in self.model.specs:
+                self.model.params[s.name].main_grad = self.grad_flat[s.offset:s.offset + s.numel].view(s.shape)
+        if self.opt is None:
+            self.opt = FlatAdam(self.model.flat, self.grad_flat, lr=self.cfg.lr,
+                                betas=self.cfg.betas, weight_decay=self.cfg.weight_decay,
+                                clip_grad=self.cfg.clip_grad, placement=self.cfg.optimizer_placement)
+
+    def release_grads(self):
+        """Free the gradient buffer (colocated mode: give the memory to the KV cache)."""
+        for s in self.model.specs:
+            p = self.model.params[s.name]
+            if hasattr(p, "main_grad"):
+                del p.main_grad
+        self.grad_flat = None
+        if self.opt is not None:
+            self.opt.g = None
+        if self.dev.type == "cuda":
+            torch.cuda.empty_cache()
+
+    # ------------------------------------------------------------------ batching
+    def _mb_inputs(self, items: list[TrainItem]):
+        toks, cu, sel, tgt = [], [0], [], []
+        for it in items:
+            base = len(toks)
+            toks.extend(it.tokens)
+            cu.append(len(toks))
+            # hidden at position p predicts token p+1: response tokens P..L-1 <- rows P-1..L-2
+            sel.extend(range(base + it.prompt_len - 1, base + len(it.tokens) - 1))
+            tgt.extend(it.tokens[it.prompt_len:])
+        dev = self.dev
+        meta = VarlenMeta(cu, dev)
+        return (torch.tensor(toks, dtype=torch.int32, device=dev), meta,
+                torch.tensor(sel, dtype=torch.long, device=dev),
+                torch.tensor(tgt, dtype=torch.int32, device=dev))
+
+    def _replay(self, items: list[TrainItem]):
+        if not self.cfg.use_routing_replay or not items or items[0].routed_experts is None:
+            return None
+        parts = []
+        for it in items:
+            ex = it.routed_experts
+            # the last token never went through the model during rollout; repeat its predecessor
+            ex = np.concatenate([ex, ex[-1:]], 0)[: len(it.tokens)]
+            parts.append(ex)
+        return torch.from_numpy(np.concatenate(parts, 0)).to(self.dev, non_blocking=True)
+
+    # ------------------------------------------------------------------ log-probs
+    @torch.no_grad()
+    def compute_logprobs(self, items: list[TrainItem]) -> list[np.ndarray]:
+        """Forward-only response log-probs of every item (old / ref log-probs)."""
+        out: list[np.ndarray | None] = [None] * len(items)
+        W = self.model.lm_head_weight()
+        for mb in pack_microbatches([len(it.tokens) for it in items], self.cfg.max_tokens_per_gpu):
+            sub = [items[i] for i in mb]
+            tok, meta, sel, tgt = self._mb_inputs(sub)
+            h = self.model.forward_train(tok, meta, replay_experts=self._replay(sub))
+            lp, _ = lm_head_logprob(h.index_select(0, sel), W, tgt, self.cfg.temperature,
+                                    self.cfg.logprob_chunk)
+            lp = lp.cpu().numpy()
+            o = 0
+            for i in mb:
+                n = items[i].resp_len
+                out[i] = lp[o:o + n]
+                o += n
+        return out
+
+    # ------------------------------------------------------------------ train
+    def train_step(self, items: list[TrainItem], global_num_samples: int | None = None,
+                   global_num_tokens: int | None = None) -> dict:
+        cfg = self.cfg
+        self._ensure_grads()
+        model = self.model
+        t0 = time.perf_counter()
+        self.grad_flat.zero_()
+        n_samples = global_num_samples or len(items)
+        n_tokens = global_num_tokens or sum(
+            (sum(it.loss_mask) if it.loss_mask is not None else it.resp_len) for it in items)
+        W = model.lm_head_weight()
+        metrics = torch.zeros(len(METRIC_NAMES) + 1, dtype=torch.float64, device=self.dev)
+        mbs = pack_microbatches([len(it.tokens) for it in items], cfg.max_tokens_per_gpu)
+        for mb in mbs:
+            sub = [items[i] for i in mb]
+            tok, meta, sel, tgt = self._mb_inputs(sub)
+            adv, old, roll, ref, wgt = [], [], [], [], []
+            for it in sub:
+                n = it.resp_len
+                mask = np.asarray(it.loss_mask if it.loss_mask is not None else [1] * n, np.float32)
+                a = it.advantage
+                adv.append(np.full(n, a, np.float32) if np.isscalar(a) else np.asarray(a, np.float32))
+                if it.old_logp is not None:
+                    old.append(np.asarray(it.old_logp, np.float32))
+                elif it.rollout_logp is not None:
+                    old.append(np.asarray(it.rollout_logp, np.float32))
+                else:
+                    old.append(np.zeros(n, np.float32))
+                roll.append(np.asarray(it.rollout_logp if it.rollout_logp is not None else old[-1], np.float32))
+                if it.ref_logp is not None:
+                    ref.append(np.asarray(it.ref_logp, np.float32))
+                if cfg.per_token_loss:
+                    wgt.append(mask / max(n_tokens, 1))
+                else:
+                    wgt.append(mask / max(mask.sum(), 1.0) / n_samples)
+            T = lambda xs: torch.from_numpy(np.concatenate(xs)).to(self.dev, non_blocking=True)
+            h = model.forward_train(tok, meta, replay_experts=self._replay(sub))
+            hs = h.index_select(0, sel)
+            lp, ent = lm_head_logprob(hs, W, tgt, cfg.temperature, cfg.logprob_chunk)
+            loss, m = policy_loss(lp, T(old), T(adv), T(wgt), cfg.loss,
+                                  T(roll) if cfg.loss.use_tis else None,
+                                  T(ref) if ref and cfg.loss.kl_type != "none" else None)
+            if cfg.entropy_coef:
+                loss = loss - cfg.entropy_coef * (ent * T(wgt)).sum()
+            loss.backward()
+            metrics[: len(METRIC_NAMES)] += m.double().to(self.dev)
+            metrics[-1] += ((ent.detach() * T(wgt)).sum()).double()
+        # parameters whose gradient came through autograd (embedding, norms) -> flat buffer
+        for name, p in model.params.items():
+            if p.grad is not None:
+                p.main_grad.add_(p.grad.to(p.main_grad.dtype))
+                p.grad = None
+        t1 = time.perf_counter()
+        if self.dp_group is not None and dist.get_world_size(self.dp_group) > 1:
+            self._reduce_grads()
+        self.opt.step()
+        model.weight_version += 1
+        out = {k: float(v) for k, v in zip(METRIC_NAMES + ["entropy"], metrics.tolist())}
+        out["grad_norm"] = float(self.opt.grad_norm())
+        out["num_microbatches"] = len(mbs)
+        self.timers["train_fwd_bwd"] = t1 - t0
+        self.timers["train_total"] = time.perf_counter() - t0
+        return out
+
+    def _reduce_grads(self):
+        """Sum gradients over data-parallel ranks (replicated region) and expert-data-parallel
+        ranks (expert region, none when EP == world)."""
+        dense = self.grad_flat[: self.model.dense_numel]
+        dist.all_reduce(dense, group=self.dp_group)
+        ep_dp = getattr(self, "expert_dp_group", None)
+        if ep_dp is not None and dist.get_world_size(ep_dp) > 1:
+            dist.all_reduce(self.grad_flat[self.model.dense_numel:], group=ep_dp)
