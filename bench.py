@@ -1,0 +1,240 @@
+"""Headline benchmark: one colocated GRPO step (rollout + log-probs + policy update) of
+Qwen3-30B-A3B (random init, synthetic prompts/rewards) per timed step.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+Workload per GPU (weak scaling): 8 prompts x 8 samples, 512 uniform-random prompt tokens,
+responses of uniform 1024..8192 tokens (the length is sampled per response; generation stops
+there), temperature 1.0, Bernoulli(0.5) rewards, GRPO advantages, PPO clip 0.2, TIS cap 2.0,
+Rollout Routing Replay (routing recorded in rollout, replayed in training), Adam lr 1e-6.
+At N GPUs the global batch is N x 64 samples (N x 8 prompts), i.e. the BASELINE config's
+64 prompts x 8 samples at N = 8.
+
+Timing: W untimed warm-up steps, then K steps bracketed by barrier + synchronize, device-timed
+with CUDA events; the max over ranks is reported. Inputs are larger than L2 every step (the
+model itself is ~61 GB). `e2e` times the same public API call (ColocatedRL.step) on the host
+clock, including the host->device copy of the prompts and the device->host read of the result.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="qwen3-30b-a3b")
+    ap.add_argument("--prompts-per-gpu", type=int, default=8)
+    ap.add_argument("--samples-per-prompt", type=int, default=8)
+    ap.add_argument("--prompt-len", type=int, default=512)
+    ap.add_argument("--resp-min", type=int, default=1024)
+    ap.add_argument("--resp-max", type=int, default=8192)
+    ap.add_argument("--max-tokens-per-gpu", type=int, default=16384)
+    ap.add_argument("--no-graph", action="store_true")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append([x.strip() for x in line.split(",")])
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        time.sleep(0.2)
+        sm, reasons, smax = [], set(), None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            try:
+                sm.append(float(s[1]))
+                smax = float(s[2])
+                for n, v in zip(names, s[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except Exception:
+                pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+METRIC = "GRPO step s & rollout tok/s at 1/2/4/8 B200 (Qwen3-30B-A3B); weight-sync s"
+
+
+def reference_arm(args):
+    here = os.path.dirname(os.path.abspath(__file__))
+    ref = os.path.join(here, "baseline", "_ref")
+    why = ("reference runtime stack (ray, sglang, megatron-core, transformer_engine) is not "
+           "installed and cannot be installed offline; its Docker build clones forks from GitHub")
+    if not os.path.isdir(ref):
+        why = "baseline/_ref not installed; " + why
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why, "metric": METRIC}), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from miles_b200.engine.engine import RolloutEngine
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops import _lib
+    from miles_b200.ops.rl import PolicyLossCfg
+    from miles_b200.trainer.actor import Actor, ActorConfig
+    from miles_b200.trainer.grpo import ColocatedRL, RLConfig
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    group = dist.group.WORLD if world > 1 else None
+
+    cfg = preset(args.model)
+    model = Transformer(cfg, device=dev, seed=1234)
+    engine = RolloutEngine(model, max_batch=args.prompts_per_gpu * args.samples_per_prompt,
+                           use_cuda_graph=not args.no_graph,
+                           max_pages_per_seq=(args.prompt_len + args.resp_max + 63) // 64 + 1)
+    acfg = ActorConfig(lr=1e-6, max_tokens_per_gpu=args.max_tokens_per_gpu,
+                       loss=PolicyLossCfg(eps_clip=0.2, eps_clip_high=0.2, use_tis=True,
+                                          tis_clip=2.0),
+                       use_routing_replay=cfg.is_moe)
+    actor = Actor(model, acfg, dp_group=group)
+    rl = ColocatedRL(engine, actor, RLConfig(n_samples_per_prompt=args.samples_per_prompt,
+                                             routing_replay=cfg.is_moe, seed=rank))
+    rng = np.random.default_rng(1000 + rank)
+    nsamp = args.prompts_per_gpu * args.samples_per_prompt
+
+    def workload():
+        prompts = [rng.integers(0, cfg.vocab_size, args.prompt_len).tolist()
+                   for _ in range(args.prompts_per_gpu)]
+        lens = rng.integers(args.resp_min, args.resp_max + 1, nsamp).tolist()
+        rewards = (rng.random(nsamp) < 0.5).astype(np.float32).tolist()
+        return prompts, lens, rewards
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        rl.step(*[x for x in workload()[:2]], rewards=workload()[2])
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    n0 = _lib.launch_count()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    tokens = resp = 0
+    rollout_s = train_s = lp_s = 0.0
+    t_host0 = time.perf_counter()
+    ev0.record()
+    for _ in range(args.steps):
+        prompts, lens, rewards = workload()
+        m = rl.step(prompts, lens, rewards)
+        tokens += m["tokens_total"]
+        resp += m["response_tokens"]
+        rollout_s += m["perf/rollout_time"]
+        lp_s += m["perf/log_probs_time"]
+        train_s += m["perf/actor_train_time"]
+    ev1.record()
+    barrier()
+    t_host = time.perf_counter() - t_host0
+    clocks = sampler.stop()
+    launches = _lib.launch_count() - n0
+    ms = ev0.elapsed_time(ev1) / args.steps
+    vals = torch.tensor([ms, t_host / args.steps * 1e3, rollout_s, lp_s, train_s,
+                         float(tokens), float(resp)], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = vals[:5].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = vals[5:].clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        vals = torch.cat([mx, sm])
+    ms, host_ms, rollout_s, lp_s, train_s, tokens, resp = vals.tolist()
+    step_s = ms / 1e3
+    value = tokens / args.steps / step_s
+    if rank == 0:
+        h2d = args.prompts_per_gpu * args.prompt_len * 4 * world
+        d2h = int(resp / args.steps) * 8 + 8 * 8
+        out = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s (GRPO step throughput: prompt+response tokens rolled out and trained per second, whole job)",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (uniform-random prompt tokens, Bernoulli(0.5) rewards, random-init weights)",
+            "config": {"model": "Qwen3-30B-A3B" if args.model == "qwen3-30b-a3b" else args.model,
+                       "global_batch": nsamp * world, "prompts": args.prompts_per_gpu * world,
+                       "samples_per_prompt": args.samples_per_prompt, "seq_len": args.prompt_len + args.resp_max,
+                       "prompt_len": args.prompt_len, "response_len": [args.resp_min, args.resp_max],
+                       "parallelism": f"dp{world}" if world > 1 else "dp1",
+                       "routing_replay": cfg.is_moe, "tis_cap": 2.0,
+                       "l2": "inputs larger than L2 (61 GB of weights streamed every step)"},
+            "grpo_step_s": step_s,
+            "rollout_tok_s": resp / args.steps / (rollout_s / args.steps),
+            "rollout_s": rollout_s / args.steps, "log_probs_s": lp_s / args.steps,
+            "train_s": train_s / args.steps, "weight_sync_s": 0.0,
+            "weight_sync_note": "colocated engine shares the trainer's parameter buffer: refit is a weight-version bump",
+            "clocks": clocks,
+            "e2e": {"value": tokens / (host_ms / 1e3 * args.steps), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "train_rollout_logprob_abs_diff": rl.last_metrics.get("train/train_rollout_logprob_abs_diff"),
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -27,6 +27,7 @@ import torch
 
 from miles_b200.models.transformer import KVCache, Transformer
 from miles_b200.ops.attention import PAGE, VarlenMeta
+from miles_b200.ops import _lib
 from miles_b200.ops.logprob import sample_from_hidden
 
 _BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256, 384, 512)
@@ -81,6 +82,7 @@ class RolloutEngine:
         self._mem_fraction = mem_fraction
         self.cache: KVCache | None = None
         self.graphs: dict[int, tuple] = {}
+        self.graph_launches: dict[int, int] = {}
         self.pool = None
         self.aborted = False
         self.stats = {}
@@ -162,8 +164,10 @@ class RolloutEngine:
         if self.pool is None:
             self.pool = torch.cuda.graph_pool_handle()
         g = torch.cuda.CUDAGraph()
+        n0 = _lib.launch_count()
         with torch.cuda.graph(g, pool=self.pool):
             out = self._step_fn(st)
+        self.graph_launches[B] = _lib.launch_count() - n0
         entry = (g, st, out)
         self.graphs[B] = entry
         return entry
@@ -268,6 +272,7 @@ class RolloutEngine:
             st["seeds"].copy_(torch.from_numpy(seed), non_blocking=True)
             if g is not None:
                 g.replay()
+                _lib.add_launches(self.graph_launches[Bb])
                 tok, lp = out
             else:
                 tok, lp = self._step_fn(st)

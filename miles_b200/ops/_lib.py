@@ -39,6 +39,8 @@ class _Checked:
             raw = getattr(self._mod, name)
 
             def fn(*args, _raw=raw, _name=name):
+                global LAUNCHES
+                LAUNCHES += 1
                 rc = _raw(*args)
                 if isinstance(rc, int) and rc != 0:
                     raise KernelLaunchError(f"{_name} failed with status {rc}")
@@ -49,6 +51,18 @@ class _Checked:
 
 
 _CHECKED = None
+# Number of native launcher calls issued from Python (each issues >= 1 kernel). Work replayed
+# from a captured CUDA graph is added by the engine (launches recorded at capture time).
+LAUNCHES = 0
+
+
+def launch_count() -> int:
+    return LAUNCHES
+
+
+def add_launches(n: int) -> None:
+    global LAUNCHES
+    LAUNCHES += n
 
 
 def lib():
