@@ -101,7 +101,9 @@ class Actor:
                                          device=self.dev)
             for s in self.model.specs:
                 self.model.params[s.name].main_grad = self.grad_flat[s.offset:s.offset + s.numel].view(s.shape)
-        if self.opt is None:
+        if self.opt is not None:
+            self.opt.g = self.grad_flat
+        else:
             self.opt = FlatAdam(self.model.flat, self.grad_flat, lr=self.cfg.lr,
                                 betas=self.cfg.betas, weight_decay=self.cfg.weight_decay,
                                 clip_grad=self.cfg.clip_grad, placement=self.cfg.optimizer_placement)

@@ -44,10 +44,11 @@ def test_grpo_step_cpu():
     prompts = [rng.integers(0, 4096, 64).tolist() for _ in range(8)]
     before = m.flat.clone()
     met = rl.step(prompts, rewards=rng.integers(0, 2, 32).astype(float).tolist())
+    met = rl.step(prompts, rewards=rng.integers(0, 2, 32).astype(float).tolist())
     assert met["train/train_rollout_logprob_abs_diff"] < 1e-4
     assert np.isfinite(met["grad_norm"])
     assert not torch.equal(before, m.flat)
-    assert m.weight_version == 1
+    assert m.weight_version == 2
 
 
 def test_moe_engine_and_replay_cpu():
