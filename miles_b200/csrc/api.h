@@ -35,8 +35,9 @@ int mb_qk_norm_rope_bwd(const void* dq, const void* dk, const void* dv, const vo
                         const float* cos_t, const float* sin_t, const float* rstd, void* dqkv,
                         float* dw_part, int nparts, float* dw_out, int T, int nq, int nkv,
                         int use_norm, cudaStream_t st);
-int mb_swiglu_fwd(const void* gu, void* out, long long T, int I, cudaStream_t st);
-int mb_swiglu_bwd(const void* gu, const void* dout, void* dgu, long long T, int I, cudaStream_t st);
+int mb_swiglu_fwd(const void* gu, void* out, long long T, int I, const int* nrows, cudaStream_t st);
+int mb_swiglu_bwd(const void* gu, const void* dout, void* dgu, long long T, int I, const int* nrows,
+                  cudaStream_t st);
 int mb_router_fwd(const float* logits, const float* bias, const int* idx_in, int* idx_out,
                   float* w_out, int T, int E, int k, int score_fn, int renorm, int n_group,
                   int topk_group, float scale, cudaStream_t st);

@@ -102,15 +102,15 @@ int64_t qk_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, t
                                nq, nkv, use_norm, cur_stream());
 }
 
-int64_t swiglu_fwd(torch::Tensor gu, torch::Tensor out) {
+int64_t swiglu_fwd(torch::Tensor gu, torch::Tensor out, OT nrows) {
   TORCH_CHECK(gu.is_contiguous() && out.is_contiguous());
   const int I = out.size(-1);
-  return mb_swiglu_fwd(P(gu), P(out), out.numel() / I, I, cur_stream());
+  return mb_swiglu_fwd(P(gu), P(out), out.numel() / I, I, PT<int>(nrows), cur_stream());
 }
-int64_t swiglu_bwd(torch::Tensor gu, torch::Tensor dout, torch::Tensor dgu) {
+int64_t swiglu_bwd(torch::Tensor gu, torch::Tensor dout, torch::Tensor dgu, OT nrows) {
   TORCH_CHECK(gu.is_contiguous() && dout.is_contiguous() && dgu.is_contiguous());
   const int I = dout.size(-1);
-  return mb_swiglu_bwd(P(gu), P(dout), P(dgu), dout.numel() / I, I, cur_stream());
+  return mb_swiglu_bwd(P(gu), P(dout), P(dgu), dout.numel() / I, I, PT<int>(nrows), cur_stream());
 }
 
 int64_t router_fwd(torch::Tensor logits, OT bias, OT idx_in, torch::Tensor idx_out,

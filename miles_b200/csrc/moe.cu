@@ -314,57 +314,60 @@ __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, const int
   for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
 }
 
-// dx[t] = sum_j dxs[dest[t*k+j]] (slot order), one warp per token.
+// dx[t] = sum_j dxs[dest[t*k+j]] (slot order), one warp per (token, 256-column chunk).
 __global__ void moe_gather_bwd_kernel(const __nv_bfloat16* __restrict__ dxs,
                                       const int* __restrict__ dest, int T, int k, int H,
                                       __nv_bfloat16* __restrict__ dx) {
-  const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const long long gw = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  for (int c = lane * 8; c < H; c += 256) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < k; ++j) {
-      const uint4 v = *reinterpret_cast<const uint4*>(dxs + (long long)dest[t * k + j] * H + c);
-      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
+  const int nch = H / 256;
+  if (gw >= (long long)T * nch) return;
+  const int t = (int)(gw / nch);
+  const int c = (int)(gw % nch) * 256 + lane * 8;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int j = 0; j < k; ++j) {
+    const uint4 v = *reinterpret_cast<const uint4*>(dxs + (long long)dest[t * k + j] * H + c);
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(b[q]);
-    }
-    uint4 o;
-    __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) ob[q] = __float2bfloat16(acc[q]);
-    *reinterpret_cast<uint4*>(dx + (long long)t * H + c) = o;
+    for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(b[q]);
   }
+  uint4 o;
+  __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) ob[q] = __float2bfloat16(acc[q]);
+  *reinterpret_cast<uint4*>(dx + (long long)t * H + c) = o;
 }
 
 // y[t] = sum_j w[t,j] * ys[dest[t*k+j]] (+ add[t]); fp32 accumulation in slot order.
+// One warp per (token, 256-column chunk) so small decode batches still spread over the GPU.
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ ys, const int* __restrict__ dest,
                                    const float* __restrict__ w, const __nv_bfloat16* __restrict__ add,
                                    int T, int k, int H, __nv_bfloat16* __restrict__ y) {
-  const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const long long gw = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  for (int c = lane * 8; c < H; c += 256) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < k; ++j) {
-      const float wj = w[t * k + j];
-      const uint4 v = *reinterpret_cast<const uint4*>(ys + (long long)dest[t * k + j] * H + c);
-      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
+  const int nch = H / 256;
+  if (gw >= (long long)T * nch) return;
+  const int t = (int)(gw / nch);
+  const int c = (int)(gw % nch) * 256 + lane * 8;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int j = 0; j < k; ++j) {
+    const float wj = w[t * k + j];
+    const uint4 v = *reinterpret_cast<const uint4*>(ys + (long long)dest[t * k + j] * H + c);
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] += wj * __bfloat162float(b[q]);
-    }
-    if (add) {
-      const uint4 v = *reinterpret_cast<const uint4*>(add + (long long)t * H + c);
-      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(b[q]);
-    }
-    uint4 o;
-    __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) ob[q] = __float2bfloat16(acc[q]);
-    *reinterpret_cast<uint4*>(y + (long long)t * H + c) = o;
+    for (int q = 0; q < 8; ++q) acc[q] += wj * __bfloat162float(b[q]);
   }
+  if (add) {
+    const uint4 v = *reinterpret_cast<const uint4*>(add + (long long)t * H + c);
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(b[q]);
+  }
+  uint4 o;
+  __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) ob[q] = __float2bfloat16(acc[q]);
+  *reinterpret_cast<uint4*>(y + (long long)t * H + c) = o;
 }
 
 // Backward of the combine: dys[dest] = w * dy[t]; dw[t,j] = <dy[t], ys[dest]>. One warp/token.
@@ -457,7 +460,8 @@ extern "C" int mb_moe_gather_bwd(const void* dxs, const int* dest, int T, int k,
                                  cudaStream_t st) {
   if (T == 0) return 0;
   if (H % 256) return -1;
-  moe_gather_bwd_kernel<<<(T + 7) / 8, 256, 0, st>>>((const __nv_bfloat16*)dxs, dest, T, k, H,
+  const long long wg = (long long)T * (H / 256);
+  moe_gather_bwd_kernel<<<(unsigned)((wg + 7) / 8), 256, 0, st>>>((const __nv_bfloat16*)dxs, dest, T, k, H,
                                                      (__nv_bfloat16*)dx);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -466,7 +470,8 @@ extern "C" int mb_moe_combine(const void* ys, const int* dest, const float* w, c
                               int T, int k, int H, void* y, cudaStream_t st) {
   if (T == 0) return 0;
   if (H % 256) return -1;
-  moe_combine_kernel<<<(T + 7) / 8, 256, 0, st>>>((const __nv_bfloat16*)ys, dest, w,
+  const long long wc = (long long)T * (H / 256);
+  moe_combine_kernel<<<(unsigned)((wc + 7) / 8), 256, 0, st>>>((const __nv_bfloat16*)ys, dest, w,
                                                   (const __nv_bfloat16*)add, T, k, H,
                                                   (__nv_bfloat16*)y);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;

@@ -313,7 +313,9 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq,
 // SwiGLU: out = silu(gate) * up, gate/up halves of each row of gu [T, 2I] (row stride 2I).
 // ----------------------------------------------------------------------------------------------
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu,
-                                  __nv_bfloat16* __restrict__ out, long long T, int I) {
+                                  __nv_bfloat16* __restrict__ out, long long T, int I,
+                                  const int* __restrict__ nrows) {
+  if (nrows) T = min(T, (long long)*nrows);  // rows beyond the live MoE segments are skipped
   const long long n8 = T * I / 8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
        i += (long long)gridDim.x * blockDim.x) {
@@ -338,7 +340,9 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu,
 
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu,
                                   const __nv_bfloat16* __restrict__ dout,
-                                  __nv_bfloat16* __restrict__ dgu, long long T, int I) {
+                                  __nv_bfloat16* __restrict__ dgu, long long T, int I,
+                                  const int* __restrict__ nrows) {
+  if (nrows) T = min(T, (long long)*nrows);
   const long long n8 = T * I / 8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
        i += (long long)gridDim.x * blockDim.x) {
@@ -459,21 +463,22 @@ extern "C" int mb_qk_norm_rope_bwd(const void* dq, const void* dk, const void* d
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
-extern "C" int mb_swiglu_fwd(const void* gu, void* out, long long T, int I, cudaStream_t st) {
-  if (T == 0) return 0;
-  if (I % 8) return -1;
-  const long long n8 = T * I / 8;
-  swiglu_fwd_kernel<<<grid_for(n8, 256), 256, 0, st>>>((const __nv_bfloat16*)gu,
-                                                       (__nv_bfloat16*)out, T, I);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
-}
-
-extern "C" int mb_swiglu_bwd(const void* gu, const void* dout, void* dgu, long long T, int I,
+extern "C" int mb_swiglu_fwd(const void* gu, void* out, long long T, int I, const int* nrows,
                              cudaStream_t st) {
   if (T == 0) return 0;
   if (I % 8) return -1;
   const long long n8 = T * I / 8;
+  swiglu_fwd_kernel<<<grid_for(n8, 256), 256, 0, st>>>((const __nv_bfloat16*)gu,
+                                                       (__nv_bfloat16*)out, T, I, nrows);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+extern "C" int mb_swiglu_bwd(const void* gu, const void* dout, void* dgu, long long T, int I,
+                             const int* nrows, cudaStream_t st) {
+  if (T == 0) return 0;
+  if (I % 8) return -1;
+  const long long n8 = T * I / 8;
   swiglu_bwd_kernel<<<grid_for(n8, 256), 256, 0, st>>>(
-      (const __nv_bfloat16*)gu, (const __nv_bfloat16*)dout, (__nv_bfloat16*)dgu, T, I);
+      (const __nv_bfloat16*)gu, (const __nv_bfloat16*)dout, (__nv_bfloat16*)dgu, T, I, nrows);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

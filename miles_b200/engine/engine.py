@@ -220,6 +220,9 @@ class RolloutEngine:
             cu.append(len(toks))
         meta = VarlenMeta(cu, dev)
         rec = [] if self.n_moe else None
+        nvtx = dev.type == "cuda"
+        if nvtx:
+            torch.cuda.nvtx.range_push("prefill")
         h = self.model.forward_prefill(torch.tensor(toks, dtype=torch.int32, device=dev), meta,
                                        self.cache, torch.tensor(slots, dtype=torch.int64, device=dev),
                                        record=rec)
@@ -237,6 +240,8 @@ class RolloutEngine:
                 if s.req.return_routed_experts:
                     s.experts.append(ex[cu[b]:cu[b + 1]])
         self._accept(wave, tok.tolist(), lp.tolist())
+        if nvtx:
+            torch.cuda.nvtx.range_pop()
         # ---- decode
         steps = 0
         while not self.aborted:
@@ -270,6 +275,8 @@ class RolloutEngine:
             st["pt"].copy_(torch.from_numpy(pt), non_blocking=True)
             st["inv_t"].copy_(torch.from_numpy(invt), non_blocking=True)
             st["seeds"].copy_(torch.from_numpy(seed), non_blocking=True)
+            if nvtx:
+                torch.cuda.nvtx.range_push("decode_step")
             if g is not None:
                 g.replay()
                 _lib.add_launches(self.graph_launches[Bb])
@@ -282,6 +289,8 @@ class RolloutEngine:
                     if s.req.return_routed_experts:
                         s.experts.append(ex[j:j + 1])
             self._accept(live, tok[:n].tolist(), lp[:n].tolist())
+            if nvtx:
+                torch.cuda.nvtx.range_pop()
             steps += 1
         if self.aborted:
             for s in wave:

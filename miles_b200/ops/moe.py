@@ -93,11 +93,18 @@ class MoEPlan:
         lib().moe_permute_plan(idx.contiguous().view(-1), E, ALIGN, hist, base, self.counts,
                                self.offsets, self.dest)
 
-    def gather(self, x: torch.Tensor) -> torch.Tensor:
+    def gather(self, x: torch.Tensor, zero_pad: bool = True) -> torch.Tensor:
+        """Expert-sorted copy of x. Padding rows only matter to the weight-grad contraction, so
+        they are zeroed only when a backward will follow."""
         xs = torch.empty(self.rows, x.shape[1], dtype=x.dtype, device=x.device)
         lib().moe_gather(x, self.dest, self.k, xs)
-        lib().moe_zero_pad(self.counts, self.offsets, xs)
+        if zero_pad:
+            lib().moe_zero_pad(self.counts, self.offsets, xs)
         return xs
+
+    @property
+    def total_rows(self) -> torch.Tensor:
+        return self.offsets[self.E:]
 
 
 def _accum_grouped_wgrad(w: torch.Tensor, dy: torch.Tensor, x: torch.Tensor, plan: MoEPlan):
@@ -111,14 +118,14 @@ def _accum_grouped_wgrad(w: torch.Tensor, dy: torch.Tensor, x: torch.Tensor, pla
 def experts_forward(xs, w1, w2, plan: MoEPlan):
     gu = G.grouped_nt(xs, w1, plan.offsets)
     a = torch.empty(gu.shape[0], gu.shape[1] // 2, dtype=gu.dtype, device=gu.device)
-    lib().swiglu_fwd(gu, a)
+    lib().swiglu_fwd(gu, a, plan.total_rows)
     ys = G.grouped_nt(a, w2, plan.offsets)
     return gu, a, ys
 
 
 class _MoE(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, router_w, w1, w2, bias, cfg: RouterCfg, replay_idx, record):
+    def forward(ctx, x, router_w, w1, w2, bias, cfg: RouterCfg, replay_idx, record, need_bwd):
         T, H = x.shape
         x = x.contiguous()
         logits = G.matmul_nt(x, router_w, out_dtype=torch.float32)
@@ -129,7 +136,7 @@ class _MoE(torch.autograd.Function):
         if record is not None:
             record(idx)
         plan = MoEPlan(idx, cfg.E)
-        xs = plan.gather(x)
+        xs = plan.gather(x, zero_pad=need_bwd)
         gu, a, ys = experts_forward(xs, w1, w2, plan)
         y = torch.empty_like(x)
         lib().moe_combine(ys, plan.dest, w, None, y)
@@ -151,7 +158,7 @@ class _MoE(torch.autograd.Function):
         da = G.grouped_nn(dys, w2, plan.offsets)
         dw2 = _accum_grouped_wgrad(w2, dys, a, plan)
         dgu = torch.empty_like(gu)
-        lib().swiglu_bwd(gu, da, dgu)
+        lib().swiglu_bwd(gu, da, dgu, plan.total_rows)
         dxs = G.grouped_nn(dgu, w1, plan.offsets)
         dw1 = _accum_grouped_wgrad(w1, dgu, xs, plan)
         dx = torch.empty_like(x)
@@ -160,7 +167,7 @@ class _MoE(torch.autograd.Function):
         lib().router_bwd(logits, idx, dw, dlogits, cfg.score_fn, cfg.renorm, cfg.scale)
         dx.add_(G.matmul_nn(dlogits, router_w))
         dwr = G._accumulate_wgrad(router_w, dlogits, x)
-        return dx, dwr, dw1, dw2, None, None, None, None
+        return dx, dwr, dw1, dw2, None, None, None, None, None
 
 
 def moe_experts(x, router_w, w1, w2, cfg: RouterCfg, bias=None, replay_idx=None, record=None):
@@ -172,4 +179,4 @@ def moe_experts(x, router_w, w1, w2, cfg: RouterCfg, bias=None, replay_idx=None,
         if record is not None:
             record(idx)
         return y
-    return _MoE.apply(x, router_w, w1, w2, bias, cfg, replay_idx, record)
+    return _MoE.apply(x, router_w, w1, w2, bias, cfg, replay_idx, record, torch.is_grad_enabled())

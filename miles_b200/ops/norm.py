@@ -238,7 +238,7 @@ class _SwiGLU(torch.autograd.Function):
     def forward(ctx, gu):
         gu = gu.contiguous()
         out = torch.empty(*gu.shape[:-1], gu.shape[-1] // 2, dtype=gu.dtype, device=gu.device)
-        lib().swiglu_fwd(gu, out)
+        lib().swiglu_fwd(gu, out, None)
         ctx.save_for_backward(gu)
         return out
 
@@ -246,7 +246,7 @@ class _SwiGLU(torch.autograd.Function):
     def backward(ctx, dout):
         (gu,) = ctx.saved_tensors
         dgu = torch.empty_like(gu)
-        lib().swiglu_bwd(gu, dout.contiguous(), dgu)
+        lib().swiglu_bwd(gu, dout.contiguous(), dgu, None)
         return dgu
 
 
