@@ -57,9 +57,10 @@ int mb_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse
                 const int* cu_seqlens, const int* blk_seq, const int* blk_idx, int nblocks,
                 long long q_stride, long long k_stride, long long v_stride, long long o_stride,
                 int nq, int nkv, int T, float softmax_scale, cudaStream_t st);
+int mb_attn_decode_nsplit(int max_pages);
 int mb_attn_decode(const void* q, const void* kc, const void* vc, void* o, const int* page_table,
                    const int* ctx_lens, int B, int max_pages, int nq, int nkv, float softmax_scale,
-                   cudaStream_t st);
+                   float* ws_o, float* ws_ml, cudaStream_t st);
 int mb_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
                 const float* lse, float* delta, void* dq, void* dk, void* dv,
                 const int* cu_seqlens, const int* blk_seq, const int* blk_idx, int nblocks,

@@ -189,18 +189,47 @@ MB_DEVICE void kv_block_update(const uint32_t (&qf)[8][4], uint32_t ktile, uint3
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Canonical split-KV combination. Keys are processed in chunks of CHUNK_BLOCKS blocks; each
+// chunk's (m, l, o) starts from scratch and the chunk partials are merged in increasing chunk
+// order into a running total. The prefill kernel performs the merges in registers/shared
+// memory; the decode path computes chunks in separate CTAs and merges them in a combine
+// kernel with the very same non-contracted float operations, so both give identical bits.
+// ---------------------------------------------------------------------------------------------
+constexpr int CHUNK_BLOCKS = 16;  // 1024 keys per chunk
+
+// (M, L) <- merge((M, L), (m, l)); returns the factors applied to the old total and the chunk.
+MB_DEVICE void merge_stats(float& M, float& L, float m, float l, float& fa, float& fb) {
+  if (m == -INFINITY) { fa = 1.f; fb = 0.f; return; }
+  if (M == -INFINITY) { M = m; L = l; fa = 0.f; fb = 1.f; return; }
+  const float Mn = fmaxf(M, m);
+  fa = exp2f(__fsub_rn(M, Mn));
+  fb = exp2f(__fsub_rn(m, Mn));
+  L = __fadd_rn(__fmul_rn(L, fa), __fmul_rn(l, fb));
+  M = Mn;
+}
+MB_DEVICE float merge_val(float O, float o, float fa, float fb) {
+  if (fb == 0.f) return O;
+  if (fa == 0.f) return o;
+  return __fadd_rn(__fmul_rn(O, fa), __fmul_rn(o, fb));
+}
+
 // Write normalised output rows and LSE (natural log).
 MB_DEVICE void finish_rows(const float (&o)[16][4], const float (&m)[2], const float (&l)[2],
                            __nv_bfloat16* out0, __nv_bfloat16* out1, bool ok0, bool ok1,
                            float* lse0, float* lse1, int lane) {
   const int c = lane & 3;
-  const float inv0 = l[0] > 0.f ? 1.f / l[0] : 0.f;
-  const float inv1 = l[1] > 0.f ? 1.f / l[1] : 0.f;
+  const float inv0 = l[0] > 0.f ? __frcp_rn(l[0]) : 0.f;
+  const float inv1 = l[1] > 0.f ? __frcp_rn(l[1]) : 0.f;
 #pragma unroll
   for (int n = 0; n < 16; ++n) {
     const int col = n * 8 + 2 * c;
-    if (ok0) *reinterpret_cast<uint32_t*>(out0 + col) = pack2(o[n][0] * inv0, o[n][1] * inv0);
-    if (ok1) *reinterpret_cast<uint32_t*>(out1 + col) = pack2(o[n][2] * inv1, o[n][3] * inv1);
+    if (ok0)
+      *reinterpret_cast<uint32_t*>(out0 + col) =
+          pack2(__fmul_rn(o[n][0], inv0), __fmul_rn(o[n][1], inv0));
+    if (ok1)
+      *reinterpret_cast<uint32_t*>(out1 + col) =
+          pack2(__fmul_rn(o[n][2], inv1), __fmul_rn(o[n][3], inv1));
   }
   if (c == 0) {
     const float ln2 = 0.69314718055994530942f;
@@ -253,6 +282,23 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const FwdParams p) {
   const int g = lane >> 2;
   const int qpos0 = m0 + warp * 16 + g, qpos1 = qpos0 + 8;
   uint32_t qf[8][4];
+  // running total of merged chunks: O in shared memory laid out [element][thread]
+  float* otot = reinterpret_cast<float*>(smem + 5 * TILE_BYTES);
+  float Mt[2] = {-INFINITY, -INFINITY}, Lt[2] = {0.f, 0.f};
+  auto merge_chunk = [&]() {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float fa, fb;
+      merge_stats(Mt[r], Lt[r], m[r], l[r], fa, fb);
+#pragma unroll
+      for (int n = 0; n < 16; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int i = n * 4 + r * 2 + e;
+          otot[i * 128 + tid] = merge_val(otot[i * 128 + tid], o[n][r * 2 + e], fa, fb);
+        }
+    }
+  };
   for (int j = 0; j < nblocks; ++j) {
     if (j + 1 < nblocks) load_kv(j + 1, (j + 1) & 1);
     cp_async_commit();
@@ -262,10 +308,26 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const FwdParams p) {
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) load_a(sq, warp * 16, ks, lane, qf[ks]);
     }
+    if (j > 0 && j % CHUNK_BLOCKS == 0) {  // chunk boundary: fold the finished chunk in
+      merge_chunk();
+#pragma unroll
+      for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      m[0] = m[1] = -INFINITY;
+      l[0] = l[1] = 0.f;
+    }
     kv_block_update(qf, sk[j & 1], sv[j & 1], j * BN, qpos0, qpos1, p.scale_log2, m, l, o, lane);
     __syncthreads();
   }
   cp_async_wait<0>();
+  if (nblocks > CHUNK_BLOCKS) {
+    merge_chunk();
+#pragma unroll
+    for (int n = 0; n < 16; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[n][i] = otot[(n * 4 + i) * 128 + tid];
+    m[0] = Mt[0]; m[1] = Mt[1];
+    l[0] = Lt[0]; l[1] = Lt[1];
+  }
   const bool ok0 = qpos0 < len, ok1 = qpos1 < len;
   __nv_bfloat16* out0 = p.o + (long long)(start + qpos0) * p.o_stride + (long long)h * D;
   __nv_bfloat16* out1 = p.o + (long long)(start + qpos1) * p.o_stride + (long long)h * D;
@@ -287,9 +349,12 @@ struct DecParams {
   const int* ctx_lens;      // [B] number of valid keys (query position = ctx_len - 1)
   int max_pages, nq, nkv;
   float scale_log2;
+  float* ws_o;              // [B, nq, nsplit_max, 128] chunk partial outputs (unnormalised)
+  float* ws_ml;             // [B, nq, nsplit_max, 2]   chunk partial (m, l)
+  int nsplit_max;
 };
 
-constexpr int DEC_STAGES = 2;
+constexpr int DEC_STAGES = 3;
 
 __global__ void __launch_bounds__(32) attn_decode_kernel(const DecParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -300,47 +365,102 @@ __global__ void __launch_bounds__(32) attn_decode_kernel(const DecParams p) {
   const int ctx = p.ctx_lens[b];
   if (ctx <= 0) return;
   const int qpos = ctx - 1;
+  const int nblocks_all = qpos / BN + 1;
+  const int nsplit = (nblocks_all + CHUNK_BLOCKS - 1) / CHUNK_BLOCKS;
+  const int split = blockIdx.z;
+  if (split >= nsplit) return;
+  const int jbeg = split * CHUNK_BLOCKS;
+  const int nblocks = min(nblocks_all - jbeg, CHUNK_BLOCKS);
   const __nv_bfloat16* qbase = p.q + ((long long)b * p.nq + (long long)hk * G) * D;
   load_tile(sq, qbase, [&](int r) { return (long long)r * D; }, G, lane, 32);
-  const int nblocks = qpos / BN + 1;
   const long long kstride = (long long)p.nkv * D;
   auto kv_tile = [&](int j, int which) {
     return sq + TILE_BYTES + (uint32_t)((j % DEC_STAGES) * 2 + which) * TILE_BYTES;
   };
-  auto load_kv = [&](int j) {
-    const int page = p.page_table[(long long)b * p.max_pages + j];
-    const int kv = min(BN, ctx - j * BN);
+  auto load_kv = [&](int j) {  // j: block index local to this split
+    const int jj = jbeg + j;
+    const int page = p.page_table[(long long)b * p.max_pages + jj];
+    const int kv = min(BN, ctx - jj * BN);
     const long long slot0 = (long long)page * BN;
     load_tile(kv_tile(j, 0), p.kc + slot0 * kstride + (long long)hk * D,
               [&](int r) { return (long long)r * kstride; }, kv, lane, 32);
     load_tile(kv_tile(j, 1), p.vc + slot0 * kstride + (long long)hk * D,
               [&](int r) { return (long long)r * kstride; }, kv, lane, 32);
   };
-  load_kv(0);
-  cp_async_commit();
+#pragma unroll
+  for (int s = 0; s < DEC_STAGES - 1; ++s) {
+    if (s < nblocks) load_kv(s);
+    cp_async_commit();
+  }
   float o[16][4];
 #pragma unroll
   for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
   uint32_t qf[8][4];
   for (int j = 0; j < nblocks; ++j) {
-    if (j + 1 < nblocks) load_kv(j + 1);
+    if (j + DEC_STAGES - 1 < nblocks) load_kv(j + DEC_STAGES - 1);
     cp_async_commit();
-    cp_async_wait<1>();
+    cp_async_wait<DEC_STAGES - 1>();
     __syncwarp();
     if (j == 0) {
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) load_a(sq, 0, ks, lane, qf[ks]);
     }
-    kv_block_update(qf, kv_tile(j, 0), kv_tile(j, 1), j * BN, qpos, qpos, p.scale_log2, m, l, o,
-                    lane);
+    kv_block_update(qf, kv_tile(j, 0), kv_tile(j, 1), (jbeg + j) * BN, qpos, qpos, p.scale_log2,
+                    m, l, o, lane);
     __syncwarp();
   }
   cp_async_wait<0>();
-  const int g = lane >> 2;
-  __nv_bfloat16* out0 = p.o + ((long long)b * p.nq + (long long)hk * G + g) * D;
-  __nv_bfloat16* out1 = out0 + 8 * D;
-  finish_rows(o, m, l, out0, out1, g < G, g + 8 < G, nullptr, nullptr, lane);
+  const int g = lane >> 2, c = lane & 3;
+  if (nsplit == 1) {
+    __nv_bfloat16* out0 = p.o + ((long long)b * p.nq + (long long)hk * G + g) * D;
+    __nv_bfloat16* out1 = out0 + 8 * D;
+    finish_rows(o, m, l, out0, out1, g < G, g + 8 < G, nullptr, nullptr, lane);
+    return;
+  }
+  // several chunks: publish this chunk's partial for the combine kernel
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = g + r * 8;
+    if (row >= G) continue;
+    const long long base = ((long long)b * p.nq + (long long)hk * G + row) * p.nsplit_max + split;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      const int col = n * 8 + 2 * c;
+      p.ws_o[base * D + col] = o[n][r * 2];
+      p.ws_o[base * D + col + 1] = o[n][r * 2 + 1];
+    }
+    if (c == 0) {
+      p.ws_ml[base * 2] = m[r];
+      p.ws_ml[base * 2 + 1] = l[r];
+    }
+  }
+}
+
+// Merge the chunk partials of every (sequence, query head) in chunk order (same operations as
+// the prefill kernel's in-register merge) and write the bf16 output. One warp per row; lane
+// owns columns lane*4 .. lane*4+3.
+__global__ void attn_decode_combine_kernel(const DecParams p, int B) {
+  const long long w = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long long)B * p.nq) return;
+  const int b = (int)(w / p.nq);
+  const int ctx = p.ctx_lens[b];
+  if (ctx <= 0) return;
+  const int nsplit = ((ctx - 1) / BN + 1 + CHUNK_BLOCKS - 1) / CHUNK_BLOCKS;
+  if (nsplit <= 1) return;
+  float M = -INFINITY, L = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < nsplit; ++s) {
+    const long long base = w * p.nsplit_max + s;
+    float fa, fb;
+    merge_stats(M, L, p.ws_ml[base * 2], p.ws_ml[base * 2 + 1], fa, fb);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) O[i] = merge_val(O[i], p.ws_o[base * D + lane * 4 + i], fa, fb);
+  }
+  const float inv = L > 0.f ? __frcp_rn(L) : 0.f;
+  __nv_bfloat16* out = p.o + w * D + lane * 4;
+  *reinterpret_cast<uint32_t*>(out) = pack2(__fmul_rn(O[0], inv), __fmul_rn(O[1], inv));
+  *reinterpret_cast<uint32_t*>(out + 2) = pack2(__fmul_rn(O[2], inv), __fmul_rn(O[3], inv));
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -631,7 +751,7 @@ extern "C" int mb_attn_fwd(const void* q, const void* k, const void* v, void* o,
   FwdParams p{(const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
               (__nv_bfloat16*)o, lse, cu_seqlens, blk_seq, blk_idx, q_stride, k_stride, v_stride,
               o_stride, nq, nkv, T, softmax_scale * 1.4426950408889634f};
-  const int smem = 5 * TILE_BYTES;
+  const int smem = 5 * TILE_BYTES + 64 * 128 * (int)sizeof(float);  // + merged-chunk totals
   static bool set = false;
   if (!set) {
     cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -641,21 +761,35 @@ extern "C" int mb_attn_fwd(const void* q, const void* k, const void* v, void* o,
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+// Number of 1024-key chunks a decode over `max_pages` pages can need (workspace sizing).
+extern "C" int mb_attn_decode_nsplit(int max_pages) {
+  return (max_pages + CHUNK_BLOCKS - 1) / CHUNK_BLOCKS;
+}
+
+// ws_o: float [B, nq, nsplit_max, 128]; ws_ml: float [B, nq, nsplit_max, 2] (only touched when a
+// sequence spans more than one 1024-key chunk).
 extern "C" int mb_attn_decode(const void* q, const void* kc, const void* vc, void* o,
                               const int* page_table, const int* ctx_lens, int B, int max_pages,
-                              int nq, int nkv, float softmax_scale, cudaStream_t st) {
+                              int nq, int nkv, float softmax_scale, float* ws_o, float* ws_ml,
+                              cudaStream_t st) {
   if (B == 0) return 0;
   if (nq % nkv || nq / nkv > 16) return -1;
+  const int nsplit_max = (max_pages + CHUNK_BLOCKS - 1) / CHUNK_BLOCKS;
+  if (nsplit_max > 1 && (!ws_o || !ws_ml)) return -3;
   DecParams p{(const __nv_bfloat16*)q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc,
               (__nv_bfloat16*)o, page_table, ctx_lens, max_pages, nq, nkv,
-              softmax_scale * 1.4426950408889634f};
+              softmax_scale * 1.4426950408889634f, ws_o, ws_ml, nsplit_max};
   const int smem = (1 + 2 * DEC_STAGES) * TILE_BYTES;
   static bool set = false;
   if (!set) {
     cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     set = true;
   }
-  attn_decode_kernel<<<dim3(B, nkv), 32, smem, st>>>(p);
+  attn_decode_kernel<<<dim3(B, nkv, nsplit_max), 32, smem, st>>>(p);
+  if (nsplit_max > 1) {
+    const long long w = (long long)B * nq;
+    attn_decode_combine_kernel<<<(unsigned)((w + 7) / 8), 256, 0, st>>>(p, B);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

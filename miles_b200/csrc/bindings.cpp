@@ -163,11 +163,13 @@ int64_t attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tenso
                        PT<int>(blk_idx), blk_seq.numel(), q.stride(0), k.stride(0), v.stride(0),
                        o.stride(0), nq, nkv, q.size(0), (float)scale, cur_stream());
 }
+int64_t attn_decode_nsplit(int64_t max_pages) { return mb_attn_decode_nsplit(max_pages); }
 int64_t attn_decode(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor o,
                  torch::Tensor page_table, torch::Tensor ctx_lens, int64_t nq, int64_t nkv,
-                 double scale) {
+                 double scale, OT ws_o, OT ws_ml) {
   return mb_attn_decode(P(q), P(kc), P(vc), P(o), PT<int>(page_table), PT<int>(ctx_lens),
-                          q.size(0), page_table.size(1), nq, nkv, (float)scale, cur_stream());
+                          q.size(0), page_table.size(1), nq, nkv, (float)scale, PT<float>(ws_o),
+                          PT<float>(ws_ml), cur_stream());
 }
 int64_t attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
               torch::Tensor dout, torch::Tensor lse, torch::Tensor delta, torch::Tensor dq,
@@ -258,6 +260,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine_bwd", &moe_combine_bwd);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_decode", &attn_decode);
+  m.def("attn_decode_nsplit", &attn_decode_nsplit);
   m.def("attn_bwd", &attn_bwd);
   m.def("logprob_fwd", &logprob_fwd);
   m.def("logprob_bwd", &logprob_bwd);

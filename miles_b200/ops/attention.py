@@ -16,6 +16,7 @@ from miles_b200.ops._lib import lib, use_native
 
 BLOCK = 64
 PAGE = 64  # KV-cache page size (tokens); equals the attention key block
+CHUNK_PAGES = 16  # keys are merged in canonical 1024-key chunks (csrc/attention.cu)
 
 
 def block_table(cu_seqlens: list[int], device) -> tuple[torch.Tensor, torch.Tensor]:
@@ -141,5 +142,12 @@ def decode_attention(q, k_cache, v_cache, page_table, ctx_lens, scale: float | N
         return r
     if out is None:
         out = torch.empty_like(q)
-    lib().attn_decode(q, k_cache, v_cache, out, page_table, ctx_lens, nq, nkv, scale)
+    # keys are processed in 1024-key chunks merged in a fixed order (the same chunking the
+    # training kernel uses); long contexts split across CTAs and need a small fp32 workspace
+    nsplit = (page_table.shape[1] + CHUNK_PAGES - 1) // CHUNK_PAGES
+    ws_o = ws_ml = None
+    if nsplit > 1:
+        ws_o = torch.empty(B * nq * nsplit * D, dtype=torch.float32, device=q.device)
+        ws_ml = torch.empty(B * nq * nsplit * 2, dtype=torch.float32, device=q.device)
+    lib().attn_decode(q, k_cache, v_cache, out, page_table, ctx_lens, nq, nkv, scale, ws_o, ws_ml)
     return out

@@ -169,7 +169,7 @@ def _packed(lens, nq, nkv, seed=5):
 
 def test_attention_fwd_bwd():
     from miles_b200.ops.attention import VarlenMeta, attention_ref, varlen_attention
-    q, k, v, cu = _packed([1, 63, 64, 65, 200, 7], 8, 2)
+    q, k, v, cu = _packed([1, 63, 64, 65, 200, 7, 1300], 8, 2)
     meta = VarlenMeta(cu, DEV)
     q.requires_grad_(); k.requires_grad_(); v.requires_grad_()
     o = varlen_attention(q, k, v, meta)
@@ -188,21 +188,21 @@ def test_decode_matches_prefill_bitwise():
     """Rollout decode rows are bitwise equal to the corresponding training-forward rows."""
     from miles_b200.ops.attention import VarlenMeta, decode_attention, varlen_attention
     nq, nkv = 8, 2
-    lens = [5, 64, 130]
+    lens = [5, 64, 130, 2500, 1025, 1024]
     q, k, v, cu = _packed(lens, nq, nkv, seed=6)
     meta = VarlenMeta(cu, DEV)
     o = varlen_attention(q, k, v, meta)
     B = len(lens)
-    max_pages = 4
+    max_pages = 40
     nslots = B * max_pages * 64
     kc = torch.full((nslots, nkv, 128), float("nan"), device=DEV, dtype=BF)
     vc = torch.full((nslots, nkv, 128), float("nan"), device=DEV, dtype=BF)
     pt = torch.arange(B * max_pages, dtype=torch.int32, device=DEV).view(B, max_pages).flip(1).contiguous()
     for b, L in enumerate(lens):
-        for t in range(L):
-            page = int(pt[b, t // 64])
-            kc[page * 64 + t % 64] = k[cu[b] + t]
-            vc[page * 64 + t % 64] = v[cu[b] + t]
+        t = torch.arange(L, device=DEV)
+        slots = pt[b].long()[t // 64] * 64 + t % 64
+        kc[slots] = k[cu[b]:cu[b + 1]]
+        vc[slots] = v[cu[b]:cu[b + 1]]
     qd = torch.stack([q[cu[b + 1] - 1] for b in range(B)])
     ctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
     od = decode_attention(qd, kc, vc, pt, ctx)
