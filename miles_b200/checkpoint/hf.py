@@ -1,0 +1,166 @@
+"""HuggingFace safetensors import / export with per-family name mapping.
+
+Our flat parameter layout fuses projections (qkv_proj = [q; k; v], gate_up_proj = [gate; up],
+experts.w1 = E x [gate; up], experts.w2 = E x down). The converters split / join them to the HF
+names of Qwen2/Qwen3 (dense), Qwen3-MoE and DeepSeek-V3-style MoE checkpoints, stream shards of
+at most `max_shard_bytes`, and write `model.safetensors.index.json`.
+
+Reference: megatron_to_hf/* (qwen3moe.py:65-76 QKV split, gate/up chunk, expert indices,
+router and e_score_correction_bias names), tools/convert_torch_dist_to_hf.py,
+megatron_utils/model.py save_hf (:718-772).
+"""
+from __future__ import annotations
+
+import json
+import os
+from typing import Iterator
+
+import torch
+from safetensors import safe_open
+from safetensors.torch import save_file
+
+from miles_b200.models.config import ModelConfig
+from miles_b200.models.transformer import Transformer
+
+
+def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
+    """Yield (hf_name, tensor) for every parameter, splitting fused projections."""
+    cfg = model.cfg
+    H, D, nq, nkv = cfg.hidden_size, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads
+    P = model.params
+    pre = "model."
+    yield pre + "embed_tokens.weight", P["embed_tokens.weight"].data
+    for i in range(cfg.num_layers):
+        L = f"layers.{i}."
+        yield pre + L + "input_layernorm.weight", P[L + "input_layernorm.weight"].data
+        yield pre + L + "post_attention_layernorm.weight", P[L + "post_attention_layernorm.weight"].data
+        qkv = P[L + "self_attn.qkv_proj.weight"].data
+        q, k, v = torch.split(qkv, [nq * D, nkv * D, nkv * D], 0)
+        yield pre + L + "self_attn.q_proj.weight", q
+        yield pre + L + "self_attn.k_proj.weight", k
+        yield pre + L + "self_attn.v_proj.weight", v
+        yield pre + L + "self_attn.o_proj.weight", P[L + "self_attn.o_proj.weight"].data
+        if cfg.qk_norm:
+            yield pre + L + "self_attn.q_norm.weight", P[L + "self_attn.q_norm.weight"].data
+            yield pre + L + "self_attn.k_norm.weight", P[L + "self_attn.k_norm.weight"].data
+        if cfg.layer_is_moe(i):
+            yield pre + L + "mlp.gate.weight", P[L + "mlp.gate.weight"].data
+            if L + "mlp.gate.e_score_correction_bias" in P:
+                yield pre + L + "mlp.gate.e_score_correction_bias", P[L + "mlp.gate.e_score_correction_bias"].data
+            w1 = P[L + "mlp.experts.w1"].data
+            w2 = P[L + "mlp.experts.w2"].data
+            I = cfg.moe_intermediate_size
+            for e in range(w1.shape[0]):
+                yield pre + L + f"mlp.experts.{e}.gate_proj.weight", w1[e, :I]
+                yield pre + L + f"mlp.experts.{e}.up_proj.weight", w1[e, I:]
+                yield pre + L + f"mlp.experts.{e}.down_proj.weight", w2[e]
+            if cfg.num_shared_experts:
+                gu = P[L + "mlp.shared_experts.gate_up_proj.weight"].data
+                Is = gu.shape[0] // 2
+                yield pre + L + "mlp.shared_experts.gate_proj.weight", gu[:Is]
+                yield pre + L + "mlp.shared_experts.up_proj.weight", gu[Is:]
+                yield pre + L + "mlp.shared_experts.down_proj.weight", P[L + "mlp.shared_experts.down_proj.weight"].data
+        else:
+            gu = P[L + "mlp.gate_up_proj.weight"].data
+            I = gu.shape[0] // 2
+            yield pre + L + "mlp.gate_proj.weight", gu[:I]
+            yield pre + L + "mlp.up_proj.weight", gu[I:]
+            yield pre + L + "mlp.down_proj.weight", P[L + "mlp.down_proj.weight"].data
+    yield pre + "norm.weight", P["norm.weight"].data
+    if not cfg.tie_embeddings:
+        yield "lm_head.weight", P["lm_head.weight"].data
+
+
+def hf_config_dict(cfg: ModelConfig) -> dict:
+    d = {"vocab_size": cfg.vocab_size, "hidden_size": cfg.hidden_size,
+         "num_hidden_layers": cfg.num_layers, "num_attention_heads": cfg.num_heads,
+         "num_key_value_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
+         "intermediate_size": cfg.intermediate_size, "rms_norm_eps": cfg.rms_eps,
+         "rope_theta": cfg.rope_theta, "rope_scaling": cfg.rope_scaling,
+         "max_position_embeddings": cfg.max_position, "tie_word_embeddings": cfg.tie_embeddings,
+         "torch_dtype": "bfloat16"}
+    if cfg.arch == "qwen3_moe":
+        d.update(model_type="qwen3_moe", architectures=["Qwen3MoeForCausalLM"],
+                 num_experts=cfg.num_experts, num_experts_per_tok=cfg.topk,
+                 moe_intermediate_size=cfg.moe_intermediate_size, norm_topk_prob=cfg.norm_topk_prob,
+                 decoder_sparse_step=1, mlp_only_layers=[])
+    elif cfg.arch == "deepseek_v3":
+        d.update(model_type="deepseek_v3", architectures=["DeepseekV3ForCausalLM"],
+                 n_routed_experts=cfg.num_experts, num_experts_per_tok=cfg.topk,
+                 moe_intermediate_size=cfg.moe_intermediate_size, n_shared_experts=cfg.num_shared_experts,
+                 first_k_dense_replace=cfg.first_k_dense, scoring_func=cfg.router_score,
+                 n_group=cfg.n_group, topk_group=cfg.topk_group,
+                 routed_scaling_factor=cfg.routed_scaling_factor, norm_topk_prob=cfg.norm_topk_prob)
+    else:
+        d.update(model_type="qwen3", architectures=["Qwen3ForCausalLM"])
+    return d
+
+
+def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> None:
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(hf_config_dict(model.cfg), f, indent=2)
+    shard, size, idx, weight_map = {}, 0, 0, {}
+    total = 0
+
+    def flush():
+        nonlocal shard, size, idx
+        if not shard:
+            return
+        idx += 1
+        fn = f"model-{idx:05d}.safetensors"
+        save_file(shard, os.path.join(path, fn), metadata={"format": "pt"})
+        for n in shard:
+            weight_map[n] = fn
+        shard, size = {}, 0
+
+    for name, t in to_hf_tensors(model):
+        t = t.detach().to("cpu").contiguous().clone()
+        nb = t.numel() * t.element_size()
+        if size + nb > max_shard_bytes:
+            flush()
+        shard[name] = t
+        size += nb
+        total += nb
+    flush()
+    with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {"total_size": total}, "weight_map": weight_map}, f, indent=1)
+
+
+def _open_all(path: str) -> dict[str, str]:
+    idx = os.path.join(path, "model.safetensors.index.json")
+    if os.path.exists(idx):
+        with open(idx) as f:
+            return json.load(f)["weight_map"]
+    files = [f for f in os.listdir(path) if f.endswith(".safetensors")]
+    m = {}
+    for fn in files:
+        with safe_open(os.path.join(path, fn), "pt") as f:
+            for k in f.keys():
+                m[k] = fn
+    return m
+
+
+@torch.no_grad()
+def load_hf(model: Transformer, path: str) -> None:
+    """Load an HF checkpoint into the flat parameter buffer (joins fused projections)."""
+    cfg = model.cfg
+    wmap = _open_all(path)
+    handles: dict[str, object] = {}
+
+    def get(name):
+        fn = wmap[name]
+        if fn not in handles:
+            handles[fn] = safe_open(os.path.join(path, fn), "pt")
+        return handles[fn].get_tensor(name)
+
+    targets = dict(to_hf_tensors(model))  # views into model.flat
+    for name, dst in targets.items():
+        src_name = name
+        if src_name not in wmap and src_name.startswith("model.") is False and ("model." + src_name) in wmap:
+            src_name = "model." + src_name
+        if src_name not in wmap:
+            if name == "lm_head.weight" and cfg.tie_embeddings:
+                continue
+            raise KeyError(f"{name} missing from {path}")
+        dst.copy_(get(src_name).to(dst.dtype))

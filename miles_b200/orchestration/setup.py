@@ -1,0 +1,122 @@
+"""Process-level setup shared by train.py / train_async.py: distributed init, model, engine,
+actor, tokenizer and the rollout manager for this GPU process.
+
+Reference: miles/ray/placement_group.py (create_*), miles/ray/train_actor.py (init:
+env ranks, init_process_group(nccl) + gloo group :30-104), megatron_utils/actor.py init
+(:52-194: model, optimizer, checkpoint load, ref backup, weight updater).
+"""
+from __future__ import annotations
+
+import json
+import os
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from miles_b200.engine.engine import RolloutEngine
+from miles_b200.models.config import ModelConfig, preset
+from miles_b200.models.transformer import Transformer
+from miles_b200.ops.rl import PolicyLossCfg
+from miles_b200.trainer.actor import Actor, ActorConfig
+
+
+@dataclass
+class ProcessContext:
+    rank: int
+    world: int
+    local_rank: int
+    device: torch.device
+    dp_group: object = None
+    gloo_group: object = None
+
+
+def init_distributed(args) -> ProcessContext:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    use_cuda = torch.cuda.is_available() and not os.environ.get("MILES_B200_FORCE_CPU")
+    if use_cuda:
+        torch.cuda.set_device(local)
+        dev = torch.device("cuda", local)
+    else:
+        dev = torch.device("cpu")
+    dp = gloo = None
+    if world > 1 and not dist.is_initialized():
+        import datetime
+
+        backend = "nccl" if use_cuda else "gloo"
+        kw = {"device_id": dev} if use_cuda else {}
+        dist.init_process_group(backend, timeout=datetime.timedelta(minutes=args.distributed_timeout_minutes), **kw)
+    if world > 1:
+        dp = dist.group.WORLD
+        gloo = dist.new_group(backend="gloo") if use_cuda else dp
+    return ProcessContext(rank, world, local, dev, dp, gloo)
+
+
+def model_config(args) -> ModelConfig:
+    if args.model_name:
+        return preset(args.model_name)
+    if args.hf_checkpoint:
+        return ModelConfig.from_hf(args.hf_checkpoint)
+    raise ValueError("pass --model-name <preset> or --hf-checkpoint <dir>")
+
+
+def load_tokenizer(args):
+    if not args.hf_checkpoint or not os.path.isdir(args.hf_checkpoint):
+        return None
+    try:
+        from transformers import AutoTokenizer
+
+        return AutoTokenizer.from_pretrained(args.hf_checkpoint, trust_remote_code=True)
+    except Exception:
+        return None
+
+
+def build_model(args, ctx: ProcessContext) -> Transformer:
+    cfg = model_config(args)
+    dtype = torch.bfloat16 if ctx.device.type == "cuda" else torch.float32
+    model = Transformer(cfg, device=ctx.device, dtype=dtype, seed=args.seed)
+    loaded = False
+    if args.load:
+        from miles_b200.checkpoint.torch_dist import is_torch_dist
+
+        if is_torch_dist(args.load):
+            loaded = True  # the actor loads it (with optimizer state) once built
+    if not loaded and args.hf_checkpoint and os.path.isdir(args.hf_checkpoint) and any(
+            f.endswith(".safetensors") for f in os.listdir(args.hf_checkpoint)):
+        from miles_b200.checkpoint.hf import load_hf
+
+        load_hf(model, args.hf_checkpoint)
+    return model
+
+
+def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
+    loss = PolicyLossCfg(eps_clip=args.eps_clip, eps_clip_high=args.eps_clip_high,
+                         eps_clip_c=args.eps_clip_c, use_tis=args.use_tis,
+                         tis_clip_low=args.tis_clip_low, tis_clip=args.tis_clip,
+                         kl_coef=args.kl_loss_coef if args.use_kl_loss else 0.0,
+                         kl_type=args.kl_loss_type if args.use_kl_loss else "none")
+    placement = "host" if args.optimizer_cpu_offload else "auto"
+    cfg = ActorConfig(lr=args.lr, betas=(args.adam_beta1, args.adam_beta2),
+                      weight_decay=args.weight_decay, clip_grad=args.clip_grad,
+                      max_tokens_per_gpu=args.max_tokens_per_gpu or 16384, loss=loss,
+                      entropy_coef=args.entropy_coef, per_token_loss=args.calculate_per_token_loss,
+                      temperature=args.rollout_temperature,
+                      use_rollout_logprobs=args.use_rollout_logprobs,
+                      use_routing_replay=args.use_routing_replay,
+                      grad_dtype=torch.float32 if (ctx.device.type != "cuda" or args.accumulate_allreduce_grads_in_fp32) else torch.bfloat16,
+                      optimizer_placement=placement,
+                      logprob_chunk=args.log_probs_chunk_size if args.log_probs_chunk_size > 0 else 4096)
+    return Actor(model, cfg, dp_group=ctx.dp_group)
+
+
+def build_engine(args, model: Transformer, ctx: ProcessContext) -> RolloutEngine:
+    mem = float(args.sglang_args.get("mem_fraction_static", 0.85)) if hasattr(args, "sglang_args") else 0.85
+    max_len = (args.rollout_max_prompt_len or 1024) + (args.rollout_max_response_len or 1024)
+    if args.rollout_max_context_len:
+        max_len = max(max_len, args.rollout_max_context_len)
+    return RolloutEngine(model, max_batch=args.rollout_max_batch,
+                         num_pages=None if ctx.device.type == "cuda" else 4096,
+                         mem_fraction=mem, use_cuda_graph=not args.no_cuda_graph,
+                         max_pages_per_seq=(max_len + 63) // 64 + 1)

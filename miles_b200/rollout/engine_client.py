@@ -1,0 +1,139 @@
+"""Engine clients used by rollout / generate functions.
+
+Rollout code talks to an engine through one async call,
+
+    await client.generate(input_ids, sampling_params, return_logprob=True,
+                          return_routed_experts=False) -> dict
+
+whose result mirrors an SGLang /generate response ({"output_ids", "text", "meta_info": {
+"finish_reason": {"type": ...}, "output_token_logprobs": [(logp, token_id, None), ...],
+"routed_experts", "weight_version"}}), so user generate functions written for the reference
+keep working.
+
+  * LocalEngineClient batches concurrent requests from many asyncio tasks into calls of the
+    in-process RolloutEngine (running in a worker thread so `abort()` stays responsive).
+  * HttpEngineClient posts to an engine server / router URL.
+
+Reference: sglang_rollout.py generate (:131-231, HTTP POST /generate, abort :333-374).
+"""
+from __future__ import annotations
+
+import asyncio
+import threading
+import time
+
+import numpy as np
+
+from miles_b200.engine.engine import GenRequest, RolloutEngine
+
+
+def _result_dict(res, tokenizer=None) -> dict:
+    text = tokenizer.decode(res.tokens) if tokenizer is not None else ""
+    meta = {
+        "finish_reason": {"type": res.finish_reason},
+        "output_token_logprobs": [(lp, t, None) for lp, t in zip(res.logprobs, res.tokens)],
+        "completion_tokens": len(res.tokens),
+        "weight_version": str(res.weight_version),
+    }
+    if res.routed_experts is not None:
+        meta["routed_experts"] = res.routed_experts
+    return {"output_ids": res.tokens, "text": text, "meta_info": meta}
+
+
+class LocalEngineClient:
+    def __init__(self, engine: RolloutEngine, tokenizer=None, max_wait_s: float = 0.002,
+                 max_batch: int | None = None):
+        self.engine = engine
+        self.tokenizer = tokenizer
+        self.max_wait_s = max_wait_s
+        self.max_batch = max_batch or engine.max_batch * 8
+        self._pending: list[tuple[GenRequest, asyncio.Future]] = []
+        self._lock = threading.Lock()
+        self._runner: asyncio.Task | None = None
+        self._rid = 0
+        self.num_requests = 0
+
+    async def generate(self, input_ids: list[int], sampling_params: dict,
+                       return_logprob: bool = True, return_routed_experts: bool = False) -> dict:
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        self._rid += 1
+        stop = tuple(sampling_params.get("stop_token_ids") or ())
+        temp = float(sampling_params.get("temperature", 1.0))
+        req = GenRequest(prompt=list(input_ids),
+                         max_new_tokens=int(sampling_params.get("max_new_tokens", 128)),
+                         temperature=temp, seed=int(sampling_params.get("sampling_seed", self._rid)),
+                         stop_token_ids=stop, return_routed_experts=return_routed_experts,
+                         rid=self._rid)
+        self._pending.append((req, fut))
+        self.num_requests += 1
+        if self._runner is None or self._runner.done():
+            self._runner = asyncio.ensure_future(self._run())
+        res = await fut
+        return _result_dict(res, self.tokenizer)
+
+    async def _run(self):
+        loop = asyncio.get_running_loop()
+        while self._pending:
+            await asyncio.sleep(self.max_wait_s)
+            batch, self._pending = self._pending[: self.max_batch], self._pending[self.max_batch:]
+            reqs = [r for r, _ in batch]
+            try:
+                results = await loop.run_in_executor(None, self.engine.generate, reqs)
+            except Exception as e:  # propagate to every waiter
+                for _, f in batch:
+                    if not f.done():
+                        f.set_exception(e)
+                continue
+            for (_, f), r in zip(batch, results):
+                if not f.done():
+                    f.set_result(r)
+
+    def abort(self):
+        """Abort in-flight generations (they finish with finish_reason 'abort')."""
+        self.engine.abort()
+        for req, f in self._pending:
+            if not f.done():
+                from miles_b200.engine.engine import GenResult
+                f.set_result(GenResult(req.rid, [], [], "abort"))
+        self._pending = []
+
+    async def health(self) -> bool:
+        return True
+
+
+class HttpEngineClient:
+    """Client of an engine server (miles_b200.rollout.server) or of the router."""
+
+    def __init__(self, url: str, timeout: float | None = None):
+        self.url = url.rstrip("/")
+        self.timeout = timeout
+
+    async def generate(self, input_ids, sampling_params, return_logprob=True,
+                       return_routed_experts=False) -> dict:
+        from miles_b200.utils.http_utils import post
+
+        out = await post(f"{self.url}/generate", {
+            "input_ids": list(input_ids), "sampling_params": sampling_params,
+            "return_logprob": return_logprob, "return_routed_experts": return_routed_experts})
+        re_ = out.get("meta_info", {}).get("routed_experts")
+        if isinstance(re_, list):
+            out["meta_info"]["routed_experts"] = np.asarray(re_, dtype=np.int32)
+        return out
+
+    def abort(self):
+        import requests
+
+        try:
+            requests.post(f"{self.url}/abort_request", json={"abort_all": True}, timeout=10)
+        except Exception:
+            pass
+
+    async def health(self) -> bool:
+        from miles_b200.utils.http_utils import get
+
+        try:
+            await get(f"{self.url}/health_generate")
+            return True
+        except Exception:
+            return False

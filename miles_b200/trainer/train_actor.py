@@ -1,0 +1,129 @@
+"""Per-GPU training actor: turns one rollout's data into policy updates.
+
+    train(rollout_id, data):
+      old log-probs   (forward with the current = rollout weights; bitwise equal to the
+                       engine's, so --use-rollout-logprobs skips it with no change in value)
+      ref log-probs   (--use-kl-loss / --kl-coef: weights swapped in from a pinned host backup)
+      advantages      (GRPO/GSPO/RF++/RF++-baseline/PPO/OPD)
+      num_steps_per_rollout optimizer steps over the rollout's samples
+      CI checks       (--ci-test: ppo_kl / clipfrac / kl_loss ~ 0 on-policy; log-prob equality)
+
+Also provides the named weight backups (actor / ref / old_actor) used for model switching.
+
+Reference: megatron_utils/actor.py (train_actor :367-466, switch_model :559-583,
+TensorBackuper usage :136-156), utils/tensor_backper.py:10-115,
+training_utils/ci_utils.py:12-24, training_utils/log_utils.py:171-200.
+"""
+from __future__ import annotations
+
+import time
+
+import numpy as np
+import torch
+
+from miles_b200.trainer.actor import Actor
+from miles_b200.trainer.advantages import compute_advantages, data_to_items
+
+
+class TensorBackuper:
+    """Pinned host copies of the flat parameter buffer under named tags."""
+
+    def __init__(self, model, enabled: bool = True):
+        self.model = model
+        self.enabled = enabled
+        self.backups: dict[str, torch.Tensor] = {}
+
+    def backup(self, tag: str):
+        if not self.enabled:
+            return
+        src = self.model.flat
+        dst = self.backups.get(tag)
+        if dst is None:
+            dst = torch.empty(src.numel(), dtype=src.dtype, pin_memory=src.is_cuda)
+            self.backups[tag] = dst
+        dst.copy_(src, non_blocking=True)
+        if src.is_cuda:
+            torch.cuda.current_stream().synchronize()
+
+    def restore(self, tag: str):
+        self.model.flat.copy_(self.backups[tag], non_blocking=True)
+
+    def hash(self, tag: str | None = None) -> int:
+        t = self.backups[tag] if tag else self.model.flat
+        return int(t.view(torch.int16).to(torch.int64).sum().item()) if t.numel() else 0
+
+
+class TrainActor:
+    def __init__(self, args, actor: Actor, dp_group=None):
+        self.args = args
+        self.actor = actor
+        self.model = actor.model
+        self.dp_group = dp_group
+        self.backuper = TensorBackuper(self.model, enabled=not args.disable_weights_backuper)
+        self.need_ref = bool(args.use_kl_loss or args.kl_coef)
+        self.metrics: dict = {}
+
+    def init_ref(self):
+        """The reference policy is the initial weights (or --ref-load, loaded by the caller)."""
+        if self.need_ref:
+            self.backuper.backup("ref")
+
+    def _switch(self, tag: str):
+        self.backuper.backup("actor")
+        self.backuper.restore(tag)
+
+    def train(self, rollout_id: int, data: dict) -> dict:
+        a = self.args
+        t0 = time.perf_counter()
+        items = data_to_items(data)
+        old = None
+        if not a.use_rollout_logprobs:
+            old = self.actor.compute_logprobs(items)
+            for it, o in zip(items, old):
+                it.old_logp = o
+        t1 = time.perf_counter()
+        ref = None
+        if self.need_ref:
+            self._switch("ref")
+            ref = self.actor.compute_logprobs(items)
+            self.backuper.restore("actor")
+            for it, r in zip(items, ref):
+                it.ref_logp = r
+        logp = old if old is not None else [np.asarray(it.rollout_logp) for it in items]
+        if not a.disable_compute_advantages_and_returns:
+            advs, _ = compute_advantages(a, data, log_probs=logp, ref_log_probs=ref, dp_group=self.dp_group)
+            for it, adv in zip(items, advs):
+                it.advantage = adv
+        m = {}
+        if old is not None and items and items[0].rollout_logp is not None:
+            d = np.concatenate([np.abs(o - np.asarray(it.rollout_logp, np.float32)) for it, o in zip(items, old)])
+            m["train/train_rollout_logprob_abs_diff"] = float(d.mean()) if d.size else 0.0
+        steps = a.num_steps_per_rollout or 1
+        per = (len(items) + steps - 1) // steps
+        for s in range(steps):
+            sub = items[s * per:(s + 1) * per]
+            if not sub:
+                continue
+            out = self.actor.train_step(sub, global_num_samples=len(sub) * (
+                torch.distributed.get_world_size(self.dp_group) if self.dp_group is not None else 1))
+            for k, v in out.items():
+                m[f"train/{k}" if "/" not in k else k] = v
+        t2 = time.perf_counter()
+        m["perf/log_probs_time"] = t1 - t0
+        m["perf/actor_train_time"] = t2 - t1
+        n_tok = sum(len(t) for t in data["tokens"])
+        m["perf/actor_train_tok_per_s"] = n_tok / max(t2 - t1, 1e-9)
+        if a.ci_test:
+            self.ci_checks(rollout_id, m)
+        self.metrics = m
+        return m
+
+    def ci_checks(self, rollout_id: int, m: dict):
+        """On-policy invariants (reference training_utils/ci_utils.py:12-24)."""
+        if rollout_id == 0 and not self.args.ci_disable_logprobs_checker:
+            d = m.get("train/train_rollout_logprob_abs_diff")
+            assert d is None or d < 0.03, f"train/rollout log-prob mismatch {d}"
+        if self.args.num_steps_per_rollout in (None, 1) and not self.args.ci_disable_kl_checker:
+            w = max(m.get("train/weight", 1.0), 1e-12)
+            assert abs(m.get("train/ppo_kl", 0.0) / w) < 1e-6, m.get("train/ppo_kl")
+            assert m.get("train/pg_clipfrac", 0.0) / w < 1e-6

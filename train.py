@@ -1,0 +1,95 @@
+"""Synchronous RL driver (colocated): one process per GPU.
+
+    torchrun --nproc-per-node 8 train.py --model-name qwen3-30b-a3b --prompt-data data.jsonl \
+        --rollout-batch-size 64 --n-samples-per-prompt 8 --rm-type math ...
+
+Per rollout id: generate (this GPU's engine, this rank's prompt shard) -> release KV memory ->
+train (log-probs, advantages, policy update, DP gradient reduction) -> periodic save ->
+weight-version bump (colocated refit) -> periodic eval.
+
+Reference: train.py:13-104 (the same loop across Ray actors and SGLang servers).
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+import torch  # noqa: E402
+
+from miles_b200.checkpoint.torch_dist import (get_checkpoint_iteration, is_torch_dist,  # noqa: E402
+                                              load_checkpoint, save_checkpoint, wait_async_save)
+from miles_b200.orchestration.rollout_manager import RolloutManager  # noqa: E402
+from miles_b200.orchestration.setup import (build_actor, build_engine, build_model,  # noqa: E402
+                                            init_distributed, load_tokenizer)
+from miles_b200.rollout.engine_client import LocalEngineClient  # noqa: E402
+from miles_b200.trainer.train_actor import TrainActor  # noqa: E402
+from miles_b200.utils.arguments import parse_args  # noqa: E402
+from miles_b200.utils.misc import load_function, should_run_periodic_action  # noqa: E402
+from miles_b200.utils.tracking import Tracker  # noqa: E402
+
+
+def setup(args):
+    ctx = init_distributed(args)
+    model = build_model(args, ctx)
+    actor = build_actor(args, model, ctx)
+    engine = build_engine(args, model, ctx)
+    tok = load_tokenizer(args)
+    client = LocalEngineClient(engine, tok)
+    ds_cls = load_function(args.data_source_path)
+    data_source = ds_cls(args, tok)
+    manager = RolloutManager(args, data_source, client, tok, ctx.rank, ctx.world)
+    trainer = TrainActor(args, actor, ctx.dp_group)
+    start = 0
+    if args.load and is_torch_dist(args.load):
+        actor._ensure_grads()
+        info = load_checkpoint(args.load, model, actor.opt, load_optim=not args.no_load_optim)
+        start = info.get("extra", {}).get("rollout_id", info["iteration"]) + 1
+        data_source.load(start - 1)
+    if args.start_rollout_id is not None:
+        start = args.start_rollout_id
+    trainer.init_ref()
+    tracker = Tracker(args, ctx.rank)
+    return ctx, model, actor, engine, manager, trainer, tracker, start, data_source
+
+
+def train(args):
+    ctx, model, actor, engine, manager, trainer, tracker, start, data_source = setup(args)
+    num_rollout = args.num_rollout
+    if args.eval_interval and not args.skip_eval_before_train:
+        tracker.log(manager.eval(start), start)
+    for rollout_id in range(start, num_rollout):
+        actor.release_grads()
+        data = manager.generate(rollout_id)
+        engine.release_memory()
+        if args.debug_rollout_only:
+            tracker.log(data["metrics"], rollout_id)
+            continue
+        m = trainer.train(rollout_id, data)
+        m.update(data["metrics"])
+        if should_run_periodic_action(rollout_id, args.save_interval, num_rollout) and args.save:
+            save_checkpoint(args.save, rollout_id, model, actor.opt, extra={"rollout_id": rollout_id},
+                            save_optim=not args.no_save_optim, async_save=args.async_save)
+            data_source.save(rollout_id)
+            if args.save_hf:
+                from miles_b200.checkpoint.hf import save_hf
+
+                if ctx.rank == 0:
+                    save_hf(model, args.save_hf.format(rollout_id=rollout_id))
+        # colocated refit: the engine reads the trainer's parameter buffer in place
+        m["rollout/weight_version"] = model.weight_version
+        if should_run_periodic_action(rollout_id, args.eval_interval, num_rollout):
+            m.update(manager.eval(rollout_id))
+        tracker.log(m, rollout_id)
+    wait_async_save()
+    if args.ci_metric_checker_key:
+        from miles_b200.utils.metric_checker import check_metric
+
+        check_metric(args, tracker.history)
+    tracker.finish()
+    return tracker.history
+
+
+if __name__ == "__main__":
+    train(parse_args())
