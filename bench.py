@@ -118,6 +118,8 @@ def main():
     if args.impl == "reference":
         reference_arm(args)
         return
+    # the KV cache (rollout) and the gradient buffer (training) take turns on the same memory
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     import torch
     import torch.distributed as dist
 
@@ -165,8 +167,16 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        rl.step(*[x for x in workload()[:2]], rewards=workload()[2])
+    def progress(tag, m):
+        if rank == 0:
+            keys = ("perf/rollout_time", "perf/log_probs_time", "perf/actor_train_time",
+                    "perf/step_time", "response_tokens", "train/train_rollout_logprob_abs_diff",
+                    "grad_norm")
+            print(tag, json.dumps({k: m.get(k) for k in keys}), file=sys.stderr, flush=True)
+
+    for i in range(args.warmup):
+        prompts, lens, rewards = workload()
+        progress(f"warmup {i}", rl.step(prompts, lens, rewards))
     barrier()
     sampler = ClockSampler(local)
     sampler.start()
@@ -180,6 +190,7 @@ def main():
     for _ in range(args.steps):
         prompts, lens, rewards = workload()
         m = rl.step(prompts, lens, rewards)
+        progress("timed", m)
         tokens += m["tokens_total"]
         resp += m["response_tokens"]
         rollout_s += m["perf/rollout_time"]

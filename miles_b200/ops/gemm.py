@@ -100,10 +100,31 @@ def matmul_tn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
     return gemm(a, True, b, True, out, M, N, K, epi=epi)
 
 
+# Persistent gradient buffers of parameters, keyed by the parameter's storage address. Lookups
+# by address (not by tensor attribute) survive activation-checkpoint recomputation, whose saved
+# tensors come back as detached aliases without Python attributes.
+_MAIN_GRADS: dict[int, torch.Tensor] = {}
+
+
+def register_main_grad(param: torch.Tensor, grad: torch.Tensor) -> None:
+    _MAIN_GRADS[param.data_ptr()] = grad
+
+
+def clear_main_grads() -> None:
+    _MAIN_GRADS.clear()
+
+
+def main_grad_of(w: torch.Tensor) -> torch.Tensor | None:
+    g = _MAIN_GRADS.get(w.data_ptr())
+    if g is not None and g.shape == w.shape:
+        return g
+    return getattr(w, "main_grad", None)
+
+
 def _accumulate_wgrad(w: torch.Tensor, dy2: torch.Tensor, x2: torch.Tensor) -> torch.Tensor | None:
-    """Weight-grad dW = dy^T x. When the parameter carries a persistent `main_grad` buffer
-    (the trainer's gradient bucket), accumulate into it in place and return None."""
-    main = getattr(w, "main_grad", None)
+    """Weight-grad dW = dy^T x. When the parameter has a persistent gradient buffer (the
+    trainer's flat gradient bucket), accumulate into it in place and return None."""
+    main = main_grad_of(w)
     if main is not None:
         matmul_tn(dy2, x2, out=main, accumulate=True)
         return None

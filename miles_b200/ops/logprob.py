@@ -56,7 +56,7 @@ class _LMHeadLogProb(torch.autograd.Function):
         V = W.shape[0]
         dev = h.device
         dh = torch.empty_like(h)
-        main = getattr(W, "main_grad", None)
+        main = G.main_grad_of(W)
         dW = None
         if main is None and ctx.needs_input_grad[1]:
             dW = torch.zeros(V, H, dtype=torch.float32, device=dev)

@@ -108,7 +108,7 @@ class MoEPlan:
 
 
 def _accum_grouped_wgrad(w: torch.Tensor, dy: torch.Tensor, x: torch.Tensor, plan: MoEPlan):
-    main = getattr(w, "main_grad", None)
+    main = G.main_grad_of(w)
     if main is not None:
         G.grouped_tn(dy, x, plan.offsets, plan.E, out=main, accumulate=True)
         return None

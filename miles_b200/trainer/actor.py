@@ -26,6 +26,7 @@ import torch
 import torch.distributed as dist
 
 from miles_b200.models.transformer import Transformer
+from miles_b200.ops.gemm import clear_main_grads, register_main_grad
 from miles_b200.ops.attention import VarlenMeta
 from miles_b200.ops.logprob import lm_head_logprob
 from miles_b200.ops.rl import METRIC_NAMES, PolicyLossCfg, policy_loss
@@ -100,7 +101,9 @@ class Actor:
             self.grad_flat = torch.zeros(self.model.flat.numel(), dtype=self.cfg.grad_dtype,
                                          device=self.dev)
             for s in self.model.specs:
-                self.model.params[s.name].main_grad = self.grad_flat[s.offset:s.offset + s.numel].view(s.shape)
+                g = self.grad_flat[s.offset:s.offset + s.numel].view(s.shape)
+                self.model.params[s.name].main_grad = g
+                register_main_grad(self.model.params[s.name], g)
         if self.opt is not None:
             self.opt.g = self.grad_flat
         else:
@@ -114,6 +117,7 @@ class Actor:
             p = self.model.params[s.name]
             if hasattr(p, "main_grad"):
                 del p.main_grad
+        clear_main_grads()
         self.grad_flat = None
         if self.opt is not None:
             self.opt.g = None
