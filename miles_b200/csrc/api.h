@@ -93,3 +93,19 @@ int mb_adam(void* param, float* master, void* m, void* v, const void* grad, long
 #ifdef __cplusplus
 }
 #endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+int mb_fp8_block_cast(const void* x, int M, int N, int bm, int bn, void* y, float* scale_inv,
+                      int ue8m0, cudaStream_t st);
+int mb_fp8_group_cast(const void* x, long long M, int N, int group, void* y, float* scale,
+                      int ue8m0, cudaStream_t st);
+int mb_int4_fake_quant(const void* x, long long M, int N, int group, int sym, int dtype, void* q,
+                       void* scale, void* zero, cudaStream_t st);
+int mb_nvfp4_quant(const void* x, long long M, int N, float global_scale, void* packed,
+                   void* bscale, cudaStream_t st);
+int mb_mxfp8_quant(const void* x, long long M, int N, void* y, void* sexp, cudaStream_t st);
+#ifdef __cplusplus
+}
+#endif

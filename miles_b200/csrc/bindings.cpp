@@ -242,7 +242,43 @@ int64_t adam(torch::Tensor param, OT master, torch::Tensor m, torch::Tensor v, t
                    (unsigned long long)seed, PT<float>(skip), cur_stream());
 }
 
+// ------------------------------------------------------------------ quantization
+int64_t fp8_block_cast(torch::Tensor x, int64_t bm, int64_t bn, torch::Tensor y,
+                       torch::Tensor scale_inv, bool ue8m0) {
+  TORCH_CHECK(x.is_contiguous() && x.dim() == 2);
+  return mb_fp8_block_cast(P(x), x.size(0), x.size(1), bm, bn, P(y), PT<float>(scale_inv), ue8m0,
+                           cur_stream());
+}
+int64_t fp8_group_cast(torch::Tensor x, int64_t group, torch::Tensor y, torch::Tensor scale,
+                       bool ue8m0) {
+  TORCH_CHECK(x.is_contiguous() && x.dim() == 2);
+  return mb_fp8_group_cast(P(x), x.size(0), x.size(1), group, P(y), PT<float>(scale), ue8m0,
+                           cur_stream());
+}
+int64_t int4_fake_quant(torch::Tensor x, int64_t group, bool sym, torch::Tensor q,
+                        torch::Tensor scale, OT zero) {
+  TORCH_CHECK(x.is_contiguous() && x.dim() == 2);
+  const int dt = x.scalar_type() == at::kBFloat16 ? 0 : (x.scalar_type() == at::kHalf ? 1 : 2);
+  return mb_int4_fake_quant(P(x), x.size(0), x.size(1), group, sym, dt, P(q), P(scale), P(zero),
+                            cur_stream());
+}
+int64_t nvfp4_quant(torch::Tensor x, double global_scale, torch::Tensor packed,
+                    torch::Tensor bscale) {
+  TORCH_CHECK(x.is_contiguous() && x.dim() == 2);
+  return mb_nvfp4_quant(P(x), x.size(0), x.size(1), (float)global_scale, P(packed), P(bscale),
+                        cur_stream());
+}
+int64_t mxfp8_quant(torch::Tensor x, torch::Tensor y, torch::Tensor sexp) {
+  TORCH_CHECK(x.is_contiguous() && x.dim() == 2);
+  return mb_mxfp8_quant(P(x), x.size(0), x.size(1), P(y), P(sexp), cur_stream());
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("fp8_block_cast", &fp8_block_cast);
+  m.def("fp8_group_cast", &fp8_group_cast);
+  m.def("int4_fake_quant", &int4_fake_quant);
+  m.def("nvfp4_quant", &nvfp4_quant);
+  m.def("mxfp8_quant", &mxfp8_quant);
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM (dense / grouped)");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
