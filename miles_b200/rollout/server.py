@@ -13,6 +13,11 @@ Reference: backends/sglang_utils/sglang_engine.py (server launch :55-108, contro
 """
 from __future__ import annotations
 
+try:  # module level: FastAPI resolves string annotations against module globals
+    from fastapi import Request
+except ImportError:  # pragma: no cover
+    Request = None
+
 import asyncio
 import os
 import threading

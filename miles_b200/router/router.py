@@ -13,6 +13,11 @@ Reference: miles/router/router.py:32-237 (MilesRouter), docs/en/advanced/miles-r
 """
 from __future__ import annotations
 
+try:  # module level: FastAPI resolves string annotations against module globals
+    from fastapi import Request
+except ImportError:  # pragma: no cover
+    Request = None
+
 import asyncio
 import threading
 
