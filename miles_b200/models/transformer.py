@@ -47,7 +47,8 @@ class ParamSpec:
         return n
 
 
-def param_specs(cfg: ModelConfig) -> list[ParamSpec]:
+def param_specs(cfg: ModelConfig, ep_size: int = 1) -> list[ParamSpec]:
+    """Parameter layout; with expert parallelism each rank holds E / ep_size experts."""
     H, D = cfg.hidden_size, cfg.head_dim
     nq, nkv = cfg.num_heads, cfg.num_kv_heads
     specs = [ParamSpec("embed_tokens.weight", (cfg.vocab_size, H), "normal")]
@@ -64,9 +65,10 @@ def param_specs(cfg: ModelConfig) -> list[ParamSpec]:
                       ParamSpec(p + "self_attn.k_norm.weight", (D,), "ones")]
         if cfg.layer_is_moe(i):
             E, I = cfg.num_experts, cfg.moe_intermediate_size
+            El = E // ep_size
             specs += [ParamSpec(p + "mlp.gate.weight", (E, H), "normal"),
-                      ParamSpec(p + "mlp.experts.w1", (E, 2 * I, H), "normal"),
-                      ParamSpec(p + "mlp.experts.w2", (E, H, I), "normal")]
+                      ParamSpec(p + "mlp.experts.w1", (El, 2 * I, H), "normal"),
+                      ParamSpec(p + "mlp.experts.w2", (El, H, I), "normal")]
             if cfg.router_score == "sigmoid":
                 specs.append(ParamSpec(p + "mlp.gate.e_score_correction_bias", (E,), "zeros"))
             if cfg.num_shared_experts:
@@ -111,12 +113,19 @@ class KVCache:
 
 class Transformer(torch.nn.Module):
     def __init__(self, cfg: ModelConfig, device="cuda", dtype=torch.bfloat16, seed: int = 0,
-                 init_std: float = 0.02, materialize: bool = True):
+                 init_std: float = 0.02, materialize: bool = True, ep_group=None):
         super().__init__()
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype
-        self.specs = param_specs(cfg)
+        self.ep = None
+        if ep_group is not None and cfg.is_moe:
+            from miles_b200.parallel.ep import EPContext
+
+            self.ep = EPContext(ep_group, cfg.num_experts)
+            if self.ep.size == 1:
+                self.ep = None
+        self.specs = param_specs(cfg, self.ep.size if self.ep else 1)
         total = self.specs[-1].offset + self.specs[-1].numel
         self.numel = total
         ex = [sp.offset for sp in self.specs if is_expert_param(sp.name)]
@@ -181,9 +190,16 @@ class Transformer(torch.nn.Module):
     def _mlp(self, i: int, x: torch.Tensor, replay=None, record=None) -> torch.Tensor:
         pre = f"layers.{i}.mlp."
         if i in self.router_cfgs:
-            y = moe_experts(x, self.params[pre + "gate.weight"], self.params[pre + "experts.w1"],
-                            self.params[pre + "experts.w2"], self.router_cfgs[i],
-                            self.params.get(pre + "gate.e_score_correction_bias"), replay, record)
+            if self.ep is not None:
+                from miles_b200.parallel.ep import moe_experts_ep
+
+                y = moe_experts_ep(x, self.params[pre + "gate.weight"], self.params[pre + "experts.w1"],
+                                   self.params[pre + "experts.w2"], self.router_cfgs[i], self.ep,
+                                   self.params.get(pre + "gate.e_score_correction_bias"), replay, record)
+            else:
+                y = moe_experts(x, self.params[pre + "gate.weight"], self.params[pre + "experts.w1"],
+                                self.params[pre + "experts.w2"], self.router_cfgs[i],
+                                self.params.get(pre + "gate.e_score_correction_bias"), replay, record)
             if self.cfg.num_shared_experts:
                 s = swiglu(G.linear(x, self.params[pre + "shared_experts.gate_up_proj.weight"]))
                 y = y + G.linear(s, self.params[pre + "shared_experts.down_proj.weight"])

@@ -1,0 +1,142 @@
+"""Expert parallelism for the MoE layer (training and rollout).
+
+Each rank of the expert-parallel group owns E / ep consecutive experts. For a batch of local
+tokens:
+
+  1. route (replicated router on local tokens; or R3-replayed routing)
+  2. plan the send order with the deterministic permute kernel, using destination ranks as the
+     groups (entries (t, j) ordered by destination rank, then token, then slot)
+  3. exchange row counts, then all-to-all the hidden rows and their local expert ids
+  4. received rows -> expert-sorted 128-row padded segments -> grouped tcgen05 GEMMs
+  5. reverse all-to-all of the expert outputs, then the fixed-order weighted combine
+The backward runs the same exchanges in reverse. The baseline exchange is NCCL all-to-all
+(`all_to_all_single`); the order of every row is a pure function of (source rank, token, slot),
+so results do not depend on timing.
+
+Reference: Megatron MoE alltoall token dispatcher (--moe-token-dispatcher-type alltoall),
+DeepEP flex dispatcher (--moe-enable-deepep), expert index offsets for naming
+(update_weight/common.py:186-190).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from miles_b200.ops import gemm as G
+from miles_b200.ops._lib import lib
+from miles_b200.ops.moe import ALIGN, MoEPlan, RouterCfg, _accum_grouped_wgrad
+
+
+class EPContext:
+    def __init__(self, group, num_experts: int):
+        self.group = group
+        self.size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        assert num_experts % self.size == 0
+        self.E = num_experts
+        self.E_local = num_experts // self.size
+        self.first = self.rank * self.E_local
+
+
+def _exchange_counts(send_counts: torch.Tensor, ep: EPContext) -> torch.Tensor:
+    recv = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv, send_counts, group=ep.group)
+    return recv
+
+
+def _a2a(x: torch.Tensor, send_splits: list[int], recv_splits: list[int], ep: EPContext):
+    out = x.new_empty((sum(recv_splits),) + tuple(x.shape[1:]))
+    dist.all_to_all_single(out, x.contiguous(), recv_splits, send_splits, group=ep.group)
+    return out
+
+
+class _MoEEP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, router_w, w1, w2, bias, cfg: RouterCfg, ep: EPContext, replay_idx, record,
+                need_bwd):
+        T, H = x.shape
+        k = cfg.k
+        x = x.contiguous()
+        logits = G.matmul_nt(x, router_w, out_dtype=torch.float32)
+        idx = torch.empty(T, k, dtype=torch.int32, device=x.device)
+        w = torch.empty(T, k, dtype=torch.float32, device=x.device)
+        lib().router_fwd(logits, bias, replay_idx, idx, w, k, cfg.score_fn, cfg.renorm,
+                         cfg.n_group, cfg.topk_group, cfg.scale)
+        if record is not None:
+            record(idx)
+        # send plan: groups = destination ranks, no padding
+        dest_rank = torch.div(idx, ep.E_local, rounding_mode="floor").to(torch.int32)
+        n = T * k
+        nch = max(1, (n + 1023) // 1024)
+        hist = torch.empty(nch * ep.size, dtype=torch.int32, device=x.device)
+        base = torch.empty_like(hist)
+        send_counts = torch.empty(ep.size, dtype=torch.int32, device=x.device)
+        send_off = torch.empty(ep.size + 1, dtype=torch.int32, device=x.device)
+        send_pos = torch.empty(n, dtype=torch.int32, device=x.device)
+        lib().moe_permute_plan(dest_rank.view(-1), ep.size, 1, hist, base, send_counts, send_off, send_pos)
+        send_x = torch.empty(n, H, dtype=x.dtype, device=x.device)
+        lib().moe_gather(x, send_pos, k, send_x)
+        local_eid = (idx - dest_rank * ep.E_local).view(-1)
+        send_eid = torch.empty(n, dtype=torch.int32, device=x.device)
+        send_eid.index_copy_(0, send_pos.long(), local_eid.to(torch.int32))
+        recv_counts = _exchange_counts(send_counts, ep)
+        ss, rs = send_counts.tolist(), recv_counts.tolist()
+        recv_x = _a2a(send_x, ss, rs, ep)
+        recv_eid = _a2a(send_eid, ss, rs, ep)
+        # local experts on the received rows (one "token" per row, k = 1)
+        plan = MoEPlan(recv_eid.view(-1, 1), ep.E_local)
+        xs = plan.gather(recv_x, zero_pad=need_bwd)
+        gu = G.grouped_nt(xs, w1, plan.offsets)
+        a = torch.empty(gu.shape[0], gu.shape[1] // 2, dtype=gu.dtype, device=gu.device)
+        lib().swiglu_fwd(gu, a, plan.total_rows)
+        ys = G.grouped_nt(a, w2, plan.offsets)
+        back = torch.empty(recv_x.shape[0], H, dtype=x.dtype, device=x.device)
+        if back.shape[0]:
+            ones = torch.ones(back.shape[0], 1, dtype=torch.float32, device=x.device)
+            lib().moe_combine(ys, plan.dest, ones, None, back)
+        ret = _a2a(back, rs, ss, ep)  # rows back in send order
+        y = torch.empty_like(x)
+        lib().moe_combine(ret, send_pos, w, None, y)
+        ctx.save_for_backward(x, router_w, w1, w2, logits, idx, w, send_pos, xs, gu, a, ret)
+        ctx.misc = (cfg, ep, plan, ss, rs)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, router_w, w1, w2, logits, idx, w, send_pos, xs, gu, a, ret = ctx.saved_tensors
+        cfg, ep, plan, ss, rs = ctx.misc
+        T, H = x.shape
+        k = cfg.k
+        dy = dy.contiguous()
+        dret = torch.empty_like(ret)
+        dw = torch.empty_like(w)
+        lib().moe_combine_bwd(dy, ret, send_pos, w, dret, dw)
+        dback = _a2a(dret, ss, rs, ep)                    # gradient w.r.t. `back`
+        dys = torch.empty(plan.rows, H, dtype=x.dtype, device=x.device)
+        lib().moe_gather(dback, plan.dest, 1, dys)        # back[r] = ys[dest[r]] -> scatter
+        lib().moe_zero_pad(plan.counts, plan.offsets, dys)
+        da = G.grouped_nn(dys, w2, plan.offsets)
+        dw2 = _accum_grouped_wgrad(w2, dys, a, plan)
+        dgu = torch.empty_like(gu)
+        lib().swiglu_bwd(gu, da, dgu, plan.total_rows)
+        dxs = G.grouped_nn(dgu, w1, plan.offsets)
+        dw1 = _accum_grouped_wgrad(w1, dgu, xs, plan)
+        drecv = torch.empty(dback.shape[0], H, dtype=x.dtype, device=x.device)
+        if drecv.shape[0]:
+            lib().moe_gather_bwd(dxs, plan.dest, 1, drecv)
+        dsend = _a2a(drecv, rs, ss, ep)
+        dx = torch.empty_like(x)
+        lib().moe_gather_bwd(dsend, send_pos, k, dx)
+        dlogits = torch.empty(T, cfg.E, dtype=torch.bfloat16, device=x.device)
+        lib().router_bwd(logits, idx, dw, dlogits, cfg.score_fn, cfg.renorm, cfg.scale)
+        dx.add_(G.matmul_nn(dlogits, router_w))
+        dwr = G._accumulate_wgrad(router_w, dlogits, x)
+        return dx, dwr, dw1, dw2, None, None, None, None, None, None
+
+
+def moe_experts_ep(x, router_w, w1_local, w2_local, cfg: RouterCfg, ep: EPContext, bias=None,
+                   replay_idx=None, record=None):
+    """Expert-parallel MoE: w1_local [E/ep, 2I, H], w2_local [E/ep, H, I] hold this rank's
+    experts; routing and the output are over the global expert set."""
+    return _MoEEP.apply(x, router_w, w1_local, w2_local, bias, cfg, ep, replay_idx, record,
+                        torch.is_grad_enabled())
