@@ -109,3 +109,21 @@ int mb_mxfp8_quant(const void* x, long long M, int N, void* y, void* sexp, cudaS
 #ifdef __cplusplus
 }
 #endif
+
+// Allocation-free decode attention (no counterpart in the reference implementation; an
+// addition of this library). Same inputs/outputs as mb_attn_decode, but the split-KV workspace
+// is a fixed 4 MiB device array inside the library instead of caller memory, for callers that
+// cannot allocate device memory. Returns -9 if the call would need more than that workspace,
+// -10/-11 on device / symbol lookup failure. The first call on a device resolves the array's
+// address (do it before any stream capture); concurrent calls on unordered streams race on the
+// shared workspace.
+#ifdef __cplusplus
+extern "C" {
+#endif
+#define MB_NOALLOC_TOO_LARGE (-9)
+int mb_attn_decode_noalloc(const void* q, const void* kc, const void* vc, void* o,
+                           const int* page_table, const int* ctx_lens, int B, int max_pages,
+                           int nq, int nkv, float softmax_scale, cudaStream_t st);
+#ifdef __cplusplus
+}
+#endif

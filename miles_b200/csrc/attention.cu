@@ -822,3 +822,49 @@ extern "C" int mb_attn_bwd(const void* q, const void* k, const void* v, const vo
   attn_bwd_dq_kernel<<<dim3(nblocks, nq), 128, smem_q, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
+
+// =============================================================================================
+// Allocation-free decode attention.
+//
+// Some callers cannot allocate device memory at the point where they run decode attention:
+// code executing inside another framework's memory pool or under a strict memory budget, and
+// C/C++ hosts that link this library without a caching allocator (calling cudaMalloc there
+// would synchronise the device or fail once the pool has claimed the GPU). For them this entry
+// point takes only inputs and outputs; the split-KV workspace that mb_attn_decode receives from
+// its caller lives instead in the fixed device array below.
+//
+//  * Limit: kNoAllocWsFloats floats (4 MiB) shared by the partial outputs and the (m, l)
+//    pairs; a call needing more (B * nq * nsplit * 130 floats, nsplit = ceil(max_pages / 16))
+//    is rejected with MB_NOALLOC_TOO_LARGE before anything is launched.
+//  * Every GPU that loads the library holds the array until the process exits.
+//  * Set-up: the first call on each device (with that device current) resolves the array's
+//    device address with cudaGetSymbolAddress and caches it; make that first call before any
+//    stream capture starts.
+//  * The array is shared by every call and keeps the last call's contents. No part of it has
+//    to start at zero (each call writes every slot it later reads), but calls whose kernels
+//    overlap on the GPU (different streams, no ordering) race on it: order them.
+// =============================================================================================
+constexpr long long kNoAllocWsFloats = 1ll << 20;
+static __device__ __align__(256) float g_noalloc_ws[kNoAllocWsFloats];
+static float* g_noalloc_ws_ptr[128] = {nullptr};
+
+extern "C" int mb_attn_decode_noalloc(const void* q, const void* kc, const void* vc, void* o,
+                                      const int* page_table, const int* ctx_lens, int B,
+                                      int max_pages, int nq, int nkv, float softmax_scale,
+                                      cudaStream_t st) {
+  if (B == 0) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return -10;
+  const long long nsplit = (max_pages + CHUNK_BLOCKS - 1) / CHUNK_BLOCKS;
+  const long long need = nsplit > 1 ? (long long)B * nq * nsplit * (D + 2) : 0;
+  if (need > kNoAllocWsFloats) return -9;  // MB_NOALLOC_TOO_LARGE
+  if (g_noalloc_ws_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_ws) != cudaSuccess || ptr == nullptr) return -11;
+    g_noalloc_ws_ptr[dev] = static_cast<float*>(ptr);
+  }
+  float* ws_o = g_noalloc_ws_ptr[dev];
+  float* ws_ml = ws_o + (long long)B * nq * nsplit * D;
+  return mb_attn_decode(q, kc, vc, o, page_table, ctx_lens, B, max_pages, nq, nkv, softmax_scale,
+                        ws_o, ws_ml, st);
+}
