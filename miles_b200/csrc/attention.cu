@@ -251,6 +251,8 @@ struct FwdParams {
 };
 
 __global__ void __launch_bounds__(128) attn_fwd_kernel(const FwdParams p) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sq = smem_u32(smem);
   const uint32_t sk[2] = {sq + TILE_BYTES, sq + 3 * TILE_BYTES};
@@ -357,6 +359,8 @@ struct DecParams {
 constexpr int DEC_STAGES = 3;
 
 __global__ void __launch_bounds__(32) attn_decode_kernel(const DecParams p) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sq = smem_u32(smem);
   const int lane = threadIdx.x;
@@ -441,6 +445,8 @@ __global__ void __launch_bounds__(32) attn_decode_kernel(const DecParams p) {
 // the prefill kernel's in-register merge) and write the bf16 output. One warp per row; lane
 // owns columns lane*4 .. lane*4+3.
 __global__ void attn_decode_combine_kernel(const DecParams p, int B) {
+  pdl_trigger();
+  pdl_wait();
   const long long w = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (w >= (long long)B * p.nq) return;
@@ -471,6 +477,8 @@ __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ o,
                                       const __nv_bfloat16* __restrict__ dout,
                                       long long o_stride, long long do_stride, int T, int nq,
                                       float* __restrict__ delta) {
+  pdl_trigger();
+  pdl_wait();
   const long long w = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (w >= (long long)T * nq) return;
@@ -500,6 +508,8 @@ struct BwdParams {
 // heads of the group and over query blocks qb >= kb in a fixed order; accumulates dK, dV in
 // registers.
 __global__ void __launch_bounds__(128, 1) attn_bwd_dkdv_kernel(const BwdParams p) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sk = smem_u32(smem), sv = sk + TILE_BYTES;
   const uint32_t sq = sk + 2 * TILE_BYTES, sdo = sk + 3 * TILE_BYTES;
@@ -646,6 +656,8 @@ __global__ void __launch_bounds__(128, 1) attn_bwd_dkdv_kernel(const BwdParams p
 
 // CTA = (query block, query head). dQ = scale * sum_j dS_j K_j over key blocks 0..qb.
 __global__ void __launch_bounds__(128, 1) attn_bwd_dq_kernel(const BwdParams p) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sq = smem_u32(smem), sdo = sq + TILE_BYTES;
   const uint32_t sk = sq + 2 * TILE_BYTES, sv = sq + 3 * TILE_BYTES;
@@ -740,6 +752,7 @@ __global__ void __launch_bounds__(128, 1) attn_bwd_dq_kernel(const BwdParams p) 
 }  // namespace mb
 
 using namespace mb::attn;
+using mb::mb_launch;
 
 extern "C" int mb_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
                            const int* cu_seqlens, const int* blk_seq, const int* blk_idx,
@@ -757,7 +770,7 @@ extern "C" int mb_attn_fwd(const void* q, const void* k, const void* v, void* o,
     cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     set = true;
   }
-  attn_fwd_kernel<<<dim3(nblocks, nq), 128, smem, st>>>(p);
+  mb_launch(attn_fwd_kernel, dim3(nblocks, nq), 128, smem, st, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -785,10 +798,10 @@ extern "C" int mb_attn_decode(const void* q, const void* kc, const void* vc, voi
     cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     set = true;
   }
-  attn_decode_kernel<<<dim3(B, nkv, nsplit_max), 32, smem, st>>>(p);
+  mb_launch(attn_decode_kernel, dim3(B, nkv, nsplit_max), 32, smem, st, p);
   if (nsplit_max > 1) {
     const long long w = (long long)B * nq;
-    attn_decode_combine_kernel<<<(unsigned)((w + 7) / 8), 256, 0, st>>>(p, B);
+    mb_launch(attn_decode_combine_kernel, (unsigned)((w + 7) / 8), 256, 0, st, p, B);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -803,7 +816,7 @@ extern "C" int mb_attn_bwd(const void* q, const void* k, const void* v, const vo
   if (nblocks == 0) return 0;
   if (nq % nkv) return -1;
   const long long warps = (long long)T * nq;
-  attn_bwd_delta_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+  mb_launch(attn_bwd_delta_kernel, (unsigned)((warps + 7) / 8), 256, 0, st, 
       (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, o_stride, do_stride, T, nq, delta);
   BwdParams p{(const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
               (const __nv_bfloat16*)dout, lse, delta, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk,
@@ -818,8 +831,8 @@ extern "C" int mb_attn_bwd(const void* q, const void* k, const void* v, const vo
     cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
     set = true;
   }
-  attn_bwd_dkdv_kernel<<<dim3(nblocks, nkv), 128, smem_kv, st>>>(p);
-  attn_bwd_dq_kernel<<<dim3(nblocks, nq), 128, smem_q, st>>>(p);
+  mb_launch(attn_bwd_dkdv_kernel, dim3(nblocks, nkv), 128, smem_kv, st, p);
+  mb_launch(attn_bwd_dq_kernel, dim3(nblocks, nq), 128, smem_q, st, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

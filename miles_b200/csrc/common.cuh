@@ -17,7 +17,42 @@
 
 #define MB_DEVICE __device__ __forceinline__
 
+#include <cstdlib>
+#include <utility>
+
 namespace mb {
+
+// ---------------------------------------------------------------------------------------------
+// Programmatic dependent launch (PDL). Every kernel of the library is launched with programmatic
+// stream serialization; inside, `pdl_trigger()` lets the next kernel in the stream start
+// launching immediately and `pdl_wait()` (griddepcontrol.wait) blocks until the previous kernel
+// has completed and its memory is visible. The next kernel's launch latency and prologue
+// (barrier init, TMEM allocation, descriptor prefetch) therefore overlap the previous kernel's
+// tail. Kernels call pdl_wait() before touching any input. MB_NO_PDL=1 disables it.
+// ---------------------------------------------------------------------------------------------
+MB_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MB_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+  static const bool on = std::getenv("MB_NO_PDL") == nullptr;
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t mb_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------------------------
 // Error reporting

@@ -90,8 +90,16 @@ MB_DEVICE TileInfo get_tile(const GemmParams& p, int t) {
     ti.kend = __ldg(p.group_offsets + ti.g + 1);
     ti.c_off = (long long)ti.g * p.c_group_stride;
   } else {
-    ti.m0 = (t % mt) * BM;
-    ti.n0 = (t / mt) * BN;
+    if (MODE == 1) {
+      // N-fastest: the N-tiles of one expert segment run on neighbouring CTAs at the same time
+      // and share the segment's A-tile through L2 (instead of re-reading it from DRAM once per
+      // N-tile sweep over all experts).
+      ti.m0 = (t / nt) * BM;
+      ti.n0 = (t % nt) * BN;
+    } else {
+      ti.m0 = (t % mt) * BM;
+      ti.n0 = (t / mt) * BN;
+    }
     ti.kbeg = 0;
     ti.kend = p.K;
     if (MODE == 1) {
@@ -164,6 +172,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // inputs are read only after the previous kernel completes
 
   const int ntiles = num_tiles<BN, MODE>(p);
 
@@ -396,7 +406,7 @@ static int launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPa
   const int tiles = MODE == 2 ? p.num_groups * mt * nt : mt * nt;
   if (tiles == 0) return 0;
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-  kern<<<grid, 192, Cfg::SMEM_BYTES, st>>>(ta, tb, p);
+  mb_launch(kern, grid, 192, Cfg::SMEM_BYTES, st, ta, tb, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 

@@ -23,6 +23,8 @@ __global__ void router_fwd_kernel(const float* __restrict__ logits, const float*
                                   const int* __restrict__ idx_in, int* __restrict__ idx_out,
                                   float* __restrict__ w_out, int T, int E, int k, int score_fn,
                                   int renorm, int n_group, int topk_group, float scale) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -150,6 +152,8 @@ __global__ void router_fwd_kernel(const float* __restrict__ logits, const float*
 __global__ void router_bwd_kernel(const float* __restrict__ logits, const int* __restrict__ idx,
                                   const float* __restrict__ dw, __nv_bfloat16* __restrict__ dlogits,
                                   int T, int E, int k, int score_fn, int renorm, float scale) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -231,6 +235,8 @@ __global__ void router_bwd_kernel(const float* __restrict__ logits, const int* _
 constexpr int kChunk = 1024;
 
 __global__ void moe_hist_kernel(const int* __restrict__ idx, int n, int E, int* __restrict__ hist) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int h[kMaxE];
   for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
   __syncthreads();
@@ -243,6 +249,8 @@ __global__ void moe_hist_kernel(const int* __restrict__ idx, int n, int E, int* 
 __global__ void moe_scan_kernel(const int* __restrict__ hist, int nchunks, int E, int align,
                                 int* __restrict__ counts, int* __restrict__ offsets,
                                 int* __restrict__ chunk_base) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int padded[kMaxE + 1];
   const int e = threadIdx.x;
   int total = 0;
@@ -273,6 +281,8 @@ __global__ void moe_scan_kernel(const int* __restrict__ hist, int nchunks, int E
 
 __global__ void moe_scatter_kernel(const int* __restrict__ idx, int n, int E,
                                    const int* __restrict__ chunk_base, int* __restrict__ dest) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int wcnt[32][kMaxE];
   const int wid = threadIdx.x / 32, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) wcnt[i / E][i % E] = 0;
@@ -294,6 +304,8 @@ __global__ void moe_scatter_kernel(const int* __restrict__ idx, int n, int E,
 // Zero the padding rows of every expert segment: [offsets[e] + counts[e], offsets[e+1]).
 __global__ void moe_zero_pad_kernel(const int* __restrict__ counts, const int* __restrict__ offsets,
                                     __nv_bfloat16* __restrict__ buf, int H) {
+  pdl_trigger();
+  pdl_wait();
   const int e = blockIdx.x;
   const int r0 = offsets[e] + counts[e], r1 = offsets[e + 1];
   const int nvec = H / 8;
@@ -305,6 +317,8 @@ __global__ void moe_zero_pad_kernel(const int* __restrict__ counts, const int* _
 // x_sorted[dest[t*k+j]] = x[t]; one warp per entry.
 __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ dest,
                                   int n, int k, int H, __nv_bfloat16* __restrict__ xs) {
+  pdl_trigger();
+  pdl_wait();
   const long long w = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (w >= n) return;
@@ -318,6 +332,8 @@ __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, const int
 __global__ void moe_gather_bwd_kernel(const __nv_bfloat16* __restrict__ dxs,
                                       const int* __restrict__ dest, int T, int k, int H,
                                       __nv_bfloat16* __restrict__ dx) {
+  pdl_trigger();
+  pdl_wait();
   const long long gw = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   const int nch = H / 256;
@@ -343,6 +359,8 @@ __global__ void moe_gather_bwd_kernel(const __nv_bfloat16* __restrict__ dxs,
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ ys, const int* __restrict__ dest,
                                    const float* __restrict__ w, const __nv_bfloat16* __restrict__ add,
                                    int T, int k, int H, __nv_bfloat16* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   const long long gw = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   const int nch = H / 256;
@@ -376,6 +394,8 @@ __global__ void moe_combine_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
                                        const int* __restrict__ dest, const float* __restrict__ w,
                                        int T, int k, int H, __nv_bfloat16* __restrict__ dys,
                                        float* __restrict__ dw) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -412,7 +432,7 @@ extern "C" int mb_router_fwd(const float* logits, const float* bias, const int* 
                              int n_group, int topk_group, float scale, cudaStream_t st) {
   if (T == 0) return 0;
   if (E > kMaxE || k > kMaxK || (n_group > 1 && (n_group > 32 || E % n_group))) return -1;
-  router_fwd_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, idx_in, idx_out, w_out, T, E, k,
+  mb_launch(router_fwd_kernel, (T + 7) / 8, 256, 0, st, logits, bias, idx_in, idx_out, w_out, T, E, k,
                                                  score_fn, renorm, n_group, topk_group, scale);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -422,7 +442,7 @@ extern "C" int mb_router_bwd(const float* logits, const int* idx, const float* d
                              cudaStream_t st) {
   if (T == 0) return 0;
   if (E > kMaxE || k > kMaxK) return -1;
-  router_bwd_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, idx, dw, (__nv_bfloat16*)dlogits, T, E, k,
+  mb_launch(router_bwd_kernel, (T + 7) / 8, 256, 0, st, logits, idx, dw, (__nv_bfloat16*)dlogits, T, E, k,
                                                  score_fn, renorm, scale);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -433,17 +453,17 @@ extern "C" int mb_moe_permute_plan(const int* idx, int n, int E, int align, int*
                                    cudaStream_t st) {
   if (E > kMaxE || align <= 0) return -1;
   const int nchunks = (n + kChunk - 1) / kChunk;
-  if (n > 0) moe_hist_kernel<<<nchunks, kChunk, 0, st>>>(idx, n, E, hist);
-  moe_scan_kernel<<<1, kMaxE, 0, st>>>(hist, n > 0 ? nchunks : 0, E, align, counts, offsets,
+  if (n > 0) mb_launch(moe_hist_kernel, nchunks, kChunk, 0, st, idx, n, E, hist);
+  mb_launch(moe_scan_kernel, 1, kMaxE, 0, st, hist, n > 0 ? nchunks : 0, E, align, counts, offsets,
                                        chunk_base);
-  if (n > 0) moe_scatter_kernel<<<nchunks, kChunk, 0, st>>>(idx, n, E, chunk_base, dest);
+  if (n > 0) mb_launch(moe_scatter_kernel, nchunks, kChunk, 0, st, idx, n, E, chunk_base, dest);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
 extern "C" int mb_moe_zero_pad(const int* counts, const int* offsets, void* buf, int E, int H,
                                cudaStream_t st) {
   if (H % 8) return -1;
-  moe_zero_pad_kernel<<<E, 128, 0, st>>>(counts, offsets, (__nv_bfloat16*)buf, H);
+  mb_launch(moe_zero_pad_kernel, E, 128, 0, st, counts, offsets, (__nv_bfloat16*)buf, H);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -451,7 +471,7 @@ extern "C" int mb_moe_gather(const void* x, const int* dest, int n, int k, int H
                              cudaStream_t st) {
   if (n == 0) return 0;
   if (H % 8) return -1;
-  moe_gather_kernel<<<(n + 7) / 8, 256, 0, st>>>((const __nv_bfloat16*)x, dest, n, k, H,
+  mb_launch(moe_gather_kernel, (n + 7) / 8, 256, 0, st, (const __nv_bfloat16*)x, dest, n, k, H,
                                                  (__nv_bfloat16*)xs);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -461,7 +481,7 @@ extern "C" int mb_moe_gather_bwd(const void* dxs, const int* dest, int T, int k,
   if (T == 0) return 0;
   if (H % 256) return -1;
   const long long wg = (long long)T * (H / 256);
-  moe_gather_bwd_kernel<<<(unsigned)((wg + 7) / 8), 256, 0, st>>>((const __nv_bfloat16*)dxs, dest, T, k, H,
+  mb_launch(moe_gather_bwd_kernel, (unsigned)((wg + 7) / 8), 256, 0, st, (const __nv_bfloat16*)dxs, dest, T, k, H,
                                                      (__nv_bfloat16*)dx);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -471,7 +491,7 @@ extern "C" int mb_moe_combine(const void* ys, const int* dest, const float* w, c
   if (T == 0) return 0;
   if (H % 256) return -1;
   const long long wc = (long long)T * (H / 256);
-  moe_combine_kernel<<<(unsigned)((wc + 7) / 8), 256, 0, st>>>((const __nv_bfloat16*)ys, dest, w,
+  mb_launch(moe_combine_kernel, (unsigned)((wc + 7) / 8), 256, 0, st, (const __nv_bfloat16*)ys, dest, w,
                                                   (const __nv_bfloat16*)add, T, k, H,
                                                   (__nv_bfloat16*)y);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
@@ -481,7 +501,7 @@ extern "C" int mb_moe_combine_bwd(const void* dy, const void* ys, const int* des
                                   int T, int k, int H, void* dys, float* dw, cudaStream_t st) {
   if (T == 0) return 0;
   if (H % 256) return -1;
-  moe_combine_bwd_kernel<<<(T + 7) / 8, 256, 0, st>>>((const __nv_bfloat16*)dy,
+  mb_launch(moe_combine_bwd_kernel, (T + 7) / 8, 256, 0, st, (const __nv_bfloat16*)dy,
                                                       (const __nv_bfloat16*)ys, dest, w, T, k, H,
                                                       (__nv_bfloat16*)dys, dw);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;

@@ -20,6 +20,8 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
                                    const __nv_bfloat16* __restrict__ w,
                                    __nv_bfloat16* __restrict__ h_out, __nv_bfloat16* __restrict__ y,
                                    float* __restrict__ rstd_out, int rows, float eps) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int PER = H / 32;  // elements per lane
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -80,6 +82,8 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
                                    const __nv_bfloat16* __restrict__ dres,  // optional: added to dx
                                    __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part,
                                    int rows, int rows_per_block) {
+  pdl_trigger();
+  pdl_wait();
   const int warps = blockDim.x / 32;
   const int wid = threadIdx.x / 32, lane = threadIdx.x & 31;
   extern __shared__ float sh[];
@@ -144,6 +148,8 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
 __global__ void reduce_parts_kernel(const float* __restrict__ parts, int nparts, int n,
                                     float* __restrict__ out_f32, __nv_bfloat16* __restrict__ out_bf16,
                                     int accumulate) {
+  pdl_trigger();
+  pdl_wait();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= n) return;
   float s = 0.f;
@@ -172,6 +178,8 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, l
                                         const long long* __restrict__ slot, long long ld_kv,
                                         float* __restrict__ rstd_out, int T, int nq, int nkv,
                                         float eps, int use_norm) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int D = 128, HALF = 64;
   const int nh = nq + 2 * nkv;
   const long long gw = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
@@ -232,6 +240,8 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq,
                                         __nv_bfloat16* __restrict__ dqkv,
                                         float* __restrict__ dw_part,  // [gridDim.x, 2, D]
                                         int T, int nq, int nkv, int use_norm) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int D = 128, HALF = 64;
   const int nh = nq + 2 * nkv;
   const int warps = blockDim.x / 32;
@@ -315,6 +325,8 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq,
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu,
                                   __nv_bfloat16* __restrict__ out, long long T, int I,
                                   const int* __restrict__ nrows) {
+  pdl_trigger();
+  pdl_wait();
   if (nrows) T = min(T, (long long)*nrows);  // rows beyond the live MoE segments are skipped
   const long long n8 = T * I / 8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
@@ -342,6 +354,8 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu,
                                   const __nv_bfloat16* __restrict__ dout,
                                   __nv_bfloat16* __restrict__ dgu, long long T, int I,
                                   const int* __restrict__ nrows) {
+  pdl_trigger();
+  pdl_wait();
   if (nrows) T = min(T, (long long)*nrows);
   const long long n8 = T * I / 8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
@@ -389,7 +403,7 @@ extern "C" int mb_rmsnorm_fwd(const void* x, const void* res, const void* w, voi
   const int grid = (rows + rpb - 1) / rpb;
 #define RMS_CASE(HH)                                                                           \
   case HH:                                                                                     \
-    rmsnorm_fwd_kernel<HH><<<grid, block, 0, st>>>(                                            \
+    mb_launch(rmsnorm_fwd_kernel<HH>, grid, block, 0, st,                                             \
         (const __nv_bfloat16*)x, (const __nv_bfloat16*)res, (const __nv_bfloat16*)w,           \
         (__nv_bfloat16*)h_out, (__nv_bfloat16*)y, rstd, rows, eps);                            \
     break;
@@ -415,7 +429,7 @@ extern "C" int mb_rmsnorm_bwd(const void* dy, const void* x, const void* w, cons
     auto k = rmsnorm_bwd_kernel<HH>;                                                           \
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                                (int)smem);                                     \
-    k<<<grid, block, smem, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x,           \
+    mb_launch(k, grid, block, smem, st, (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x,           \
                                  (const __nv_bfloat16*)w, rstd, (const __nv_bfloat16*)dres,   \
                                  (__nv_bfloat16*)dx, dw_part, rows, rpb);                      \
   } break;
@@ -425,7 +439,7 @@ extern "C" int mb_rmsnorm_bwd(const void* dy, const void* x, const void* w, cons
     default: return -1;
   }
 #undef RMSB_CASE
-  reduce_parts_kernel<<<(H + 255) / 256, 256, 0, st>>>(dw_part, grid, H, dw_f32,
+  mb_launch(reduce_parts_kernel, (H + 255) / 256, 256, 0, st, dw_part, grid, H, dw_f32,
                                                        (__nv_bfloat16*)dw_bf16, accumulate);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -439,7 +453,7 @@ extern "C" int mb_qk_norm_rope_fwd(const void* qkv, long long ld_in, const void*
   const long long warps = (long long)T * (nq + 2 * nkv);
   const int block = 256;
   const long long grid = (warps + 7) / 8;
-  qk_norm_rope_fwd_kernel<<<(unsigned)grid, block, 0, st>>>(
+  mb_launch(qk_norm_rope_fwd_kernel, (unsigned)grid, block, 0, st, 
       (const __nv_bfloat16*)qkv, ld_in, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, pos,
       cos_t, sin_t, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out, slot,
       ld_kv, rstd, T, nq, nkv, eps, use_norm);
@@ -454,12 +468,12 @@ extern "C" int mb_qk_norm_rope_bwd(const void* dq, const void* dk, const void* d
                                    int T, int nq, int nkv, int use_norm, cudaStream_t st) {
   if (T == 0) return 0;
   const int block = 256;
-  qk_norm_rope_bwd_kernel<<<nparts, block, 0, st>>>(
+  mb_launch(qk_norm_rope_bwd_kernel, nparts, block, 0, st, 
       (const __nv_bfloat16*)dq, (const __nv_bfloat16*)dk, (const __nv_bfloat16*)dv,
       (const __nv_bfloat16*)qkv, ld_in, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, pos,
       cos_t, sin_t, rstd, (__nv_bfloat16*)dqkv, use_norm ? dw_part : nullptr, T, nq, nkv,
       use_norm);
-  if (use_norm) reduce_parts_kernel<<<1, 256, 0, st>>>(dw_part, nparts, 256, dw_out, nullptr, 0);
+  if (use_norm) mb_launch(reduce_parts_kernel, 1, 256, 0, st, dw_part, nparts, 256, dw_out, nullptr, 0);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -468,7 +482,7 @@ extern "C" int mb_swiglu_fwd(const void* gu, void* out, long long T, int I, cons
   if (T == 0) return 0;
   if (I % 8) return -1;
   const long long n8 = T * I / 8;
-  swiglu_fwd_kernel<<<grid_for(n8, 256), 256, 0, st>>>((const __nv_bfloat16*)gu,
+  mb_launch(swiglu_fwd_kernel, grid_for(n8, 256), 256, 0, st, (const __nv_bfloat16*)gu,
                                                        (__nv_bfloat16*)out, T, I, nrows);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -478,7 +492,7 @@ extern "C" int mb_swiglu_bwd(const void* gu, const void* dout, void* dgu, long l
   if (T == 0) return 0;
   if (I % 8) return -1;
   const long long n8 = T * I / 8;
-  swiglu_bwd_kernel<<<grid_for(n8, 256), 256, 0, st>>>(
+  mb_launch(swiglu_bwd_kernel, grid_for(n8, 256), 256, 0, st, 
       (const __nv_bfloat16*)gu, (const __nv_bfloat16*)dout, (__nv_bfloat16*)dgu, T, I, nrows);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

@@ -64,6 +64,8 @@ MB_DEVICE SoftStats row_stats(const float* __restrict__ z, int V, float inv_temp
 __global__ void __launch_bounds__(LS_THREADS) logprob_fwd_kernel(
     const float* __restrict__ logits, long long ld, const int* __restrict__ target, int V,
     float inv_temp, float* __restrict__ logp, float* __restrict__ ent, float* __restrict__ lse) {
+  pdl_trigger();
+  pdl_wait();
   const long long r = blockIdx.x;
   const float* z = logits + r * ld;
   const SoftStats st = row_stats(z, V, inv_temp);
@@ -81,6 +83,8 @@ __global__ void __launch_bounds__(LS_THREADS) logprob_bwd_kernel(
     float inv_temp, const float* __restrict__ lse, const float* __restrict__ g_lp,
     const float* __restrict__ g_ent, const float* __restrict__ ent,
     __nv_bfloat16* __restrict__ dlogits, long long ldd) {
+  pdl_trigger();
+  pdl_wait();
   const long long r = blockIdx.x;
   const float* z = logits + r * ld;
   const float l = lse[r];
@@ -114,6 +118,8 @@ __global__ void __launch_bounds__(LS_THREADS) sample_kernel(
     const float* __restrict__ logits, long long ld, int V, const float* __restrict__ inv_temps,
     const unsigned long long* __restrict__ seeds, const int* __restrict__ positions,
     int* __restrict__ tokens, float* __restrict__ logp) {
+  pdl_trigger();
+  pdl_wait();
   const long long r = blockIdx.x;
   const float* z = logits + r * ld;
   const float itemp = inv_temps[r];
@@ -180,6 +186,8 @@ struct PolicyLossParams {
 };
 
 __global__ void policy_loss_kernel(const PolicyLossParams p) {
+  pdl_trigger();
+  pdl_wait();
   float acc[PL_METRICS] = {0, 0, 0, 0, 0, 0, 0};
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.n; i += gridDim.x * blockDim.x) {
     const float w = p.weight[i];
@@ -244,6 +252,8 @@ __global__ void policy_loss_kernel(const PolicyLossParams p) {
 // Sum [nparts, n] partials in fixed order into out[n] (single CTA).
 __global__ void sum_parts_kernel(const float* __restrict__ part, int nparts, int n,
                                  float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   for (int c = threadIdx.x; c < n; c += blockDim.x) {
     float s = 0.f;
     for (int q = 0; q < nparts; ++q) s += part[q * n + c];
@@ -259,6 +269,8 @@ __global__ void sum_parts_kernel(const float* __restrict__ part, int nparts, int
 __global__ void gae_kernel(const float* __restrict__ rewards, const float* __restrict__ values,
                            const int* __restrict__ cu, int B, float gamma, float lam,
                            float* __restrict__ adv, float* __restrict__ ret) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   const int s = cu[b], e = cu[b + 1];
@@ -276,6 +288,8 @@ __global__ void gae_kernel(const float* __restrict__ rewards, const float* __res
 // GRPO: per group of `gsize` rewards, adv = r - mean (optionally / (std + eps)); unbiased std.
 __global__ void grpo_adv_kernel(const float* __restrict__ r, int ngroups, int gsize, int norm_std,
                                 float eps, float* __restrict__ adv) {
+  pdl_trigger();
+  pdl_wait();
   const int g = blockIdx.x * blockDim.x + threadIdx.x;
   if (g >= ngroups) return;
   const float* x = r + (long long)g * gsize;
@@ -296,6 +310,8 @@ __global__ void grpo_adv_kernel(const float* __restrict__ r, int ngroups, int gs
 // ---------------------------------------------------------------------------------------------
 template <typename T>
 __global__ void sqnorm_part_kernel(const T* __restrict__ x, long long n, float* __restrict__ part) {
+  pdl_trigger();
+  pdl_wait();
   float s = 0.f;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
@@ -313,6 +329,8 @@ __global__ void sqnorm_part_kernel(const T* __restrict__ x, long long n, float* 
 }
 
 __global__ void sqnorm_final_kernel(const float* __restrict__ part, int nparts, float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float sh[256];
   float s = 0.f;
   for (int i = threadIdx.x; i < nparts; i += 256) s += part[i];
@@ -355,6 +373,8 @@ MB_DEVICE __nv_bfloat16 sr_bf16(float x, uint32_t rnd) {
 }
 
 __global__ void adam_kernel(const AdamParams p) {
+  pdl_trigger();
+  pdl_wait();
   if (p.skip && *p.skip != 0.f) return;
   float gscale = p.inv_loss_scale;
   if (p.sqnorm && p.max_norm > 0.f) {
@@ -392,6 +412,8 @@ __global__ void adam_kernel(const AdamParams p) {
 // Non-finite check of a flat fp32/bf16 buffer: sets *flag = 1 if any element is inf/nan.
 template <typename T>
 __global__ void nonfinite_kernel(const T* __restrict__ x, long long n, float* __restrict__ flag) {
+  pdl_trigger();
+  pdl_wait();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
     if (!isfinite((float)x[i])) { *flag = 1.f; return; }
@@ -410,7 +432,7 @@ static int gsz(long long n, int block, int cap = 148 * 8) {
 extern "C" int mb_logprob_fwd(const float* logits, long long ld, const int* target, int n, int V,
                               float inv_temp, float* logp, float* ent, float* lse, cudaStream_t st) {
   if (n == 0) return 0;
-  logprob_fwd_kernel<<<n, LS_THREADS, 0, st>>>(logits, ld, target, V, inv_temp, logp, ent, lse);
+  mb_launch(logprob_fwd_kernel, n, LS_THREADS, 0, st, logits, ld, target, V, inv_temp, logp, ent, lse);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -419,7 +441,7 @@ extern "C" int mb_logprob_bwd(const float* logits, long long ld, const int* targ
                               const float* g_ent, const float* ent, void* dlogits, long long ldd,
                               cudaStream_t st) {
   if (n == 0) return 0;
-  logprob_bwd_kernel<<<n, LS_THREADS, 0, st>>>(logits, ld, target, V, inv_temp, lse, g_lp, g_ent,
+  mb_launch(logprob_bwd_kernel, n, LS_THREADS, 0, st, logits, ld, target, V, inv_temp, lse, g_lp, g_ent,
                                                ent, (__nv_bfloat16*)dlogits, ldd);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -428,7 +450,7 @@ extern "C" int mb_sample(const float* logits, long long ld, int n, int V, const 
                          const unsigned long long* seeds, const int* positions, int* tokens,
                          float* logp, cudaStream_t st) {
   if (n == 0) return 0;
-  sample_kernel<<<n, LS_THREADS, 0, st>>>(logits, ld, V, inv_temps, seeds, positions, tokens, logp);
+  mb_launch(sample_kernel, n, LS_THREADS, 0, st, logits, ld, V, inv_temps, seeds, positions, tokens, logp);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -441,22 +463,22 @@ extern "C" int mb_policy_loss(const float* logp, const float* old_logp, const fl
   const int grid = gsz(n, 256, 256);
   PolicyLossParams p{logp, old_logp, adv, weight, rollout_logp, ref_logp, dlogp, pg_out, part, n,
                      eps, eps_hi, eps_c, tis_lo, tis_hi, kl_coef, kl_type, use_tis};
-  policy_loss_kernel<<<grid, 256, 0, st>>>(p);
-  sum_parts_kernel<<<1, 32, 0, st>>>(part, grid, PL_METRICS, metrics);
+  mb_launch(policy_loss_kernel, grid, 256, 0, st, p);
+  mb_launch(sum_parts_kernel, 1, 32, 0, st, part, grid, PL_METRICS, metrics);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
 extern "C" int mb_gae(const float* rewards, const float* values, const int* cu, int B, float gamma,
                       float lam, float* adv, float* ret, cudaStream_t st) {
   if (B == 0) return 0;
-  gae_kernel<<<(B + 127) / 128, 128, 0, st>>>(rewards, values, cu, B, gamma, lam, adv, ret);
+  mb_launch(gae_kernel, (B + 127) / 128, 128, 0, st, rewards, values, cu, B, gamma, lam, adv, ret);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
 extern "C" int mb_grpo_adv(const float* r, int ngroups, int gsize, int norm_std, float eps,
                            float* adv, cudaStream_t st) {
   if (ngroups == 0) return 0;
-  grpo_adv_kernel<<<(ngroups + 127) / 128, 128, 0, st>>>(r, ngroups, gsize, norm_std, eps, adv);
+  mb_launch(grpo_adv_kernel, (ngroups + 127) / 128, 128, 0, st, r, ngroups, gsize, norm_std, eps, adv);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -466,18 +488,18 @@ extern "C" int mb_sqnorm(const void* x, long long n, int is_bf16, float* part, f
   if (n == 0) return 0;
   const int grid = gsz(n, 256);
   if (is_bf16)
-    sqnorm_part_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, n, part);
+    mb_launch(sqnorm_part_kernel<__nv_bfloat16>, grid, 256, 0, st, (const __nv_bfloat16*)x, n, part);
   else
-    sqnorm_part_kernel<float><<<grid, 256, 0, st>>>((const float*)x, n, part);
-  sqnorm_final_kernel<<<1, 256, 0, st>>>(part, grid, out);
+    mb_launch(sqnorm_part_kernel<float>, grid, 256, 0, st, (const float*)x, n, part);
+  mb_launch(sqnorm_final_kernel, 1, 256, 0, st, part, grid, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
 extern "C" int mb_nonfinite(const void* x, long long n, int is_bf16, float* flag, cudaStream_t st) {
   if (n == 0) return 0;
   const int grid = gsz(n, 256);
-  if (is_bf16) nonfinite_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, n, flag);
-  else nonfinite_kernel<float><<<grid, 256, 0, st>>>((const float*)x, n, flag);
+  if (is_bf16) mb_launch(nonfinite_kernel<__nv_bfloat16>, grid, 256, 0, st, (const __nv_bfloat16*)x, n, flag);
+  else mb_launch(nonfinite_kernel<float>, grid, 256, 0, st, (const float*)x, n, flag);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -494,6 +516,6 @@ extern "C" int mb_adam(void* param, float* master, void* m, void* v, const void*
   p.bc2 = 1.f - powf(b2, (float)step);
   p.sqnorm = sqnorm; p.max_norm = max_norm; p.inv_loss_scale = inv_loss_scale; p.seed = seed;
   p.skip = skip;
-  adam_kernel<<<gsz(n, 256, 148 * 16), 256, 0, st>>>(p);
+  mb_launch(adam_kernel, gsz(n, 256, 148 * 16), 256, 0, st, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
