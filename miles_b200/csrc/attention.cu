@@ -339,7 +339,8 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const FwdParams p) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Decode: CTA = (sequence, kv head), one warp; rows = the G query heads of the group (G <= 16).
+// Decode: CTA = (sequence, kv head, chunk), four warps; rows = the G query heads of the group
+// (G <= 16).
 // KV cache layout: [num_slots, nkv, 128] with slot = page * 64 + offset; block j of a sequence
 // is page page_table[b][j].
 // ---------------------------------------------------------------------------------------------
@@ -357,13 +358,120 @@ struct DecParams {
 };
 
 constexpr int DEC_STAGES = 3;
+constexpr int DEC_WARPS = 4;
+// shared memory: Q (16 rows) | DEC_STAGES x (K tile, V tile) | P fragments | row-max partials
+constexpr int DEC_Q_BYTES = 16 * D * 2;
+constexpr int DEC_P_OFF = DEC_Q_BYTES + 2 * DEC_STAGES * TILE_BYTES;
+constexpr int DEC_RED_OFF = DEC_P_OFF + 4 * 4 * 32 * 4;
+constexpr int DEC_SMEM = DEC_RED_OFF + DEC_WARPS * 2 * 32 * 4;
 
-__global__ void __launch_bounds__(32) attn_decode_kernel(const DecParams p) {
+// kv_block_update computed by four warps of one CTA, with bit-identical results. Warp w owns
+// keys 16w..16w+15 of the score tile (score fragments s[2w], s[2w+1] of the one-warp version,
+// accumulated over the same k-steps) and output columns 32w..32w+31 (n-tiles 4w..4w+3, fed by
+// the same P fragments in the same k order). The row max is exact in any order; the row sum is
+// recomputed by every warp from the shared P fragments in the one-warp order (j = 0..7, then
+// the two xor shuffles), so every warp holds the same (m, l) as kv_block_update would.
+MB_DEVICE void kv_block_update_4w(const uint32_t (&qf)[8][4], uint32_t ktile, uint32_t vtile,
+                                  uint32_t* __restrict__ pbuf, float* __restrict__ red, int kbase,
+                                  int qpos, float scale_log2, float (&m)[2], float (&l)[2],
+                                  float (&o)[4][4], int warp, int lane) {
+  float s[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    uint32_t b00, b01, b10, b11;
+    load_b_nt(ktile, warp * 16, ks, lane, b00, b01, b10, b11);
+    mma16816(s[0], qf[ks], b00, b01);
+    mma16816(s[1], qf[ks], b10, b11);
+  }
+  const int c = lane & 3;
+  float mx0 = m[0], mx1 = m[1];
+#pragma unroll
+  for (int jj = 0; jj < 2; ++jj) {
+    const int k0 = kbase + (2 * warp + jj) * 8 + 2 * c;
+    s[jj][0] = (k0 > qpos) ? -INFINITY : s[jj][0] * scale_log2;
+    s[jj][1] = (k0 + 1 > qpos) ? -INFINITY : s[jj][1] * scale_log2;
+    s[jj][2] = (k0 > qpos) ? -INFINITY : s[jj][2] * scale_log2;
+    s[jj][3] = (k0 + 1 > qpos) ? -INFINITY : s[jj][3] * scale_log2;
+    mx0 = fmaxf(mx0, fmaxf(s[jj][0], s[jj][1]));
+    mx1 = fmaxf(mx1, fmaxf(s[jj][2], s[jj][3]));
+  }
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffff, mx0, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffff, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffff, mx1, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffff, mx1, 2));
+  red[(warp * 2 + 0) * 32 + lane] = mx0;
+  red[(warp * 2 + 1) * 32 + lane] = mx1;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < DEC_WARPS; ++w) {
+    mx0 = fmaxf(mx0, red[(w * 2 + 0) * 32 + lane]);
+    mx1 = fmaxf(mx1, red[(w * 2 + 1) * 32 + lane]);
+  }
+  const float sub0 = (mx0 == -INFINITY) ? 0.f : mx0;
+  const float sub1 = (mx1 == -INFINITY) ? 0.f : mx1;
+  const float alpha0 = exp2f(((m[0] == -INFINITY) ? sub0 : m[0]) - sub0);
+  const float alpha1 = exp2f(((m[1] == -INFINITY) ? sub1 : m[1]) - sub1);
+  m[0] = mx0;
+  m[1] = mx1;
+  // this warp's P fragments: kk = warp; registers 0/1 from jj = 0, registers 2/3 from jj = 1
+#pragma unroll
+  for (int jj = 0; jj < 2; ++jj) {
+    const float p0 = exp2f(s[jj][0] - sub0), p1 = exp2f(s[jj][1] - sub0);
+    const float p2 = exp2f(s[jj][2] - sub1), p3 = exp2f(s[jj][3] - sub1);
+    const __nv_bfloat162 h01 = __floats2bfloat162_rn(p0, p1);
+    const __nv_bfloat162 h23 = __floats2bfloat162_rn(p2, p3);
+    pbuf[(warp * 4 + jj * 2 + 0) * 32 + lane] = *reinterpret_cast<const uint32_t*>(&h01);
+    pbuf[(warp * 4 + jj * 2 + 1) * 32 + lane] = *reinterpret_cast<const uint32_t*>(&h23);
+  }
+  __syncthreads();
+  uint32_t pa[4][4];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) pa[kk][r] = pbuf[(kk * 4 + r) * 32 + lane];
+  float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int kk = j >> 1, r = (j & 1) * 2;
+    const __nv_bfloat162 h01 = *reinterpret_cast<const __nv_bfloat162*>(&pa[kk][r]);
+    const __nv_bfloat162 h23 = *reinterpret_cast<const __nv_bfloat162*>(&pa[kk][r + 1]);
+    rs0 += __low2float(h01) + __high2float(h01);
+    rs1 += __low2float(h23) + __high2float(h23);
+  }
+  rs0 += __shfl_xor_sync(0xffffffff, rs0, 1);
+  rs0 += __shfl_xor_sync(0xffffffff, rs0, 2);
+  rs1 += __shfl_xor_sync(0xffffffff, rs1, 1);
+  rs1 += __shfl_xor_sync(0xffffffff, rs1, 2);
+  l[0] = l[0] * alpha0 + rs0;
+  l[1] = l[1] * alpha1 + rs1;
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    o[n][0] *= alpha0; o[n][1] *= alpha0;
+    o[n][2] *= alpha1; o[n][3] *= alpha1;
+  }
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+    for (int pp = 0; pp < 2; ++pp) {
+      uint32_t b00, b01, b10, b11;
+      load_b_t(vtile, kk * 16, warp * 2 + pp, lane, b00, b01, b10, b11);
+      mma16816(o[2 * pp], pa[kk], b00, b01);
+      mma16816(o[2 * pp + 1], pa[kk], b10, b11);
+    }
+  }
+}
+
+// One CTA of four warps per (sequence, kv head, 1024-key chunk).
+__global__ void __launch_bounds__(DEC_WARPS * 32) attn_decode_kernel(const DecParams p) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sq = smem_u32(smem);
-  const int lane = threadIdx.x;
+  uint32_t* pbuf = reinterpret_cast<uint32_t*>(smem + DEC_P_OFF);
+  float* red = reinterpret_cast<float*>(smem + DEC_RED_OFF);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.x, hk = blockIdx.y;
   const int G = p.nq / p.nkv;
   const int ctx = p.ctx_lens[b];
@@ -376,10 +484,14 @@ __global__ void __launch_bounds__(32) attn_decode_kernel(const DecParams p) {
   const int jbeg = split * CHUNK_BLOCKS;
   const int nblocks = min(nblocks_all - jbeg, CHUNK_BLOCKS);
   const __nv_bfloat16* qbase = p.q + ((long long)b * p.nq + (long long)hk * G) * D;
-  load_tile(sq, qbase, [&](int r) { return (long long)r * D; }, G, lane, 32);
+  for (int i = tid; i < 16 * 16; i += DEC_WARPS * 32) {  // 16 query rows, rows >= G zero
+    const int r = i >> 4, ch = i & 15;
+    const bool ok = r < G;
+    cp_async16(sq + swz(r, ch), ok ? qbase + (long long)r * D + ch * 8 : qbase, ok);
+  }
   const long long kstride = (long long)p.nkv * D;
   auto kv_tile = [&](int j, int which) {
-    return sq + TILE_BYTES + (uint32_t)((j % DEC_STAGES) * 2 + which) * TILE_BYTES;
+    return sq + DEC_Q_BYTES + (uint32_t)((j % DEC_STAGES) * 2 + which) * TILE_BYTES;
   };
   auto load_kv = [&](int j) {  // j: block index local to this split
     const int jj = jbeg + j;
@@ -387,39 +499,51 @@ __global__ void __launch_bounds__(32) attn_decode_kernel(const DecParams p) {
     const int kv = min(BN, ctx - jj * BN);
     const long long slot0 = (long long)page * BN;
     load_tile(kv_tile(j, 0), p.kc + slot0 * kstride + (long long)hk * D,
-              [&](int r) { return (long long)r * kstride; }, kv, lane, 32);
+              [&](int r) { return (long long)r * kstride; }, kv, tid, DEC_WARPS * 32);
     load_tile(kv_tile(j, 1), p.vc + slot0 * kstride + (long long)hk * D,
-              [&](int r) { return (long long)r * kstride; }, kv, lane, 32);
+              [&](int r) { return (long long)r * kstride; }, kv, tid, DEC_WARPS * 32);
   };
 #pragma unroll
   for (int s = 0; s < DEC_STAGES - 1; ++s) {
     if (s < nblocks) load_kv(s);
     cp_async_commit();
   }
-  float o[16][4];
+  float o[4][4];
 #pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  for (int n = 0; n < 4; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
   uint32_t qf[8][4];
   for (int j = 0; j < nblocks; ++j) {
     if (j + DEC_STAGES - 1 < nblocks) load_kv(j + DEC_STAGES - 1);
     cp_async_commit();
     cp_async_wait<DEC_STAGES - 1>();
-    __syncwarp();
+    __syncthreads();
     if (j == 0) {
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) load_a(sq, 0, ks, lane, qf[ks]);
     }
-    kv_block_update(qf, kv_tile(j, 0), kv_tile(j, 1), (jbeg + j) * BN, qpos, qpos, p.scale_log2,
-                    m, l, o, lane);
-    __syncwarp();
+    kv_block_update_4w(qf, kv_tile(j, 0), kv_tile(j, 1), pbuf, red, (jbeg + j) * BN, qpos,
+                       p.scale_log2, m, l, o, warp, lane);
+    __syncthreads();  // the stage and P buffers are rewritten next iteration
   }
   cp_async_wait<0>();
   const int g = lane >> 2, c = lane & 3;
   if (nsplit == 1) {
+    // same arithmetic as finish_rows, for this warp's 32 columns
+    const float inv0 = l[0] > 0.f ? __frcp_rn(l[0]) : 0.f;
+    const float inv1 = l[1] > 0.f ? __frcp_rn(l[1]) : 0.f;
     __nv_bfloat16* out0 = p.o + ((long long)b * p.nq + (long long)hk * G + g) * D;
     __nv_bfloat16* out1 = out0 + 8 * D;
-    finish_rows(o, m, l, out0, out1, g < G, g + 8 < G, nullptr, nullptr, lane);
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const int col = (warp * 4 + n) * 8 + 2 * c;
+      if (g < G)
+        *reinterpret_cast<uint32_t*>(out0 + col) =
+            pack2(__fmul_rn(o[n][0], inv0), __fmul_rn(o[n][1], inv0));
+      if (g + 8 < G)
+        *reinterpret_cast<uint32_t*>(out1 + col) =
+            pack2(__fmul_rn(o[n][2], inv1), __fmul_rn(o[n][3], inv1));
+    }
     return;
   }
   // several chunks: publish this chunk's partial for the combine kernel
@@ -429,12 +553,12 @@ __global__ void __launch_bounds__(32) attn_decode_kernel(const DecParams p) {
     if (row >= G) continue;
     const long long base = ((long long)b * p.nq + (long long)hk * G + row) * p.nsplit_max + split;
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      const int col = n * 8 + 2 * c;
+    for (int n = 0; n < 4; ++n) {
+      const int col = (warp * 4 + n) * 8 + 2 * c;
       p.ws_o[base * D + col] = o[n][r * 2];
       p.ws_o[base * D + col + 1] = o[n][r * 2 + 1];
     }
-    if (c == 0) {
+    if (c == 0 && warp == 0) {
       p.ws_ml[base * 2] = m[r];
       p.ws_ml[base * 2 + 1] = l[r];
     }
@@ -792,13 +916,13 @@ extern "C" int mb_attn_decode(const void* q, const void* kc, const void* vc, voi
   DecParams p{(const __nv_bfloat16*)q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc,
               (__nv_bfloat16*)o, page_table, ctx_lens, max_pages, nq, nkv,
               softmax_scale * 1.4426950408889634f, ws_o, ws_ml, nsplit_max};
-  const int smem = (1 + 2 * DEC_STAGES) * TILE_BYTES;
+  const int smem = DEC_SMEM;
   static bool set = false;
   if (!set) {
     cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     set = true;
   }
-  mb_launch(attn_decode_kernel, dim3(B, nkv, nsplit_max), 32, smem, st, p);
+  mb_launch(attn_decode_kernel, dim3(B, nkv, nsplit_max), DEC_WARPS * 32, smem, st, p);
   if (nsplit_max > 1) {
     const long long w = (long long)B * nq;
     mb_launch(attn_decode_combine_kernel, (unsigned)((w + 7) / 8), 256, 0, st, p, B);

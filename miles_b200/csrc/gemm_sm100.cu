@@ -43,6 +43,7 @@ struct GemmParams {
   int epi;                   // 0 store bf16, 1 store f32, 2 accumulate into bf16, 3 accumulate into f32
   float alpha;
   int* err;                  // device error word (may be null)
+  int a_stage_bytes;         // bytes TMA writes for one A stage (K-major A may load < BM rows)
 };
 
 constexpr int BM = 128;
@@ -54,7 +55,10 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  // narrow N tiles serve small-M (decode) GEMMs, which are bound by the B stream: keep more
+  // stages in flight for them
+  static constexpr int STAGE_CAP = BN <= 32 ? 12 : 8;
+  static constexpr int STAGES = STAGES_RAW > STAGE_CAP ? STAGE_CAP : STAGES_RAW;
   static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -189,7 +193,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           if (!wait_or_abort(empty_bar + s, phase ^ 1, abort_flag, p.err)) goto producer_done;
           uint8_t* sa = smem + s * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
-          mbar_arrive_expect_tx(full_bar + s, Cfg::STAGE_BYTES);
+          mbar_arrive_expect_tx(full_bar + s, p.a_stage_bytes + Cfg::B_BYTES);
           if (A_MN) {
             tma_load_2d(sa, &tmA, full_bar + s, ti.m0, k);
             tma_load_2d(sa + 64 * 128, &tmA, full_bar + s, ti.m0 + 64, k);
@@ -261,32 +265,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       const int row = ti.m0 + quad * 32 + lane;
       const bool row_ok = row < p.M;
       const long long rbase = ti.c_off + (long long)row * p.ldc;
+      constexpr int CW = BN < 32 ? 16 : 32;  // columns per TMEM load
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < BN / CW; ++c) {
         uint32_t r[32];
         __syncwarp();
         if (!empty_k) {
-          const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32;
-          tmem_ld_32x32b_x32(taddr, r);
+          const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * CW;
+          if constexpr (CW == 32) tmem_ld_32x32b_x32(taddr, r);
+          else tmem_ld_32x32b_x16(taddr, r);
           tmem_ld_wait();
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = 0u;
+          for (int i = 0; i < CW; ++i) r[i] = 0u;
         }
         if (!row_ok) continue;
         if (empty_k && (p.epi & 2)) continue;  // accumulate nothing
-        const int col0 = ti.n0 + c * 32;
+        const int col0 = ti.n0 + c * CW;
         if (col0 >= p.N) continue;
         float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
-        const bool full_cols = col0 + 32 <= p.N;
+        for (int i = 0; i < CW; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+        const bool full_cols = col0 + CW <= p.N;
         if (p.epi == 0 || p.epi == 2) {
           __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.C) + rbase + col0;
           if (full_cols) {
             uint4* o4 = reinterpret_cast<uint4*>(out);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < CW / 8; ++q) {
               float w[8];
 #pragma unroll
               for (int i = 0; i < 8; ++i) w[i] = v[q * 8 + i];
@@ -304,7 +310,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
               o4[q] = pk;
             }
           } else {
-            for (int i = 0; i < 32 && col0 + i < p.N; ++i) {
+            for (int i = 0; i < CW && col0 + i < p.N; ++i) {
               float w = v[i];
               if (p.epi == 2) w += __bfloat162float(out[i]);
               out[i] = __float2bfloat16(w);
@@ -315,7 +321,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           if (full_cols) {
             float4* o4 = reinterpret_cast<float4*>(out);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
+            for (int q = 0; q < CW / 4; ++q) {
               float4 w = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
               if (p.epi == 3) {
                 const float4 o = o4[q];
@@ -324,7 +330,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
               o4[q] = w;
             }
           } else {
-            for (int i = 0; i < 32 && col0 + i < p.N; ++i) {
+            for (int i = 0; i < CW && col0 + i < p.N; ++i) {
               out[i] = (p.epi == 3 ? out[i] : 0.f) + v[i];
             }
           }
@@ -414,8 +420,11 @@ template <int BN, int MODE>
 static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                           const GemmParams& p, cudaStream_t st) {
   if (!a_mn && !b_mn) return launch_cfg<BN, false, false, MODE>(ta, tb, p, st);
-  if (!a_mn && b_mn) return launch_cfg<BN, false, true, MODE>(ta, tb, p, st);
-  if (a_mn && b_mn) return launch_cfg<BN, true, true, MODE>(ta, tb, p, st);
+  // narrow tiles (BN < 64) are built for K-major operands only (an MN-major B tile needs
+  // 64-element rows for the 128-byte swizzle)
+  if constexpr (BN < 64) return -5;
+  else if (!a_mn && b_mn) return launch_cfg<BN, false, true, MODE>(ta, tb, p, st);
+  else if (a_mn && b_mn) return launch_cfg<BN, true, true, MODE>(ta, tb, p, st);
   return -5;  // (MN, K) is not instantiated
 }
 
@@ -423,6 +432,8 @@ template <int MODE>
 static int dispatch_bn(int bn, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                        const GemmParams& p, cudaStream_t st) {
   switch (bn) {
+    case 16: return dispatch_major<16, MODE>(a_mn, b_mn, ta, tb, p, st);
+    case 32: return dispatch_major<32, MODE>(a_mn, b_mn, ta, tb, p, st);
     case 64: return dispatch_major<64, MODE>(a_mn, b_mn, ta, tb, p, st);
     case 128: return dispatch_major<128, MODE>(a_mn, b_mn, ta, tb, p, st);
     case 256: return dispatch_major<256, MODE>(a_mn, b_mn, ta, tb, p, st);
@@ -452,7 +463,10 @@ extern "C" int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, l
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) return -8;
   CUtensorMap ta, tb;
-  const uint32_t a_box_rows = a_mn ? BK : BM;
+  // Dense GEMMs with M < 128 (decode) load only the first round_up(M, 8) rows of each A tile:
+  // the remaining rows of the UMMA tile hold stale shared memory and produce output rows that
+  // are never stored (each output row depends on its own A row only).
+  const uint32_t a_box_rows = a_mn ? BK : (mode == 0 && M < BM ? (uint32_t)((M + 7) / 8 * 8) : BM);
   const uint32_t b_box_rows = b_mn ? BK : (uint32_t)bn;
   int rc = make_map(&ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a_rows, a_cols, lda, 64, a_box_rows);
   if (rc) return rc;
@@ -464,6 +478,7 @@ extern "C" int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, l
   p.group_offsets = group_offsets; p.num_groups = num_groups;
   p.b_rows_per_group = b_rows_per_group;
   p.epi = epi; p.alpha = alpha; p.err = err;
+  p.a_stage_bytes = a_mn ? BM * BK * 2 : (int)a_box_rows * BK * 2;
   switch (mode) {
     case 0: return dispatch_bn<0>(bn, a_mn, b_mn, ta, tb, p, stream);
     case 1: return dispatch_bn<1>(bn, a_mn, b_mn, ta, tb, p, stream);

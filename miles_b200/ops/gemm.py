@@ -25,15 +25,16 @@ def _num_sms(dev: torch.device) -> int:
     return _NUM_SMS[i]
 
 
-def _pick_bn(M: int, N: int, dev: torch.device, groups: int = 1) -> int:
+def _pick_bn(M: int, N: int, dev: torch.device, groups: int = 1, narrow: bool = False) -> int:
     """Widest N tile that still fills the machine. The N tile width never changes the
-    per-element reduction order, so the choice does not affect results."""
+    per-element reduction order, so the choice does not affect results. Tiles narrower than 64
+    (built for K-major operands only, ``narrow``) spread small-M decode GEMMs over more SMs."""
     mt = (M + 127) // 128 * groups
     sms = _num_sms(dev)
-    for bn in (256, 128):
+    for bn in ((256, 128, 64, 32) if narrow else (256, 128)):
         if mt * ((N + bn - 1) // bn) >= sms:
             return bn
-    return 64
+    return 16 if narrow else 64
 
 
 def gemm(a: torch.Tensor, a_mn: bool, b: torch.Tensor, b_mn: bool, out: torch.Tensor,
@@ -42,7 +43,8 @@ def gemm(a: torch.Tensor, a_mn: bool, b: torch.Tensor, b_mn: bool, out: torch.Te
          epi: int = EPI_STORE_BF16, alpha: float = 1.0, bn: int | None = None) -> torch.Tensor:
     """Raw launcher: out[M,N] (=|+=) alpha * A[M,K] @ B[N,K]^T with stored operand layouts."""
     if bn is None:
-        bn = _pick_bn(M, N, a.device, num_groups if mode == 2 else 1)
+        bn = _pick_bn(M, N, a.device, num_groups if mode == 2 else 1,
+                      narrow=not a_mn and not b_mn)
     lib().gemm(a, a_mn, b, b_mn, out, M, N, K, mode, group_offsets, num_groups,
                b_rows_per_group, c_group_stride, epi, alpha, bn, err_word(a.device))
     return out
@@ -180,7 +182,7 @@ def grouped_nt(x: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor,
                 out[a:b] = (x[a:b].float() @ w[e].float().t()).to(out.dtype)
         return out
     return gemm(x, False, w.view(E * N, K), False, out, R, N, K, mode=1, group_offsets=offsets,
-                num_groups=E, b_rows_per_group=N, bn=_pick_bn(R, N, x.device))
+                num_groups=E, b_rows_per_group=N, bn=_pick_bn(R, N, x.device, narrow=True))
 
 
 def grouped_nn(dy: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor,

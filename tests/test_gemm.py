@@ -29,7 +29,7 @@ def test_nt(M, N, K):
     check_device_error()
 
 
-@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("bn", [16, 32, 64, 128, 256])
 def test_tile_width_invariance(bn):
     """Different N-tile widths give bitwise identical results (batch invariance)."""
     torch.manual_seed(1)
@@ -43,6 +43,12 @@ def test_tile_width_invariance(bn):
     # row 7 computed alone equals row 7 computed inside the batch
     one = G.matmul_nt(a[7:8].contiguous(), b)
     assert torch.equal(one[0], ref[7])
+    # small-M GEMMs (short A boxes, narrow tiles) match the batched rows bitwise
+    for m in (3, 8, 40, 64, 100):
+        part = G.gemm(a[:m].contiguous(), False, b, False,
+                      torch.empty(m, 512, device="cuda", dtype=torch.bfloat16), m, 512, 1024,
+                      bn=bn)
+        assert torch.equal(part, ref[:m]), m
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 512, 384), (1000, 2048, 768)])
