@@ -11,7 +11,12 @@ int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, long long ld
                  const void* b, long long b_rows, long long b_cols, long long ldb, bool b_mn,
                  void* c, long long ldc, int M, int N, int K, int mode, const int* group_offsets,
                  int num_groups, int b_rows_per_group, long long c_group_stride, int epi,
-                 float alpha, int bn, int* err, cudaStream_t stream);
+                 float alpha, int bn, const int* group_counts, int* err, cudaStream_t stream);
+int mb_gemm_bf16_swiglu(const void* a, long long a_rows, long long lda, const void* b,
+                        long long b_rows, long long ldb, void* out, long long ldo, void* gu,
+                        long long ldgu, int M, int F, int K, int mode, const int* group_offsets,
+                        int num_groups, int bn, const int* group_counts, int* err,
+                        cudaStream_t stream);
 
 #ifdef __cplusplus
 }

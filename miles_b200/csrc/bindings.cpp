@@ -21,7 +21,7 @@ static cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().strea
 int64_t gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor c, int64_t M,
           int64_t N, int64_t K, int64_t mode, c10::optional<torch::Tensor> group_offsets,
           int64_t num_groups, int64_t b_rows_per_group, int64_t c_group_stride, int64_t epi,
-          double alpha, int64_t bn, torch::Tensor err) {
+          double alpha, int64_t bn, c10::optional<torch::Tensor> group_counts, torch::Tensor err) {
   CHECK_CUDA(a); CHECK_CUDA(b); CHECK_CUDA(c);
   CHECK_DT(a, at::kBFloat16); CHECK_DT(b, at::kBFloat16);
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "gemm operands must be 2-D views");
@@ -44,11 +44,48 @@ int64_t gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
   int rc = mb_gemm_bf16(a.data_ptr(), a.size(0), a.size(1), a.stride(0), a_mn, b.data_ptr(),
                         b.size(0), b.size(1), b.stride(0), b_mn, c.data_ptr(), ldc, (int)M, (int)N,
                         (int)K, (int)mode, go, (int)num_groups, (int)b_rows_per_group,
-                        c_group_stride, (int)epi, (float)alpha, (int)bn, err.data_ptr<int>(),
-                        cur_stream());
+                        c_group_stride, (int)epi, (float)alpha, (int)bn,
+                        group_counts.has_value() ? group_counts.value().data_ptr<int>() : nullptr,
+                        err.data_ptr<int>(), cur_stream());
   return rc;
 }
 
+// out[M, F] = silu(a @ b_gate^T) * (a @ b_up^T), b: [groups * 2F, K] ([gate; up] per group);
+// gu (optional) receives the [M, 2F] product.
+int64_t gemm_swiglu(torch::Tensor a, torch::Tensor b, torch::Tensor out,
+                    c10::optional<torch::Tensor> gu, int64_t M, int64_t F, int64_t K, int64_t mode,
+                    c10::optional<torch::Tensor> group_offsets, int64_t num_groups, int64_t bn,
+                    c10::optional<torch::Tensor> group_counts, torch::Tensor err) {
+  CHECK_CUDA(a); CHECK_CUDA(b); CHECK_CUDA(out);
+  CHECK_DT(a, at::kBFloat16); CHECK_DT(b, at::kBFloat16); CHECK_DT(out, at::kBFloat16);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm_swiglu operands must be 2-D");
+  CHECK_ROWMAJOR(a); CHECK_ROWMAJOR(b); CHECK_ROWMAJOR(out);
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0 && out.stride(0) % 8 == 0,
+              "row strides must be 16-byte multiples");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "operands must be 16-byte aligned");
+  void* gup = nullptr;
+  int64_t ldgu = 0;
+  if (gu.has_value()) {
+    CHECK_CUDA(gu.value()); CHECK_DT(gu.value(), at::kBFloat16); CHECK_ROWMAJOR(gu.value());
+    gup = gu.value().data_ptr();
+    ldgu = gu.value().stride(0);
+    TORCH_CHECK(ldgu % 8 == 0 && reinterpret_cast<uintptr_t>(gup) % 16 == 0, "gu misaligned");
+  }
+  const int* go = nullptr;
+  if (mode != 0) {
+    TORCH_CHECK(group_offsets.has_value(), "grouped mode needs group_offsets");
+    CHECK_DT(group_offsets.value(), at::kInt);
+    go = group_offsets.value().data_ptr<int>();
+  }
+  c10::cuda::CUDAGuard g(a.device());
+  return mb_gemm_bf16_swiglu(a.data_ptr(), a.size(0), a.stride(0), b.data_ptr(), b.size(0),
+                             b.stride(0), out.data_ptr(), out.stride(0), gup, ldgu, (int)M, (int)F,
+                             (int)K, (int)mode, go, (int)num_groups, (int)bn,
+                             group_counts.has_value() ? group_counts.value().data_ptr<int>() : nullptr,
+                             err.data_ptr<int>(), cur_stream());
+}
 
 // ------------------------------------------------------------------ thin wrappers
 // Optional tensors are passed as None; shapes are validated in miles_b200/ops/*.py and the
@@ -280,6 +317,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvfp4_quant", &nvfp4_quant);
   m.def("mxfp8_quant", &mxfp8_quant);
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM (dense / grouped)");
+  m.def("gemm_swiglu", &gemm_swiglu, "tcgen05 bf16 GEMM with fused SwiGLU epilogue");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);

@@ -44,6 +44,16 @@ struct GemmParams {
   float alpha;
   int* err;                  // device error word (may be null)
   int a_stage_bytes;         // bytes TMA writes for one A stage (K-major A may load < BM rows)
+  // Fused SwiGLU epilogue (epi 4): B holds [gate; up] rows per group (F each, N = 2F). An N tile
+  // of width BN takes BN/2 gate rows and the matching BN/2 up rows, so the epilogue sees both
+  // halves of its output columns and writes silu(gate) * up (width F, row stride ldc); when C2
+  // is set it also writes the [gate | up] product (width 2F, row stride ldc2) for the backward.
+  int swiglu_f;
+  void* C2;
+  long long ldc2;
+  // mode 1, optional: rows per group before padding; padding rows of the output are then not
+  // written (callers that run no backward over the padded buffer)
+  const int* group_counts;
 };
 
 constexpr int BM = 128;
@@ -59,7 +69,9 @@ struct GemmCfg {
   // stages in flight for them
   static constexpr int STAGE_CAP = BN <= 32 ? 12 : 8;
   static constexpr int STAGES = STAGES_RAW > STAGE_CAP ? STAGE_CAP : STAGES_RAW;
-  static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
+  // two accumulators of BN columns; tcgen05.alloc takes a power of two >= 32
+  static constexpr int TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128
+                                 : (2 * BN) <= 256 ? 256 : 512;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -136,6 +148,60 @@ MB_DEVICE bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort
   return false;
 }
 
+// SwiGLU epilogue of one accumulator (see GemmParams::swiglu_f). The gate/up products are
+// rounded to bf16 first and then combined with the same expression as the stand-alone SwiGLU
+// kernel, so the fused result is bitwise equal to GEMM followed by SwiGLU.
+template <int BN>
+MB_DEVICE void swiglu_epilogue(const GemmParams& p, const TileInfo& ti, uint32_t tbase, int row,
+                               bool row_ok, bool empty_k) {
+  constexpr int HB = BN / 2;
+  constexpr int CW = HB < 32 ? 16 : 32;
+#pragma unroll 1
+  for (int c = 0; c < HB / CW; ++c) {
+    uint32_t rg[32], ru[32];
+    __syncwarp();
+    if (!empty_k) {
+      if constexpr (CW == 32) {
+        tmem_ld_32x32b_x32(tbase + c * CW, rg);
+        tmem_ld_32x32b_x32(tbase + HB + c * CW, ru);
+      } else {
+        tmem_ld_32x32b_x16(tbase + c * CW, rg);
+        tmem_ld_32x32b_x16(tbase + HB + c * CW, ru);
+      }
+      tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int i = 0; i < CW; ++i) rg[i] = ru[i] = 0u;
+    }
+    if (!row_ok) continue;
+    const int col0 = (ti.n0 >> 1) + c * CW;  // column inside [0, F)
+    if (col0 >= p.swiglu_f) continue;
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.C) + ti.c_off + (long long)row * p.ldc + col0;
+    __nv_bfloat16* gu = p.C2 ? reinterpret_cast<__nv_bfloat16*>(p.C2) + (long long)row * p.ldc2 + col0
+                             : nullptr;
+#pragma unroll
+    for (int q = 0; q < CW / 8; ++q) {
+      uint4 og, ou, oa;
+      __nv_bfloat16* gb = reinterpret_cast<__nv_bfloat16*>(&og);
+      __nv_bfloat16* ub = reinterpret_cast<__nv_bfloat16*>(&ou);
+      __nv_bfloat16* ab = reinterpret_cast<__nv_bfloat16*>(&oa);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        gb[i] = __float2bfloat16(__uint_as_float(rg[q * 8 + i]) * p.alpha);
+        ub[i] = __float2bfloat16(__uint_as_float(ru[q * 8 + i]) * p.alpha);
+        const float g = __bfloat162float(gb[i]);
+        const float sg = g / (1.f + expf(-g));
+        ab[i] = __float2bfloat16(__bfloat162float(__float2bfloat16(sg)) * __bfloat162float(ub[i]));
+      }
+      reinterpret_cast<uint4*>(out)[q] = oa;
+      if (gu) {
+        reinterpret_cast<uint4*>(gu)[q] = og;
+        reinterpret_cast<uint4*>(gu + p.swiglu_f)[q] = ou;
+      }
+    }
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int MODE>
 __global__ void __launch_bounds__(192, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -204,6 +270,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
               tma_load_2d(sb + j * 64 * 128, &tmB, full_bar + s, ti.n0 + 64 * j, ti.brow0 + k);
+          } else if (p.swiglu_f) {
+            const int nh = ti.n0 >> 1;
+            tma_load_2d(sb, &tmB, full_bar + s, k, ti.brow0 + nh);
+            tma_load_2d(sb + (BN / 2) * 128, &tmB, full_bar + s, k, ti.brow0 + p.swiglu_f + nh);
           } else {
             tma_load_2d(sb, &tmB, full_bar + s, k, ti.brow0 + ti.n0);
           }
@@ -263,8 +333,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       tc_fence_after();
       const bool empty_k = ti.kend <= ti.kbeg;
       const int row = ti.m0 + quad * 32 + lane;
-      const bool row_ok = row < p.M;
+      bool row_ok = row < p.M;
+      if (MODE == 1 && p.group_counts)
+        row_ok = row_ok && row - __ldg(p.group_offsets + ti.g) < __ldg(p.group_counts + ti.g);
       const long long rbase = ti.c_off + (long long)row * p.ldc;
+      if constexpr (BN >= 32) {
+        if (p.epi == 4) {
+          swiglu_epilogue<BN>(p, ti, tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN, row,
+                              row_ok, empty_k);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty_bar + acc);
+          if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+          continue;
+        }
+      }
       constexpr int CW = BN < 32 ? 16 : 32;  // columns per TMEM load
 #pragma unroll 1
       for (int c = 0; c < BN / CW; ++c) {
@@ -436,6 +519,7 @@ static int dispatch_bn(int bn, bool a_mn, bool b_mn, const CUtensorMap& ta, cons
     case 32: return dispatch_major<32, MODE>(a_mn, b_mn, ta, tb, p, st);
     case 64: return dispatch_major<64, MODE>(a_mn, b_mn, ta, tb, p, st);
     case 128: return dispatch_major<128, MODE>(a_mn, b_mn, ta, tb, p, st);
+    case 192: return dispatch_major<192, MODE>(a_mn, b_mn, ta, tb, p, st);
     case 256: return dispatch_major<256, MODE>(a_mn, b_mn, ta, tb, p, st);
   }
   return -6;
@@ -449,12 +533,13 @@ static int dispatch_bn(int bn, bool a_mn, bool b_mn, const CUtensorMap& ta, cons
 //   b: pointer + stored shape [b_rows, b_cols]          (b_mn: b_rows = K(*groups), b_cols = N)
 // Returns 0 on success, negative on a configuration error.
 // ---------------------------------------------------------------------------------------------
-extern "C" int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, long long lda,
-                            bool a_mn, const void* b, long long b_rows, long long b_cols,
-                            long long ldb, bool b_mn, void* c, long long ldc, int M, int N, int K,
-                            int mode, const int* group_offsets, int num_groups,
-                            int b_rows_per_group, long long c_group_stride, int epi, float alpha,
-                            int bn, int* err, cudaStream_t stream) {
+static int gemm_entry(const void* a, long long a_rows, long long a_cols, long long lda, bool a_mn,
+                      const void* b, long long b_rows, long long b_cols, long long ldb, bool b_mn,
+                      void* c, long long ldc, int M, int N, int K, int mode,
+                      const int* group_offsets, int num_groups, int b_rows_per_group,
+                      long long c_group_stride, int epi, float alpha, int bn, int swiglu_f,
+                      void* c2, long long ldc2, const int* group_counts, int* err,
+                      cudaStream_t stream) {
   using namespace mb;
   if (a_mn && !b_mn) return -5;
   // The driver's tensor-map encoder needs a current context in the calling thread; a thread
@@ -467,7 +552,7 @@ extern "C" int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, l
   // the remaining rows of the UMMA tile hold stale shared memory and produce output rows that
   // are never stored (each output row depends on its own A row only).
   const uint32_t a_box_rows = a_mn ? BK : (mode == 0 && M < BM ? (uint32_t)((M + 7) / 8 * 8) : BM);
-  const uint32_t b_box_rows = b_mn ? BK : (uint32_t)bn;
+  const uint32_t b_box_rows = b_mn ? BK : (uint32_t)(swiglu_f ? bn / 2 : bn);
   int rc = make_map(&ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a_rows, a_cols, lda, 64, a_box_rows);
   if (rc) return rc;
   rc = make_map(&tb, b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b_rows, b_cols, ldb, 64, b_box_rows);
@@ -479,6 +564,8 @@ extern "C" int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, l
   p.b_rows_per_group = b_rows_per_group;
   p.epi = epi; p.alpha = alpha; p.err = err;
   p.a_stage_bytes = a_mn ? BM * BK * 2 : (int)a_box_rows * BK * 2;
+  p.swiglu_f = swiglu_f; p.C2 = c2; p.ldc2 = ldc2;
+  p.group_counts = mode == 1 ? group_counts : nullptr;
   switch (mode) {
     case 0: return dispatch_bn<0>(bn, a_mn, b_mn, ta, tb, p, stream);
     case 1: return dispatch_bn<1>(bn, a_mn, b_mn, ta, tb, p, stream);
@@ -487,3 +574,29 @@ extern "C" int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, l
   return -7;
 }
 
+
+extern "C" int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, long long lda,
+                            bool a_mn, const void* b, long long b_rows, long long b_cols,
+                            long long ldb, bool b_mn, void* c, long long ldc, int M, int N, int K,
+                            int mode, const int* group_offsets, int num_groups,
+                            int b_rows_per_group, long long c_group_stride, int epi, float alpha,
+                            int bn, const int* group_counts, int* err, cudaStream_t stream) {
+  if (epi == 4) return -7;
+  return gemm_entry(a, a_rows, a_cols, lda, a_mn, b, b_rows, b_cols, ldb, b_mn, c, ldc, M, N, K,
+                    mode, group_offsets, num_groups, b_rows_per_group, c_group_stride, epi, alpha,
+                    bn, 0, nullptr, 0, group_counts, err, stream);
+}
+
+// out[M, F] = silu(A B_gate^T) * (A B_up^T) with B = [gate; up] ([2F, K] per group, K-major),
+// optionally also storing the [M, 2F] product into gu (row stride ldgu). Dense (mode 0) or
+// grouped-M (mode 1). Requires F % (bn / 2) == 0 and bn >= 32.
+extern "C" int mb_gemm_bf16_swiglu(const void* a, long long a_rows, long long lda, const void* b,
+                                   long long b_rows, long long ldb, void* out, long long ldo,
+                                   void* gu, long long ldgu, int M, int F, int K, int mode,
+                                   const int* group_offsets, int num_groups, int bn,
+                                   const int* group_counts, int* err, cudaStream_t stream) {
+  if (bn < 32 || F % (bn / 2) || (mode != 0 && mode != 1)) return -1;
+  return gemm_entry(a, a_rows, K, lda, false, b, b_rows, K, ldb, false, out, ldo, M, 2 * F, K,
+                    mode, group_offsets, num_groups, 2 * F, 0, 4, 1.f, bn, F, gu, ldgu, group_counts,
+                    err, stream);
+}

@@ -201,11 +201,11 @@ class Transformer(torch.nn.Module):
                                 self.params[pre + "experts.w2"], self.router_cfgs[i],
                                 self.params.get(pre + "gate.e_score_correction_bias"), replay, record)
             if self.cfg.num_shared_experts:
-                s = swiglu(G.linear(x, self.params[pre + "shared_experts.gate_up_proj.weight"]))
+                s = G.linear_swiglu(x, self.params[pre + "shared_experts.gate_up_proj.weight"])
                 y = y + G.linear(s, self.params[pre + "shared_experts.down_proj.weight"])
             return y
-        gu = G.linear(x, self.params[pre + "gate_up_proj.weight"])
-        return G.linear(swiglu(gu), self.params[pre + "down_proj.weight"])
+        return G.linear(G.linear_swiglu(x, self.params[pre + "gate_up_proj.weight"]),
+                        self.params[pre + "down_proj.weight"])
 
     def _layer_train(self, i, m_prev, r_prev, meta, replay):
         cfg = self.cfg

@@ -25,28 +25,47 @@ def _num_sms(dev: torch.device) -> int:
     return _NUM_SMS[i]
 
 
-def _pick_bn(M: int, N: int, dev: torch.device, groups: int = 1, narrow: bool = False) -> int:
-    """Widest N tile that still fills the machine. The N tile width never changes the
-    per-element reduction order, so the choice does not affect results. Tiles narrower than 64
-    (built for K-major operands only, ``narrow``) spread small-M decode GEMMs over more SMs."""
-    mt = (M + 127) // 128 * groups
+def _pick_bn(M: int, N: int, dev: torch.device, groups: int = 1, narrow: bool = False,
+             mtiles: int | None = None) -> int:
+    """N tile width. The width never changes the per-element reduction order, so the choice does
+    not affect results. Problems with enough 256-wide tiles to fill the machine use 256; smaller
+    ones use the narrowest tile that still fits in one wave (a small-M GEMM costs about one
+    K-long UMMA chain per wave, so more CTAs stream the weights in parallel at no extra
+    latency). Tiles narrower than 64 are built for K-major operands only (``narrow``).
+    ``mtiles`` bounds the number of M tiles that hold rows (grouped GEMMs whose padded buffer is
+    mostly empty)."""
+    mt = mtiles if mtiles is not None else (M + 127) // 128 * groups
     sms = _num_sms(dev)
-    for bn in ((256, 128, 64, 32) if narrow else (256, 128)):
-        if mt * ((N + bn - 1) // bn) >= sms:
-            return bn
-    return 16 if narrow else 64
+    if mt * ((N + 255) // 256) >= sms:
+        # several waves: pick the width with the fewest column-rounds of work
+        # (waves x width), i.e. the least wave-quantisation loss; 256 unless another is >5% better
+        def cost(bn):
+            return -(-mt * ((N + bn - 1) // bn) // sms) * bn
+        best = 256
+        for bn in (192, 128):
+            if cost(bn) < 0.95 * cost(best):
+                best = bn
+        return best
+    cands = (256, 128, 64, 32, 16) if narrow else (256, 128, 64)
+    best = cands[0]
+    for bn in cands:
+        if mt * ((N + bn - 1) // bn) > sms:
+            break
+        best = bn
+    return best
 
 
 def gemm(a: torch.Tensor, a_mn: bool, b: torch.Tensor, b_mn: bool, out: torch.Tensor,
          M: int, N: int, K: int, *, mode: int = 0, group_offsets: torch.Tensor | None = None,
          num_groups: int = 1, b_rows_per_group: int = 0, c_group_stride: int = 0,
-         epi: int = EPI_STORE_BF16, alpha: float = 1.0, bn: int | None = None) -> torch.Tensor:
+         epi: int = EPI_STORE_BF16, alpha: float = 1.0, bn: int | None = None,
+         group_counts: torch.Tensor | None = None) -> torch.Tensor:
     """Raw launcher: out[M,N] (=|+=) alpha * A[M,K] @ B[N,K]^T with stored operand layouts."""
     if bn is None:
         bn = _pick_bn(M, N, a.device, num_groups if mode == 2 else 1,
                       narrow=not a_mn and not b_mn)
     lib().gemm(a, a_mn, b, b_mn, out, M, N, K, mode, group_offsets, num_groups,
-               b_rows_per_group, c_group_stride, epi, alpha, bn, err_word(a.device))
+               b_rows_per_group, c_group_stride, epi, alpha, bn, group_counts, err_word(a.device))
     return out
 
 
@@ -164,12 +183,102 @@ def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------------------------------
+# GEMM + SwiGLU (fused epilogue): a = silu(x @ w_gate^T) * (x @ w_up^T), w = [gate; up]
+# ------------------------------------------------------------------------------------------
+def _swiglu_bn(M: int, F: int, dev: torch.device, mtiles: int | None = None) -> int | None:
+    bn = _pick_bn(M, 2 * F, dev, narrow=True, mtiles=mtiles)
+    for cand in sorted({max(bn, 32), 32, 64, 128, 256}, key=lambda c: (c < max(bn, 32), c)):
+        if F % (cand // 2) == 0:
+            return cand
+    return None
+
+
+def gemm_swiglu(x: torch.Tensor, w2d: torch.Tensor, F: int, *, mode: int = 0,
+                offsets: torch.Tensor | None = None, num_groups: int = 1, save_gu: bool = False,
+                mtiles: int | None = None, counts: torch.Tensor | None = None):
+    """Fused GEMM + SwiGLU on stored operands (x: [M, K]; w2d: [groups * 2F, K]). Returns
+    (a [M, F], gu [M, 2F] or None). Bitwise equal to the GEMM followed by the SwiGLU kernel."""
+    M, K = x.shape
+    a = torch.empty(M, F, dtype=torch.bfloat16, device=x.device)
+    gu = torch.empty(M, 2 * F, dtype=torch.bfloat16, device=x.device) if save_gu else None
+    bn = _swiglu_bn(M, F, x.device, mtiles)
+    if bn is None:
+        raise ValueError(f"no N tile divides F={F}")
+    lib().gemm_swiglu(x, w2d, a, gu, M, F, K, mode, offsets, num_groups, bn, counts,
+                      err_word(x.device))
+    return a, gu
+
+
+class _LinearSwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w):
+        shp = x.shape
+        a, gu = gemm_swiglu(x.reshape(-1, shp[-1]).contiguous(), w, w.shape[0] // 2, save_gu=True)
+        ctx.save_for_backward(x, w, gu)
+        return a.view(*shp[:-1], w.shape[0] // 2)
+
+    @staticmethod
+    def backward(ctx, da):
+        x, w, gu = ctx.saved_tensors
+        from miles_b200.ops.norm import swiglu_bwd_raw
+
+        x2 = x.reshape(-1, x.shape[-1])
+        dgu = swiglu_bwd_raw(gu, da.reshape(-1, da.shape[-1]).contiguous())
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = matmul_nn(dgu, w).view(x.shape)
+        if ctx.needs_input_grad[1]:
+            dw = _accumulate_wgrad(w, dgu, x2)
+        return dx, dw
+
+
+def linear_swiglu(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """swiglu(x @ w.T) with w = [gate; up] ([2F, in]); one kernel on the GPU."""
+    if not use_native(x):
+        from miles_b200.ops.norm import swiglu_ref
+
+        return swiglu_ref(torch.nn.functional.linear(x, w))
+    if not (torch.is_grad_enabled() and (x.requires_grad or w.requires_grad)):
+        shp = x.shape
+        a, _ = gemm_swiglu(x.reshape(-1, shp[-1]).contiguous(), w, w.shape[0] // 2)
+        return a.view(*shp[:-1], w.shape[0] // 2)
+    return _LinearSwiGLU.apply(x, w)
+
+
+# ------------------------------------------------------------------------------------------
 # Grouped (MoE) GEMMs
 # ------------------------------------------------------------------------------------------
+def grouped_nt_swiglu(x: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor,
+                      n_rows: int | None = None, save_gu: bool = False,
+                      counts: torch.Tensor | None = None):
+    """Per-expert swiglu(x_e @ w[e]^T) with w: [E, 2F, K] ([gate; up] per expert). Returns
+    (a [R, F], gu [R, 2F] or None). With ``counts`` (rows per expert before padding) the
+    padding rows of the outputs are left unwritten."""
+    R, K = x.shape
+    E, N2, _ = w.shape
+    F = N2 // 2
+    if not use_native(x):
+        from miles_b200.ops.norm import swiglu_ref
+
+        gu = grouped_nt(x, w, offsets)
+        return swiglu_ref(gu), (gu if save_gu else None)
+    return gemm_swiglu(x, w.view(E * N2, K), F, mode=1, offsets=offsets, num_groups=E,
+                       save_gu=save_gu, mtiles=_grouped_mtiles(R, E, n_rows), counts=counts)
+
+
+def _grouped_mtiles(R: int, E: int, n_rows: int | None) -> int:
+    mt = (R + 127) // 128
+    if n_rows is None:
+        return mt
+    return min(mt, (n_rows + 127) // 128 + min(E, n_rows))
+
+
 def grouped_nt(x: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor,
-               out: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None, n_rows: int | None = None,
+               counts: torch.Tensor | None = None) -> torch.Tensor:
     """Per-expert x_e @ w[e]^T. x: [R, K] sorted by expert with segments padded to 128 rows
-    (offsets: int32 [E+1], device); w: [E, N, K]. Returns [R, N]."""
+    (offsets: int32 [E+1], device); w: [E, N, K]. Returns [R, N]. ``n_rows`` (the unpadded row
+    count, if known) bounds the number of M tiles that hold rows."""
     R, K = x.shape
     E, N, _ = w.shape
     if out is None:
@@ -182,7 +291,9 @@ def grouped_nt(x: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor,
                 out[a:b] = (x[a:b].float() @ w[e].float().t()).to(out.dtype)
         return out
     return gemm(x, False, w.view(E * N, K), False, out, R, N, K, mode=1, group_offsets=offsets,
-                num_groups=E, b_rows_per_group=N, bn=_pick_bn(R, N, x.device, narrow=True))
+                num_groups=E, b_rows_per_group=N,
+                bn=_pick_bn(R, N, x.device, narrow=True, mtiles=_grouped_mtiles(R, E, n_rows)),
+                group_counts=counts)
 
 
 def grouped_nn(dy: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor,

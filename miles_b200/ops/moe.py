@@ -115,11 +115,14 @@ def _accum_grouped_wgrad(w: torch.Tensor, dy: torch.Tensor, x: torch.Tensor, pla
     return G.grouped_tn(dy, x, plan.offsets, plan.E)
 
 
-def experts_forward(xs, w1, w2, plan: MoEPlan):
-    gu = G.grouped_nt(xs, w1, plan.offsets)
-    a = torch.empty(gu.shape[0], gu.shape[1] // 2, dtype=gu.dtype, device=gu.device)
-    lib().swiglu_fwd(gu, a, plan.total_rows)
-    ys = G.grouped_nt(a, w2, plan.offsets)
+def experts_forward(xs, w1, w2, plan: MoEPlan, save_gu: bool = True):
+    """gate_up GEMM with the SwiGLU fused into its epilogue, then the down GEMM. The
+    pre-activation gu is kept only when a backward follows."""
+    n = plan.T * plan.k
+    # without a backward the padding rows are never read: skip writing them
+    cnt = None if save_gu else plan.counts
+    a, gu = G.grouped_nt_swiglu(xs, w1, plan.offsets, n_rows=n, save_gu=save_gu, counts=cnt)
+    ys = G.grouped_nt(a, w2, plan.offsets, n_rows=n, counts=cnt)
     return gu, a, ys
 
 
@@ -137,7 +140,7 @@ class _MoE(torch.autograd.Function):
             record(idx)
         plan = MoEPlan(idx, cfg.E)
         xs = plan.gather(x, zero_pad=need_bwd)
-        gu, a, ys = experts_forward(xs, w1, w2, plan)
+        gu, a, ys = experts_forward(xs, w1, w2, plan, save_gu=need_bwd)
         y = torch.empty_like(x)
         lib().moe_combine(ys, plan.dest, w, None, y)
         ctx.save_for_backward(x, router_w, w1, w2, logits, idx, w, xs, gu, a, ys)

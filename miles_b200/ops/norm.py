@@ -250,6 +250,18 @@ class _SwiGLU(torch.autograd.Function):
         return dgu
 
 
+def swiglu_bwd_raw(gu: torch.Tensor, dout: torch.Tensor) -> torch.Tensor:
+    """d(gu) of the SwiGLU given its output grad (no autograd)."""
+    if not use_native(gu):
+        g = gu.detach().requires_grad_(True)
+        with torch.enable_grad():
+            swiglu_ref(g).backward(dout)
+        return g.grad
+    dgu = torch.empty_like(gu)
+    lib().swiglu_bwd(gu, dout, dgu, None)
+    return dgu
+
+
 def swiglu(gu: torch.Tensor) -> torch.Tensor:
     """silu(gate) * up over the two halves of the last dim ([gate | up])."""
     if not use_native(gu):

@@ -133,3 +133,39 @@ def test_worker_thread_and_error_path():
     with pytest.raises(RuntimeError):
         G.gemm(a, False, w, True, torch.empty(300, 512, device="cuda", dtype=torch.bfloat16),
                300, 512, 768, bn=96)
+
+
+@pytest.mark.parametrize("M,F,K", [(1, 768, 2048), (64, 768, 2048), (300, 1024, 512),
+                                   (2048, 9728 // 4, 640)])
+def test_swiglu_epilogue_bitwise(M, F, K):
+    """GEMM with the fused SwiGLU epilogue equals GEMM followed by the SwiGLU kernel, bit for
+    bit, and matches the fp32 reference."""
+    from miles_b200.ops.norm import swiglu, swiglu_ref
+
+    torch.manual_seed(3)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(2 * F, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    gu_ref = G.matmul_nt(x, w)
+    a_ref = swiglu(gu_ref)
+    a, gu = G.gemm_swiglu(x, w, F, save_gu=True)
+    assert torch.equal(gu, gu_ref)
+    assert torch.equal(a, a_ref)
+    _close(a, swiglu_ref((x.float() @ w.float().t()).to(torch.bfloat16)).float())
+
+
+def test_grouped_swiglu_bitwise():
+    from miles_b200.ops.moe import MoEPlan
+    from miles_b200.ops.norm import swiglu
+
+    torch.manual_seed(4)
+    E, F, K, T, k = 16, 256, 512, 40, 4
+    idx = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)]).int()
+    plan = MoEPlan(idx, E)
+    x = torch.randn(T, K, device="cuda", dtype=torch.bfloat16)
+    xs = plan.gather(x)
+    w = torch.randn(E, 2 * F, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    gu_ref = G.grouped_nt(xs, w, plan.offsets)
+    a, gu = G.grouped_nt_swiglu(xs, w, plan.offsets, n_rows=T * k, save_gu=True)
+    total = int(plan.offsets[-1])
+    assert torch.equal(gu[:total], gu_ref[:total])
+    assert torch.equal(a[:total], swiglu(gu_ref[:total]))
