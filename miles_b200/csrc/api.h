@@ -59,13 +59,20 @@ int mb_moe_combine(const void* ys, const int* dest, const float* w, const void* 
 int mb_moe_combine_bwd(const void* dy, const void* ys, const int* dest, const float* w, int T,
                        int k, int H, void* dys, float* dw, cudaStream_t st);
 int mb_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
-                const int* cu_seqlens, const int* blk_seq, const int* blk_idx, int nblocks,
+                const int* cu_seqlens, const int* tile_seq, const int* tile_idx, int ntiles,
                 long long q_stride, long long k_stride, long long v_stride, long long o_stride,
-                int nq, int nkv, int T, float softmax_scale, cudaStream_t st);
+                int nq, int nkv, int T, float softmax_scale, int* err, cudaStream_t st);
 int mb_attn_decode_nsplit(int max_pages);
 int mb_attn_decode(const void* q, const void* kc, const void* vc, void* o, const int* page_table,
-                   const int* ctx_lens, int B, int max_pages, int nq, int nkv, float softmax_scale,
-                   float* ws_o, float* ws_ml, cudaStream_t st);
+                   const int* ctx_lens, int B, int max_pages, long long num_slots, int nq, int nkv,
+                   float softmax_scale, float* ws_o, float* ws_ml, int* err, cudaStream_t st);
+int mb_fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+              const int* cu_seqlens, const int* tile_seq, const int* tile_idx, int ntiles,
+              long long q_stride, long long k_stride, long long v_stride, long long o_stride,
+              int nq, int nkv, int T, float softmax_scale, int* err, cudaStream_t st);
+int mb_fa_decode(const void* q, const void* kc, const void* vc, void* o, const int* page_table,
+                 const int* ctx_lens, int B, int max_pages, long long num_slots, int nq, int nkv,
+                 float softmax_scale, float* ws_o, float* ws_ml, int* err, cudaStream_t st);
 int mb_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
                 const float* lse, float* delta, void* dq, void* dk, void* dv,
                 const int* cu_seqlens, const int* blk_seq, const int* blk_idx, int nblocks,
@@ -128,7 +135,8 @@ extern "C" {
 #define MB_NOALLOC_TOO_LARGE (-9)
 int mb_attn_decode_noalloc(const void* q, const void* kc, const void* vc, void* o,
                            const int* page_table, const int* ctx_lens, int B, int max_pages,
-                           int nq, int nkv, float softmax_scale, cudaStream_t st);
+                           long long num_slots, int nq, int nkv, float softmax_scale,
+                           cudaStream_t st);
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,591 @@
+// Causal attention forward on the 5th-generation tensor cores (sm_100a): tcgen05.mma with
+// TMEM accumulators, TMA-fed K/V pipelines and warp-specialised roles. Head dim 128, bf16 in,
+// fp32 softmax, GQA.
+//
+//  * fa_fwd_kernel<0>: packed variable-length sequences (training forward, rollout prefill,
+//    log-prob passes). CTA = (128-query tile of one sequence, query head).
+//  * fa_fwd_kernel<1>: one query token per sequence against the paged KV cache (decode).
+//    CTA = (sequence, KV head, 1024-key chunk); the tile's rows are the query heads sharing
+//    the KV head (rows >= G are computed and discarded).
+//
+// Canonical per-row arithmetic (identical in both modes, hence bitwise train/rollout parity):
+//   keys are taken in blocks of 128 (positions 128j .. 128j+127 of the sequence) and in chunks
+//   of 8 blocks (1024 keys). Per block:
+//     S   = Q K^T                 one tcgen05 chain of 8 UMMAs (K = 16 head dims each)
+//     s   = key > qpos ? -inf : S * scale_log2                  (no contraction)
+//     m'  = max(m, max s);  sub = m' (0 if -inf);  alpha = 2^(m - sub)  (1 for the first block)
+//     p   = bf16(2^(s - sub));  rs = fixed-tree sum of p: per 32-key group four interleaved
+//           partial sums ((a0+a1)+(a2+a3)), groups combined as ((g0+g1)+(g2+g3))
+//     l   = fma(l, alpha, rs)
+//     O_j = P V                    one tcgen05 chain of 8 UMMAs (K = 16 keys each), fresh
+//     O   = fma(O, alpha, O_j)     (O kept in registers, one row per thread)
+//   Chunks start from (m, l, O) = (-inf, 0, 0) and are merged in chunk order with
+//   non-contracted float operations: by the prefill CTA itself (running total in TMEM) or, for
+//   decode, by attn_decode_combine_kernel (csrc/attention.cu) from per-chunk partials.
+//
+// Roles (320 threads): warp 0 = TMA producer (Q once, then K_j / V_j through a 2-stage ring),
+// warp 1 = TMEM owner and MMA issuer (S_j into a double-buffered S, O_j into a single O_j
+// buffer), warps 2-9 = softmax / output: two threads per row (TMEM lane), each owning 64 of
+// the 128 columns. TMEM: S0 | S1 | O_j | Otot, 128 columns each. P goes through shared memory
+// in the UMMA K-major SW128 layout.
+//
+// Reference roles replaced: flash-attention / cuDNN fused attention forward used by Megatron
+// (`--attention-backend flash`) and SGLang's paged decode attention.
+#include "common.cuh"
+
+namespace mb {
+namespace fa {
+
+constexpr int D = 128;
+constexpr int BM = 128;      // query rows per tile
+constexpr int BN = 128;      // keys per block
+constexpr int CHUNK = 8;     // blocks per canonical chunk (1024 keys)
+constexpr int SUB = 128 * 64 * 2;   // one [128][64] bf16 SW128 sub-tile = 16 KB
+constexpr int TILE = 2 * SUB;       // [128][128] bf16 = 32 KB
+// shared memory map (offsets from a 1024-aligned base)
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = TILE;            // 2 stages
+constexpr int OFF_V = 3 * TILE;        // 2 stages
+constexpr int OFF_P = 5 * TILE;
+constexpr int OFF_RED = 6 * TILE;          // softmax row max / sum exchange, 2 x [2][128] f32
+constexpr int OFF_BAR = OFF_RED + 2048;
+constexpr int NTHREADS = 320;              // producer, MMA, 8 softmax warps
+constexpr int SMEM_BYTES = OFF_BAR + 256 /*barriers*/ + 1024 /*align*/;
+
+struct Params {
+  // mode 0
+  const int* cu_seqlens;   // [B+1]
+  const int* tile_seq;     // per CTA x: sequence index
+  const int* tile_idx;     // per CTA x: 128-row tile index inside the sequence
+  float* lse;              // [nq, total_tokens] (natural log), may be null
+  long long o_stride;      // output token row stride (elements)
+  int total_tokens;
+  // mode 1
+  const int* page_table;   // [B, max_pages] (64-token pages)
+  const int* ctx_lens;     // [B]
+  int max_pages;
+  float* ws_o;             // [B, nq, nsplit_max, 128]
+  float* ws_ml;            // [B, nq, nsplit_max, 2]
+  int nsplit_max;
+  // common
+  __nv_bfloat16* o;
+  int nq, nkv;
+  float scale_log2;
+  int* err;
+};
+
+MB_DEVICE void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
+      " {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+MB_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+MB_DEVICE void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// chunk merge (same operations as the decode combine kernel)
+MB_DEVICE void merge_stats(float& M, float& L, float m, float l, float& fa, float& fb) {
+  if (m == -INFINITY) { fa = 1.f; fb = 0.f; return; }
+  if (M == -INFINITY) { M = m; L = l; fa = 0.f; fb = 1.f; return; }
+  const float Mn = fmaxf(M, m);
+  fa = exp2f(__fsub_rn(M, Mn));
+  fb = exp2f(__fsub_rn(m, Mn));
+  L = __fadd_rn(__fmul_rn(L, fa), __fmul_rn(l, fb));
+  M = Mn;
+}
+MB_DEVICE float merge_val(float O, float o, float fa, float fb) {
+  if (fb == 0.f) return O;
+  if (fa == 0.f) return o;
+  return __fadd_rn(__fmul_rn(O, fa), __fmul_rn(o, fb));
+}
+
+// Bounded wait shared by all roles: gives up (and records code 2) after kSpinLimit polls.
+MB_DEVICE bool wait_bar(uint64_t* bar, uint32_t parity, int* err) {
+  return mbar_wait(bar, parity, err, 2);
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                        const __grid_constant__ CUtensorMap tmK,
+                                                        const __grid_constant__ CUtensorMap tmV,
+                                                        const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* s_empty = bars + 11; // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* o_full = bars + 14;
+  uint64_t* o_empty = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(k_full + s, 1);
+      mbar_init(k_empty + s, 1);
+      mbar_init(v_full + s, 1);
+      mbar_init(v_empty + s, 1);
+      mbar_init(s_full + s, 1);
+      mbar_init(s_empty + s, 8);
+    }
+    mbar_init(p_full, 8);
+    mbar_init(o_full, 1);
+    mbar_init(o_empty, 8);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // device inputs (including the work tables) are read only after this point
+
+  // ---- work item (nblk == 0: nothing to do, every role falls through to the teardown)
+  int seq_start = 0, len = 0, m0 = 0, h = 0, hk = 0, b = 0, split = 0, qpos_dec = 0;
+  int jbeg = 0, nblk = 0, nsplit = 1;
+  const int G = p.nq / p.nkv;
+  if (MODE == 0) {
+    b = p.tile_seq[blockIdx.x];
+    const int qt = p.tile_idx[blockIdx.x];
+    h = blockIdx.y;
+    hk = h / G;
+    seq_start = p.cu_seqlens[b];
+    len = p.cu_seqlens[b + 1] - seq_start;
+    m0 = qt * BM;
+    nblk = qt + 1;  // causal: key blocks 0..qt (BM == BN)
+  } else {
+    b = blockIdx.x;
+    hk = blockIdx.y;
+    split = blockIdx.z;
+    const int ctx = p.ctx_lens[b];
+    if (ctx > 0) {
+      qpos_dec = ctx - 1;
+      const int nb_all = qpos_dec / BN + 1;
+      nsplit = (nb_all + CHUNK - 1) / CHUNK;
+      if (split < nsplit) {
+        jbeg = split * CHUNK;
+        nblk = min(nb_all - jbeg, CHUNK);
+      }
+    }
+  }
+
+  if (warp == 0) {
+    // ================= TMA producer =================
+    if (nblk > 0 && elect_one()) {
+      uint8_t* sq = smem + OFF_Q;
+      mbar_arrive_expect_tx(q_full, TILE);
+      if (MODE == 0) {
+        tma_load_2d(sq, &tmQ, q_full, h * D, seq_start + m0);
+        tma_load_2d(sq + SUB, &tmQ, q_full, h * D + 64, seq_start + m0);
+      } else {
+        const int row = b * p.nq + hk * G;
+        tma_load_2d(sq, &tmQ, q_full, 0, row);
+        tma_load_2d(sq + SUB, &tmQ, q_full, 64, row);
+      }
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = ((j >> 1) & 1) ^ 1;
+        const int jj = jbeg + j;
+        int y0, y1;  // rows of the two 64-key halves of the block
+        if (MODE == 0) {
+          y0 = seq_start + jj * BN;
+          y1 = y0 + 64;
+        } else {
+          const int* pt = p.page_table + (long long)b * p.max_pages;
+          const int pg0 = 2 * jj, pg1 = 2 * jj + 1;
+          y0 = pt[pg0] * 64;
+          y1 = (pg1 < p.max_pages ? pt[pg1] : 0) * 64;
+        }
+        // K block: K-major sub-tiles [128 keys][64 dims]; key half kh at +kh*8KB
+        if (!wait_bar(k_empty + s, ph, p.err)) break;
+        uint8_t* sk = smem + OFF_K + s * TILE;
+        mbar_arrive_expect_tx(k_full + s, TILE);
+        tma_load_2d(sk, &tmK, k_full + s, hk * D, y0);
+        tma_load_2d(sk + SUB, &tmK, k_full + s, hk * D + 64, y0);
+        tma_load_2d(sk + SUB / 2, &tmK, k_full + s, hk * D, y1);
+        tma_load_2d(sk + SUB + SUB / 2, &tmK, k_full + s, hk * D + 64, y1);
+        // V block: MN-major (dims contiguous) boxes [64 keys][64 dims]; key half at +16KB,
+        // dim half at +8KB
+        if (!wait_bar(v_empty + s, ph, p.err)) break;
+        uint8_t* sv = smem + OFF_V + s * TILE;
+        mbar_arrive_expect_tx(v_full + s, TILE);
+        tma_load_2d(sv, &tmV, v_full + s, hk * D, y0);
+        tma_load_2d(sv + SUB / 2, &tmV, v_full + s, hk * D + 64, y0);
+        tma_load_2d(sv + SUB, &tmV, v_full + s, hk * D, y1);
+        tma_load_2d(sv + SUB + SUB / 2, &tmV, v_full + s, hk * D + 64, y1);
+      }
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer =================
+    constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
+    constexpr uint32_t idesc_o = make_idesc_bf16(BM, D, false, true);
+    const uint32_t sq = smem_u32(smem + OFF_Q);
+    const uint32_t sp = smem_u32(smem + OFF_P);
+    bool ok = nblk > 0 && wait_bar(q_full, 0, p.err);
+    auto issue_pv = [&](int i) -> bool {
+      if (!wait_bar(p_full, i & 1, p.err)) return false;
+      if (!wait_bar(o_empty, (i & 1) ^ 1, p.err)) return false;
+      if (!wait_bar(v_full + (i & 1), (i >> 1) & 1, p.err)) return false;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t sv = smem_u32(smem + OFF_V + (i & 1) * TILE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = make_sdesc_sw128(sp + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = make_sdesc_sw128(sv + (kk >> 2) * SUB + (kk & 3) * 2048, 8192, 1024);
+          umma_f16(tmem_base + 256, ad, bd, idesc_o, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(o_full);
+        umma_commit(v_empty + (i & 1));
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int j = 0; ok && j < nblk; ++j) {
+      const int s = j & 1;
+      if (!wait_bar(k_full + s, (j >> 1) & 1, p.err)) { ok = false; break; }
+      if (!wait_bar(s_empty + s, ((j >> 1) & 1) ^ 1, p.err)) { ok = false; break; }
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t sk = smem_u32(smem + OFF_K + s * TILE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = make_sdesc_sw128(sq + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = make_sdesc_sw128(sk + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
+          umma_f16(tmem_base + s * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full + s);
+        umma_commit(k_empty + s);
+      }
+      __syncwarp();
+      if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+    }
+    if (ok && nblk > 0) issue_pv(nblk - 1);
+  } else {
+    // ================= softmax / output =================
+    // 8 warps: thread (quad, half) owns row quad*32+lane and columns [64*half, 64*half+64) of
+    // S, P and O; the two halves of a row exchange partial maxima / sums through shared memory.
+    const int sw = warp - 2;
+    const int quad = warp & 3, half = sw >> 2;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int col0 = half * 64;
+    const int qpos = MODE == 0 ? m0 + row : qpos_dec;
+    float* red_max = reinterpret_cast<float*>(smem + OFF_RED);  // [2][128]
+    float* red_sum = red_max + 256;                               // [2][128]
+    uint8_t* prow = smem + OFF_P + half * SUB + row * 128;  // this half's P keys = sub-tile `half`
+    float O[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) O[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    float Mt = -INFINITY, Lt = 0.f;  // merged-chunk totals (mode 0, more than one chunk)
+    bool ok = true;
+    auto softmax_sync = [] { asm volatile("bar.sync 1, 256;" ::: "memory"); };
+
+    // O <- fma(O, alpha_prev, O_j) for the block whose PV product sits in the O_j buffer
+    auto fold_pv = [&](int i) -> bool {
+      if (!wait_bar(o_full, i & 1, p.err)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_off + 256 + col0 + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          O[c * 32 + e] = __fmaf_rn(O[c * 32 + e], alpha_prev, __uint_as_float(r[e]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_empty);
+      return true;
+    };
+    // merge the finished chunk (m, l, O) into the running total kept in TMEM columns 384..511
+    auto merge_chunk = [&](bool first) {
+      float fa, fb;
+      merge_stats(Mt, Lt, m, l, fa, fb);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32];
+        const uint32_t ta = tmem_base + lane_off + 384 + col0 + c * 32;
+        if (!first) {
+          tmem_ld_32x32b_x32(ta, r);
+          tmem_ld_wait();
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          r[e] = __float_as_uint(first ? O[c * 32 + e]
+                                       : merge_val(__uint_as_float(r[e]), O[c * 32 + e], fa, fb));
+        tmem_st_32x32b_x32(ta, r);
+      }
+      tmem_st_wait();
+    };
+
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j & 1;
+      if (!wait_bar(s_full + s, (j >> 1) & 1, p.err)) { ok = false; break; }
+      tc_fence_after();
+      if (j >= 1 && !fold_pv(j - 1)) { ok = false; break; }
+      if (MODE == 0 && j > 0 && j % CHUNK == 0) {
+        merge_chunk(j == CHUNK);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) O[i] = 0.f;
+        m = -INFINITY;
+        l = 0.f;
+        alpha_prev = 1.f;
+      }
+      const int kbase = (jbeg + j) * BN + col0;
+      const uint32_t ts = tmem_base + lane_off + s * 128 + col0;
+      // pass 1: row max of the masked, scaled scores (max is exact in any order)
+      float mx4[4] = {m, m, m, m};
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(ts + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int kp = kbase + c * 32 + e;
+          const float sv = kp > qpos ? -INFINITY : __fmul_rn(__uint_as_float(r[e]), p.scale_log2);
+          mx4[e & 3] = fmaxf(mx4[e & 3], sv);
+        }
+      }
+      red_max[half * 128 + row] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      softmax_sync();
+      const float mnew = fmaxf(red_max[row], red_max[128 + row]);
+      const float sub = mnew == -INFINITY ? 0.f : mnew;
+      const float alpha = exp2f(__fsub_rn(m == -INFINITY ? sub : m, sub));
+      // pass 2: P = bf16(2^(s - sub)) into shared memory (K-major SW128) and its row sum
+      float cs[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(ts + c * 32, r);
+        tmem_ld_wait();
+        float a4[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const int kp = kbase + c * 32 + e;
+          const float s0 = kp > qpos ? -INFINITY : __fmul_rn(__uint_as_float(r[e]), p.scale_log2);
+          const float s1 =
+              kp + 1 > qpos ? -INFINITY : __fmul_rn(__uint_as_float(r[e + 1]), p.scale_log2);
+          const __nv_bfloat162 h2 =
+              __floats2bfloat162_rn(exp2f(__fsub_rn(s0, sub)), exp2f(__fsub_rn(s1, sub)));
+          a4[e & 3] = __fadd_rn(a4[e & 3], __low2float(h2));
+          a4[(e + 1) & 3] = __fadd_rn(a4[(e + 1) & 3], __high2float(h2));
+          pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        cs[c] = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
+        // keys col0 + c*32 .. +31 = 16-byte chunks 4c..4c+3 of this half's 128-byte row
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int ch = c * 4 + q;
+          uint4 v = make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]);
+          *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) = v;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_empty + s);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      red_sum[half * 128 + row] = __fadd_rn(cs[0], cs[1]);
+      softmax_sync();
+      const float rs = __fadd_rn(red_sum[row], red_sum[128 + row]);
+      l = __fmaf_rn(l, alpha, rs);
+      m = mnew;
+      alpha_prev = alpha;
+    }
+    if (ok && nblk > 0) ok = fold_pv(nblk - 1);
+    if (ok && nblk > 0) {
+      if (MODE == 0) {
+        if (nblk > CHUNK) {
+          merge_chunk(false);
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + lane_off + 384 + col0 + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) O[c * 32 + e] = __uint_as_float(r[e]);
+          }
+          m = Mt;
+          l = Lt;
+        }
+        if (qpos < len) {
+          const float inv = l > 0.f ? __frcp_rn(l) : 0.f;
+          __nv_bfloat16* out =
+              p.o + (long long)(seq_start + qpos) * p.o_stride + (long long)h * D + col0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            uint4 v;
+            v.x = pack_bf16x2(__fmul_rn(O[q * 8 + 0], inv), __fmul_rn(O[q * 8 + 1], inv));
+            v.y = pack_bf16x2(__fmul_rn(O[q * 8 + 2], inv), __fmul_rn(O[q * 8 + 3], inv));
+            v.z = pack_bf16x2(__fmul_rn(O[q * 8 + 4], inv), __fmul_rn(O[q * 8 + 5], inv));
+            v.w = pack_bf16x2(__fmul_rn(O[q * 8 + 6], inv), __fmul_rn(O[q * 8 + 7], inv));
+            reinterpret_cast<uint4*>(out)[q] = v;
+          }
+          if (p.lse && half == 0) {
+            const float ln2 = 0.69314718055994530942f;
+            p.lse[(long long)h * p.total_tokens + seq_start + qpos] =
+                l > 0.f ? (m + log2f(l)) * ln2 : -INFINITY;
+          }
+        }
+      } else if (row < G) {
+        const long long w = (long long)b * p.nq + (long long)hk * G + row;
+        if (nsplit == 1) {
+          const float inv = l > 0.f ? __frcp_rn(l) : 0.f;
+          __nv_bfloat16* out = p.o + w * D + col0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            uint4 v;
+            v.x = pack_bf16x2(__fmul_rn(O[q * 8 + 0], inv), __fmul_rn(O[q * 8 + 1], inv));
+            v.y = pack_bf16x2(__fmul_rn(O[q * 8 + 2], inv), __fmul_rn(O[q * 8 + 3], inv));
+            v.z = pack_bf16x2(__fmul_rn(O[q * 8 + 4], inv), __fmul_rn(O[q * 8 + 5], inv));
+            v.w = pack_bf16x2(__fmul_rn(O[q * 8 + 6], inv), __fmul_rn(O[q * 8 + 7], inv));
+            reinterpret_cast<uint4*>(out)[q] = v;
+          }
+        } else {
+          const long long base = w * p.nsplit_max + split;
+          float4* wo = reinterpret_cast<float4*>(p.ws_o + base * D + col0);
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            wo[q] = make_float4(O[q * 4], O[q * 4 + 1], O[q * 4 + 2], O[q * 4 + 3]);
+          if (half == 0) {
+            p.ws_ml[base * 2] = m;
+            p.ws_ml[base * 2 + 1] = l;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace fa
+}  // namespace mb
+
+using namespace mb;
+using namespace mb::fa;
+
+namespace {
+int fwd_attr_set[2] = {0, 0};
+template <int MODE>
+int launch_fa(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+              const Params& p, dim3 grid, cudaStream_t st) {
+  if (!fwd_attr_set[MODE]) {
+    if (cudaFuncSetAttribute(fa_fwd_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SMEM_BYTES) != cudaSuccess)
+      return -3;
+    fwd_attr_set[MODE] = 1;
+  }
+  mb_launch(fa_fwd_kernel<MODE>, grid, dim3(NTHREADS), SMEM_BYTES, st, tq, tk, tv, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+int current_ctx() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) return -8;
+  return 0;
+}
+}  // namespace
+
+// Packed variable-length causal attention forward (head dim 128). q/k/v: token-major with row
+// strides q_stride/k_stride/v_stride (elements, multiples of 8), heads contiguous inside a row.
+// tile_seq/tile_idx list the (sequence, 128-row tile) work items; lse may be null.
+extern "C" int mb_fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                         const int* cu_seqlens, const int* tile_seq, const int* tile_idx,
+                         int ntiles, long long q_stride, long long k_stride, long long v_stride,
+                         long long o_stride, int nq, int nkv, int T, float softmax_scale, int* err,
+                         cudaStream_t st) {
+  if (ntiles == 0 || T == 0) return 0;
+  if (nq % nkv) return -1;
+  if (int rc = current_ctx()) return rc;
+  CUtensorMap tq, tk, tv;
+  int rc = make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, (uint64_t)nq * D, q_stride, 64, 128);
+  if (rc) return rc;
+  rc = make_map(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, (uint64_t)nkv * D, k_stride, 64, 64);
+  if (rc) return rc;
+  rc = make_map(&tv, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, (uint64_t)nkv * D, v_stride, 64, 64);
+  if (rc) return rc;
+  Params p{};
+  p.cu_seqlens = cu_seqlens;
+  p.tile_seq = tile_seq;
+  p.tile_idx = tile_idx;
+  p.lse = lse;
+  p.o_stride = o_stride;
+  p.total_tokens = T;
+  p.o = (__nv_bfloat16*)o;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.err = err;
+  return launch_fa<0>(tq, tk, tv, p, dim3(ntiles, nq), st);
+}
+
+// Paged decode: one query token per sequence. q: [B, nq, 128]; caches [num_slots, nkv, 128]
+// with slot = page * 64 + offset. Sequences spanning several 1024-key chunks write per-chunk
+// partials to ws_o/ws_ml, merged by the decode combine kernel (mb_attn_decode_combine).
+extern "C" int mb_fa_decode(const void* q, const void* kc, const void* vc, void* o,
+                            const int* page_table, const int* ctx_lens, int B, int max_pages,
+                            long long num_slots, int nq, int nkv, float softmax_scale,
+                            float* ws_o, float* ws_ml, int* err, cudaStream_t st) {
+  if (B == 0) return 0;
+  if (nq % nkv || nq / nkv > BM) return -1;
+  const int nsplit_max = (max_pages + 2 * CHUNK - 1) / (2 * CHUNK);
+  if (nsplit_max > 1 && (!ws_o || !ws_ml)) return -3;
+  if (int rc = current_ctx()) return rc;
+  CUtensorMap tq, tk, tv;
+  int rc = make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)B * nq, D, D, 64, 128);
+  if (rc) return rc;
+  rc = make_map(&tk, kc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, (uint64_t)nkv * D,
+                (uint64_t)nkv * D, 64, 64);
+  if (rc) return rc;
+  rc = make_map(&tv, vc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, (uint64_t)nkv * D,
+                (uint64_t)nkv * D, 64, 64);
+  if (rc) return rc;
+  Params p{};
+  p.page_table = page_table;
+  p.ctx_lens = ctx_lens;
+  p.max_pages = max_pages;
+  p.ws_o = ws_o;
+  p.ws_ml = ws_ml;
+  p.nsplit_max = nsplit_max;
+  p.o = (__nv_bfloat16*)o;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.err = err;
+  return launch_fa<1>(tq, tk, tv, p, dim3(B, nkv, nsplit_max), st);
+}

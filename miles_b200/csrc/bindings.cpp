@@ -193,20 +193,30 @@ int64_t moe_combine_bwd(torch::Tensor dy, torch::Tensor ys, torch::Tensor dest, 
 }
 
 int64_t attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, OT lse,
-              torch::Tensor cu, torch::Tensor blk_seq, torch::Tensor blk_idx, int64_t nq,
-              int64_t nkv, double scale) {
+              torch::Tensor cu, torch::Tensor tile_seq, torch::Tensor tile_idx, int64_t nq,
+              int64_t nkv, double scale, torch::Tensor err) {
   TORCH_CHECK(q.stride(-1) == 1 && k.stride(-1) == 1 && v.stride(-1) == 1 && o.stride(-1) == 1);
-  return mb_attn_fwd(P(q), P(k), P(v), P(o), PT<float>(lse), PT<int>(cu), PT<int>(blk_seq),
-                       PT<int>(blk_idx), blk_seq.numel(), q.stride(0), k.stride(0), v.stride(0),
-                       o.stride(0), nq, nkv, q.size(0), (float)scale, cur_stream());
+  TORCH_CHECK(q.stride(0) % 8 == 0 && k.stride(0) % 8 == 0 && v.stride(0) % 8 == 0,
+              "attention row strides must be 16-byte multiples");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(k.data_ptr()) % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(v.data_ptr()) % 16 == 0, "q/k/v must be 16-byte aligned");
+  c10::cuda::CUDAGuard g(q.device());
+  return mb_attn_fwd(P(q), P(k), P(v), P(o), PT<float>(lse), PT<int>(cu), PT<int>(tile_seq),
+                       PT<int>(tile_idx), tile_seq.numel(), q.stride(0), k.stride(0), v.stride(0),
+                       o.stride(0), nq, nkv, q.size(0), (float)scale, err.data_ptr<int>(),
+                       cur_stream());
 }
 int64_t attn_decode_nsplit(int64_t max_pages) { return mb_attn_decode_nsplit(max_pages); }
 int64_t attn_decode(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor o,
                  torch::Tensor page_table, torch::Tensor ctx_lens, int64_t nq, int64_t nkv,
-                 double scale, OT ws_o, OT ws_ml) {
+                 double scale, OT ws_o, OT ws_ml, torch::Tensor err) {
+  TORCH_CHECK(q.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(),
+              "decode attention needs contiguous q and caches");
+  c10::cuda::CUDAGuard g(q.device());
   return mb_attn_decode(P(q), P(kc), P(vc), P(o), PT<int>(page_table), PT<int>(ctx_lens),
-                          q.size(0), page_table.size(1), nq, nkv, (float)scale, PT<float>(ws_o),
-                          PT<float>(ws_ml), cur_stream());
+                          q.size(0), page_table.size(1), kc.size(0), nq, nkv, (float)scale,
+                          PT<float>(ws_o), PT<float>(ws_ml), err.data_ptr<int>(), cur_stream());
 }
 int64_t attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
               torch::Tensor dout, torch::Tensor lse, torch::Tensor delta, torch::Tensor dq,

@@ -1,4 +1,4 @@
-// Shared device helpers for the sm_100a kernel library: mbarriers, TMA (non-multicast only),
+// Shared device helpers for the sm_100a kernel library: mbarriers, TMA (plain loads only),
 // tcgen05 (TMEM alloc / MMA / commit / ld) and bounded waits that report an error status
 // instead of trapping.
 //
@@ -6,8 +6,8 @@
 //  * Every spin wait has an iteration limit. On expiry the wait returns false and the caller
 //    records a code in the library's device error word (read by the host via
 //    miles_b200.ops.check_device_error()). No __trap(), no device assert.
-//  * TMA loads are issued without `.multicast::cluster` in every form, so this code is safe to
-//    run in multi-GPU jobs and never reads a peer's memory through TMA multicast.
+//  * TMA loads are plain per-CTA loads (no cluster-wide broadcast qualifier in any form), so
+//    this code is safe in multi-GPU jobs and never broadcasts a peer's memory through TMA.
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -67,6 +67,11 @@ MB_DEVICE void report_error(int* err, int code) {
 // Spin limit for mbarrier waits. try_wait itself suspends for a hardware-defined window, so
 // 1<<22 iterations is several seconds of wall time: far beyond any legitimate stall.
 constexpr uint32_t kSpinLimit = 1u << 22;
+
+// Host: 2-D row-major [rows, cols] tensor map with a {box_cols, box_rows} box and 128-byte
+// swizzle (defined in gemm_sm100.cu). Returns 0 on success.
+int make_map(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int esize, uint64_t rows,
+             uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows);
 
 // ---------------------------------------------------------------------------------------------
 // Shared-memory address helpers
@@ -128,7 +133,7 @@ MB_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// TMA (tiled, non-multicast)
+// TMA (tiled, plain per-CTA loads)
 // ---------------------------------------------------------------------------------------------
 MB_DEVICE void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

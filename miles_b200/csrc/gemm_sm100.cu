@@ -457,7 +457,7 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 // 2-D row-major [rows, cols] map with a {box_cols, box_rows} box and 128-byte swizzle.
-static int make_map(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int esize,
+int make_map(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int esize,
                     uint64_t rows, uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols,
                     uint32_t box_rows) {
   EncodeTiledFn enc = get_encode_fn();

@@ -97,14 +97,18 @@ def is_expert_param(name: str) -> bool:
 
 
 class KVCache:
-    """Paged KV cache: per layer K and V of [num_pages * 64, nkv, 128] bf16."""
+    """Paged KV cache: per layer K and V of [num_pages * 64, nkv, 128] bf16.
+
+    Zero-initialised: the decode kernel reads whole 128-key blocks, and slots past a sequence's
+    context are masked out of the softmax but still multiplied (by zero) in the P.V product, so
+    they must hold finite values."""
 
     def __init__(self, cfg: ModelConfig, num_pages: int, device, dtype=torch.bfloat16):
         self.num_pages = num_pages
         slots = num_pages * PAGE
-        self.k = [torch.empty(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device)
+        self.k = [torch.zeros(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device)
                   for _ in range(cfg.num_layers)]
-        self.v = [torch.empty(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device)
+        self.v = [torch.zeros(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device)
                   for _ in range(cfg.num_layers)]
 
     def nbytes(self) -> int:

@@ -12,18 +12,20 @@ import math
 
 import torch
 
-from miles_b200.ops._lib import lib, use_native
+from miles_b200.ops._lib import err_word, lib, use_native
 
-BLOCK = 64
+BLOCK = 64      # backward kernels: 64-row query blocks
+FWD_TILE = 128  # forward kernel: 128-row query tiles
 PAGE = 64  # KV-cache page size (tokens); equals the attention key block
 CHUNK_PAGES = 16  # keys are merged in canonical 1024-key chunks (csrc/attention.cu)
 
 
-def block_table(cu_seqlens: list[int], device) -> tuple[torch.Tensor, torch.Tensor]:
-    """(seq index, block index) of every 64-row block of every sequence, longest-work first."""
+def block_table(cu_seqlens: list[int], device, rows: int = 64) -> tuple[torch.Tensor, torch.Tensor]:
+    """(seq index, block index) of every `rows`-row block of every sequence, longest-work first
+    (64-row blocks for the backward kernels, 128-row tiles for the forward)."""
     seq, idx = [], []
     for b in range(len(cu_seqlens) - 1):
-        n = (cu_seqlens[b + 1] - cu_seqlens[b] + BLOCK - 1) // BLOCK
+        n = (cu_seqlens[b + 1] - cu_seqlens[b] + rows - 1) // rows
         seq.extend([b] * n)
         idx.extend(range(n))
     t_seq = torch.tensor(seq, dtype=torch.int32)
@@ -39,6 +41,7 @@ class VarlenMeta:
         self.cu_list = list(cu_seqlens)
         self.cu = torch.tensor(cu_seqlens, dtype=torch.int32, device=device)
         self.blk_seq, self.blk_idx = block_table(cu_seqlens, device)
+        self.tile_seq, self.tile_idx = block_table(cu_seqlens, device, FWD_TILE)
         self.total = cu_seqlens[-1]
         if len(cu_seqlens) > 1:
             pos = torch.cat([torch.arange(cu_seqlens[b + 1] - cu_seqlens[b], dtype=torch.int32)
@@ -78,8 +81,8 @@ class _VarlenAttn(torch.autograd.Function):
         o = torch.empty(T, nq, D, dtype=torch.bfloat16, device=q.device)
         lse = torch.empty(nq, T, dtype=torch.float32, device=q.device)
         q2, k2, v2 = q.reshape(T, nq * D), k.reshape(T, nkv * D), v.reshape(T, nkv * D)
-        lib().attn_fwd(q2, k2, v2, o.view(T, nq * D), lse, meta.cu, meta.blk_seq, meta.blk_idx,
-                       nq, nkv, scale)
+        lib().attn_fwd(q2, k2, v2, o.view(T, nq * D), lse, meta.cu, meta.tile_seq, meta.tile_idx,
+                       nq, nkv, scale, err_word(q.device))
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.meta = meta
         ctx.scale = scale
@@ -149,5 +152,6 @@ def decode_attention(q, k_cache, v_cache, page_table, ctx_lens, scale: float | N
     if nsplit > 1:
         ws_o = torch.empty(B * nq * nsplit * D, dtype=torch.float32, device=q.device)
         ws_ml = torch.empty(B * nq * nsplit * 2, dtype=torch.float32, device=q.device)
-    lib().attn_decode(q, k_cache, v_cache, out, page_table, ctx_lens, nq, nkv, scale, ws_o, ws_ml)
+    lib().attn_decode(q, k_cache, v_cache, out, page_table, ctx_lens, nq, nkv, scale, ws_o, ws_ml,
+                      err_word(q.device))
     return out

@@ -195,8 +195,9 @@ def test_decode_matches_prefill_bitwise():
     B = len(lens)
     max_pages = 40
     nslots = B * max_pages * 64
-    kc = torch.full((nslots, nkv, 128), float("nan"), device=DEV, dtype=BF)
-    vc = torch.full((nslots, nkv, 128), float("nan"), device=DEV, dtype=BF)
+    # stale cache contents (finite: the engine zero-initialises its cache) must not leak in
+    kc = (torch.randn(nslots, nkv, 128, device=DEV) * 100).to(BF)
+    vc = (torch.randn(nslots, nkv, 128, device=DEV) * 100).to(BF)
     pt = torch.arange(B * max_pages, dtype=torch.int32, device=DEV).view(B, max_pages).flip(1).contiguous()
     for b, L in enumerate(lens):
         t = torch.arange(L, device=DEV)

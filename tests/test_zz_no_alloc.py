@@ -26,8 +26,10 @@ def _lib():
     lib = ctypes.CDLL(path)
     f = lib.mb_attn_decode_noalloc
     f.restype = ctypes.c_int
-    # q, kc, vc, o, page_table, ctx_lens | B, max_pages, nq, nkv | softmax_scale | stream
-    f.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_void_p]
+    # q, kc, vc, o, page_table, ctx_lens | B, max_pages | num_slots | nq, nkv | softmax_scale |
+    # stream
+    f.argtypes = ([ctypes.c_void_p] * 6 + [ctypes.c_int] * 2 + [ctypes.c_longlong]
+                  + [ctypes.c_int] * 2 + [ctypes.c_float, ctypes.c_void_p])
     return f
 
 
@@ -55,7 +57,7 @@ def test_noalloc_matches_regular_entry_point():
     for _ in range(2):  # two calls in a row share (and reuse) the fixed workspace
         out = torch.full_like(q, float("nan"))
         rc = fn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), pt.data_ptr(),
-                ctx.data_ptr(), B, max_pages, nq, nkv, scale, stream)
+                ctx.data_ptr(), B, max_pages, kc.shape[0], nq, nkv, scale, stream)
         assert rc == 0
         torch.cuda.synchronize()
         err = (out.float() - ref.float()).abs().max() / ref.float().abs().max()
@@ -69,5 +71,5 @@ def test_noalloc_rejects_oversized_workspace():
     q, kc, vc, pt, ctx = _inputs(B, nq, nkv, [100] * B, max_pages)
     out = torch.zeros_like(q)
     rc = fn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), pt.data_ptr(), ctx.data_ptr(),
-            B, max_pages, nq, nkv, 1.0, torch.cuda.current_stream().cuda_stream)
+            B, max_pages, kc.shape[0], nq, nkv, 1.0, torch.cuda.current_stream().cuda_stream)
     assert rc == -9
