@@ -12,9 +12,10 @@
 //   keys are taken in blocks of 128 (positions 128j .. 128j+127 of the sequence) and in chunks
 //   of 8 blocks (1024 keys). Per block:
 //     S   = Q K^T                 one tcgen05 chain of 8 UMMAs (K = 16 head dims each)
-//     s   = key > qpos ? -inf : S * scale_log2                  (no contraction)
-//     m'  = max(m, max s);  sub = m' (0 if -inf);  alpha = 2^(m - sub)  (1 for the first block)
-//     p   = bf16(2^(s - sub));  rs = fixed-tree sum of p: per 32-key group four interleaved
+//     m'  = max(m, max(S over keys <= qpos) * scale_log2);  sub = m' (0 if -inf)
+//     alpha = 2^(m - sub)  (1 for the first block)
+//     p   = key > qpos ? 0 : bf16(ex2.approx(fma(S, scale_log2, -sub)))
+//           rs = fixed-tree sum of p: per 32-key group four interleaved
 //           partial sums ((a0+a1)+(a2+a3)), groups combined as ((g0+g1)+(g2+g3))
 //     l   = fma(l, alpha, rs)
 //     O_j = P V                    one tcgen05 chain of 8 UMMAs (K = 16 keys each), fresh
@@ -26,8 +27,9 @@
 // Roles (320 threads): warp 0 = TMA producer (Q once, then K_j / V_j through a 2-stage ring),
 // warp 1 = TMEM owner and MMA issuer (S_j into a double-buffered S, O_j into a single O_j
 // buffer), warps 2-9 = softmax / output: two threads per row (TMEM lane), each owning 64 of
-// the 128 columns. TMEM: S0 | S1 | O_j | Otot, 128 columns each. P goes through shared memory
-// in the UMMA K-major SW128 layout.
+// the 128 columns. TMEM: S0 | S1 | O_j | Otot, 128 columns each. P_j (bf16) is written over the
+// first 64 columns of its S buffer and fed to the P.V UMMA straight from tensor memory; the
+// O_j fold is deferred to the end of the next block so the softmax never waits for P.V.
 //
 // Reference roles replaced: flash-attention / cuDNN fused attention forward used by Megatron
 // (`--attention-backend flash`) and SGLang's paged decode attention.
@@ -46,8 +48,7 @@ constexpr int TILE = 2 * SUB;       // [128][128] bf16 = 32 KB
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = TILE;            // 2 stages
 constexpr int OFF_V = 3 * TILE;        // 2 stages
-constexpr int OFF_P = 5 * TILE;
-constexpr int OFF_RED = 6 * TILE;          // softmax row max / sum exchange, 2 x [2][128] f32
+constexpr int OFF_RED = 5 * TILE;          // softmax row max / sum exchange, 2 x [2][128] f32
 constexpr int OFF_BAR = OFF_RED + 2048;
 constexpr int NTHREADS = 320;              // producer, MMA, 8 softmax warps
 constexpr int SMEM_BYTES = OFF_BAR + 256 /*barriers*/ + 1024 /*align*/;
@@ -85,6 +86,22 @@ MB_DEVICE void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: A (M = 128 lanes x K = 16 bf16 packed in 8
+// 32-bit columns, lower k in the low half) is read from tensor memory.
+MB_DEVICE void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// 2^x with the hardware approximation (ex2.approx.ftz): one MUFU op; 2^-inf = +0.
+MB_DEVICE float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 MB_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 MB_DEVICE void fence_proxy_async_smem() {
@@ -127,8 +144,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
   uint64_t* v_full = bars + 5;   // [2]
   uint64_t* v_empty = bars + 7;  // [2]
   uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_empty = bars + 11; // [2]
-  uint64_t* p_full = bars + 13;
+  uint64_t* p_full = bars + 11;  // [2] one per S/P buffer
   uint64_t* o_full = bars + 14;
   uint64_t* o_empty = bars + 15;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
@@ -143,9 +159,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
       mbar_init(v_full + s, 1);
       mbar_init(v_empty + s, 1);
       mbar_init(s_full + s, 1);
-      mbar_init(s_empty + s, 8);
     }
     mbar_init(p_full, 8);
+    mbar_init(p_full + 1, 8);
     mbar_init(o_full, 1);
     mbar_init(o_empty, 8);
     fence_barrier_init();
@@ -244,20 +260,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
     constexpr uint32_t idesc_o = make_idesc_bf16(BM, D, false, true);
     const uint32_t sq = smem_u32(smem + OFF_Q);
-    const uint32_t sp = smem_u32(smem + OFF_P);
     bool ok = nblk > 0 && wait_bar(q_full, 0, p.err);
+    // O_i = P_i V_i with P_i (bf16) in TMEM columns 0..63 of S buffer i&1
     auto issue_pv = [&](int i) -> bool {
-      if (!wait_bar(p_full, i & 1, p.err)) return false;
+      if (!wait_bar(p_full + (i & 1), (i >> 1) & 1, p.err)) return false;
       if (!wait_bar(o_empty, (i & 1) ^ 1, p.err)) return false;
       if (!wait_bar(v_full + (i & 1), (i >> 1) & 1, p.err)) return false;
       tc_fence_after();
       if (elect_one()) {
         const uint32_t sv = smem_u32(smem + OFF_V + (i & 1) * TILE);
+        const uint32_t pa = tmem_base + (i & 1) * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = make_sdesc_sw128(sp + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = make_sdesc_sw128(sv + (kk >> 2) * SUB + (kk & 3) * 2048, 8192, 1024);
-          umma_f16(tmem_base + 256, ad, bd, idesc_o, kk > 0 ? 1u : 0u);
+          umma_f16_ts(tmem_base + 256, pa + kk * 8, bd, idesc_o, kk > 0 ? 1u : 0u);
         }
         umma_commit(o_full);
         umma_commit(v_empty + (i & 1));
@@ -268,7 +284,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     for (int j = 0; ok && j < nblk; ++j) {
       const int s = j & 1;
       if (!wait_bar(k_full + s, (j >> 1) & 1, p.err)) { ok = false; break; }
-      if (!wait_bar(s_empty + s, ((j >> 1) & 1) ^ 1, p.err)) { ok = false; break; }
+      // S buffer s last held P_{j-2}: wait until PV_{j-2} has consumed it
+      if (j >= 2 && !wait_bar(o_full, (j - 2) & 1, p.err)) { ok = false; break; }
       tc_fence_after();
       if (elect_one()) {
         const uint32_t sk = smem_u32(smem + OFF_K + s * TILE);
@@ -297,7 +314,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     const int qpos = MODE == 0 ? m0 + row : qpos_dec;
     float* red_max = reinterpret_cast<float*>(smem + OFF_RED);  // [2][128]
     float* red_sum = red_max + 256;                               // [2][128]
-    uint8_t* prow = smem + OFF_P + half * SUB + row * 128;  // this half's P keys = sub-tile `half`
     float O[64];
 #pragma unroll
     for (int i = 0; i < 64; ++i) O[i] = 0.f;
@@ -345,12 +361,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
       tmem_st_wait();
     };
 
+    // Block j: S_j -> P_j (into the S buffer) while PV_{j-1} runs; O_{j-1} is folded in at the
+    // end of the block (at the start at chunk boundaries, where the chunk must be complete).
     for (int j = 0; j < nblk; ++j) {
       const int s = j & 1;
       if (!wait_bar(s_full + s, (j >> 1) & 1, p.err)) { ok = false; break; }
       tc_fence_after();
-      if (j >= 1 && !fold_pv(j - 1)) { ok = false; break; }
-      if (MODE == 0 && j > 0 && j % CHUNK == 0) {
+      const bool boundary = MODE == 0 && j > 0 && j % CHUNK == 0;
+      if (boundary) {
+        if (!fold_pv(j - 1)) { ok = false; break; }
         merge_chunk(j == CHUNK);
 #pragma unroll
         for (int i = 0; i < 64; ++i) O[i] = 0.f;
@@ -360,66 +379,72 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
       }
       const int kbase = (jbeg + j) * BN + col0;
       const uint32_t ts = tmem_base + lane_off + s * 128 + col0;
-      // pass 1: row max of the masked, scaled scores (max is exact in any order)
-      float mx4[4] = {m, m, m, m};
+      // Only the last block of a row's key range can hold keys past the query position (for
+      // prefill tiles the diagonal block, for decode the block holding the context end).
+      const bool masked = j == nblk - 1;
+      // pass 1: row max of the raw scores (scaling is monotonic, so max(S) * scale equals the
+      // max of the scaled scores bit for bit; max is exact in any order)
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(ts + c * 32, r);
         tmem_ld_wait();
+        if (masked) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int kp = kbase + c * 32 + e;
-          const float sv = kp > qpos ? -INFINITY : __fmul_rn(__uint_as_float(r[e]), p.scale_log2);
-          mx4[e & 3] = fmaxf(mx4[e & 3], sv);
+          for (int e = 0; e < 32; ++e) {
+            const float sv = kbase + c * 32 + e > qpos ? -INFINITY : __uint_as_float(r[e]);
+            mx4[e & 3] = fmaxf(mx4[e & 3], sv);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(r[e]));
         }
       }
       red_max[half * 128 + row] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       softmax_sync();
-      const float mnew = fmaxf(red_max[row], red_max[128 + row]);
+      const float raw = fmaxf(red_max[row], red_max[128 + row]);
+      const float mnew = fmaxf(m, raw == -INFINITY ? -INFINITY : __fmul_rn(raw, p.scale_log2));
       const float sub = mnew == -INFINITY ? 0.f : mnew;
       const float alpha = exp2f(__fsub_rn(m == -INFINITY ? sub : m, sub));
-      // pass 2: P = bf16(2^(s - sub)) into shared memory (K-major SW128) and its row sum
+      const float nsub = -sub;
+      // pass 2: P = bf16(2^fma(S, scale, -sub)) (kept packed in registers) and its row sum
       float cs[2];
+      uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(ts + c * 32, r);
         tmem_ld_wait();
         float a4[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const int kp = kbase + c * 32 + e;
-          const float s0 = kp > qpos ? -INFINITY : __fmul_rn(__uint_as_float(r[e]), p.scale_log2);
-          const float s1 =
-              kp + 1 > qpos ? -INFINITY : __fmul_rn(__uint_as_float(r[e + 1]), p.scale_log2);
-          const __nv_bfloat162 h2 =
-              __floats2bfloat162_rn(exp2f(__fsub_rn(s0, sub)), exp2f(__fsub_rn(s1, sub)));
+          float p0 = ex2_approx(__fmaf_rn(__uint_as_float(r[e]), p.scale_log2, nsub));
+          float p1 = ex2_approx(__fmaf_rn(__uint_as_float(r[e + 1]), p.scale_log2, nsub));
+          if (masked) {
+            const int kp = kbase + c * 32 + e;
+            p0 = kp > qpos ? 0.f : p0;
+            p1 = kp + 1 > qpos ? 0.f : p1;
+          }
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
           a4[e & 3] = __fadd_rn(a4[e & 3], __low2float(h2));
           a4[(e + 1) & 3] = __fadd_rn(a4[(e + 1) & 3], __high2float(h2));
-          pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+          pk[c * 16 + (e >> 1)] = *reinterpret_cast<const uint32_t*>(&h2);
         }
         cs[c] = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
-        // keys col0 + c*32 .. +31 = 16-byte chunks 4c..4c+3 of this half's 128-byte row
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ch = c * 4 + q;
-          uint4 v = make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]);
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) = v;
-        }
       }
+      red_sum[half * 128 + row] = __fadd_rn(cs[0], cs[1]);
+      softmax_sync();  // both halves have read S_j: P_j may overwrite its first 64 columns
+      // P_j: this thread's 64 keys = packed columns half*32 .. half*32+31 of the S buffer
+      tmem_st_32x32b_x32(tmem_base + lane_off + s * 128 + half * 32, pk);
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty + s);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      red_sum[half * 128 + row] = __fadd_rn(cs[0], cs[1]);
-      softmax_sync();
+      if (lane == 0) mbar_arrive(p_full + s);
       const float rs = __fadd_rn(red_sum[row], red_sum[128 + row]);
       l = __fmaf_rn(l, alpha, rs);
       m = mnew;
+      if (j >= 1 && !boundary && !fold_pv(j - 1)) { ok = false; break; }
       alpha_prev = alpha;
     }
     if (ok && nblk > 0) ok = fold_pv(nblk - 1);
