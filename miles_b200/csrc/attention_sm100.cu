@@ -3,10 +3,12 @@
 // fp32 softmax, GQA.
 //
 //  * fa_fwd_kernel<0>: packed variable-length sequences (training forward, rollout prefill,
-//    log-prob passes). CTA = (128-query tile of one sequence, query head).
+//    log-prob passes). Work item = (128-query tile of one sequence, query head).
 //  * fa_fwd_kernel<1>: one query token per sequence against the paged KV cache (decode).
-//    CTA = (sequence, KV head, 1024-key chunk); the tile's rows are the query heads sharing
-//    the KV head (rows >= G are computed and discarded).
+//    Work item = (sequence, KV head, 1024-key chunk); the tile's rows are the query heads
+//    sharing the KV head (rows >= G are discarded; warps holding none of them idle).
+//  Both are persistent: one CTA per SM walks a strided list of work items, so the barrier /
+//  TMEM set-up is paid once per SM and the K/V pipeline runs across item boundaries.
 //
 // Canonical per-row arithmetic (identical in both modes, hence bitwise train/rollout parity):
 //   keys are taken in blocks of 128 (positions 128j .. 128j+127 of the sequence) and in chunks
@@ -34,6 +36,8 @@
 // Reference roles replaced: flash-attention / cuDNN fused attention forward used by Megatron
 // (`--attention-backend flash`) and SGLang's paged decode attention.
 #include "common.cuh"
+
+#include <cstdio>
 
 namespace mb {
 namespace fa {
@@ -129,11 +133,57 @@ MB_DEVICE bool wait_bar(uint64_t* bar, uint32_t parity, int* err) {
   return mbar_wait(bar, parity, err, 2);
 }
 
+// Work item of a persistent CTA. Mode 0: item = (128-row tile, query head), heads fastest so
+// that CTAs running at the same time share K/V tiles through L2. Mode 1: item = (sequence, KV
+// head, chunk). nblk == 0 marks an empty item (decode chunk past the context end).
+struct Item {
+  int seq_start, len, m0, h, hk, b, split, qpos, jbeg, nblk, nsplit;
+};
+
+template <int MODE>
+MB_DEVICE Item get_item(const Params& p, int t) {
+  Item it{};
+  const int G = p.nq / p.nkv;
+  if (MODE == 0) {
+    const int tile = t / p.nq;
+    it.h = t - tile * p.nq;
+    it.hk = it.h / G;
+    it.b = p.tile_seq[tile];
+    const int qt = p.tile_idx[tile];
+    it.seq_start = p.cu_seqlens[it.b];
+    it.len = p.cu_seqlens[it.b + 1] - it.seq_start;
+    it.m0 = qt * BM;
+    it.nblk = qt + 1;  // causal: key blocks 0..qt (BM == BN)
+    it.nsplit = 1;
+  } else {
+    const int per_b = p.nkv * p.nsplit_max;
+    it.b = t / per_b;
+    const int r = t - it.b * per_b;
+    it.hk = r / p.nsplit_max;
+    it.split = r - it.hk * p.nsplit_max;
+    const int ctx = p.ctx_lens[it.b];
+    it.nblk = 0;
+    it.nsplit = 1;
+    if (ctx > 0) {
+      it.qpos = ctx - 1;
+      const int nb_all = it.qpos / BN + 1;
+      it.nsplit = (nb_all + CHUNK - 1) / CHUNK;
+      if (it.split < it.nsplit) {
+        it.jbeg = it.split * CHUNK;
+        it.nblk = min(nb_all - it.jbeg, CHUNK);
+      }
+    }
+  }
+  return it;
+}
+
+// Persistent: CTA x processes items x, x + gridDim.x, ... Buffer indices and mbarrier parities
+// follow running counters (blocks `g`, non-empty items `n`) that every role advances alike.
 template <int MODE>
 __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                         const __grid_constant__ CUtensorMap tmK,
                                                         const __grid_constant__ CUtensorMap tmV,
-                                                        const Params p) {
+                                                        const Params p, int n_items) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -145,23 +195,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
   uint64_t* v_empty = bars + 7;  // [2]
   uint64_t* s_full = bars + 9;   // [2]
   uint64_t* p_full = bars + 11;  // [2] one per S/P buffer
+  uint64_t* q_empty = bars + 13;
   uint64_t* o_full = bars + 14;
   uint64_t* o_empty = bars + 15;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.nq / p.nkv;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(k_full + s, 1);
       mbar_init(k_empty + s, 1);
       mbar_init(v_full + s, 1);
       mbar_init(v_empty + s, 1);
       mbar_init(s_full + s, 1);
+      mbar_init(p_full + s, 8);
     }
-    mbar_init(p_full, 8);
-    mbar_init(p_full + 1, 8);
     mbar_init(o_full, 1);
     mbar_init(o_empty, 8);
     fence_barrier_init();
@@ -180,79 +232,57 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
   pdl_trigger();
   pdl_wait();  // device inputs (including the work tables) are read only after this point
 
-  // ---- work item (nblk == 0: nothing to do, every role falls through to the teardown)
-  int seq_start = 0, len = 0, m0 = 0, h = 0, hk = 0, b = 0, split = 0, qpos_dec = 0;
-  int jbeg = 0, nblk = 0, nsplit = 1;
-  const int G = p.nq / p.nkv;
-  if (MODE == 0) {
-    b = p.tile_seq[blockIdx.x];
-    const int qt = p.tile_idx[blockIdx.x];
-    h = blockIdx.y;
-    hk = h / G;
-    seq_start = p.cu_seqlens[b];
-    len = p.cu_seqlens[b + 1] - seq_start;
-    m0 = qt * BM;
-    nblk = qt + 1;  // causal: key blocks 0..qt (BM == BN)
-  } else {
-    b = blockIdx.x;
-    hk = blockIdx.y;
-    split = blockIdx.z;
-    const int ctx = p.ctx_lens[b];
-    if (ctx > 0) {
-      qpos_dec = ctx - 1;
-      const int nb_all = qpos_dec / BN + 1;
-      nsplit = (nb_all + CHUNK - 1) / CHUNK;
-      if (split < nsplit) {
-        jbeg = split * CHUNK;
-        nblk = min(nb_all - jbeg, CHUNK);
-      }
-    }
-  }
-
   if (warp == 0) {
     // ================= TMA producer =================
-    if (nblk > 0 && elect_one()) {
-      uint8_t* sq = smem + OFF_Q;
-      mbar_arrive_expect_tx(q_full, TILE);
-      if (MODE == 0) {
-        tma_load_2d(sq, &tmQ, q_full, h * D, seq_start + m0);
-        tma_load_2d(sq + SUB, &tmQ, q_full, h * D + 64, seq_start + m0);
-      } else {
-        const int row = b * p.nq + hk * G;
-        tma_load_2d(sq, &tmQ, q_full, 0, row);
-        tma_load_2d(sq + SUB, &tmQ, q_full, 64, row);
-      }
-      for (int j = 0; j < nblk; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = ((j >> 1) & 1) ^ 1;
-        const int jj = jbeg + j;
-        int y0, y1;  // rows of the two 64-key halves of the block
+    if (elect_one()) {
+      int g = 0, n = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < n_items; t += gridDim.x) {
+        const Item it = get_item<MODE>(p, t);
+        if (it.nblk == 0) continue;
+        uint8_t* sq = smem + OFF_Q;
+        if (!wait_bar(q_empty, (n & 1) ^ 1, p.err)) break;
+        mbar_arrive_expect_tx(q_full, TILE);
         if (MODE == 0) {
-          y0 = seq_start + jj * BN;
-          y1 = y0 + 64;
+          tma_load_2d(sq, &tmQ, q_full, it.h * D, it.seq_start + it.m0);
+          tma_load_2d(sq + SUB, &tmQ, q_full, it.h * D + 64, it.seq_start + it.m0);
         } else {
-          const int* pt = p.page_table + (long long)b * p.max_pages;
-          const int pg0 = 2 * jj, pg1 = 2 * jj + 1;
-          y0 = pt[pg0] * 64;
-          y1 = (pg1 < p.max_pages ? pt[pg1] : 0) * 64;
+          const int row = it.b * p.nq + it.hk * G;
+          tma_load_2d(sq, &tmQ, q_full, 0, row);
+          tma_load_2d(sq + SUB, &tmQ, q_full, 64, row);
         }
-        // K block: K-major sub-tiles [128 keys][64 dims]; key half kh at +kh*8KB
-        if (!wait_bar(k_empty + s, ph, p.err)) break;
-        uint8_t* sk = smem + OFF_K + s * TILE;
-        mbar_arrive_expect_tx(k_full + s, TILE);
-        tma_load_2d(sk, &tmK, k_full + s, hk * D, y0);
-        tma_load_2d(sk + SUB, &tmK, k_full + s, hk * D + 64, y0);
-        tma_load_2d(sk + SUB / 2, &tmK, k_full + s, hk * D, y1);
-        tma_load_2d(sk + SUB + SUB / 2, &tmK, k_full + s, hk * D + 64, y1);
-        // V block: MN-major (dims contiguous) boxes [64 keys][64 dims]; key half at +16KB,
-        // dim half at +8KB
-        if (!wait_bar(v_empty + s, ph, p.err)) break;
-        uint8_t* sv = smem + OFF_V + s * TILE;
-        mbar_arrive_expect_tx(v_full + s, TILE);
-        tma_load_2d(sv, &tmV, v_full + s, hk * D, y0);
-        tma_load_2d(sv + SUB / 2, &tmV, v_full + s, hk * D + 64, y0);
-        tma_load_2d(sv + SUB, &tmV, v_full + s, hk * D, y1);
-        tma_load_2d(sv + SUB + SUB / 2, &tmV, v_full + s, hk * D + 64, y1);
+        ++n;
+        for (int j = 0; j < it.nblk; ++j, ++g) {
+          const int s = g & 1;
+          const uint32_t ph = ((g >> 1) & 1) ^ 1;
+          const int jj = it.jbeg + j;
+          int y0, y1;  // rows of the two 64-key halves of the block
+          if (MODE == 0) {
+            y0 = it.seq_start + jj * BN;
+            y1 = y0 + 64;
+          } else {
+            const int* pt = p.page_table + (long long)it.b * p.max_pages;
+            const int pg1 = 2 * jj + 1;
+            y0 = pt[2 * jj] * 64;
+            y1 = (pg1 < p.max_pages ? pt[pg1] : 0) * 64;
+          }
+          // K block: K-major sub-tiles [128 keys][64 dims]; key half at +8KB
+          if (!wait_bar(k_empty + s, ph, p.err)) { ok = false; break; }
+          uint8_t* sk = smem + OFF_K + s * TILE;
+          mbar_arrive_expect_tx(k_full + s, TILE);
+          tma_load_2d(sk, &tmK, k_full + s, it.hk * D, y0);
+          tma_load_2d(sk + SUB, &tmK, k_full + s, it.hk * D + 64, y0);
+          tma_load_2d(sk + SUB / 2, &tmK, k_full + s, it.hk * D, y1);
+          tma_load_2d(sk + SUB + SUB / 2, &tmK, k_full + s, it.hk * D + 64, y1);
+          // V block: MN-major boxes [64 keys][64 dims]; key half at +16KB, dim half at +8KB
+          if (!wait_bar(v_empty + s, ph, p.err)) { ok = false; break; }
+          uint8_t* sv = smem + OFF_V + s * TILE;
+          mbar_arrive_expect_tx(v_full + s, TILE);
+          tma_load_2d(sv, &tmV, v_full + s, it.hk * D, y0);
+          tma_load_2d(sv + SUB / 2, &tmV, v_full + s, it.hk * D + 64, y0);
+          tma_load_2d(sv + SUB, &tmV, v_full + s, it.hk * D, y1);
+          tma_load_2d(sv + SUB + SUB / 2, &tmV, v_full + s, it.hk * D + 64, y1);
+        }
       }
     }
   } else if (warp == 1) {
@@ -260,8 +290,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
     constexpr uint32_t idesc_o = make_idesc_bf16(BM, D, false, true);
     const uint32_t sq = smem_u32(smem + OFF_Q);
-    bool ok = nblk > 0 && wait_bar(q_full, 0, p.err);
-    // O_i = P_i V_i with P_i (bf16) in TMEM columns 0..63 of S buffer i&1
+    // O_i = P_i V_i with P_i (bf16) in TMEM columns 0..63 of S buffer i&1 (i: running block)
     auto issue_pv = [&](int i) -> bool {
       if (!wait_bar(p_full + (i & 1), (i >> 1) & 1, p.err)) return false;
       if (!wait_bar(o_empty, (i & 1) ^ 1, p.err)) return false;
@@ -281,27 +310,36 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
       __syncwarp();
       return true;
     };
-    for (int j = 0; ok && j < nblk; ++j) {
-      const int s = j & 1;
-      if (!wait_bar(k_full + s, (j >> 1) & 1, p.err)) { ok = false; break; }
-      // S buffer s last held P_{j-2}: wait until PV_{j-2} has consumed it
-      if (j >= 2 && !wait_bar(o_full, (j - 2) & 1, p.err)) { ok = false; break; }
-      tc_fence_after();
-      if (elect_one()) {
-        const uint32_t sk = smem_u32(smem + OFF_K + s * TILE);
+    int g = 0, n = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < n_items; t += gridDim.x) {
+      const Item it = get_item<MODE>(p, t);
+      if (it.nblk == 0) continue;
+      if (!wait_bar(q_full, n & 1, p.err)) break;
+      ++n;
+      for (int j = 0; j < it.nblk; ++j, ++g) {
+        const int s = g & 1;
+        if (!wait_bar(k_full + s, (g >> 1) & 1, p.err)) { ok = false; break; }
+        // S buffer s last held P_{g-2}: wait until PV_{g-2} has consumed it
+        if (g >= 2 && !wait_bar(o_full, (g - 2) & 1, p.err)) { ok = false; break; }
+        tc_fence_after();
+        if (elect_one()) {
+          const uint32_t sk = smem_u32(smem + OFF_K + s * TILE);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = make_sdesc_sw128(sq + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = make_sdesc_sw128(sk + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
-          umma_f16(tmem_base + s * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = make_sdesc_sw128(sq + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = make_sdesc_sw128(sk + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
+            umma_f16(tmem_base + s * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(s_full + s);
+          umma_commit(k_empty + s);
+          if (j == it.nblk - 1) umma_commit(q_empty);  // last S of the item: Q may be reloaded
         }
-        umma_commit(s_full + s);
-        umma_commit(k_empty + s);
+        __syncwarp();
+        if (g >= 1 && !issue_pv(g - 1)) { ok = false; break; }
       }
-      __syncwarp();
-      if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
     }
-    if (ok && nblk > 0) issue_pv(nblk - 1);
+    if (ok && g > 0) issue_pv(g - 1);
   } else {
     // ================= softmax / output =================
     // 8 warps: thread (quad, half) owns row quad*32+lane and columns [64*half, 64*half+64) of
@@ -311,146 +349,162 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     const int row = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const int col0 = half * 64;
-    const int qpos = MODE == 0 ? m0 + row : qpos_dec;
+    // decode tiles hold G valid rows: warps of lane quadrants past them only keep the
+    // barrier protocol (their rows are computed by nobody and discarded)
+    const bool idle = MODE == 1 && quad * 32 >= G;
     float* red_max = reinterpret_cast<float*>(smem + OFF_RED);  // [2][128]
     float* red_sum = red_max + 256;                               // [2][128]
-    float O[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) O[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-    float Mt = -INFINITY, Lt = 0.f;  // merged-chunk totals (mode 0, more than one chunk)
-    bool ok = true;
     auto softmax_sync = [] { asm volatile("bar.sync 1, 256;" ::: "memory"); };
+    int g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < n_items; t += gridDim.x) {
+      const Item it = get_item<MODE>(p, t);
+      if (it.nblk == 0) continue;
+      const int qpos = MODE == 0 ? it.m0 + row : it.qpos;
+      float O[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) O[i] = 0.f;
+      float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+      float Mt = -INFINITY, Lt = 0.f;  // merged-chunk totals (mode 0, more than one chunk)
 
-    // O <- fma(O, alpha_prev, O_j) for the block whose PV product sits in the O_j buffer
-    auto fold_pv = [&](int i) -> bool {
-      if (!wait_bar(o_full, i & 1, p.err)) return false;
-      tc_fence_after();
+      // O <- fma(O, alpha_prev, O_i) for running block i (its PV product is in the O_j buffer)
+      auto fold_pv = [&](int i) -> bool {
+        if (!wait_bar(o_full, i & 1, p.err)) return false;
+        tc_fence_after();
+        if (!idle) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_off + 256 + col0 + c * 32, r);
-        tmem_ld_wait();
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + lane_off + 256 + col0 + c * 32, r);
+            tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          O[c * 32 + e] = __fmaf_rn(O[c * 32 + e], alpha_prev, __uint_as_float(r[e]));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(o_empty);
-      return true;
-    };
-    // merge the finished chunk (m, l, O) into the running total kept in TMEM columns 384..511
-    auto merge_chunk = [&](bool first) {
-      float fa, fb;
-      merge_stats(Mt, Lt, m, l, fa, fb);
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t r[32];
-        const uint32_t ta = tmem_base + lane_off + 384 + col0 + c * 32;
-        if (!first) {
-          tmem_ld_32x32b_x32(ta, r);
-          tmem_ld_wait();
+            for (int e = 0; e < 32; ++e)
+              O[c * 32 + e] = __fmaf_rn(O[c * 32 + e], alpha_prev, __uint_as_float(r[e]));
+          }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_empty);
+        return true;
+      };
+      // merge the finished chunk (m, l, O) into the running total in TMEM columns 384..511
+      auto merge_chunk = [&](bool first) {
+        float fa, fb;
+        merge_stats(Mt, Lt, m, l, fa, fb);
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          r[e] = __float_as_uint(first ? O[c * 32 + e]
-                                       : merge_val(__uint_as_float(r[e]), O[c * 32 + e], fa, fb));
-        tmem_st_32x32b_x32(ta, r);
-      }
-      tmem_st_wait();
-    };
+        for (int c = 0; c < 2; ++c) {
+          uint32_t r[32];
+          const uint32_t ta = tmem_base + lane_off + 384 + col0 + c * 32;
+          if (!first) {
+            tmem_ld_32x32b_x32(ta, r);
+            tmem_ld_wait();
+          }
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            r[e] = __float_as_uint(first ? O[c * 32 + e]
+                                         : merge_val(__uint_as_float(r[e]), O[c * 32 + e], fa, fb));
+          tmem_st_32x32b_x32(ta, r);
+        }
+        tmem_st_wait();
+      };
 
-    // Block j: S_j -> P_j (into the S buffer) while PV_{j-1} runs; O_{j-1} is folded in at the
-    // end of the block (at the start at chunk boundaries, where the chunk must be complete).
-    for (int j = 0; j < nblk; ++j) {
-      const int s = j & 1;
-      if (!wait_bar(s_full + s, (j >> 1) & 1, p.err)) { ok = false; break; }
-      tc_fence_after();
-      const bool boundary = MODE == 0 && j > 0 && j % CHUNK == 0;
-      if (boundary) {
-        if (!fold_pv(j - 1)) { ok = false; break; }
-        merge_chunk(j == CHUNK);
+      // Block j: S_j -> P_j (into the S buffer) while PV_{j-1} runs; O_{j-1} is folded in at
+      // the end of the block (at the start at chunk boundaries, where the chunk must be
+      // complete).
+      for (int j = 0; j < it.nblk; ++j, ++g) {
+        const int s = g & 1;
+        if (!wait_bar(s_full + s, (g >> 1) & 1, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const bool boundary = MODE == 0 && j > 0 && j % CHUNK == 0;
+        if (boundary) {
+          if (!fold_pv(g - 1)) { ok = false; break; }
+          merge_chunk(j == CHUNK);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) O[i] = 0.f;
-        m = -INFINITY;
-        l = 0.f;
-        alpha_prev = 1.f;
-      }
-      const int kbase = (jbeg + j) * BN + col0;
-      const uint32_t ts = tmem_base + lane_off + s * 128 + col0;
-      // Only the last block of a row's key range can hold keys past the query position (for
-      // prefill tiles the diagonal block, for decode the block holding the context end).
-      const bool masked = j == nblk - 1;
-      // pass 1: row max of the raw scores (scaling is monotonic, so max(S) * scale equals the
-      // max of the scaled scores bit for bit; max is exact in any order)
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(ts + c * 32, r);
-        tmem_ld_wait();
-        if (masked) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float sv = kbase + c * 32 + e > qpos ? -INFINITY : __uint_as_float(r[e]);
-            mx4[e & 3] = fmaxf(mx4[e & 3], sv);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(r[e]));
+          for (int i = 0; i < 64; ++i) O[i] = 0.f;
+          m = -INFINITY;
+          l = 0.f;
+          alpha_prev = 1.f;
         }
-      }
-      red_max[half * 128 + row] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      softmax_sync();
-      const float raw = fmaxf(red_max[row], red_max[128 + row]);
-      const float mnew = fmaxf(m, raw == -INFINITY ? -INFINITY : __fmul_rn(raw, p.scale_log2));
-      const float sub = mnew == -INFINITY ? 0.f : mnew;
-      const float alpha = exp2f(__fsub_rn(m == -INFINITY ? sub : m, sub));
-      const float nsub = -sub;
-      // pass 2: P = bf16(2^fma(S, scale, -sub)) (kept packed in registers) and its row sum
-      float cs[2];
-      uint32_t pk[32];
+        const int kbase = (it.jbeg + j) * BN + col0;
+        const uint32_t ts = tmem_base + lane_off + s * 128 + col0;
+        // Only the last block of a row's key range can hold keys past the query position (for
+        // prefill tiles the diagonal block, for decode the block holding the context end).
+        const bool masked = j == it.nblk - 1;
+        // pass 1: row max of the raw scores (scaling is monotonic, so max(S) * scale equals
+        // the max of the scaled scores bit for bit; max is exact in any order)
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (!idle) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(ts + c * 32, r);
-        tmem_ld_wait();
-        float a4[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(ts + c * 32, r);
+            tmem_ld_wait();
+            if (masked) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p0 = ex2_approx(__fmaf_rn(__uint_as_float(r[e]), p.scale_log2, nsub));
-          float p1 = ex2_approx(__fmaf_rn(__uint_as_float(r[e + 1]), p.scale_log2, nsub));
-          if (masked) {
-            const int kp = kbase + c * 32 + e;
-            p0 = kp > qpos ? 0.f : p0;
-            p1 = kp + 1 > qpos ? 0.f : p1;
+              for (int e = 0; e < 32; ++e) {
+                const float sv = kbase + c * 32 + e > qpos ? -INFINITY : __uint_as_float(r[e]);
+                mx4[e & 3] = fmaxf(mx4[e & 3], sv);
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(r[e]));
+            }
           }
-          const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-          a4[e & 3] = __fadd_rn(a4[e & 3], __low2float(h2));
-          a4[(e + 1) & 3] = __fadd_rn(a4[(e + 1) & 3], __high2float(h2));
-          pk[c * 16 + (e >> 1)] = *reinterpret_cast<const uint32_t*>(&h2);
         }
-        cs[c] = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
+        red_max[half * 128 + row] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        softmax_sync();
+        const float raw = fmaxf(red_max[row], red_max[128 + row]);
+        const float mnew = fmaxf(m, raw == -INFINITY ? -INFINITY : __fmul_rn(raw, p.scale_log2));
+        const float sub = mnew == -INFINITY ? 0.f : mnew;
+        const float alpha = exp2f(__fsub_rn(m == -INFINITY ? sub : m, sub));
+        const float nsub = -sub;
+        // pass 2: P = bf16(2^fma(S, scale, -sub)) (kept packed in registers) and its row sum
+        float cs[2] = {0.f, 0.f};
+        uint32_t pk[32];
+        if (!idle) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(ts + c * 32, r);
+            tmem_ld_wait();
+            float a4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              float p0 = ex2_approx(__fmaf_rn(__uint_as_float(r[e]), p.scale_log2, nsub));
+              float p1 = ex2_approx(__fmaf_rn(__uint_as_float(r[e + 1]), p.scale_log2, nsub));
+              if (masked) {
+                const int kp = kbase + c * 32 + e;
+                p0 = kp > qpos ? 0.f : p0;
+                p1 = kp + 1 > qpos ? 0.f : p1;
+              }
+              const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+              a4[e & 3] = __fadd_rn(a4[e & 3], __low2float(h2));
+              a4[(e + 1) & 3] = __fadd_rn(a4[(e + 1) & 3], __high2float(h2));
+              pk[c * 16 + (e >> 1)] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            cs[c] = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
+          }
+        }
+        red_sum[half * 128 + row] = __fadd_rn(cs[0], cs[1]);
+        softmax_sync();  // both halves have read S_j: P_j may overwrite its first 64 columns
+        if (!idle) {
+          // P_j: this thread's 64 keys = packed columns half*32 .. half*32+31 of the S buffer
+          tmem_st_32x32b_x32(tmem_base + lane_off + s * 128 + half * 32, pk);
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + s);
+        const float rs = __fadd_rn(red_sum[row], red_sum[128 + row]);
+        l = __fmaf_rn(l, alpha, rs);
+        m = mnew;
+        if (j >= 1 && !boundary && !fold_pv(g - 1)) { ok = false; break; }
+        alpha_prev = alpha;
       }
-      red_sum[half * 128 + row] = __fadd_rn(cs[0], cs[1]);
-      softmax_sync();  // both halves have read S_j: P_j may overwrite its first 64 columns
-      // P_j: this thread's 64 keys = packed columns half*32 .. half*32+31 of the S buffer
-      tmem_st_32x32b_x32(tmem_base + lane_off + s * 128 + half * 32, pk);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full + s);
-      const float rs = __fadd_rn(red_sum[row], red_sum[128 + row]);
-      l = __fmaf_rn(l, alpha, rs);
-      m = mnew;
-      if (j >= 1 && !boundary && !fold_pv(j - 1)) { ok = false; break; }
-      alpha_prev = alpha;
-    }
-    if (ok && nblk > 0) ok = fold_pv(nblk - 1);
-    if (ok && nblk > 0) {
+      if (!ok) break;
+      if (!fold_pv(g - 1)) { ok = false; break; }
       if (MODE == 0) {
-        if (nblk > CHUNK) {
+        if (it.nblk > CHUNK) {
           merge_chunk(false);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
@@ -463,10 +517,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
           m = Mt;
           l = Lt;
         }
-        if (qpos < len) {
+        if (qpos < it.len) {
           const float inv = l > 0.f ? __frcp_rn(l) : 0.f;
           __nv_bfloat16* out =
-              p.o + (long long)(seq_start + qpos) * p.o_stride + (long long)h * D + col0;
+              p.o + (long long)(it.seq_start + qpos) * p.o_stride + (long long)it.h * D + col0;
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             uint4 v;
@@ -478,13 +532,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
           }
           if (p.lse && half == 0) {
             const float ln2 = 0.69314718055994530942f;
-            p.lse[(long long)h * p.total_tokens + seq_start + qpos] =
+            p.lse[(long long)it.h * p.total_tokens + it.seq_start + qpos] =
                 l > 0.f ? (m + log2f(l)) * ln2 : -INFINITY;
           }
         }
       } else if (row < G) {
-        const long long w = (long long)b * p.nq + (long long)hk * G + row;
-        if (nsplit == 1) {
+        const long long w = (long long)it.b * p.nq + (long long)it.hk * G + row;
+        if (it.nsplit == 1) {
           const float inv = l > 0.f ? __frcp_rn(l) : 0.f;
           __nv_bfloat16* out = p.o + w * D + col0;
 #pragma unroll
@@ -497,7 +551,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
             reinterpret_cast<uint4*>(out)[q] = v;
           }
         } else {
-          const long long base = w * p.nsplit_max + split;
+          const long long base = w * p.nsplit_max + it.split;
           float4* wo = reinterpret_cast<float4*>(p.ws_o + base * D + col0);
 #pragma unroll
           for (int q = 0; q < 16; ++q)
@@ -527,17 +581,33 @@ using namespace mb::fa;
 
 namespace {
 int fwd_attr_set[2] = {0, 0};
+int g_sms = 0;
 template <int MODE>
 int launch_fa(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-              const Params& p, dim3 grid, cudaStream_t st) {
+              const Params& p, int n_items, cudaStream_t st) {
   if (!fwd_attr_set[MODE]) {
     if (cudaFuncSetAttribute(fa_fwd_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              SMEM_BYTES) != cudaSuccess)
       return -3;
     fwd_attr_set[MODE] = 1;
   }
-  mb_launch(fa_fwd_kernel<MODE>, grid, dim3(NTHREADS), SMEM_BYTES, st, tq, tk, tv, p);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  if (g_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int grid = n_items < g_sms ? n_items : g_sms;
+  mb_launch(fa_fwd_kernel<MODE>, dim3(grid), dim3(NTHREADS), SMEM_BYTES, st, tq, tk, tv, p,
+            n_items);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, fa_fwd_kernel<MODE>);
+    fprintf(stderr, "fa_fwd_kernel launch failed: %s (regs %d, max threads %d, smem %d)\n",
+            cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, SMEM_BYTES);
+    return -2;
+  }
+  return 0;
 }
 int current_ctx() {
   int dev = 0;
@@ -576,7 +646,7 @@ extern "C" int mb_fa_fwd(const void* q, const void* k, const void* v, void* o, f
   p.nkv = nkv;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.err = err;
-  return launch_fa<0>(tq, tk, tv, p, dim3(ntiles, nq), st);
+  return launch_fa<0>(tq, tk, tv, p, ntiles * nq, st);
 }
 
 // Paged decode: one query token per sequence. q: [B, nq, 128]; caches [num_slots, nkv, 128]
@@ -612,5 +682,5 @@ extern "C" int mb_fa_decode(const void* q, const void* kc, const void* vc, void*
   p.nkv = nkv;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.err = err;
-  return launch_fa<1>(tq, tk, tv, p, dim3(B, nkv, nsplit_max), st);
+  return launch_fa<1>(tq, tk, tv, p, B * nkv * nsplit_max, st);
 }
