@@ -29,8 +29,9 @@
 // Roles (320 threads): warp 0 = TMA producer (Q once, then K_j / V_j through a 2-stage ring),
 // warp 1 = TMEM owner and MMA issuer (S_j into a double-buffered S, O_j into a single O_j
 // buffer), warps 2-9 = softmax / output: two threads per row (TMEM lane), each owning 64 of
-// the 128 columns. TMEM: S0 | S1 | O_j | Otot, 128 columns each. P_j (bf16) is written over the
-// first 64 columns of its S buffer and fed to the P.V UMMA straight from tensor memory; the
+// the 128 columns. TMEM: S0 | S1 | O_j | Otot, 128 columns each. P_j (bf16) is written over its
+// S buffer (keys 0-63 in columns 0-31, keys 64-127 in columns 64-95: each thread overwrites only
+// scores it has already read) and fed to the P.V UMMA straight from tensor memory; the
 // O_j fold is deferred to the end of the next block so the softmax never waits for P.V.
 //
 // Reference roles replaced: flash-attention / cuDNN fused attention forward used by Megatron
@@ -106,6 +107,15 @@ MB_DEVICE float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+MB_DEVICE void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0],"
+      " {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
 }
 MB_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 MB_DEVICE void fence_proxy_async_smem() {
@@ -301,8 +311,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         const uint32_t pa = tmem_base + (i & 1) * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
+          // keys 16kk..16kk+15: packed P columns (kk>>2)*64 + (kk&3)*8 of the S buffer
           const uint64_t bd = make_sdesc_sw128(sv + (kk >> 2) * SUB + (kk & 3) * 2048, 8192, 1024);
-          umma_f16_ts(tmem_base + 256, pa + kk * 8, bd, idesc_o, kk > 0 ? 1u : 0u);
+          umma_f16_ts(tmem_base + 256, pa + (kk >> 2) * 64 + (kk & 3) * 8, bd, idesc_o,
+                      kk > 0 ? 1u : 0u);
         }
         umma_commit(o_full);
         umma_commit(v_empty + (i & 1));
@@ -458,9 +470,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         const float sub = mnew == -INFINITY ? 0.f : mnew;
         const float alpha = exp2f(__fsub_rn(m == -INFINITY ? sub : m, sub));
         const float nsub = -sub;
-        // pass 2: P = bf16(2^fma(S, scale, -sub)) (kept packed in registers) and its row sum
+        // pass 2: P = bf16(2^fma(S, scale, -sub)) and its row sum. This thread's 64 keys are
+        // packed into columns half*64 .. half*64+31 of the S buffer (inside the columns it has
+        // itself just read), one 32-key group at a time.
         float cs[2] = {0.f, 0.f};
-        uint32_t pk[32];
         if (!idle) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
@@ -468,6 +481,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
             tmem_ld_32x32b_x32(ts + c * 32, r);
             tmem_ld_wait();
             float a4[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t pk[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
               float p0 = ex2_approx(__fmaf_rn(__uint_as_float(r[e]), p.scale_log2, nsub));
@@ -480,21 +494,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
               const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
               a4[e & 3] = __fadd_rn(a4[e & 3], __low2float(h2));
               a4[(e + 1) & 3] = __fadd_rn(a4[(e + 1) & 3], __high2float(h2));
-              pk[c * 16 + (e >> 1)] = *reinterpret_cast<const uint32_t*>(&h2);
+              pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
             }
             cs[c] = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
+            tmem_st_32x32b_x16(tmem_base + lane_off + s * 128 + half * 64 + c * 16, pk);
           }
-        }
-        red_sum[half * 128 + row] = __fadd_rn(cs[0], cs[1]);
-        softmax_sync();  // both halves have read S_j: P_j may overwrite its first 64 columns
-        if (!idle) {
-          // P_j: this thread's 64 keys = packed columns half*32 .. half*32+31 of the S buffer
-          tmem_st_32x32b_x32(tmem_base + lane_off + s * 128 + half * 32, pk);
           tmem_st_wait();
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full + s);
+        red_sum[half * 128 + row] = __fadd_rn(cs[0], cs[1]);
+        softmax_sync();
         const float rs = __fadd_rn(red_sum[row], red_sum[128 + row]);
         l = __fmaf_rn(l, alpha, rs);
         m = mnew;

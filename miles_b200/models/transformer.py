@@ -96,6 +96,9 @@ def is_expert_param(name: str) -> bool:
     return ".mlp.experts." in name
 
 
+FLAT_ALIGN = 8192
+
+
 class KVCache:
     """Paged KV cache: per layer K and V of [num_pages * 64, nkv, 128] bf16.
 
@@ -134,7 +137,11 @@ class Transformer(torch.nn.Module):
         self.numel = total
         ex = [sp.offset for sp in self.specs if is_expert_param(sp.name)]
         self.dense_numel = ex[0] if ex else total
-        self.flat = torch.empty(total, dtype=dtype, device=self.device)
+        # padded to a multiple of 8192 elements so that the flat buffers split evenly over
+        # 1/2/4/8 data-parallel ranks (sharded optimizer); the tail is never a parameter
+        padded = (total + FLAT_ALIGN - 1) // FLAT_ALIGN * FLAT_ALIGN
+        self.flat = torch.zeros(padded, dtype=dtype, device=self.device) if padded != total else \
+            torch.empty(total, dtype=dtype, device=self.device)
         self.params: dict[str, torch.nn.Parameter] = {}
         for s in self.specs:
             p = torch.nn.Parameter(self.flat[s.offset:s.offset + s.numel].view(s.shape))

@@ -109,7 +109,14 @@ class Actor:
         else:
             self.opt = FlatAdam(self.model.flat, self.grad_flat, lr=self.cfg.lr,
                                 betas=self.cfg.betas, weight_decay=self.cfg.weight_decay,
-                                clip_grad=self.cfg.clip_grad, placement=self.cfg.optimizer_placement)
+                                clip_grad=self.cfg.clip_grad, placement=self.cfg.optimizer_placement,
+                                dp_group=self.dp_group if self._sharded() else None)
+
+    def _sharded(self) -> bool:
+        """Optimizer sharded over the data-parallel group (ZeRO-1): every rank holds the whole
+        flat buffer (no expert parallelism) and there is more than one rank."""
+        return (self.dp_group is not None and dist.get_world_size(self.dp_group) > 1
+                and self.model.ep is None)
 
     def release_grads(self):
         """Free the gradient buffer (colocated mode: give the memory to the KV cache)."""
@@ -225,9 +232,9 @@ class Actor:
                 p.main_grad.add_(p.grad.to(p.main_grad.dtype))
                 p.grad = None
         t1 = time.perf_counter()
-        if self.dp_group is not None and dist.get_world_size(self.dp_group) > 1:
+        if self.dp_group is not None and dist.get_world_size(self.dp_group) > 1 and not self._sharded():
             self._reduce_grads()
-        self.opt.step()
+        self.opt.step()  # sharded: reduce-scatter + shard update + all-gather inside
         model.weight_version += 1
         out = {k: float(v) for k, v in zip(METRIC_NAMES + ["entropy"], metrics.tolist())}
         out["grad_norm"] = float(self.opt.grad_norm())

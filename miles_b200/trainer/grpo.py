@@ -97,7 +97,10 @@ class ColocatedRL:
                 num += len(d)
             diff /= max(num, 1)
         t_lp = time.perf_counter()
-        m = self.actor.train_step(items)
+        dp = self.actor.dp_group
+        world = torch.distributed.get_world_size(dp) if dp is not None else 1
+        # loss weights are 1 / (global sample count); gradients are summed over DP ranks
+        m = self.actor.train_step(items, global_num_samples=len(items) * world)
         t_train = time.perf_counter()
         self.rollout_id += 1
         n_resp = sum(s.response_length for s in samples)

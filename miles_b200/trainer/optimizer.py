@@ -1,11 +1,22 @@
-"""Flat-buffer AdamW with device or host-offloaded state.
+"""Flat-buffer AdamW with device or host-offloaded state, optionally sharded over data-parallel
+ranks (ZeRO-1).
 
 State placements:
   * "device"  : fp32 master + fp32 m/v on the GPU (the default when it fits)
-  * "host"    : bf16 m/v in pinned host memory, streamed through the GPU in chunks on a copy
-                stream while the Adam kernel runs on the previous chunk; the bf16 parameters are
+  * "host"    : bf16 m/v in pinned host memory, streamed through the GPU in chunks while the
+                Adam kernel runs on the previous chunk (host->device and device->host copies on
+                two streams, so both PCIe directions are busy at once); the bf16 parameters are
                 the master copy and updates use stochastic rounding. This is the single-GPU
                 placement for models whose fp32 state cannot fit (e.g. a 30B MoE on one B200).
+
+Sharding (``dp_group`` with more than one rank): rank r owns elements [r*S, (r+1)*S) of the
+flat buffers (S = n / world; the model pads its flat buffer so that n divides evenly). One step
+is: reduce-scatter of the gradient into the owned shard (in place, NCCL), the global gradient
+norm as an all-reduce of the shard norms, Adam on the shard only (optimizer state is 1/world
+of the unsharded size, placed on the device when it fits), and an in-place all-gather of the
+updated parameters. Replaces Megatron's distributed optimizer (the reference forces it:
+megatron_utils/arguments.py:14; grad reduce-scatter / param all-gather in model.py:537-612).
+
 Gradient clipping uses a device-side norm (no host sync); a non-finite gradient skips the
 step on the device (the reference's NaN/Inf guard, megatron_utils/model.py:452-461).
 
@@ -14,15 +25,23 @@ Reference role: Megatron distributed optimizer / HybridDeviceOptimizer (--optimi
 from __future__ import annotations
 
 import torch
+import torch.distributed as dist
 
 from miles_b200.ops.optim import adam_, nonfinite_, sqnorm_
+
+
+def _is_nccl(group) -> bool:
+    try:
+        return dist.get_backend(group) == "nccl"
+    except Exception:  # noqa: BLE001
+        return False
 
 
 class FlatAdam:
     def __init__(self, params_flat: torch.Tensor, grads_flat: torch.Tensor, lr: float = 1e-6,
                  betas=(0.9, 0.98), eps: float = 1e-8, weight_decay: float = 0.0,
                  clip_grad: float = 1.0, placement: str = "auto", chunk: int = 1 << 28,
-                 seed: int = 1234):
+                 seed: int = 1234, dp_group=None):
         self.p = params_flat
         self.g = grads_flat
         self.lr = lr
@@ -35,81 +54,117 @@ class FlatAdam:
         self.chunk = chunk
         n = params_flat.numel()
         dev = params_flat.device
+        self.group = dp_group
+        self.world = dist.get_world_size(dp_group) if dp_group is not None else 1
+        self.rank = dist.get_rank(dp_group) if dp_group is not None else 0
+        if self.world > 1 and n % self.world:
+            raise ValueError(f"flat buffer of {n} elements does not split over {self.world} ranks")
+        self.shard = n // self.world
+        self.lo = self.rank * self.shard
+        ns = self.shard
         if placement == "auto":
             placement = "device"
             if dev.type == "cuda":
                 free, _ = torch.cuda.mem_get_info(dev)
-                if 12 * n > 0.8 * free:
+                if 12 * ns > 0.8 * free:
                     placement = "host"
         self.placement = placement
         if placement == "device":
-            self.master = params_flat.float()
-            self.m = torch.zeros(n, dtype=torch.float32, device=dev)
-            self.v = torch.zeros(n, dtype=torch.float32, device=dev)
+            self.master = params_flat[self.lo:self.lo + ns].float()
+            self.m = torch.zeros(ns, dtype=torch.float32, device=dev)
+            self.v = torch.zeros(ns, dtype=torch.float32, device=dev)
         else:
             self.master = None
             pin = dev.type == "cuda"
-            self.m = torch.zeros(n, dtype=torch.bfloat16, pin_memory=pin)
-            self.v = torch.zeros(n, dtype=torch.bfloat16, pin_memory=pin)
+            self.m = torch.zeros(ns, dtype=torch.bfloat16, pin_memory=pin)
+            self.v = torch.zeros(ns, dtype=torch.bfloat16, pin_memory=pin)
             if dev.type == "cuda":
-                c = min(chunk, n)
+                c = min(chunk, ns)
                 self.stage = [(torch.empty(c, dtype=torch.bfloat16, device=dev),
                                torch.empty(c, dtype=torch.bfloat16, device=dev)) for _ in range(2)]
-                self.copy_stream = torch.cuda.Stream(dev)
+                self.h2d = torch.cuda.Stream(dev)
+                self.d2h = torch.cuda.Stream(dev)
         self.sq = torch.zeros(1, dtype=torch.float32, device=dev)
         self.skip = torch.zeros(1, dtype=torch.float32, device=dev)
 
     def grad_norm(self) -> torch.Tensor:
         return self.sq.sqrt()
 
+    # ------------------------------------------------------------------ collectives
+    def _reduce_scatter_grads(self) -> None:
+        mine = self.g[self.lo:self.lo + self.shard]
+        if _is_nccl(self.group):
+            dist.reduce_scatter_tensor(mine, self.g, group=self.group)  # in place
+        else:  # gloo has no reduce-scatter: sum everything, keep the shard
+            dist.all_reduce(self.g, group=self.group)
+
+    def _all_gather_params(self) -> None:
+        mine = self.p[self.lo:self.lo + self.shard]
+        if _is_nccl(self.group):
+            dist.all_gather_into_tensor(self.p, mine, group=self.group)  # in place
+        else:
+            parts = list(self.p.view(self.world, self.shard).unbind(0))
+            gathered = [torch.empty_like(mine) for _ in range(self.world)]
+            dist.all_gather(gathered, mine.clone(), group=self.group)
+            for dst, src in zip(parts, gathered):
+                dst.copy_(src)
+
+    # ------------------------------------------------------------------ step
     @torch.no_grad()
     def step(self) -> None:
         self.step_id += 1
+        if self.world > 1:
+            self._reduce_scatter_grads()
+        lo, hi = self.lo, self.lo + self.shard
+        p, g = self.p[lo:hi], self.g[lo:hi]
         self.sq.zero_()
         self.skip.zero_()
-        sqnorm_(self.g, self.sq)
+        sqnorm_(g, self.sq)
+        if self.world > 1:
+            dist.all_reduce(self.sq, group=self.group)
         nonfinite_(self.sq, self.skip)
         common = dict(lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.wd,
                       step=self.step_id, sqnorm=self.sq, max_norm=self.clip,
-                      seed=self.seed * 1000003 + self.step_id, skip=self.skip)
-        if self.placement == "device":
-            adam_(self.p, self.g, self.m, self.v, master=self.master, **common)
-            return
-        if self.p.device.type != "cuda":
-            adam_(self.p, self.g, self.m, self.v, master=None, **common)
-            return
-        n = self.p.numel()
-        cur = torch.cuda.current_stream(self.p.device)
-        cs = self.copy_stream
-        events = []
+                      seed=self.seed * 1000003 + self.step_id + 7919 * self.rank, skip=self.skip)
+        if self.placement == "device" or p.device.type != "cuda":
+            adam_(p, g, self.m, self.v, master=self.master, **common)
+        else:
+            self._host_step(p, g, common)
+        if self.world > 1:
+            self._all_gather_params()
+
+    def _host_step(self, p: torch.Tensor, g: torch.Tensor, common: dict) -> None:
+        n = p.numel()
+        cur = torch.cuda.current_stream(p.device)
+        backs: list[torch.cuda.Event] = []
         for ci, a in enumerate(range(0, n, self.chunk)):
             b = min(n, a + self.chunk)
             sm, sv = self.stage[ci % 2]
             sm, sv = sm[: b - a], sv[: b - a]
-            with torch.cuda.stream(cs):
-                if len(events) >= 2:
-                    cs.wait_event(events[-2])  # stage buffer free again (its D2H has finished)
+            with torch.cuda.stream(self.h2d):
+                if ci >= 2:
+                    self.h2d.wait_event(backs[ci - 2])  # stage buffer free (its D2H finished)
                 sm.copy_(self.m[a:b], non_blocking=True)
                 sv.copy_(self.v[a:b], non_blocking=True)
                 loaded = torch.cuda.Event()
-                loaded.record(cs)
+                loaded.record(self.h2d)
             cur.wait_event(loaded)
-            common["seed"] = self.seed * 1000003 + self.step_id * 4099 + ci
-            adam_(self.p[a:b], self.g[a:b], sm, sv, master=None, **common)
+            common["seed"] = self.seed * 1000003 + self.step_id * 4099 + ci + 7919 * self.rank
+            adam_(p[a:b], g[a:b], sm, sv, master=None, **common)
             done = torch.cuda.Event()
             done.record(cur)
-            with torch.cuda.stream(cs):
-                cs.wait_event(done)
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(done)
                 self.m[a:b].copy_(sm, non_blocking=True)
                 self.v[a:b].copy_(sv, non_blocking=True)
                 back = torch.cuda.Event()
-                back.record(cs)
-            events.append(back)
-        cur.wait_stream(cs)
+                back.record(self.d2h)
+            backs.append(back)
+        cur.wait_stream(self.d2h)
 
     def state_dict(self) -> dict:
         return {"step": self.step_id, "m": self.m, "v": self.v, "master": self.master,
-                "placement": self.placement}
+                "placement": self.placement, "shard": (self.rank, self.world)}
 
     def load_state_dict(self, sd: dict) -> None:
         self.step_id = sd["step"]
