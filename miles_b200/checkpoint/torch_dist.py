@@ -100,21 +100,33 @@ def is_torch_dist(path: str) -> bool:
 _ASYNC: threading.Thread | None = None
 
 
+def _optim_state(optimizer) -> dict:
+    """Optimizer tensors under checkpoint keys. A state sharded over data-parallel ranks is
+    stored under per-shard keys (each rank writes its own; loading needs the same world)."""
+    osd = optimizer.state_dict()
+    rank, world = osd.get("shard", (0, 1))
+    sfx = f".shard{rank}of{world}" if world > 1 else ""
+    out = {"m" + sfx: osd["m"], "v" + sfx: osd["v"]}
+    if osd.get("master") is not None:
+        out["master" + sfx] = osd["master"]
+    return out
+
+
 def save_checkpoint(save: str, iteration: int, model: Transformer, optimizer=None,
-                    extra: dict | None = None, save_optim: bool = True, async_save: bool = False):
+                    extra: dict | None = None, save_optim: bool = True, async_save: bool = False,
+                    process_group=None):
+    """process_group: the ranks that hold this model (default: the whole world); every one of
+    them must call this."""
     global _ASYNC
     d = os.path.join(save, f"iter_{iteration:07d}")
     os.makedirs(d, exist_ok=True)
     sd = {"model": model_state_dict(model)}
     if optimizer is not None and save_optim:
-        osd = optimizer.state_dict()
-        sd["optimizer"] = {"m": osd["m"], "v": osd["v"]}
-        if osd.get("master") is not None:
-            sd["optimizer"]["master"] = osd["master"]
-    rank0 = not torch.distributed.is_initialized() or torch.distributed.get_rank() == 0
+        sd["optimizer"] = _optim_state(optimizer)
+    rank0 = not torch.distributed.is_initialized() or torch.distributed.get_rank(process_group) == 0
 
     def _write(sd_cpu):
-        dcp.save(sd_cpu, checkpoint_id=d)
+        dcp.save(sd_cpu, checkpoint_id=d, process_group=process_group)
         if rank0:
             torch.save({"iteration": iteration, "optimizer_step": getattr(optimizer, "step_id", 0),
                         "weight_version": model.weight_version, "extra": extra or {},
@@ -139,7 +151,7 @@ def wait_async_save():
 
 @torch.no_grad()
 def load_checkpoint(load: str, model: Transformer, optimizer=None, load_optim: bool = True,
-                    iteration: int | None = None) -> dict:
+                    iteration: int | None = None, process_group=None) -> dict:
     it = iteration if iteration is not None else get_checkpoint_iteration(load)
     if it is None:
         raise FileNotFoundError(f"no torch_dist checkpoint under {load}")
@@ -147,11 +159,8 @@ def load_checkpoint(load: str, model: Transformer, optimizer=None, load_optim: b
     cfg = model.cfg
     sd = {"model": {k: torch.empty_like(v) for k, v in model_state_dict(model).items()}}
     if optimizer is not None and load_optim:
-        osd = optimizer.state_dict()
-        sd["optimizer"] = {"m": osd["m"], "v": osd["v"]}
-        if osd.get("master") is not None:
-            sd["optimizer"]["master"] = osd["master"]
-    dcp.load(sd, checkpoint_id=d)
+        sd["optimizer"] = _optim_state(optimizer)  # views of the live state: loaded in place
+    dcp.load(sd, checkpoint_id=d, process_group=process_group)
     for name, p in model.params.items():
         t = sd["model"][megatron_name(name, cfg)]
         if name.endswith("qkv_proj.weight"):

@@ -131,6 +131,10 @@ def add_rollout_args(p):
     g.add_argument("--rollout-external", action="store_true", default=False)
     g.add_argument("--rollout-external-engine-addrs", nargs="+", default=None)
     g.add_argument("--update-weight-transfer-mode", choices=["broadcast", "p2p"], default="broadcast")
+    g.add_argument("--update-weight-quant", choices=["none", "fp8"], default="none",
+                   help="quantise weights at refit (fp8: 128x128 block-scaled e4m3 broadcast)")
+    g.add_argument("--fully-async", action="store_true", default=False,
+                   help="train_async.py: keep generation running continuously on the rollout GPUs")
     g.add_argument("--p2p-transfer-num-workers", type=int, default=4)
     g.add_argument("--p2p-transfer-timeout", type=float, default=300.0)
     g.add_argument("--rollout-task-type", default=None)

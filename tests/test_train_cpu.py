@@ -54,3 +54,29 @@ def test_train_gloo_world2(tmp_path):
            *_argv(tmp_path, ["--actor-num-gpus-per-node", "2", "--num-rollout", "1"])]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=580)
     assert r.returncode == 0, r.stderr[-3000:]
+
+
+def _async_run(tmp_path, extra, port):
+    _dataset(tmp_path / "d.jsonl")
+    env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", str(port),
+           os.path.join(ROOT, "train_async.py"),
+           *_argv(tmp_path, ["--actor-num-gpus-per-node", "1", "--rollout-num-gpus", "1",
+                             "--num-rollout", "3", "--save-interval", "100", *extra])]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=580)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return r
+
+
+@pytest.mark.timeout(600)
+def test_train_async_disaggregated(tmp_path):
+    """1 trainer + 1 rollout rank: one-step-ahead pipeline with bf16 broadcast refits."""
+    _async_run(tmp_path, [], 29641)
+
+
+@pytest.mark.timeout(600)
+def test_train_async_fully_async_fp8_refit(tmp_path):
+    """Continuous generation worker (partial rollout, staleness filter) and fp8 refits."""
+    _async_run(tmp_path, ["--fully-async", "--partial-rollout", "--max-weight-staleness", "4",
+                          "--update-weight-quant", "fp8"], 29643)
