@@ -254,11 +254,11 @@ int64_t policy_loss(torch::Tensor logp, torch::Tensor old_logp, torch::Tensor ad
                  torch::Tensor weight, OT rollout_logp, OT ref_logp, torch::Tensor dlogp,
                  OT pg_out, torch::Tensor part, torch::Tensor metrics, double eps, double eps_hi,
                  double eps_c, double tis_lo, double tis_hi, double kl_coef, int64_t kl_type,
-                 bool use_tis) {
+                 int64_t use_tis) {
   return mb_policy_loss(PT<float>(logp), PT<float>(old_logp), PT<float>(adv), PT<float>(weight),
                           PT<float>(rollout_logp), PT<float>(ref_logp), PT<float>(dlogp),
                           PT<float>(pg_out), PT<float>(part), PT<float>(metrics), logp.numel(),
-                          eps, eps_hi, eps_c, tis_lo, tis_hi, kl_coef, kl_type, use_tis,
+                          eps, eps_hi, eps_c, tis_lo, tis_hi, kl_coef, kl_type, (int)use_tis,
                           cur_stream());
 }
 int64_t gae(torch::Tensor rewards, torch::Tensor values, torch::Tensor cu, double gamma, double lam,

@@ -166,7 +166,8 @@ __global__ void __launch_bounds__(LS_THREADS) sample_kernel(
 // normaliser):
 //   ppo_kl = old - logp, ratio = exp(-ppo_kl)
 //   pg = max(-A r, -A clip(r, 1-eps, 1+eps_hi)); if eps_c > 1 and A < 0: pg = min(pg, -A eps_c)
-//   pg *= tis (tis = clamp(exp(old - rollout), tis_lo, tis_hi), a constant) when enabled
+//   pg *= tis, a constant: use_tis 1 = TIS (clamp(exp(old - rollout), tis_lo, tis_hi)),
+//   use_tis 2 = IcePop (exp(old - rollout) inside [tis_lo, tis_hi], else 0)
 //   kl term: kl_coef * KL(logp || ref) of type k1 / k2 / k3 (low_var_kl, clamped to [-10, 10])
 // loss = sum_i w_i (pg_i + kl_coef kl_i); dlogp_i = w_i (dpg_i + kl_coef dkl_i).
 // Metric partials per block: [sum w*pg, sum w*clipfrac, sum w*ppo_kl, sum w*kl, sum w*tis,
@@ -182,7 +183,7 @@ struct PolicyLossParams {
   int n;
   float eps, eps_hi, eps_c, tis_lo, tis_hi, kl_coef;
   int kl_type;  // 0 none, 1 k1, 2 k2, 3 k3/low_var_kl
-  int use_tis;
+  int use_tis;  // 0 off, 1 TIS (clamp), 2 IcePop (mask)
 };
 
 __global__ void policy_loss_kernel(const PolicyLossParams p) {
@@ -208,7 +209,8 @@ __global__ void policy_loss_kernel(const PolicyLossParams p) {
     float tis = 1.f, tis_clip = 0.f;
     if (p.use_tis) {
       const float raw = expf(p.old_logp[i] - p.rollout_logp[i]);
-      tis = fminf(fmaxf(raw, p.tis_lo), p.tis_hi);
+      tis = p.use_tis == 2 ? ((raw >= p.tis_lo && raw <= p.tis_hi) ? raw : 0.f)
+                           : fminf(fmaxf(raw, p.tis_lo), p.tis_hi);
       tis_clip = (tis != raw) ? 1.f : 0.f;
       pg *= tis;
       dpg *= tis;

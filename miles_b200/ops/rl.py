@@ -27,6 +27,13 @@ class PolicyLossCfg:
     tis_clip: float = 2.0
     kl_coef: float = 0.0
     kl_type: str = "none"
+    tis_mode: str = "tis"         # "tis": clamp the IS ratio; "icepop": zero it outside [low, high]
+    loss_type: str = "policy_loss"  # policy_loss | sft_loss | custom_loss
+    custom_loss_path: str | None = None
+    custom_tis_path: str | None = None
+    use_opsm: bool = False
+    opsm_delta: float = 1e-4
+    gspo: bool = False
 
 
 def policy_loss_ref(logp, old_logp, adv, weight, cfg: PolicyLossCfg, rollout_logp=None,
@@ -45,7 +52,11 @@ def policy_loss_ref(logp, old_logp, adv, weight, cfg: PolicyLossCfg, rollout_log
     tis_clip = torch.zeros_like(logp)
     if cfg.use_tis:
         raw = (old_logp - rollout_logp).exp()
-        tis = raw.clamp(cfg.tis_clip_low, cfg.tis_clip)
+        if cfg.tis_mode == "icepop":
+            tis = torch.where((raw >= cfg.tis_clip_low) & (raw <= cfg.tis_clip), raw,
+                              torch.zeros_like(raw))
+        else:
+            tis = raw.clamp(cfg.tis_clip_low, cfg.tis_clip)
         tis_clip = (tis != raw).to(logp.dtype)
         pg = pg * tis.detach()
     kl = torch.zeros_like(logp)
@@ -87,7 +98,7 @@ class _PolicyLoss(torch.autograd.Function):
                           None if ref_logp is None else ref_logp.float().contiguous(),
                           dlogp, None, part, metrics, cfg.eps_clip, cfg.eps_clip_high, eps_c,
                           cfg.tis_clip_low, cfg.tis_clip, cfg.kl_coef, KL_TYPES[cfg.kl_type],
-                          cfg.use_tis)
+                          (2 if cfg.tis_mode == "icepop" else 1) if cfg.use_tis else 0)
         ctx.save_for_backward(dlogp)
         loss = metrics[0] + cfg.kl_coef * metrics[3]
         ctx.mark_non_differentiable(metrics)

@@ -92,9 +92,18 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
 
 
 def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
+    from miles_b200.trainer.is_functions import KERNEL_MODES
+
+    tis_path = args.custom_tis_function_path
+    tis_mode = KERNEL_MODES.get(tis_path or "", "tis")
     loss = PolicyLossCfg(eps_clip=args.eps_clip, eps_clip_high=args.eps_clip_high,
                          eps_clip_c=args.eps_clip_c, use_tis=args.use_tis,
                          tis_clip_low=args.tis_clip_low, tis_clip=args.tis_clip,
+                         tis_mode=tis_mode,
+                         custom_tis_path=None if tis_path in KERNEL_MODES or not tis_path else tis_path,
+                         loss_type=args.loss_type, custom_loss_path=args.custom_loss_function_path,
+                         use_opsm=args.use_opsm, opsm_delta=args.opsm_delta,
+                         gspo=args.advantage_estimator == "gspo",
                          kl_coef=args.kl_loss_coef if args.use_kl_loss else 0.0,
                          kl_type=args.kl_loss_type if args.use_kl_loss else "none")
     placement = "host" if args.optimizer_cpu_offload else "auto"
@@ -120,3 +129,26 @@ def build_engine(args, model: Transformer, ctx: ProcessContext) -> RolloutEngine
                          num_pages=None if ctx.device.type == "cuda" else 4096,
                          mem_fraction=mem, use_cuda_graph=not args.no_cuda_graph,
                          max_pages_per_seq=(max_len + 63) // 64 + 1)
+
+
+def build_critic(args, ctx: ProcessContext):
+    """PPO value model (same architecture, its own weights and optimizer) when
+    --advantage-estimator ppo; None otherwise."""
+    if not getattr(args, "use_critic", False):
+        return None
+    from miles_b200.trainer.critic import Critic
+
+    cfg = model_config(args)
+    dtype = torch.bfloat16 if ctx.device.type == "cuda" else torch.float32
+    body = Transformer(cfg, device=ctx.device, dtype=dtype, seed=args.seed + 1)
+    if args.critic_load:
+        from miles_b200.checkpoint.torch_dist import is_torch_dist, load_checkpoint
+
+        if is_torch_dist(args.critic_load):
+            load_checkpoint(args.critic_load, body)
+    acfg = ActorConfig(lr=args.critic_lr, betas=(args.adam_beta1, args.adam_beta2),
+                       weight_decay=args.weight_decay, clip_grad=args.clip_grad,
+                       max_tokens_per_gpu=args.max_tokens_per_gpu or 16384,
+                       grad_dtype=torch.float32 if ctx.device.type != "cuda" else torch.bfloat16,
+                       optimizer_placement="host" if args.optimizer_cpu_offload else "auto")
+    return Critic(body, acfg, value_clip=args.value_clip, dp_group=ctx.dp_group)

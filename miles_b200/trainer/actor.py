@@ -17,6 +17,7 @@ loss scaling :828-927), megatron_utils/model.py (train_one_step :318-490).
 """
 from __future__ import annotations
 
+import dataclasses
 import math
 import time
 from dataclasses import dataclass, field
@@ -31,6 +32,7 @@ from miles_b200.ops.attention import VarlenMeta
 from miles_b200.ops.logprob import lm_head_logprob
 from miles_b200.ops.rl import METRIC_NAMES, PolicyLossCfg, policy_loss
 from miles_b200.trainer.optimizer import FlatAdam
+from miles_b200.utils.misc import load_function
 
 
 @dataclass
@@ -85,6 +87,13 @@ def pack_microbatches(lengths: list[int], max_tokens: int) -> list[list[int]]:
     return [sorted(b) for b in bins]
 
 
+def _seg_mean(x: torch.Tensor, mask: torch.Tensor, seg: torch.Tensor, nseq: int) -> torch.Tensor:
+    """Per-token broadcast of the masked mean of x over each token's sequence (differentiable)."""
+    num = torch.zeros(nseq, dtype=x.dtype, device=x.device).index_add(0, seg, x)
+    den = torch.zeros(nseq, dtype=x.dtype, device=x.device).index_add(0, seg, mask).clamp_min(1.0)
+    return (num / den).index_select(0, seg)
+
+
 class Actor:
     def __init__(self, model: Transformer, cfg: ActorConfig, dp_group=None):
         self.model = model
@@ -94,6 +103,8 @@ class Actor:
         self.grad_flat: torch.Tensor | None = None
         self.opt: FlatAdam | None = None
         self.timers: dict[str, float] = {}
+        self._custom_loss = None
+        self._custom_tis = None
 
     # ------------------------------------------------------------------ memory
     def _ensure_grads(self):
@@ -218,9 +229,10 @@ class Actor:
             h = model.forward_train(tok, meta, replay_experts=self._replay(sub))
             hs = h.index_select(0, sel)
             lp, ent = lm_head_logprob(hs, W, tgt, cfg.temperature, cfg.logprob_chunk)
-            loss, m = policy_loss(lp, T(old), T(adv), T(wgt), cfg.loss,
-                                  T(roll) if cfg.loss.use_tis else None,
-                                  T(ref) if ref and cfg.loss.kl_type != "none" else None)
+            seg = torch.from_numpy(np.repeat(np.arange(len(sub)), [it.resp_len for it in sub])).to(self.dev)
+            loss, m = self._loss(lp, ent, seg, len(sub), T(old), T(adv), T(wgt),
+                                 T(roll) if any(r is not None for r in roll) else None,
+                                 T(ref) if ref and cfg.loss.kl_type != "none" else None)
             if cfg.entropy_coef:
                 loss = loss - cfg.entropy_coef * (ent * T(wgt)).sum()
             loss.backward()
@@ -242,6 +254,47 @@ class Actor:
         self.timers["train_fwd_bwd"] = t1 - t0
         self.timers["train_total"] = time.perf_counter() - t0
         return out
+
+    # ------------------------------------------------------------------ losses
+    def _loss(self, lp, ent, seg, nseq, old, adv, wgt, roll, ref):
+        """Loss of one micro-batch (token-level tensors over its response tokens; `seg` maps a
+        token to its sample). Returns (loss, metrics [len(METRIC_NAMES)] weighted sums)."""
+        cfg = self.cfg
+        lc = cfg.loss
+        if lc.loss_type == "sft_loss":
+            # SFT: negative log-likelihood of the (loss-masked) response tokens
+            loss = -(lp * wgt).sum()
+            m = torch.zeros(len(METRIC_NAMES), dtype=torch.float32, device=lp.device)
+            m[0] = loss.detach()
+            m[len(METRIC_NAMES) - 1] = wgt.sum()
+            return loss, m
+        if lc.loss_type == "custom_loss":
+            if self._custom_loss is None:
+                self._custom_loss = load_function(lc.custom_loss_path)
+            return self._custom_loss(lp=lp, entropy=ent, old_log_probs=old, advantages=adv,
+                                     weights=wgt, rollout_log_probs=roll, ref_log_probs=ref,
+                                     segments=seg, cfg=lc)
+        w = wgt
+        mask = (wgt > 0).float()
+        if lc.use_opsm:
+            # off-policy sequence masking: drop sequences with negative advantage whose
+            # sequence-level KL(old || current) exceeds opsm_delta
+            kl = _seg_mean((old - lp.detach()) * mask, mask, seg, nseq)
+            w = w * (1.0 - ((adv < 0) & (kl > lc.opsm_delta)).float())
+        if lc.use_tis and lc.custom_tis_path and roll is not None:
+            if self._custom_tis is None:
+                self._custom_tis = load_function(lc.custom_tis_path)
+            # reference hook signature: scales pg_loss; applied to the (detached) weights
+            scaled, _, _ = self._custom_tis(lc, pg_loss=torch.ones_like(lp), train_log_probs=[old],
+                                            rollout_log_probs=[roll], loss_masks=[mask])
+            w = w * scaled.detach()
+            lc = dataclasses.replace(lc, use_tis=False)
+        lp_in, old_in = lp, old
+        if lc.gspo:
+            # GSPO: sequence-level importance ratio exp(mean_t(logp - old)) on every token
+            lp_in = _seg_mean(lp * mask, mask, seg, nseq)
+            old_in = _seg_mean(old * mask, mask, seg, nseq)
+        return policy_loss(lp_in, old_in, adv, w, lc, roll if lc.use_tis else None, ref)
 
     def _reduce_grads(self):
         """Sum gradients over data-parallel ranks (replicated region) and expert-data-parallel

@@ -54,9 +54,10 @@ class TensorBackuper:
 
 
 class TrainActor:
-    def __init__(self, args, actor: Actor, dp_group=None):
+    def __init__(self, args, actor: Actor, dp_group=None, critic=None):
         self.args = args
         self.actor = actor
+        self.critic = critic  # PPO value model (miles_b200/trainer/critic.py) or None
         self.model = actor.model
         self.dp_group = dp_group
         self.backuper = TensorBackuper(self.model, enabled=not args.disable_weights_backuper)
@@ -90,11 +91,22 @@ class TrainActor:
             for it, r in zip(items, ref):
                 it.ref_logp = r
         logp = old if old is not None else [np.asarray(it.rollout_logp) for it in items]
+        values = self.critic.values(items) if self.critic is not None else None
+        rets = None
         if not a.disable_compute_advantages_and_returns:
-            advs, _ = compute_advantages(a, data, log_probs=logp, ref_log_probs=ref, dp_group=self.dp_group)
+            advs, rets = compute_advantages(a, data, log_probs=logp, ref_log_probs=ref,
+                                            values=values, dp_group=self.dp_group)
             for it, adv in zip(items, advs):
                 it.advantage = adv
         m = {}
+        world = torch.distributed.get_world_size(self.dp_group) if self.dp_group is not None else 1
+        if self.critic is not None and rets is not None:
+            cm = self.critic.train_step(items, rets, values, global_num_samples=len(items) * world)
+            m.update({f"critic/{k}": v for k, v in cm.items()})
+            if rollout_id < (a.num_critic_only_steps or 0):
+                m["perf/log_probs_time"] = t1 - t0
+                self.metrics = m
+                return m
         if old is not None and items and items[0].rollout_logp is not None:
             d = np.concatenate([np.abs(o - np.asarray(it.rollout_logp, np.float32)) for it, o in zip(items, old)])
             m["train/train_rollout_logprob_abs_diff"] = float(d.mean()) if d.size else 0.0

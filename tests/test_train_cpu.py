@@ -80,3 +80,20 @@ def test_train_async_fully_async_fp8_refit(tmp_path):
     """Continuous generation worker (partial rollout, staleness filter) and fp8 refits."""
     _async_run(tmp_path, ["--fully-async", "--partial-rollout", "--max-weight-staleness", "4",
                           "--update-weight-quant", "fp8"], 29643)
+
+
+def test_train_ppo_with_critic(tmp_path, monkeypatch):
+    """--advantage-estimator ppo: critic values -> GAE advantages -> value + policy updates."""
+    monkeypatch.setenv("MILES_B200_FORCE_CPU", "1")
+    _dataset(tmp_path / "d.jsonl")
+    sys.path.insert(0, ROOT)
+    import train as T
+    from miles_b200.utils.arguments import parse_args
+    from miles_b200.rollout.default import GenerateState
+
+    GenerateState._inst = None
+    hist = T.train(parse_args(_argv(tmp_path, ["--advantage-estimator", "ppo", "--save-interval", "100",
+                                               "--ci-disable-kl-checker"])))
+    assert len(hist) == 2
+    assert all("critic/value_loss" in h for h in hist)
+    assert np.isfinite(hist[-1]["critic/value_loss"])

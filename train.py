@@ -21,8 +21,8 @@ import torch  # noqa: E402
 from miles_b200.checkpoint.torch_dist import (get_checkpoint_iteration, is_torch_dist,  # noqa: E402
                                               load_checkpoint, save_checkpoint, wait_async_save)
 from miles_b200.orchestration.rollout_manager import RolloutManager  # noqa: E402
-from miles_b200.orchestration.setup import (build_actor, build_engine, build_model,  # noqa: E402
-                                            init_distributed, load_tokenizer)
+from miles_b200.orchestration.setup import (build_actor, build_critic, build_engine,  # noqa: E402
+                                            build_model, init_distributed, load_tokenizer)
 from miles_b200.rollout.engine_client import LocalEngineClient  # noqa: E402
 from miles_b200.trainer.train_actor import TrainActor  # noqa: E402
 from miles_b200.utils.arguments import parse_args  # noqa: E402
@@ -40,7 +40,7 @@ def setup(args):
     ds_cls = load_function(args.data_source_path)
     data_source = ds_cls(args, tok)
     manager = RolloutManager(args, data_source, client, tok, ctx.rank, ctx.world)
-    trainer = TrainActor(args, actor, ctx.dp_group)
+    trainer = TrainActor(args, actor, ctx.dp_group, critic=build_critic(args, ctx))
     start = 0
     if args.load and is_torch_dist(args.load):
         actor._ensure_grads()
