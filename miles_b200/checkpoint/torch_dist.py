@@ -121,6 +121,14 @@ def save_checkpoint(save: str, iteration: int, model: Transformer, optimizer=Non
     d = os.path.join(save, f"iter_{iteration:07d}")
     os.makedirs(d, exist_ok=True)
     sd = {"model": model_state_dict(model)}
+    lora = getattr(model, "lora", None)
+    if lora is not None:
+        # adapters are saved on their own (base weights are frozen); their AdamW state with them
+        if not torch.distributed.is_initialized() or torch.distributed.get_rank(process_group) == 0:
+            lora.save(os.path.join(d, "lora_adapter.pt"))
+            if optimizer is not None and save_optim:
+                torch.save(optimizer.state_dict(), os.path.join(d, "lora_optim.pt"))
+        save_optim = False
     if optimizer is not None and save_optim:
         sd["optimizer"] = _optim_state(optimizer)
     rank0 = not torch.distributed.is_initialized() or torch.distributed.get_rank(process_group) == 0
@@ -158,6 +166,13 @@ def load_checkpoint(load: str, model: Transformer, optimizer=None, load_optim: b
     d = os.path.join(load, f"iter_{it:07d}")
     cfg = model.cfg
     sd = {"model": {k: torch.empty_like(v) for k, v in model_state_dict(model).items()}}
+    lora = getattr(model, "lora", None)
+    if lora is not None:
+        if os.path.exists(os.path.join(d, "lora_adapter.pt")):
+            lora.load(os.path.join(d, "lora_adapter.pt"))
+        if optimizer is not None and load_optim and os.path.exists(os.path.join(d, "lora_optim.pt")):
+            optimizer.load_state_dict(torch.load(os.path.join(d, "lora_optim.pt"), weights_only=False))
+        load_optim = False
     if optimizer is not None and load_optim:
         sd["optimizer"] = _optim_state(optimizer)  # views of the live state: loaded in place
     dcp.load(sd, checkpoint_id=d, process_group=process_group)

@@ -159,6 +159,19 @@ class Transformer(torch.nn.Module):
                     self.router_cfgs[i] = rc
         self.recompute = True
         self.weight_version = 0
+        self.lora = None  # miles_b200.models.lora.LoRA when adapters are attached
+
+    # -------------------------------------------------------------------------------- projections
+    def _lin(self, x: torch.Tensor, name: str) -> torch.Tensor:
+        y = G.linear(x, self.params[name])
+        if self.lora is not None and name in self.lora:
+            y = y + self.lora.delta(name, x)
+        return y
+
+    def _lin_swiglu(self, x: torch.Tensor, name: str) -> torch.Tensor:
+        if self.lora is not None and name in self.lora:
+            return swiglu(self._lin(x, name))
+        return G.linear_swiglu(x, self.params[name])
 
     # -------------------------------------------------------------------------------- params
     @torch.no_grad()
@@ -190,13 +203,13 @@ class Transformer(torch.nn.Module):
     def _attn_train(self, i: int, x: torch.Tensor, meta: VarlenMeta) -> torch.Tensor:
         cfg = self.cfg
         pre = f"layers.{i}.self_attn."
-        qkv = G.linear(x, self.params[pre + "qkv_proj.weight"])
+        qkv = self._lin(x, pre + "qkv_proj.weight")
         q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
                                self.params.get(pre + "k_norm.weight"), meta.positions,
                                self.rope_cos, self.rope_sin, cfg.num_heads, cfg.num_kv_heads,
                                cfg.rms_eps, cfg.qk_norm)
         o = varlen_attention(q, k, v, meta)
-        return G.linear(o.reshape(x.shape[0], -1), self.params[pre + "o_proj.weight"])
+        return self._lin(o.reshape(x.shape[0], -1), pre + "o_proj.weight")
 
     def _mlp(self, i: int, x: torch.Tensor, replay=None, record=None) -> torch.Tensor:
         pre = f"layers.{i}.mlp."
@@ -215,8 +228,7 @@ class Transformer(torch.nn.Module):
                 s = G.linear_swiglu(x, self.params[pre + "shared_experts.gate_up_proj.weight"])
                 y = y + G.linear(s, self.params[pre + "shared_experts.down_proj.weight"])
             return y
-        return G.linear(G.linear_swiglu(x, self.params[pre + "gate_up_proj.weight"]),
-                        self.params[pre + "down_proj.weight"])
+        return self._lin(self._lin_swiglu(x, pre + "gate_up_proj.weight"), pre + "down_proj.weight")
 
     def _layer_train(self, i, m_prev, r_prev, meta, replay):
         cfg = self.cfg
@@ -282,7 +294,7 @@ class Transformer(torch.nn.Module):
             ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
             x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
             pre = f"layers.{i}.self_attn."
-            qkv = G.linear(x, self.params[pre + "qkv_proj.weight"])
+            qkv = self._lin(x, pre + "qkv_proj.weight")
             q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
                                    self.params.get(pre + "k_norm.weight"), meta.positions,
                                    self.rope_cos, self.rope_sin, cfg.num_heads, cfg.num_kv_heads,
@@ -290,7 +302,7 @@ class Transformer(torch.nn.Module):
             cache.k[i].index_copy_(0, slots, k)
             cache.v[i].index_copy_(0, slots, v)
             o = varlen_attention(q, k, v, meta)
-            a = G.linear(o.reshape(x.shape[0], -1), self.params[pre + "o_proj.weight"])
+            a = self._lin(o.reshape(x.shape[0], -1), pre + "o_proj.weight")
             x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"],
                                  cfg.rms_eps)
             rec = record.append if (record is not None and i in self.router_cfgs) else None
@@ -312,14 +324,14 @@ class Transformer(torch.nn.Module):
             ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
             x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
             pre = f"layers.{i}.self_attn."
-            qkv = G.linear(x, self.params[pre + "qkv_proj.weight"])
+            qkv = self._lin(x, pre + "qkv_proj.weight")
             q = qk_norm_rope_to_cache(qkv, self.params.get(pre + "q_norm.weight"),
                                       self.params.get(pre + "k_norm.weight"), positions,
                                       self.rope_cos, self.rope_sin, cfg.num_heads,
                                       cfg.num_kv_heads, cache.k[i], cache.v[i], slots,
                                       cfg.rms_eps, cfg.qk_norm)
             o = decode_attention(q, cache.k[i], cache.v[i], page_table, ctx_lens)
-            a = G.linear(o.reshape(B, -1), self.params[pre + "o_proj.weight"])
+            a = self._lin(o.reshape(B, -1), pre + "o_proj.weight")
             x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"],
                                  cfg.rms_eps)
             rec = record.append if (record is not None and i in self.router_cfgs) else None

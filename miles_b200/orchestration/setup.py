@@ -88,6 +88,13 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
         from miles_b200.checkpoint.hf import load_hf
 
         load_hf(model, args.hf_checkpoint)
+    if getattr(args, "lora_rank", 0):
+        from miles_b200.models.lora import LoRA
+
+        model.lora = LoRA(model, args.lora_rank, args.lora_alpha, args.target_modules,
+                          args.lora_dropout, seed=args.seed)
+        if args.lora_adapter_path:
+            model.lora.load(args.lora_adapter_path)
     return model
 
 

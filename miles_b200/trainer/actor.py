@@ -108,6 +108,16 @@ class Actor:
 
     # ------------------------------------------------------------------ memory
     def _ensure_grads(self):
+        if self.model.lora is not None:
+            # LoRA: base weights frozen, only the adapters train (no flat gradient buffer)
+            if self.opt is None:
+                from miles_b200.models.lora import LoRAOptimizer
+
+                for p in self.model.params.values():
+                    p.requires_grad_(False)
+                self.opt = LoRAOptimizer(self.model.lora, self.cfg.lr, self.cfg.betas,
+                                         self.cfg.weight_decay, self.cfg.clip_grad, self.dp_group)
+            return
         if self.grad_flat is None:
             self.grad_flat = torch.zeros(self.model.flat.numel(), dtype=self.cfg.grad_dtype,
                                          device=self.dev)
@@ -127,7 +137,7 @@ class Actor:
         """Optimizer sharded over the data-parallel group (ZeRO-1): every rank holds the whole
         flat buffer (no expert parallelism) and there is more than one rank."""
         return (self.dp_group is not None and dist.get_world_size(self.dp_group) > 1
-                and self.model.ep is None)
+                and self.model.ep is None and self.model.lora is None)
 
     def release_grads(self):
         """Free the gradient buffer (colocated mode: give the memory to the KV cache)."""
@@ -196,7 +206,8 @@ class Actor:
         self._ensure_grads()
         model = self.model
         t0 = time.perf_counter()
-        self.grad_flat.zero_()
+        if self.grad_flat is not None:
+            self.grad_flat.zero_()
         n_samples = global_num_samples or len(items)
         n_tokens = global_num_tokens or sum(
             (sum(it.loss_mask) if it.loss_mask is not None else it.resp_len) for it in items)
@@ -244,7 +255,8 @@ class Actor:
                 p.main_grad.add_(p.grad.to(p.main_grad.dtype))
                 p.grad = None
         t1 = time.perf_counter()
-        if self.dp_group is not None and dist.get_world_size(self.dp_group) > 1 and not self._sharded():
+        if (self.dp_group is not None and dist.get_world_size(self.dp_group) > 1
+                and not self._sharded() and model.lora is None):
             self._reduce_grads()
         self.opt.step()  # sharded: reduce-scatter + shard update + all-gather inside
         model.weight_version += 1
