@@ -32,6 +32,13 @@ from miles_b200.utils.tracking import Tracker  # noqa: E402
 
 def setup(args):
     ctx = init_distributed(args)
+    if args.env_report:
+        from miles_b200.utils.env_report import report
+
+        report(ctx.rank)
+    from miles_b200.utils import dumper
+
+    dumper.configure(args, ctx.rank)
     model = build_model(args, ctx)
     actor = build_actor(args, model, ctx)
     engine = build_engine(args, model, ctx)
@@ -56,6 +63,9 @@ def setup(args):
 
 def train(args):
     ctx, model, actor, engine, manager, trainer, tracker, start, data_source = setup(args)
+    from miles_b200.utils.profile_utils import TrainProfiler
+
+    profiler = TrainProfiler(args, ctx.rank)
     num_rollout = args.num_rollout
     if args.eval_interval and not args.skip_eval_before_train:
         tracker.log(manager.eval(start), start)
@@ -66,7 +76,10 @@ def train(args):
         if args.debug_rollout_only:
             tracker.log(data["metrics"], rollout_id)
             continue
+        profiler.start("train_overall")
         m = trainer.train(rollout_id, data)
+        profiler.stop("train_overall")
+        profiler.step()
         m.update(data["metrics"])
         if should_run_periodic_action(rollout_id, args.save_interval, num_rollout) and args.save:
             save_checkpoint(args.save, rollout_id, model, actor.opt, extra={"rollout_id": rollout_id},
