@@ -101,3 +101,44 @@ def test_sft_loss_mask():
     assert mask == [0, 0, 0, 0, 0, 1, 1, 1, 0, 0, 0, 0, 1, 1]
     s = build_sft_sample(_ToyTok(), Sample(prompt=msgs, index=0))
     assert s.response_length == 9 and s.loss_mask == mask[5:]
+
+
+class _FakeClient:
+    def __init__(self):
+        self.calls = []
+
+    async def generate(self, ids, sp, return_logprob=True, return_routed_experts=False):
+        self.calls.append(list(ids))
+        out = [500 + len(self.calls), 4]  # one content token + end-of-turn
+        return {"output_ids": out, "text": f"r{len(self.calls)}",
+                "meta_info": {"output_token_logprobs": [[-0.5, t] for t in out],
+                              "finish_reason": {"type": "stop"}}}
+
+
+def test_session_server_tito():
+    from fastapi.testclient import TestClient
+
+    from miles_b200.rollout.session import SessionRegistry, build_session_app
+
+    tok, client = _ToyTok(), _FakeClient()
+    reg = SessionRegistry(tok, client)
+    app = TestClient(build_session_app(reg))
+    sid = app.post("/sessions").json()["session_id"]
+    m1 = [{"role": "user", "content": "solve it"}]
+    r1 = app.post(f"/sessions/{sid}/v1/chat/completions", json={"messages": m1}).json()
+    assert r1["choices"][0]["message"]["content"] == "r1"
+    m2 = m1 + [r1["choices"][0]["message"], {"role": "tool", "content": "42"}]
+    app.post(f"/sessions/{sid}/v1/chat/completions", json={"messages": m2})
+    # second prompt = first checkpoint tokens (as generated) + tool turn + generation prompt
+    first = client.calls[0] + [501, 4]
+    assert client.calls[1][:len(first)] == first
+    assert client.calls[1][len(first):] == [tok._w("<tool>"), tok._w("42"), 4, 3]
+    traj = app.get(f"/sessions/{sid}").json()
+    mask = traj["loss_mask"]
+    assert sum(mask) == 4 and mask[len(first) - 2:len(first)] == [1, 1] and mask[-2:] == [1, 1]
+    # retry from the first checkpoint: rolls back one assistant step
+    app.post(f"/sessions/{sid}/v1/chat/completions", json={"messages": m2})
+    assert app.get(f"/sessions/{sid}").json()["num_turns"] == 2
+    s = reg.get(sid).to_sample()
+    assert s.response_length == len(s.loss_mask) and s.loss_mask[0] == 1
+    assert app.post("/sessions/nope/v1/chat/completions", json={"messages": m1}).status_code == 404
