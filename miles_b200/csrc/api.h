@@ -50,6 +50,10 @@ int mb_router_bwd(const float* logits, const int* idx, const float* dw, void* dl
                   int k, int score_fn, int renorm, float scale, cudaStream_t st);
 int mb_moe_permute_plan(const int* idx, int n, int E, int align, int* hist, int* chunk_base,
                         int* counts, int* offsets, int* dest, cudaStream_t st);
+int mb_moe_route_dispatch(const float* logits, const float* bias, const int* idx_in, const void* x,
+                          int T, int E, int k, int H, int score_fn, int renorm, int n_group,
+                          int topk_group, float scale, int align, int* idx_out, float* w_out,
+                          int* counts, int* offsets, int* dest, void* xs, cudaStream_t st);
 int mb_moe_zero_pad(const int* counts, const int* offsets, void* buf, int E, int H, cudaStream_t st);
 int mb_moe_gather(const void* x, const int* dest, int n, int k, int H, void* xs, cudaStream_t st);
 int mb_moe_gather_bwd(const void* dxs, const int* dest, int T, int k, int H, void* dx,

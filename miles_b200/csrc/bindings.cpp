@@ -158,6 +158,18 @@ int64_t router_fwd(torch::Tensor logits, OT bias, OT idx_in, torch::Tensor idx_o
                          PT<float>(w_out), logits.size(0), logits.size(1), k, score_fn, renorm,
                          n_group, topk_group, (float)scale, cur_stream());
 }
+int64_t moe_route_dispatch(torch::Tensor logits, OT bias, OT idx_in, torch::Tensor x,
+                           torch::Tensor idx_out, torch::Tensor w_out, torch::Tensor counts,
+                           torch::Tensor offsets, torch::Tensor dest, torch::Tensor xs, int64_t k,
+                           int64_t score_fn, bool renorm, int64_t n_group, int64_t topk_group,
+                           double scale, int64_t align) {
+  CHECK_DT(logits, at::kFloat); TORCH_CHECK(logits.is_contiguous() && x.is_contiguous());
+  return mb_moe_route_dispatch(PT<float>(logits), PT<float>(bias), PT<int>(idx_in), P(x),
+                               logits.size(0), logits.size(1), k, x.size(1), score_fn, renorm,
+                               n_group, topk_group, (float)scale, align, PT<int>(idx_out),
+                               PT<float>(w_out), PT<int>(counts), PT<int>(offsets), PT<int>(dest),
+                               P(xs), cur_stream());
+}
 int64_t router_bwd(torch::Tensor logits, torch::Tensor idx, torch::Tensor dw, torch::Tensor dlogits,
                 int64_t score_fn, bool renorm, double scale) {
   return mb_router_bwd(PT<float>(logits), PT<int>(idx), PT<float>(dw), P(dlogits),
@@ -335,6 +347,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("router_fwd", &router_fwd);
+  m.def("moe_route_dispatch", &moe_route_dispatch);
   m.def("router_bwd", &router_bwd);
   m.def("moe_permute_plan", &moe_permute_plan);
   m.def("moe_zero_pad", &moe_zero_pad);

@@ -19,15 +19,16 @@ constexpr int kMaxK = 16;
 // of `n_group` groups (group score = sum of its top-2 biased scores); weights are the unbiased
 // sigmoid scores of the selected experts, renormalised if `renorm`, times `scale`.
 // replay: when idx_in != nullptr the selection is read from it (R3) instead of computed.
-__global__ void router_fwd_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
-                                  const int* __restrict__ idx_in, int* __restrict__ idx_out,
-                                  float* __restrict__ w_out, int T, int E, int k, int score_fn,
-                                  int renorm, int n_group, int topk_group, float scale) {
-  pdl_trigger();
-  pdl_wait();
-  const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
+// Routing of token t by one warp (all 32 lanes call it). `gscore` is 32 floats of shared
+// memory owned by the calling warp (group scores of the group-limited selection). Both the
+// training router kernel and the fused decode route+dispatch kernel use this function, so
+// their selections and weights are bitwise equal.
+__device__ __forceinline__ void route_token(const float* __restrict__ logits,
+                                            const float* __restrict__ bias,
+                                            const int* __restrict__ idx_in, int* __restrict__ idx_out,
+                                            float* __restrict__ w_out, int t, int E, int k,
+                                            int score_fn, int renorm, int n_group, int topk_group,
+                                            float scale, float* gscore, int lane) {
   constexpr int PER = kMaxE / 32;
   const int per = (E + 31) / 32;
   float sc[PER], sel[PER];
@@ -65,8 +66,6 @@ __global__ void router_fwd_kernel(const float* __restrict__ logits, const float*
     }
     if (n_group > 1) {
       const int gsz = E / n_group;
-      __shared__ float gscore_sh[32][32];
-      const int wid = threadIdx.x / 32;
       for (int g = 0; g < n_group; ++g) {
         float b1 = -INFINITY, b2 = -INFINITY;
 #pragma unroll
@@ -84,7 +83,7 @@ __global__ void router_fwd_kernel(const float* __restrict__ logits, const float*
           const float n2 = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
           b1 = n1; b2 = n2;
         }
-        if (lane == 0) gscore_sh[wid][g] = b1 + b2;
+        if (lane == 0) gscore[g] = b1 + b2;
       }
       __syncwarp();
       unsigned keep = 0;  // best topk_group groups, ties -> lower group index
@@ -93,7 +92,7 @@ __global__ void router_fwd_kernel(const float* __restrict__ logits, const float*
           int best = -1;
           float bv = -INFINITY;
           for (int g = 0; g < n_group; ++g)
-            if (!((keep >> g) & 1u) && (best < 0 || gscore_sh[wid][g] > bv)) { best = g; bv = gscore_sh[wid][g]; }
+            if (!((keep >> g) & 1u) && (best < 0 || gscore[g] > bv)) { best = g; bv = gscore[g]; }
           keep |= 1u << best;
         }
       }
@@ -146,6 +145,20 @@ __global__ void router_fwd_kernel(const float* __restrict__ logits, const float*
       w_out[(long long)t * k + j] = wsel[j] * inv * scale;
     }
   }
+}
+
+__global__ void router_fwd_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                                  const int* __restrict__ idx_in, int* __restrict__ idx_out,
+                                  float* __restrict__ w_out, int T, int E, int k, int score_fn,
+                                  int renorm, int n_group, int topk_group, float scale) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float gscore_sh[32][32];
+  const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  route_token(logits, bias, idx_in, idx_out, w_out, t, E, k, score_fn, renorm, n_group,
+              topk_group, scale, gscore_sh[threadIdx.x / 32], lane);
 }
 
 // Backward of router_fwd (softmax or sigmoid) to d(logits), written as bf16 for the router GEMM.
@@ -427,6 +440,101 @@ __global__ void moe_combine_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
 
 using namespace mb;
 
+
+// ---------------------------------------------------------------------------------------------
+// Fused routing + dispatch for small batches (decode): one launch replaces router top-k,
+// histogram, scan, scatter and gather. Every CTA routes all T tokens itself (route_token, the
+// training router's arithmetic) and builds the whole plan in shared memory; CTA 0 publishes
+// idx / weights / counts / offsets / dest, and the CTAs split the row gather. Row order inside
+// an expert segment is ascending (token, slot), as in the multi-kernel plan.
+// Shared memory: idx[n] | dest[n] | w[n] | cnt[E] | run[E] | offs[E+1] | wc[8][E].
+// ---------------------------------------------------------------------------------------------
+constexpr int kRDWarps = 8;
+constexpr int kRDMaxN = 4096;
+
+__global__ void __launch_bounds__(kRDWarps * 32)
+moe_route_dispatch_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                          const int* __restrict__ idx_in, const __nv_bfloat16* __restrict__ x,
+                          int T, int E, int k, int H, int score_fn, int renorm, int n_group,
+                          int topk_group, float scale, int align, int* __restrict__ idx_out,
+                          float* __restrict__ w_out, int* __restrict__ counts_out,
+                          int* __restrict__ offsets_out, int* __restrict__ dest_out,
+                          __nv_bfloat16* __restrict__ xs) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ int rd_smem[];
+  const int n = T * k;
+  int* idx_s = rd_smem;
+  int* dest_s = idx_s + n;
+  float* w_s = reinterpret_cast<float*>(dest_s + n);
+  int* cnt = reinterpret_cast<int*>(w_s + n);
+  int* run = cnt + E;
+  int* offs = run + E;
+  int* wc = offs + E + 1;  // [kRDWarps][E]
+  __shared__ float gscore_sh[kRDWarps][32];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int t = warp; t < T; t += kRDWarps)
+    route_token(logits, bias, idx_in, idx_s, w_s, t, E, k, score_fn, renorm, n_group, topk_group,
+                scale, gscore_sh[warp], lane);
+  for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+  for (int i = tid; i < kRDWarps * E; i += blockDim.x) wc[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += blockDim.x) atomicAdd(&cnt[idx_s[i]], 1);
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      offs[e] = acc;
+      run[e] = acc;
+      acc += (cnt[e] + align - 1) / align * align;
+    }
+    offs[E] = acc;
+  }
+  __syncthreads();
+  // stable ranks, one block-sized chunk of entries at a time
+  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+    const int i = c0 + tid;
+    const bool valid = i < n;
+    const int e = valid ? idx_s[i] : -1 - lane;
+    const unsigned peers = __match_any_sync(0xffffffff, e);
+    const int r = __popc(peers & ((1u << lane) - 1u));
+    if (valid && r == 0) wc[warp * E + e] = __popc(peers);
+    __syncthreads();
+    if (valid) {
+      int b = run[e];
+      for (int w = 0; w < warp; ++w) b += wc[w * E + e];
+      dest_s[i] = b + r;
+    }
+    __syncthreads();
+    for (int ee = tid; ee < E; ee += blockDim.x) {
+      int add = 0;
+      for (int w = 0; w < kRDWarps; ++w) {
+        add += wc[w * E + ee];
+        wc[w * E + ee] = 0;
+      }
+      run[ee] += add;
+    }
+    __syncthreads();
+  }
+  if (blockIdx.x == 0) {
+    for (int i = tid; i < n; i += blockDim.x) {
+      idx_out[i] = idx_s[i];
+      w_out[i] = w_s[i];
+      dest_out[i] = dest_s[i];
+    }
+    for (int e = tid; e < E; e += blockDim.x) counts_out[e] = cnt[e];
+    if (tid == 0) offsets_out[E] = offs[E];
+    for (int e = tid; e < E; e += blockDim.x) offsets_out[e] = offs[e];
+  }
+  // gather: CTA b copies rows b, b + gridDim.x, ...
+  const int nvec = H / 8;
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + (long long)(i / k) * H);
+    uint4* dst = reinterpret_cast<uint4*>(xs + (long long)dest_s[i] * H);
+    for (int c = tid; c < nvec; c += blockDim.x) dst[c] = src[c];
+  }
+}
+
 extern "C" int mb_router_fwd(const float* logits, const float* bias, const int* idx_in, int* idx_out,
                              float* w_out, int T, int E, int k, int score_fn, int renorm,
                              int n_group, int topk_group, float scale, cudaStream_t st) {
@@ -504,5 +612,33 @@ extern "C" int mb_moe_combine_bwd(const void* dy, const void* ys, const int* des
   mb_launch(moe_combine_bwd_kernel, (T + 7) / 8, 256, 0, st, (const __nv_bfloat16*)dy,
                                                       (const __nv_bfloat16*)ys, dest, w, T, k, H,
                                                       (__nv_bfloat16*)dys, dw);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// Fused route + dispatch for n = T * k <= 4096 (decode batches). Outputs as mb_router_fwd +
+// mb_moe_permute_plan + mb_moe_gather (padding rows of xs are not written).
+extern "C" int mb_moe_route_dispatch(const float* logits, const float* bias, const int* idx_in,
+                                     const void* x, int T, int E, int k, int H, int score_fn,
+                                     int renorm, int n_group, int topk_group, float scale,
+                                     int align, int* idx_out, float* w_out, int* counts,
+                                     int* offsets, int* dest, void* xs, cudaStream_t st) {
+  if (T == 0) return 0;
+  const int n = T * k;
+  if (E > kMaxE || k > kMaxK || n > kRDMaxN || H % 8 || align <= 0 ||
+      (n_group > 1 && (n_group > 32 || E % n_group)))
+    return -1;
+  const size_t smem = (size_t)(3 * n + 3 * E + 1 + kRDWarps * E) * sizeof(int);
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(moe_route_dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)((3 * kRDMaxN + 3 * kMaxE + 1 + kRDWarps * kMaxE) * sizeof(int))) != cudaSuccess)
+      return -3;
+    attr = true;
+  }
+  int grid = (n + 3) / 4;
+  grid = grid < 1 ? 1 : (grid > 148 ? 148 : grid);
+  mb_launch(moe_route_dispatch_kernel, grid, kRDWarps * 32, smem, st, logits, bias, idx_in,
+            (const __nv_bfloat16*)x, T, E, k, H, score_fn, renorm, n_group, topk_group, scale,
+            align, idx_out, w_out, counts, offsets, dest, (__nv_bfloat16*)xs);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

@@ -18,6 +18,7 @@ from miles_b200.ops import gemm as G
 from miles_b200.ops._lib import lib, use_native
 from miles_b200.ops.norm import swiglu_ref
 
+FUSED_DISPATCH_MAX_ROWS = 4096  # T * k limit of the fused route + dispatch kernel
 ALIGN = 128
 
 
@@ -78,6 +79,28 @@ def moe_ref(x, router_w, w1, w2, cfg: RouterCfg, bias=None, replay_idx=None):
 class MoEPlan:
     """Device-side dispatch plan for one batch: dest rows, padded offsets and counts."""
 
+    @classmethod
+    def fused(cls, logits, bias, replay_idx, x, cfg: "RouterCfg"):
+        """Routing + plan + gather in one kernel (small batches, no backward). Returns
+        (plan, idx, w, xs)."""
+        T = logits.shape[0]
+        k, E = cfg.k, cfg.E
+        n = T * k
+        dev = logits.device
+        self = cls.__new__(cls)
+        self.E, self.k, self.T = E, k, T
+        self.rows = ((n + E * (ALIGN - 1)) + ALIGN - 1) // ALIGN * ALIGN
+        self.counts = torch.empty(E, dtype=torch.int32, device=dev)
+        self.offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        self.dest = torch.empty(n, dtype=torch.int32, device=dev)
+        idx = torch.empty(T, k, dtype=torch.int32, device=dev)
+        w = torch.empty(T, k, dtype=torch.float32, device=dev)
+        xs = torch.empty(self.rows, x.shape[1], dtype=x.dtype, device=dev)
+        lib().moe_route_dispatch(logits, bias, replay_idx, x, idx, w, self.counts, self.offsets,
+                                 self.dest, xs, k, cfg.score_fn, cfg.renorm, cfg.n_group,
+                                 cfg.topk_group, cfg.scale, ALIGN)
+        return self, idx, w, xs
+
     def __init__(self, idx: torch.Tensor, E: int):
         T, k = idx.shape
         n = T * k
@@ -132,14 +155,21 @@ class _MoE(torch.autograd.Function):
         T, H = x.shape
         x = x.contiguous()
         logits = G.matmul_nt(x, router_w, out_dtype=torch.float32)
-        idx = torch.empty(T, cfg.k, dtype=torch.int32, device=x.device)
-        w = torch.empty(T, cfg.k, dtype=torch.float32, device=x.device)
-        lib().router_fwd(logits, bias, replay_idx, idx, w, cfg.k, cfg.score_fn, cfg.renorm,
-                         cfg.n_group, cfg.topk_group, cfg.scale)
-        if record is not None:
-            record(idx)
-        plan = MoEPlan(idx, cfg.E)
-        xs = plan.gather(x, zero_pad=need_bwd)
+        if not need_bwd and T * cfg.k <= FUSED_DISPATCH_MAX_ROWS:
+            # decode-sized batch: one kernel for routing, plan and gather
+            plan, idx, w, xs = MoEPlan.fused(logits, bias, replay_idx.contiguous().view(T, cfg.k)
+                                             if replay_idx is not None else None, x, cfg)
+            if record is not None:
+                record(idx)
+        else:
+            idx = torch.empty(T, cfg.k, dtype=torch.int32, device=x.device)
+            w = torch.empty(T, cfg.k, dtype=torch.float32, device=x.device)
+            lib().router_fwd(logits, bias, replay_idx, idx, w, cfg.k, cfg.score_fn, cfg.renorm,
+                             cfg.n_group, cfg.topk_group, cfg.scale)
+            if record is not None:
+                record(idx)
+            plan = MoEPlan(idx, cfg.E)
+            xs = plan.gather(x, zero_pad=need_bwd)
         gu, a, ys = experts_forward(xs, w1, w2, plan, save_gu=need_bwd)
         y = torch.empty_like(x)
         lib().moe_combine(ys, plan.dest, w, None, y)

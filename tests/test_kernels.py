@@ -296,3 +296,31 @@ def test_adam():
     wref = wref - 1e-3 * (upd + 0.1 * wref)
     assert (master - wref).abs().max().item() < 1e-5
     assert torch.equal(p, master.to(BF))
+
+
+@pytest.mark.parametrize("score_fn,T", [("softmax", 1), ("softmax", 64), ("sigmoid", 300)])
+def test_fused_route_dispatch_matches_multi_kernel(score_fn, T):
+    """The single-kernel decode route+dispatch equals router_fwd + permute plan + gather."""
+    from miles_b200.ops._lib import lib
+    from miles_b200.ops.moe import MoEPlan, RouterCfg
+
+    torch.manual_seed(11)
+    E, k, H = 128, 8, 2048
+    cfg = RouterCfg(E, k, score_fn, True, 8 if score_fn == "sigmoid" else 1,
+                    4 if score_fn == "sigmoid" else 1, 2.5 if score_fn == "sigmoid" else 1.0)
+    logits = torch.randn(T, E, device=DEV)
+    bias = torch.randn(E, device=DEV) * 0.1 if score_fn == "sigmoid" else None
+    x = torch.randn(T, H, device=DEV, dtype=BF)
+    idx = torch.empty(T, k, dtype=torch.int32, device=DEV)
+    w = torch.empty(T, k, dtype=torch.float32, device=DEV)
+    lib().router_fwd(logits, bias, None, idx, w, k, cfg.score_fn, cfg.renorm, cfg.n_group,
+                     cfg.topk_group, cfg.scale)
+    ref = MoEPlan(idx, E)
+    xs_ref = ref.gather(x, zero_pad=False)
+    plan, idx2, w2, xs = MoEPlan.fused(logits, bias, None, x, cfg)
+    torch.cuda.synchronize()
+    assert torch.equal(idx, idx2) and torch.equal(w, w2)
+    assert torch.equal(ref.counts, plan.counts) and torch.equal(ref.offsets, plan.offsets)
+    assert torch.equal(ref.dest, plan.dest)
+    rows = ref.dest.long()
+    assert torch.equal(xs[rows], xs_ref[rows])
