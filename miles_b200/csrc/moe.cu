@@ -473,9 +473,14 @@ moe_route_dispatch_kernel(const float* __restrict__ logits, const float* __restr
   int* wc = offs + E + 1;  // [kRDWarps][E]
   __shared__ float gscore_sh[kRDWarps][32];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int t = warp; t < T; t += kRDWarps)
-    route_token(logits, bias, idx_in, idx_s, w_s, t, E, k, score_fn, renorm, n_group, topk_group,
-                scale, gscore_sh[warp], lane);
+  const bool routed = logits == nullptr;  // idx_out already holds the routing (plan + gather only)
+  if (routed) {
+    for (int i = tid; i < n; i += blockDim.x) idx_s[i] = idx_out[i];
+  } else {
+    for (int t = warp; t < T; t += kRDWarps)
+      route_token(logits, bias, idx_in, idx_s, w_s, t, E, k, score_fn, renorm, n_group,
+                  topk_group, scale, gscore_sh[warp], lane);
+  }
   for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
   for (int i = tid; i < kRDWarps * E; i += blockDim.x) wc[i] = 0;
   __syncthreads();
@@ -516,10 +521,13 @@ moe_route_dispatch_kernel(const float* __restrict__ logits, const float* __restr
     }
     __syncthreads();
   }
+  // every CTA has read idx_out (when pre-routed) before this point: the grid never writes it then
   if (blockIdx.x == 0) {
     for (int i = tid; i < n; i += blockDim.x) {
-      idx_out[i] = idx_s[i];
-      w_out[i] = w_s[i];
+      if (!routed) {
+        idx_out[i] = idx_s[i];
+        w_out[i] = w_s[i];
+      }
       dest_out[i] = dest_s[i];
     }
     for (int e = tid; e < E; e += blockDim.x) counts_out[e] = cnt[e];
@@ -637,6 +645,14 @@ extern "C" int mb_moe_route_dispatch(const float* logits, const float* bias, con
   }
   int grid = (n + 3) / 4;
   grid = grid < 1 ? 1 : (grid > 148 ? 148 : grid);
+  // Every CTA routes all T tokens itself; past one warp-pass of tokens that redundant work
+  // costs more than a separate, fully parallel router launch, so larger batches route first and
+  // run this kernel for the plan + gather only.
+  if (T > kRDWarps) {
+    mb_launch(router_fwd_kernel, (T + 7) / 8, 256, 0, st, logits, bias, idx_in, idx_out, w_out,
+              T, E, k, score_fn, renorm, n_group, topk_group, scale);
+    logits = nullptr;
+  }
   mb_launch(moe_route_dispatch_kernel, grid, kRDWarps * 32, smem, st, logits, bias, idx_in,
             (const __nv_bfloat16*)x, T, E, k, H, score_fn, renorm, n_group, topk_group, scale,
             align, idx_out, w_out, counts, offsets, dest, (__nv_bfloat16*)xs);

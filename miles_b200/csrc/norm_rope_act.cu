@@ -14,60 +14,78 @@ namespace mb {
 // RMSNorm over rows of length H (H % 256 == 0, H <= 8192), one warp per row.
 //   optional fused residual: h = x + res (bf16), y = norm(h)
 // ----------------------------------------------------------------------------------------------
+// One CTA per row: NT = H / 8 / CPT threads, each owning CPT 16-byte chunks (chunk c of the
+// row at c = tid + j * NT). Sum of squares: per thread in chunk/element order, then the warp
+// xor tree, then the warps in index order (fixed, so every launch gives the same bits).
 template <int H>
-__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
-                                   const __nv_bfloat16* __restrict__ res,
-                                   const __nv_bfloat16* __restrict__ w,
-                                   __nv_bfloat16* __restrict__ h_out, __nv_bfloat16* __restrict__ y,
-                                   float* __restrict__ rstd_out, int rows, float eps) {
+struct RmsShape {
+  static constexpr int NCH = H / 8;
+  static constexpr int CPT = NCH / 128 > 1 ? NCH / 128 : 1;
+  static constexpr int NT = NCH / CPT;
+  static_assert(NCH % CPT == 0 && NT % 32 == 0, "unsupported hidden size");
+};
+
+template <int H>
+__global__ void __launch_bounds__(RmsShape<H>::NT)
+rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res,
+                   const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ h_out,
+                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, int rows,
+                   float eps) {
   pdl_trigger();
   pdl_wait();
-  constexpr int PER = H / 32;  // elements per lane
-  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
+  using S = RmsShape<H>;
+  constexpr int NW = S::NT / 32;
+  __shared__ float wsum[NW];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
   if (row >= rows) return;
-  const __nv_bfloat16* xr = x + (long long)row * H;
-  float v[PER];
+  const long long base = (long long)row * H;
+  float v[S::CPT * 8];
 #pragma unroll
-  for (int i = 0; i < PER / 8; ++i) {
-    const int col = (i * 32 + lane) * 8;
-    uint4 a = *reinterpret_cast<const uint4*>(xr + col);
+  for (int j = 0; j < S::CPT; ++j) {
+    const int col = (tid + j * S::NT) * 8;
+    const uint4 a = *reinterpret_cast<const uint4*>(x + base + col);
     const __nv_bfloat16* ab = reinterpret_cast<const __nv_bfloat16*>(&a);
     if (res) {
-      uint4 b = *reinterpret_cast<const uint4*>(res + (long long)row * H + col);
-      const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&b);
+      const uint4 r = *reinterpret_cast<const uint4*>(res + base + col);
+      const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&r);
       uint4 o;
       __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        ob[j] = __float2bfloat16(__bfloat162float(ab[j]) + __bfloat162float(bb[j]));
-        v[i * 8 + j] = __bfloat162float(ob[j]);
+      for (int e = 0; e < 8; ++e) {
+        ob[e] = __float2bfloat16(__bfloat162float(ab[e]) + __bfloat162float(rb[e]));
+        v[j * 8 + e] = __bfloat162float(ob[e]);
       }
-      *reinterpret_cast<uint4*>(h_out + (long long)row * H + col) = o;
+      *reinterpret_cast<uint4*>(h_out + base + col) = o;
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[i * 8 + j] = __bfloat162float(ab[j]);
+      for (int e = 0; e < 8; ++e) v[j * 8 + e] = __bfloat162float(ab[e]);
     }
   }
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < PER; ++i) ss += v[i] * v[i];
+  for (int i = 0; i < S::CPT * 8; ++i) ss += v[i] * v[i];
   ss = warp_sum(ss);
-  const float rstd = rsqrtf(ss / (float)H + eps);
-  if (lane == 0 && rstd_out) rstd_out[row] = rstd;
+  if ((tid & 31) == 0) wsum[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
 #pragma unroll
-  for (int i = 0; i < PER / 8; ++i) {
-    const int col = (i * 32 + lane) * 8;
-    uint4 wv = *reinterpret_cast<const uint4*>(w + col);
+  for (int i = 0; i < NW; ++i) tot += wsum[i];
+  const float rstd = rsqrtf(tot / (float)H + eps);
+  if (tid == 0 && rstd_out) rstd_out[row] = rstd;
+#pragma unroll
+  for (int j = 0; j < S::CPT; ++j) {
+    const int col = (tid + j * S::NT) * 8;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + col);
     const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv);
     uint4 o;
     __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float nrm = __bfloat162float(__float2bfloat16(v[i * 8 + j] * rstd));
-      ob[j] = __float2bfloat16(nrm * __bfloat162float(wb[j]));
+    for (int e = 0; e < 8; ++e) {
+      const float nrm = __bfloat162float(__float2bfloat16(v[j * 8 + e] * rstd));
+      ob[e] = __float2bfloat16(nrm * __bfloat162float(wb[e]));
     }
-    *reinterpret_cast<uint4*>(y + (long long)row * H + col) = o;
+    *reinterpret_cast<uint4*>(y + base + col) = o;
   }
 }
 
@@ -399,11 +417,9 @@ static int grid_for(long long n, int block) {
 extern "C" int mb_rmsnorm_fwd(const void* x, const void* res, const void* w, void* h_out, void* y,
                               float* rstd, int rows, int H, float eps, cudaStream_t st) {
   if (rows == 0) return 0;
-  const int block = 256, rpb = block / 32;
-  const int grid = (rows + rpb - 1) / rpb;
 #define RMS_CASE(HH)                                                                           \
   case HH:                                                                                     \
-    mb_launch(rmsnorm_fwd_kernel<HH>, grid, block, 0, st,                                             \
+    mb_launch(rmsnorm_fwd_kernel<HH>, rows, RmsShape<HH>::NT, 0, st,                           \
         (const __nv_bfloat16*)x, (const __nv_bfloat16*)res, (const __nv_bfloat16*)w,           \
         (__nv_bfloat16*)h_out, (__nv_bfloat16*)y, rstd, rows, eps);                            \
     break;
