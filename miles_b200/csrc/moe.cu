@@ -486,16 +486,27 @@ moe_route_dispatch_kernel(const float* __restrict__ logits, const float* __restr
   __syncthreads();
   for (int i = tid; i < n; i += blockDim.x) atomicAdd(&cnt[idx_s[i]], 1);
   __syncthreads();
-  if (tid == 0) {
-    int acc = 0;
-    for (int e = 0; e < E; ++e) {
-      offs[e] = acc;
-      run[e] = acc;
-      acc += (cnt[e] + align - 1) / align * align;
+  {  // exclusive scan of the padded counts: per-warp shuffle scan, then warp totals in order
+    const int pc = tid < E ? (cnt[tid] + align - 1) / align * align : 0;
+    int incl = pc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffff, incl, o);
+      if (lane >= o) incl += y;
     }
-    offs[E] = acc;
+    if (lane == 31) wc[warp] = incl;  // wc is free until the rank loop (re-zeroed below)
+    __syncthreads();
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += wc[w];
+    if (tid < E) {
+      offs[tid] = before + incl - pc;
+      run[tid] = before + incl - pc;
+    }
+    if (tid == E - 1) offs[E] = before + incl;
+    __syncthreads();
+    if (tid < kRDWarps) wc[tid] = 0;
+    __syncthreads();
   }
-  __syncthreads();
   // stable ranks, one block-sized chunk of entries at a time
   for (int c0 = 0; c0 < n; c0 += blockDim.x) {
     const int i = c0 + tid;
@@ -643,8 +654,9 @@ extern "C" int mb_moe_route_dispatch(const float* logits, const float* bias, con
       return -3;
     attr = true;
   }
-  int grid = (n + 3) / 4;
-  grid = grid < 1 ? 1 : (grid > 148 ? 148 : grid);
+  // one row per CTA up to the SM count: the plan is rebuilt redundantly per CTA (cheap), the
+  // gather latency is not
+  const int grid = n < 148 ? n : 148;
   // Every CTA routes all T tokens itself; past one warp-pass of tokens that redundant work
   // costs more than a separate, fully parallel router launch, so larger batches route first and
   // run this kernel for the plan + gather only.
