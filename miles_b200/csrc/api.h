@@ -82,7 +82,14 @@ int mb_attn_bwd(const void* q, const void* k, const void* v, const void* o, cons
                 const int* cu_seqlens, const int* blk_seq, const int* blk_idx, int nblocks,
                 long long q_stride, long long k_stride, long long v_stride, long long o_stride,
                 long long do_stride, long long dq_stride, long long dk_stride,
-                long long dv_stride, int nq, int nkv, int T, float softmax_scale, cudaStream_t st);
+                long long dv_stride, int nq, int nkv, int T, float softmax_scale, int* err,
+                cudaStream_t st);
+int mb_fa_bwd(const void* q, const void* k, const void* v, const void* dout, const float* lse,
+              const float* delta, void* dq, void* dk, void* dv, const int* cu_seqlens,
+              const int* tile_seq, const int* tile_idx, int ntiles, long long q_stride,
+              long long k_stride, long long v_stride, long long do_stride, long long dq_stride,
+              long long dk_stride, long long dv_stride, int nq, int nkv, int T,
+              float softmax_scale, int* err, cudaStream_t st);
 int mb_logprob_fwd(const float* logits, long long ld, const int* target, int n, int V,
                    float inv_temp, float* logp, float* ent, float* lse, cudaStream_t st);
 int mb_logprob_bwd(const float* logits, long long ld, const int* target, int n, int V,

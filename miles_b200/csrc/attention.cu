@@ -481,28 +481,16 @@ extern "C" int mb_attn_bwd(const void* q, const void* k, const void* v, const vo
                            int nblocks, long long q_stride, long long k_stride, long long v_stride,
                            long long o_stride, long long do_stride, long long dq_stride,
                            long long dk_stride, long long dv_stride, int nq, int nkv, int T,
-                           float softmax_scale, cudaStream_t st) {
+                           float softmax_scale, int* err, cudaStream_t st) {
+  // blk_seq / blk_idx: the 128-row tile table of the forward (tcgen05 backward kernels)
   if (nblocks == 0) return 0;
   if (nq % nkv) return -1;
   const long long warps = (long long)T * nq;
   mb_launch(attn_bwd_delta_kernel, (unsigned)((warps + 7) / 8), 256, 0, st, 
       (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, o_stride, do_stride, T, nq, delta);
-  BwdParams p{(const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
-              (const __nv_bfloat16*)dout, lse, delta, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk,
-              (__nv_bfloat16*)dv, cu_seqlens, blk_seq, blk_idx, q_stride, k_stride, v_stride,
-              do_stride, dq_stride, dk_stride, dv_stride, nq, nkv, T,
-              softmax_scale * 1.4426950408889634f, softmax_scale};
-  const int smem_kv = 4 * TILE_BYTES + 128 * sizeof(float);
-  const int smem_q = 4 * TILE_BYTES;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(attn_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_kv);
-    cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_q);
-    set = true;
-  }
-  mb_launch(attn_bwd_dkdv_kernel, dim3(nblocks, nkv), 128, smem_kv, st, p);
-  mb_launch(attn_bwd_dq_kernel, dim3(nblocks, nq), 128, smem_q, st, p);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  return mb_fa_bwd(q, k, v, dout, lse, delta, dq, dk, dv, cu_seqlens, blk_seq, blk_idx, nblocks,
+                   q_stride, k_stride, v_stride, do_stride, dq_stride, dk_stride, dv_stride, nq,
+                   nkv, T, softmax_scale, err, st);
 }
 
 // =============================================================================================

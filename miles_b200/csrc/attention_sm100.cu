@@ -138,9 +138,14 @@ MB_DEVICE float merge_val(float O, float o, float fa, float fb) {
   return __fadd_rn(__fmul_rn(O, fa), __fmul_rn(o, fb));
 }
 
-// Bounded wait shared by all roles: gives up (and records code 2) after kSpinLimit polls.
+// Bounded wait shared by all roles: gives up (and records code 2) after the wait limit.
 MB_DEVICE bool wait_bar(uint64_t* bar, uint32_t parity, int* err) {
   return mbar_wait(bar, parity, err, 2);
+}
+// Warp-uniform bounded wait (every lane polls; the result is true only if all lanes saw the
+// phase complete), for warps that go on to warp-collective tcgen05.ld / tcgen05.st.
+MB_DEVICE bool wait_warp(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return __all_sync(0xffffffff, mbar_wait(bar, parity, err, code));
 }
 
 // Work item of a persistent CTA. Mode 0: item = (128-row tile, query head), heads fastest so
@@ -381,7 +386,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
 
       // O <- fma(O, alpha_prev, O_i) for running block i (its PV product is in the O_j buffer)
       auto fold_pv = [&](int i) -> bool {
-        if (!wait_bar(o_full, i & 1, p.err)) return false;
+        if (!wait_warp(o_full, i & 1, p.err, 2)) return false;
         tc_fence_after();
         if (!idle) {
 #pragma unroll
@@ -423,14 +428,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
       // Block j: S_j -> P_j (into the S buffer) while PV_{j-1} runs; O_{j-1} is folded in at
       // the end of the block (at the start at chunk boundaries, where the chunk must be
       // complete).
+      // A failed wait (ok = false) skips the TMEM work but keeps executing the named barriers,
+      // so the other softmax warps never block on a barrier this warp stopped reaching.
       for (int j = 0; j < it.nblk; ++j, ++g) {
         const int s = g & 1;
-        if (!wait_bar(s_full + s, (g >> 1) & 1, p.err)) { ok = false; break; }
+        ok = ok && wait_warp(s_full + s, (g >> 1) & 1, p.err, 2);
         tc_fence_after();
         const bool boundary = MODE == 0 && j > 0 && j % CHUNK == 0;
         if (boundary) {
-          if (!fold_pv(g - 1)) { ok = false; break; }
-          merge_chunk(j == CHUNK);
+          ok = ok && fold_pv(g - 1);
+          if (ok) merge_chunk(j == CHUNK);
 #pragma unroll
           for (int i = 0; i < 64; ++i) O[i] = 0.f;
           m = -INFINITY;
@@ -445,7 +452,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         // pass 1: row max of the raw scores (scaling is monotonic, so max(S) * scale equals
         // the max of the scaled scores bit for bit; max is exact in any order)
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (!idle) {
+        if (!idle && ok) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             uint32_t r[32];
@@ -474,7 +481,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         // packed into columns half*64 .. half*64+31 of the S buffer (inside the columns it has
         // itself just read), one 32-key group at a time.
         float cs[2] = {0.f, 0.f};
-        if (!idle) {
+        if (!idle && ok) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             uint32_t r[32];
@@ -503,17 +510,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full + s);
+        if (lane == 0 && ok) mbar_arrive(p_full + s);
         red_sum[half * 128 + row] = __fadd_rn(cs[0], cs[1]);
         softmax_sync();
         const float rs = __fadd_rn(red_sum[row], red_sum[128 + row]);
         l = __fmaf_rn(l, alpha, rs);
         m = mnew;
-        if (j >= 1 && !boundary && !fold_pv(g - 1)) { ok = false; break; }
+        if (j >= 1 && !boundary) ok = ok && fold_pv(g - 1);
         alpha_prev = alpha;
       }
-      if (!ok) break;
-      if (!fold_pv(g - 1)) { ok = false; break; }
+      ok = ok && fold_pv(g - 1);
+      if (!ok) continue;  // every softmax warp runs the same iterations (named barriers)
       if (MODE == 0) {
         if (it.nblk > CHUNK) {
           merge_chunk(false);
@@ -576,6 +583,453 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     }
   }
 
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// =============================================================================================
+// Backward (tcgen05). Two deterministic kernels (no atomics: every output tile has one owner
+// that walks its inputs in a fixed order):
+//   fa_bwd_dkdv_kernel: CTA = (128-key block j of one sequence, KV head). For every query head
+//     of the group and every query tile i >= j:
+//       S^T = K Q^T, dP^T = V dO^T (UMMA, keys x queries), P^T = 2^(S^T scale - lse2),
+//       dS^T = P^T (dP^T - delta); dV += P^T dO, dK += dS^T Q (P^T / dS^T from TMEM).
+//   fa_bwd_dq_kernel:   CTA = (128-query tile i, query head). For every key block j <= i:
+//       S = Q K^T, dP = dO V^T, P, dS as above (rows = queries); dQ += dS K.
+// dK and dQ are scaled by the softmax scale at the end. Q / dO / K tiles are loaded once in
+// the K-major SW128 layout and read both as K-major operands (contraction over the head dim)
+// and as MN-major operands (contraction over tokens: leading byte offset = one 16 KB d-half
+// sub-tile).
+// Roles: warp 0 TMA, warp 1 TMEM + MMA, warps 2-9 elementwise (two threads per TMEM lane, 64
+// columns each), the same warps write the outputs.
+// =============================================================================================
+struct BwdParams {
+  const int* cu_seqlens;
+  const int* tile_seq;
+  const int* tile_idx;
+  const float* lse;    // [nq, T] natural log
+  const float* delta;  // [nq, T]
+  __nv_bfloat16 *dq, *dk, *dv;
+  long long dq_stride, dk_stride, dv_stride;
+  int nq, nkv, T;
+  float scale_log2, scale;
+  int* err;
+};
+
+constexpr int BW_THREADS = 320;
+// dkdv smem: K | V (32 KB each) | 2 stages x (Q | dO) | 2 x (lse2 | delta) [128 f32 each] | bars
+constexpr int BW_OFF_K = 0;
+constexpr int BW_OFF_V = TILE;
+constexpr int BW_OFF_STAGE = 2 * TILE;            // stage s: Q at +s*2*TILE, dO at +TILE
+constexpr int BW_OFF_LD = 6 * TILE;               // [2][2][128] floats = 2 KB
+constexpr int BW_OFF_BAR = BW_OFF_LD + 2048;
+constexpr int BW_SMEM = BW_OFF_BAR + 256 + 1024;
+
+MB_DEVICE void load_tile_kmajor(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  tma_load_2d(dst, map, bar, x, y);
+  tma_load_2d(dst + SUB, map, bar, x + 64, y);
+}
+
+__global__ void __launch_bounds__(BW_THREADS, 1)
+fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                   const BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BW_OFF_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* st_full = bars + 1;   // [2]
+  uint64_t* st_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* pd_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(st_full + s, 1);
+      mbar_init(st_empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 8);
+    mbar_init(pd_done, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();
+
+  const int G = p.nq / p.nkv;
+  const int b = p.tile_seq[blockIdx.x], j = p.tile_idx[blockIdx.x];
+  const int hk = blockIdx.y;
+  const int seq_start = p.cu_seqlens[b], len = p.cu_seqlens[b + 1] - seq_start;
+  const int ntile = (len + BM - 1) / BM;
+  const int nq_tiles = ntile - j;          // query tiles j .. ntile-1
+  const int nsteps = G * nq_tiles;         // (head, query tile) pairs, head-major
+  auto step_hi = [&](int n, int& h, int& i) { h = hk * G + n / nq_tiles; i = j + n % nq_tiles; };
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(kv_full, 2 * TILE);
+      load_tile_kmajor(smem + BW_OFF_K, &tmK, kv_full, hk * D, seq_start + j * BN);
+      load_tile_kmajor(smem + BW_OFF_V, &tmV, kv_full, hk * D, seq_start + j * BN);
+      for (int n = 0; n < nsteps; ++n) {
+        const int s = n & 1;
+        if (!mbar_wait(st_empty + s, ((n >> 1) & 1) ^ 1, p.err, 21)) break;
+        int h, i;
+        step_hi(n, h, i);
+        uint8_t* st = smem + BW_OFF_STAGE + s * 2 * TILE;
+        mbar_arrive_expect_tx(st_full + s, 2 * TILE);
+        load_tile_kmajor(st, &tmQ, st_full + s, h * D, seq_start + i * BM);
+        load_tile_kmajor(st + TILE, &tmDO, st_full + s, h * D, seq_start + i * BM);
+      }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, false, false);
+    constexpr uint32_t idesc_mn = make_idesc_bf16(128, 128, false, true);
+    const uint32_t sk = smem_u32(smem + BW_OFF_K), sv = smem_u32(smem + BW_OFF_V);
+    bool ok = mbar_wait(kv_full, 0, p.err, 22);
+    for (int n = 0; ok && n < nsteps; ++n) {
+      const int s = n & 1;
+      if (!mbar_wait(st_full + s, (n >> 1) & 1, p.err, 23)) break;
+      if (n >= 1 && !mbar_wait(pd_done, (n - 1) & 1, p.err, 24)) break;  // P^T / dS^T consumed
+      tc_fence_after();
+      const uint32_t sq = smem_u32(smem + BW_OFF_STAGE + s * 2 * TILE), sdo = sq + TILE;
+      if (elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T (contract over d)
+          const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
+          umma_f16(tmem_base, make_sdesc_sw128(sk + off, 16, 1024),
+                   make_sdesc_sw128(sq + off, 16, 1024), idesc_s, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // dP^T = V dO^T
+          const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
+          umma_f16(tmem_base + 128, make_sdesc_sw128(sv + off, 16, 1024),
+                   make_sdesc_sw128(sdo + off, 16, 1024), idesc_s, kk > 0);
+        }
+        umma_commit(s_full);
+      }
+      __syncwarp();
+      if (!mbar_wait(p_full, n & 1, p.err, 25)) break;
+      tc_fence_after();
+      if (elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // dV += P^T dO (contract over queries)
+          const uint32_t pa = (kk >> 2) * 64 + (kk & 3) * 8;
+          umma_f16_ts(tmem_base + 256, tmem_base + pa,
+                      make_sdesc_sw128(sdo + kk * 2048, SUB, 1024), idesc_mn,
+                      (n > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // dK += dS^T Q
+          const uint32_t pa = (kk >> 2) * 64 + (kk & 3) * 8;
+          umma_f16_ts(tmem_base + 384, tmem_base + 128 + pa,
+                      make_sdesc_sw128(sq + kk * 2048, SUB, 1024), idesc_mn,
+                      (n > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(pd_done);
+        umma_commit(st_empty + s);
+      }
+      __syncwarp();
+    }
+  } else {
+    const int sw = warp - 2, quad = warp & 3, half = sw >> 2;
+    const int row = quad * 32 + lane;  // key within the block
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int kpos = j * BN + row;
+    float* ld = reinterpret_cast<float*>(smem + BW_OFF_LD);  // [2 bufs][lse2 128 | delta 128]
+    const int tid = threadIdx.x - 64;                          // 0..255
+    auto sync256 = [] { asm volatile("bar.sync 1, 256;" ::: "memory"); };
+    const float LOG2E = 1.4426950408889634f;
+    auto fetch = [&](int n) -> float {  // value this thread stores for step n
+      int h, i;
+      step_hi(n, h, i);
+      const int q = i * BM + (tid & 127);
+      if (q >= len) return 0.f;
+      const long long at = (long long)h * p.T + seq_start + q;
+      return tid < 128 ? p.lse[at] * LOG2E : p.delta[at];
+    };
+    bool ok = true;
+    if (nsteps > 0) {
+      ld[tid] = fetch(0);
+      sync256();
+    }
+    for (int n = 0; n < nsteps; ++n) {
+      const float nxt = n + 1 < nsteps ? fetch(n + 1) : 0.f;  // prefetch next step's vectors
+      int h, i;
+      step_hi(n, h, i);
+      const float* lse2 = ld + (n & 1) * 256;
+      const float* dlt = lse2 + 128;
+      ok = ok && wait_warp(s_full, n & 1, p.err, 26);  // on failure keep the barrier protocol
+      tc_fence_after();
+      const bool edge = (i == j) || (i == ntile - 1);
+#pragma unroll
+      for (int c = 0; c < 2 && ok; ++c) {
+        uint32_t rs[32], rp[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_off + half * 64 + c * 32, rs);
+        tmem_ld_32x32b_x32(tmem_base + lane_off + 128 + half * 64 + c * 32, rp);
+        tmem_ld_wait();
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], dv2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int ql = half * 64 + c * 32 + e + u;  // query within the tile
+            float pp = ex2_approx(__fmaf_rn(__uint_as_float(rs[e + u]), p.scale_log2, -lse2[ql]));
+            if (edge) {
+              const int qpos = i * BM + ql;
+              if (qpos < kpos || qpos >= len) pp = 0.f;
+            }
+            pv[u] = pp;
+            dv2[u] = pp * (__uint_as_float(rp[e + u]) - dlt[ql]);
+          }
+          const __nv_bfloat162 hp = __floats2bfloat162_rn(pv[0], pv[1]);
+          const __nv_bfloat162 hd = __floats2bfloat162_rn(dv2[0], dv2[1]);
+          pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+          dk[e >> 1] = *reinterpret_cast<const uint32_t*>(&hd);
+        }
+        tmem_st_32x32b_x16(tmem_base + lane_off + half * 64 + c * 16, pk);
+        tmem_st_32x32b_x16(tmem_base + lane_off + 128 + half * 64 + c * 16, dk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive(p_full);
+      ld[((n + 1) & 1) * 256 + tid] = nxt;
+      sync256();  // next step's vectors visible; this step's reads done
+    }
+    if (__all_sync(0xffffffff, ok) && nsteps > 0 && wait_warp(pd_done, (nsteps - 1) & 1, p.err, 27)) {
+      tc_fence_after();
+      // tcgen05.ld is warp-collective: every lane loads, only rows inside the sequence store
+      const bool kok = kpos < len;
+      const long long r = seq_start + (kok ? kpos : 0);
+      __nv_bfloat16* dv_out = p.dv + r * p.dv_stride + (long long)hk * D + half * 64;
+      __nv_bfloat16* dk_out = p.dk + r * p.dk_stride + (long long)hk * D + half * 64;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t a[32], bb[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_off + 256 + half * 64 + c * 32, a);
+        tmem_ld_32x32b_x32(tmem_base + lane_off + 384 + half * 64 + c * 32, bb);
+        tmem_ld_wait();
+        if (!kok) continue;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 ov, okv;
+          ov.x = pack_bf16x2(__uint_as_float(a[q * 8 + 0]), __uint_as_float(a[q * 8 + 1]));
+          ov.y = pack_bf16x2(__uint_as_float(a[q * 8 + 2]), __uint_as_float(a[q * 8 + 3]));
+          ov.z = pack_bf16x2(__uint_as_float(a[q * 8 + 4]), __uint_as_float(a[q * 8 + 5]));
+          ov.w = pack_bf16x2(__uint_as_float(a[q * 8 + 6]), __uint_as_float(a[q * 8 + 7]));
+          okv.x = pack_bf16x2(__uint_as_float(bb[q * 8 + 0]) * p.scale, __uint_as_float(bb[q * 8 + 1]) * p.scale);
+          okv.y = pack_bf16x2(__uint_as_float(bb[q * 8 + 2]) * p.scale, __uint_as_float(bb[q * 8 + 3]) * p.scale);
+          okv.z = pack_bf16x2(__uint_as_float(bb[q * 8 + 4]) * p.scale, __uint_as_float(bb[q * 8 + 5]) * p.scale);
+          okv.w = pack_bf16x2(__uint_as_float(bb[q * 8 + 6]) * p.scale, __uint_as_float(bb[q * 8 + 7]) * p.scale);
+          reinterpret_cast<uint4*>(dv_out + c * 32)[q] = ov;
+          reinterpret_cast<uint4*>(dk_out + c * 32)[q] = okv;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// dq smem: Q | dO (32 KB each) | 2 stages x (K | V) | bars
+constexpr int BQ_OFF_Q = 0;
+constexpr int BQ_OFF_DO = TILE;
+constexpr int BQ_OFF_STAGE = 2 * TILE;
+constexpr int BQ_OFF_BAR = 6 * TILE;
+constexpr int BQ_SMEM = BQ_OFF_BAR + 256 + 1024;
+
+__global__ void __launch_bounds__(BW_THREADS, 1)
+fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                 const BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BQ_OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* st_full = bars + 1;   // [2]
+  uint64_t* st_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* pd_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(st_full + s, 1);
+      mbar_init(st_empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 8);
+    mbar_init(pd_done, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();
+
+  const int G = p.nq / p.nkv;
+  const int b = p.tile_seq[blockIdx.x], i = p.tile_idx[blockIdx.x];
+  const int h = blockIdx.y, hk = h / G;
+  const int seq_start = p.cu_seqlens[b], len = p.cu_seqlens[b + 1] - seq_start;
+  const int nsteps = i + 1;  // key blocks 0..i
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(q_full, 2 * TILE);
+      load_tile_kmajor(smem + BQ_OFF_Q, &tmQ, q_full, h * D, seq_start + i * BM);
+      load_tile_kmajor(smem + BQ_OFF_DO, &tmDO, q_full, h * D, seq_start + i * BM);
+      for (int n = 0; n < nsteps; ++n) {
+        const int s = n & 1;
+        if (!mbar_wait(st_empty + s, ((n >> 1) & 1) ^ 1, p.err, 28)) break;
+        uint8_t* st = smem + BQ_OFF_STAGE + s * 2 * TILE;
+        mbar_arrive_expect_tx(st_full + s, 2 * TILE);
+        load_tile_kmajor(st, &tmK, st_full + s, hk * D, seq_start + n * BN);
+        load_tile_kmajor(st + TILE, &tmV, st_full + s, hk * D, seq_start + n * BN);
+      }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, false, false);
+    constexpr uint32_t idesc_mn = make_idesc_bf16(128, 128, false, true);
+    const uint32_t sq = smem_u32(smem + BQ_OFF_Q), sdo = smem_u32(smem + BQ_OFF_DO);
+    bool ok = mbar_wait(q_full, 0, p.err, 29);
+    for (int n = 0; ok && n < nsteps; ++n) {
+      const int s = n & 1;
+      if (!mbar_wait(st_full + s, (n >> 1) & 1, p.err, 30)) break;
+      if (n >= 1 && !mbar_wait(pd_done, (n - 1) & 1, p.err, 31)) break;
+      tc_fence_after();
+      const uint32_t sk = smem_u32(smem + BQ_OFF_STAGE + s * 2 * TILE), sv = sk + TILE;
+      if (elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // S = Q K^T
+          const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
+          umma_f16(tmem_base, make_sdesc_sw128(sq + off, 16, 1024),
+                   make_sdesc_sw128(sk + off, 16, 1024), idesc_s, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // dP = dO V^T
+          const uint32_t off = (kk >> 2) * SUB + (kk & 3) * 32;
+          umma_f16(tmem_base + 128, make_sdesc_sw128(sdo + off, 16, 1024),
+                   make_sdesc_sw128(sv + off, 16, 1024), idesc_s, kk > 0);
+        }
+        umma_commit(s_full);
+      }
+      __syncwarp();
+      if (!mbar_wait(p_full, n & 1, p.err, 32)) break;
+      tc_fence_after();
+      if (elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K (contract over keys)
+          const uint32_t pa = (kk >> 2) * 64 + (kk & 3) * 8;
+          umma_f16_ts(tmem_base + 256, tmem_base + 128 + pa,
+                      make_sdesc_sw128(sk + kk * 2048, SUB, 1024), idesc_mn,
+                      (n > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(pd_done);
+        umma_commit(st_empty + s);
+      }
+      __syncwarp();
+    }
+  } else {
+    const int sw = warp - 2, quad = warp & 3, half = sw >> 2;
+    const int row = quad * 32 + lane;  // query within the tile
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int qpos = i * BM + row;
+    const bool qok = qpos < len;
+    const long long at = (long long)h * p.T + seq_start + (qok ? qpos : 0);
+    const float lse2 = qok ? p.lse[at] * 1.4426950408889634f : 0.f;
+    const float dlt = qok ? p.delta[at] : 0.f;
+    bool ok = true;
+    for (int n = 0; n < nsteps; ++n) {
+      if (!wait_warp(s_full, n & 1, p.err, 33)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = n == i;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t rs[32], rp[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_off + half * 64 + c * 32, rs);
+        tmem_ld_32x32b_x32(tmem_base + lane_off + 128 + half * 64 + c * 32, rp);
+        tmem_ld_wait();
+        uint32_t dk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float d2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            float pp = ex2_approx(__fmaf_rn(__uint_as_float(rs[e + u]), p.scale_log2, -lse2));
+            if (!qok || (diag && n * BN + half * 64 + c * 32 + e + u > qpos)) pp = 0.f;
+            d2[u] = pp * (__uint_as_float(rp[e + u]) - dlt);
+          }
+          const __nv_bfloat162 hd = __floats2bfloat162_rn(d2[0], d2[1]);
+          dk[e >> 1] = *reinterpret_cast<const uint32_t*>(&hd);
+        }
+        tmem_st_32x32b_x16(tmem_base + lane_off + 128 + half * 64 + c * 16, dk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (__all_sync(0xffffffff, ok) && nsteps > 0 && wait_warp(pd_done, (nsteps - 1) & 1, p.err, 34)) {
+      tc_fence_after();
+      // tcgen05.ld is warp-collective: every lane loads, only rows inside the sequence store
+      __nv_bfloat16* out = p.dq + (long long)(seq_start + (qok ? qpos : 0)) * p.dq_stride +
+                           (long long)h * D + half * 64;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t a[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_off + 256 + half * 64 + c * 32, a);
+        tmem_ld_wait();
+        if (!qok) continue;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(a[q * 8 + 0]) * p.scale, __uint_as_float(a[q * 8 + 1]) * p.scale);
+          v.y = pack_bf16x2(__uint_as_float(a[q * 8 + 2]) * p.scale, __uint_as_float(a[q * 8 + 3]) * p.scale);
+          v.z = pack_bf16x2(__uint_as_float(a[q * 8 + 4]) * p.scale, __uint_as_float(a[q * 8 + 5]) * p.scale);
+          v.w = pack_bf16x2(__uint_as_float(a[q * 8 + 6]) * p.scale, __uint_as_float(a[q * 8 + 7]) * p.scale);
+          reinterpret_cast<uint4*>(out + c * 32)[q] = v;
+        }
+      }
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -694,4 +1148,45 @@ extern "C" int mb_fa_decode(const void* q, const void* kc, const void* vc, void*
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.err = err;
   return launch_fa<1>(tq, tk, tv, p, B * nkv * nsplit_max, st);
+}
+
+// Backward of mb_fa_fwd: dq [T, nq, 128], dk / dv [T, nkv, 128] (row strides given; every row
+// is written). delta = rowsum(dO * O) [nq, T] and lse [nq, T] come from the caller.
+extern "C" int mb_fa_bwd(const void* q, const void* k, const void* v, const void* dout,
+                         const float* lse, const float* delta, void* dq, void* dk, void* dv,
+                         const int* cu_seqlens, const int* tile_seq, const int* tile_idx,
+                         int ntiles, long long q_stride, long long k_stride, long long v_stride,
+                         long long do_stride, long long dq_stride, long long dk_stride,
+                         long long dv_stride, int nq, int nkv, int T, float softmax_scale,
+                         int* err, cudaStream_t st) {
+  if (ntiles == 0 || T == 0) return 0;
+  if (nq % nkv) return -1;
+  if (int rc = current_ctx()) return rc;
+  CUtensorMap tq, tk, tv, tdo;
+  int rc = make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, (uint64_t)nq * D, q_stride, 64, 128);
+  if (rc) return rc;
+  rc = make_map(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, (uint64_t)nkv * D, k_stride, 64, 128);
+  if (rc) return rc;
+  rc = make_map(&tv, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, (uint64_t)nkv * D, v_stride, 64, 128);
+  if (rc) return rc;
+  rc = make_map(&tdo, dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, (uint64_t)nq * D, do_stride, 64, 128);
+  if (rc) return rc;
+  BwdParams p{cu_seqlens, tile_seq, tile_idx, lse, delta, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk,
+              (__nv_bfloat16*)dv, dq_stride, dk_stride, dv_stride, nq, nkv, T,
+              softmax_scale * 1.4426950408889634f, softmax_scale, err};
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(fa_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BW_SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(fa_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BQ_SMEM) != cudaSuccess)
+      return -3;
+    attr = true;
+  }
+  mb_launch(fa_bwd_dkdv_kernel, dim3(ntiles, nkv), dim3(BW_THREADS), BW_SMEM, st, tq, tk, tv, tdo, p);
+  mb_launch(fa_bwd_dq_kernel, dim3(ntiles, nq), dim3(BW_THREADS), BQ_SMEM, st, tq, tk, tv, tdo, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    fprintf(stderr, "fa_bwd launch failed: %s\n", cudaGetErrorString(e));
+    return -2;
+  }
+  return 0;
 }

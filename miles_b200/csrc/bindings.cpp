@@ -233,12 +233,15 @@ int64_t attn_decode(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::
 int64_t attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
               torch::Tensor dout, torch::Tensor lse, torch::Tensor delta, torch::Tensor dq,
               torch::Tensor dk, torch::Tensor dv, torch::Tensor cu, torch::Tensor blk_seq,
-              torch::Tensor blk_idx, int64_t nq, int64_t nkv, double scale) {
+              torch::Tensor blk_idx, int64_t nq, int64_t nkv, double scale, torch::Tensor err) {
+  TORCH_CHECK(q.stride(0) % 8 == 0 && k.stride(0) % 8 == 0 && v.stride(0) % 8 == 0 &&
+              dout.stride(0) % 8 == 0, "attention row strides must be 16-byte multiples");
+  c10::cuda::CUDAGuard g(q.device());
   return mb_attn_bwd(P(q), P(k), P(v), P(o), P(dout), PT<float>(lse), PT<float>(delta), P(dq),
                        P(dk), P(dv), PT<int>(cu), PT<int>(blk_seq), PT<int>(blk_idx),
                        blk_seq.numel(), q.stride(0), k.stride(0), v.stride(0), o.stride(0),
                        dout.stride(0), dq.stride(0), dk.stride(0), dv.stride(0), nq, nkv,
-                       q.size(0), (float)scale, cur_stream());
+                       q.size(0), (float)scale, err.data_ptr<int>(), cur_stream());
 }
 
 int64_t logprob_fwd(torch::Tensor logits, torch::Tensor target, double inv_temp, OT logp, OT ent,

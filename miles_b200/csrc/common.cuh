@@ -64,8 +64,8 @@ MB_DEVICE void report_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
-// Spin limit for mbarrier waits. try_wait itself suspends for a hardware-defined window, so
-// 1<<22 iterations is several seconds of wall time: far beyond any legitimate stall.
+// Spin limit for mbarrier waits: with the suspend hint of mbar_try_wait, 1<<22 polls is about
+// 2 s of wall time, far beyond any legitimate stall.
 constexpr uint32_t kSpinLimit = 1u << 22;
 
 // Host: 2-D row-major [rows, cols] tensor map with a {box_cols, box_rows} box and 128-byte
@@ -111,22 +111,38 @@ MB_DEVICE void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One poll; a waiting thread may be suspended for up to kSuspendHintNs before it returns, which
+// bounds the wall time of kSpinLimit polls (about 2 s) independently of the hardware default.
+constexpr uint32_t kSuspendHintNs = 500;
 MB_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred P;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, P;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait; returns false (and records `code`) if the phase never completed.
+MB_DEVICE uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wall-clock limit of one bounded wait (nanoseconds of %globaltimer).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// Bounded wait; returns false (and records `code`) if the phase did not complete within
+// kWaitLimitNs of wall time (or kSpinLimit polls, whichever comes first).
 MB_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 63 && global_ns() - t0 > kWaitLimitNs) break;
   }
   report_error(err, code);
   return false;

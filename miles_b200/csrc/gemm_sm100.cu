@@ -139,9 +139,14 @@ MB_DEVICE TileInfo get_tile(const GemmParams& p, int t) {
 
 // Bounded wait that also gives up promptly once another role has aborted.
 MB_DEVICE bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 255 && *abort_flag) return false;
+    if ((i & 63) == 63 && (*abort_flag || global_ns() - t0 > kWaitLimitNs)) {
+      if (*abort_flag) return false;
+      break;
+    }
   }
   report_error(err, 1);
   *abort_flag = 1;
@@ -329,7 +334,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const TileInfo ti = get_tile<BN, MODE>(p, t);
       if (!ti.valid) continue;
-      if (!wait_or_abort(tfull_bar + acc, acc_phase, abort_flag, p.err)) break;
+      // warp-uniform: the TMEM loads below are warp-collective
+      if (!__all_sync(0xffffffff, wait_or_abort(tfull_bar + acc, acc_phase, abort_flag, p.err))) break;
       tc_fence_after();
       const bool empty_k = ti.kend <= ti.kbeg;
       const int row = ti.m0 + quad * 32 + lane;

@@ -101,7 +101,8 @@ class _VarlenAttn(torch.autograd.Function):
         delta = torch.empty(nq, T, dtype=torch.float32, device=q.device)
         lib().attn_bwd(q.reshape(T, -1), k.reshape(T, -1), v.reshape(T, -1), o.view(T, -1),
                        do.view(T, -1), lse, delta, dq.view(T, -1), dk.view(T, -1), dv.view(T, -1),
-                       meta.cu, meta.blk_seq, meta.blk_idx, nq, nkv, ctx.scale)
+                       meta.cu, meta.tile_seq, meta.tile_idx, nq, nkv, ctx.scale,
+                       err_word(q.device))
         return dq, dk, dv, None, None
 
 
