@@ -91,7 +91,10 @@ class RolloutEngine:
     # ------------------------------------------------------------------ memory
     def kv_bytes_per_page(self) -> int:
         c = self.cfg
-        return 2 * c.num_layers * PAGE * c.num_kv_heads * c.head_dim * 2
+        from miles_b200.models.transformer import kv_cache_shape
+
+        nkv, hd = kv_cache_shape(c)
+        return (1 if c.kv_lora_rank else 2) * c.num_layers * PAGE * nkv * hd * 2
 
     def resume_memory(self):
         """Allocate the KV cache (and lazily the decode graphs). Mirrors resume_memory_occupation."""

@@ -168,6 +168,14 @@ def preset(name: str) -> ModelConfig:
         return ModelConfig(arch="qwen3_moe", vocab_size=8192, hidden_size=512, num_layers=2,
                            num_heads=8, num_kv_heads=2, head_dim=128, num_experts=16, topk=4,
                            moe_intermediate_size=256, max_position=8192)
+    if n in ("tiny-mla",):  # CPU / GPU plumbing shape of the DeepSeek-style MLA + MoE family
+        return ModelConfig(arch="deepseek_v3", vocab_size=4096, hidden_size=256, num_layers=2,
+                           num_heads=4, num_kv_heads=4, head_dim=128, intermediate_size=512,
+                           num_experts=8, topk=2, moe_intermediate_size=128, num_shared_experts=1,
+                           first_k_dense=1, router_score="sigmoid", n_group=2, topk_group=1,
+                           kv_lora_rank=64, qk_nope_head_dim=32, qk_rope_head_dim=16,
+                           v_head_dim=32, qk_norm=False, routed_scaling_factor=2.5,
+                           max_position=4096)
     if n in ("dsv3-small", "deepseek-v3-small"):
         # BASELINE config 5 shape: MLA + MoE, sigmoid grouped routing, shared experts
         return ModelConfig(arch="deepseek_v3", vocab_size=163840, hidden_size=2048, num_layers=27,

@@ -54,13 +54,16 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1) -> list[ParamSpec]:
     specs = [ParamSpec("embed_tokens.weight", (cfg.vocab_size, H), "normal")]
     for i in range(cfg.num_layers):
         p = f"layers.{i}."
-        specs += [
-            ParamSpec(p + "input_layernorm.weight", (H,), "ones"),
-            ParamSpec(p + "self_attn.qkv_proj.weight", ((nq + 2 * nkv) * D, H), "normal"),
-            ParamSpec(p + "self_attn.o_proj.weight", (H, nq * D), "normal"),
-            ParamSpec(p + "post_attention_layernorm.weight", (H,), "ones"),
-        ]
-        if cfg.qk_norm:
+        specs.append(ParamSpec(p + "input_layernorm.weight", (H,), "ones"))
+        if cfg.kv_lora_rank:  # multi-head latent attention (models/mla.py)
+            from miles_b200.models.mla import mla_param_shapes
+
+            specs += [ParamSpec(n, shp, init) for n, shp, init in mla_param_shapes(cfg, p + "self_attn.")]
+        else:
+            specs += [ParamSpec(p + "self_attn.qkv_proj.weight", ((nq + 2 * nkv) * D, H), "normal"),
+                      ParamSpec(p + "self_attn.o_proj.weight", (H, nq * D), "normal")]
+        specs.append(ParamSpec(p + "post_attention_layernorm.weight", (H,), "ones"))
+        if cfg.qk_norm and not cfg.kv_lora_rank:
             specs += [ParamSpec(p + "self_attn.q_norm.weight", (D,), "ones"),
                       ParamSpec(p + "self_attn.k_norm.weight", (D,), "ones")]
         if cfg.layer_is_moe(i):
@@ -99,6 +102,13 @@ def is_expert_param(name: str) -> bool:
 FLAT_ALIGN = 8192
 
 
+def kv_cache_shape(cfg: ModelConfig) -> tuple[int, int]:
+    """(heads, dim) of one cached token per layer: GQA K and V, or the MLA latent [c | k_pe]."""
+    if cfg.kv_lora_rank:
+        return 1, cfg.kv_lora_rank + cfg.qk_rope_head_dim
+    return cfg.num_kv_heads, cfg.head_dim
+
+
 class KVCache:
     """Paged KV cache: per layer K and V of [num_pages * 64, nkv, 128] bf16.
 
@@ -109,10 +119,12 @@ class KVCache:
     def __init__(self, cfg: ModelConfig, num_pages: int, device, dtype=torch.bfloat16):
         self.num_pages = num_pages
         slots = num_pages * PAGE
-        self.k = [torch.zeros(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device)
+        nkv, hd = kv_cache_shape(cfg)
+        self.k = [torch.zeros(slots, nkv, hd, dtype=dtype, device=device)
                   for _ in range(cfg.num_layers)]
-        self.v = [torch.zeros(slots, cfg.num_kv_heads, cfg.head_dim, dtype=dtype, device=device)
-                  for _ in range(cfg.num_layers)]
+        # MLA caches only the latent (+ rotary key) in `k`
+        vs = 1 if cfg.kv_lora_rank else slots
+        self.v = [torch.zeros(vs, nkv, hd, dtype=dtype, device=device) for _ in range(cfg.num_layers)]
 
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in self.k + self.v)
@@ -160,6 +172,11 @@ class Transformer(torch.nn.Module):
         self.recompute = True
         self.weight_version = 0
         self.lora = None  # miles_b200.models.lora.LoRA when adapters are attached
+        self.mla = None
+        if cfg.kv_lora_rank:
+            from miles_b200.models.mla import MLA
+
+            self.mla = MLA(self)
 
     # -------------------------------------------------------------------------------- projections
     def _lin(self, x: torch.Tensor, name: str) -> torch.Tensor:
@@ -202,6 +219,8 @@ class Transformer(torch.nn.Module):
     # -------------------------------------------------------------------------------- blocks
     def _attn_train(self, i: int, x: torch.Tensor, meta: VarlenMeta) -> torch.Tensor:
         cfg = self.cfg
+        if self.mla is not None:
+            return self.mla.attn(i, x, meta)
         pre = f"layers.{i}.self_attn."
         qkv = self._lin(x, pre + "qkv_proj.weight")
         q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
@@ -294,15 +313,18 @@ class Transformer(torch.nn.Module):
             ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
             x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
             pre = f"layers.{i}.self_attn."
-            qkv = self._lin(x, pre + "qkv_proj.weight")
-            q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
-                                   self.params.get(pre + "k_norm.weight"), meta.positions,
-                                   self.rope_cos, self.rope_sin, cfg.num_heads, cfg.num_kv_heads,
-                                   cfg.rms_eps, cfg.qk_norm)
-            cache.k[i].index_copy_(0, slots, k)
-            cache.v[i].index_copy_(0, slots, v)
-            o = varlen_attention(q, k, v, meta)
-            a = self._lin(o.reshape(x.shape[0], -1), pre + "o_proj.weight")
+            if self.mla is not None:
+                a = self.mla.attn(i, x, meta, cache, slots)
+            else:
+                qkv = self._lin(x, pre + "qkv_proj.weight")
+                q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
+                                       self.params.get(pre + "k_norm.weight"), meta.positions,
+                                       self.rope_cos, self.rope_sin, cfg.num_heads, cfg.num_kv_heads,
+                                       cfg.rms_eps, cfg.qk_norm)
+                cache.k[i].index_copy_(0, slots, k)
+                cache.v[i].index_copy_(0, slots, v)
+                o = varlen_attention(q, k, v, meta)
+                a = self._lin(o.reshape(x.shape[0], -1), pre + "o_proj.weight")
             x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"],
                                  cfg.rms_eps)
             rec = record.append if (record is not None and i in self.router_cfgs) else None
@@ -324,14 +346,17 @@ class Transformer(torch.nn.Module):
             ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
             x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
             pre = f"layers.{i}.self_attn."
-            qkv = self._lin(x, pre + "qkv_proj.weight")
-            q = qk_norm_rope_to_cache(qkv, self.params.get(pre + "q_norm.weight"),
-                                      self.params.get(pre + "k_norm.weight"), positions,
-                                      self.rope_cos, self.rope_sin, cfg.num_heads,
-                                      cfg.num_kv_heads, cache.k[i], cache.v[i], slots,
-                                      cfg.rms_eps, cfg.qk_norm)
-            o = decode_attention(q, cache.k[i], cache.v[i], page_table, ctx_lens)
-            a = self._lin(o.reshape(B, -1), pre + "o_proj.weight")
+            if self.mla is not None:
+                a = self.mla.decode(i, x, positions, cache, page_table, ctx_lens, slots)
+            else:
+                qkv = self._lin(x, pre + "qkv_proj.weight")
+                q = qk_norm_rope_to_cache(qkv, self.params.get(pre + "q_norm.weight"),
+                                          self.params.get(pre + "k_norm.weight"), positions,
+                                          self.rope_cos, self.rope_sin, cfg.num_heads,
+                                          cfg.num_kv_heads, cache.k[i], cache.v[i], slots,
+                                          cfg.rms_eps, cfg.qk_norm)
+                o = decode_attention(q, cache.k[i], cache.v[i], page_table, ctx_lens)
+                a = self._lin(o.reshape(B, -1), pre + "o_proj.weight")
             x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"],
                                  cfg.rms_eps)
             rec = record.append if (record is not None and i in self.router_cfgs) else None
