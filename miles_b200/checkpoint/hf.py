@@ -21,12 +21,14 @@ from safetensors.torch import save_file
 
 from miles_b200.models.config import ModelConfig
 from miles_b200.models.transformer import Transformer
+from miles_b200.parallel.tp import tp_gather, tp_slice
 
 
 def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
-    """Yield (hf_name, tensor) for every parameter, splitting fused projections."""
+    """Yield (hf_name, tensor) for every parameter, splitting fused projections. Under tensor
+    parallelism the tensors are this rank's slices (miles_b200/parallel/tp.py: hf_shard_dim)."""
     cfg = model.cfg
-    H, D, nq, nkv = cfg.hidden_size, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads
+    H, D, nq, nkv = cfg.hidden_size, cfg.head_dim, model.nq, model.nkv
     P = model.params
     pre = "model."
     yield pre + "embed_tokens.weight", P["embed_tokens.weight"].data
@@ -34,13 +36,18 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
         L = f"layers.{i}."
         yield pre + L + "input_layernorm.weight", P[L + "input_layernorm.weight"].data
         yield pre + L + "post_attention_layernorm.weight", P[L + "post_attention_layernorm.weight"].data
-        qkv = P[L + "self_attn.qkv_proj.weight"].data
-        q, k, v = torch.split(qkv, [nq * D, nkv * D, nkv * D], 0)
-        yield pre + L + "self_attn.q_proj.weight", q
-        yield pre + L + "self_attn.k_proj.weight", k
-        yield pre + L + "self_attn.v_proj.weight", v
-        yield pre + L + "self_attn.o_proj.weight", P[L + "self_attn.o_proj.weight"].data
-        if cfg.qk_norm:
+        if cfg.kv_lora_rank:  # MLA parameters carry their HF names already
+            for n in P:
+                if n.startswith(L + "self_attn."):
+                    yield pre + n, P[n].data
+        else:
+            qkv = P[L + "self_attn.qkv_proj.weight"].data
+            q, k, v = torch.split(qkv, [nq * D, nkv * D, nkv * D], 0)
+            yield pre + L + "self_attn.q_proj.weight", q
+            yield pre + L + "self_attn.k_proj.weight", k
+            yield pre + L + "self_attn.v_proj.weight", v
+            yield pre + L + "self_attn.o_proj.weight", P[L + "self_attn.o_proj.weight"].data
+        if cfg.qk_norm and not cfg.kv_lora_rank:
             yield pre + L + "self_attn.q_norm.weight", P[L + "self_attn.q_norm.weight"].data
             yield pre + L + "self_attn.k_norm.weight", P[L + "self_attn.k_norm.weight"].data
         if cfg.layer_is_moe(i):
@@ -49,7 +56,7 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
                 yield pre + L + "mlp.gate.e_score_correction_bias", P[L + "mlp.gate.e_score_correction_bias"].data
             w1 = P[L + "mlp.experts.w1"].data
             w2 = P[L + "mlp.experts.w2"].data
-            I = cfg.moe_intermediate_size
+            I = w1.shape[1] // 2
             for e in range(w1.shape[0]):
                 yield pre + L + f"mlp.experts.{e}.gate_proj.weight", w1[e, :I]
                 yield pre + L + f"mlp.experts.{e}.up_proj.weight", w1[e, I:]
@@ -114,8 +121,13 @@ def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> No
             weight_map[n] = fn
         shard, size = {}, 0
 
+    # tensor parallel: every TP rank takes part in the gathers, TP rank 0 writes
+    writer = model.tp is None or model.tp.rank == 0
     for name, t in to_hf_tensors(model):
-        t = t.detach().to("cpu").contiguous().clone()
+        t = tp_gather(name, t.detach(), model.tp)
+        if not writer:
+            continue
+        t = t.to("cpu").contiguous().clone()
         nb = t.numel() * t.element_size()
         if size + nb > max_shard_bytes:
             flush()
@@ -163,4 +175,4 @@ def load_hf(model: Transformer, path: str) -> None:
             if name == "lm_head.weight" and cfg.tie_embeddings:
                 continue
             raise KeyError(f"{name} missing from {path}")
-        dst.copy_(get(src_name).to(dst.dtype))
+        dst.copy_(tp_slice(name, get(src_name), model.tp).to(dst.dtype))

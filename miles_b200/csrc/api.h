@@ -151,3 +151,31 @@ int mb_attn_decode_noalloc(const void* q, const void* kc, const void* vc, void* 
 #ifdef __cplusplus
 }
 #endif
+
+// Symmetric peer memory and in-kernel collectives (symm.cu) and the fused GEMM + all-reduce
+// GEMM half (gemm_sm100.cu, epilogue 5).
+#ifdef __cplusplus
+extern "C" {
+#endif
+int mb_ipc_handle_size();
+int mb_symm_malloc(long long bytes, long long* ptr_out);
+int mb_symm_free(long long ptr);
+int mb_ipc_get_handle(long long ptr, void* handle_out);
+int mb_ipc_open(const void* handle, long long* ptr_out);
+int mb_ipc_close(long long ptr);
+int mb_symm_barrier(const long long* flag_ptrs, int* my_flags, int* ctl, int rank, int world,
+                    long long timeout_ns, int* err, cudaStream_t st);
+int mb_symm_allreduce(const long long* flag_ptrs, const long long* stage_ptrs, int* my_flags,
+                      int* ctl, const void* my_stage, long long cap, const void* src, int rows,
+                      int H, int rank, int world, const void* res, const void* norm_w,
+                      float eps, void* out, void* h_out, float* rstd, long long timeout_ns,
+                      int* err, cudaStream_t st);
+int mb_symm_copy(const void* src, void* dst, long long bytes, cudaStream_t st);
+int mb_gemm_bf16_peer(const void* a, long long a_rows, long long a_cols, long long lda, bool a_mn,
+                      const void* b, long long b_rows, long long b_cols, long long ldb, bool b_mn,
+                      int M, int N, int K, const long long* peer_ptrs, int npeers, long long ldc,
+                      const int* par_word, long long par_stride, int bn, int* err,
+                      cudaStream_t stream);
+#ifdef __cplusplus
+}
+#endif

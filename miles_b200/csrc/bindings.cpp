@@ -335,7 +335,88 @@ int64_t mxfp8_quant(torch::Tensor x, torch::Tensor y, torch::Tensor sexp) {
   return mb_mxfp8_quant(P(x), x.size(0), x.size(1), P(y), P(sexp), cur_stream());
 }
 
+// ------------------------------------------------------------------ symmetric memory
+// Raw device allocations shared with peer processes through CUDA IPC handles. Pointers cross
+// the binding as int64 addresses; peer pointer lists as std::vector<int64_t>.
+int64_t symm_malloc(int64_t bytes, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  long long p = 0;
+  int rc = mb_symm_malloc(bytes, &p);
+  TORCH_CHECK(rc == 0, "symm_malloc failed");
+  return p;
+}
+int64_t symm_free(int64_t ptr) { return mb_symm_free(ptr); }
+torch::Tensor ipc_get_handle(int64_t ptr) {
+  auto t = torch::empty({mb_ipc_handle_size()}, torch::dtype(torch::kUInt8));
+  TORCH_CHECK(mb_ipc_get_handle(ptr, t.data_ptr()) == 0, "cudaIpcGetMemHandle failed");
+  return t;
+}
+int64_t ipc_open(torch::Tensor handle, int64_t device) {
+  TORCH_CHECK(handle.numel() == mb_ipc_handle_size() && handle.is_contiguous());
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  long long p = 0;
+  TORCH_CHECK(mb_ipc_open(handle.data_ptr(), &p) == 0, "cudaIpcOpenMemHandle failed");
+  return p;
+}
+int64_t ipc_close(int64_t ptr) { return mb_ipc_close(ptr); }
+// Wrap a raw device address as a tensor view (no ownership).
+torch::Tensor from_ptr(int64_t ptr, std::vector<int64_t> shape, c10::ScalarType dt, int64_t device) {
+  auto opts = torch::TensorOptions().dtype(dt).device(torch::kCUDA, device);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), shape, [](void*) {}, opts);
+}
+int64_t symm_barrier(std::vector<int64_t> flag_ptrs, torch::Tensor my_flags, torch::Tensor ctl,
+                     int64_t rank, int64_t world, int64_t timeout_ns, torch::Tensor err) {
+  return mb_symm_barrier((const long long*)flag_ptrs.data(), PT<int>(my_flags), PT<int>(ctl), rank,
+                         world, timeout_ns, PT<int>(err), cur_stream());
+}
+int64_t symm_allreduce(std::vector<int64_t> flag_ptrs, std::vector<int64_t> stage_ptrs,
+                       torch::Tensor my_flags, torch::Tensor ctl, torch::Tensor my_stage,
+                       int64_t cap, OT src, int64_t rows, int64_t H, int64_t rank, int64_t world,
+                       OT res, OT norm_w, double eps, torch::Tensor out, OT h_out, OT rstd,
+                       int64_t timeout_ns, torch::Tensor err) {
+  if (src.has_value()) { CHECK_DT(src.value(), at::kBFloat16); TORCH_CHECK(src.value().is_contiguous()); }
+  CHECK_DT(out, at::kBFloat16);
+  TORCH_CHECK(out.is_contiguous() && out.numel() >= rows * H);
+  return mb_symm_allreduce((const long long*)flag_ptrs.data(), (const long long*)stage_ptrs.data(),
+                           PT<int>(my_flags), PT<int>(ctl), P(my_stage), cap, P(src), rows, H,
+                           rank, world, P(res), P(norm_w), (float)eps, P(out), P(h_out),
+                           PT<float>(rstd), timeout_ns, PT<int>(err), cur_stream());
+}
+int64_t symm_copy(torch::Tensor src, int64_t dst_ptr, int64_t bytes) {
+  return mb_symm_copy(src.data_ptr(), reinterpret_cast<void*>(dst_ptr), bytes, cur_stream());
+}
+int64_t symm_copy_ptr(int64_t src_ptr, int64_t dst_ptr, int64_t bytes) {
+  return mb_symm_copy(reinterpret_cast<void*>(src_ptr), reinterpret_cast<void*>(dst_ptr), bytes,
+                      cur_stream());
+}
+// Fused GEMM + all-reduce, GEMM half: y = a @ b^T (b_mn: a @ b) stored into peer staging areas.
+int64_t gemm_peer(torch::Tensor a, torch::Tensor b, bool b_mn, int64_t M, int64_t N, int64_t K,
+                  std::vector<int64_t> peer_ptrs, int64_t ldc, torch::Tensor par_word,
+                  int64_t par_stride, int64_t bn, torch::Tensor err) {
+  CHECK_CUDA(a); CHECK_CUDA(b);
+  CHECK_DT(a, at::kBFloat16); CHECK_DT(b, at::kBFloat16);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2);
+  CHECK_ROWMAJOR(a); CHECK_ROWMAJOR(b);
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0 && N % 8 == 0 && ldc % 8 == 0);
+  c10::cuda::CUDAGuard g(a.device());
+  return mb_gemm_bf16_peer(a.data_ptr(), a.size(0), a.size(1), a.stride(0), false, b.data_ptr(),
+                           b.size(0), b.size(1), b.stride(0), b_mn, (int)M, (int)N, (int)K,
+                           (const long long*)peer_ptrs.data(), (int)peer_ptrs.size(), ldc,
+                           PT<int>(par_word), par_stride, (int)bn, PT<int>(err), cur_stream());
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("symm_malloc", &symm_malloc);
+  m.def("symm_free", &symm_free);
+  m.def("ipc_get_handle", &ipc_get_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("from_ptr", &from_ptr);
+  m.def("symm_barrier", &symm_barrier);
+  m.def("symm_allreduce", &symm_allreduce);
+  m.def("symm_copy", &symm_copy);
+  m.def("symm_copy_ptr", &symm_copy_ptr);
+  m.def("gemm_peer", &gemm_peer, "tcgen05 GEMM storing its tiles into peer staging areas");
   m.def("fp8_block_cast", &fp8_block_cast);
   m.def("fp8_group_cast", &fp8_group_cast);
   m.def("int4_fake_quant", &int4_fake_quant);

@@ -40,7 +40,8 @@ struct GemmParams {
   const int* group_offsets;  // modes 1,2
   int num_groups;
   int b_rows_per_group;      // mode 1: rows of B's 2-D view per group
-  int epi;                   // 0 store bf16, 1 store f32, 2 accumulate into bf16, 3 accumulate into f32
+  int epi;                   // 0 store bf16, 1 store f32, 2 accumulate into bf16, 3 accumulate into f32,
+                             // 4 SwiGLU (below), 5 store bf16 to peers (below)
   float alpha;
   int* err;                  // device error word (may be null)
   int a_stage_bytes;         // bytes TMA writes for one A stage (K-major A may load < BM rows)
@@ -54,6 +55,13 @@ struct GemmParams {
   // mode 1, optional: rows per group before padding; padding rows of the output are then not
   // written (callers that run no backward over the padded buffer)
   const int* group_counts;
+  // epi 5: store bf16 tiles into `npeers` destinations (peer ranks' staging areas of a fused
+  // GEMM + all-reduce). Destination d is peer_c[d] + (par_word[0] & 1) * par_stride, row stride
+  // ldc; the parity word is the collective's epoch counter, read after the PDL wait.
+  void* peer_c[8];
+  int npeers;
+  const int* par_word;
+  long long par_stride;
 };
 
 constexpr int BM = 128;
@@ -329,6 +337,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   } else {
     // ---------------- Epilogue (warps 2..5) ----------------
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const long long par_off =
+        p.epi == 5 ? (long long)(*reinterpret_cast<const volatile int*>(p.par_word) & 1) * p.par_stride : 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -376,8 +386,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 #pragma unroll
         for (int i = 0; i < CW; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
         const bool full_cols = col0 + CW <= p.N;
-        if (p.epi == 0 || p.epi == 2) {
-          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.C) + rbase + col0;
+        if (p.epi == 0 || p.epi == 2 || p.epi == 5) {
+         const int ndst = p.epi == 5 ? p.npeers : 1;
+         for (int d = 0; d < ndst; ++d) {
+          __nv_bfloat16* out = (p.epi == 5 ? reinterpret_cast<__nv_bfloat16*>(p.peer_c[d]) + par_off
+                                           : reinterpret_cast<__nv_bfloat16*>(p.C)) + rbase + col0;
           if (full_cols) {
             uint4* o4 = reinterpret_cast<uint4*>(out);
 #pragma unroll
@@ -405,6 +418,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
               out[i] = __float2bfloat16(w);
             }
           }
+         }
         } else {
           float* out = reinterpret_cast<float*>(p.C) + rbase + col0;
           if (full_cols) {
@@ -545,7 +559,8 @@ static int gemm_entry(const void* a, long long a_rows, long long a_cols, long lo
                       const int* group_offsets, int num_groups, int b_rows_per_group,
                       long long c_group_stride, int epi, float alpha, int bn, int swiglu_f,
                       void* c2, long long ldc2, const int* group_counts, int* err,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const long long* peer_ptrs = nullptr, int npeers = 0,
+                      const int* par_word = nullptr, long long par_stride = 0) {
   using namespace mb;
   if (a_mn && !b_mn) return -5;
   // The driver's tensor-map encoder needs a current context in the calling thread; a thread
@@ -572,6 +587,14 @@ static int gemm_entry(const void* a, long long a_rows, long long a_cols, long lo
   p.a_stage_bytes = a_mn ? BM * BK * 2 : (int)a_box_rows * BK * 2;
   p.swiglu_f = swiglu_f; p.C2 = c2; p.ldc2 = ldc2;
   p.group_counts = mode == 1 ? group_counts : nullptr;
+  p.npeers = 0; p.par_word = par_word; p.par_stride = par_stride;
+  for (int i = 0; i < 8; ++i) p.peer_c[i] = nullptr;
+  if (epi == 5) {
+    if (npeers < 1 || npeers > 8 || !par_word) return -1;
+    p.npeers = npeers;
+    for (int i = 0; i < npeers; ++i) p.peer_c[i] = reinterpret_cast<void*>(peer_ptrs[i]);
+    p.C = p.peer_c[0];
+  }
   switch (mode) {
     case 0: return dispatch_bn<0>(bn, a_mn, b_mn, ta, tb, p, stream);
     case 1: return dispatch_bn<1>(bn, a_mn, b_mn, ta, tb, p, stream);
@@ -587,7 +610,7 @@ extern "C" int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, l
                             int mode, const int* group_offsets, int num_groups,
                             int b_rows_per_group, long long c_group_stride, int epi, float alpha,
                             int bn, const int* group_counts, int* err, cudaStream_t stream) {
-  if (epi == 4) return -7;
+  if (epi == 4 || epi == 5) return -7;
   return gemm_entry(a, a_rows, a_cols, lda, a_mn, b, b_rows, b_cols, ldb, b_mn, c, ldc, M, N, K,
                     mode, group_offsets, num_groups, b_rows_per_group, c_group_stride, epi, alpha,
                     bn, 0, nullptr, 0, group_counts, err, stream);
@@ -605,4 +628,18 @@ extern "C" int mb_gemm_bf16_swiglu(const void* a, long long a_rows, long long ld
   return gemm_entry(a, a_rows, K, lda, false, b, b_rows, K, ldb, false, out, ldo, M, 2 * F, K,
                     mode, group_offsets, num_groups, 2 * F, 0, 4, 1.f, bn, F, gu, ldgu, group_counts,
                     err, stream);
+}
+
+// Fused GEMM + all-reduce, GEMM half: C = A B^T (dense, mode 0) with every bf16 output tile
+// stored straight into `npeers` peer staging areas over NVLink (epi 5); the reduce half is
+// mb_symm_allreduce with src = null (symm.cu).
+extern "C" int mb_gemm_bf16_peer(const void* a, long long a_rows, long long a_cols, long long lda,
+                                 bool a_mn, const void* b, long long b_rows, long long b_cols,
+                                 long long ldb, bool b_mn, int M, int N, int K,
+                                 const long long* peer_ptrs, int npeers, long long ldc,
+                                 const int* par_word, long long par_stride, int bn, int* err,
+                                 cudaStream_t stream) {
+  return gemm_entry(a, a_rows, a_cols, lda, a_mn, b, b_rows, b_cols, ldb, b_mn, nullptr, ldc, M, N,
+                    K, 0, nullptr, 1, 0, 0, 5, 1.f, bn, 0, nullptr, 0, nullptr, err, stream,
+                    peer_ptrs, npeers, par_word, par_stride);
 }

@@ -93,7 +93,7 @@ class RolloutEngine:
         c = self.cfg
         from miles_b200.models.transformer import kv_cache_shape
 
-        nkv, hd = kv_cache_shape(c)
+        nkv, hd = kv_cache_shape(c, self.model.tp_size)
         return (1 if c.kv_lora_rank else 2) * c.num_layers * PAGE * nkv * hd * 2
 
     def resume_memory(self):
@@ -108,7 +108,7 @@ class RolloutEngine:
             else:
                 n = 1024
         n = max(n, 2)
-        self.cache = KVCache(self.cfg, n, self.dev, self.model.dtype)
+        self.cache = KVCache(self.cfg, n, self.dev, self.model.dtype, self.model.tp_size)
         self.free_pages = list(range(n - 1, 0, -1))  # page 0 = trash page for padded rows
 
     def release_memory(self):

@@ -32,10 +32,13 @@ import torch
 import torch.nn.functional as F
 
 from miles_b200.ops.norm import rms_norm
+from miles_b200.parallel.tp import copy_to_tp, reduce_from_tp
 
 
-def mla_param_shapes(cfg, p: str):
-    H, nh = cfg.hidden_size, cfg.num_heads
+def mla_param_shapes(cfg, p: str, tp_size: int = 1):
+    """Parameter shapes of one MLA layer; tensor parallelism splits the heads (q_proj /
+    q_b_proj / kv_b_proj rows, o_proj columns) and replicates the latent projections."""
+    H, nh = cfg.hidden_size, cfg.num_heads // tp_size
     dn, dr, dv, r = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
     out = []
     if cfg.q_lora_rank:
@@ -67,6 +70,7 @@ class MLA:
         cfg = model.cfg
         self.m = model
         self.cfg = cfg
+        self.nh = cfg.num_heads // model.tp_size  # this rank's heads
         from miles_b200.ops.norm import rope_tables
 
         self.cos, self.sin = rope_tables(cfg.max_position, cfg.qk_rope_head_dim, cfg.rope_theta,
@@ -83,10 +87,10 @@ class MLA:
         p = f"layers.{i}.self_attn."
         if cfg.q_lora_rank:
             qa = rms_norm(m._lin(x, p + "q_a_proj.weight"), m.params[p + "q_a_layernorm.weight"], cfg.rms_eps)
-            q = m._lin(qa, p + "q_b_proj.weight")
+            q = m._lin(copy_to_tp(qa, m.tp), p + "q_b_proj.weight")
         else:
-            q = m._lin(x, p + "q_proj.weight")
-        q = q.view(x.shape[0], cfg.num_heads, cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
+            q = m._lin(copy_to_tp(x, m.tp), p + "q_proj.weight")
+        q = q.view(x.shape[0], self.nh, cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
         q_nope, q_pe = q.split([cfg.qk_nope_head_dim, cfg.qk_rope_head_dim], -1)
         return q_nope, _rope(q_pe, pos, self.cos, self.sin)
 
@@ -100,14 +104,21 @@ class MLA:
 
     def _expand(self, i: int, c: torch.Tensor, k_pe: torch.Tensor):
         cfg, m = self.cfg, self.m
-        kv = m._lin(c, f"layers.{i}.self_attn.kv_b_proj.weight").view(
-            c.shape[0], cfg.num_heads, cfg.qk_nope_head_dim + cfg.v_head_dim)
+        kv = m._lin(copy_to_tp(c, m.tp), f"layers.{i}.self_attn.kv_b_proj.weight").view(
+            c.shape[0], self.nh, cfg.qk_nope_head_dim + cfg.v_head_dim)
         k_nope, v = kv.split([cfg.qk_nope_head_dim, cfg.v_head_dim], -1)
-        k = torch.cat([k_nope, k_pe[:, None, :].expand(-1, cfg.num_heads, -1)], -1)
+        k = torch.cat([k_nope, copy_to_tp(k_pe, m.tp)[:, None, :].expand(-1, self.nh, -1)], -1)
         return k, v
 
     # ------------------------------------------------------------------ training / prefill
-    def attn(self, i: int, x: torch.Tensor, meta, cache=None, slots=None) -> torch.Tensor:
+    def _out(self, i: int, o: torch.Tensor, pending: bool):
+        """o_proj (row parallel): the reduced output, or (pending) what the caller reduces."""
+        name = f"layers.{i}.self_attn.o_proj.weight"
+        if pending:
+            return self.m._pending_out(o, name)
+        return reduce_from_tp(self.m._lin(o, name), self.m.tp)
+
+    def attn(self, i: int, x: torch.Tensor, meta, cache=None, slots=None, pending: bool = False):
         cfg = self.cfg
         pos = meta.positions
         q_nope, q_pe = self._q(i, x, pos)
@@ -116,7 +127,7 @@ class MLA:
             cache.k[i].index_copy_(0, slots, torch.cat([c, k_pe], -1).unsqueeze(1).to(cache.k[i].dtype))
         k, v = self._expand(i, c, k_pe)
         q = torch.cat([q_nope, q_pe], -1)
-        o = torch.empty(x.shape[0], cfg.num_heads, cfg.v_head_dim, dtype=x.dtype, device=x.device)
+        o = torch.empty(x.shape[0], self.nh, cfg.v_head_dim, dtype=x.dtype, device=x.device)
         outs = []
         cu = meta.cu_list
         for b in range(len(cu) - 1):
@@ -127,14 +138,14 @@ class MLA:
             outs.append(F.scaled_dot_product_attention(qs, ks, vs, is_causal=True, scale=self.scale)
                         [0].transpose(0, 1))
         o = torch.cat(outs, 0) if outs else o
-        return self.m._lin(o.reshape(x.shape[0], -1), f"layers.{i}.self_attn.o_proj.weight")
+        return self._out(i, o.reshape(x.shape[0], -1), pending)
 
     # ------------------------------------------------------------------ decode (absorbed)
     def decode(self, i: int, x: torch.Tensor, positions: torch.Tensor, cache, page_table: torch.Tensor,
-               ctx_lens: torch.Tensor, slots: torch.Tensor) -> torch.Tensor:
+               ctx_lens: torch.Tensor, slots: torch.Tensor, pending: bool = False):
         cfg = self.cfg
         B = x.shape[0]
-        nh, dn, dv, r = cfg.num_heads, cfg.qk_nope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
+        nh, dn, dv, r = self.nh, cfg.qk_nope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
         q_nope, q_pe = self._q(i, x, positions)
         c, k_pe = self._latent(i, x, positions)
         cache.k[i].index_copy_(0, slots, torch.cat([c, k_pe], -1).unsqueeze(1).to(cache.k[i].dtype))
@@ -152,4 +163,4 @@ class MLA:
         pr = torch.softmax(sc, -1)
         o_lat = torch.einsum("bht,btc->bhc", pr, ck)
         o = torch.einsum("bhc,hvc->bhv", o_lat, w_uv.float()).to(x.dtype)
-        return self.m._lin(o.reshape(B, -1), f"layers.{i}.self_attn.o_proj.weight")
+        return self._out(i, o.reshape(B, -1), pending)

@@ -30,6 +30,7 @@ from miles_b200.ops.attention import PAGE, VarlenMeta, decode_attention, varlen_
 from miles_b200.ops.moe import RouterCfg, moe_experts
 from miles_b200.ops.norm import (add_rms_norm, qk_norm_rope, qk_norm_rope_to_cache, rms_norm,
                                  rope_tables, swiglu)
+from miles_b200.parallel.tp import copy_to_tp, reduce_from_tp
 
 
 @dataclass
@@ -47,10 +48,15 @@ class ParamSpec:
         return n
 
 
-def param_specs(cfg: ModelConfig, ep_size: int = 1) -> list[ParamSpec]:
-    """Parameter layout; with expert parallelism each rank holds E / ep_size experts."""
+def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1) -> list[ParamSpec]:
+    """Parameter layout; with expert parallelism each rank holds E / ep_size experts, with
+    tensor parallelism each rank holds 1 / tp_size of the heads and intermediate dimensions
+    (miles_b200/parallel/tp.py)."""
     H, D = cfg.hidden_size, cfg.head_dim
-    nq, nkv = cfg.num_heads, cfg.num_kv_heads
+    t = tp_size
+    if cfg.num_heads % t or cfg.num_kv_heads % t:
+        raise ValueError(f"heads ({cfg.num_heads} q / {cfg.num_kv_heads} kv) do not split over TP {t}")
+    nq, nkv = cfg.num_heads // t, cfg.num_kv_heads // t
     specs = [ParamSpec("embed_tokens.weight", (cfg.vocab_size, H), "normal")]
     for i in range(cfg.num_layers):
         p = f"layers.{i}."
@@ -58,7 +64,7 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1) -> list[ParamSpec]:
         if cfg.kv_lora_rank:  # multi-head latent attention (models/mla.py)
             from miles_b200.models.mla import mla_param_shapes
 
-            specs += [ParamSpec(n, shp, init) for n, shp, init in mla_param_shapes(cfg, p + "self_attn.")]
+            specs += [ParamSpec(n, shp, init) for n, shp, init in mla_param_shapes(cfg, p + "self_attn.", t)]
         else:
             specs += [ParamSpec(p + "self_attn.qkv_proj.weight", ((nq + 2 * nkv) * D, H), "normal"),
                       ParamSpec(p + "self_attn.o_proj.weight", (H, nq * D), "normal")]
@@ -67,7 +73,7 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1) -> list[ParamSpec]:
             specs += [ParamSpec(p + "self_attn.q_norm.weight", (D,), "ones"),
                       ParamSpec(p + "self_attn.k_norm.weight", (D,), "ones")]
         if cfg.layer_is_moe(i):
-            E, I = cfg.num_experts, cfg.moe_intermediate_size
+            E, I = cfg.num_experts, cfg.moe_intermediate_size // t
             El = E // ep_size
             specs += [ParamSpec(p + "mlp.gate.weight", (E, H), "normal"),
                       ParamSpec(p + "mlp.experts.w1", (El, 2 * I, H), "normal"),
@@ -75,11 +81,11 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1) -> list[ParamSpec]:
             if cfg.router_score == "sigmoid":
                 specs.append(ParamSpec(p + "mlp.gate.e_score_correction_bias", (E,), "zeros"))
             if cfg.num_shared_experts:
-                Is = I * cfg.num_shared_experts
+                Is = cfg.moe_intermediate_size * cfg.num_shared_experts // t
                 specs += [ParamSpec(p + "mlp.shared_experts.gate_up_proj.weight", (2 * Is, H), "normal"),
                           ParamSpec(p + "mlp.shared_experts.down_proj.weight", (H, Is), "normal")]
         else:
-            I = cfg.intermediate_size
+            I = cfg.intermediate_size // t
             specs += [ParamSpec(p + "mlp.gate_up_proj.weight", (2 * I, H), "normal"),
                       ParamSpec(p + "mlp.down_proj.weight", (H, I), "normal")]
     specs.append(ParamSpec("norm.weight", (H,), "ones"))
@@ -102,11 +108,12 @@ def is_expert_param(name: str) -> bool:
 FLAT_ALIGN = 8192
 
 
-def kv_cache_shape(cfg: ModelConfig) -> tuple[int, int]:
-    """(heads, dim) of one cached token per layer: GQA K and V, or the MLA latent [c | k_pe]."""
+def kv_cache_shape(cfg: ModelConfig, tp_size: int = 1) -> tuple[int, int]:
+    """(heads, dim) of one cached token per layer: GQA K and V (this TP rank's KV heads), or the
+    MLA latent [c | k_pe] (replicated over TP ranks)."""
     if cfg.kv_lora_rank:
         return 1, cfg.kv_lora_rank + cfg.qk_rope_head_dim
-    return cfg.num_kv_heads, cfg.head_dim
+    return cfg.num_kv_heads // tp_size, cfg.head_dim
 
 
 class KVCache:
@@ -116,10 +123,11 @@ class KVCache:
     context are masked out of the softmax but still multiplied (by zero) in the P.V product, so
     they must hold finite values."""
 
-    def __init__(self, cfg: ModelConfig, num_pages: int, device, dtype=torch.bfloat16):
+    def __init__(self, cfg: ModelConfig, num_pages: int, device, dtype=torch.bfloat16,
+                 tp_size: int = 1):
         self.num_pages = num_pages
         slots = num_pages * PAGE
-        nkv, hd = kv_cache_shape(cfg)
+        nkv, hd = kv_cache_shape(cfg, tp_size)
         self.k = [torch.zeros(slots, nkv, hd, dtype=dtype, device=device)
                   for _ in range(cfg.num_layers)]
         # MLA caches only the latent (+ rotary key) in `k`
@@ -132,11 +140,22 @@ class KVCache:
 
 class Transformer(torch.nn.Module):
     def __init__(self, cfg: ModelConfig, device="cuda", dtype=torch.bfloat16, seed: int = 0,
-                 init_std: float = 0.02, materialize: bool = True, ep_group=None):
+                 init_std: float = 0.02, materialize: bool = True, ep_group=None, tp_group=None,
+                 tp_backend: str = "auto", tp_cap_rows: int = 16384):
         super().__init__()
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype
+        self.tp = None
+        if tp_group is not None:
+            from miles_b200.parallel.tp import TPContext
+
+            self.tp = TPContext(tp_group, tp_backend, cfg.hidden_size, tp_cap_rows)
+            if self.tp.size == 1:
+                self.tp = None
+        self.tp_size = self.tp.size if self.tp else 1
+        self.nq = cfg.num_heads // self.tp_size      # this rank's query heads
+        self.nkv = cfg.num_kv_heads // self.tp_size  # this rank's KV heads
         self.ep = None
         if ep_group is not None and cfg.is_moe:
             from miles_b200.parallel.ep import EPContext
@@ -144,7 +163,9 @@ class Transformer(torch.nn.Module):
             self.ep = EPContext(ep_group, cfg.num_experts)
             if self.ep.size == 1:
                 self.ep = None
-        self.specs = param_specs(cfg, self.ep.size if self.ep else 1)
+        if self.ep is not None and self.tp is not None:
+            raise ValueError("expert parallelism combined with tensor parallelism is not supported")
+        self.specs = param_specs(cfg, self.ep.size if self.ep else 1, self.tp_size)
         total = self.specs[-1].offset + self.specs[-1].numel
         self.numel = total
         ex = [sp.offset for sp in self.specs if is_expert_param(sp.name)]
@@ -222,15 +243,19 @@ class Transformer(torch.nn.Module):
         if self.mla is not None:
             return self.mla.attn(i, x, meta)
         pre = f"layers.{i}.self_attn."
-        qkv = self._lin(x, pre + "qkv_proj.weight")
+        qkv = self._lin(copy_to_tp(x, self.tp), pre + "qkv_proj.weight")
         q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
                                self.params.get(pre + "k_norm.weight"), meta.positions,
-                               self.rope_cos, self.rope_sin, cfg.num_heads, cfg.num_kv_heads,
+                               self.rope_cos, self.rope_sin, self.nq, self.nkv,
                                cfg.rms_eps, cfg.qk_norm)
         o = varlen_attention(q, k, v, meta)
-        return self._lin(o.reshape(x.shape[0], -1), pre + "o_proj.weight")
+        return reduce_from_tp(self._lin(o.reshape(x.shape[0], -1), pre + "o_proj.weight"), self.tp)
 
     def _mlp(self, i: int, x: torch.Tensor, replay=None, record=None) -> torch.Tensor:
+        return reduce_from_tp(self._mlp_partial(i, copy_to_tp(x, self.tp), replay, record), self.tp)
+
+    def _mlp_partial(self, i: int, x: torch.Tensor, replay=None, record=None) -> torch.Tensor:
+        """MLP / MoE output before the tensor-parallel all-reduce (the full output at TP 1)."""
         pre = f"layers.{i}.mlp."
         if i in self.router_cfgs:
             if self.ep is not None:
@@ -301,6 +326,45 @@ class Transformer(torch.nn.Module):
         return y
 
     # -------------------------------------------------------------------------------- inference
+    # Under tensor parallelism the output of every row-parallel projection is a partial sum;
+    # the inference paths carry it as a "pending" value and reduce it together with the
+    # residual add + RMSNorm that follows. With the symmetric-memory backend that is ONE fused
+    # step: the row-parallel GEMM stores its tiles into the peers' staging over NVLink and the
+    # reduce kernel does sum + residual + norm (dense layers), or the reduce kernel pushes a
+    # MoE layer's combined output and does the same.
+    def _tp_fused(self, rows: int) -> bool:
+        return (self.tp is not None and self.tp.backend == "symm" and self.device.type == "cuda"
+                and self.lora is None and rows <= self.tp.cap_rows)
+
+    def _add_norm(self, pending, r, w):
+        """(x, r') = add_rms_norm(allreduce(pending), r, w); pending is a tensor (partial or
+        full output) or ("gemm", a, W) meaning a @ W^T still to be computed."""
+        eps = self.cfg.rms_eps
+        if isinstance(pending, tuple):
+            _, a, W = pending
+            if self._tp_fused(a.shape[0]):
+                return self.tp.symm().gemm_all_reduce(a, W, res=r, norm_w=w, eps=eps)
+            pending = G.linear(a, W)
+        if self.tp is not None:
+            if self._tp_fused(pending.shape[0]):
+                return self.tp.symm().all_reduce_add_norm(pending, r, w, eps)
+            pending = self.tp.all_reduce(pending)
+        if r is None:
+            return rms_norm(pending, w, eps), pending
+        return add_rms_norm(pending, r, w, eps)
+
+    def _pending_out(self, a: torch.Tensor, name: str):
+        """Row-parallel projection a @ W^T, deferred when it can fuse with its all-reduce."""
+        if self._tp_fused(a.shape[0]):
+            return ("gemm", a, self.params[name])
+        return self._lin(a, name)
+
+    def _pending_mlp(self, i: int, x: torch.Tensor):
+        pre = f"layers.{i}.mlp."
+        if i in self.router_cfgs or self.tp is None:
+            return self._mlp_partial(i, x)
+        return self._pending_out(self._lin_swiglu(x, pre + "gate_up_proj.weight"), pre + "down_proj.weight")
+
     @torch.no_grad()
     def forward_prefill(self, tokens: torch.Tensor, meta: VarlenMeta, cache: KVCache,
                         slots: torch.Tensor, record: list | None = None) -> torch.Tensor:
@@ -308,28 +372,28 @@ class Transformer(torch.nn.Module):
         Returns the final hidden of every token [T, H]."""
         cfg = self.cfg
         r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
-        m = None
+        pend = None
         for i in range(cfg.num_layers):
             ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
-            x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
+            x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if pend is None else self._add_norm(pend, r, ln1)
             pre = f"layers.{i}.self_attn."
+            post = self.params[f"layers.{i}.post_attention_layernorm.weight"]
             if self.mla is not None:
-                a = self.mla.attn(i, x, meta, cache, slots)
+                x2, r = self._add_norm(self.mla.attn(i, x, meta, cache, slots, pending=True), r, post)
             else:
                 qkv = self._lin(x, pre + "qkv_proj.weight")
                 q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
                                        self.params.get(pre + "k_norm.weight"), meta.positions,
-                                       self.rope_cos, self.rope_sin, cfg.num_heads, cfg.num_kv_heads,
+                                       self.rope_cos, self.rope_sin, self.nq, self.nkv,
                                        cfg.rms_eps, cfg.qk_norm)
                 cache.k[i].index_copy_(0, slots, k)
                 cache.v[i].index_copy_(0, slots, v)
                 o = varlen_attention(q, k, v, meta)
-                a = self._lin(o.reshape(x.shape[0], -1), pre + "o_proj.weight")
-            x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"],
-                                 cfg.rms_eps)
+                x2, r = self._add_norm(self._pending_out(o.reshape(x.shape[0], -1), pre + "o_proj.weight"),
+                                       r, post)
             rec = record.append if (record is not None and i in self.router_cfgs) else None
-            m = self._mlp(i, x2, record=rec)
-        y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
+            pend = self._mlp_partial(i, x2, record=rec) if rec is not None else self._pending_mlp(i, x2)
+        y, _ = self._add_norm(pend, r, self.params["norm.weight"])
         return y
 
     @torch.no_grad()
@@ -341,27 +405,27 @@ class Transformer(torch.nn.Module):
         cfg = self.cfg
         B = tokens.shape[0]
         r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
-        m = None
+        pend = None
         for i in range(cfg.num_layers):
             ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
-            x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
+            x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if pend is None else self._add_norm(pend, r, ln1)
             pre = f"layers.{i}.self_attn."
+            post = self.params[f"layers.{i}.post_attention_layernorm.weight"]
             if self.mla is not None:
-                a = self.mla.decode(i, x, positions, cache, page_table, ctx_lens, slots)
+                a = self.mla.decode(i, x, positions, cache, page_table, ctx_lens, slots, pending=True)
             else:
                 qkv = self._lin(x, pre + "qkv_proj.weight")
                 q = qk_norm_rope_to_cache(qkv, self.params.get(pre + "q_norm.weight"),
                                           self.params.get(pre + "k_norm.weight"), positions,
-                                          self.rope_cos, self.rope_sin, cfg.num_heads,
-                                          cfg.num_kv_heads, cache.k[i], cache.v[i], slots,
+                                          self.rope_cos, self.rope_sin, self.nq,
+                                          self.nkv, cache.k[i], cache.v[i], slots,
                                           cfg.rms_eps, cfg.qk_norm)
                 o = decode_attention(q, cache.k[i], cache.v[i], page_table, ctx_lens)
-                a = self._lin(o.reshape(B, -1), pre + "o_proj.weight")
-            x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"],
-                                 cfg.rms_eps)
+                a = self._pending_out(o.reshape(B, -1), pre + "o_proj.weight")
+            x2, r = self._add_norm(a, r, post)
             rec = record.append if (record is not None and i in self.router_cfgs) else None
-            m = self._mlp(i, x2, record=rec)
-        y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
+            pend = self._mlp_partial(i, x2, record=rec) if rec is not None else self._pending_mlp(i, x2)
+        y, _ = self._add_norm(pend, r, self.params["norm.weight"])
         return y
 
     def flops_per_token(self, ctx: float) -> float:

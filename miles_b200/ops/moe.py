@@ -69,9 +69,11 @@ def moe_ref(x, router_w, w1, w2, cfg: RouterCfg, bias=None, replay_idx=None):
         tok, slot = (idx == e).nonzero(as_tuple=True)
         if tok.numel() == 0:
             continue
-        gu = (x[tok].float() @ w1[e].float().t()).to(torch.bfloat16)
+        # intermediate roundings follow the activation dtype (bf16 on the kernel path)
+        rd = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
+        gu = (x[tok].float() @ w1[e].float().t()).to(rd)
         a = swiglu_ref(gu)
-        o = (a.float() @ w2[e].float().t()).to(torch.bfloat16)
+        o = (a.float() @ w2[e].float().t()).to(rd)
         y.index_add_(0, tok, w[tok, slot][:, None] * o.float())
     return y.to(x.dtype), idx
 

@@ -1,0 +1,177 @@
+"""Tensor parallelism (Megatron-style column / row parallel layers) for the transformer.
+
+Layout over a TP group of size t (rank r holds the r-th contiguous slice):
+  * attention: query heads and KV heads are split t ways (qkv_proj rows, o_proj columns);
+    MLA splits its heads the same way (q_proj / q_b_proj and kv_b_proj rows, o_proj columns),
+    the latent projections (kv_a_proj_with_mqa, q_a_proj) stay replicated
+  * dense MLP and shared experts: the intermediate dimension is split (gate_up rows, down
+    columns); routed experts split their intermediate dimension the same way
+  * embeddings, norms, the router and the LM head are replicated
+A column-parallel projection takes `copy_to_tp(x)` (identity forward, all-reduce of the input
+gradient backward); a row-parallel projection is followed by `reduce_from_tp` (all-reduce
+forward, identity backward). Replicated parameters that only see this rank's heads or
+intermediate slice (QK-norm weights; the router under a split MoE) get partial gradients,
+which `tp_partial_param_names` lists and the trainer all-reduces over the TP group.
+
+All-reduce backends:
+  * "symm" (CUDA): the in-kernel one-shot all-reduce over symmetric peer memory
+    (parallel/symm.py) — rank-ordered fp32 sums, so the rollout engine (which fuses the
+    decode all-reduce into the row-parallel GEMM and the following residual + RMSNorm) and the
+    trainer produce bitwise identical activations;
+  * "nccl" (or any torch.distributed backend, e.g. gloo on CPU): dist.all_reduce.
+
+Reference: Megatron tensor / sequence parallel layers used through megatron_utils
+(--tensor-model-parallel-size; arguments.py Megatron defaults), SGLang TP engines
+(--rollout-num-gpus-per-engine).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+class TPContext:
+    def __init__(self, group, backend: str = "auto", hidden: int = 0, cap_rows: int = 16384):
+        self.group = group
+        self.size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if backend == "auto":
+            backend = "symm" if dist.get_backend(group) == "nccl" else "torch"
+        self.backend = backend
+        self.hidden = hidden
+        self.cap_rows = cap_rows
+        self._symm = None
+
+    def symm(self):
+        if self._symm is None:
+            from miles_b200.parallel.symm import SymmComm
+
+            self._symm = SymmComm(self.group, hidden=self.hidden, cap_rows=self.cap_rows)
+        return self._symm
+
+    def use_symm(self, x: torch.Tensor) -> bool:
+        return (self.backend == "symm" and x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2
+                and x.shape[1] == self.hidden and x.shape[0] <= self.cap_rows)
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.size == 1:
+            return x
+        if self.use_symm(x):
+            return self.symm().all_reduce(x)
+        y = x.contiguous().clone()
+        dist.all_reduce(y, group=self.group)
+        return y
+
+    def shard(self, n: int) -> tuple[int, int]:
+        """[lo, hi) of this rank's slice of a dimension of size n."""
+        if n % self.size:
+            raise ValueError(f"dimension {n} does not split over tensor-parallel size {self.size}")
+        s = n // self.size
+        return self.rank * s, (self.rank + 1) * s
+
+
+class _CopyToTP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, tp):
+        ctx.tp = tp
+        return x
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.tp.all_reduce(g.contiguous()), None
+
+
+class _ReduceFromTP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, tp):
+        return tp.all_reduce(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, None
+
+
+def copy_to_tp(x: torch.Tensor, tp: TPContext | None) -> torch.Tensor:
+    if tp is None or tp.size == 1:
+        return x
+    return _CopyToTP.apply(x, tp) if torch.is_grad_enabled() and x.requires_grad else x
+
+
+def reduce_from_tp(x: torch.Tensor, tp: TPContext | None) -> torch.Tensor:
+    if tp is None or tp.size == 1:
+        return x
+    if torch.is_grad_enabled() and x.requires_grad:
+        return _ReduceFromTP.apply(x, tp)
+    return tp.all_reduce(x)
+
+
+# ------------------------------------------------------------------ parameter layout
+_COL = ("self_attn.q_proj.weight", "self_attn.q_b_proj.weight", "self_attn.kv_b_proj.weight",
+        "mlp.gate_proj.weight", "mlp.up_proj.weight", "shared_experts.gate_proj.weight",
+        "shared_experts.up_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight")
+_ROW = ("self_attn.o_proj.weight", "mlp.down_proj.weight", "shared_experts.down_proj.weight")
+
+
+def hf_shard_dim(hf_name: str) -> int | None:
+    """Dimension along which an HF tensor is split over TP ranks (None: replicated)."""
+    if ".experts." in hf_name and "shared_experts" not in hf_name:
+        if hf_name.endswith(("gate_proj.weight", "up_proj.weight")):
+            return 0
+        if hf_name.endswith("down_proj.weight"):
+            return 1
+        return None
+    if hf_name.endswith(_COL):
+        return 0
+    if hf_name.endswith(_ROW):
+        return 1
+    return None
+
+
+def tp_slice(hf_name: str, full: torch.Tensor, tp: TPContext | None) -> torch.Tensor:
+    if tp is None or tp.size == 1:
+        return full
+    d = hf_shard_dim(hf_name)
+    if d is None:
+        return full
+    lo, hi = tp.shard(full.shape[d])
+    return full.narrow(d, lo, hi - lo)
+
+
+def tp_partial_param_names(model) -> list[str]:
+    """Replicated parameters whose gradient on one TP rank covers only its own slice."""
+    if model.tp is None or model.tp.size == 1:
+        return []
+    out = []
+    for name in model.params:
+        if name.endswith(("self_attn.q_norm.weight", "self_attn.k_norm.weight")):
+            out.append(name)
+        elif name.endswith("mlp.gate.weight"):
+            out.append(name)  # router logits feed a combine of partial expert outputs
+    return out
+
+
+def tp_gather(hf_name: str, local: torch.Tensor, tp: TPContext | None) -> torch.Tensor:
+    """Full tensor from every rank's slice (collective over the TP group)."""
+    if tp is None or tp.size == 1:
+        return local
+    d = hf_shard_dim(hf_name)
+    if d is None:
+        return local
+    parts = [torch.empty_like(local) for _ in range(tp.size)]
+    dist.all_gather(parts, local.contiguous(), group=tp.group)
+    return torch.cat(parts, d)
+
+
+_SHARDED_INTERNAL = ("self_attn.qkv_proj.weight", "self_attn.o_proj.weight", "mlp.gate_up_proj.weight",
+                     "mlp.down_proj.weight", "mlp.experts.w1", "mlp.experts.w2",
+                     "shared_experts.gate_up_proj.weight", "shared_experts.down_proj.weight",
+                     "self_attn.q_proj.weight", "self_attn.q_b_proj.weight",
+                     "self_attn.kv_b_proj.weight")
+
+
+def tp_replicated_ranges(model) -> list[tuple[int, int]]:
+    """Flat-buffer ranges of the parameters every TP rank holds in full."""
+    if model.tp is None or model.tp.size == 1:
+        return []
+    return [(s.offset, s.offset + s.numel) for s in model.specs
+            if not s.name.endswith(_SHARDED_INTERNAL)]

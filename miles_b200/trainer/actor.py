@@ -28,6 +28,7 @@ import torch.distributed as dist
 
 from miles_b200.models.transformer import Transformer
 from miles_b200.ops.gemm import clear_main_grads, register_main_grad
+from miles_b200.parallel.tp import tp_partial_param_names, tp_replicated_ranges
 from miles_b200.ops.attention import VarlenMeta
 from miles_b200.ops.logprob import lm_head_logprob
 from miles_b200.ops.rl import METRIC_NAMES, PolicyLossCfg, policy_loss
@@ -131,7 +132,9 @@ class Actor:
             self.opt = FlatAdam(self.model.flat, self.grad_flat, lr=self.cfg.lr,
                                 betas=self.cfg.betas, weight_decay=self.cfg.weight_decay,
                                 clip_grad=self.cfg.clip_grad, placement=self.cfg.optimizer_placement,
-                                dp_group=self.dp_group if self._sharded() else None)
+                                dp_group=self.dp_group if self._sharded() else None,
+                                tp_group=self.model.tp.group if self.model.tp else None,
+                                tp_repl_ranges=tp_replicated_ranges(self.model))
 
     def _sharded(self) -> bool:
         """Optimizer sharded over the data-parallel group (ZeRO-1): every rank holds the whole
@@ -255,6 +258,9 @@ class Actor:
                 p.main_grad.add_(p.grad.to(p.main_grad.dtype))
                 p.grad = None
         t1 = time.perf_counter()
+        if model.tp is not None:
+            for name in tp_partial_param_names(model):
+                dist.all_reduce(model.params[name].main_grad, group=model.tp.group)
         if (self.dp_group is not None and dist.get_world_size(self.dp_group) > 1
                 and not self._sharded() and model.lora is None):
             self._reduce_grads()
