@@ -54,7 +54,16 @@ def megatron_name(name: str, cfg) -> str:
     L = f"decoder.layers.{i}."
     moe = cfg.layer_is_moe(i)
     table = {
-        "input_layernorm.weight": "self_attention.linear_qkv.layer_norm_weight",
+        "input_layernorm.weight": ("input_layernorm.weight" if cfg.kv_lora_rank
+                                   else "self_attention.linear_qkv.layer_norm_weight"),
+        # multi-head latent attention (Megatron MLASelfAttention names)
+        "self_attn.q_proj.weight": "self_attention.linear_q_proj.weight",
+        "self_attn.q_a_proj.weight": "self_attention.linear_q_down_proj.weight",
+        "self_attn.q_a_layernorm.weight": "self_attention.linear_q_up_proj.layer_norm_weight",
+        "self_attn.q_b_proj.weight": "self_attention.linear_q_up_proj.weight",
+        "self_attn.kv_a_proj_with_mqa.weight": "self_attention.linear_kv_down_proj.weight",
+        "self_attn.kv_a_layernorm.weight": "self_attention.linear_kv_up_proj.layer_norm_weight",
+        "self_attn.kv_b_proj.weight": "self_attention.linear_kv_up_proj.weight",
         "self_attn.qkv_proj.weight": "self_attention.linear_qkv.weight",
         "self_attn.o_proj.weight": "self_attention.linear_proj.weight",
         "self_attn.q_norm.weight": "self_attention.q_layernorm.weight",
@@ -72,14 +81,27 @@ def megatron_name(name: str, cfg) -> str:
     return L + table[rest]
 
 
+def _key(model: Transformer, name: str) -> str:
+    """Checkpoint key; under tensor parallelism a sharded parameter is stored per TP rank
+    (suffix ``.tp<rank>of<size>``), so a torch_dist checkpoint reloads at the same TP size
+    (the HF path reshards between sizes)."""
+    k = megatron_name(name, model.cfg)
+    if model.tp is not None:
+        from miles_b200.parallel.tp import is_tp_sharded
+
+        if is_tp_sharded(name):
+            k += f".tp{model.tp.rank}of{model.tp.size}"
+    return k
+
+
 def model_state_dict(model: Transformer) -> dict[str, torch.Tensor]:
     cfg = model.cfg
     sd = {}
     for name, p in model.params.items():
         t = p.data
         if name.endswith("qkv_proj.weight"):
-            t = _qkv_to_megatron(t, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim)
-        sd[megatron_name(name, cfg)] = t
+            t = _qkv_to_megatron(t, model.nq, model.nkv, cfg.head_dim)
+        sd[_key(model, name)] = t
     return sd
 
 
@@ -177,9 +199,9 @@ def load_checkpoint(load: str, model: Transformer, optimizer=None, load_optim: b
         sd["optimizer"] = _optim_state(optimizer)  # views of the live state: loaded in place
     dcp.load(sd, checkpoint_id=d, process_group=process_group)
     for name, p in model.params.items():
-        t = sd["model"][megatron_name(name, cfg)]
+        t = sd["model"][_key(model, name)]
         if name.endswith("qkv_proj.weight"):
-            t = _qkv_from_megatron(t, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim)
+            t = _qkv_from_megatron(t, model.nq, model.nkv, cfg.head_dim)
         p.data.copy_(t)
     common = torch.load(os.path.join(d, "common.pt"), weights_only=False) if os.path.exists(os.path.join(d, "common.pt")) else {}
     if optimizer is not None and load_optim:

@@ -29,6 +29,18 @@ class ProcessContext:
     device: torch.device
     dp_group: object = None
     gloo_group: object = None
+    tp_group: object = None        # tensor-parallel group (consecutive ranks)
+    ep_group: object = None        # expert-parallel group (consecutive ranks)
+    expert_dp_group: object = None  # ranks holding the same experts
+    dp_rank: int = 0
+    dp_size: int = 1
+
+
+def _groups(world: int, size: int):
+    """(consecutive groups of `size`, strided groups across them) as rank lists."""
+    blocks = [list(range(b, b + size)) for b in range(0, world, size)]
+    strided = [list(range(i, world, size)) for i in range(size)]
+    return blocks, strided
 
 
 def init_distributed(args) -> ProcessContext:
@@ -48,10 +60,38 @@ def init_distributed(args) -> ProcessContext:
         backend = "nccl" if use_cuda else "gloo"
         kw = {"device_id": dev} if use_cuda else {}
         dist.init_process_group(backend, timeout=datetime.timedelta(minutes=args.distributed_timeout_minutes), **kw)
+    ctx = ProcessContext(rank, world, local, dev)
     if world > 1:
         dp = dist.group.WORLD
         gloo = dist.new_group(backend="gloo") if use_cuda else dp
-    return ProcessContext(rank, world, local, dev, dp, gloo)
+        ctx.dp_group, ctx.gloo_group, ctx.dp_rank, ctx.dp_size = dp, gloo, rank, world
+        tp = getattr(args, "tensor_model_parallel_size", 1)
+        ep = getattr(args, "expert_model_parallel_size", 1)
+        if tp > 1 and ep > 1:
+            raise ValueError("tensor and expert parallelism cannot be combined")
+        if tp > 1:
+            # TP groups are consecutive ranks (one NVSwitch domain); DP across them
+            blocks, strided = _groups(world, tp)
+            for ranks in blocks:
+                g = dist.new_group(ranks)
+                if rank in ranks:
+                    ctx.tp_group = g
+            for ranks in strided:
+                g = dist.new_group(ranks)
+                if rank in ranks:
+                    ctx.dp_group = g
+            ctx.dp_rank, ctx.dp_size = rank // tp, world // tp
+        if ep > 1:
+            blocks, strided = _groups(world, ep)
+            for ranks in blocks:
+                g = dist.new_group(ranks)
+                if rank in ranks:
+                    ctx.ep_group = g
+            for ranks in strided:
+                g = dist.new_group(ranks)
+                if rank in ranks:
+                    ctx.expert_dp_group = g
+    return ctx
 
 
 def model_config(args) -> ModelConfig:
@@ -76,7 +116,9 @@ def load_tokenizer(args):
 def build_model(args, ctx: ProcessContext) -> Transformer:
     cfg = model_config(args)
     dtype = torch.bfloat16 if ctx.device.type == "cuda" else torch.float32
-    model = Transformer(cfg, device=ctx.device, dtype=dtype, seed=args.seed)
+    model = Transformer(cfg, device=ctx.device, dtype=dtype, seed=args.seed, tp_group=ctx.tp_group,
+                        ep_group=ctx.ep_group,
+                        tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
     loaded = False
     if args.load:
         from miles_b200.checkpoint.torch_dist import is_torch_dist
@@ -124,7 +166,9 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                       grad_dtype=torch.float32 if (ctx.device.type != "cuda" or args.accumulate_allreduce_grads_in_fp32) else torch.bfloat16,
                       optimizer_placement=placement,
                       logprob_chunk=args.log_probs_chunk_size if args.log_probs_chunk_size > 0 else 4096)
-    return Actor(model, cfg, dp_group=ctx.dp_group)
+    actor = Actor(model, cfg, dp_group=ctx.dp_group)
+    actor.expert_dp_group = ctx.expert_dp_group
+    return actor
 
 
 def build_engine(args, model: Transformer, ctx: ProcessContext) -> RolloutEngine:

@@ -169,6 +169,11 @@ _SHARDED_INTERNAL = ("self_attn.qkv_proj.weight", "self_attn.o_proj.weight", "ml
                      "self_attn.kv_b_proj.weight")
 
 
+def is_tp_sharded(name: str) -> bool:
+    """True for internal parameter names that tensor parallelism splits."""
+    return name.endswith(_SHARDED_INTERNAL)
+
+
 def tp_replicated_ranges(model) -> list[tuple[int, int]]:
     """Flat-buffer ranges of the parameters every TP rank holds in full."""
     if model.tp is None or model.tp.size == 1:

@@ -56,6 +56,24 @@ def test_train_gloo_world2(tmp_path):
     assert r.returncode == 0, r.stderr[-3000:]
 
 
+@pytest.mark.timeout(900)
+def test_train_tp2(tmp_path):
+    """Tensor parallel 2 (both ranks one TP group): two GRPO steps with torch_dist saves, then a
+    resume from the TP-sharded checkpoint and an HF export gathered over the TP group."""
+    _dataset(tmp_path / "d.jsonl")
+    env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
+    base = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+            "--master-addr", "127.0.0.1", "--master-port", "29627", os.path.join(ROOT, "train.py")]
+    tp = ["--actor-num-gpus-per-node", "2", "--tensor-model-parallel-size", "2"]
+    r = subprocess.run(base + _argv(tmp_path, tp), env=env, capture_output=True, text=True, timeout=400)
+    assert r.returncode == 0, r.stderr[-3000:]
+    r = subprocess.run(base + _argv(tmp_path, tp + ["--load", str(tmp_path / "ckpt"), "--num-rollout", "3",
+                                                    "--save-hf", str(tmp_path / "hf_{rollout_id}")]),
+                       env=env, capture_output=True, text=True, timeout=400)
+    assert r.returncode == 0, r.stderr[-3000:]
+    assert os.path.exists(tmp_path / "hf_2" / "model.safetensors.index.json")
+
+
 def _async_run(tmp_path, extra, port):
     _dataset(tmp_path / "d.jsonl")
     env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=ROOT, OMP_NUM_THREADS="2")

@@ -46,7 +46,9 @@ def setup(args):
     client = LocalEngineClient(engine, tok)
     ds_cls = load_function(args.data_source_path)
     data_source = ds_cls(args, tok)
-    manager = RolloutManager(args, data_source, client, tok, ctx.rank, ctx.world)
+    # prompts are sharded over data-parallel replicas: the ranks of one tensor-parallel group
+    # generate (and train on) the same samples
+    manager = RolloutManager(args, data_source, client, tok, ctx.dp_rank, ctx.dp_size)
     trainer = TrainActor(args, actor, ctx.dp_group, critic=build_critic(args, ctx))
     start = 0
     if args.load and is_torch_dist(args.load):
@@ -88,7 +90,7 @@ def train(args):
             if args.save_hf:
                 from miles_b200.checkpoint.hf import save_hf
 
-                if ctx.rank == 0:
+                if ctx.dp_rank == 0:  # the TP group of replica 0 (save_hf gathers over it)
                     save_hf(model, args.save_hf.format(rollout_id=rollout_id))
         # colocated refit: the engine reads the trainer's parameter buffer in place
         m["rollout/weight_version"] = model.weight_version
