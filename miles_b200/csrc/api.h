@@ -171,6 +171,8 @@ int mb_symm_allreduce(const long long* flag_ptrs, const long long* stage_ptrs, i
                       float eps, void* out, void* h_out, float* rstd, long long timeout_ns,
                       int* err, cudaStream_t st);
 int mb_symm_copy(const void* src, void* dst, long long bytes, cudaStream_t st);
+int mb_fp8_block_dequant(const void* q, const float* s, int M, int N, int bm, int bn, void* out,
+                         cudaStream_t st);
 int mb_gemm_bf16_peer(const void* a, long long a_rows, long long a_cols, long long lda, bool a_mn,
                       const void* b, long long b_rows, long long b_cols, long long ldb, bool b_mn,
                       int M, int N, int K, const long long* peer_ptrs, int npeers, long long ldc,

@@ -389,6 +389,21 @@ int64_t symm_copy_ptr(int64_t src_ptr, int64_t dst_ptr, int64_t bytes) {
   return mb_symm_copy(reinterpret_cast<void*>(src_ptr), reinterpret_cast<void*>(dst_ptr), bytes,
                       cur_stream());
 }
+// Refit: quantise a local bf16 weight into (possibly peer) fp8 + scale buffers, and dequantise
+// from (possibly peer) buffers into a local bf16 weight.
+int64_t fp8_block_cast_ptr(torch::Tensor x, int64_t bm, int64_t bn, int64_t y_ptr, int64_t s_ptr,
+                           bool ue8m0) {
+  TORCH_CHECK(x.is_contiguous() && x.dim() == 2 && x.scalar_type() == at::kBFloat16);
+  return mb_fp8_block_cast(P(x), x.size(0), x.size(1), bm, bn, reinterpret_cast<void*>(y_ptr),
+                           reinterpret_cast<float*>(s_ptr), ue8m0, cur_stream());
+}
+int64_t fp8_block_dequant_ptr(int64_t q_ptr, int64_t s_ptr, int64_t bm, int64_t bn,
+                              torch::Tensor out) {
+  TORCH_CHECK(out.is_contiguous() && out.dim() == 2 && out.scalar_type() == at::kBFloat16);
+  return mb_fp8_block_dequant(reinterpret_cast<void*>(q_ptr), reinterpret_cast<float*>(s_ptr),
+                              out.size(0), out.size(1), bm, bn, P(out), cur_stream());
+}
+
 // Fused GEMM + all-reduce, GEMM half: y = a @ b^T (b_mn: a @ b) stored into peer staging areas.
 int64_t gemm_peer(torch::Tensor a, torch::Tensor b, bool b_mn, int64_t M, int64_t N, int64_t K,
                   std::vector<int64_t> peer_ptrs, int64_t ldc, torch::Tensor par_word,
@@ -416,6 +431,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_allreduce", &symm_allreduce);
   m.def("symm_copy", &symm_copy);
   m.def("symm_copy_ptr", &symm_copy_ptr);
+  m.def("fp8_block_cast_ptr", &fp8_block_cast_ptr);
+  m.def("fp8_block_dequant_ptr", &fp8_block_dequant_ptr);
   m.def("gemm_peer", &gemm_peer, "tcgen05 GEMM storing its tiles into peer staging areas");
   m.def("fp8_block_cast", &fp8_block_cast);
   m.def("fp8_group_cast", &fp8_group_cast);

@@ -32,6 +32,7 @@
 // broadcast in update_weight/broadcast.py.
 #include "common.cuh"
 #include <cstring>
+#include <cuda_fp8.h>
 
 namespace mb {
 
@@ -286,6 +287,31 @@ __global__ void symm_copy_kernel(const uint4* src, uint4* dst, long long n) {
     dst[i] = src[i];
 }
 
+// 128x128-block fp8 (e4m3) -> bf16 with per-block fp32 scales; q and s may live in a peer's
+// memory (refit: the trainer quantised straight into the owner engine's staging). 16 elements
+// (one 16-byte fp8 load, two 16-byte bf16 stores) per thread step; N % 16 == 0.
+__global__ void fp8_block_dequant_kernel(const uint8_t* q, const float* s, int M, int N, int bm,
+                                         int bn, __nv_bfloat16* out) {
+  pdl_trigger();
+  pdl_wait();
+  const int gn = (N + bn - 1) / bn;
+  const long long n16 = (long long)M * N / 16;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long e = i * 16;
+    const int row = (int)(e / N), col = (int)(e % N);
+    const float sc = s[(long long)(row / bm) * gn + col / bn];
+    const uint4 v = ld_volatile_v4(q + e);
+    const __nv_fp8_e4m3* f = reinterpret_cast<const __nv_fp8_e4m3*>(&v);
+    uint4 o[2];
+    __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(o);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) ob[k] = __float2bfloat16(float(f[k]) * sc);
+    *reinterpret_cast<uint4*>(out + e) = o[0];
+    *reinterpret_cast<uint4*>(out + e + 8) = o[1];
+  }
+}
+
 }  // namespace mb
 
 using namespace mb;
@@ -397,6 +423,19 @@ int mb_symm_copy(const void* src, void* dst, long long bytes, cudaStream_t st) {
   long long g = (n + 255) / 256;
   if (g > 148 * 8) g = 148 * 8;
   mb_launch(symm_copy_kernel, (int)g, 256, 0, st, (const uint4*)src, (uint4*)dst, n);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+int mb_fp8_block_dequant(const void* q, const float* s, int M, int N, int bm, int bn, void* out,
+                         cudaStream_t st) {
+  if (N % 16 || bn % 16 || (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) % 16)
+    return -1;
+  if (M == 0) return 0;
+  const long long n16 = (long long)M * N / 16;
+  long long g = (n16 + 255) / 256;
+  if (g > 148 * 8) g = 148 * 8;
+  mb_launch(fp8_block_dequant_kernel, (int)g, 256, 0, st, (const uint8_t*)q, s, M, N, bm, bn,
+            (__nv_bfloat16*)out);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

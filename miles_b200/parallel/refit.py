@@ -84,17 +84,230 @@ class WeightRefit:
     def sync(self) -> dict:
         """Run the refit on this rank (source or engine). Returns timing / volume stats."""
         is_src = dist.get_rank() == self.src
-        if self.model.flat.is_cuda:
+        cuda = self.model.flat.is_cuda
+        if cuda:
             torch.cuda.synchronize(self.model.flat.device)
+            dist.barrier(group=self.group)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
         t0 = time.perf_counter()
         nbytes = self._broadcast_flat() if self.mode == "bf16" else self._broadcast_fp8(is_src)
+        if cuda:
+            e1.record()
         ver = torch.tensor([self.model.weight_version], dtype=torch.int64, device=self.model.flat.device)
         dist.broadcast(ver, self.src, group=self.group)
-        if self.model.flat.is_cuda:
+        if cuda:
             torch.cuda.synchronize(self.model.flat.device)
-        dt = time.perf_counter() - t0
+            # device time of the transfer, max over the group's ranks
+            t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=self.model.flat.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            dt = float(t)
+        else:
+            dt = time.perf_counter() - t0
         if not is_src:
             self.model.weight_version = int(ver.item())
         self.last_stats = {"perf/update_weights_time": dt, "update_weights/bytes": nbytes,
                            "update_weights/GBps": nbytes / dt / 1e9 if dt > 0 else 0.0}
         return self.last_stats
+
+
+# ---------------------------------------------------------------------------------------------
+# Peer-memory refit (one node): the trainer's kernels store straight into the engines' staging
+# buffers over NVLink, the engines pull from each other.
+# ---------------------------------------------------------------------------------------------
+class PeerRefit:
+    """Same role and API as WeightRefit, over symmetric peer memory instead of NCCL broadcast.
+
+    Every rank of `group` (the source trainer rank and the engine ranks, one node) maps an
+    IPC-shared staging area of `bucket_bytes`. Parameters go in buckets; each parameter of a
+    bucket has one owner engine (least-loaded first), so the source sends every byte once:
+
+      1. source: for each parameter, a kernel reads the local bf16 weight and stores into the
+         owner engine's staging over NVLink: a plain copy ("bf16") or the 128x128 block fp8
+         quantisation itself writing the fp8 values and scales ("fp8": quantise and transfer in
+         one pass, half the bytes)
+      2. device barrier over the group (flags in symmetric memory, bounded waits)
+      3. every engine: for each parameter, a kernel reads the owner's staging (its own or a
+         peer's, over NVLink) and writes the local weight: a copy, or the fp8 dequantisation
+      4. device barrier (the staging is reused by the next bucket)
+    i.e. a scatter from the source followed by an all-gather among the engines, done by SM
+    loads/stores inside the kernels. A host barrier over the group first puts every rank in the
+    refit, so the device barriers only wait for in-flight work.
+
+    Reference: update_weight/update_weight_from_distributed.py + broadcast.py (bucketed NCCL
+    broadcast) and update_weight_from_tensor.py (CUDA-IPC handles into colocated engines);
+    processors/quantizer_fp8.py (fp8 block quantisation at refit).
+    """
+
+    def __init__(self, model: Transformer, group, src: int, bucket_bytes: int = 1 << 30,
+                 mode: str = "bf16", timeout_s: float = 5.0):
+        from miles_b200.parallel.symm import SymmBuffer
+
+        if mode not in ("bf16", "fp8"):
+            raise ValueError(f"unknown refit mode {mode}")
+        self.model = model
+        self.group = group
+        self.src = src
+        self.mode = mode
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.src_g = src if group is None else dist.get_group_rank(group, src)
+        self.engines = [r for r in range(self.world) if r != self.src_g]
+        self.cap = max(1 << 20, bucket_bytes // 16 * 16)
+        self.buf = SymmBuffer(256 + self.cap, group, model.flat.device)
+        self.flag_ptrs = list(self.buf.peers)
+        self.stage = [p + 256 for p in self.buf.peers]
+        self.my_flags = self.buf.view(0, (8,), torch.int32)
+        self.ctl = torch.zeros(4, dtype=torch.int32, device=model.flat.device)
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.plan = self._plan()
+        self.last_stats: dict = {}
+
+    # ------------------------------------------------------------------ layout
+    @staticmethod
+    def _pad(n: int) -> int:
+        return (n + 255) // 256 * 256
+
+    def _items(self):
+        """(name, 2-D view or None, bytes in staging) per parameter."""
+        out = []
+        for s in self.model.specs:
+            p = self.model.params[s.name].data
+            w = None
+            if self.mode == "fp8":
+                if p.dim() == 2 and p.shape[0] >= 128 and p.shape[1] >= 128 and p.shape[1] % 16 == 0:
+                    w = p
+                elif p.dim() == 3 and p.shape[1] >= 128 and p.shape[2] >= 128 and p.shape[2] % 16 == 0:
+                    w = p.reshape(-1, p.shape[2])
+            if w is not None:
+                M, N = w.shape
+                nb = self._pad(M * N) + self._pad(((M + 127) // 128) * ((N + 127) // 128) * 4)
+            else:
+                nb = self._pad(p.numel() * p.element_size())
+            out.append((s.name, w, nb))
+        return out
+
+    def _plan(self):
+        """Buckets of (name, 2-D view, owner engine, staging offset)."""
+        buckets, cur, used = [], [], {e: 0 for e in self.engines}
+        for name, w, nb in self._items():
+            if nb > self.cap:
+                raise ValueError(f"{name} needs {nb} staging bytes, more than the bucket ({self.cap})")
+            owner = min(self.engines, key=lambda e: used[e])
+            if used[owner] + nb > self.cap:
+                buckets.append(cur)
+                cur, used = [], {e: 0 for e in self.engines}
+                owner = self.engines[0]
+            cur.append((name, w, owner, used[owner]))
+            used[owner] += nb
+        if cur:
+            buckets.append(cur)
+        return buckets
+
+    # ------------------------------------------------------------------ transfer
+    def _barrier(self):
+        from miles_b200.ops._lib import err_word, lib
+
+        lib().symm_barrier(self.flag_ptrs, self.my_flags, self.ctl, self.rank, self.world,
+                           self.timeout_ns, err_word(self.model.flat.device))
+
+    def _send(self, bucket):
+        from miles_b200.ops._lib import lib
+
+        C = lib()
+        sent = 0
+        for name, w, owner, off in bucket:
+            dst = self.stage[owner] + off
+            if w is not None:
+                M, N = w.shape
+                C.fp8_block_cast_ptr(w.contiguous(), 128, 128, dst, dst + self._pad(M * N), False)
+                sent += M * N + ((M + 127) // 128) * ((N + 127) // 128) * 4
+            else:
+                p = self.model.params[name].data
+                nb = p.numel() * p.element_size()
+                self._copy(p.data_ptr(), dst, nb)
+                sent += nb
+        return sent
+
+    def _recv(self, bucket):
+        from miles_b200.ops._lib import lib
+
+        C = lib()
+        for name, w, owner, off in bucket:
+            src = self.stage[owner] + off
+            if w is not None:
+                M, N = w.shape
+                C.fp8_block_dequant_ptr(src, src + self._pad(M * N), 128, 128, w)
+            else:
+                p = self.model.params[name].data
+                self._copy(src, p.data_ptr(), p.numel() * p.element_size())
+
+    @staticmethod
+    def _copy(src: int, dst: int, nb: int):
+        from miles_b200.ops._lib import lib
+
+        body = nb // 16 * 16
+        if body:
+            lib().symm_copy_ptr(src, dst, body)
+        if nb > body:  # ragged tail (never for 256-byte aligned bf16 tensors of even size)
+            t_src = _raw_bytes(src + body, nb - body)
+            t_dst = _raw_bytes(dst + body, nb - body)
+            t_dst.copy_(t_src)
+
+    @torch.no_grad()
+    def sync(self) -> dict:
+        is_src = self.rank == self.src_g
+        dev = self.model.flat.device
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)  # everyone is in the refit before any device wait
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        nbytes = 0
+        for bucket in self.plan:
+            if is_src:
+                nbytes += self._send(bucket)
+            self._barrier()
+            if not is_src:
+                self._recv(bucket)
+            self._barrier()
+        e1.record()
+        ver = torch.tensor([self.model.weight_version], dtype=torch.int64, device=dev)
+        dist.broadcast(ver, self.src, group=self.group)
+        torch.cuda.synchronize(dev)
+        from miles_b200.ops._lib import check_device_error
+
+        check_device_error(dev)
+        dt = e0.elapsed_time(e1) / 1e3
+        t = torch.tensor([dt], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)  # device time, max over ranks
+        dt = float(t)
+        nb = torch.tensor([nbytes], dtype=torch.float64, device=dev)
+        dist.broadcast(nb, self.src, group=self.group)
+        nbytes = int(nb)
+        if not is_src:
+            self.model.weight_version = int(ver.item())
+        self.last_stats = {"perf/update_weights_time": dt, "update_weights/bytes": nbytes,
+                           "update_weights/GBps": nbytes / dt / 1e9 if dt > 0 else 0.0}
+        return self.last_stats
+
+    def close(self):
+        torch.cuda.synchronize(self.model.flat.device)
+        dist.barrier(group=self.group)
+        self.buf.close()
+
+
+def _raw_bytes(ptr: int, n: int) -> torch.Tensor:
+    from miles_b200.ops import _lib
+
+    return _lib._C.from_ptr(ptr, [n], torch.uint8, torch.cuda.current_device())
+
+
+def make_refit(model: Transformer, group, src: int, bucket_bytes: int, mode: str,
+               transport: str = "auto"):
+    """WeightRefit (NCCL broadcast) or PeerRefit (symmetric peer memory). "auto" picks the
+    peer transport when every rank of the group is a CUDA process of an NCCL job."""
+    if transport == "auto":
+        transport = "peer" if (model.flat.is_cuda and dist.get_backend(group) == "nccl") else "nccl"
+    if transport == "peer":
+        return PeerRefit(model, group, src, bucket_bytes, mode)
+    return WeightRefit(model, group, src, bucket_bytes, mode)

@@ -1,0 +1,106 @@
+"""Weight-refit microbenchmark: seconds and GB/s for one trainer -> engine refit.
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m miles_b200.parallel.refit_bench \
+        --model qwen3-32b --mode bf16|fp8 --transport peer|nccl|both
+
+Rank 0 is the trainer (source, random-init weights of the named architecture); ranks 1..N-1 are
+rollout engines. Each timed refit is device-timed (CUDA events around the transfer, max over
+ranks); after the last one every engine checks its weights against the source (bitwise for
+bf16; for fp8 against the 128x128 block quantisation of the source). Rank 0 prints one JSON
+line per transport.
+
+Reference: the refit path of update_weight_from_distributed.py (bucketed NCCL broadcast) that
+BASELINE's weight-sync metric times.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+
+def _digest(model) -> torch.Tensor:
+    """Order-sensitive checksum of the flat parameter buffer (int64 on the device), computed in
+    chunks so no full-size temporary is allocated."""
+    flat = model.flat.view(torch.int16)
+    acc = torch.zeros(1, dtype=torch.int64, device=flat.device)
+    chunk = 1 << 26
+    w = torch.arange(chunk, device=flat.device, dtype=torch.int64) % 1021 + 1
+    for a in range(0, flat.numel(), chunk):
+        v = flat[a:a + chunk].to(torch.int64)
+        acc += (v * w[: v.numel()]).sum() * ((a // chunk) % 7919 + 1)
+    return acc
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="qwen3-32b")
+    ap.add_argument("--mode", choices=["bf16", "fp8"], default="bf16")
+    ap.add_argument("--transport", choices=["peer", "nccl", "both"], default="both")
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--bucket-mb", type=int, default=1024)
+    a = ap.parse_args(argv)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.parallel.refit import PeerRefit, WeightRefit
+
+    cfg = preset(a.model)
+    model = Transformer(cfg, device=dev, seed=1, materialize=rank == 0)
+    if rank != 0:
+        model.flat.zero_()
+    ref_digest = None
+    if a.mode == "fp8" and rank == 0:
+        # what the engines must end up with: every 2-D weight through the block quantisation
+        from miles_b200.ops.quant import fp8_block_dequant, fp8_block_quant
+
+        saved = model.flat.clone()
+        for s in model.specs:
+            p = model.params[s.name].data
+            w = p if p.dim() == 2 else (p.reshape(-1, p.shape[2]) if p.dim() == 3 else None)
+            if w is not None and w.shape[0] >= 128 and w.shape[1] >= 128 and w.shape[1] % 16 == 0:
+                q, sc = fp8_block_quant(w)
+                w.copy_(fp8_block_dequant(q, sc))
+        ref_digest = _digest(model)
+        model.flat.copy_(saved)
+        del saved
+    else:
+        ref_digest = _digest(model) if rank == 0 else None
+    ref = ref_digest if ref_digest is not None else torch.zeros(1, dtype=torch.int64, device=dev)
+    dist.broadcast(ref, 0)
+    transports = ["peer", "nccl"] if a.transport == "both" else [a.transport]
+    for tr in transports:
+        cls = PeerRefit if tr == "peer" else WeightRefit
+        refit = cls(model, dist.group.WORLD, 0, a.bucket_mb << 20, a.mode)
+        times, stats = [], {}
+        for it in range(a.iters + 1):
+            if rank != 0:
+                model.flat.zero_()
+            stats = refit.sync()
+            if it:  # the first refit is a warm-up
+                times.append(stats["perf/update_weights_time"])
+        ok = torch.tensor([1 if rank == 0 or torch.equal(_digest(model), ref) else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if hasattr(refit, "close"):
+            refit.close()
+        if rank == 0:
+            t = sorted(times)[len(times) // 2]
+            print(json.dumps({"metric": "weight_sync_s", "transport": tr, "mode": a.mode,
+                              "model": a.model, "n_gpus": world, "engines": world - 1,
+                              "seconds": round(t, 5), "bytes": stats["update_weights/bytes"],
+                              "GBps_out_of_trainer": round(stats["update_weights/bytes"] / t / 1e9, 1),
+                              "all_times": [round(x, 5) for x in times],
+                              "engines_match_source": bool(ok.item())}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -131,6 +131,9 @@ def add_rollout_args(p):
     g.add_argument("--rollout-external", action="store_true", default=False)
     g.add_argument("--rollout-external-engine-addrs", nargs="+", default=None)
     g.add_argument("--update-weight-transfer-mode", choices=["broadcast", "p2p"], default="broadcast")
+    g.add_argument("--update-weight-transport", choices=["auto", "peer", "nccl"], default="auto",
+                   help="trainer -> engine refit: kernels storing into the engines' IPC-mapped "
+                        "staging over NVLink (peer), or NCCL broadcast")
     g.add_argument("--update-weight-quant", choices=["none", "fp8"], default="none",
                    help="quantise weights at refit (fp8: 128x128 block-scaled e4m3 broadcast)")
     g.add_argument("--fully-async", action="store_true", default=False,

@@ -221,3 +221,46 @@ def test_symm_two_ranks(tmp_path):
     print({k: v for k, v in r.items() if k != "tokens"})
     assert r["ok"]
     assert r["tp2_logprob_diff"] == 0.0
+
+
+def _two_rank_refit(rank, port, out):
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                            device_id=torch.device("cuda", rank))
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops import check_device_error
+    from miles_b200.parallel.refit import PeerRefit, WeightRefit
+
+    cfg = preset("small-moe")
+    m = Transformer(cfg, device="cuda", seed=9, materialize=rank == 0)
+    res = {}
+    for mode in ("bf16", "fp8"):
+        got = {}
+        for cls in (WeightRefit, PeerRefit):
+            if rank == 1:
+                m.flat.zero_()
+            r = cls(m, dist.group.WORLD, 0, 4 << 20, mode)  # small buckets: several rounds
+            st = r.sync()
+            got[cls.__name__] = m.flat.clone()
+            if hasattr(r, "close"):
+                r.close()
+            res[f"{mode}_{cls.__name__}_GBps"] = st["update_weights/GBps"]
+        if rank == 1:
+            res[f"{mode}_equal"] = bool(torch.equal(got["WeightRefit"], got["PeerRefit"]))
+            res[f"{mode}_nonzero"] = bool(got["PeerRefit"].abs().sum() > 0)
+    check_device_error()
+    if rank == 1:
+        torch.save(res, out)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_refit_matches_nccl_refit(tmp_path):
+    out = str(tmp_path / "refit.pt")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    mp.spawn(_two_rank_refit, args=(29695, out), nprocs=2, join=True)
+    r = torch.load(out)
+    print(r)
+    assert r["bf16_equal"] and r["fp8_equal"] and r["bf16_nonzero"]

@@ -39,7 +39,7 @@ import torch.distributed as dist  # noqa: E402
 from miles_b200.orchestration.rollout_manager import RolloutManager  # noqa: E402
 from miles_b200.orchestration.setup import (ProcessContext, build_actor, build_engine,  # noqa: E402
                                             build_model, load_tokenizer)
-from miles_b200.parallel.refit import WeightRefit  # noqa: E402
+from miles_b200.parallel.refit import make_refit  # noqa: E402
 from miles_b200.rollout.engine_client import LocalEngineClient  # noqa: E402
 from miles_b200.trainer.train_actor import TrainActor  # noqa: E402
 from miles_b200.utils.arguments import parse_args  # noqa: E402
@@ -109,8 +109,10 @@ def run_trainer(args, ctx, T, train_gloo, refit_group, data_gloo):
     actor = build_actor(args, model, ctx)
     trainer = TrainActor(args, actor, ctx.dp_group)
     trainer.init_ref()
-    refit = WeightRefit(model, refit_group, src=0, bucket_bytes=args.update_weight_buffer_size,
-                        mode="fp8" if args.update_weight_quant == "fp8" else "bf16")
+    # only trainer rank 0 belongs to the refit group (it holds the full parameters)
+    refit = make_refit(model, refit_group, src=0, bucket_bytes=args.update_weight_buffer_size,
+                       mode="fp8" if args.update_weight_quant == "fp8" else "bf16",
+                       transport=args.update_weight_transport) if ctx.rank == 0 else None
     tracker = Tracker(args, ctx.rank)
     start, N = 0, args.num_rollout
     if ctx.rank == 0:
@@ -157,8 +159,9 @@ def run_engine(args, ctx, T, R, refit_group, data_gloo):
     client = LocalEngineClient(engine, tok)
     ds_cls = load_function(args.data_source_path)
     manager = RolloutManager(args, ds_cls(args, tok), client, tok, ctx.rank - T, R)
-    refit = WeightRefit(model, refit_group, src=0, bucket_bytes=args.update_weight_buffer_size,
-                        mode="fp8" if args.update_weight_quant == "fp8" else "bf16")
+    refit = make_refit(model, refit_group, src=0, bucket_bytes=args.update_weight_buffer_size,
+                       mode="fp8" if args.update_weight_quant == "fp8" else "bf16",
+                       transport=args.update_weight_transport)
     refit.sync()
     start, N = 0, args.num_rollout
     worker = None
