@@ -176,8 +176,13 @@ int mb_fp8_block_dequant(const void* q, const float* s, int M, int N, int bm, in
 int mb_gemm_bf16_peer(const void* a, long long a_rows, long long a_cols, long long lda, bool a_mn,
                       const void* b, long long b_rows, long long b_cols, long long ldb, bool b_mn,
                       int M, int N, int K, const long long* peer_ptrs, int npeers, long long ldc,
-                      const int* par_word, long long par_stride, int bn, int* err,
+                      const int* par_word, long long par_stride, int scatter_rows, int bn, int* err,
                       cudaStream_t stream);
+int mb_symm_collective(int kind, const long long* flag_ptrs, const long long* stage_ptrs,
+                       int* my_flags, int* ctl, const void* my_stage, long long cap,
+                       const void* src, int rows, int H, int rank, int world, const void* res,
+                       const void* norm_w, float eps, void* out, void* h_out, float* rstd,
+                       long long timeout_ns, int* err, cudaStream_t st);
 #ifdef __cplusplus
 }
 #endif

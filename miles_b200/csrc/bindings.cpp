@@ -382,6 +382,21 @@ int64_t symm_allreduce(std::vector<int64_t> flag_ptrs, std::vector<int64_t> stag
                            rank, world, P(res), P(norm_w), (float)eps, P(out), P(h_out),
                            PT<float>(rstd), timeout_ns, PT<int>(err), cur_stream());
 }
+int64_t symm_collective(int64_t kind, std::vector<int64_t> flag_ptrs, std::vector<int64_t> stage_ptrs,
+                        torch::Tensor my_flags, torch::Tensor ctl, torch::Tensor my_stage,
+                        int64_t cap, OT src, int64_t rows, int64_t H, int64_t rank, int64_t world,
+                        OT res, OT norm_w, double eps, torch::Tensor out, OT h_out, OT rstd,
+                        int64_t timeout_ns, torch::Tensor err) {
+  if (src.has_value()) { CHECK_DT(src.value(), at::kBFloat16); TORCH_CHECK(src.value().is_contiguous()); }
+  CHECK_DT(out, at::kBFloat16);
+  TORCH_CHECK(out.is_contiguous());
+  TORCH_CHECK(out.numel() >= (kind == 2 ? world : 1) * rows * H, "output too small");
+  return mb_symm_collective((int)kind, (const long long*)flag_ptrs.data(),
+                            (const long long*)stage_ptrs.data(), PT<int>(my_flags), PT<int>(ctl),
+                            P(my_stage), cap, P(src), rows, H, rank, world, P(res), P(norm_w),
+                            (float)eps, P(out), P(h_out), PT<float>(rstd), timeout_ns,
+                            PT<int>(err), cur_stream());
+}
 int64_t symm_copy(torch::Tensor src, int64_t dst_ptr, int64_t bytes) {
   return mb_symm_copy(src.data_ptr(), reinterpret_cast<void*>(dst_ptr), bytes, cur_stream());
 }
@@ -407,7 +422,7 @@ int64_t fp8_block_dequant_ptr(int64_t q_ptr, int64_t s_ptr, int64_t bm, int64_t 
 // Fused GEMM + all-reduce, GEMM half: y = a @ b^T (b_mn: a @ b) stored into peer staging areas.
 int64_t gemm_peer(torch::Tensor a, torch::Tensor b, bool b_mn, int64_t M, int64_t N, int64_t K,
                   std::vector<int64_t> peer_ptrs, int64_t ldc, torch::Tensor par_word,
-                  int64_t par_stride, int64_t bn, torch::Tensor err) {
+                  int64_t par_stride, int64_t scatter_rows, int64_t bn, torch::Tensor err) {
   CHECK_CUDA(a); CHECK_CUDA(b);
   CHECK_DT(a, at::kBFloat16); CHECK_DT(b, at::kBFloat16);
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2);
@@ -417,7 +432,8 @@ int64_t gemm_peer(torch::Tensor a, torch::Tensor b, bool b_mn, int64_t M, int64_
   return mb_gemm_bf16_peer(a.data_ptr(), a.size(0), a.size(1), a.stride(0), false, b.data_ptr(),
                            b.size(0), b.size(1), b.stride(0), b_mn, (int)M, (int)N, (int)K,
                            (const long long*)peer_ptrs.data(), (int)peer_ptrs.size(), ldc,
-                           PT<int>(par_word), par_stride, (int)bn, PT<int>(err), cur_stream());
+                           PT<int>(par_word), par_stride, (int)scatter_rows, (int)bn, PT<int>(err),
+                           cur_stream());
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -429,6 +445,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("from_ptr", &from_ptr);
   m.def("symm_barrier", &symm_barrier);
   m.def("symm_allreduce", &symm_allreduce);
+  m.def("symm_collective", &symm_collective);
   m.def("symm_copy", &symm_copy);
   m.def("symm_copy_ptr", &symm_copy_ptr);
   m.def("fp8_block_cast_ptr", &fp8_block_cast_ptr);

@@ -60,6 +60,8 @@ struct GemmParams {
   // ldc; the parity word is the collective's epoch counter, read after the PDL wait.
   void* peer_c[8];
   int npeers;
+  int scatter_rows;  // > 0: row r goes only to peer r / scatter_rows, at row r % scatter_rows
+                     // (GEMM + reduce-scatter); 0: every row to every peer (GEMM + all-reduce)
   const int* par_word;
   long long par_stride;
 };
@@ -387,10 +389,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         for (int i = 0; i < CW; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
         const bool full_cols = col0 + CW <= p.N;
         if (p.epi == 0 || p.epi == 2 || p.epi == 5) {
-         const int ndst = p.epi == 5 ? p.npeers : 1;
-         for (int d = 0; d < ndst; ++d) {
+         int d0 = 0, d1 = 1;
+         long long rb = rbase;
+         if (p.epi == 5) {
+           if (p.scatter_rows > 0) {
+             d0 = row / p.scatter_rows;
+             d1 = d0 + 1;
+             rb = (long long)(row - d0 * p.scatter_rows) * p.ldc;
+           } else {
+             d1 = p.npeers;
+           }
+         }
+         for (int d = d0; d < d1; ++d) {
           __nv_bfloat16* out = (p.epi == 5 ? reinterpret_cast<__nv_bfloat16*>(p.peer_c[d]) + par_off
-                                           : reinterpret_cast<__nv_bfloat16*>(p.C)) + rbase + col0;
+                                           : reinterpret_cast<__nv_bfloat16*>(p.C)) + rb + col0;
           if (full_cols) {
             uint4* o4 = reinterpret_cast<uint4*>(out);
 #pragma unroll
@@ -560,7 +572,8 @@ static int gemm_entry(const void* a, long long a_rows, long long a_cols, long lo
                       long long c_group_stride, int epi, float alpha, int bn, int swiglu_f,
                       void* c2, long long ldc2, const int* group_counts, int* err,
                       cudaStream_t stream, const long long* peer_ptrs = nullptr, int npeers = 0,
-                      const int* par_word = nullptr, long long par_stride = 0) {
+                      const int* par_word = nullptr, long long par_stride = 0,
+                      int scatter_rows = 0) {
   using namespace mb;
   if (a_mn && !b_mn) return -5;
   // The driver's tensor-map encoder needs a current context in the calling thread; a thread
@@ -587,12 +600,14 @@ static int gemm_entry(const void* a, long long a_rows, long long a_cols, long lo
   p.a_stage_bytes = a_mn ? BM * BK * 2 : (int)a_box_rows * BK * 2;
   p.swiglu_f = swiglu_f; p.C2 = c2; p.ldc2 = ldc2;
   p.group_counts = mode == 1 ? group_counts : nullptr;
-  p.npeers = 0; p.par_word = par_word; p.par_stride = par_stride;
+  p.npeers = 0; p.par_word = par_word; p.par_stride = par_stride; p.scatter_rows = 0;
   for (int i = 0; i < 8; ++i) p.peer_c[i] = nullptr;
   if (epi == 5) {
     if (npeers < 1 || npeers > 8 || !par_word) return -1;
     p.npeers = npeers;
     for (int i = 0; i < npeers; ++i) p.peer_c[i] = reinterpret_cast<void*>(peer_ptrs[i]);
+    if (scatter_rows < 0 || (scatter_rows > 0 && (long long)scatter_rows * npeers != M)) return -1;
+    p.scatter_rows = scatter_rows;
     p.C = p.peer_c[0];
   }
   switch (mode) {
@@ -630,16 +645,17 @@ extern "C" int mb_gemm_bf16_swiglu(const void* a, long long a_rows, long long ld
                     err, stream);
 }
 
-// Fused GEMM + all-reduce, GEMM half: C = A B^T (dense, mode 0) with every bf16 output tile
-// stored straight into `npeers` peer staging areas over NVLink (epi 5); the reduce half is
-// mb_symm_allreduce with src = null (symm.cu).
+// Fused GEMM + all-reduce / reduce-scatter, GEMM half: C = A B^T (dense, mode 0) with every
+// bf16 output tile stored straight into peer staging areas over NVLink (epi 5): all `npeers`
+// of them (all-reduce), or only the owner of the row (scatter_rows = M / npeers rows per rank,
+// reduce-scatter). The reduce half is mb_symm_collective with src = null (symm.cu).
 extern "C" int mb_gemm_bf16_peer(const void* a, long long a_rows, long long a_cols, long long lda,
                                  bool a_mn, const void* b, long long b_rows, long long b_cols,
                                  long long ldb, bool b_mn, int M, int N, int K,
                                  const long long* peer_ptrs, int npeers, long long ldc,
-                                 const int* par_word, long long par_stride, int bn, int* err,
-                                 cudaStream_t stream) {
+                                 const int* par_word, long long par_stride, int scatter_rows,
+                                 int bn, int* err, cudaStream_t stream) {
   return gemm_entry(a, a_rows, a_cols, lda, a_mn, b, b_rows, b_cols, ldb, b_mn, nullptr, ldc, M, N,
                     K, 0, nullptr, 1, 0, 0, 5, 1.f, bn, 0, nullptr, 0, nullptr, err, stream,
-                    peer_ptrs, npeers, par_word, par_stride);
+                    peer_ptrs, npeers, par_word, par_stride, scatter_rows);
 }

@@ -114,7 +114,9 @@ struct ReduceArgs {
   __nv_bfloat16* h_out;           // norm mode with residual: h = sum + res
   float* rstd_out;                // optional
   long long cap;                  // rows per staging slot
-  int rows, H, rank, world;
+  int rows, H, rank, world;       // rows: rows of each slot the consumer reads
+  int scatter_rows;               // push: 0 = every peer gets all `rows` rows of src;
+                                  // 1 = peer r gets rows [r*rows, (r+1)*rows) (reduce-scatter)
   float eps;
   long long timeout_ns;
   int* err;
@@ -125,13 +127,25 @@ struct ReduceArgs {
 MB_DEVICE void push_and_announce(const ReduceArgs& a, int par, int e) {
   const long long n8 = (long long)a.rows * a.H / 8;
   const long long slot = (long long)a.cap * a.H;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
-       i += (long long)gridDim.x * blockDim.x) {
-    const uint4 v = *reinterpret_cast<const uint4*>(a.src + i * 8);
-    for (int r = 0; r < a.world; ++r) {
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.stage.p[r]) +
-                           ((long long)par * a.world + a.rank) * slot + i * 8;
+  const long long my_slot = ((long long)par * a.world + a.rank) * slot;
+  if (a.scatter_rows) {
+    // row block r of src -> peer r (each element crosses NVLink once)
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8 * a.world;
+         i += (long long)gridDim.x * blockDim.x) {
+      const int r = (int)(i / n8);
+      const uint4 v = *reinterpret_cast<const uint4*>(a.src + i * 8);
+      __nv_bfloat16* dst =
+          reinterpret_cast<__nv_bfloat16*>(a.stage.p[r]) + my_slot + (i - r * n8) * 8;
       *reinterpret_cast<uint4*>(dst) = v;
+    }
+  } else {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+         i += (long long)gridDim.x * blockDim.x) {
+      const uint4 v = *reinterpret_cast<const uint4*>(a.src + i * 8);
+      for (int r = 0; r < a.world; ++r) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.stage.p[r]) + my_slot + i * 8;
+        *reinterpret_cast<uint4*>(dst) = v;
+      }
     }
   }
   __threadfence_system();
@@ -171,6 +185,26 @@ __global__ void __launch_bounds__(256) symm_allreduce_kernel(ReduceArgs a) {
       o.z = pack_bf16x2(acc[4], acc[5]);
       o.w = pack_bf16x2(acc[6], acc[7]);
       *reinterpret_cast<uint4*>(a.out + i * 8) = o;
+    }
+  }
+  finish(a.ctl, e);
+}
+
+// All-gather: out[r * rows + i] = slot_r[i] (rows of every rank, in rank order).
+__global__ void __launch_bounds__(256) symm_allgather_kernel(ReduceArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int e = *reinterpret_cast<volatile int*>(a.ctl) + 1;
+  const int par = (e - 1) & 1;
+  push_and_announce(a, par, e);
+  if (wait_all(a.my_flags, a.world, e, a.timeout_ns, a.err)) {
+    const long long n8 = (long long)a.rows * a.H / 8;
+    const long long slot = (long long)a.cap * a.H;
+    const __nv_bfloat16* base = a.my_stage + (long long)par * a.world * slot;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8 * a.world;
+         i += (long long)gridDim.x * blockDim.x) {
+      const int r = (int)(i / n8);
+      *reinterpret_cast<uint4*>(a.out + i * 8) = ld_volatile_v4(base + r * slot + (i - r * n8) * 8);
     }
   }
   finish(a.ctl, e);
@@ -331,6 +365,11 @@ static int coll_grid(long long work, int per_cta) {
 }
 
 extern "C" {
+int mb_symm_collective(int kind, const long long* flag_ptrs, const long long* stage_ptrs,
+                       int* my_flags, int* ctl, const void* my_stage, long long cap,
+                       const void* src, int rows, int H, int rank, int world, const void* res,
+                       const void* norm_w, float eps, void* out, void* h_out, float* rstd,
+                       long long timeout_ns, int* err, cudaStream_t st);
 
 int mb_ipc_handle_size() { return (int)sizeof(cudaIpcMemHandle_t); }
 
@@ -382,7 +421,20 @@ int mb_symm_allreduce(const long long* flag_ptrs, const long long* stage_ptrs, i
                       int H, int rank, int world, const void* res, const void* norm_w,
                       float eps, void* out, void* h_out, float* rstd, long long timeout_ns,
                       int* err, cudaStream_t st) {
-  if (world < 1 || world > kMaxPeers || rows > cap || H % 8) return -1;
+  return mb_symm_collective(0, flag_ptrs, stage_ptrs, my_flags, ctl, my_stage, cap, src, rows, H,
+                            rank, world, res, norm_w, eps, out, h_out, rstd, timeout_ns, err, st);
+}
+
+// kind 0: all-reduce (above); 1: reduce-scatter (src holds world * rows rows, row block r
+// goes to rank r, out = this rank's summed block of `rows` rows; norm_w / res fuse the
+// residual + RMSNorm on that block); 2: all-gather (src holds `rows` rows, out world * rows).
+int mb_symm_collective(int kind, const long long* flag_ptrs, const long long* stage_ptrs,
+                       int* my_flags, int* ctl, const void* my_stage, long long cap,
+                       const void* src, int rows, int H, int rank, int world, const void* res,
+                       const void* norm_w, float eps, void* out, void* h_out, float* rstd,
+                       long long timeout_ns, int* err, cudaStream_t st) {
+  if (world < 1 || world > kMaxPeers || rows > cap || H % 8 || kind < 0 || kind > 2) return -1;
+  if (kind == 2 && (!src || norm_w)) return -1;
   if (rows == 0) return 0;
   ReduceArgs a;
   a.flags = to_peers(flag_ptrs, world);
@@ -397,7 +449,10 @@ int mb_symm_allreduce(const long long* flag_ptrs, const long long* stage_ptrs, i
   a.rstd_out = rstd;
   a.cap = cap; a.rows = rows; a.H = H; a.rank = rank; a.world = world; a.eps = eps;
   a.timeout_ns = timeout_ns; a.err = err;
-  if (!norm_w) {
+  a.scatter_rows = kind == 1;
+  if (kind == 2) {
+    mb_launch(symm_allgather_kernel, coll_grid((long long)rows * H / 8 * world, 256 * 4), 256, 0, st, a);
+  } else if (!norm_w) {
     mb_launch(symm_allreduce_kernel, coll_grid((long long)rows * H / 8, 256 * 4), 256, 0, st, a);
   } else {
     if (res && !h_out) return -1;

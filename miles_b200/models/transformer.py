@@ -30,7 +30,8 @@ from miles_b200.ops.attention import PAGE, VarlenMeta, decode_attention, varlen_
 from miles_b200.ops.moe import RouterCfg, moe_experts
 from miles_b200.ops.norm import (add_rms_norm, qk_norm_rope, qk_norm_rope_to_cache, rms_norm,
                                  rope_tables, swiglu)
-from miles_b200.parallel.tp import copy_to_tp, reduce_from_tp
+from miles_b200.parallel.tp import (copy_to_tp, reduce_from_tp, row_parallel_rs, sp_gather,
+                                    sp_gather_replicated, sp_reduce_scatter, sp_split)
 
 
 @dataclass
@@ -154,6 +155,8 @@ class Transformer(torch.nn.Module):
             if self.tp.size == 1:
                 self.tp = None
         self.tp_size = self.tp.size if self.tp else 1
+        # sequence parallelism (training forward): residual stream sharded over TP ranks by rows
+        self.sequence_parallel = False
         self.nq = cfg.num_heads // self.tp_size      # this rank's query heads
         self.nkv = cfg.num_kv_heads // self.tp_size  # this rank's KV heads
         self.ep = None
@@ -287,6 +290,73 @@ class Transformer(torch.nn.Module):
         m = self._mlp(i, x2, replay=replay)
         return m, r
 
+    # -------------------------------------------------------------------------------- sequence parallel
+    def _layer_train_sp(self, i, m_prev, r_prev, meta, replay):
+        """One layer on this rank's rows: norms on T/tp rows, column-parallel projections on the
+        all-gathered rows, row-parallel projections ending in a (fused) reduce-scatter."""
+        cfg, tp = self.cfg, self.tp
+        ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
+        if m_prev is None:
+            x, r = rms_norm(r_prev, ln1, cfg.rms_eps), r_prev
+        else:
+            x, r = add_rms_norm(m_prev, r_prev, ln1, cfg.rms_eps)
+        pre = f"layers.{i}.self_attn."
+        xf = sp_gather(x, tp)
+        qkv = self._lin(xf, pre + "qkv_proj.weight")
+        q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
+                               self.params.get(pre + "k_norm.weight"), meta.positions,
+                               self.rope_cos, self.rope_sin, self.nq, self.nkv, cfg.rms_eps, cfg.qk_norm)
+        o = varlen_attention(q, k, v, meta)
+        a = self._row_rs(o.reshape(xf.shape[0], -1), pre + "o_proj.weight")
+        x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
+        x2f = sp_gather(x2, tp)
+        if i in self.router_cfgs:
+            m = sp_reduce_scatter(self._mlp_partial(i, x2f, replay=replay), tp)
+        else:
+            pm = f"layers.{i}.mlp."
+            m = self._row_rs(self._lin_swiglu(x2f, pm + "gate_up_proj.weight"), pm + "down_proj.weight")
+        return m, r
+
+    def _row_rs(self, a: torch.Tensor, name: str) -> torch.Tensor:
+        if self.lora is not None and name in self.lora:
+            return sp_reduce_scatter(self._lin(a, name), self.tp)
+        return row_parallel_rs(a, self.params[name], self.tp, G.linear)
+
+    def _forward_train_sp(self, tokens, meta, replay_experts):
+        from miles_b200.ops.attention import VarlenMeta
+
+        cfg, tp = self.cfg, self.tp
+        if self.mla is not None:
+            raise NotImplementedError("sequence parallelism is not implemented for MLA models")
+        T = tokens.shape[0]
+        pad = (-T) % tp.size
+        if pad:
+            # a padding sequence at the end so the rows split evenly over the TP ranks
+            tokens = torch.cat([tokens, tokens.new_zeros(pad)])
+            meta = VarlenMeta(list(meta.cu_list) + [T + pad], tokens.device)
+            if replay_experts is not None:
+                replay_experts = torch.cat([replay_experts, replay_experts[:1].expand(pad, -1, -1)])
+        r = sp_split(F.embedding(tokens.long(), self.params["embed_tokens.weight"]), tp)
+        m = None
+        moe_i = 0
+        for i in range(cfg.num_layers):
+            replay = None
+            if i in self.router_cfgs:
+                if replay_experts is not None:
+                    replay = replay_experts[:, moe_i].contiguous()
+                moe_i += 1
+            if self.recompute and torch.is_grad_enabled():
+                if m is None:
+                    m, r = checkpoint(lambda rr, i=i, rp=replay: self._layer_train_sp(i, None, rr, meta, rp),
+                                      r, use_reentrant=False)
+                else:
+                    m, r = checkpoint(lambda mm, rr, i=i, rp=replay: self._layer_train_sp(i, mm, rr, meta, rp),
+                                      m, r, use_reentrant=False)
+            else:
+                m, r = self._layer_train_sp(i, m, r, meta, replay)
+        y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
+        return sp_gather_replicated(y, tp)[:T]
+
     # -------------------------------------------------------------------------------- train
     def forward_train(self, tokens: torch.Tensor, meta: VarlenMeta,
                       replay_experts: torch.Tensor | None = None,
@@ -294,6 +364,8 @@ class Transformer(torch.nn.Module):
         """tokens int [T] packed; returns final hidden [T, H] (after the final norm).
         replay_experts: int32 [T, L_moe, k] routing to replay (R3)."""
         cfg = self.cfg
+        if self.tp is not None and self.sequence_parallel and record_experts is None:
+            return self._forward_train_sp(tokens, meta, replay_experts)
         r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
         m = None
         moe_i = 0

@@ -119,6 +119,8 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
     model = Transformer(cfg, device=ctx.device, dtype=dtype, seed=args.seed, tp_group=ctx.tp_group,
                         ep_group=ctx.ep_group,
                         tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
+    if getattr(args, "sequence_parallel", False) and model.tp is not None and model.mla is None:
+        model.sequence_parallel = True
     loaded = False
     if args.load:
         from miles_b200.checkpoint.torch_dist import is_torch_dist

@@ -169,7 +169,9 @@ class PeerRefit:
         return (n + 255) // 256 * 256
 
     def _items(self):
-        """(name, 2-D view or None, bytes in staging) per parameter."""
+        """Transfer units (name, kind, lo, hi, staging bytes): kind "fp8" moves rows [lo, hi) of
+        a 2-D weight view (multiples of 128 rows, so quantisation blocks never straddle units);
+        kind "copy" moves bytes [lo, hi) of the parameter. Units never exceed the staging."""
         out = []
         for s in self.model.specs:
             p = self.model.params[s.name].data
@@ -181,28 +183,40 @@ class PeerRefit:
                     w = p.reshape(-1, p.shape[2])
             if w is not None:
                 M, N = w.shape
-                nb = self._pad(M * N) + self._pad(((M + 127) // 128) * ((N + 127) // 128) * 4)
+                gn = (N + 127) // 128
+                per_blk = self._pad(128 * N) + self._pad(gn * 4)  # upper bound per 128 rows
+                step = max(1, self.cap // per_blk) * 128
+                for r0 in range(0, M, step):
+                    r1 = min(M, r0 + step)
+                    rows = r1 - r0
+                    nb = self._pad(rows * N) + self._pad(((rows + 127) // 128) * gn * 4)
+                    out.append((s.name, "fp8", r0, r1, nb))
             else:
-                nb = self._pad(p.numel() * p.element_size())
-            out.append((s.name, w, nb))
+                total = p.numel() * p.element_size()
+                step = self.cap // 256 * 256
+                for b0 in range(0, total, step):
+                    b1 = min(total, b0 + step)
+                    out.append((s.name, "copy", b0, b1, self._pad(b1 - b0)))
         return out
 
     def _plan(self):
-        """Buckets of (name, 2-D view, owner engine, staging offset)."""
+        """Buckets of (name, kind, lo, hi, owner engine, staging offset)."""
         buckets, cur, used = [], [], {e: 0 for e in self.engines}
-        for name, w, nb in self._items():
-            if nb > self.cap:
-                raise ValueError(f"{name} needs {nb} staging bytes, more than the bucket ({self.cap})")
+        for name, kind, lo, hi, nb in self._items():
             owner = min(self.engines, key=lambda e: used[e])
             if used[owner] + nb > self.cap:
                 buckets.append(cur)
                 cur, used = [], {e: 0 for e in self.engines}
                 owner = self.engines[0]
-            cur.append((name, w, owner, used[owner]))
+            cur.append((name, kind, lo, hi, owner, used[owner]))
             used[owner] += nb
         if cur:
             buckets.append(cur)
         return buckets
+
+    def _view2d(self, name: str) -> torch.Tensor:
+        p = self.model.params[name].data
+        return p if p.dim() == 2 else p.reshape(-1, p.shape[-1])
 
     # ------------------------------------------------------------------ transfer
     def _barrier(self):
@@ -216,31 +230,29 @@ class PeerRefit:
 
         C = lib()
         sent = 0
-        for name, w, owner, off in bucket:
+        for name, kind, lo, hi, owner, off in bucket:
             dst = self.stage[owner] + off
-            if w is not None:
+            if kind == "fp8":
+                w = self._view2d(name)[lo:hi]
                 M, N = w.shape
-                C.fp8_block_cast_ptr(w.contiguous(), 128, 128, dst, dst + self._pad(M * N), False)
+                C.fp8_block_cast_ptr(w, 128, 128, dst, dst + self._pad(M * N), False)
                 sent += M * N + ((M + 127) // 128) * ((N + 127) // 128) * 4
             else:
-                p = self.model.params[name].data
-                nb = p.numel() * p.element_size()
-                self._copy(p.data_ptr(), dst, nb)
-                sent += nb
+                self._copy(self.model.params[name].data_ptr() + lo, dst, hi - lo)
+                sent += hi - lo
         return sent
 
     def _recv(self, bucket):
         from miles_b200.ops._lib import lib
 
         C = lib()
-        for name, w, owner, off in bucket:
+        for name, kind, lo, hi, owner, off in bucket:
             src = self.stage[owner] + off
-            if w is not None:
-                M, N = w.shape
-                C.fp8_block_dequant_ptr(src, src + self._pad(M * N), 128, 128, w)
+            if kind == "fp8":
+                w = self._view2d(name)[lo:hi]
+                C.fp8_block_dequant_ptr(src, src + self._pad(w.shape[0] * w.shape[1]), 128, 128, w)
             else:
-                p = self.model.params[name].data
-                self._copy(src, p.data_ptr(), p.numel() * p.element_size())
+                self._copy(src, self.model.params[name].data_ptr() + lo, hi - lo)
 
     @staticmethod
     def _copy(src: int, dst: int, nb: int):

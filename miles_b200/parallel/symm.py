@@ -155,7 +155,7 @@ class SymmComm:
         a = a.contiguous()
         bn = _pick_bn(M, N, a.device, narrow=not w_mn)
         lib().gemm_peer(a, w, w_mn, M, N, K, self.gemm_dst, N, self.ctl,
-                        self.world * self.slot_elems, bn, self.err)
+                        self.world * self.slot_elems, 0, bn, self.err)
         out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
         if norm_w is None:
             self._reduce(None, M, N, None, None, 0.0, out, None, None)
@@ -163,6 +163,57 @@ class SymmComm:
         h = torch.empty_like(out) if res is not None else None
         self._reduce(None, M, N, res, norm_w, eps, out, h, None)
         return out, h
+
+    # ------------------------------------------------------------------ sequence parallel
+    def _coll(self, kind, src, rows, H, res, norm_w, eps, out, h_out, rstd):
+        lib().symm_collective(kind, self.flag_ptrs, self.stage_ptrs, self.my_flags, self.ctl,
+                              self.my_stage, self.cap, src, rows, H, self.rank, self.world, res,
+                              norm_w, eps, out, h_out, rstd, self.timeout_ns, self.err)
+        self.calls += 1
+
+    def reduce_scatter(self, x: torch.Tensor, res=None, norm_w=None, eps: float = 0.0,
+                       rstd: torch.Tensor | None = None):
+        """Row block `rank` of sum_r x_r ([rows/world, H]); with norm_w returns (y, h) of the
+        fused residual + RMSNorm on that block."""
+        rows, H = x.shape
+        R = rows // self.world
+        if R * self.world != rows:
+            raise ValueError(f"{rows} rows do not split over {self.world} ranks")
+        self._check(R, H)
+        out = torch.empty(R, H, dtype=x.dtype, device=x.device)
+        if norm_w is None:
+            self._coll(1, x.contiguous(), R, H, None, None, 0.0, out, None, None)
+            return out
+        h = torch.empty_like(out) if res is not None else None
+        self._coll(1, x.contiguous(), R, H, res, norm_w, eps, out, h, rstd)
+        return out, h
+
+    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
+        """Rows of every rank in rank order ([world * rows, H])."""
+        rows, H = x.shape
+        self._check(rows, H)
+        out = torch.empty(self.world * rows, H, dtype=x.dtype, device=x.device)
+        self._coll(2, x.contiguous(), rows, H, None, None, 0.0, out, None, None)
+        return out
+
+    def gemm_reduce_scatter(self, a: torch.Tensor, w: torch.Tensor, w_mn: bool = False):
+        """Row block `rank` of sum_r (a_r @ w_r^T): the GEMM epilogue stores every output row only
+        into its owner's staging (each element crosses NVLink once), the reduce kernel sums."""
+        from miles_b200.ops.gemm import _pick_bn
+
+        M, K = a.shape
+        N = w.shape[1] if w_mn else w.shape[0]
+        R = M // self.world
+        if R * self.world != M:
+            raise ValueError(f"{M} rows do not split over {self.world} ranks")
+        self._check(R, N)
+        a = a.contiguous()
+        bn = _pick_bn(M, N, a.device, narrow=not w_mn)
+        lib().gemm_peer(a, w, w_mn, M, N, K, self.gemm_dst, N, self.ctl,
+                        self.world * self.slot_elems, R, bn, self.err)
+        out = torch.empty(R, N, dtype=torch.bfloat16, device=a.device)
+        self._coll(1, None, R, N, None, None, 0.0, out, None, None)
+        return out
 
     def close(self):
         torch.cuda.synchronize(self.device)

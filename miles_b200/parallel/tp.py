@@ -62,6 +62,45 @@ class TPContext:
         dist.all_reduce(y, group=self.group)
         return y
 
+    # ------------------------------------------------------------------ sequence parallel
+    def _symm_rows(self, x: torch.Tensor, rows: int) -> bool:
+        return (self.backend == "symm" and x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2
+                and x.shape[1] == self.hidden and rows <= self.cap_rows)
+
+    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
+        """Rows of every TP rank, in rank order."""
+        if self.size == 1:
+            return x
+        x = x.contiguous()
+        if self._symm_rows(x, x.shape[0]):
+            return self.symm().all_gather(x)
+        out = x.new_empty((self.size * x.shape[0],) + tuple(x.shape[1:]))
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(out, x, group=self.group)
+        else:
+            dist.all_gather(list(out.chunk(self.size, 0)), x, group=self.group)
+        return out
+
+    def reduce_scatter(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's row block of the sum over TP ranks."""
+        if self.size == 1:
+            return x
+        x = x.contiguous()
+        R = x.shape[0] // self.size
+        if self._symm_rows(x, R):
+            return self.symm().reduce_scatter(x)
+        if dist.get_backend(self.group) == "nccl":
+            out = x.new_empty((R,) + tuple(x.shape[1:]))
+            dist.reduce_scatter_tensor(out, x, group=self.group)
+            return out
+        y = x.clone()
+        dist.all_reduce(y, group=self.group)
+        return y[self.rank * R:(self.rank + 1) * R].contiguous()
+
+    def local_rows(self, x: torch.Tensor) -> torch.Tensor:
+        R = x.shape[0] // self.size
+        return x[self.rank * R:(self.rank + 1) * R]
+
     def shard(self, n: int) -> tuple[int, int]:
         """[lo, hi) of this rank's slice of a dimension of size n."""
         if n % self.size:
@@ -138,12 +177,16 @@ def tp_slice(hf_name: str, full: torch.Tensor, tp: TPContext | None) -> torch.Te
 
 
 def tp_partial_param_names(model) -> list[str]:
-    """Replicated parameters whose gradient on one TP rank covers only its own slice."""
+    """Replicated parameters whose gradient on one TP rank covers only its own slice (its heads,
+    its intermediate slice, or under sequence parallelism its rows)."""
     if model.tp is None or model.tp.size == 1:
         return []
     out = []
+    sp_norms = ("input_layernorm.weight", "post_attention_layernorm.weight")
     for name in model.params:
         if name.endswith(("self_attn.q_norm.weight", "self_attn.k_norm.weight")):
+            out.append(name)
+        elif model.sequence_parallel and (name.endswith(sp_norms) or name == "norm.weight"):
             out.append(name)
         elif name.endswith("mlp.gate.weight"):
             out.append(name)  # router logits feed a combine of partial expert outputs
@@ -180,3 +223,122 @@ def tp_replicated_ranges(model) -> list[tuple[int, int]]:
         return []
     return [(s.offset, s.offset + s.numel) for s in model.specs
             if not s.name.endswith(_SHARDED_INTERNAL)]
+
+
+
+# ------------------------------------------------------------------ sequence parallel
+# Under sequence parallelism the residual stream, norms and embeddings hold T / tp rows per
+# rank; column-parallel projections take the all-gathered rows, row-parallel projections end
+# in a reduce-scatter (fused into the GEMM epilogue with the symmetric-memory backend).
+class _SPGather(torch.autograd.Function):
+    """Forward all-gather rows; backward reduce-scatter."""
+
+    @staticmethod
+    def forward(ctx, x, tp):
+        ctx.tp = tp
+        return tp.all_gather(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.tp.reduce_scatter(g), None
+
+
+class _SPReduceScatter(torch.autograd.Function):
+    """Forward reduce-scatter rows; backward all-gather."""
+
+    @staticmethod
+    def forward(ctx, x, tp):
+        ctx.tp = tp
+        return tp.reduce_scatter(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.tp.all_gather(g), None
+
+
+class _SPSplit(torch.autograd.Function):
+    """Forward: this rank's rows of a replicated tensor; backward all-gather (so the gradient of
+    the replicated input is complete and identical on every rank)."""
+
+    @staticmethod
+    def forward(ctx, x, tp):
+        ctx.tp = tp
+        return tp.local_rows(x).contiguous()
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.tp.all_gather(g.contiguous()), None
+
+
+class _SPGatherReplicated(torch.autograd.Function):
+    """Forward all-gather rows into a tensor every rank then uses identically; backward keeps
+    this rank's rows of the (identical) gradient."""
+
+    @staticmethod
+    def forward(ctx, x, tp):
+        ctx.tp = tp
+        return tp.all_gather(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.tp.local_rows(g).contiguous(), None
+
+
+class _RowParallelRS(torch.autograd.Function):
+    """y_local = reduce_scatter(x @ w^T) with the GEMM's epilogue storing each output row into
+    its owner's staging (symmetric-memory backend); backward all-gathers dy."""
+
+    @staticmethod
+    def forward(ctx, x, w, tp):
+        ctx.tp = tp
+        ctx.save_for_backward(x, w)
+        return tp.symm().gemm_reduce_scatter(x, w)
+
+    @staticmethod
+    def backward(ctx, g):
+        from miles_b200.ops import gemm as G
+
+        x, w = ctx.saved_tensors
+        dy = ctx.tp.all_gather(g.contiguous())
+        dx = G.matmul_nn(dy, w)
+        dw = G._accumulate_wgrad(w, dy, x) if ctx.needs_input_grad[1] else None
+        return dx, dw, None
+
+
+def sp_gather(x, tp):
+    if tp is None or tp.size == 1:
+        return x
+    return _SPGather.apply(x, tp) if torch.is_grad_enabled() and x.requires_grad else tp.all_gather(x)
+
+
+def sp_reduce_scatter(x, tp):
+    if tp is None or tp.size == 1:
+        return x
+    if torch.is_grad_enabled() and x.requires_grad:
+        return _SPReduceScatter.apply(x, tp)
+    return tp.reduce_scatter(x)
+
+
+def sp_split(x, tp):
+    if tp is None or tp.size == 1:
+        return x
+    if torch.is_grad_enabled() and x.requires_grad:
+        return _SPSplit.apply(x, tp)
+    return tp.local_rows(x).contiguous()
+
+
+def sp_gather_replicated(x, tp):
+    if tp is None or tp.size == 1:
+        return x
+    if torch.is_grad_enabled() and x.requires_grad:
+        return _SPGatherReplicated.apply(x, tp)
+    return tp.all_gather(x)
+
+
+def row_parallel_rs(x, w, tp, lin):
+    """reduce_scatter(x @ w^T): fused GEMM + reduce-scatter when the symmetric-memory backend
+    covers the shape, else `lin(x, w)` followed by the reduce-scatter collective."""
+    if tp is not None and tp.size > 1 and tp.backend == "symm" and x.is_cuda \
+            and x.shape[0] // tp.size <= tp.cap_rows and w.shape[0] == tp.hidden:
+        return _RowParallelRS.apply(x, w, tp)
+    return sp_reduce_scatter(lin(x, w), tp)

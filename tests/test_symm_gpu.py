@@ -145,6 +145,20 @@ def _two_rank(rank, port, out):
         y_ref, h_ref = add_rms_norm(ref, r, nw, 1e-6)
         y, h = comm.gemm_all_reduce(a, w, res=r, norm_w=nw, eps=1e-6)
         ok &= torch.equal(y, y_ref) and torch.equal(h, h_ref)
+    # reduce-scatter / all-gather / fused GEMM + reduce-scatter
+    x = torch.randn(512, H, device="cuda", dtype=torch.bfloat16)
+    ref = x.clone()
+    dist.all_reduce(ref)
+    ok &= torch.equal(comm.reduce_scatter(x), ref[rank * 256:(rank + 1) * 256])
+    parts = [torch.empty(100, H, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    dist.all_gather(parts, x[:100].contiguous())
+    ok &= torch.equal(comm.all_gather(x[:100]), torch.cat(parts))
+    a = torch.randn(512, 1024, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(H, 1024, device="cuda", dtype=torch.bfloat16) * 0.03
+    ref = G.linear(a, w)
+    dist.all_reduce(ref)
+    ok &= torch.equal(comm.gemm_reduce_scatter(a, w), ref[rank * 256:(rank + 1) * 256])
+    res["rs_ag_ok"] = bool(ok)
     # decode-shaped timing: fused GEMM+AR+norm vs GEMM, NCCL all-reduce, add_rms_norm
     M, K = 64, 2048
     a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
@@ -202,6 +216,18 @@ def _two_rank(rank, port, out):
                                     torch.tensor(o.tokens, device="cuda"), 1.0, 4096)
             diff = max(diff, (lp.float().cpu() - torch.tensor(o.logprobs)).abs().max().item())
     res["tp2_logprob_diff"] = diff
+    # sequence parallel training forward == TP forward (bitwise), and it backpropagates
+    toks = torch.randint(0, cfg.vocab_size, (301,), generator=g).to("cuda", torch.int32)
+    meta = VarlenMeta([0, 120, 301], "cuda")
+    with torch.no_grad():
+        h_tp = m.forward_train(toks, meta)
+    m.sequence_parallel = True
+    h_sp = m.forward_train(toks, meta)
+    res["sp_equal"] = bool(torch.equal(h_sp.detach(), h_tp))
+    h_sp.float().pow(2).mean().backward()
+    gw = m.params["layers.0.self_attn.o_proj.weight"].grad
+    res["sp_grad_finite"] = bool(gw is not None and torch.isfinite(gw.float()).all())
+    m.sequence_parallel = False
     res["tokens"] = [o.tokens for o in outs]
     check_device_error()
     res["ok"] = bool(ok)
@@ -221,6 +247,7 @@ def test_symm_two_ranks(tmp_path):
     print({k: v for k, v in r.items() if k != "tokens"})
     assert r["ok"]
     assert r["tp2_logprob_diff"] == 0.0
+    assert r["rs_ag_ok"] and r["sp_equal"] and r["sp_grad_finite"]
 
 
 def _two_rank_refit(rank, port, out):

@@ -46,6 +46,25 @@ def _run(rank, world, port, preset_name, ckpt, out_dir):
         if name in partial:
             dist.all_reduce(gr)
         grads[name] = gr
+    # sequence parallel: same forward, same gradients (37 rows: exercises the padding)
+    sp = {}
+    if cfg.kv_lora_rank == 0:
+        for p in m.params.values():
+            p.grad = None
+        m.sequence_parallel = True
+        hs = m.forward_train(toks, meta)
+        hs.pow(2).mean().backward()
+        sp["h"] = hs.detach()
+        partial_sp = set(tp_partial_param_names(m))
+        sp["grads"] = {}
+        for name, p in m.params.items():
+            if p.grad is None:
+                continue
+            gr = p.grad.clone()
+            if name in partial_sp:
+                dist.all_reduce(gr)
+            sp["grads"][name] = gr
+        m.sequence_parallel = False
     # engine decode (prefill + 4 greedy steps)
     from miles_b200.engine.engine import GenRequest, RolloutEngine
 
@@ -54,7 +73,7 @@ def _run(rank, world, port, preset_name, ckpt, out_dir):
                          GenRequest(toks[9:30].tolist(), 4, temperature=0.0, rid=1)])
     save_hf(m, os.path.join(out_dir, "resaved"))
     if rank == 0:
-        torch.save({"h": h.detach(), "grads": grads, "tokens": [o.tokens for o in outs],
+        torch.save({"h": h.detach(), "grads": grads, "sp": sp, "tokens": [o.tokens for o in outs],
                     "lps": [o.logprobs for o in outs]}, os.path.join(out_dir, f"tp{world}.pt"))
     dist.destroy_process_group()
 
@@ -123,6 +142,12 @@ def test_tp2_matches_tp1(tmp_path, preset_name, port):
         g1 = _rank0_slice(name, m1.params[name].grad, cfg, 2)
         assert g1.shape == g2.shape, name
         assert torch.allclose(g2, g1, atol=1e-5, rtol=1e-3), (name, (g2 - g1).abs().max())
+    if r["sp"]:
+        assert torch.allclose(r["sp"]["h"], h1, atol=2e-5, rtol=1e-4), (r["sp"]["h"] - h1).abs().max()
+        assert set(r["sp"]["grads"]) == set(r["grads"])
+        for name, g2 in r["sp"]["grads"].items():
+            g1 = _rank0_slice(name, m1.params[name].grad, cfg, 2)
+            assert torch.allclose(g2, g1, atol=1e-5, rtol=1e-3), ("sp", name, (g2 - g1).abs().max())
     assert r["tokens"] == [o.tokens for o in outs1]
     for a, b in zip(r["lps"], [o.logprobs for o in outs1]):
         assert np.abs(np.asarray(a) - np.asarray(b)).max() < 1e-4
