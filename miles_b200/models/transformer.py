@@ -142,7 +142,7 @@ class KVCache:
 class Transformer(torch.nn.Module):
     def __init__(self, cfg: ModelConfig, device="cuda", dtype=torch.bfloat16, seed: int = 0,
                  init_std: float = 0.02, materialize: bool = True, ep_group=None, tp_group=None,
-                 tp_backend: str = "auto", tp_cap_rows: int = 16384):
+                 tp_backend: str = "auto", tp_cap_rows: int = 16384, cp_group=None):
         super().__init__()
         self.cfg = cfg
         self.device = torch.device(device)
@@ -157,6 +157,17 @@ class Transformer(torch.nn.Module):
         self.tp_size = self.tp.size if self.tp else 1
         # sequence parallelism (training forward): residual stream sharded over TP ranks by rows
         self.sequence_parallel = False
+        self.cp = None  # context parallelism (training forward), miles_b200/parallel/cp.py
+        if cp_group is not None:
+            from miles_b200.parallel.cp import CPContext
+
+            self.cp = CPContext(cp_group)
+            if self.cp.size == 1:
+                self.cp = None
+            elif self.tp is not None:
+                raise ValueError("context parallelism combined with tensor parallelism is not supported")
+            elif cfg.num_kv_heads % self.cp.size:
+                raise ValueError(f"{cfg.num_kv_heads} KV heads do not split over CP {self.cp.size}")
         self.nq = cfg.num_heads // self.tp_size      # this rank's query heads
         self.nkv = cfg.num_kv_heads // self.tp_size  # this rank's KV heads
         self.ep = None
@@ -357,6 +368,91 @@ class Transformer(torch.nn.Module):
         y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
         return sp_gather_replicated(y, tp)[:T]
 
+    # -------------------------------------------------------------------------------- context parallel
+    def _layer_train_cp(self, i, m_prev, r_prev, meta, pos, replay):
+        cfg, cp = self.cfg, self.cp
+        from miles_b200.parallel.cp import heads_to_tokens, tokens_to_heads
+
+        ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
+        if m_prev is None:
+            x, r = rms_norm(r_prev, ln1, cfg.rms_eps), r_prev
+        else:
+            x, r = add_rms_norm(m_prev, r_prev, ln1, cfg.rms_eps)
+        pre = f"layers.{i}.self_attn."
+        qkv = self._lin(x, pre + "qkv_proj.weight")
+        q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
+                               self.params.get(pre + "k_norm.weight"), pos,
+                               self.rope_cos, self.rope_sin, self.nq, self.nkv, cfg.rms_eps, cfg.qk_norm)
+        o = varlen_attention(tokens_to_heads(q, cp), tokens_to_heads(k, cp), tokens_to_heads(v, cp), meta)
+        a = self._lin(heads_to_tokens(o, cp).reshape(x.shape[0], -1), pre + "o_proj.weight")
+        x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
+        return self._mlp(i, x2, replay=replay), r
+
+    def _forward_train_cp(self, tokens, meta, replay_experts):
+        """Final hidden of this CP rank's rows [lo, hi) of the (padded) batch."""
+        from miles_b200.ops.attention import VarlenMeta
+
+        cfg, cp = self.cfg, self.cp
+        if self.mla is not None:
+            raise NotImplementedError("context parallelism is not implemented for MLA models")
+        T = tokens.shape[0]
+        Tp, lo, hi = cp.rows(T)
+        if Tp > T:
+            tokens = torch.cat([tokens, tokens.new_zeros(Tp - T)])
+            meta = VarlenMeta(list(meta.cu_list) + [Tp], tokens.device)
+            if replay_experts is not None:
+                replay_experts = torch.cat([replay_experts, replay_experts[:1].expand(Tp - T, -1, -1)])
+        pos = meta.positions[lo:hi].contiguous()
+        r = F.embedding(tokens[lo:hi].long(), self.params["embed_tokens.weight"])
+        m = None
+        moe_i = 0
+        for i in range(cfg.num_layers):
+            replay = None
+            if i in self.router_cfgs:
+                if replay_experts is not None:
+                    replay = replay_experts[lo:hi, moe_i].contiguous()
+                moe_i += 1
+            if self.recompute and torch.is_grad_enabled():
+                if m is None:
+                    m, r = checkpoint(lambda rr, i=i, rp=replay: self._layer_train_cp(i, None, rr, meta, pos, rp),
+                                      r, use_reentrant=False)
+                else:
+                    m, r = checkpoint(lambda mm, rr, i=i, rp=replay: self._layer_train_cp(i, mm, rr, meta, pos, rp),
+                                      m, r, use_reentrant=False)
+            else:
+                m, r = self._layer_train_cp(i, m, r, meta, pos, replay)
+        y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
+        return y
+
+    def selected_logprob(self, tokens, meta, sel, targets, temperature: float, chunk: int,
+                         replay_experts=None):
+        """(log-prob, entropy) of `targets` at hidden rows `sel` (ascending) of the training
+        forward. Under context parallelism each rank scores the rows it holds and the results
+        are all-gathered; every CP rank returns the full vectors."""
+        from miles_b200.ops.logprob import lm_head_logprob
+
+        W = self.lm_head_weight()
+        h = self.forward_train(tokens, meta, replay_experts=replay_experts)
+        if self.cp is None:
+            return lm_head_logprob(h.index_select(0, sel), W, targets, temperature, chunk)
+        from miles_b200.parallel.cp import gather_parts
+
+        cp = self.cp
+        Tp, lo, hi = cp.rows(tokens.shape[0])
+        R = hi - lo
+        sel_h = sel.cpu()
+        sizes = [int(((sel_h >= r * R) & (sel_h < (r + 1) * R)).sum()) for r in range(cp.size)]
+        mask = (sel >= lo) & (sel < hi)
+        idx = sel[mask] - lo
+        if idx.numel():
+            lp, ent = lm_head_logprob(h.index_select(0, idx), W, targets[mask], temperature, chunk)
+        else:
+            # nothing to score here; stay on the autograd graph so the backward (and its
+            # collectives) runs on every CP rank
+            z = (h[:1].float().sum() * 0).reshape(1)[:0]
+            lp, ent = z, z
+        return gather_parts(lp, cp, sizes), gather_parts(ent, cp, sizes)
+
     # -------------------------------------------------------------------------------- train
     def forward_train(self, tokens: torch.Tensor, meta: VarlenMeta,
                       replay_experts: torch.Tensor | None = None,
@@ -366,6 +462,10 @@ class Transformer(torch.nn.Module):
         cfg = self.cfg
         if self.tp is not None and self.sequence_parallel and record_experts is None:
             return self._forward_train_sp(tokens, meta, replay_experts)
+        if self.cp is not None:
+            if record_experts is not None:
+                raise NotImplementedError("routing capture under context parallelism")
+            return self._forward_train_cp(tokens, meta, replay_experts)
         r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
         m = None
         moe_i = 0

@@ -32,6 +32,7 @@ class ProcessContext:
     tp_group: object = None        # tensor-parallel group (consecutive ranks)
     ep_group: object = None        # expert-parallel group (consecutive ranks)
     expert_dp_group: object = None  # ranks holding the same experts
+    cp_group: object = None        # context-parallel group (consecutive ranks)
     dp_rank: int = 0
     dp_size: int = 1
 
@@ -67,8 +68,20 @@ def init_distributed(args) -> ProcessContext:
         ctx.dp_group, ctx.gloo_group, ctx.dp_rank, ctx.dp_size = dp, gloo, rank, world
         tp = getattr(args, "tensor_model_parallel_size", 1)
         ep = getattr(args, "expert_model_parallel_size", 1)
+        cp = getattr(args, "context_parallel_size", 1)
         if tp > 1 and ep > 1:
             raise ValueError("tensor and expert parallelism cannot be combined")
+        if cp > 1 and (tp > 1 or ep > 1):
+            raise ValueError("context parallelism is supported with data parallelism only")
+        if cp > 1:
+            # CP groups are consecutive ranks; gradients reduce over every rank (DP x CP),
+            # data is sharded over DP replicas only
+            blocks, _ = _groups(world, cp)
+            for ranks in blocks:
+                g = dist.new_group(ranks)
+                if rank in ranks:
+                    ctx.cp_group = g
+            ctx.dp_rank, ctx.dp_size = rank // cp, world // cp
         if tp > 1:
             # TP groups are consecutive ranks (one NVSwitch domain); DP across them
             blocks, strided = _groups(world, tp)
@@ -117,7 +130,7 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
     cfg = model_config(args)
     dtype = torch.bfloat16 if ctx.device.type == "cuda" else torch.float32
     model = Transformer(cfg, device=ctx.device, dtype=dtype, seed=args.seed, tp_group=ctx.tp_group,
-                        ep_group=ctx.ep_group,
+                        ep_group=ctx.ep_group, cp_group=ctx.cp_group,
                         tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
     if getattr(args, "sequence_parallel", False) and model.tp is not None and model.mla is None:
         model.sequence_parallel = True

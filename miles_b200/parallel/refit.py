@@ -122,16 +122,17 @@ class PeerRefit:
     IPC-shared staging area of `bucket_bytes`. Parameters go in buckets; each parameter of a
     bucket has one owner engine (least-loaded first), so the source sends every byte once:
 
-      1. source: for each parameter, a kernel reads the local bf16 weight and stores into the
-         owner engine's staging over NVLink: a plain copy ("bf16") or the 128x128 block fp8
-         quantisation itself writing the fp8 values and scales ("fp8": quantise and transfer in
-         one pass, half the bytes)
+      1. source: for each parameter, the 128x128 block fp8 quantisation kernel reads the local
+         bf16 weight and writes the fp8 values and scales straight into the owner engine's
+         staging (quantise and transfer in one pass, half the bytes)
       2. device barrier over the group (flags in symmetric memory, bounded waits)
-      3. every engine: for each parameter, a kernel reads the owner's staging (its own or a
-         peer's, over NVLink) and writes the local weight: a copy, or the fp8 dequantisation
+      3. every engine: for each parameter, the dequantisation kernel reads the owner's staging
+         (its own or a peer's, over NVLink) and writes the local bf16 weight
       4. device barrier (the staging is reused by the next bucket)
     i.e. a scatter from the source followed by an all-gather among the engines, done by SM
-    loads/stores inside the kernels. A host barrier over the group first puts every rank in the
+    loads/stores inside the kernels. "bf16" needs no staging: the flat parameter buffers
+    themselves are IPC-mapped, the source stores slice j of its buffer into engine j's buffer,
+    and every engine loads the remaining slices from the others. A host barrier over the group first puts every rank in the
     refit, so the device barriers only wait for in-flight work.
 
     Reference: update_weight/update_weight_from_distributed.py + broadcast.py (bucketed NCCL
@@ -160,7 +161,14 @@ class PeerRefit:
         self.my_flags = self.buf.view(0, (8,), torch.int32)
         self.ctl = torch.zeros(4, dtype=torch.int32, device=model.flat.device)
         self.timeout_ns = int(timeout_s * 1e9)
-        self.plan = self._plan()
+        self.plan = self._plan() if mode == "fp8" else []
+        self.flat_ptrs: list[int] = []
+        self._peer_flat = None
+        if mode == "bf16":
+            from miles_b200.parallel.symm import PeerTensor
+
+            self._peer_flat = PeerTensor(model.flat, group)
+            self.flat_ptrs = self._peer_flat.ptrs
         self.last_stats: dict = {}
 
     # ------------------------------------------------------------------ layout
@@ -266,6 +274,30 @@ class PeerRefit:
             t_dst = _raw_bytes(dst + body, nb - body)
             t_dst.copy_(t_src)
 
+    # ------------------------------------------------------------------ bf16: direct
+    def _direct_bf16(self, is_src: bool) -> int:
+        """bf16: no staging at all. The flat parameter buffers are IPC-mapped; the source stores
+        slice j of its buffer straight into engine j's buffer, then every engine loads the other
+        slices from the engine that received them."""
+        flat = self.model.flat
+        nb = flat.numel() * flat.element_size()
+        E = len(self.engines)
+        step = (nb // E + 255) // 256 * 256
+        slices = [(j * step, min(nb, (j + 1) * step)) for j in range(E)]
+        if is_src:
+            for j, e in enumerate(self.engines):
+                lo, hi = slices[j]
+                if hi > lo:
+                    self._copy(self.flat_ptrs[self.src_g] + lo, self.flat_ptrs[e] + lo, hi - lo)
+        self._barrier()
+        if not is_src:
+            for j, e in enumerate(self.engines):
+                lo, hi = slices[j]
+                if e != self.rank and hi > lo:
+                    self._copy(self.flat_ptrs[e] + lo, self.flat_ptrs[self.rank] + lo, hi - lo)
+        self._barrier()
+        return nb
+
     @torch.no_grad()
     def sync(self) -> dict:
         is_src = self.rank == self.src_g
@@ -275,13 +307,16 @@ class PeerRefit:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         nbytes = 0
-        for bucket in self.plan:
-            if is_src:
-                nbytes += self._send(bucket)
-            self._barrier()
-            if not is_src:
-                self._recv(bucket)
-            self._barrier()
+        if self.mode == "bf16":
+            nbytes = self._direct_bf16(is_src)
+        else:
+            for bucket in self.plan:
+                if is_src:
+                    nbytes += self._send(bucket)
+                self._barrier()
+                if not is_src:
+                    self._recv(bucket)
+                self._barrier()
         e1.record()
         ver = torch.tensor([self.model.weight_version], dtype=torch.int64, device=dev)
         dist.broadcast(ver, self.src, group=self.group)
@@ -305,6 +340,8 @@ class PeerRefit:
     def close(self):
         torch.cuda.synchronize(self.model.flat.device)
         dist.barrier(group=self.group)
+        if self._peer_flat is not None:
+            self._peer_flat.close()
         self.buf.close()
 
 

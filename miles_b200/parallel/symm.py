@@ -85,6 +85,36 @@ class SymmBuffer:
         self._closed = True
 
 
+class PeerTensor:
+    """Device pointers to every rank's copy of a tensor allocated by torch (e.g. a model's flat
+    parameter buffer): the storage's CUDA IPC handle and byte offset are exchanged over `group`
+    and opened on every other rank."""
+
+    def __init__(self, t: torch.Tensor, group=None):
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        info = t.untyped_storage()._share_cuda_()
+        handle, off = bytes(info[1]), int(info[3]) + t.storage_offset() * t.element_size()
+        items: list = [None] * self.world
+        dist.all_gather_object(items, (handle, off), group=group)
+        C = _raw()
+        self._bases: list[int] = []
+        self.ptrs: list[int] = []
+        for r, (h, o) in enumerate(items):
+            if r == self.rank:
+                self.ptrs.append(t.data_ptr())
+            else:
+                base = C.ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8), t.device.index)
+                self._bases.append(base)
+                self.ptrs.append(base + o)
+
+    def close(self):
+        C = _raw()
+        for b in self._bases:
+            C.ipc_close(b)
+        self._bases = []
+
+
 class SymmComm:
     def __init__(self, group=None, hidden: int = 4096, cap_rows: int = 256,
                  device: torch.device | None = None, timeout_s: float = 2.0):

@@ -30,7 +30,6 @@ from miles_b200.models.transformer import Transformer
 from miles_b200.ops.gemm import clear_main_grads, register_main_grad
 from miles_b200.parallel.tp import tp_partial_param_names, tp_replicated_ranges
 from miles_b200.ops.attention import VarlenMeta
-from miles_b200.ops.logprob import lm_head_logprob
 from miles_b200.ops.rl import METRIC_NAMES, PolicyLossCfg, policy_loss
 from miles_b200.trainer.optimizer import FlatAdam
 from miles_b200.utils.misc import load_function
@@ -187,13 +186,11 @@ class Actor:
     def compute_logprobs(self, items: list[TrainItem]) -> list[np.ndarray]:
         """Forward-only response log-probs of every item (old / ref log-probs)."""
         out: list[np.ndarray | None] = [None] * len(items)
-        W = self.model.lm_head_weight()
         for mb in pack_microbatches([len(it.tokens) for it in items], self.cfg.max_tokens_per_gpu):
             sub = [items[i] for i in mb]
             tok, meta, sel, tgt = self._mb_inputs(sub)
-            h = self.model.forward_train(tok, meta, replay_experts=self._replay(sub))
-            lp, _ = lm_head_logprob(h.index_select(0, sel), W, tgt, self.cfg.temperature,
-                                    self.cfg.logprob_chunk)
+            lp, _ = self.model.selected_logprob(tok, meta, sel, tgt, self.cfg.temperature,
+                                                self.cfg.logprob_chunk, self._replay(sub))
             lp = lp.cpu().numpy()
             o = 0
             for i in mb:
@@ -214,7 +211,6 @@ class Actor:
         n_samples = global_num_samples or len(items)
         n_tokens = global_num_tokens or sum(
             (sum(it.loss_mask) if it.loss_mask is not None else it.resp_len) for it in items)
-        W = model.lm_head_weight()
         metrics = torch.zeros(len(METRIC_NAMES) + 1, dtype=torch.float64, device=self.dev)
         mbs = pack_microbatches([len(it.tokens) for it in items], cfg.max_tokens_per_gpu)
         for mb in mbs:
@@ -240,9 +236,8 @@ class Actor:
                 else:
                     wgt.append(mask / max(mask.sum(), 1.0) / n_samples)
             T = lambda xs: torch.from_numpy(np.concatenate(xs)).to(self.dev, non_blocking=True)
-            h = model.forward_train(tok, meta, replay_experts=self._replay(sub))
-            hs = h.index_select(0, sel)
-            lp, ent = lm_head_logprob(hs, W, tgt, cfg.temperature, cfg.logprob_chunk)
+            lp, ent = model.selected_logprob(tok, meta, sel, tgt, cfg.temperature,
+                                             cfg.logprob_chunk, self._replay(sub))
             seg = torch.from_numpy(np.repeat(np.arange(len(sub)), [it.resp_len for it in sub])).to(self.dev)
             loss, m = self._loss(lp, ent, seg, len(sub), T(old), T(adv), T(wgt),
                                  T(roll) if any(r is not None for r in roll) else None,

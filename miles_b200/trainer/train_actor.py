@@ -54,12 +54,17 @@ class TensorBackuper:
 
 
 class TrainActor:
-    def __init__(self, args, actor: Actor, dp_group=None, critic=None):
+    def __init__(self, args, actor: Actor, dp_group=None, critic=None,
+                 data_parallel_size: int | None = None):
+        """dp_group reduces gradients (data- x context-parallel ranks); data_parallel_size is
+        the number of distinct data shards (the loss normalisation counts samples over them)."""
         self.args = args
         self.actor = actor
         self.critic = critic  # PPO value model (miles_b200/trainer/critic.py) or None
         self.model = actor.model
         self.dp_group = dp_group
+        self.data_world = data_parallel_size or (
+            torch.distributed.get_world_size(dp_group) if dp_group is not None else 1)
         self.backuper = TensorBackuper(self.model, enabled=not args.disable_weights_backuper)
         self.need_ref = bool(args.use_kl_loss or args.kl_coef)
         self.metrics: dict = {}
@@ -99,7 +104,7 @@ class TrainActor:
             for it, adv in zip(items, advs):
                 it.advantage = adv
         m = {}
-        world = torch.distributed.get_world_size(self.dp_group) if self.dp_group is not None else 1
+        world = self.data_world
         if self.critic is not None and rets is not None:
             cm = self.critic.train_step(items, rets, values, global_num_samples=len(items) * world)
             m.update({f"critic/{k}": v for k, v in cm.items()})
@@ -116,8 +121,7 @@ class TrainActor:
             sub = items[s * per:(s + 1) * per]
             if not sub:
                 continue
-            out = self.actor.train_step(sub, global_num_samples=len(sub) * (
-                torch.distributed.get_world_size(self.dp_group) if self.dp_group is not None else 1))
+            out = self.actor.train_step(sub, global_num_samples=len(sub) * self.data_world)
             for k, v in out.items():
                 m[f"train/{k}" if "/" not in k else k] = v
         t2 = time.perf_counter()

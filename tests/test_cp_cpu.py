@@ -1,0 +1,88 @@
+"""Context parallelism on CPU (gloo, 2 ranks): the per-token log-probs of a CP2 forward equal
+the single-rank ones, and the CP ranks' gradients sum to the single-rank gradients; then one
+train.py GRPO step with --context-parallel-size 2."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _inputs(cfg):
+    from miles_b200.ops.attention import VarlenMeta
+
+    g = torch.Generator().manual_seed(0)
+    toks = torch.randint(0, cfg.vocab_size, (41,), generator=g, dtype=torch.int32)
+    cu = [0, 13, 41]
+    sel = torch.tensor(list(range(5, 12)) + list(range(20, 40)))
+    tgt = toks[sel + 1].clone()
+    return toks, VarlenMeta(cu, "cpu"), sel, tgt
+
+
+def _run(rank, world, port, name, out):
+    os.environ["MILES_B200_FORCE_CPU"] = "1"
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+
+    cfg = preset(name)
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=3, cp_group=dist.group.WORLD)
+    assert m.cp is not None
+    toks, meta, sel, tgt = _inputs(cfg)
+    lp, ent = m.selected_logprob(toks, meta, sel, tgt, 1.0, 4096)
+    (lp.sum() + 0.1 * ent.sum()).backward()
+    grads = {}
+    for n, p in m.params.items():
+        if p.grad is not None:
+            gr = p.grad.clone()
+            dist.all_reduce(gr)
+            grads[n] = gr
+    if rank == 0:
+        torch.save({"lp": lp.detach(), "ent": ent.detach(), "grads": grads}, out)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name,port", [("tiny", 29681), ("tiny-moe", 29682)])
+def test_cp2_matches_single(tmp_path, name, port):
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+
+    cfg = preset(name)
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=3)
+    toks, meta, sel, tgt = _inputs(cfg)
+    lp, ent = m.selected_logprob(toks, meta, sel, tgt, 1.0, 4096)
+    (lp.sum() + 0.1 * ent.sum()).backward()
+    out = str(tmp_path / "cp.pt")
+    mp.spawn(_run, args=(2, port, name, out), nprocs=2, join=True)
+    r = torch.load(out)
+    assert torch.allclose(r["lp"], lp.detach(), atol=1e-5), (r["lp"] - lp).abs().max()
+    assert torch.allclose(r["ent"], ent.detach(), atol=1e-5)
+    assert set(r["grads"]) == {n for n, p in m.params.items() if p.grad is not None}
+    for n, g in r["grads"].items():
+        assert torch.allclose(g, m.params[n].grad, atol=1e-5, rtol=1e-3), (n, (g - m.params[n].grad).abs().max())
+
+
+@pytest.mark.timeout(600)
+def test_train_cp2(tmp_path):
+    import json
+
+    rng = np.random.default_rng(0)
+    with open(tmp_path / "d.jsonl", "w") as f:
+        for _ in range(8):
+            f.write(json.dumps({"input": rng.integers(0, 4096, 64).tolist(), "label": "1"}) + "\n")
+    env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", "29637", os.path.join(ROOT, "train.py"),
+           "--model-name", "tiny", "--prompt-data", str(tmp_path / "d.jsonl"), "--label-key", "label",
+           "--rollout-batch-size", "4", "--n-samples-per-prompt", "4", "--rollout-max-response-len", "16",
+           "--rm-type", "random", "--num-rollout", "1", "--lr", "1e-3", "--max-tokens-per-gpu", "1024",
+           "--actor-num-gpus-per-node", "2", "--context-parallel-size", "2", "--ci-test"]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=580)
+    assert r.returncode == 0, r.stderr[-3000:]

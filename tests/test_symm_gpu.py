@@ -228,6 +228,19 @@ def _two_rank(rank, port, out):
     gw = m.params["layers.0.self_attn.o_proj.weight"].grad
     res["sp_grad_finite"] = bool(gw is not None and torch.isfinite(gw.float()).all())
     m.sequence_parallel = False
+    # context parallel 2: log-probs bitwise equal to the single-GPU forward
+    m_cp = Transformer(cfg, device="cuda", seed=4, cp_group=dist.group.WORLD)
+    m_1 = Transformer(cfg, device="cuda", seed=4)
+    sel = torch.arange(130, 300, device="cuda")
+    tgt = toks[sel + 1]
+    with torch.no_grad():
+        lp_cp, _ = m_cp.selected_logprob(toks, meta, sel, tgt, 1.0, 4096)
+        lp_1, _ = m_1.selected_logprob(toks, meta, sel, tgt, 1.0, 4096)
+    res["cp_equal"] = bool(torch.equal(lp_cp, lp_1))
+    lp_cp, _ = m_cp.selected_logprob(toks, meta, sel, tgt, 1.0, 4096)
+    lp_cp.sum().backward()
+    res["cp_grad_finite"] = bool(torch.isfinite(m_cp.params["layers.1.self_attn.qkv_proj.weight"].grad.float()).all())
+    del m_cp, m_1
     res["tokens"] = [o.tokens for o in outs]
     check_device_error()
     res["ok"] = bool(ok)
@@ -248,6 +261,7 @@ def test_symm_two_ranks(tmp_path):
     assert r["ok"]
     assert r["tp2_logprob_diff"] == 0.0
     assert r["rs_ag_ok"] and r["sp_equal"] and r["sp_grad_finite"]
+    assert r["cp_equal"] and r["cp_grad_finite"]
 
 
 def _two_rank_refit(rank, port, out):

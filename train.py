@@ -49,7 +49,8 @@ def setup(args):
     # prompts are sharded over data-parallel replicas: the ranks of one tensor-parallel group
     # generate (and train on) the same samples
     manager = RolloutManager(args, data_source, client, tok, ctx.dp_rank, ctx.dp_size)
-    trainer = TrainActor(args, actor, ctx.dp_group, critic=build_critic(args, ctx))
+    trainer = TrainActor(args, actor, ctx.dp_group, critic=build_critic(args, ctx),
+                         data_parallel_size=ctx.dp_size)
     start = 0
     if args.load and is_torch_dist(args.load):
         actor._ensure_grads()
