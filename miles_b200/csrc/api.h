@@ -161,6 +161,7 @@ int mb_ipc_handle_size();
 int mb_symm_malloc(long long bytes, long long* ptr_out);
 int mb_symm_free(long long ptr);
 int mb_ipc_get_handle(long long ptr, void* handle_out);
+int mb_ipc_get_handle_range(long long ptr, void* handle_out, long long* offset_out);
 int mb_ipc_open(const void* handle, long long* ptr_out);
 int mb_ipc_close(long long ptr);
 int mb_symm_barrier(const long long* flag_ptrs, int* my_flags, int* ctl, int rank, int world,

@@ -351,6 +351,13 @@ torch::Tensor ipc_get_handle(int64_t ptr) {
   TORCH_CHECK(mb_ipc_get_handle(ptr, t.data_ptr()) == 0, "cudaIpcGetMemHandle failed");
   return t;
 }
+// (handle of the containing allocation, byte offset of ptr in it)
+std::tuple<torch::Tensor, int64_t> ipc_get_handle_range(int64_t ptr) {
+  auto t = torch::empty({mb_ipc_handle_size()}, torch::dtype(torch::kUInt8));
+  long long off = 0;
+  TORCH_CHECK(mb_ipc_get_handle_range(ptr, t.data_ptr(), &off) == 0, "IPC handle lookup failed");
+  return {t, off};
+}
 int64_t ipc_open(torch::Tensor handle, int64_t device) {
   TORCH_CHECK(handle.numel() == mb_ipc_handle_size() && handle.is_contiguous());
   c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
@@ -441,6 +448,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &symm_free);
   m.def("ipc_get_handle", &ipc_get_handle);
   m.def("ipc_open", &ipc_open);
+  m.def("ipc_get_handle_range", &ipc_get_handle_range);
   m.def("ipc_close", &ipc_close);
   m.def("from_ptr", &from_ptr);
   m.def("symm_barrier", &symm_barrier);

@@ -392,6 +392,30 @@ int mb_ipc_get_handle(long long ptr, void* handle_out) {
   return 0;
 }
 
+// Handle of the allocation that contains `ptr` (e.g. a tensor inside a caching-allocator block)
+// and ptr's byte offset from the allocation's base; the importer adds the offset to the base
+// that cudaIpcOpenMemHandle returns.
+int mb_ipc_get_handle_range(long long ptr, void* handle_out, long long* offset_out) {
+  typedef CUresult (*range_fn)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static range_fn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !p)
+      return -3;
+    fn = reinterpret_cast<range_fn>(p);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, (CUdeviceptr)ptr) != CUDA_SUCCESS) return -3;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return -2;
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = ptr - (long long)base;
+  return 0;
+}
+
 int mb_ipc_open(const void* handle, long long* ptr_out) {
   cudaIpcMemHandle_t h;
   memcpy(&h, handle, sizeof(h));

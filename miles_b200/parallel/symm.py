@@ -93,8 +93,8 @@ class PeerTensor:
     def __init__(self, t: torch.Tensor, group=None):
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        info = t.untyped_storage()._share_cuda_()
-        handle, off = bytes(info[1]), int(info[3]) + t.storage_offset() * t.element_size()
+        h, off = _raw().ipc_get_handle_range(t.data_ptr())
+        handle = bytes(h.numpy().tobytes())
         items: list = [None] * self.world
         dist.all_gather_object(items, (handle, off), group=group)
         C = _raw()
