@@ -31,8 +31,9 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
     H, D, nq, nkv = cfg.hidden_size, cfg.head_dim, model.nq, model.nkv
     P = model.params
     pre = "model."
-    yield pre + "embed_tokens.weight", P["embed_tokens.weight"].data
-    for i in range(cfg.num_layers):
+    if "embed_tokens.weight" in P:
+        yield pre + "embed_tokens.weight", P["embed_tokens.weight"].data
+    for i in model.layer_ids:
         L = f"layers.{i}."
         yield pre + L + "input_layernorm.weight", P[L + "input_layernorm.weight"].data
         yield pre + L + "post_attention_layernorm.weight", P[L + "post_attention_layernorm.weight"].data
@@ -73,8 +74,9 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
             yield pre + L + "mlp.gate_proj.weight", gu[:I]
             yield pre + L + "mlp.up_proj.weight", gu[I:]
             yield pre + L + "mlp.down_proj.weight", P[L + "mlp.down_proj.weight"].data
-    yield pre + "norm.weight", P["norm.weight"].data
-    if not cfg.tie_embeddings:
+    if "norm.weight" in P:
+        yield pre + "norm.weight", P["norm.weight"].data
+    if not cfg.tie_embeddings and "lm_head.weight" in P:
         yield "lm_head.weight", P["lm_head.weight"].data
 
 
@@ -115,17 +117,23 @@ def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> No
         if not shard:
             return
         idx += 1
-        fn = f"model-{idx:05d}.safetensors"
+        fn = f"model-{idx:05d}.safetensors" if stage is None else f"model-pp{stage:02d}-{idx:05d}.safetensors"
         save_file(shard, os.path.join(path, fn), metadata={"format": "pt"})
         for n in shard:
             weight_map[n] = fn
         shard, size = {}, 0
 
-    # tensor parallel: every TP rank takes part in the gathers, TP rank 0 writes
+    # tensor parallel: every TP rank takes part in the gathers, TP rank 0 writes;
+    # pipeline parallel: every stage writes its own files, stage 0 writes the merged index
     writer = model.tp is None or model.tp.rank == 0
+    stage = model.pp.stage if model.pp is not None else None
+    if stage is not None and stage > 0 and model.cfg.tie_embeddings:
+        skip = {"model.embed_tokens.weight"}  # stage 0 writes the tied embedding
+    else:
+        skip = set()
     for name, t in to_hf_tensors(model):
         t = tp_gather(name, t.detach(), model.tp)
-        if not writer:
+        if not writer or name in skip:
             continue
         t = t.to("cpu").contiguous().clone()
         nb = t.numel() * t.element_size()
@@ -135,6 +143,17 @@ def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> No
         size += nb
         total += nb
     flush()
+    if model.pp is not None:
+        import torch.distributed as dist
+
+        parts: list = [None] * model.pp.size
+        dist.all_gather_object(parts, (weight_map, total), group=model.pp.group)
+        if stage != 0:
+            return
+        weight_map, total = {}, 0
+        for wm, tt in parts:
+            weight_map.update(wm)
+            total += tt
     with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
         json.dump({"metadata": {"total_size": total}, "weight_map": weight_map}, f, indent=1)
 

@@ -122,12 +122,24 @@ def is_torch_dist(path: str) -> bool:
 _ASYNC: threading.Thread | None = None
 
 
-def _optim_state(optimizer) -> dict:
+def _mp_suffix(model) -> str:
+    """Key suffix of this rank's model-parallel part (TP rank / pipeline stage)."""
+    if model is None:
+        return ""
+    if getattr(model, "tp", None) is not None:
+        return f".tp{model.tp.rank}of{model.tp.size}"
+    if getattr(model, "pp", None) is not None:
+        return f".pp{model.pp.stage}of{model.pp.size}"
+    return ""
+
+
+def _optim_state(optimizer, model=None) -> dict:
     """Optimizer tensors under checkpoint keys. A state sharded over data-parallel ranks is
-    stored under per-shard keys (each rank writes its own; loading needs the same world)."""
+    stored under per-shard keys (each rank writes its own; loading needs the same world), and
+    under model parallelism per TP rank / pipeline stage."""
     osd = optimizer.state_dict()
     rank, world = osd.get("shard", (0, 1))
-    sfx = f".shard{rank}of{world}" if world > 1 else ""
+    sfx = (f".shard{rank}of{world}" if world > 1 else "") + _mp_suffix(model)
     out = {"m" + sfx: osd["m"], "v" + sfx: osd["v"]}
     if osd.get("master") is not None:
         out["master" + sfx] = osd["master"]
@@ -152,7 +164,7 @@ def save_checkpoint(save: str, iteration: int, model: Transformer, optimizer=Non
                 torch.save(optimizer.state_dict(), os.path.join(d, "lora_optim.pt"))
         save_optim = False
     if optimizer is not None and save_optim:
-        sd["optimizer"] = _optim_state(optimizer)
+        sd["optimizer"] = _optim_state(optimizer, model)
     rank0 = not torch.distributed.is_initialized() or torch.distributed.get_rank(process_group) == 0
 
     def _write(sd_cpu):
@@ -196,7 +208,7 @@ def load_checkpoint(load: str, model: Transformer, optimizer=None, load_optim: b
             optimizer.load_state_dict(torch.load(os.path.join(d, "lora_optim.pt"), weights_only=False))
         load_optim = False
     if optimizer is not None and load_optim:
-        sd["optimizer"] = _optim_state(optimizer)  # views of the live state: loaded in place
+        sd["optimizer"] = _optim_state(optimizer, model)  # views of the live state: loaded in place
     dcp.load(sd, checkpoint_id=d, process_group=process_group)
     for name, p in model.params.items():
         t = sd["model"][_key(model, name)]

@@ -49,17 +49,22 @@ class ParamSpec:
         return n
 
 
-def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1) -> list[ParamSpec]:
+def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=None,
+                first: bool = True, last: bool = True) -> list[ParamSpec]:
     """Parameter layout; with expert parallelism each rank holds E / ep_size experts, with
     tensor parallelism each rank holds 1 / tp_size of the heads and intermediate dimensions
-    (miles_b200/parallel/tp.py)."""
+    (miles_b200/parallel/tp.py); a pipeline stage holds `layers` only, the embedding on the first
+    stage and the final norm + LM head on the last (tied embeddings: a copy on the last stage)."""
     H, D = cfg.hidden_size, cfg.head_dim
     t = tp_size
     if cfg.num_heads % t or cfg.num_kv_heads % t:
         raise ValueError(f"heads ({cfg.num_heads} q / {cfg.num_kv_heads} kv) do not split over TP {t}")
     nq, nkv = cfg.num_heads // t, cfg.num_kv_heads // t
-    specs = [ParamSpec("embed_tokens.weight", (cfg.vocab_size, H), "normal")]
-    for i in range(cfg.num_layers):
+    layers = range(cfg.num_layers) if layers is None else layers
+    specs = []
+    if first or (last and cfg.tie_embeddings):
+        specs.append(ParamSpec("embed_tokens.weight", (cfg.vocab_size, H), "normal"))
+    for i in layers:
         p = f"layers.{i}."
         specs.append(ParamSpec(p + "input_layernorm.weight", (H,), "ones"))
         if cfg.kv_lora_rank:  # multi-head latent attention (models/mla.py)
@@ -89,9 +94,10 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1) -> list[Pa
             I = cfg.intermediate_size // t
             specs += [ParamSpec(p + "mlp.gate_up_proj.weight", (2 * I, H), "normal"),
                       ParamSpec(p + "mlp.down_proj.weight", (H, I), "normal")]
-    specs.append(ParamSpec("norm.weight", (H,), "ones"))
-    if not cfg.tie_embeddings:
-        specs.append(ParamSpec("lm_head.weight", (cfg.vocab_size, H), "normal"))
+    if last:
+        specs.append(ParamSpec("norm.weight", (H,), "ones"))
+        if not cfg.tie_embeddings:
+            specs.append(ParamSpec("lm_head.weight", (cfg.vocab_size, H), "normal"))
     # Replicated (dense) parameters first, routed-expert parameters last: under expert
     # parallelism the two regions reduce over different groups.
     specs = [s for s in specs if not is_expert_param(s.name)] + [s for s in specs if is_expert_param(s.name)]
@@ -142,7 +148,8 @@ class KVCache:
 class Transformer(torch.nn.Module):
     def __init__(self, cfg: ModelConfig, device="cuda", dtype=torch.bfloat16, seed: int = 0,
                  init_std: float = 0.02, materialize: bool = True, ep_group=None, tp_group=None,
-                 tp_backend: str = "auto", tp_cap_rows: int = 16384, cp_group=None):
+                 tp_backend: str = "auto", tp_cap_rows: int = 16384, cp_group=None,
+                 pp_group=None):
         super().__init__()
         self.cfg = cfg
         self.device = torch.device(device)
@@ -179,7 +186,20 @@ class Transformer(torch.nn.Module):
                 self.ep = None
         if self.ep is not None and self.tp is not None:
             raise ValueError("expert parallelism combined with tensor parallelism is not supported")
-        self.specs = param_specs(cfg, self.ep.size if self.ep else 1, self.tp_size)
+        self.pp = None  # pipeline parallelism (training), miles_b200/parallel/pp.py
+        if pp_group is not None:
+            from miles_b200.parallel.pp import PPContext
+
+            self.pp = PPContext(pp_group, cfg.num_layers)
+            if self.pp.size == 1:
+                self.pp = None
+            elif self.tp is not None or self.cp is not None or self.ep is not None:
+                raise ValueError("pipeline parallelism is supported with data parallelism only")
+        self.layer_ids = list(range(self.pp.lo, self.pp.hi)) if self.pp else list(range(cfg.num_layers))
+        self.is_first = self.pp is None or self.pp.is_first
+        self.is_last = self.pp is None or self.pp.is_last
+        self.specs = param_specs(cfg, self.ep.size if self.ep else 1, self.tp_size, self.layer_ids,
+                                 self.is_first, self.is_last)
         total = self.specs[-1].offset + self.specs[-1].numel
         self.numel = total
         ex = [sp.offset for sp in self.specs if is_expert_param(sp.name)]
@@ -195,15 +215,21 @@ class Transformer(torch.nn.Module):
             self.params[s.name] = p
         if materialize:
             self.init_weights(seed, init_std)
+            if self.pp is not None and cfg.tie_embeddings:
+                from miles_b200.parallel.pp import sync_tied_embedding
+
+                sync_tied_embedding(self)
         self.rope_cos, self.rope_sin = rope_tables(cfg.max_position, cfg.head_dim, cfg.rope_theta,
                                                    self.device, cfg.rope_scaling)
         self.router_cfgs = {}
         if cfg.is_moe:
             rc = RouterCfg(cfg.num_experts, cfg.topk, cfg.router_score, cfg.norm_topk_prob,
                            cfg.n_group, cfg.topk_group, cfg.routed_scaling_factor)
-            for i in range(cfg.num_layers):
+            for i in self.layer_ids:
                 if cfg.layer_is_moe(i):
                     self.router_cfgs[i] = rc
+        # global ordinal of every MoE layer (column of the R3 routing tensors)
+        self.moe_index = {i: j for j, i in enumerate(i for i in range(cfg.num_layers) if cfg.layer_is_moe(i))}
         self.recompute = True
         self.weight_version = 0
         self.lora = None  # miles_b200.models.lora.LoRA when adapters are attached
@@ -456,9 +482,13 @@ class Transformer(torch.nn.Module):
     # -------------------------------------------------------------------------------- train
     def forward_train(self, tokens: torch.Tensor, meta: VarlenMeta,
                       replay_experts: torch.Tensor | None = None,
-                      record_experts: list | None = None) -> torch.Tensor:
+                      record_experts: list | None = None,
+                      hidden_in: torch.Tensor | None = None) -> torch.Tensor:
         """tokens int [T] packed; returns final hidden [T, H] (after the final norm).
-        replay_experts: int32 [T, L_moe, k] routing to replay (R3)."""
+        replay_experts: int32 [T, L_moe, k] routing to replay (R3).
+        Pipeline stages: a stage after the first takes the residual stream `hidden_in`, a stage
+        before the last returns its residual stream (bitwise what the next layer's fused
+        residual add would have formed)."""
         cfg = self.cfg
         if self.tp is not None and self.sequence_parallel and record_experts is None:
             return self._forward_train_sp(tokens, meta, replay_experts)
@@ -466,15 +496,12 @@ class Transformer(torch.nn.Module):
             if record_experts is not None:
                 raise NotImplementedError("routing capture under context parallelism")
             return self._forward_train_cp(tokens, meta, replay_experts)
-        r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
+        r = F.embedding(tokens.long(), self.params["embed_tokens.weight"]) if self.is_first else hidden_in
         m = None
-        moe_i = 0
-        for i in range(cfg.num_layers):
+        for i in self.layer_ids:
             replay = None
-            if i in self.router_cfgs:
-                if replay_experts is not None:
-                    replay = replay_experts[:, moe_i].contiguous()
-                moe_i += 1
+            if i in self.router_cfgs and replay_experts is not None:
+                replay = replay_experts[:, self.moe_index[i]].contiguous()
             if self.recompute and torch.is_grad_enabled():
                 if m is None:
                     m, r = checkpoint(lambda rr, i=i, rp=replay: self._layer_train(i, None, rr, meta, rp),
@@ -494,6 +521,8 @@ class Transformer(torch.nn.Module):
                     m = self._mlp(i, x2, replay=replay, record=rec)
                 else:
                     m, r = self._layer_train(i, m, r, meta, replay)
+        if not self.is_last:
+            return r if m is None else m + r
         y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
         return y
 

@@ -33,6 +33,7 @@ class ProcessContext:
     ep_group: object = None        # expert-parallel group (consecutive ranks)
     expert_dp_group: object = None  # ranks holding the same experts
     cp_group: object = None        # context-parallel group (consecutive ranks)
+    pp_group: object = None        # pipeline group (one rank per stage)
     dp_rank: int = 0
     dp_size: int = 1
 
@@ -69,6 +70,25 @@ def init_distributed(args) -> ProcessContext:
         tp = getattr(args, "tensor_model_parallel_size", 1)
         ep = getattr(args, "expert_model_parallel_size", 1)
         cp = getattr(args, "context_parallel_size", 1)
+        pp = getattr(args, "pipeline_model_parallel_size", 1)
+        if pp > 1:
+            if tp > 1 or ep > 1 or cp > 1:
+                raise ValueError("pipeline parallelism is supported with data parallelism only")
+            from miles_b200.parallel.pp import register_tied_embedding_groups
+
+            # stage s holds ranks [s*D, (s+1)*D) (its DP group); pipeline d is {d + s*D}
+            D = world // pp
+            for d in range(D):
+                g = dist.new_group([d + s_ * D for s_ in range(pp)])
+                if rank % D == d:
+                    ctx.pp_group = g
+            for s_ in range(pp):
+                ranks = list(range(s_ * D, (s_ + 1) * D))
+                g = dist.new_group(ranks)
+                if rank in ranks:
+                    ctx.dp_group = g
+            register_tied_embedding_groups(world, pp)
+            ctx.dp_rank, ctx.dp_size = rank % D, D
         if tp > 1 and ep > 1:
             raise ValueError("tensor and expert parallelism cannot be combined")
         if cp > 1 and (tp > 1 or ep > 1):
@@ -130,7 +150,7 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
     cfg = model_config(args)
     dtype = torch.bfloat16 if ctx.device.type == "cuda" else torch.float32
     model = Transformer(cfg, device=ctx.device, dtype=dtype, seed=args.seed, tp_group=ctx.tp_group,
-                        ep_group=ctx.ep_group, cp_group=ctx.cp_group,
+                        ep_group=ctx.ep_group, cp_group=ctx.cp_group, pp_group=ctx.pp_group,
                         tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
     if getattr(args, "sequence_parallel", False) and model.tp is not None and model.mla is None:
         model.sequence_parallel = True
@@ -218,3 +238,16 @@ def build_critic(args, ctx: ProcessContext):
                        grad_dtype=torch.float32 if ctx.device.type != "cuda" else torch.bfloat16,
                        optimizer_placement="host" if args.optimizer_cpu_offload else "auto")
     return Critic(body, acfg, value_clip=args.value_clip, dp_group=ctx.dp_group)
+
+
+def build_engine_model(args, model: Transformer, ctx: ProcessContext) -> Transformer:
+    """The model the colocated rollout engine runs. Pipeline stages hold a slice of the layers,
+    so under pipeline parallelism every rank also keeps a full-depth copy that is refreshed from
+    the stages after each training step (parallel/pp.py gather_full_weights)."""
+    if model.pp is None:
+        return model
+    from miles_b200.parallel.pp import gather_full_weights
+
+    full = Transformer(model.cfg, device=ctx.device, dtype=model.dtype, materialize=False)
+    gather_full_weights(model, full)
+    return full

@@ -132,8 +132,21 @@ class Actor:
                                 betas=self.cfg.betas, weight_decay=self.cfg.weight_decay,
                                 clip_grad=self.cfg.clip_grad, placement=self.cfg.optimizer_placement,
                                 dp_group=self.dp_group if self._sharded() else None,
-                                tp_group=self.model.tp.group if self.model.tp else None,
-                                tp_repl_ranges=tp_replicated_ranges(self.model))
+                                **self._norm_scope())
+
+    def _norm_scope(self) -> dict:
+        """Gradient-norm group of model-parallel ranks and the flat ranges this rank leaves out."""
+        m = self.model
+        if m.tp is not None:
+            return {"norm_group": m.tp.group,
+                    "norm_exclude": tp_replicated_ranges(m) if m.tp.rank != 0 else []}
+        if m.pp is not None:
+            ex = []
+            if m.cfg.tie_embeddings and m.pp.is_last and not m.pp.is_first:
+                sp = next(s for s in m.specs if s.name == "embed_tokens.weight")
+                ex.append((sp.offset, sp.offset + sp.numel))
+            return {"norm_group": m.pp.group, "norm_exclude": ex}
+        return {}
 
     def _sharded(self) -> bool:
         """Optimizer sharded over the data-parallel group (ZeRO-1): every rank holds the whole
@@ -186,6 +199,8 @@ class Actor:
     def compute_logprobs(self, items: list[TrainItem]) -> list[np.ndarray]:
         """Forward-only response log-probs of every item (old / ref log-probs)."""
         out: list[np.ndarray | None] = [None] * len(items)
+        if self.model.pp is not None:
+            return self._logprobs_pp(items)
         for mb in pack_microbatches([len(it.tokens) for it in items], self.cfg.max_tokens_per_gpu):
             sub = [items[i] for i in mb]
             tok, meta, sel, tgt = self._mb_inputs(sub)
@@ -198,6 +213,37 @@ class Actor:
                 out[i] = lp[o:o + n]
                 o += n
         return out
+
+    @torch.no_grad()
+    def _logprobs_pp(self, items):
+        from miles_b200.ops.logprob import lm_head_logprob
+        from miles_b200.parallel.pp import run_forward_only
+
+        model, cfg = self.model, self.cfg
+        mbs = pack_microbatches([len(it.tokens) for it in items], cfg.max_tokens_per_gpu)
+        subs = [[items[i] for i in mb] for mb in mbs]
+        ins = [self._mb_inputs(sub) for sub in subs]
+        shapes = [(x[0].shape[0], model.cfg.hidden_size) for x in ins]
+        out: list = [None] * len(items)
+
+        def forward(j, h):
+            tok, meta, sel, tgt = ins[j]
+            y = model.forward_train(tok, meta, replay_experts=self._replay(subs[j]), hidden_in=h)
+            if model.is_last:
+                lp, _ = lm_head_logprob(y.index_select(0, sel), model.lm_head_weight(), tgt,
+                                        cfg.temperature, cfg.logprob_chunk)
+                lp = lp.float().cpu().numpy()
+                o = 0
+                for i in mbs[j]:
+                    n = items[i].resp_len
+                    out[i] = lp[o:o + n]
+                    o += n
+            return y
+
+        run_forward_only(model.pp, len(ins), shapes, model.dtype, self.dev, forward)
+        box = [out]
+        dist.broadcast_object_list(box, model.pp.ranks[-1], group=model.pp.group)
+        return box[0]
 
     # ------------------------------------------------------------------ train
     def train_step(self, items: list[TrainItem], global_num_samples: int | None = None,
@@ -213,40 +259,15 @@ class Actor:
             (sum(it.loss_mask) if it.loss_mask is not None else it.resp_len) for it in items)
         metrics = torch.zeros(len(METRIC_NAMES) + 1, dtype=torch.float64, device=self.dev)
         mbs = pack_microbatches([len(it.tokens) for it in items], cfg.max_tokens_per_gpu)
-        for mb in mbs:
+        if model.pp is not None:
+            self._train_pp(items, mbs, n_samples, n_tokens, metrics)
+        for mb in ([] if model.pp is not None else mbs):
             sub = [items[i] for i in mb]
-            tok, meta, sel, tgt = self._mb_inputs(sub)
-            adv, old, roll, ref, wgt = [], [], [], [], []
-            for it in sub:
-                n = it.resp_len
-                mask = np.asarray(it.loss_mask if it.loss_mask is not None else [1] * n, np.float32)
-                a = it.advantage
-                adv.append(np.full(n, a, np.float32) if np.isscalar(a) else np.asarray(a, np.float32))
-                if it.old_logp is not None:
-                    old.append(np.asarray(it.old_logp, np.float32))
-                elif it.rollout_logp is not None:
-                    old.append(np.asarray(it.rollout_logp, np.float32))
-                else:
-                    old.append(np.zeros(n, np.float32))
-                roll.append(np.asarray(it.rollout_logp if it.rollout_logp is not None else old[-1], np.float32))
-                if it.ref_logp is not None:
-                    ref.append(np.asarray(it.ref_logp, np.float32))
-                if cfg.per_token_loss:
-                    wgt.append(mask / max(n_tokens, 1))
-                else:
-                    wgt.append(mask / max(mask.sum(), 1.0) / n_samples)
-            T = lambda xs: torch.from_numpy(np.concatenate(xs)).to(self.dev, non_blocking=True)
-            lp, ent = model.selected_logprob(tok, meta, sel, tgt, cfg.temperature,
-                                             cfg.logprob_chunk, self._replay(sub))
-            seg = torch.from_numpy(np.repeat(np.arange(len(sub)), [it.resp_len for it in sub])).to(self.dev)
-            loss, m = self._loss(lp, ent, seg, len(sub), T(old), T(adv), T(wgt),
-                                 T(roll) if any(r is not None for r in roll) else None,
-                                 T(ref) if ref and cfg.loss.kl_type != "none" else None)
-            if cfg.entropy_coef:
-                loss = loss - cfg.entropy_coef * (ent * T(wgt)).sum()
+            prep = self._mb_prepare(sub, n_samples, n_tokens)
+            lp, ent = model.selected_logprob(prep["tok"], prep["meta"], prep["sel"], prep["tgt"],
+                                             cfg.temperature, cfg.logprob_chunk, self._replay(sub))
+            loss = self._mb_loss(prep, lp, ent, metrics)
             loss.backward()
-            metrics[: len(METRIC_NAMES)] += m.double().to(self.dev)
-            metrics[-1] += ((ent.detach() * T(wgt)).sum()).double()
         # parameters whose gradient came through autograd (embedding, norms) -> flat buffer
         for name, p in model.params.items():
             if p.grad is not None:
@@ -267,6 +288,82 @@ class Actor:
         self.timers["train_fwd_bwd"] = t1 - t0
         self.timers["train_total"] = time.perf_counter() - t0
         return out
+
+    # ------------------------------------------------------------------ micro-batch pieces
+    def _mb_prepare(self, sub: list[TrainItem], n_samples: int, n_tokens: int) -> dict:
+        """Host-built inputs and per-token loss terms of one micro-batch."""
+        cfg = self.cfg
+        tok, meta, sel, tgt = self._mb_inputs(sub)
+        adv, old, roll, ref, wgt = [], [], [], [], []
+        for it in sub:
+            n = it.resp_len
+            mask = np.asarray(it.loss_mask if it.loss_mask is not None else [1] * n, np.float32)
+            a = it.advantage
+            adv.append(np.full(n, a, np.float32) if np.isscalar(a) else np.asarray(a, np.float32))
+            if it.old_logp is not None:
+                old.append(np.asarray(it.old_logp, np.float32))
+            elif it.rollout_logp is not None:
+                old.append(np.asarray(it.rollout_logp, np.float32))
+            else:
+                old.append(np.zeros(n, np.float32))
+            roll.append(np.asarray(it.rollout_logp if it.rollout_logp is not None else old[-1], np.float32))
+            if it.ref_logp is not None:
+                ref.append(np.asarray(it.ref_logp, np.float32))
+            if cfg.per_token_loss:
+                wgt.append(mask / max(n_tokens, 1))
+            else:
+                wgt.append(mask / max(mask.sum(), 1.0) / n_samples)
+        T = lambda xs: torch.from_numpy(np.concatenate(xs)).to(self.dev, non_blocking=True)
+        seg = torch.from_numpy(np.repeat(np.arange(len(sub)), [it.resp_len for it in sub])).to(self.dev)
+        return {"tok": tok, "meta": meta, "sel": sel, "tgt": tgt, "n": len(sub), "seg": seg,
+                "old": T(old), "adv": T(adv), "wgt": T(wgt),
+                "roll": T(roll) if any(r is not None for r in roll) else None,
+                "ref": T(ref) if ref and cfg.loss.kl_type != "none" else None}
+
+    def _mb_loss(self, prep: dict, lp, ent, metrics: torch.Tensor):
+        cfg = self.cfg
+        loss, m = self._loss(lp, ent, prep["seg"], prep["n"], prep["old"], prep["adv"], prep["wgt"],
+                             prep["roll"], prep["ref"])
+        if cfg.entropy_coef:
+            loss = loss - cfg.entropy_coef * (ent * prep["wgt"]).sum()
+        metrics[: len(METRIC_NAMES)] += m.double().to(self.dev)
+        metrics[-1] += ((ent.detach() * prep["wgt"]).sum()).double()
+        return loss
+
+    def _train_pp(self, items, mbs, n_samples, n_tokens, metrics):
+        """One training pass over the micro-batches through the 1F1B pipeline; the loss and the
+        metrics live on the last stage, which broadcasts the metrics to the other stages."""
+        from miles_b200.ops.logprob import lm_head_logprob
+        from miles_b200.parallel.pp import reduce_tied_embedding, run_1f1b
+
+        model, cfg = self.model, self.cfg
+        subs = [[items[i] for i in mb] for mb in mbs]
+        preps = [self._mb_prepare(sub, n_samples, n_tokens) for sub in subs]
+        shapes = [(p["tok"].shape[0], model.cfg.hidden_size) for p in preps]
+
+        def forward(j, h):
+            p = preps[j]
+            out = model.forward_train(p["tok"], p["meta"], replay_experts=self._replay(subs[j]),
+                                      hidden_in=h)
+            if not model.is_last:
+                return out
+            lp, ent = lm_head_logprob(out.index_select(0, p["sel"]), model.lm_head_weight(), p["tgt"],
+                                      cfg.temperature, cfg.logprob_chunk)
+            return self._mb_loss(p, lp, ent, metrics)
+
+        def backward(j, out, g):
+            if g is None:
+                out.backward()
+            else:
+                out.backward(g)
+
+        run_1f1b(model.pp, len(preps), shapes, model.dtype, self.dev, forward, backward)
+        for name, p in model.params.items():  # autograd-held grads -> flat buffer before the tie
+            if p.grad is not None:
+                p.main_grad.add_(p.grad.to(p.main_grad.dtype))
+                p.grad = None
+        reduce_tied_embedding(model)
+        dist.broadcast(metrics, model.pp.ranks[-1], group=model.pp.group)
 
     # ------------------------------------------------------------------ losses
     def _loss(self, lp, ent, seg, nseq, old, adv, wgt, roll, ref):

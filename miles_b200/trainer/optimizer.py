@@ -41,14 +41,16 @@ class FlatAdam:
     def __init__(self, params_flat: torch.Tensor, grads_flat: torch.Tensor, lr: float = 1e-6,
                  betas=(0.9, 0.98), eps: float = 1e-8, weight_decay: float = 0.0,
                  clip_grad: float = 1.0, placement: str = "auto", chunk: int = 1 << 28,
-                 seed: int = 1234, dp_group=None, tp_group=None, tp_repl_ranges=None):
-        """tp_group / tp_repl_ranges: under tensor parallelism every TP rank runs its own
-        optimizer over its slice; the gradient norm adds the sharded elements of all TP ranks
-        and counts the replicated elements (flat ranges `tp_repl_ranges`) once."""
+                 seed: int = 1234, dp_group=None, norm_group=None, norm_exclude=None):
+        """norm_group / norm_exclude: under model parallelism (TP, PP) every rank runs its own
+        optimizer over its part of the model; the gradient norm sums the squares over
+        `norm_group`, leaving out this rank's flat ranges `norm_exclude` (parameters another
+        rank of the group already counts: TP-replicated ones on TP ranks > 0, the last pipeline
+        stage's copy of tied embeddings)."""
         self.p = params_flat
-        self.tp_group = tp_group
-        self.tp_world = dist.get_world_size(tp_group) if tp_group is not None else 1
-        self.tp_repl = list(tp_repl_ranges or [])
+        self.norm_group = norm_group
+        self.norm_world = dist.get_world_size(norm_group) if norm_group is not None else 1
+        self.norm_exclude = list(norm_exclude or [])
         self.g = grads_flat
         self.lr = lr
         self.betas = betas
@@ -126,18 +128,17 @@ class FlatAdam:
         self.sq.zero_()
         self.skip.zero_()
         sqnorm_(g, self.sq)
-        if self.tp_world > 1:
-            # each TP rank contributes 1/tp of the replicated elements' squares
-            sq_r = torch.zeros_like(self.sq)
-            for a, b in self.tp_repl:
+        if self.norm_world > 1 and self.norm_exclude:
+            sq_x = torch.zeros_like(self.sq)
+            for a, b in self.norm_exclude:
                 a, b = max(a, lo), min(b, hi)
                 if a < b:
-                    sqnorm_(self.g[a:b], sq_r)
-            self.sq.sub_(sq_r * (1.0 - 1.0 / self.tp_world))
+                    sqnorm_(self.g[a:b], sq_x)
+            self.sq.sub_(sq_x)
         if self.world > 1:
             dist.all_reduce(self.sq, group=self.group)
-        if self.tp_world > 1:
-            dist.all_reduce(self.sq, group=self.tp_group)
+        if self.norm_world > 1:
+            dist.all_reduce(self.sq, group=self.norm_group)
         nonfinite_(self.sq, self.skip)
         common = dict(lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.wd,
                       step=self.step_id, sqnorm=self.sq, max_norm=self.clip,

@@ -1,0 +1,111 @@
+"""Pipeline parallelism on CPU (gloo): a PP2 / PP3 actor step over several micro-batches (1F1B)
+gives the same old log-probs, metrics and updated parameters as one rank, tied embeddings
+included; train.py runs with --pipeline-model-parallel-size 2."""
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _items(cfg, n=5):
+    from miles_b200.trainer.actor import TrainItem
+
+    rng = np.random.default_rng(1)
+    out = []
+    for i in range(n):
+        P, R = int(rng.integers(5, 20)), int(rng.integers(3, 12))
+        toks = rng.integers(0, cfg.vocab_size, P + R).tolist()
+        out.append(TrainItem(toks, P, advantage=float(rng.normal()),
+                             rollout_logp=(-rng.random(R)).tolist()))
+    return out
+
+
+def _actor(model):
+    from miles_b200.trainer.actor import Actor, ActorConfig
+
+    # small token budget: several micro-batches go through the pipeline
+    return Actor(model, ActorConfig(lr=1e-3, max_tokens_per_gpu=40, grad_dtype=torch.float32,
+                                    optimizer_placement="device"))
+
+
+def _step(model, cfg):
+    a = _actor(model)
+    items = _items(cfg)
+    old = a.compute_logprobs(items)
+    for it, o in zip(items, old):
+        it.old_logp = o
+    m = a.train_step(items)
+    return old, m
+
+
+def _run(rank, world, port, name, ckpt, out):
+    os.environ["MILES_B200_FORCE_CPU"] = "1"
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    from miles_b200.checkpoint.hf import load_hf
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+
+    cfg = preset(name)
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=7, pp_group=dist.group.WORLD)
+    load_hf(m, ckpt)
+    old, met = _step(m, cfg)
+    torch.save({"old": old, "metrics": met, "params": {k: v.detach().clone() for k, v in m.params.items()}},
+               f"{out}.{rank}")
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name,world,port", [("tiny", 2, 29661), ("tiny-moe", 2, 29662)])
+def test_pp_matches_single(tmp_path, name, world, port):
+    from miles_b200.checkpoint.hf import save_hf
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+
+    cfg = preset(name)
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=7)
+    ckpt = str(tmp_path / "hf")
+    save_hf(m, ckpt)
+    old1, met1 = _step(m, cfg)
+    out = str(tmp_path / "pp")
+    mp.spawn(_run, args=(world, port, name, ckpt, out), nprocs=world, join=True)
+    seen = set()
+    for r in range(world):
+        res = torch.load(f"{out}.{r}", weights_only=False)
+        for a, b in zip(res["old"], old1):
+            assert np.abs(a - b).max() < 1e-5
+        for k in ("pg_loss", "grad_norm"):
+            if k in met1:
+                assert abs(res["metrics"][k] - met1[k]) < 1e-4 * max(1.0, abs(met1[k])), (k, res["metrics"][k], met1[k])
+        for k, v in res["params"].items():
+            assert torch.allclose(v, m.params[k].detach(), atol=1e-5), (r, k, (v - m.params[k]).abs().max())
+            seen.add(k)
+    assert seen == set(m.params)
+
+
+@pytest.mark.timeout(600)
+def test_train_pp2(tmp_path):
+    rng = np.random.default_rng(0)
+    with open(tmp_path / "d.jsonl", "w") as f:
+        for _ in range(8):
+            f.write(json.dumps({"input": rng.integers(0, 4096, 64).tolist(), "label": "1"}) + "\n")
+    env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", "29647", os.path.join(ROOT, "train.py"),
+           "--model-name", "tiny", "--prompt-data", str(tmp_path / "d.jsonl"), "--label-key", "label",
+           "--rollout-batch-size", "4", "--n-samples-per-prompt", "4", "--rollout-max-response-len", "16",
+           "--rm-type", "random", "--num-rollout", "2", "--lr", "1e-3", "--max-tokens-per-gpu", "128",
+           "--actor-num-gpus-per-node", "2", "--pipeline-model-parallel-size", "2", "--ci-test",
+           "--save", str(tmp_path / "ckpt"), "--save-interval", "1",
+           "--save-hf", str(tmp_path / "hf_{rollout_id}")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=580)
+    assert r.returncode == 0, r.stderr[-3000:]
+    idx = json.load(open(tmp_path / "hf_1" / "model.safetensors.index.json"))["weight_map"]
+    assert "model.layers.0.mlp.down_proj.weight" in idx and "model.layers.1.mlp.down_proj.weight" in idx

@@ -22,7 +22,8 @@ from miles_b200.checkpoint.torch_dist import (get_checkpoint_iteration, is_torch
                                               load_checkpoint, save_checkpoint, wait_async_save)
 from miles_b200.orchestration.rollout_manager import RolloutManager  # noqa: E402
 from miles_b200.orchestration.setup import (build_actor, build_critic, build_engine,  # noqa: E402
-                                            build_model, init_distributed, load_tokenizer)
+                                            build_engine_model, build_model, init_distributed,
+                                            load_tokenizer)
 from miles_b200.rollout.engine_client import LocalEngineClient  # noqa: E402
 from miles_b200.trainer.train_actor import TrainActor  # noqa: E402
 from miles_b200.utils.arguments import parse_args  # noqa: E402
@@ -41,7 +42,8 @@ def setup(args):
     dumper.configure(args, ctx.rank)
     model = build_model(args, ctx)
     actor = build_actor(args, model, ctx)
-    engine = build_engine(args, model, ctx)
+    engine_model = build_engine_model(args, model, ctx)
+    engine = build_engine(args, engine_model, ctx)
     tok = load_tokenizer(args)
     client = LocalEngineClient(engine, tok)
     ds_cls = load_function(args.data_source_path)
@@ -81,6 +83,10 @@ def train(args):
             continue
         profiler.start("train_overall")
         m = trainer.train(rollout_id, data)
+        if engine.model is not model:  # pipeline stages -> the engine's full-depth copy
+            from miles_b200.parallel.pp import gather_full_weights
+
+            gather_full_weights(model, engine.model)
         profiler.stop("train_overall")
         profiler.step()
         m.update(data["metrics"])
