@@ -187,3 +187,26 @@ int mb_symm_collective(int kind, const long long* flag_ptrs, const long long* st
 #ifdef __cplusplus
 }
 #endif
+
+// Expert-parallel dispatch / combine over symmetric peer memory (moe_ep.cu).
+#ifdef __cplusplus
+extern "C" {
+#endif
+int mb_ep_publish(const int* counts, int E, int E_local, int rank, int world,
+                  const long long* table_ptrs, cudaStream_t st);
+int mb_ep_offsets(const int* table, int world, int E_local, int align, int* offsets, int* counts,
+                  int* base, long long cap, int* err, cudaStream_t st);
+int mb_ep_dispatch(const void* x, const int* idx, const int* dest_g, const int* off_g, int T,
+                   int k, int H, int E_local, int rank, int world, const long long* base_ptrs,
+                   const long long* xs_ptrs, long long cap, int* pos, int* err, cudaStream_t st);
+int mb_ep_combine(const long long* ys_ptrs, int world, const int* idx, const int* pos,
+                  const float* w, const void* add, int T, int k, int H, int E_local, void* y,
+                  void* saved, cudaStream_t st);
+int mb_ep_combine_bwd(const void* dy, const void* saved, const int* idx, const int* pos,
+                      const float* w, int T, int k, int H, int E_local, int world,
+                      const long long* dys_ptrs, float* dw, cudaStream_t st);
+int mb_ep_gather_bwd(const long long* dxs_ptrs, int world, const int* idx, const int* pos, int T,
+                     int k, int H, int E_local, void* dx, cudaStream_t st);
+#ifdef __cplusplus
+}
+#endif

@@ -443,7 +443,55 @@ int64_t gemm_peer(torch::Tensor a, torch::Tensor b, bool b_mn, int64_t M, int64_
                            cur_stream());
 }
 
+// ------------------------------------------------------------------ expert-parallel dispatch
+#define LLP(v) ((const long long*)(v).data())
+int64_t ep_publish(torch::Tensor counts, int64_t E_local, int64_t rank,
+                   std::vector<int64_t> table_ptrs) {
+  return mb_ep_publish(PT<int>(counts), counts.numel(), E_local, rank, table_ptrs.size(),
+                       LLP(table_ptrs), cur_stream());
+}
+int64_t ep_offsets(torch::Tensor table, int64_t world, int64_t E_local, int64_t align,
+                   torch::Tensor offsets, torch::Tensor counts, torch::Tensor base, int64_t cap,
+                   torch::Tensor err) {
+  return mb_ep_offsets(PT<int>(table), world, E_local, align, PT<int>(offsets), PT<int>(counts),
+                       PT<int>(base), cap, PT<int>(err), cur_stream());
+}
+int64_t ep_dispatch(torch::Tensor x, torch::Tensor idx, torch::Tensor dest_g, torch::Tensor off_g,
+                    int64_t E_local, int64_t rank, std::vector<int64_t> base_ptrs,
+                    std::vector<int64_t> xs_ptrs, int64_t cap, torch::Tensor pos, torch::Tensor err) {
+  TORCH_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16 && idx.is_contiguous());
+  return mb_ep_dispatch(P(x), PT<int>(idx), PT<int>(dest_g), PT<int>(off_g), x.size(0),
+                        idx.size(1), x.size(1), E_local, rank, base_ptrs.size(), LLP(base_ptrs),
+                        LLP(xs_ptrs), cap, PT<int>(pos), PT<int>(err), cur_stream());
+}
+int64_t ep_combine(std::vector<int64_t> ys_ptrs, torch::Tensor idx, torch::Tensor pos,
+                   torch::Tensor w, OT add, int64_t H, int64_t E_local, torch::Tensor y, OT saved) {
+  TORCH_CHECK(y.is_contiguous() && y.scalar_type() == at::kBFloat16);
+  return mb_ep_combine(LLP(ys_ptrs), ys_ptrs.size(), PT<int>(idx), PT<int>(pos), PT<float>(w),
+                       P(add), idx.size(0), idx.size(1), H, E_local, P(y), P(saved), cur_stream());
+}
+int64_t ep_combine_bwd(torch::Tensor dy, torch::Tensor saved, torch::Tensor idx, torch::Tensor pos,
+                       torch::Tensor w, int64_t E_local, std::vector<int64_t> dys_ptrs,
+                       torch::Tensor dw) {
+  TORCH_CHECK(dy.is_contiguous() && saved.is_contiguous());
+  return mb_ep_combine_bwd(P(dy), P(saved), PT<int>(idx), PT<int>(pos), PT<float>(w), idx.size(0),
+                           idx.size(1), dy.size(1), E_local, dys_ptrs.size(), LLP(dys_ptrs),
+                           PT<float>(dw), cur_stream());
+}
+int64_t ep_gather_bwd(std::vector<int64_t> dxs_ptrs, torch::Tensor idx, torch::Tensor pos,
+                      int64_t H, int64_t E_local, torch::Tensor dx) {
+  TORCH_CHECK(dx.is_contiguous());
+  return mb_ep_gather_bwd(LLP(dxs_ptrs), dxs_ptrs.size(), PT<int>(idx), PT<int>(pos), idx.size(0),
+                          idx.size(1), H, E_local, P(dx), cur_stream());
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("ep_publish", &ep_publish);
+  m.def("ep_offsets", &ep_offsets);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_combine", &ep_combine);
+  m.def("ep_combine_bwd", &ep_combine_bwd);
+  m.def("ep_gather_bwd", &ep_gather_bwd);
   m.def("symm_malloc", &symm_malloc);
   m.def("symm_free", &symm_free);
   m.def("ipc_get_handle", &ipc_get_handle);

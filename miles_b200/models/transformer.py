@@ -149,7 +149,7 @@ class Transformer(torch.nn.Module):
     def __init__(self, cfg: ModelConfig, device="cuda", dtype=torch.bfloat16, seed: int = 0,
                  init_std: float = 0.02, materialize: bool = True, ep_group=None, tp_group=None,
                  tp_backend: str = "auto", tp_cap_rows: int = 16384, cp_group=None,
-                 pp_group=None):
+                 pp_group=None, ep_cap_tokens: int = 16384):
         super().__init__()
         self.cfg = cfg
         self.device = torch.device(device)
@@ -181,7 +181,8 @@ class Transformer(torch.nn.Module):
         if ep_group is not None and cfg.is_moe:
             from miles_b200.parallel.ep import EPContext
 
-            self.ep = EPContext(ep_group, cfg.num_experts)
+            self.ep = EPContext(ep_group, cfg.num_experts, "auto", cfg.hidden_size, cfg.topk,
+                                cap_tokens=ep_cap_tokens)
             if self.ep.size == 1:
                 self.ep = None
         if self.ep is not None and self.tp is not None:

@@ -104,7 +104,7 @@ class DeviceKernelError(RuntimeError):
 
 
 _ERR_NAMES = {1: "GEMM pipeline wait timed out", 2: "attention pipeline wait timed out",
-              3: "peer flag wait timed out"}
+              3: "peer flag wait timed out", 4: "expert-parallel receive buffer overflow"}
 
 
 def check_device_error(device: torch.device | None = None, clear: bool = True) -> None:

@@ -9,9 +9,13 @@ tokens:
   3. exchange row counts, then all-to-all the hidden rows and their local expert ids
   4. received rows -> expert-sorted 128-row padded segments -> grouped tcgen05 GEMMs
   5. reverse all-to-all of the expert outputs, then the fixed-order weighted combine
-The backward runs the same exchanges in reverse. The baseline exchange is NCCL all-to-all
-(`all_to_all_single`); the order of every row is a pure function of (source rank, token, slot),
-so results do not depend on timing.
+The backward runs the same exchanges in reverse. Two transports: NCCL all-to-all
+(`all_to_all_single`, steps 3 and 5 above), and in-kernel peer memory (`_MoEEPPeer`,
+csrc/moe_ep.cu): the dispatch kernel stores every row straight into its owner's expert-sorted
+buffer and the combine kernel loads the expert outputs from the owners, with device barriers
+instead of host synchronisation. Either way the order of every row is a pure function of
+(source rank, token, slot), so results do not depend on timing, and both equal the single-GPU
+layer bit for bit.
 
 Reference: Megatron MoE alltoall token dispatcher (--moe-token-dispatcher-type alltoall),
 DeepEP flex dispatcher (--moe-enable-deepep), expert index offsets for naming
@@ -28,7 +32,11 @@ from miles_b200.ops.moe import ALIGN, MoEPlan, RouterCfg, _accum_grouped_wgrad
 
 
 class EPContext:
-    def __init__(self, group, num_experts: int):
+    def __init__(self, group, num_experts: int, transport: str = "auto", hidden: int = 0,
+                 topk: int = 8, cap_tokens: int = 16384):
+        """transport "peer": dispatch / combine by kernels storing into and loading from the
+        other ranks' symmetric buffers (csrc/moe_ep.cu); "nccl": all-to-all collectives;
+        "auto": peer under NCCL (one node), else the collectives."""
         self.group = group
         self.size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -36,6 +44,154 @@ class EPContext:
         self.E = num_experts
         self.E_local = num_experts // self.size
         self.first = self.rank * self.E_local
+        if transport == "auto":
+            transport = "peer" if dist.get_backend(group) == "nccl" and hidden > 0 else "nccl"
+        self.transport = transport
+        self.hidden, self.topk, self.cap_tokens = hidden, topk, cap_tokens
+        self._peer = None
+
+    def peer(self):
+        if self._peer is None:
+            self._peer = EPPeerBuffers(self)
+        return self._peer
+
+
+class EPPeerBuffers:
+    """Symmetric region of one EP rank: flags | table [world][E_local] | base [E_local][world] |
+    xs [cap][H] | ys [cap][H] (cap = world * cap_tokens * k rows + 128-row padding per expert)."""
+
+    def __init__(self, ep: "EPContext"):
+        from miles_b200.ops._lib import err_word
+        from miles_b200.parallel.symm import SymmBuffer
+
+        W, El, H = ep.size, ep.E_local, ep.hidden
+        self.cap = W * ep.cap_tokens * ep.topk + El * ALIGN
+        self.t_off = 256
+        self.b_off = self.t_off + ((W * El * 4 + 255) // 256) * 256
+        self.x_off = self.b_off + ((El * W * 4 + 255) // 256) * 256
+        self.y_off = self.x_off + self.cap * H * 2
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.buf = SymmBuffer(self.y_off + self.cap * H * 2, ep.group, dev)
+        P = self.buf.peers
+        self.flag_ptrs = list(P)
+        self.table_ptrs = [p + self.t_off for p in P]
+        self.base_ptrs = [p + self.b_off for p in P]
+        self.xs_ptrs = [p + self.x_off for p in P]
+        self.ys_ptrs = [p + self.y_off for p in P]
+        self.my_flags = self.buf.view(0, (8,), torch.int32)
+        self.table = self.buf.view(self.t_off, (W * El,), torch.int32)
+        self.base = self.buf.view(self.b_off, (El * W,), torch.int32)
+        self.xs = self.buf.view(self.x_off, (self.cap, H), torch.bfloat16)
+        self.ys = self.buf.view(self.y_off, (self.cap, H), torch.bfloat16)
+        self.ctl = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.err = err_word(dev)
+        self.ep = ep
+
+    def barrier(self):
+        lib().symm_barrier(self.flag_ptrs, self.my_flags, self.ctl, self.ep.rank, self.ep.size,
+                           2_000_000_000, self.err)
+
+
+class _RecvPlan:
+    """Grouped-GEMM plan of the rows an owner received (device offsets / counts, host bounds)."""
+
+    def __init__(self, offsets, counts, E, rows, n_rows):
+        self.offsets, self.counts, self.E, self.rows = offsets, counts, E, rows
+        self.T, self.k = n_rows, 1
+
+    @property
+    def total_rows(self):
+        return self.offsets[self.E:]
+
+
+class _MoEEPPeer(torch.autograd.Function):
+    """Expert-parallel MoE layer with in-kernel dispatch / combine over peer memory (see
+    csrc/moe_ep.cu for the steps and their ordering)."""
+
+    @staticmethod
+    def forward(ctx, x, router_w, w1, w2, bias, cfg: RouterCfg, ep: EPContext, replay_idx, record,
+                need_bwd):
+        T, H = x.shape
+        k = cfg.k
+        x = x.contiguous()
+        B = ep.peer()
+        C = lib()
+        dev = x.device
+        logits = G.matmul_nt(x, router_w, out_dtype=torch.float32)
+        idx = torch.empty(T, k, dtype=torch.int32, device=dev)
+        w = torch.empty(T, k, dtype=torch.float32, device=dev)
+        C.router_fwd(logits, bias, replay_idx, idx, w, k, cfg.score_fn, cfg.renorm,
+                     cfg.n_group, cfg.topk_group, cfg.scale)
+        if record is not None:
+            record(idx)
+        if T > ep.cap_tokens:
+            raise ValueError(f"{T} tokens exceed the EP buffers ({ep.cap_tokens})")
+        n = T * k
+        nch = max(1, (n + 1023) // 1024)
+        hist = torch.empty(nch * ep.E, dtype=torch.int32, device=dev)
+        hbase = torch.empty_like(hist)
+        counts_g = torch.empty(ep.E, dtype=torch.int32, device=dev)
+        off_g = torch.empty(ep.E + 1, dtype=torch.int32, device=dev)
+        dest_g = torch.empty(n, dtype=torch.int32, device=dev)
+        C.moe_permute_plan(idx.view(-1), ep.E, 1, hist, hbase, counts_g, off_g, dest_g)
+        C.ep_publish(counts_g, ep.E_local, ep.rank, B.table_ptrs)
+        B.barrier()
+        offsets = torch.empty(ep.E_local + 1, dtype=torch.int32, device=dev)
+        counts = torch.empty(ep.E_local, dtype=torch.int32, device=dev)
+        C.ep_offsets(B.table, ep.size, ep.E_local, ALIGN, offsets, counts, B.base, B.cap, B.err)
+        B.barrier()
+        pos = torch.empty(n, dtype=torch.int32, device=dev)
+        C.ep_dispatch(x, idx, dest_g, off_g, ep.E_local, ep.rank, B.base_ptrs, B.xs_ptrs, B.cap, pos, B.err)
+        B.barrier()
+        # owner: grouped expert GEMMs on the received rows
+        nb = ep.size * T * k  # bound on received rows (ranks run equal micro-batch shapes)
+        plan = _RecvPlan(offsets, counts, ep.E_local, B.cap, nb)
+        if need_bwd:
+            xs = B.xs.clone()
+            C.moe_zero_pad(counts, offsets, xs)
+        else:
+            xs = B.xs
+        cnt = None if need_bwd else counts
+        a, gu = G.grouped_nt_swiglu(xs, w1, offsets, n_rows=nb, save_gu=need_bwd, counts=cnt)
+        G.grouped_nt(a, w2, offsets, out=B.ys, n_rows=nb, counts=cnt)
+        B.barrier()
+        y = torch.empty_like(x)
+        saved = torch.empty(n, H, dtype=x.dtype, device=dev) if need_bwd else None
+        C.ep_combine(B.ys_ptrs, idx, pos, w, None, H, ep.E_local, y, saved)
+        if need_bwd:
+            ctx.save_for_backward(x, router_w, w1, w2, logits, idx, w, pos, xs, gu, a, saved,
+                                  offsets, counts)
+            ctx.misc = (cfg, ep, plan)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, router_w, w1, w2, logits, idx, w, pos, xs, gu, a, saved, offsets, counts = ctx.saved_tensors
+        cfg, ep, plan = ctx.misc
+        B = ep.peer()
+        C = lib()
+        T, H = x.shape
+        dy = dy.contiguous()
+        B.barrier()  # every rank is done reading the ys buffers of the forward combine
+        dw = torch.empty_like(w)
+        C.ep_combine_bwd(dy, saved, idx, pos, w, ep.E_local, B.ys_ptrs, dw)
+        B.barrier()
+        dys = B.ys
+        C.moe_zero_pad(counts, offsets, dys)
+        da = G.grouped_nn(dys, w2, offsets)
+        dw2 = _accum_grouped_wgrad(w2, dys, a, plan)
+        dgu = torch.empty_like(gu)
+        C.swiglu_bwd(gu, da, dgu, plan.total_rows)
+        G.grouped_nn(dgu, w1, offsets, out=B.xs)
+        dw1 = _accum_grouped_wgrad(w1, dgu, xs, plan)
+        B.barrier()
+        dx = torch.empty_like(x)
+        C.ep_gather_bwd(B.xs_ptrs, idx, pos, H, ep.E_local, dx)
+        dlogits = torch.empty(T, cfg.E, dtype=torch.bfloat16, device=x.device)
+        C.router_bwd(logits, idx, dw, dlogits, cfg.score_fn, cfg.renorm, cfg.scale)
+        dx.add_(G.matmul_nn(dlogits, router_w))
+        dwr = G._accumulate_wgrad(router_w, dlogits, x)
+        return dx, dwr, dw1, dw2, None, None, None, None, None, None
 
 
 def _exchange_counts(send_counts: torch.Tensor, ep: EPContext) -> torch.Tensor:
@@ -138,5 +294,6 @@ def moe_experts_ep(x, router_w, w1_local, w2_local, cfg: RouterCfg, ep: EPContex
                    replay_idx=None, record=None):
     """Expert-parallel MoE: w1_local [E/ep, 2I, H], w2_local [E/ep, H, I] hold this rank's
     experts; routing and the output are over the global expert set."""
-    return _MoEEP.apply(x, router_w, w1_local, w2_local, bias, cfg, ep, replay_idx, record,
-                        torch.is_grad_enabled())
+    fn = _MoEEPPeer if (ep.transport == "peer" and x.is_cuda) else _MoEEP
+    return fn.apply(x, router_w, w1_local, w2_local, bias, cfg, ep, replay_idx, record,
+                    torch.is_grad_enabled())

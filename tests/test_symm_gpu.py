@@ -305,3 +305,55 @@ def test_peer_refit_matches_nccl_refit(tmp_path):
     r = torch.load(out)
     print(r)
     assert r["bf16_equal"] and r["fp8_equal"] and r["bf16_nonzero"]
+
+
+def _two_rank_ep(rank, port, out):
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                            device_id=torch.device("cuda", rank))
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops import check_device_error
+    from miles_b200.ops.attention import VarlenMeta
+
+    cfg = preset("small-moe")
+    m = Transformer(cfg, device="cuda", seed=21 + rank, ep_group=dist.group.WORLD, ep_cap_tokens=1024)
+    assert m.ep is not None and m.ep.transport == "peer"
+    g = torch.Generator().manual_seed(5 + rank)  # different tokens per rank
+    toks = torch.randint(0, cfg.vocab_size, (333,), generator=g).to("cuda", torch.int32)
+    meta = VarlenMeta([0, 100, 333], "cuda")
+    res = {}
+    outs, grads = {}, {}
+    for tr in ("peer", "nccl"):
+        m.ep.transport = tr
+        for p in m.params.values():
+            p.grad = None
+        h = m.forward_train(toks, meta)
+        h.float().pow(2).mean().backward()
+        outs[tr] = h.detach().clone()
+        grads[tr] = {n: p.grad.clone() for n, p in m.params.items() if p.grad is not None}
+    res["fwd_equal"] = bool(torch.equal(outs["peer"], outs["nccl"]))
+    res["grad_equal"] = all(torch.equal(grads["peer"][n], grads["nccl"][n]) for n in grads["nccl"])
+    res["grad_names"] = sorted(grads["nccl"])
+    # decode-sized forward without autograd
+    with torch.no_grad():
+        hs = {}
+        for tr in ("peer", "nccl"):
+            m.ep.transport = tr
+            hs[tr] = m.forward_train(toks[:40], VarlenMeta([0, 40], "cuda"))
+        res["nograd_equal"] = bool(torch.equal(hs["peer"], hs["nccl"]))
+    check_device_error()
+    if rank == 0:
+        torch.save(res, out)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_peer_transport_matches_nccl(tmp_path):
+    out = str(tmp_path / "ep.pt")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    mp.spawn(_two_rank_ep, args=(29697, out), nprocs=2, join=True)
+    r = torch.load(out)
+    print(r)
+    assert r["fwd_equal"] and r["grad_equal"] and r["nograd_equal"]
