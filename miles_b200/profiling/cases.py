@@ -4,7 +4,10 @@
 
 cases: gemm_dense (8192x6144x2048 bf16 tcgen05 GEMM), gemm_grouped_decode (gate_up + SwiGLU of a
 64-token MoE decode step, 128 experts), attn_fwd (2 x 4096 tokens, 32 q / 4 kv heads), attn_bwd
-(same, backward), attn_decode (64 sequences x 4096 keys, paged).
+(same, backward), attn_decode (64 sequences x 4096 keys, paged), symm_ar_norm (one-rank group:
+GEMM storing into the symmetric staging + reduce/residual/RMSNorm kernel, 4096 x 2048 output),
+ep_dispatch_combine (one-rank expert-parallel layer through the peer-memory dispatch / combine
+kernels: 4096 tokens, top-8 of 128 experts, forward and backward).
 """
 import sys
 
@@ -51,5 +54,31 @@ elif case == "attn_decode":
     q = torch.randn(B, nq, 128, device='cuda', dtype=torch.bfloat16)
     lens = torch.full((B,), ctx, dtype=torch.int32, device='cuda')
     for _ in range(4): decode_attention(q, kc, vc, pt, lens)
+elif case in ("symm_ar_norm", "ep_dispatch_combine"):
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29731", rank=0, world_size=1)
+    if case == "symm_ar_norm":
+        from miles_b200.parallel.symm import SymmComm
+        H, K, M = 2048, 4096, 4096
+        comm = SymmComm(dist.group.WORLD, hidden=H, cap_rows=M)
+        a = torch.randn(M, K, device='cuda', dtype=torch.bfloat16)
+        w = torch.randn(H, K, device='cuda', dtype=torch.bfloat16) * 0.02
+        r = torch.randn(M, H, device='cuda', dtype=torch.bfloat16)
+        nw = torch.ones(H, device='cuda', dtype=torch.bfloat16)
+        for _ in range(3): comm.gemm_all_reduce(a, w, res=r, norm_w=nw, eps=1e-6)
+    else:
+        from miles_b200.ops.moe import RouterCfg
+        from miles_b200.parallel.ep import EPContext, moe_experts_ep
+        E, k, H, I, T = 128, 8, 2048, 768, 4096
+        ep = EPContext(dist.group.WORLD, E, "peer", H, k, cap_tokens=T)
+        x = torch.randn(T, H, device='cuda', dtype=torch.bfloat16, requires_grad=True)
+        rw = (torch.randn(E, H, device='cuda', dtype=torch.bfloat16) * 0.02).requires_grad_()
+        w1 = (torch.randn(E, 2 * I, H, device='cuda', dtype=torch.bfloat16) * 0.02).requires_grad_()
+        w2 = (torch.randn(E, H, I, device='cuda', dtype=torch.bfloat16) * 0.02).requires_grad_()
+        cfg = RouterCfg(E, k)
+        for _ in range(2):
+            y = moe_experts_ep(x, rw, w1, w2, cfg, ep)
+            y.backward(torch.ones_like(y))
+    dist.destroy_process_group()
 torch.cuda.synchronize()
 print("ok", case)
