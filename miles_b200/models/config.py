@@ -44,6 +44,10 @@ class ModelConfig:
     qk_nope_head_dim: int = 0
     qk_rope_head_dim: int = 0
     v_head_dim: int = 0
+    # DSA (DeepSeek-V3.2 / GLM-5 sparse attention): lightning indexer + top-k key selection
+    index_n_heads: int = 0
+    index_head_dim: int = 0
+    index_topk: int = 0
     extra: dict = field(default_factory=dict)
 
     @property
@@ -113,7 +117,7 @@ class ModelConfig:
             c.topk = d["num_experts_per_tok"]
             c.moe_intermediate_size = d["moe_intermediate_size"]
             c.norm_topk_prob = d.get("norm_topk_prob", True)
-        elif mt in ("deepseek_v3", "deepseek_v2", "kimi_k2", "glm4_moe_lite"):
+        elif mt in ("deepseek_v3", "deepseek_v2", "deepseek_v32", "kimi_k2", "glm4_moe_lite"):
             c.arch = "deepseek_v3"
             c.num_experts = d["n_routed_experts"]
             c.topk = d["num_experts_per_tok"]
@@ -131,6 +135,9 @@ class ModelConfig:
             c.qk_rope_head_dim = d.get("qk_rope_head_dim", 0)
             c.v_head_dim = d.get("v_head_dim", 0)
             c.qk_norm = False
+            c.index_n_heads = d.get("index_n_heads", 0)
+            c.index_head_dim = d.get("index_head_dim", 0)
+            c.index_topk = d.get("index_topk", 0)
         else:
             c.arch = "qwen3" if mt == "qwen3" else mt
             c.qk_norm = mt == "qwen3"
@@ -176,6 +183,14 @@ def preset(name: str) -> ModelConfig:
                            kv_lora_rank=64, qk_nope_head_dim=32, qk_rope_head_dim=16,
                            v_head_dim=32, qk_norm=False, routed_scaling_factor=2.5,
                            max_position=4096)
+    if n in ("tiny-dsa",):  # MLA + lightning indexer with top-k sparse attention (DSA)
+        return ModelConfig(arch="deepseek_v3", vocab_size=4096, hidden_size=256, num_layers=2,
+                           num_heads=4, num_kv_heads=4, head_dim=128, intermediate_size=512,
+                           num_experts=8, topk=2, moe_intermediate_size=128, num_shared_experts=1,
+                           first_k_dense=1, router_score="sigmoid", n_group=2, topk_group=1,
+                           kv_lora_rank=64, q_lora_rank=96, qk_nope_head_dim=32, qk_rope_head_dim=16,
+                           v_head_dim=32, qk_norm=False, routed_scaling_factor=2.5,
+                           index_n_heads=4, index_head_dim=32, index_topk=16, max_position=4096)
     if n in ("dsv3-small", "deepseek-v3-small"):
         # BASELINE config 5 shape: MLA + MoE, sigmoid grouped routing, shared experts
         return ModelConfig(arch="deepseek_v3", vocab_size=163840, hidden_size=2048, num_layers=27,

@@ -17,6 +17,14 @@ Decode and training compute the same function through different operation orders
 rollout log-probs are not bitwise equal to the trainer's (the importance-sampling corrections
 apply); the Qwen3 family keeps its bitwise parity.
 
+DSA (DeepSeek-V3.2 / GLM-5 sparse attention, when `index_topk` > 0): a lightning indexer scores
+every (query, key) pair as sum_h w[t, h] * relu(q_I[t, h] . k_I[s]) (q_I from the query latent,
+one LayerNorm'ed key k_I per token, per-head weights w from the hidden state), and each query
+attends only to its `index_topk` best-scoring causal keys. Training / prefill mask the dense
+attention to those keys; decode scores the cached indexer keys (stored next to the latent in the
+cache row) and masks the absorbed scores the same way. The top-k selection is discrete, so the
+indexer parameters get no gradient from the policy loss.
+
 Parameter names follow the HF DeepSeek-V3 layout (q_proj or q_a_proj / q_a_layernorm / q_b_proj,
 kv_a_proj_with_mqa, kv_a_layernorm, kv_b_proj, o_proj).
 
@@ -47,6 +55,15 @@ def mla_param_shapes(cfg, p: str, tp_size: int = 1):
                 (p + "q_b_proj.weight", (nh * (dn + dr), cfg.q_lora_rank), "normal")]
     else:
         out.append((p + "q_proj.weight", (nh * (dn + dr), H), "normal"))
+    if cfg.index_topk:  # DSA lightning indexer (replicated under TP)
+        if not cfg.q_lora_rank:
+            raise ValueError("the DSA indexer reads the low-rank query latent (q_lora_rank > 0)")
+        nI, dI = cfg.index_n_heads, cfg.index_head_dim
+        out += [(p + "indexer.wq_b.weight", (nI * dI, cfg.q_lora_rank), "normal"),
+                (p + "indexer.wk.weight", (dI, H), "normal"),
+                (p + "indexer.k_norm.weight", (dI,), "ones"),
+                (p + "indexer.k_norm.bias", (dI,), "zeros"),
+                (p + "indexer.weights_proj.weight", (nI, H), "normal")]
     out += [(p + "kv_a_proj_with_mqa.weight", (r + dr, H), "normal"),
             (p + "kv_a_layernorm.weight", (r,), "ones"),
             (p + "kv_b_proj.weight", (nh * (dn + dv), r), "normal"),
@@ -82,9 +99,54 @@ class MLA:
         self.scale = mscale * mscale / math.sqrt(cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
 
     # ------------------------------------------------------------------ projections
-    def _q(self, i: int, x: torch.Tensor, pos: torch.Tensor):
+    # ------------------------------------------------------------------ DSA indexer
+    def _index_q(self, i: int, qa: torch.Tensor, pos: torch.Tensor):
+        """Indexer queries [T, nI, dI] (rotary on the last qk_rope_head_dim dims)."""
+        cfg = self.cfg
+        p = f"layers.{i}.self_attn.indexer."
+        q = F.linear(qa.float(), self.m.params[p + "wq_b.weight"].float())
+        q = q.view(qa.shape[0], cfg.index_n_heads, cfg.index_head_dim)
+        return self._index_rope(q, pos)
+
+    def _index_k(self, i: int, x: torch.Tensor, pos: torch.Tensor):
+        """Indexer keys [T, dI] (LayerNorm, rotary on the last qk_rope_head_dim dims)."""
+        cfg, P = self.cfg, self.m.params
+        p = f"layers.{i}.self_attn.indexer."
+        k = F.linear(x.float(), P[p + "wk.weight"].float())
+        k = F.layer_norm(k, (cfg.index_head_dim,), P[p + "k_norm.weight"].float(),
+                         P[p + "k_norm.bias"].float(), 1e-6)
+        return self._index_rope(k, pos)
+
+    def _index_rope(self, t: torch.Tensor, pos: torch.Tensor):
+        dr = self.cfg.qk_rope_head_dim
+        return torch.cat([t[..., :-dr], _rope(t[..., -dr:], pos, self.cos, self.sin)], -1)
+
+    def _index_weights(self, i: int, x: torch.Tensor):
+        cfg = self.cfg
+        w = F.linear(x.float(), self.m.params[f"layers.{i}.self_attn.indexer.weights_proj.weight"].float())
+        return w * (cfg.index_n_heads ** -0.5) * (cfg.index_head_dim ** -0.5)
+
+    @staticmethod
+    def _index_scores(qI, wI, kI):
+        """[Tq, Tk] indexer scores sum_h w[t, h] relu(q_I[t, h] . k_I[s]), in fp64 so that the
+        training and decode forms (different contraction shapes) select the same keys except at
+        exact ties."""
+        qI, kI, wI = qI.double(), kI.double(), wI.double()
+        return torch.einsum("th,ths->ts", wI, torch.relu(torch.einsum("thd,sd->ths", qI, kI)))
+
+    def _topk_keep(self, scores: torch.Tensor, valid: torch.Tensor) -> torch.Tensor:
+        """Boolean mask of the index_topk best valid keys per query row."""
+        k = min(self.cfg.index_topk, scores.shape[-1])
+        sc = scores.masked_fill(~valid, float("-inf"))
+        # ties (e.g. keys whose relu terms are all zero) go to the earlier key, in every path
+        top = torch.sort(sc, dim=-1, descending=True, stable=True).indices[..., :k]
+        keep = torch.zeros_like(valid).scatter_(-1, top, True)
+        return keep & valid
+
+    def _q(self, i: int, x: torch.Tensor, pos: torch.Tensor, want_qa: bool = False):
         cfg, m = self.cfg, self.m
         p = f"layers.{i}.self_attn."
+        qa = None
         if cfg.q_lora_rank:
             qa = rms_norm(m._lin(x, p + "q_a_proj.weight"), m.params[p + "q_a_layernorm.weight"], cfg.rms_eps)
             q = m._lin(copy_to_tp(qa, m.tp), p + "q_b_proj.weight")
@@ -92,6 +154,8 @@ class MLA:
             q = m._lin(copy_to_tp(x, m.tp), p + "q_proj.weight")
         q = q.view(x.shape[0], self.nh, cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
         q_nope, q_pe = q.split([cfg.qk_nope_head_dim, cfg.qk_rope_head_dim], -1)
+        if want_qa:
+            return q_nope, _rope(q_pe, pos, self.cos, self.sin), qa
         return q_nope, _rope(q_pe, pos, self.cos, self.sin)
 
     def _latent(self, i: int, x: torch.Tensor, pos: torch.Tensor):
@@ -121,10 +185,16 @@ class MLA:
     def attn(self, i: int, x: torch.Tensor, meta, cache=None, slots=None, pending: bool = False):
         cfg = self.cfg
         pos = meta.positions
-        q_nope, q_pe = self._q(i, x, pos)
+        q_nope, q_pe, qa = self._q(i, x, pos, want_qa=True)
         c, k_pe = self._latent(i, x, pos)
+        dsa = cfg.index_topk > 0
+        if dsa:
+            with torch.no_grad():
+                qI, kI, wI = self._index_q(i, qa.detach(), pos), self._index_k(i, x.detach(), pos), \
+                    self._index_weights(i, x.detach())
         if cache is not None:
-            cache.k[i].index_copy_(0, slots, torch.cat([c, k_pe], -1).unsqueeze(1).to(cache.k[i].dtype))
+            row = [c, k_pe] + ([kI.to(c.dtype)] if dsa else [])
+            cache.k[i].index_copy_(0, slots, torch.cat(row, -1).unsqueeze(1).to(cache.k[i].dtype))
         k, v = self._expand(i, c, k_pe)
         q = torch.cat([q_nope, q_pe], -1)
         o = torch.empty(x.shape[0], self.nh, cfg.v_head_dim, dtype=x.dtype, device=x.device)
@@ -135,8 +205,14 @@ class MLA:
             if e == s:
                 continue
             qs, ks, vs = (t[s:e].transpose(0, 1).unsqueeze(0) for t in (q, k, v))
-            outs.append(F.scaled_dot_product_attention(qs, ks, vs, is_causal=True, scale=self.scale)
-                        [0].transpose(0, 1))
+            if dsa:
+                L = e - s
+                causal = torch.ones(L, L, dtype=torch.bool, device=x.device).tril()
+                keep = self._topk_keep(self._index_scores(qI[s:e], wI[s:e], kI[s:e]), causal)
+                o_b = F.scaled_dot_product_attention(qs, ks, vs, attn_mask=keep, scale=self.scale)
+            else:
+                o_b = F.scaled_dot_product_attention(qs, ks, vs, is_causal=True, scale=self.scale)
+            outs.append(o_b[0].transpose(0, 1))
         o = torch.cat(outs, 0) if outs else o
         return self._out(i, o.reshape(x.shape[0], -1), pending)
 
@@ -146,9 +222,13 @@ class MLA:
         cfg = self.cfg
         B = x.shape[0]
         nh, dn, dv, r = self.nh, cfg.qk_nope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
-        q_nope, q_pe = self._q(i, x, positions)
+        q_nope, q_pe, qa = self._q(i, x, positions, want_qa=True)
         c, k_pe = self._latent(i, x, positions)
-        cache.k[i].index_copy_(0, slots, torch.cat([c, k_pe], -1).unsqueeze(1).to(cache.k[i].dtype))
+        dsa = cfg.index_topk > 0
+        row = [c, k_pe]
+        if dsa:
+            row.append(self._index_k(i, x, positions).to(c.dtype))
+        cache.k[i].index_copy_(0, slots, torch.cat(row, -1).unsqueeze(1).to(cache.k[i].dtype))
         w = self.m.params[f"layers.{i}.self_attn.kv_b_proj.weight"].view(nh, dn + dv, r)
         w_uk, w_uv = w[:, :dn, :], w[:, dn:, :]
         q_lat = torch.einsum("bhn,hnc->bhc", q_nope.float(), w_uk.float())
@@ -156,10 +236,18 @@ class MLA:
         maxk = page_table.shape[1] * page
         t = torch.arange(maxk, device=x.device)
         rows = page_table.long()[:, t // page] * page + (t % page)[None, :]  # [B, maxk] cache rows
-        lat = cache.k[i][:, 0, :].index_select(0, rows.reshape(-1)).view(B, maxk, r + cfg.qk_rope_head_dim)
-        ck, kp = lat[..., :r].float(), lat[..., r:].float()
+        width = cache.k[i].shape[-1]
+        lat = cache.k[i][:, 0, :].index_select(0, rows.reshape(-1)).view(B, maxk, width)
+        ck, kp = lat[..., :r].float(), lat[..., r:r + cfg.qk_rope_head_dim].float()
         sc = (torch.einsum("bhc,btc->bht", q_lat, ck) + torch.einsum("bhd,btd->bht", q_pe.float(), kp)) * self.scale
-        sc = sc.masked_fill((t[None, :] >= ctx_lens[:, None].long())[:, None, :], float("-inf"))
+        valid = t[None, :] < ctx_lens[:, None].long()  # [B, maxk]
+        if dsa:
+            kI = lat[..., r + cfg.qk_rope_head_dim:].float()                       # [B, maxk, dI]
+            qI, wI = self._index_q(i, qa, positions), self._index_weights(i, x)   # [B, nI, dI], [B, nI]
+            qI, kI, wI = qI.double(), kI.double(), wI.double()
+            scI = torch.einsum("bh,bhs->bs", wI, torch.relu(torch.einsum("bhd,bsd->bhs", qI, kI)))
+            valid = self._topk_keep(scI, valid)
+        sc = sc.masked_fill(~valid[:, None, :], float("-inf"))
         pr = torch.softmax(sc, -1)
         o_lat = torch.einsum("bht,btc->bhc", pr, ck)
         o = torch.einsum("bhc,hvc->bhv", o_lat, w_uv.float()).to(x.dtype)

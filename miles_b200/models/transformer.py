@@ -118,8 +118,8 @@ FLAT_ALIGN = 8192
 def kv_cache_shape(cfg: ModelConfig, tp_size: int = 1) -> tuple[int, int]:
     """(heads, dim) of one cached token per layer: GQA K and V (this TP rank's KV heads), or the
     MLA latent [c | k_pe] (replicated over TP ranks)."""
-    if cfg.kv_lora_rank:
-        return 1, cfg.kv_lora_rank + cfg.qk_rope_head_dim
+    if cfg.kv_lora_rank:  # + the DSA indexer key when the model has one
+        return 1, cfg.kv_lora_rank + cfg.qk_rope_head_dim + (cfg.index_head_dim if cfg.index_topk else 0)
     return cfg.num_kv_heads // tp_size, cfg.head_dim
 
 

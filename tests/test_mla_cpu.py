@@ -69,3 +69,40 @@ def test_mla_grpo_step(tmp_path, monkeypatch):
                        "--use-tis", "--use-rollout-routing-replay"])
     hist = T.train(args)
     assert len(hist) == 1 and np.isfinite(hist[0]["train/pg_loss"])
+
+
+def test_dsa_decode_matches_full_forward_and_sparsifies():
+    """DSA (MLA + lightning indexer top-k): engine decode through the latent + indexer-key cache
+    reproduces the full forward, and the top-k selection changes the output once sequences are
+    longer than index_topk."""
+    import dataclasses
+
+    from miles_b200.engine.engine import GenRequest, RolloutEngine
+    from miles_b200.ops.attention import VarlenMeta
+
+    cfg = preset("tiny-dsa")
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=0)
+    assert "layers.0.self_attn.indexer.wq_b.weight" in m.params
+    eng = RolloutEngine(m, max_batch=4, num_pages=64, max_pages_per_seq=8, use_cuda_graph=False)
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(0, cfg.vocab_size, n).tolist() for n in (9, 70)]
+    outs = eng.generate([GenRequest(p, 6, temperature=0.0, rid=i) for i, p in enumerate(prompts)])
+    for p, o in zip(prompts, outs):
+        toks = p + o.tokens
+        with torch.no_grad():
+            h = m.forward_train(torch.tensor(toks, dtype=torch.int32), VarlenMeta([0, len(toks)], "cpu"))
+        logits = h.float() @ m.lm_head_weight().float().t()
+        assert logits[len(p) - 1:len(toks) - 1].argmax(-1).tolist() == o.tokens
+        lp = torch.log_softmax(logits[len(p) - 1:len(toks) - 1], -1)
+        ref = lp.gather(1, torch.tensor(o.tokens)[:, None])[:, 0].detach().numpy()
+        assert np.abs(ref - np.asarray(o.logprobs)).max() < 1e-3
+    # dense attention (top-k >= length) gives a different function on the long sequence
+    dense = Transformer(dataclasses.replace(cfg, index_topk=4096), device="cpu", dtype=torch.float32,
+                        materialize=False)
+    dense.flat.copy_(m.flat)
+    t = torch.tensor(prompts[1], dtype=torch.int32)
+    with torch.no_grad():
+        a = m.forward_train(t, VarlenMeta([0, len(t)], "cpu"))
+        b = dense.forward_train(t, VarlenMeta([0, len(t)], "cpu"))
+    assert torch.allclose(a[:16], b[:16], atol=1e-5)       # first 16 queries see <= 16 keys
+    assert (a[20:] - b[20:]).abs().max() > 1e-4
