@@ -37,7 +37,11 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
         L = f"layers.{i}."
         yield pre + L + "input_layernorm.weight", P[L + "input_layernorm.weight"].data
         yield pre + L + "post_attention_layernorm.weight", P[L + "post_attention_layernorm.weight"].data
-        if cfg.kv_lora_rank:  # MLA parameters carry their HF names already
+        if cfg.layer_is_linear(i):  # Gated DeltaNet parameters carry their HF names
+            for n in P:
+                if n.startswith(L + "linear_attn."):
+                    yield pre + n, P[n].data
+        elif cfg.kv_lora_rank:  # MLA parameters carry their HF names already
             for n in P:
                 if n.startswith(L + "self_attn."):
                     yield pre + n, P[n].data
@@ -48,7 +52,7 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
             yield pre + L + "self_attn.k_proj.weight", k
             yield pre + L + "self_attn.v_proj.weight", v
             yield pre + L + "self_attn.o_proj.weight", P[L + "self_attn.o_proj.weight"].data
-        if cfg.qk_norm and not cfg.kv_lora_rank:
+        if cfg.qk_norm and not cfg.kv_lora_rank and not cfg.layer_is_linear(i):
             yield pre + L + "self_attn.q_norm.weight", P[L + "self_attn.q_norm.weight"].data
             yield pre + L + "self_attn.k_norm.weight", P[L + "self_attn.k_norm.weight"].data
         if cfg.layer_is_moe(i):

@@ -56,7 +56,7 @@ class GenResult:
 
 
 class _Seq:
-    __slots__ = ("req", "pages", "out", "lps", "pos", "done", "reason", "experts")
+    __slots__ = ("req", "pages", "out", "lps", "pos", "done", "reason", "experts", "wave_idx")
 
     def __init__(self, req: GenRequest, pages: list[int]):
         self.req = req
@@ -67,6 +67,7 @@ class _Seq:
         self.done = False
         self.reason = ""
         self.experts: list[np.ndarray] = []
+        self.wave_idx = 0  # row of this sequence in the linear-attention state cache
 
 
 class RolloutEngine:
@@ -108,7 +109,8 @@ class RolloutEngine:
             else:
                 n = 1024
         n = max(n, 2)
-        self.cache = KVCache(self.cfg, n, self.dev, self.model.dtype, self.model.tp_size)
+        self.cache = KVCache(self.cfg, n, self.dev, self.model.dtype, self.model.tp_size,
+                             max_seqs=self.max_batch + 1)
         self.free_pages = list(range(n - 1, 0, -1))  # page 0 = trash page for padded rows
 
     def release_memory(self):
@@ -137,12 +139,15 @@ class RolloutEngine:
             "inv_t": torch.ones(B, dtype=torch.float32, device=dev),
             "seeds": torch.zeros(B, dtype=torch.int64, device=dev),
             "experts": torch.zeros(B, max(self.n_moe, 1), max(self.cfg.topk, 1), dtype=torch.int32, device=dev),
+            # linear-attention state row of every batch row (padding rows: the spare last row)
+            "state_rows": torch.full((B,), self.max_batch, dtype=torch.int64, device=dev),
         }
 
     def _step_fn(self, st):
         rec = []
         h = self.model.forward_decode(st["tokens"], st["positions"], self.cache, st["pt"], st["ctx"],
-                                      st["slots"], record=rec if self.n_moe else None)
+                                      st["slots"], record=rec if self.n_moe else None,
+                                      state_rows=st["state_rows"])
         for j, idx in enumerate(rec):
             st["experts"][:, j].copy_(idx)
         # the sampled token sits at position `positions + 1`
@@ -214,6 +219,8 @@ class RolloutEngine:
 
     def _run_wave(self, wave: list[_Seq]) -> int:
         dev = self.dev
+        for j, s in enumerate(wave):
+            s.wave_idx = j  # linear-attention state row of this sequence
         # ---- prefill (packed)
         cu = [0]
         toks, slots = [], []
@@ -228,7 +235,8 @@ class RolloutEngine:
             torch.cuda.nvtx.range_push("prefill")
         h = self.model.forward_prefill(torch.tensor(toks, dtype=torch.int32, device=dev), meta,
                                        self.cache, torch.tensor(slots, dtype=torch.int64, device=dev),
-                                       record=rec)
+                                       record=rec,
+                                       state_rows=torch.arange(len(wave), dtype=torch.int64, device=dev))
         last = torch.tensor([c - 1 for c in cu[1:]], dtype=torch.long, device=dev)
         B = len(wave)
         inv_t = torch.tensor([1.0 / s.req.temperature if s.req.temperature > 0 else 0.0 for s in wave],
@@ -261,7 +269,9 @@ class RolloutEngine:
             pt = np.zeros((Bb, self.max_pages_per_seq), np.int32)
             invt = np.ones(Bb, np.float32)
             seed = np.zeros(Bb, np.int64)
+            srow = np.full(Bb, self.max_batch, np.int64)
             for j, s in enumerate(live):
+                srow[j] = s.wave_idx
                 p = s.pos - 1 + 1  # position of the token being fed = last written + 1
                 p = len(s.req.prompt) + len(s.out) - 1
                 tokens[j] = s.out[-1]
@@ -278,6 +288,7 @@ class RolloutEngine:
             st["pt"].copy_(torch.from_numpy(pt), non_blocking=True)
             st["inv_t"].copy_(torch.from_numpy(invt), non_blocking=True)
             st["seeds"].copy_(torch.from_numpy(seed), non_blocking=True)
+            st["state_rows"].copy_(torch.from_numpy(srow), non_blocking=True)
             if nvtx:
                 torch.cuda.nvtx.range_push("decode_step")
             if g is not None:

@@ -48,11 +48,22 @@ class ModelConfig:
     index_n_heads: int = 0
     index_head_dim: int = 0
     index_topk: int = 0
+    # Gated DeltaNet hybrid (Qwen3-Next): every `linear_attn_interval`-th layer keeps softmax
+    # attention, the others are linear attention (0 = no linear layers)
+    linear_attn_interval: int = 0
+    linear_num_key_heads: int = 0
+    linear_num_value_heads: int = 0
+    linear_key_head_dim: int = 0
+    linear_value_head_dim: int = 0
+    linear_conv_kernel: int = 4
     extra: dict = field(default_factory=dict)
 
     @property
     def is_moe(self) -> bool:
         return self.num_experts > 0
+
+    def layer_is_linear(self, i: int) -> bool:
+        return self.linear_attn_interval > 0 and (i + 1) % self.linear_attn_interval != 0
 
     def layer_is_moe(self, i: int) -> bool:
         return self.is_moe and i >= self.first_k_dense and (i - self.first_k_dense) % self.moe_layer_freq == 0
@@ -111,6 +122,19 @@ class ModelConfig:
         c.rope_scaling = d.get("rope_scaling")
         c.max_position = d.get("max_position_embeddings", 32768)
         c.tie_embeddings = d.get("tie_word_embeddings", False)
+        if mt == "qwen3_next":
+            c.arch = "qwen3_next"
+            c.num_experts = d.get("num_experts", 0)
+            c.topk = d.get("num_experts_per_tok", 0)
+            c.moe_intermediate_size = d.get("moe_intermediate_size", 0)
+            c.norm_topk_prob = d.get("norm_topk_prob", True)
+            c.linear_attn_interval = d.get("full_attention_interval", 4)
+            c.linear_num_key_heads = d["linear_num_key_heads"]
+            c.linear_num_value_heads = d["linear_num_value_heads"]
+            c.linear_key_head_dim = d["linear_key_head_dim"]
+            c.linear_value_head_dim = d["linear_value_head_dim"]
+            c.linear_conv_kernel = d.get("linear_conv_kernel_dim", 4)
+            return c
         if mt in ("qwen3_moe",):
             c.arch = "qwen3_moe"
             c.num_experts = d["num_experts"]
@@ -183,6 +207,12 @@ def preset(name: str) -> ModelConfig:
                            kv_lora_rank=64, qk_nope_head_dim=32, qk_rope_head_dim=16,
                            v_head_dim=32, qk_norm=False, routed_scaling_factor=2.5,
                            max_position=4096)
+    if n in ("tiny-gdn",):  # Gated DeltaNet hybrid: layers 0-2 linear attention, layer 3 softmax
+        return ModelConfig(arch="qwen3_next", vocab_size=4096, hidden_size=256, num_layers=4,
+                           num_heads=4, num_kv_heads=2, head_dim=64, intermediate_size=512,
+                           tie_embeddings=True, max_position=4096, linear_attn_interval=4,
+                           linear_num_key_heads=2, linear_num_value_heads=4,
+                           linear_key_head_dim=32, linear_value_head_dim=32)
     if n in ("tiny-dsa",):  # MLA + lightning indexer with top-k sparse attention (DSA)
         return ModelConfig(arch="deepseek_v3", vocab_size=4096, hidden_size=256, num_layers=2,
                            num_heads=4, num_kv_heads=4, head_dim=128, intermediate_size=512,

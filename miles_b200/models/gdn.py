@@ -1,0 +1,163 @@
+"""Gated DeltaNet linear attention (Qwen3-Next-style hybrid models).
+
+Layers with `cfg.layer_is_linear(i)` replace softmax attention by a gated delta rule with a
+fixed-size recurrent state per head (keys -> values, [dk, dv]):
+
+    qkvz = x W_qkvz^T  (q, k: nk heads of dk; v, z: nv heads of dv),   (b, a) = x W_ba^T
+    q, k, v <- SiLU(causal depthwise conv1d over time, kernel K)          (channels of q, k, v)
+    q, k    <- L2-normalised per head, repeated to the nv value heads
+    beta = sigmoid(b),  g = -exp(A_log) * softplus(a + dt_bias)           (log decay per step)
+    S_t = exp(g_t) S_{t-1};  S_t += k_t (beta_t (v_t - S_t^T k_t))^T;  o_t = S_t^T q_t / sqrt(dk)
+    out = W_out (RMSNorm(o) * w_norm * SiLU(z))
+
+Training and prefill run the recurrence over each packed sequence from a zero state; the rollout
+engine keeps, per live sequence, the last K-1 conv inputs and the state S (`KVCache.lin_conv`,
+`KVCache.lin_state`, one row per engine batch slot) and advances them one token per decode step,
+so decode reproduces the training forward. This is a PyTorch implementation (fp32 recurrence);
+there is no sm_100a kernel for it yet.
+
+Parameter names follow HF Qwen3-Next (`linear_attn.*`), except that in_proj_qkvz holds
+[q; k; v; z] as contiguous blocks (HF interleaves them per key-head group) and conv1d.weight is
+stored [C, K] (HF [C, 1, K]).
+
+Reference: miles_plugins/models/qwen3_next.py (fla chunked gated delta rule through Triton) and
+qwen3_5.py; E14 in the kernel inventory.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+def gdn_param_shapes(cfg, p: str):
+    H = cfg.hidden_size
+    nk, nv, dk, dv, K = (cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim,
+                         cfg.linear_value_head_dim, cfg.linear_conv_kernel)
+    C = 2 * nk * dk + nv * dv
+    return [(p + "in_proj_qkvz.weight", (2 * nk * dk + 2 * nv * dv, H), "normal"),
+            (p + "in_proj_ba.weight", (2 * nv, H), "normal"),
+            (p + "conv1d.weight", (C, K), "normal"),
+            (p + "dt_bias", (nv,), "ones"),
+            (p + "A_log", (nv,), "zeros"),
+            (p + "norm.weight", (dv,), "ones"),
+            (p + "out_proj.weight", (H, nv * dv), "normal")]
+
+
+def gdn_state_shapes(cfg):
+    """(conv state [C, K-1], recurrent state [nv, dk, dv]) of one sequence in one layer."""
+    nk, nv, dk, dv, K = (cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim,
+                         cfg.linear_value_head_dim, cfg.linear_conv_kernel)
+    return (2 * nk * dk + nv * dv, K - 1), (nv, dk, dv)
+
+
+class GDN:
+    def __init__(self, model):
+        self.m = model
+        self.cfg = cfg = model.cfg
+        self.nk, self.nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+        self.dk, self.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        self.K = cfg.linear_conv_kernel
+        if self.nv % self.nk:
+            raise ValueError("linear value heads must be a multiple of the key heads")
+
+    def _p(self, i, name):
+        return self.m.params[f"layers.{i}.linear_attn.{name}"]
+
+    def _project(self, i, x):
+        nk, nv, dk, dv = self.nk, self.nv, self.dk, self.dv
+        qkvz = self.m._lin(x, f"layers.{i}.linear_attn.in_proj_qkvz.weight").float()
+        mixed, z = qkvz.split([2 * nk * dk + nv * dv, nv * dv], -1)
+        ba = self.m._lin(x, f"layers.{i}.linear_attn.in_proj_ba.weight").float()
+        b, a = ba.split([nv, nv], -1)
+        beta = torch.sigmoid(b)
+        g = -torch.exp(self._p(i, "A_log").float()) * F.softplus(a + self._p(i, "dt_bias").float())
+        return mixed, z, beta, g
+
+    def _conv(self, i, mixed, state):
+        """Causal depthwise conv + SiLU of [T, C] given the previous K-1 inputs [C, K-1]."""
+        w = self._p(i, "conv1d.weight").float()                  # [C, K]
+        padded = torch.cat([state.t(), mixed], 0)                # [K-1+T, C]
+        T = mixed.shape[0]
+        out = sum(w[:, j] * padded[j:j + T] for j in range(self.K))
+        return F.silu(out), padded[-(self.K - 1):].t().contiguous()
+
+    def _heads(self, conv):
+        nk, nv, dk, dv = self.nk, self.nv, self.dk, self.dv
+        q, k, v = conv.split([nk * dk, nk * dk, nv * dv], -1)
+        T = conv.shape[0]
+        r = nv // nk
+        q = F.normalize(q.view(T, nk, dk), dim=-1).repeat_interleave(r, 1)
+        k = F.normalize(k.view(T, nk, dk), dim=-1).repeat_interleave(r, 1)
+        return q, k, v.view(T, nv, dv)
+
+    def _recur(self, q, k, v, beta, g, S):
+        """Gated delta rule over T steps from state S [nv, dk, dv]; returns (o [T, nv, dv], S)."""
+        scale = 1.0 / math.sqrt(self.dk)
+        outs = []
+        for t in range(q.shape[0]):
+            S = S * torch.exp(g[t])[:, None, None]
+            err = v[t] - torch.einsum("hk,hkv->hv", k[t], S)
+            S = S + k[t][:, :, None] * (beta[t][:, None] * err)[:, None, :]
+            outs.append(torch.einsum("hk,hkv->hv", q[t], S) * scale)
+        return torch.stack(outs, 0), S
+
+    def _out(self, i, o, z, dtype):
+        T = o.shape[0]
+        o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + self.cfg.rms_eps)
+        o = o * self._p(i, "norm.weight").float() * F.silu(z.view(T, self.nv, self.dv))
+        return self.m._lin(o.reshape(T, -1).to(dtype), f"layers.{i}.linear_attn.out_proj.weight")
+
+    def _zero_states(self, device):
+        (C, Km1), (nv, dk, dv) = gdn_state_shapes(self.cfg)
+        return (torch.zeros(C, Km1, dtype=torch.float32, device=device),
+                torch.zeros(nv, dk, dv, dtype=torch.float32, device=device))
+
+    # ------------------------------------------------------------------ training / prefill
+    def attn(self, i: int, x: torch.Tensor, meta, cache=None, state_rows=None) -> torch.Tensor:
+        """Packed sequences from zero states; with `cache` the final states of sequence b are
+        written to row state_rows[b]."""
+        mixed, z, beta, g = self._project(i, x)
+        outs = []
+        cu = meta.cu_list
+        for b in range(len(cu) - 1):
+            s, e = cu[b], cu[b + 1]
+            if e == s:
+                continue
+            cst, S = self._zero_states(x.device)
+            conv, cst = self._conv(i, mixed[s:e], cst)
+            q, k, v = self._heads(conv)
+            o, S = self._recur(q, k, v, beta[s:e], g[s:e], S)
+            outs.append(o)
+            if cache is not None:
+                row = int(state_rows[b])
+                cache.lin_conv[i][row].copy_(cst)
+                cache.lin_state[i][row].copy_(S)
+        o = torch.cat(outs, 0)
+        return self._out(i, o, z, x.dtype)
+
+    # ------------------------------------------------------------------ decode
+    def decode(self, i: int, x: torch.Tensor, cache, state_rows: torch.Tensor) -> torch.Tensor:
+        """One token per row; advances the states in rows `state_rows` of the cache."""
+        mixed, z, beta, g = self._project(i, x)                  # [B, ...]
+        rows = state_rows.long()
+        cst = cache.lin_conv[i].index_select(0, rows)            # [B, C, K-1]
+        S = cache.lin_state[i].index_select(0, rows)             # [B, nv, dk, dv]
+        w = self._p(i, "conv1d.weight").float()
+        window = torch.cat([cst, mixed[:, :, None]], -1)         # [B, C, K]
+        conv = F.silu((window * w[None]).sum(-1))
+        B = x.shape[0]
+        nk, nv, dk, dv = self.nk, self.nv, self.dk, self.dv
+        q, k, v = conv.split([nk * dk, nk * dk, nv * dv], -1)
+        r = nv // nk
+        q = F.normalize(q.view(B, nk, dk), dim=-1).repeat_interleave(r, 1)
+        k = F.normalize(k.view(B, nk, dk), dim=-1).repeat_interleave(r, 1)
+        v = v.view(B, nv, dv)
+        S = S * torch.exp(g)[:, :, None, None]
+        err = v - torch.einsum("bhk,bhkv->bhv", k, S)
+        S = S + k[:, :, :, None] * (beta[:, :, None] * err)[:, :, None, :]
+        o = torch.einsum("bhk,bhkv->bhv", q, S) / math.sqrt(dk)
+        cache.lin_conv[i].index_copy_(0, rows, window[:, :, 1:].contiguous())
+        cache.lin_state[i].index_copy_(0, rows, S)
+        return self._out(i, o, z, x.dtype)

@@ -67,7 +67,11 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=Non
     for i in layers:
         p = f"layers.{i}."
         specs.append(ParamSpec(p + "input_layernorm.weight", (H,), "ones"))
-        if cfg.kv_lora_rank:  # multi-head latent attention (models/mla.py)
+        if cfg.layer_is_linear(i):  # Gated DeltaNet linear attention (models/gdn.py)
+            from miles_b200.models.gdn import gdn_param_shapes
+
+            specs += [ParamSpec(n, shp, init) for n, shp, init in gdn_param_shapes(cfg, p + "linear_attn.")]
+        elif cfg.kv_lora_rank:  # multi-head latent attention (models/mla.py)
             from miles_b200.models.mla import mla_param_shapes
 
             specs += [ParamSpec(n, shp, init) for n, shp, init in mla_param_shapes(cfg, p + "self_attn.", t)]
@@ -75,7 +79,7 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=Non
             specs += [ParamSpec(p + "self_attn.qkv_proj.weight", ((nq + 2 * nkv) * D, H), "normal"),
                       ParamSpec(p + "self_attn.o_proj.weight", (H, nq * D), "normal")]
         specs.append(ParamSpec(p + "post_attention_layernorm.weight", (H,), "ones"))
-        if cfg.qk_norm and not cfg.kv_lora_rank:
+        if cfg.qk_norm and not cfg.kv_lora_rank and not cfg.layer_is_linear(i):
             specs += [ParamSpec(p + "self_attn.q_norm.weight", (D,), "ones"),
                       ParamSpec(p + "self_attn.k_norm.weight", (D,), "ones")]
         if cfg.layer_is_moe(i):
@@ -131,18 +135,31 @@ class KVCache:
     they must hold finite values."""
 
     def __init__(self, cfg: ModelConfig, num_pages: int, device, dtype=torch.bfloat16,
-                 tp_size: int = 1):
+                 tp_size: int = 1, max_seqs: int = 0):
         self.num_pages = num_pages
         slots = num_pages * PAGE
         nkv, hd = kv_cache_shape(cfg, tp_size)
-        self.k = [torch.zeros(slots, nkv, hd, dtype=dtype, device=device)
-                  for _ in range(cfg.num_layers)]
+        lin = [cfg.layer_is_linear(i) for i in range(cfg.num_layers)]
+        self.k = [torch.zeros(0 if lin[i] else slots, nkv, hd, dtype=dtype, device=device)
+                  for i in range(cfg.num_layers)]
         # MLA caches only the latent (+ rotary key) in `k`
         vs = 1 if cfg.kv_lora_rank else slots
-        self.v = [torch.zeros(vs, nkv, hd, dtype=dtype, device=device) for _ in range(cfg.num_layers)]
+        self.v = [torch.zeros(0 if lin[i] else vs, nkv, hd, dtype=dtype, device=device)
+                  for i in range(cfg.num_layers)]
+        # linear-attention layers: conv + recurrent state per engine batch slot (fp32)
+        self.lin_conv, self.lin_state = [None] * cfg.num_layers, [None] * cfg.num_layers
+        if any(lin):
+            from miles_b200.models.gdn import gdn_state_shapes
+
+            cs, ss = gdn_state_shapes(cfg)
+            for i in range(cfg.num_layers):
+                if lin[i]:
+                    self.lin_conv[i] = torch.zeros((max_seqs,) + cs, dtype=torch.float32, device=device)
+                    self.lin_state[i] = torch.zeros((max_seqs,) + ss, dtype=torch.float32, device=device)
 
     def nbytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in self.k + self.v)
+        ts = self.k + self.v + [t for t in self.lin_conv + self.lin_state if t is not None]
+        return sum(t.numel() * t.element_size() for t in ts)
 
 
 class Transformer(torch.nn.Module):
@@ -234,6 +251,13 @@ class Transformer(torch.nn.Module):
         self.recompute = True
         self.weight_version = 0
         self.lora = None  # miles_b200.models.lora.LoRA when adapters are attached
+        self.gdn = None
+        if cfg.linear_attn_interval:
+            from miles_b200.models.gdn import GDN
+
+            if self.tp is not None or self.cp is not None or self.sequence_parallel:
+                raise ValueError("linear-attention layers run without TP / CP")
+            self.gdn = GDN(self)
         self.mla = None
         if cfg.kv_lora_rank:
             from miles_b200.models.mla import MLA
@@ -281,6 +305,8 @@ class Transformer(torch.nn.Module):
     # -------------------------------------------------------------------------------- blocks
     def _attn_train(self, i: int, x: torch.Tensor, meta: VarlenMeta) -> torch.Tensor:
         cfg = self.cfg
+        if self.gdn is not None and cfg.layer_is_linear(i):
+            return self.gdn.attn(i, x, meta)
         if self.mla is not None:
             return self.mla.attn(i, x, meta)
         pre = f"layers.{i}.self_attn."
@@ -569,8 +595,10 @@ class Transformer(torch.nn.Module):
 
     @torch.no_grad()
     def forward_prefill(self, tokens: torch.Tensor, meta: VarlenMeta, cache: KVCache,
-                        slots: torch.Tensor, record: list | None = None) -> torch.Tensor:
-        """Packed prompt prefill. Writes K/V of every token to cache rows `slots` (int64 [T]).
+                        slots: torch.Tensor, record: list | None = None,
+                        state_rows: torch.Tensor | None = None) -> torch.Tensor:
+        """Packed prompt prefill. Writes K/V of every token to cache rows `slots` (int64 [T])
+        (linear-attention layers: the final states of sequence b to row state_rows[b]).
         Returns the final hidden of every token [T, H]."""
         cfg = self.cfg
         r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
@@ -580,7 +608,9 @@ class Transformer(torch.nn.Module):
             x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if pend is None else self._add_norm(pend, r, ln1)
             pre = f"layers.{i}.self_attn."
             post = self.params[f"layers.{i}.post_attention_layernorm.weight"]
-            if self.mla is not None:
+            if self.gdn is not None and cfg.layer_is_linear(i):
+                x2, r = self._add_norm(self.gdn.attn(i, x, meta, cache, state_rows), r, post)
+            elif self.mla is not None:
                 x2, r = self._add_norm(self.mla.attn(i, x, meta, cache, slots, pending=True), r, post)
             else:
                 qkv = self._lin(x, pre + "qkv_proj.weight")
@@ -601,7 +631,7 @@ class Transformer(torch.nn.Module):
     @torch.no_grad()
     def forward_decode(self, tokens: torch.Tensor, positions: torch.Tensor, cache: KVCache,
                        page_table: torch.Tensor, ctx_lens: torch.Tensor, slots: torch.Tensor,
-                       record: list | None = None) -> torch.Tensor:
+                       record: list | None = None, state_rows: torch.Tensor | None = None) -> torch.Tensor:
         """One token per sequence. tokens int [B]; positions int32 [B]; slots int64 [B]
         (cache row of the new token); ctx_lens int32 [B] = positions + 1. Returns hidden [B,H]."""
         cfg = self.cfg
@@ -613,7 +643,9 @@ class Transformer(torch.nn.Module):
             x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if pend is None else self._add_norm(pend, r, ln1)
             pre = f"layers.{i}.self_attn."
             post = self.params[f"layers.{i}.post_attention_layernorm.weight"]
-            if self.mla is not None:
+            if self.gdn is not None and cfg.layer_is_linear(i):
+                a = self.gdn.decode(i, x, cache, state_rows)
+            elif self.mla is not None:
                 a = self.mla.decode(i, x, positions, cache, page_table, ctx_lens, slots, pending=True)
             else:
                 qkv = self._lin(x, pre + "qkv_proj.weight")
