@@ -222,22 +222,34 @@ struct RowShape {
   static_assert(NCH % CPT == 0 && NT % 32 == 0, "unsupported hidden size");
 };
 
+// ROWS rows per CTA at once (NT threads each, the per-row thread assignment and reduction tree
+// of rmsnorm_fwd_kernel), so short rows still keep enough loads in flight.
 template <int H>
-__global__ void __launch_bounds__(RowShape<H>::NT) symm_allreduce_norm_kernel(ReduceArgs a) {
+struct RowTile {
+  static constexpr int ROWS = RowShape<H>::NT >= 512 ? 1 : 512 / RowShape<H>::NT;
+  static constexpr int THREADS = ROWS * RowShape<H>::NT;
+};
+
+template <int H>
+__global__ void __launch_bounds__(RowTile<H>::THREADS) symm_allreduce_norm_kernel(ReduceArgs a) {
   pdl_trigger();
   pdl_wait();
   using S = RowShape<H>;
   constexpr int NW = S::NT / 32;
-  __shared__ float wsum[NW];
+  constexpr int ROWS = RowTile<H>::ROWS;
+  __shared__ float wsum[ROWS][NW];
   const int e = *reinterpret_cast<volatile int*>(a.ctl) + 1;
   const int par = (e - 1) & 1;
   if (a.src) push_and_announce(a, par, e);
   else if (blockIdx.x == 0) announce(a.flags, a.rank, a.world, e);
-  const int tid = threadIdx.x;
+  const int sub = threadIdx.x / S::NT;  // which of the CTA's rows
+  const int tid = threadIdx.x % S::NT;  // thread within the row
   if (wait_all(a.my_flags, a.world, e, a.timeout_ns, a.err)) {
     const long long slot = a.cap * H;
     const __nv_bfloat16* base = a.my_stage + (long long)par * a.world * slot;
-    for (int row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    for (int row0 = blockIdx.x * ROWS; row0 < a.rows; row0 += gridDim.x * ROWS) {
+      const int row = row0 + sub;
+      const bool active = row < a.rows;
       const long long rb = (long long)row * H;
       float v[S::CPT * 8];
 #pragma unroll
@@ -246,13 +258,15 @@ __global__ void __launch_bounds__(RowShape<H>::NT) symm_allreduce_norm_kernel(Re
         float acc[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-        for (int r = 0; r < a.world; ++r) {
-          const uint4 x = ld_volatile_v4(base + r * slot + rb + col);
-          const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&x);
+        if (active) {
+          for (int r = 0; r < a.world; ++r) {
+            const uint4 x = ld_volatile_v4(base + r * slot + rb + col);
+            const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&x);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) acc[k] += __bfloat162float(xb[k]);
+            for (int k = 0; k < 8; ++k) acc[k] += __bfloat162float(xb[k]);
+          }
         }
-        if (a.res) {
+        if (a.res && active) {
           const uint4 rr = *reinterpret_cast<const uint4*>(a.res + rb + col);
           const __nv_bfloat16* rbf = reinterpret_cast<const __nv_bfloat16*>(&rr);
           uint4 o;
@@ -273,12 +287,13 @@ __global__ void __launch_bounds__(RowShape<H>::NT) symm_allreduce_norm_kernel(Re
 #pragma unroll
       for (int i = 0; i < S::CPT * 8; ++i) ss += v[i] * v[i];
       ss = warp_sum(ss);
-      if ((tid & 31) == 0) wsum[tid >> 5] = ss;
+      if ((tid & 31) == 0) wsum[sub][tid >> 5] = ss;
       __syncthreads();
       float tot = 0.f;
 #pragma unroll
-      for (int i = 0; i < NW; ++i) tot += wsum[i];
-      __syncthreads();  // wsum is reused by the next row
+      for (int i = 0; i < NW; ++i) tot += wsum[sub][i];
+      __syncthreads();  // wsum is reused by the next rows
+      if (!active) continue;
       const float rstd = rsqrtf(tot / (float)H + a.eps);
       if (tid == 0 && a.rstd_out) a.rstd_out[row] = rstd;
 #pragma unroll
@@ -357,10 +372,25 @@ static Peers to_peers(const long long* ptrs, int n) {
 }
 
 // Every CTA of a collective must be resident at once (a CTA waits for announcements that other
-// CTAs of the peers' grids make), so grids are capped at two CTAs per SM.
-static int coll_grid(long long work, int per_cta) {
+// CTAs of the peers' grids make), so a grid never exceeds what the GPU holds at once: the
+// occupancy of the kernel at its block size times the SM count, at most 2 CTAs per SM (other
+// work sharing the GPU keeps room), at least one per SM.
+template <typename K>
+static int coll_grid(K kernel, int block, long long work, int per_cta) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  int occ = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, block, 0) != cudaSuccess || occ < 1)
+    occ = 1;
+  if (occ > 2) occ = 2;
   long long g = (work + per_cta - 1) / per_cta;
-  if (g > 2 * 148) g = 2 * 148;
+  const long long cap = (long long)occ * sms;
+  if (g > cap) g = cap;
   return (int)(g < 1 ? 1 : g);
 }
 
@@ -475,14 +505,19 @@ int mb_symm_collective(int kind, const long long* flag_ptrs, const long long* st
   a.timeout_ns = timeout_ns; a.err = err;
   a.scatter_rows = kind == 1;
   if (kind == 2) {
-    mb_launch(symm_allgather_kernel, coll_grid((long long)rows * H / 8 * world, 256 * 4), 256, 0, st, a);
+    mb_launch(symm_allgather_kernel, coll_grid(symm_allgather_kernel, 256, (long long)rows * H / 8 * world, 256 * 4),
+              256, 0, st, a);
   } else if (!norm_w) {
-    mb_launch(symm_allreduce_kernel, coll_grid((long long)rows * H / 8, 256 * 4), 256, 0, st, a);
+    mb_launch(symm_allreduce_kernel, coll_grid(symm_allreduce_kernel, 256, (long long)rows * H / 8, 256 * 4),
+              256, 0, st, a);
   } else {
     if (res && !h_out) return -1;
 #define AR_CASE(HH)                                                                            \
   case HH:                                                                                     \
-    mb_launch(symm_allreduce_norm_kernel<HH>, coll_grid(rows, 1), RowShape<HH>::NT, 0, st, a); \
+    mb_launch(symm_allreduce_norm_kernel<HH>,                                                 \
+              coll_grid(symm_allreduce_norm_kernel<HH>, RowTile<HH>::THREADS, rows,             \
+                        RowTile<HH>::ROWS),                                                   \
+              RowTile<HH>::THREADS, 0, st, a);                                                 \
     break;
     switch (H) {
       AR_CASE(256) AR_CASE(512) AR_CASE(1024) AR_CASE(2048) AR_CASE(2560) AR_CASE(4096)
