@@ -209,7 +209,7 @@ def preset(name: str) -> ModelConfig:
                            max_position=4096)
     if n in ("tiny-gdn",):  # Gated DeltaNet hybrid: layers 0-2 linear attention, layer 3 softmax
         return ModelConfig(arch="qwen3_next", vocab_size=4096, hidden_size=256, num_layers=4,
-                           num_heads=4, num_kv_heads=2, head_dim=64, intermediate_size=512,
+                           num_heads=4, num_kv_heads=2, head_dim=128, intermediate_size=512,
                            tie_embeddings=True, max_position=4096, linear_attn_interval=4,
                            linear_num_key_heads=2, linear_num_value_heads=4,
                            linear_key_head_dim=32, linear_value_head_dim=32)

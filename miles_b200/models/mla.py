@@ -39,8 +39,14 @@ import math
 import torch
 import torch.nn.functional as F
 
-from miles_b200.ops.norm import rms_norm
 from miles_b200.parallel.tp import copy_to_tp, reduce_from_tp
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm of the latent vectors (kv_lora_rank / q_lora_rank wide: sizes the fused norm
+    kernel is not built for), fp32 arithmetic, result in x's dtype."""
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
 
 
 def mla_param_shapes(cfg, p: str, tp_size: int = 1):
