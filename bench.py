@@ -7,7 +7,7 @@ Workload per GPU (weak scaling): 8 prompts x 8 samples, 512 uniform-random promp
 responses of uniform 1024..8192 tokens (the length is sampled per response; generation stops
 there), temperature 1.0, Bernoulli(0.5) rewards, GRPO advantages, PPO clip 0.2, TIS cap 2.0,
 Rollout Routing Replay (routing recorded in rollout, replayed in training), Adam lr 1e-6.
-At N GPUs the global batch is N x 64 samples (N x 8 prompts), i.e. the BASELINE config's
+At N GPUs the global batch is N x 64 samples (N x 8 prompts), i.e. the headline workload's
 64 prompts x 8 samples at N = 8.
 
 Timing: W untimed warm-up steps, then K steps bracketed by barrier + synchronize, device-timed
