@@ -354,6 +354,28 @@ class Transformer(torch.nn.Module):
         m = self._mlp(i, x2, replay=replay)
         return m, r
 
+    # -------------------------------------------------------------------------------- layer loop
+    def _run_layers(self, layer_fn, r, replay_experts, rows=None):
+        """Run this rank's layers: layer_fn(i, m_prev, r_prev, replay) -> (m, r), with per-layer
+        activation recompute when training. `replay_experts` [T, L_moe, k] is sliced to layer i's
+        MoE column (and to `rows`, a slice of this rank's rows, if given)."""
+        m = None
+        for i in self.layer_ids:
+            replay = None
+            if i in self.router_cfgs and replay_experts is not None:
+                col = replay_experts[:, self.moe_index[i]]
+                replay = (col if rows is None else col[rows]).contiguous()
+            if self.recompute and torch.is_grad_enabled():
+                if m is None:
+                    m, r = checkpoint(lambda rr, i=i, rp=replay: layer_fn(i, None, rr, rp), r,
+                                      use_reentrant=False)
+                else:
+                    m, r = checkpoint(lambda mm, rr, i=i, rp=replay: layer_fn(i, mm, rr, rp), m, r,
+                                      use_reentrant=False)
+            else:
+                m, r = layer_fn(i, m, r, replay)
+        return m, r
+
     # -------------------------------------------------------------------------------- sequence parallel
     def _layer_train_sp(self, i, m_prev, r_prev, meta, replay):
         """One layer on this rank's rows: norms on T/tp rows, column-parallel projections on the
@@ -401,23 +423,8 @@ class Transformer(torch.nn.Module):
             if replay_experts is not None:
                 replay_experts = torch.cat([replay_experts, replay_experts[:1].expand(pad, -1, -1)])
         r = sp_split(F.embedding(tokens.long(), self.params["embed_tokens.weight"]), tp)
-        m = None
-        moe_i = 0
-        for i in range(cfg.num_layers):
-            replay = None
-            if i in self.router_cfgs:
-                if replay_experts is not None:
-                    replay = replay_experts[:, moe_i].contiguous()
-                moe_i += 1
-            if self.recompute and torch.is_grad_enabled():
-                if m is None:
-                    m, r = checkpoint(lambda rr, i=i, rp=replay: self._layer_train_sp(i, None, rr, meta, rp),
-                                      r, use_reentrant=False)
-                else:
-                    m, r = checkpoint(lambda mm, rr, i=i, rp=replay: self._layer_train_sp(i, mm, rr, meta, rp),
-                                      m, r, use_reentrant=False)
-            else:
-                m, r = self._layer_train_sp(i, m, r, meta, replay)
+        m, r = self._run_layers(lambda i, mm, rr, rp: self._layer_train_sp(i, mm, rr, meta, rp), r,
+                                replay_experts)
         y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
         return sp_gather_replicated(y, tp)[:T]
 
@@ -457,23 +464,8 @@ class Transformer(torch.nn.Module):
                 replay_experts = torch.cat([replay_experts, replay_experts[:1].expand(Tp - T, -1, -1)])
         pos = meta.positions[lo:hi].contiguous()
         r = F.embedding(tokens[lo:hi].long(), self.params["embed_tokens.weight"])
-        m = None
-        moe_i = 0
-        for i in range(cfg.num_layers):
-            replay = None
-            if i in self.router_cfgs:
-                if replay_experts is not None:
-                    replay = replay_experts[lo:hi, moe_i].contiguous()
-                moe_i += 1
-            if self.recompute and torch.is_grad_enabled():
-                if m is None:
-                    m, r = checkpoint(lambda rr, i=i, rp=replay: self._layer_train_cp(i, None, rr, meta, pos, rp),
-                                      r, use_reentrant=False)
-                else:
-                    m, r = checkpoint(lambda mm, rr, i=i, rp=replay: self._layer_train_cp(i, mm, rr, meta, pos, rp),
-                                      m, r, use_reentrant=False)
-            else:
-                m, r = self._layer_train_cp(i, m, r, meta, pos, replay)
+        m, r = self._run_layers(lambda i, mm, rr, rp: self._layer_train_cp(i, mm, rr, meta, pos, rp), r,
+                                replay_experts, rows=slice(lo, hi))
         y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
         return y
 
@@ -524,30 +516,19 @@ class Transformer(torch.nn.Module):
                 raise NotImplementedError("routing capture under context parallelism")
             return self._forward_train_cp(tokens, meta, replay_experts)
         r = F.embedding(tokens.long(), self.params["embed_tokens.weight"]) if self.is_first else hidden_in
-        m = None
-        for i in self.layer_ids:
-            replay = None
-            if i in self.router_cfgs and replay_experts is not None:
-                replay = replay_experts[:, self.moe_index[i]].contiguous()
-            if self.recompute and torch.is_grad_enabled():
-                if m is None:
-                    m, r = checkpoint(lambda rr, i=i, rp=replay: self._layer_train(i, None, rr, meta, rp),
-                                      r, use_reentrant=False)
-                else:
-                    m, r = checkpoint(lambda mm, rr, i=i, rp=replay: self._layer_train(i, mm, rr, meta, rp),
-                                      m, r, use_reentrant=False)
-            else:
-                rec = None
-                if record_experts is not None and i in self.router_cfgs:
-                    rec = record_experts.append
-                if rec is not None:
-                    ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
-                    x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
-                    a = self._attn_train(i, x, meta)
-                    x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
-                    m = self._mlp(i, x2, replay=replay, record=rec)
-                else:
-                    m, r = self._layer_train(i, m, r, meta, replay)
+
+        def layer(i, m, r, replay):
+            if (record_experts is not None and i in self.router_cfgs
+                    and not (self.recompute and torch.is_grad_enabled())):
+                # routing capture (R3): the MoE call reports the routing it used
+                ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
+                x, r = (rms_norm(r, ln1, cfg.rms_eps), r) if m is None else add_rms_norm(m, r, ln1, cfg.rms_eps)
+                a = self._attn_train(i, x, meta)
+                x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
+                return self._mlp(i, x2, replay=replay, record=record_experts.append), r
+            return self._layer_train(i, m, r, meta, replay)
+
+        m, r = self._run_layers(layer, r, replay_experts)
         if not self.is_last:
             return r if m is None else m + r
         y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
