@@ -174,53 +174,13 @@ class PeerRefit:
     # ------------------------------------------------------------------ layout
     @staticmethod
     def _pad(n: int) -> int:
-        return (n + 255) // 256 * 256
+        return _pad256(n)
 
     def _items(self):
-        """Transfer units (name, kind, lo, hi, staging bytes): kind "fp8" moves rows [lo, hi) of
-        a 2-D weight view (multiples of 128 rows, so quantisation blocks never straddle units);
-        kind "copy" moves bytes [lo, hi) of the parameter. Units never exceed the staging."""
-        out = []
-        for s in self.model.specs:
-            p = self.model.params[s.name].data
-            w = None
-            if self.mode == "fp8":
-                if p.dim() == 2 and p.shape[0] >= 128 and p.shape[1] >= 128 and p.shape[1] % 16 == 0:
-                    w = p
-                elif p.dim() == 3 and p.shape[1] >= 128 and p.shape[2] >= 128 and p.shape[2] % 16 == 0:
-                    w = p.reshape(-1, p.shape[2])
-            if w is not None:
-                M, N = w.shape
-                gn = (N + 127) // 128
-                per_blk = self._pad(128 * N) + self._pad(gn * 4)  # upper bound per 128 rows
-                step = max(1, self.cap // per_blk) * 128
-                for r0 in range(0, M, step):
-                    r1 = min(M, r0 + step)
-                    rows = r1 - r0
-                    nb = self._pad(rows * N) + self._pad(((rows + 127) // 128) * gn * 4)
-                    out.append((s.name, "fp8", r0, r1, nb))
-            else:
-                total = p.numel() * p.element_size()
-                step = self.cap // 256 * 256
-                for b0 in range(0, total, step):
-                    b1 = min(total, b0 + step)
-                    out.append((s.name, "copy", b0, b1, self._pad(b1 - b0)))
-        return out
+        return refit_units(self.model, self.mode, self.cap)
 
     def _plan(self):
-        """Buckets of (name, kind, lo, hi, owner engine, staging offset)."""
-        buckets, cur, used = [], [], {e: 0 for e in self.engines}
-        for name, kind, lo, hi, nb in self._items():
-            owner = min(self.engines, key=lambda e: used[e])
-            if used[owner] + nb > self.cap:
-                buckets.append(cur)
-                cur, used = [], {e: 0 for e in self.engines}
-                owner = self.engines[0]
-            cur.append((name, kind, lo, hi, owner, used[owner]))
-            used[owner] += nb
-        if cur:
-            buckets.append(cur)
-        return buckets
+        return refit_buckets(self._items(), self.engines, self.cap)
 
     def _view2d(self, name: str) -> torch.Tensor:
         p = self.model.params[name].data
@@ -349,6 +309,61 @@ def _raw_bytes(ptr: int, n: int) -> torch.Tensor:
     from miles_b200.ops import _lib
 
     return _lib._C.from_ptr(ptr, [n], torch.uint8, torch.cuda.current_device())
+
+
+def _pad256(n: int) -> int:
+    return (n + 255) // 256 * 256
+
+
+def refit_units(model, mode: str, cap: int):
+    """Transfer units (name, kind, lo, hi, staging bytes) of a peer refit: kind "fp8" moves rows
+    [lo, hi) of a 2-D weight view (multiples of 128 rows, so quantisation blocks never straddle
+    units), kind "copy" moves bytes [lo, hi) of the parameter. No unit exceeds `cap` bytes."""
+    out = []
+    for s in model.specs:
+        p = model.params[s.name].data
+        w = None
+        if mode == "fp8":
+            if p.dim() == 2 and p.shape[0] >= 128 and p.shape[1] >= 128 and p.shape[1] % 16 == 0:
+                w = p
+            elif p.dim() == 3 and p.shape[1] >= 128 and p.shape[2] >= 128 and p.shape[2] % 16 == 0:
+                w = p.reshape(-1, p.shape[2])
+        if w is not None:
+            M, N = w.shape
+            gn = (N + 127) // 128
+            per_blk = _pad256(128 * N) + _pad256(gn * 4)  # upper bound per 128 rows
+            step = max(1, cap // per_blk) * 128
+            for r0 in range(0, M, step):
+                r1 = min(M, r0 + step)
+                rows = r1 - r0
+                nb = _pad256(rows * N) + _pad256(((rows + 127) // 128) * gn * 4)
+                out.append((s.name, "fp8", r0, r1, nb))
+        else:
+            total = p.numel() * p.element_size()
+            step = cap // 256 * 256
+            for b0 in range(0, total, step):
+                b1 = min(total, b0 + step)
+                out.append((s.name, "copy", b0, b1, _pad256(b1 - b0)))
+    return out
+
+
+def refit_buckets(units, engines: list[int], cap: int):
+    """Buckets of (name, kind, lo, hi, owner engine, staging offset): each unit goes to the
+    least-loaded engine of the current bucket; a bucket closes when a unit no longer fits."""
+    buckets, cur, used = [], [], {e: 0 for e in engines}
+    for name, kind, lo, hi, nb in units:
+        if nb > cap:
+            raise ValueError(f"{name}: one 128-row block needs {nb} staging bytes > {cap}")
+        owner = min(engines, key=lambda e: used[e])
+        if used[owner] + nb > cap:
+            buckets.append(cur)
+            cur, used = [], {e: 0 for e in engines}
+            owner = engines[0]
+        cur.append((name, kind, lo, hi, owner, used[owner]))
+        used[owner] += nb
+    if cur:
+        buckets.append(cur)
+    return buckets
 
 
 def make_refit(model: Transformer, group, src: int, bucket_bytes: int, mode: str,
