@@ -161,3 +161,77 @@ class GDN:
         cache.lin_conv[i].index_copy_(0, rows, window[:, :, 1:].contiguous())
         cache.lin_state[i].index_copy_(0, rows, S)
         return self._out(i, o, z, x.dtype)
+
+
+# ---------------------------------------------------------------------------------------------
+# Context parallelism: a rank holds rows [lo, hi) of the packed batch; a sequence that crosses
+# into the next rank hands over its conv and recurrent state (point-to-point, in rank order), and
+# the gradient of that state comes back the same way in the backward.
+# ---------------------------------------------------------------------------------------------
+class _RecvState(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, anchor, conv_shape, state_shape, src, group):
+        ctx.src, ctx.group = src, group
+        ctx.shapes = (conv_shape, state_shape)
+        ctx.device = anchor.device
+        cst = torch.empty(conv_shape, dtype=torch.float32, device=anchor.device)
+        S = torch.empty(state_shape, dtype=torch.float32, device=anchor.device)
+        torch.distributed.recv(cst, src, group=group)
+        torch.distributed.recv(S, src, group=group)
+        return cst, S
+
+    @staticmethod
+    def backward(ctx, g_cst, g_S):
+        g_cst = g_cst if g_cst is not None else torch.zeros(ctx.shapes[0], device=ctx.device)
+        g_S = g_S if g_S is not None else torch.zeros(ctx.shapes[1], device=ctx.device)
+        torch.distributed.send(g_cst.contiguous(), ctx.src, group=ctx.group)
+        torch.distributed.send(g_S.contiguous(), ctx.src, group=ctx.group)
+        return None, None, None, None, None
+
+
+class _SendState(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, cst, S, dst, group):
+        ctx.dst, ctx.group = dst, group
+        ctx.shapes = (cst.shape, S.shape)
+        torch.distributed.send(cst.detach().contiguous(), dst, group=group)
+        torch.distributed.send(S.detach().contiguous(), dst, group=group)
+        return cst.new_zeros(())
+
+    @staticmethod
+    def backward(ctx, g):
+        g_cst = torch.empty(ctx.shapes[0], dtype=torch.float32, device=g.device)
+        g_S = torch.empty(ctx.shapes[1], dtype=torch.float32, device=g.device)
+        torch.distributed.recv(g_cst, ctx.dst, group=ctx.group)
+        torch.distributed.recv(g_S, ctx.dst, group=ctx.group)
+        return g_cst, g_S, None, None
+
+
+def gdn_attn_cp(gdn: GDN, i: int, x: torch.Tensor, meta, lo: int, hi: int, cp) -> torch.Tensor:
+    """GDN layer on this CP rank's rows [lo, hi) of the packed (padded) batch."""
+    import torch.distributed as dist
+
+    mixed, z, beta, g = gdn._project(i, x)
+    cu = meta.cu_list
+    outs = []
+    send = None
+    for b in range(len(cu) - 1):
+        s, e = max(cu[b], lo), min(cu[b + 1], hi)
+        if e <= s:
+            continue
+        if cu[b] < lo:  # continues a sequence from the previous rank
+            (C, Km1), ss = gdn_state_shapes(gdn.cfg)
+            anchor = mixed[:0].sum()
+            cst, S = _RecvState.apply(anchor, (C, Km1), ss, dist.get_global_rank(cp.group, cp.rank - 1), cp.group)
+        else:
+            cst, S = gdn._zero_states(x.device)
+        conv, cst = gdn._conv(i, mixed[s - lo:e - lo], cst)
+        q, k, v = gdn._heads(conv)
+        o, S = gdn._recur(q, k, v, beta[s - lo:e - lo], g[s - lo:e - lo], S)
+        outs.append(o)
+        if cu[b + 1] > hi:  # the sequence goes on in the next rank
+            send = _SendState.apply(cst, S, dist.get_global_rank(cp.group, cp.rank + 1), cp.group)
+    out = gdn._out(i, torch.cat(outs, 0), z, x.dtype)
+    if send is not None:
+        out = out + send.to(out.dtype)  # keeps the hand-over on the autograd graph
+    return out

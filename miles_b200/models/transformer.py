@@ -255,8 +255,8 @@ class Transformer(torch.nn.Module):
         if cfg.linear_attn_interval:
             from miles_b200.models.gdn import GDN
 
-            if self.tp is not None or self.cp is not None or self.sequence_parallel:
-                raise ValueError("linear-attention layers run without TP / CP")
+            if self.tp is not None or self.sequence_parallel:
+                raise ValueError("linear-attention layers run without TP / SP")
             self.gdn = GDN(self)
         self.mla = None
         if cfg.kv_lora_rank:
@@ -365,7 +365,10 @@ class Transformer(torch.nn.Module):
             if i in self.router_cfgs and replay_experts is not None:
                 col = replay_experts[:, self.moe_index[i]]
                 replay = (col if rows is None else col[rows]).contiguous()
-            if self.recompute and torch.is_grad_enabled():
+            # layers that exchange point-to-point messages in their forward (linear attention
+            # under CP) are not recomputed: a recompute would send the messages twice
+            p2p = self.cp is not None and self.cfg.layer_is_linear(i)
+            if self.recompute and torch.is_grad_enabled() and not p2p:
                 if m is None:
                     m, r = checkpoint(lambda rr, i=i, rp=replay: layer_fn(i, None, rr, rp), r,
                                       use_reentrant=False)
@@ -438,6 +441,14 @@ class Transformer(torch.nn.Module):
             x, r = rms_norm(r_prev, ln1, cfg.rms_eps), r_prev
         else:
             x, r = add_rms_norm(m_prev, r_prev, ln1, cfg.rms_eps)
+        if self.gdn is not None and cfg.layer_is_linear(i):
+            # linear attention: state hand-over between consecutive CP ranks (models/gdn.py)
+            from miles_b200.models.gdn import gdn_attn_cp
+
+            _, lo, hi = cp.rows(meta.total)
+            a = gdn_attn_cp(self.gdn, i, x, meta, lo, hi, cp)
+            x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
+            return self._mlp(i, x2, replay=replay), r
         pre = f"layers.{i}.self_attn."
         qkv = self._lin(x, pre + "qkv_proj.weight")
         q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
