@@ -185,43 +185,71 @@ class RolloutEngine:
         self.aborted = True
 
     def generate(self, reqs: list[GenRequest]) -> list[GenResult]:
+        """Continuous batching: requests are admitted whenever a batch slot and enough KV pages
+        are free (prefilled as a packed batch, then joined to the running decode batch), and
+        leave the batch as soon as they finish."""
         self.resume_memory()
         self.aborted = False
         results: dict[int, GenResult] = {}
         pending = list(reqs)
+        live: list[_Seq] = []
+        free_rows = list(range(self.max_batch - 1, -1, -1))  # linear-attention state rows
         t0 = time.perf_counter()
-        n_decode_steps = 0
-        while pending:
-            wave, pending = self._admit(pending)
-            if not wave:
-                raise RuntimeError("KV cache too small for a single request")
-            n_decode_steps += self._run_wave(wave)
-            for s in wave:
-                results[s.req.rid] = self._result(s)
-                self.free_pages.extend(s.pages)
-        self.stats = {"wall_s": time.perf_counter() - t0, "decode_steps": n_decode_steps}
+        n_decode_steps = n_prefills = 0
+        while (pending or live) and not self.aborted:
+            if pending and len(live) < self.max_batch:
+                new, pending = self._admit(pending, self.max_batch - len(live))
+                if new:
+                    for sq in new:
+                        sq.wave_idx = free_rows.pop()
+                    self._prefill(new)
+                    n_prefills += 1
+                    live += new
+                elif not live:
+                    raise RuntimeError("KV cache too small for a single request")
+            running = [sq for sq in live if not sq.done]
+            if running:
+                self._decode_step(running)
+                n_decode_steps += 1
+            still = []
+            for sq in live:
+                if sq.done:
+                    results[sq.req.rid] = self._result(sq)
+                    self.free_pages.extend(sq.pages)
+                    free_rows.append(sq.wave_idx)
+                else:
+                    still.append(sq)
+            live = still
+        if self.aborted:
+            for sq in live:
+                sq.done, sq.reason = True, "abort"
+                results[sq.req.rid] = self._result(sq)
+                self.free_pages.extend(sq.pages)
+            for r in pending:
+                results[r.rid] = GenResult(r.rid, [], [], "abort", None, self.model.weight_version)
+        self.stats = {"wall_s": time.perf_counter() - t0, "decode_steps": n_decode_steps,
+                      "prefills": n_prefills}
         return [results[r.rid] for r in reqs]
 
-    def _admit(self, pending):
+    def _admit(self, pending, room: int):
+        """Take requests in order while batch slots (`room`) and KV pages last."""
         wave, rest = [], []
         for r in pending:
             need = math.ceil((len(r.prompt) + r.max_new_tokens) / PAGE)
             if need > self.max_pages_per_seq:
                 raise ValueError(f"request needs {need} pages > max_pages_per_seq")
-            if len(wave) < self.max_batch and need <= len(self.free_pages):
+            if not rest and len(wave) < room and need <= len(self.free_pages):
                 wave.append(_Seq(r, [self.free_pages.pop() for _ in range(need)]))
             else:
-                rest.append(r)
+                rest.append(r)  # keep arrival order: no request overtakes an earlier one
         return wave, rest
 
     def _slot(self, s: _Seq, pos: int) -> int:
         return s.pages[pos // PAGE] * PAGE + pos % PAGE
 
-    def _run_wave(self, wave: list[_Seq]) -> int:
+    def _prefill(self, wave: list[_Seq]) -> None:
+        """Packed prefill of newly admitted sequences; samples and accepts their first token."""
         dev = self.dev
-        for j, s in enumerate(wave):
-            s.wave_idx = j  # linear-attention state row of this sequence
-        # ---- prefill (packed)
         cu = [0]
         toks, slots = [], []
         for s in wave:
@@ -236,9 +264,9 @@ class RolloutEngine:
         h = self.model.forward_prefill(torch.tensor(toks, dtype=torch.int32, device=dev), meta,
                                        self.cache, torch.tensor(slots, dtype=torch.int64, device=dev),
                                        record=rec,
-                                       state_rows=torch.arange(len(wave), dtype=torch.int64, device=dev))
+                                       state_rows=torch.tensor([s.wave_idx for s in wave],
+                                                               dtype=torch.int64, device=dev))
         last = torch.tensor([c - 1 for c in cu[1:]], dtype=torch.long, device=dev)
-        B = len(wave)
         inv_t = torch.tensor([1.0 / s.req.temperature if s.req.temperature > 0 else 0.0 for s in wave],
                              dtype=torch.float32, device=dev)
         seeds = torch.tensor([s.req.seed for s in wave], dtype=torch.int64, device=dev)
@@ -253,64 +281,55 @@ class RolloutEngine:
         self._accept(wave, tok.tolist(), lp.tolist())
         if nvtx:
             torch.cuda.nvtx.range_pop()
-        # ---- decode
-        steps = 0
-        while not self.aborted:
-            live = [s for s in wave if not s.done]
-            if not live:
-                break
-            Bb = self._bucket(len(live))
-            g, st, out = self._get_step(Bb)
-            n = len(live)
-            tokens = np.zeros(Bb, np.int32)
-            pos = np.zeros(Bb, np.int32)
-            ctx = np.ones(Bb, np.int32)
-            slot = np.arange(Bb, dtype=np.int64) % PAGE  # trash page 0 for padding rows
-            pt = np.zeros((Bb, self.max_pages_per_seq), np.int32)
-            invt = np.ones(Bb, np.float32)
-            seed = np.zeros(Bb, np.int64)
-            srow = np.full(Bb, self.max_batch, np.int64)
+
+    def _decode_step(self, live: list[_Seq]) -> None:
+        """One token for every running sequence (CUDA graph of the batch bucket)."""
+        nvtx = self.dev.type == "cuda"
+        Bb = self._bucket(len(live))
+        g, st, out = self._get_step(Bb)
+        n = len(live)
+        tokens = np.zeros(Bb, np.int32)
+        pos = np.zeros(Bb, np.int32)
+        ctx = np.ones(Bb, np.int32)
+        slot = np.arange(Bb, dtype=np.int64) % PAGE  # trash page 0 for padding rows
+        pt = np.zeros((Bb, self.max_pages_per_seq), np.int32)
+        invt = np.ones(Bb, np.float32)
+        seed = np.zeros(Bb, np.int64)
+        srow = np.full(Bb, self.max_batch, np.int64)
+        for j, s in enumerate(live):
+            srow[j] = s.wave_idx
+            p = len(s.req.prompt) + len(s.out) - 1  # position of the token being fed
+            tokens[j] = s.out[-1]
+            pos[j] = p
+            ctx[j] = p + 1
+            slot[j] = self._slot(s, p)
+            pt[j, :len(s.pages)] = s.pages
+            invt[j] = 1.0 / s.req.temperature if s.req.temperature > 0 else 0.0
+            seed[j] = s.req.seed
+        st["tokens"].copy_(torch.from_numpy(tokens), non_blocking=True)
+        st["positions"].copy_(torch.from_numpy(pos), non_blocking=True)
+        st["ctx"].copy_(torch.from_numpy(ctx), non_blocking=True)
+        st["slots"].copy_(torch.from_numpy(slot), non_blocking=True)
+        st["pt"].copy_(torch.from_numpy(pt), non_blocking=True)
+        st["inv_t"].copy_(torch.from_numpy(invt), non_blocking=True)
+        st["seeds"].copy_(torch.from_numpy(seed), non_blocking=True)
+        st["state_rows"].copy_(torch.from_numpy(srow), non_blocking=True)
+        if nvtx:
+            torch.cuda.nvtx.range_push("decode_step")
+        if g is not None:
+            g.replay()
+            _lib.add_launches(self.graph_launches[Bb])
+            tok, lp = out
+        else:
+            tok, lp = self._step_fn(st)
+        if self.n_moe and any(s.req.return_routed_experts for s in live):
+            ex = st["experts"][:n].cpu().numpy().copy()
             for j, s in enumerate(live):
-                srow[j] = s.wave_idx
-                p = s.pos - 1 + 1  # position of the token being fed = last written + 1
-                p = len(s.req.prompt) + len(s.out) - 1
-                tokens[j] = s.out[-1]
-                pos[j] = p
-                ctx[j] = p + 1
-                slot[j] = self._slot(s, p)
-                pt[j, :len(s.pages)] = s.pages
-                invt[j] = 1.0 / s.req.temperature if s.req.temperature > 0 else 0.0
-                seed[j] = s.req.seed
-            st["tokens"].copy_(torch.from_numpy(tokens), non_blocking=True)
-            st["positions"].copy_(torch.from_numpy(pos), non_blocking=True)
-            st["ctx"].copy_(torch.from_numpy(ctx), non_blocking=True)
-            st["slots"].copy_(torch.from_numpy(slot), non_blocking=True)
-            st["pt"].copy_(torch.from_numpy(pt), non_blocking=True)
-            st["inv_t"].copy_(torch.from_numpy(invt), non_blocking=True)
-            st["seeds"].copy_(torch.from_numpy(seed), non_blocking=True)
-            st["state_rows"].copy_(torch.from_numpy(srow), non_blocking=True)
-            if nvtx:
-                torch.cuda.nvtx.range_push("decode_step")
-            if g is not None:
-                g.replay()
-                _lib.add_launches(self.graph_launches[Bb])
-                tok, lp = out
-            else:
-                tok, lp = self._step_fn(st)
-            if self.n_moe and any(s.req.return_routed_experts for s in live):
-                ex = st["experts"][:n].cpu().numpy().copy()
-                for j, s in enumerate(live):
-                    if s.req.return_routed_experts:
-                        s.experts.append(ex[j:j + 1])
-            self._accept(live, tok[:n].tolist(), lp[:n].tolist())
-            if nvtx:
-                torch.cuda.nvtx.range_pop()
-            steps += 1
-        if self.aborted:
-            for s in wave:
-                if not s.done:
-                    s.done, s.reason = True, "abort"
-        return steps
+                if s.req.return_routed_experts:
+                    s.experts.append(ex[j:j + 1])
+        self._accept(live, tok[:n].tolist(), lp[:n].tolist())
+        if nvtx:
+            torch.cuda.nvtx.range_pop()
 
     def _accept(self, seqs, toks, lps):
         for s, t, l in zip(seqs, toks, lps):
