@@ -10,7 +10,8 @@ fixed-size recurrent state per head (keys -> values, [dk, dv]):
     S_t = exp(g_t) S_{t-1};  S_t += k_t (beta_t (v_t - S_t^T k_t))^T;  o_t = S_t^T q_t / sqrt(dk)
     out = W_out (RMSNorm(o) * w_norm * SiLU(z))
 
-Training and prefill run the recurrence over each packed sequence from a zero state; the rollout
+Training and prefill run the recurrence over each packed sequence from a zero state, in chunks of
+64 steps in matrix form (a unit-triangular solve per chunk, `_recur_chunked`); the rollout
 engine keeps, per live sequence, the last K-1 conv inputs and the state S (`KVCache.lin_conv`,
 `KVCache.lin_state`, one row per engine batch slot) and advances them one token per decode step,
 so decode reproduces the training forward. This is a PyTorch implementation (fp32 recurrence);
@@ -103,6 +104,41 @@ class GDN:
             outs.append(torch.einsum("hk,hkv->hv", q[t], S) * scale)
         return torch.stack(outs, 0), S
 
+    def _recur_chunked(self, q, k, v, beta, g, S, chunk: int = 64):
+        """Same result as `_recur`, by chunks of `chunk` steps in matrix form. Inside a chunk,
+        with gamma_t the cumulative log decay from the chunk start and A the strictly lower
+        triangular A_tj = beta_t exp(gamma_t - gamma_j) (k_t . k_j):
+            u = (I + A)^-1 (beta v - beta exp(gamma) k S0)          (the delta-rule updates)
+            o_t = exp(gamma_t) S0^T q_t + sum_{j<=t} exp(gamma_t - gamma_j) (k_j . q_t) u_j
+            S_C = exp(gamma_C) S0 + sum_j exp(gamma_C - gamma_j) k_j u_j^T
+        (the unrolled recurrence S_t = exp(g_t) S_{t-1} + k_t u_t^T). Heads are the batch."""
+        scale = 1.0 / math.sqrt(self.dk)
+        T = q.shape[0]
+        outs = []
+        for c0 in range(0, T, chunk):
+            c1 = min(T, c0 + chunk)
+            C = c1 - c0
+            qc, kc, vc = q[c0:c1].transpose(0, 1), k[c0:c1].transpose(0, 1), v[c0:c1].transpose(0, 1)
+            bc = beta[c0:c1].t()                                 # [h, C]
+            gam = torch.cumsum(g[c0:c1].t(), -1)                  # [h, C]
+            diff = gam[:, :, None] - gam[:, None, :]             # gamma_t - gamma_j
+            tril_s = torch.ones(C, C, dtype=torch.bool, device=q.device).tril(-1)
+            tril_i = torch.ones(C, C, dtype=torch.bool, device=q.device).tril()
+            decay_s = torch.where(tril_s, torch.exp(diff.masked_fill(~tril_s, 0.0)), torch.zeros_like(diff))
+            decay_i = torch.where(tril_i, torch.exp(diff.masked_fill(~tril_i, 0.0)), torch.zeros_like(diff))
+            kk = torch.einsum("htd,hjd->htj", kc, kc)
+            A = bc[:, :, None] * decay_s * kk
+            eye = torch.eye(C, dtype=q.dtype, device=q.device).expand_as(A)
+            rhs = bc[:, :, None] * (vc - torch.exp(gam)[:, :, None] * torch.einsum("htd,hdv->htv", kc, S))
+            u = torch.linalg.solve_triangular(eye + A, rhs, upper=False, unitriangular=True)
+            qk = torch.einsum("htd,hjd->htj", qc, kc) * decay_i
+            o = torch.exp(gam)[:, :, None] * torch.einsum("htd,hdv->htv", qc, S) + torch.einsum("htj,hjv->htv", qk, u)
+            outs.append((o * scale).transpose(0, 1))
+            last = gam[:, -1]
+            S = torch.exp(last)[:, None, None] * S + torch.einsum(
+                "hjd,hjv->hdv", kc * torch.exp(last[:, None] - gam)[:, :, None], u)
+        return torch.cat(outs, 0), S
+
     def _out(self, i, o, z, dtype):
         T = o.shape[0]
         o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + self.cfg.rms_eps)
@@ -128,7 +164,7 @@ class GDN:
             cst, S = self._zero_states(x.device)
             conv, cst = self._conv(i, mixed[s:e], cst)
             q, k, v = self._heads(conv)
-            o, S = self._recur(q, k, v, beta[s:e], g[s:e], S)
+            o, S = self._recur_chunked(q, k, v, beta[s:e], g[s:e], S)
             outs.append(o)
             if cache is not None:
                 row = int(state_rows[b])
@@ -227,7 +263,7 @@ def gdn_attn_cp(gdn: GDN, i: int, x: torch.Tensor, meta, lo: int, hi: int, cp) -
             cst, S = gdn._zero_states(x.device)
         conv, cst = gdn._conv(i, mixed[s - lo:e - lo], cst)
         q, k, v = gdn._heads(conv)
-        o, S = gdn._recur(q, k, v, beta[s - lo:e - lo], g[s - lo:e - lo], S)
+        o, S = gdn._recur_chunked(q, k, v, beta[s - lo:e - lo], g[s - lo:e - lo], S)
         outs.append(o)
         if cu[b + 1] > hi:  # the sequence goes on in the next rank
             send = _SendState.apply(cst, S, dist.get_global_rank(cp.group, cp.rank + 1), cp.group)

@@ -67,7 +67,10 @@ def test_cp2_matches_single(tmp_path, name, port):
     assert torch.allclose(r["ent"], ent.detach(), atol=1e-5)
     assert set(r["grads"]) == {n for n, p in m.params.items() if p.grad is not None}
     for n, g in r["grads"].items():
-        assert torch.allclose(g, m.params[n].grad, atol=1e-5, rtol=1e-3), (n, (g - m.params[n].grad).abs().max())
+        # GDN: chunk boundaries of the chunked recurrence differ between the CP split and the
+        # single-rank run, so the fp32 rounding differs slightly
+        tol = 1e-4 if name == "tiny-gdn" else 1e-5
+        assert torch.allclose(g, m.params[n].grad, atol=tol, rtol=1e-3), (n, (g - m.params[n].grad).abs().max())
 
 
 @pytest.mark.timeout(600)

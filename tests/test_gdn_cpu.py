@@ -100,3 +100,22 @@ def test_gdn_hf_roundtrip_and_grpo_step(tmp_path):
     hist = T.train(args)
     assert len(hist) == 1 and np.isfinite(hist[0]["train/pg_loss"])
     assert hist[0]["train/train_rollout_logprob_abs_diff"] < 1e-4
+
+
+def test_gdn_chunked_equals_recurrence():
+    from miles_b200.models.gdn import GDN
+
+    cfg = preset("tiny-gdn")
+    g = GDN(Transformer(cfg, device="cpu", dtype=torch.float32, seed=1))
+    torch.manual_seed(1)
+    for T in (1, 5, 64, 150):
+        q = F.normalize(torch.randn(T, g.nv, g.dk), dim=-1)
+        k = F.normalize(torch.randn(T, g.nv, g.dk), dim=-1)
+        v = torch.randn(T, g.nv, g.dv)
+        beta = torch.rand(T, g.nv)
+        lg = -torch.rand(T, g.nv) * 0.5
+        S0 = torch.randn(g.nv, g.dk, g.dv) * 0.1
+        o1, S1 = g._recur(q, k, v, beta, lg, S0)
+        o2, S2 = g._recur_chunked(q, k, v, beta, lg, S0, chunk=64)
+        assert torch.allclose(o1, o2, atol=2e-5, rtol=1e-4), (T, (o1 - o2).abs().max())
+        assert torch.allclose(S1, S2, atol=2e-5, rtol=1e-4)
