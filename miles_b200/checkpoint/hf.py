@@ -90,11 +90,14 @@ def hf_config_dict(cfg: ModelConfig) -> dict:
          "num_key_value_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
          "intermediate_size": cfg.intermediate_size, "rms_norm_eps": cfg.rms_eps,
          "rope_theta": cfg.rope_theta, "rope_scaling": cfg.rope_scaling,
+         "rope_parameters": dict({"rope_theta": cfg.rope_theta, "rope_type": "default"},
+                                 **(cfg.rope_scaling or {})),
          "max_position_embeddings": cfg.max_position, "tie_word_embeddings": cfg.tie_embeddings,
          "torch_dtype": "bfloat16"}
     if cfg.arch == "qwen3_moe":
         d.update(model_type="qwen3_moe", architectures=["Qwen3MoeForCausalLM"],
-                 num_experts=cfg.num_experts, num_experts_per_tok=cfg.topk,
+                 num_experts=cfg.num_experts, num_local_experts=cfg.num_experts,
+                 num_experts_per_tok=cfg.topk,
                  moe_intermediate_size=cfg.moe_intermediate_size, norm_topk_prob=cfg.norm_topk_prob,
                  decoder_sparse_step=1, mlp_only_layers=[])
     elif cfg.arch == "deepseek_v3":
@@ -103,7 +106,24 @@ def hf_config_dict(cfg: ModelConfig) -> dict:
                  moe_intermediate_size=cfg.moe_intermediate_size, n_shared_experts=cfg.num_shared_experts,
                  first_k_dense_replace=cfg.first_k_dense, scoring_func=cfg.router_score,
                  n_group=cfg.n_group, topk_group=cfg.topk_group,
-                 routed_scaling_factor=cfg.routed_scaling_factor, norm_topk_prob=cfg.norm_topk_prob)
+                 routed_scaling_factor=cfg.routed_scaling_factor, norm_topk_prob=cfg.norm_topk_prob,
+                 kv_lora_rank=cfg.kv_lora_rank, q_lora_rank=cfg.q_lora_rank or None,
+                 qk_nope_head_dim=cfg.qk_nope_head_dim, qk_rope_head_dim=cfg.qk_rope_head_dim,
+                 v_head_dim=cfg.v_head_dim, rope_interleave=cfg.rope_interleave)
+        if cfg.index_topk:
+            d.update(model_type="deepseek_v32", architectures=["DeepseekV32ForCausalLM"],
+                     index_n_heads=cfg.index_n_heads, index_head_dim=cfg.index_head_dim,
+                     index_topk=cfg.index_topk)
+    elif cfg.arch == "qwen3_next":
+        d.update(model_type="qwen3_next", architectures=["Qwen3NextForCausalLM"],
+                 full_attention_interval=cfg.linear_attn_interval,
+                 linear_num_key_heads=cfg.linear_num_key_heads,
+                 linear_num_value_heads=cfg.linear_num_value_heads,
+                 linear_key_head_dim=cfg.linear_key_head_dim,
+                 linear_value_head_dim=cfg.linear_value_head_dim,
+                 linear_conv_kernel_dim=cfg.linear_conv_kernel,
+                 num_experts=cfg.num_experts, num_experts_per_tok=cfg.topk,
+                 moe_intermediate_size=cfg.moe_intermediate_size)
     else:
         d.update(model_type="qwen3", architectures=["Qwen3ForCausalLM"])
     return d

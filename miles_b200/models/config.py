@@ -44,6 +44,7 @@ class ModelConfig:
     qk_nope_head_dim: int = 0
     qk_rope_head_dim: int = 0
     v_head_dim: int = 0
+    rope_interleave: bool = False  # MLA rotary dims stored as interleaved pairs (DeepSeek-V3 HF)
     # DSA (DeepSeek-V3.2 / GLM-5 sparse attention): lightning indexer + top-k key selection
     index_n_heads: int = 0
     index_head_dim: int = 0
@@ -118,13 +119,17 @@ class ModelConfig:
         c.head_dim = d.get("head_dim", c.hidden_size // c.num_heads)
         c.intermediate_size = d.get("intermediate_size", 0)
         c.rms_eps = d.get("rms_norm_eps", 1e-6)
-        c.rope_theta = d.get("rope_theta", 1e4)
+        # transformers >= 5 nests the rotary settings in `rope_parameters`
+        rp = d.get("rope_parameters") or {}
+        c.rope_theta = d.get("rope_theta", rp.get("rope_theta", 1e4))
         c.rope_scaling = d.get("rope_scaling")
+        if c.rope_scaling is None and rp.get("rope_type", "default") not in ("default", None):
+            c.rope_scaling = {k: v for k, v in rp.items() if k != "rope_theta"}
         c.max_position = d.get("max_position_embeddings", 32768)
         c.tie_embeddings = d.get("tie_word_embeddings", False)
         if mt == "qwen3_next":
             c.arch = "qwen3_next"
-            c.num_experts = d.get("num_experts", 0)
+            c.num_experts = d.get("num_experts", d.get("num_local_experts", 0))
             c.topk = d.get("num_experts_per_tok", 0)
             c.moe_intermediate_size = d.get("moe_intermediate_size", 0)
             c.norm_topk_prob = d.get("norm_topk_prob", True)
@@ -137,7 +142,7 @@ class ModelConfig:
             return c
         if mt in ("qwen3_moe",):
             c.arch = "qwen3_moe"
-            c.num_experts = d["num_experts"]
+            c.num_experts = d.get("num_experts", d.get("num_local_experts"))
             c.topk = d["num_experts_per_tok"]
             c.moe_intermediate_size = d["moe_intermediate_size"]
             c.norm_topk_prob = d.get("norm_topk_prob", True)
@@ -158,6 +163,7 @@ class ModelConfig:
             c.qk_nope_head_dim = d.get("qk_nope_head_dim", 0)
             c.qk_rope_head_dim = d.get("qk_rope_head_dim", 0)
             c.v_head_dim = d.get("v_head_dim", 0)
+            c.rope_interleave = bool(d.get("rope_interleave", False))
             c.qk_norm = False
             c.index_n_heads = d.get("index_n_heads", 0)
             c.index_head_dim = d.get("index_head_dim", 0)

@@ -77,8 +77,14 @@ def mla_param_shapes(cfg, p: str, tp_size: int = 1):
     return out
 
 
-def _rope(x: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """Rotate-half RoPE over the last dim of x [T, ..., d] at positions pos [T]."""
+def _rope(x: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+          interleaved: bool = False) -> torch.Tensor:
+    """Rotate-half RoPE over the last dim of x [T, ..., d] at positions pos [T]. `interleaved`:
+    the rotary pairs are adjacent dims (x0, x1), (x2, x3), ... and are first gathered into the
+    rotate-half layout (the result stays in that layout)."""
+    if interleaved:
+        shp = x.shape
+        x = x.reshape(*shp[:-1], shp[-1] // 2, 2).transpose(-1, -2).reshape(shp)
     d = x.shape[-1] // 2
     c = cos.index_select(0, pos.long())
     s = sin.index_select(0, pos.long())
@@ -161,8 +167,8 @@ class MLA:
         q = q.view(x.shape[0], self.nh, cfg.qk_nope_head_dim + cfg.qk_rope_head_dim)
         q_nope, q_pe = q.split([cfg.qk_nope_head_dim, cfg.qk_rope_head_dim], -1)
         if want_qa:
-            return q_nope, _rope(q_pe, pos, self.cos, self.sin), qa
-        return q_nope, _rope(q_pe, pos, self.cos, self.sin)
+            return q_nope, _rope(q_pe, pos, self.cos, self.sin, self.cfg.rope_interleave), qa
+        return q_nope, _rope(q_pe, pos, self.cos, self.sin, self.cfg.rope_interleave)
 
     def _latent(self, i: int, x: torch.Tensor, pos: torch.Tensor):
         cfg, m = self.cfg, self.m
@@ -170,7 +176,7 @@ class MLA:
         kva = m._lin(x, p + "kv_a_proj_with_mqa.weight")
         c, k_pe = kva.split([cfg.kv_lora_rank, cfg.qk_rope_head_dim], -1)
         c = rms_norm(c.contiguous(), m.params[p + "kv_a_layernorm.weight"], cfg.rms_eps)
-        return c, _rope(k_pe, pos, self.cos, self.sin)
+        return c, _rope(k_pe, pos, self.cos, self.sin, self.cfg.rope_interleave)
 
     def _expand(self, i: int, c: torch.Tensor, k_pe: torch.Tensor):
         cfg, m = self.cfg, self.m
