@@ -41,7 +41,7 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
             for n in P:
                 if n.startswith(L + "linear_attn."):
                     yield pre + n, P[n].data
-        elif cfg.kv_lora_rank:  # MLA parameters carry their HF names already
+        elif cfg.kv_lora_rank or cfg.attn_output_gate:  # MLA / gated attention: HF names already
             for n in P:
                 if n.startswith(L + "self_attn."):
                     yield pre + n, P[n].data
@@ -52,7 +52,7 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
             yield pre + L + "self_attn.k_proj.weight", k
             yield pre + L + "self_attn.v_proj.weight", v
             yield pre + L + "self_attn.o_proj.weight", P[L + "self_attn.o_proj.weight"].data
-        if cfg.qk_norm and not cfg.kv_lora_rank and not cfg.layer_is_linear(i):
+        if cfg.qk_norm and not cfg.kv_lora_rank and not cfg.layer_is_linear(i) and not cfg.attn_output_gate:
             yield pre + L + "self_attn.q_norm.weight", P[L + "self_attn.q_norm.weight"].data
             yield pre + L + "self_attn.k_norm.weight", P[L + "self_attn.k_norm.weight"].data
         if cfg.layer_is_moe(i):
@@ -66,6 +66,13 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
                 yield pre + L + f"mlp.experts.{e}.gate_proj.weight", w1[e, :I]
                 yield pre + L + f"mlp.experts.{e}.up_proj.weight", w1[e, I:]
                 yield pre + L + f"mlp.experts.{e}.down_proj.weight", w2[e]
+            if cfg.shared_expert_intermediate_size:
+                gu = P[L + "mlp.shared_expert.gate_up_proj.weight"].data
+                Is = gu.shape[0] // 2
+                yield pre + L + "mlp.shared_expert.gate_proj.weight", gu[:Is]
+                yield pre + L + "mlp.shared_expert.up_proj.weight", gu[Is:]
+                yield pre + L + "mlp.shared_expert.down_proj.weight", P[L + "mlp.shared_expert.down_proj.weight"].data
+                yield pre + L + "mlp.shared_expert_gate.weight", P[L + "mlp.shared_expert_gate.weight"].data
             if cfg.num_shared_experts:
                 gu = P[L + "mlp.shared_experts.gate_up_proj.weight"].data
                 Is = gu.shape[0] // 2
@@ -82,6 +89,49 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
         yield pre + "norm.weight", P["norm.weight"].data
     if not cfg.tie_embeddings and "lm_head.weight" in P:
         yield "lm_head.weight", P["lm_head.weight"].data
+
+
+_OFFSET_NORMS = ("input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_norm.weight",
+                 "self_attn.k_norm.weight")
+
+
+def _gdn_group_split(cfg):
+    nk, nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+    r = nv // nk
+    return nk, [cfg.linear_key_head_dim, cfg.linear_key_head_dim, r * cfg.linear_value_head_dim,
+                r * cfg.linear_value_head_dim], [r, r]
+
+
+def from_hf_layout(cfg: ModelConfig, name: str, t: torch.Tensor) -> torch.Tensor:
+    """HF checkpoint tensor -> this framework's layout (identity for most tensors):
+    zero-centred norms store 1 + w; Gated DeltaNet's in_proj_qkvz / in_proj_ba are regrouped
+    from per-key-head-group interleaving into contiguous [q; k; v; z] / [b; a] blocks, and
+    conv1d.weight drops its middle dim."""
+    if cfg.norm_offset and (name.endswith(_OFFSET_NORMS) or name == "model.norm.weight"):
+        return t.float() + 1.0
+    if name.endswith("linear_attn.in_proj_qkvz.weight") or name.endswith("linear_attn.in_proj_ba.weight"):
+        nk, sq, sb = _gdn_group_split(cfg)
+        sizes = sq if name.endswith("qkvz.weight") else sb
+        parts = t.view(nk, sum(sizes), -1).split(sizes, 1)
+        return torch.cat([p.reshape(-1, t.shape[-1]) for p in parts], 0)
+    if name.endswith("linear_attn.conv1d.weight") and t.dim() == 3:
+        return t[:, 0, :]
+    return t
+
+
+def to_hf_layout(cfg: ModelConfig, name: str, t: torch.Tensor) -> torch.Tensor:
+    """Inverse of from_hf_layout."""
+    if cfg.norm_offset and (name.endswith(_OFFSET_NORMS) or name == "model.norm.weight"):
+        return (t.float() - 1.0).to(t.dtype)
+    if name.endswith("linear_attn.in_proj_qkvz.weight") or name.endswith("linear_attn.in_proj_ba.weight"):
+        nk, sq, sb = _gdn_group_split(cfg)
+        sizes = sq if name.endswith("qkvz.weight") else sb
+        blocks = t.split([s * nk for s in sizes], 0)
+        per = [b.view(nk, s, -1) for b, s in zip(blocks, sizes)]
+        return torch.cat(per, 1).reshape(t.shape)
+    if name.endswith("linear_attn.conv1d.weight") and t.dim() == 2:
+        return t[:, None, :]
+    return t
 
 
 def hf_config_dict(cfg: ModelConfig) -> dict:
@@ -123,7 +173,13 @@ def hf_config_dict(cfg: ModelConfig) -> dict:
                  linear_value_head_dim=cfg.linear_value_head_dim,
                  linear_conv_kernel_dim=cfg.linear_conv_kernel,
                  num_experts=cfg.num_experts, num_experts_per_tok=cfg.topk,
-                 moe_intermediate_size=cfg.moe_intermediate_size)
+                 moe_intermediate_size=cfg.moe_intermediate_size,
+                 shared_expert_intermediate_size=cfg.shared_expert_intermediate_size,
+                 partial_rotary_factor=cfg.partial_rotary_factor, norm_topk_prob=cfg.norm_topk_prob,
+                 decoder_sparse_step=cfg.moe_layer_freq, mlp_only_layers=[],
+                 layer_types=["linear_attention" if cfg.layer_is_linear(i) else "full_attention"
+                              for i in range(cfg.num_layers)])
+        d["rope_parameters"]["partial_rotary_factor"] = cfg.partial_rotary_factor
     else:
         d.update(model_type="qwen3", architectures=["Qwen3ForCausalLM"])
     return d
@@ -159,6 +215,7 @@ def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> No
         t = tp_gather(name, t.detach(), model.tp)
         if not writer or name in skip:
             continue
+        t = to_hf_layout(model.cfg, name, t)
         t = t.to("cpu").contiguous().clone()
         nb = t.numel() * t.element_size()
         if size + nb > max_shard_bytes:
@@ -218,4 +275,5 @@ def load_hf(model: Transformer, path: str) -> None:
             if name == "lm_head.weight" and cfg.tie_embeddings:
                 continue
             raise KeyError(f"{name} missing from {path}")
-        dst.copy_(tp_slice(name, get(src_name), model.tp).to(dst.dtype))
+        src = from_hf_layout(cfg, name, get(src_name))
+        dst.copy_(tp_slice(name, src, model.tp).to(dst.dtype))

@@ -57,6 +57,11 @@ class ModelConfig:
     linear_key_head_dim: int = 0
     linear_value_head_dim: int = 0
     linear_conv_kernel: int = 4
+    # Qwen3-Next full-attention layers: output gate, partial rotary; MoE shared expert with a gate
+    attn_output_gate: bool = False
+    partial_rotary_factor: float = 1.0
+    norm_offset: bool = False          # checkpoint RMSNorm weights are w in y = x_hat * (1 + w)
+    shared_expert_intermediate_size: int = 0
     extra: dict = field(default_factory=dict)
 
     @property
@@ -139,6 +144,12 @@ class ModelConfig:
             c.linear_key_head_dim = d["linear_key_head_dim"]
             c.linear_value_head_dim = d["linear_value_head_dim"]
             c.linear_conv_kernel = d.get("linear_conv_kernel_dim", 4)
+            c.intermediate_size = d.get("intermediate_size", 0)
+            c.attn_output_gate = True
+            c.norm_offset = True
+            c.partial_rotary_factor = d.get("partial_rotary_factor", rp.get("partial_rotary_factor", 1.0))
+            c.shared_expert_intermediate_size = d.get("shared_expert_intermediate_size", 0)
+            c.moe_layer_freq = d.get("decoder_sparse_step", 1)
             return c
         if mt in ("qwen3_moe",):
             c.arch = "qwen3_moe"
@@ -218,7 +229,9 @@ def preset(name: str) -> ModelConfig:
                            num_heads=4, num_kv_heads=2, head_dim=128, intermediate_size=512,
                            tie_embeddings=True, max_position=4096, linear_attn_interval=4,
                            linear_num_key_heads=2, linear_num_value_heads=4,
-                           linear_key_head_dim=32, linear_value_head_dim=32)
+                           linear_key_head_dim=32, linear_value_head_dim=32, attn_output_gate=True,
+                           partial_rotary_factor=0.25, norm_offset=True, num_experts=8, topk=2,
+                           moe_intermediate_size=128, shared_expert_intermediate_size=192)
     if n in ("tiny-dsa",):  # MLA + lightning indexer with top-k sparse attention (DSA)
         return ModelConfig(arch="deepseek_v3", vocab_size=4096, hidden_size=256, num_layers=2,
                            num_heads=4, num_kv_heads=4, head_dim=128, intermediate_size=512,

@@ -5,7 +5,7 @@ fixed-size recurrent state per head (keys -> values, [dk, dv]):
 
     qkvz = x W_qkvz^T  (q, k: nk heads of dk; v, z: nv heads of dv),   (b, a) = x W_ba^T
     q, k, v <- SiLU(causal depthwise conv1d over time, kernel K)          (channels of q, k, v)
-    q, k    <- L2-normalised per head, repeated to the nv value heads
+    q, k    <- L2-normalised per head (x / sqrt(|x|^2 + 1e-6)), repeated to the nv value heads
     beta = sigmoid(b),  g = -exp(A_log) * softplus(a + dt_bias)           (log decay per step)
     S_t = exp(g_t) S_{t-1};  S_t += k_t (beta_t (v_t - S_t^T k_t))^T;  o_t = S_t^T q_t / sqrt(dk)
     out = W_out (RMSNorm(o) * w_norm * SiLU(z))
@@ -53,6 +53,11 @@ def gdn_state_shapes(cfg):
     return (2 * nk * dk + nv * dv, K - 1), (nv, dk, dv)
 
 
+def _l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """x / sqrt(sum(x^2) + eps) over the last dim (the eps inside the root, as the HF layer)."""
+    return x * torch.rsqrt(x.pow(2).sum(-1, keepdim=True) + eps)
+
+
 class GDN:
     def __init__(self, model):
         self.m = model
@@ -89,8 +94,8 @@ class GDN:
         q, k, v = conv.split([nk * dk, nk * dk, nv * dv], -1)
         T = conv.shape[0]
         r = nv // nk
-        q = F.normalize(q.view(T, nk, dk), dim=-1).repeat_interleave(r, 1)
-        k = F.normalize(k.view(T, nk, dk), dim=-1).repeat_interleave(r, 1)
+        q = _l2norm(q.view(T, nk, dk)).repeat_interleave(r, 1)
+        k = _l2norm(k.view(T, nk, dk)).repeat_interleave(r, 1)
         return q, k, v.view(T, nv, dv)
 
     def _recur(self, q, k, v, beta, g, S):
@@ -187,8 +192,8 @@ class GDN:
         nk, nv, dk, dv = self.nk, self.nv, self.dk, self.dv
         q, k, v = conv.split([nk * dk, nk * dk, nv * dv], -1)
         r = nv // nk
-        q = F.normalize(q.view(B, nk, dk), dim=-1).repeat_interleave(r, 1)
-        k = F.normalize(k.view(B, nk, dk), dim=-1).repeat_interleave(r, 1)
+        q = _l2norm(q.view(B, nk, dk)).repeat_interleave(r, 1)
+        k = _l2norm(k.view(B, nk, dk)).repeat_interleave(r, 1)
         v = v.view(B, nv, dv)
         S = S * torch.exp(g)[:, :, None, None]
         err = v - torch.einsum("bhk,bhkv->bhv", k, S)

@@ -71,6 +71,10 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=Non
             from miles_b200.models.gdn import gdn_param_shapes
 
             specs += [ParamSpec(n, shp, init) for n, shp, init in gdn_param_shapes(cfg, p + "linear_attn.")]
+        elif cfg.attn_output_gate:  # Qwen3-Next gated full attention (models/qwen3_next.py)
+            from miles_b200.models.qwen3_next import gated_attn_param_shapes
+
+            specs += [ParamSpec(n, shp, init) for n, shp, init in gated_attn_param_shapes(cfg, p + "self_attn.")]
         elif cfg.kv_lora_rank:  # multi-head latent attention (models/mla.py)
             from miles_b200.models.mla import mla_param_shapes
 
@@ -90,6 +94,11 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=Non
                       ParamSpec(p + "mlp.experts.w2", (El, H, I), "normal")]
             if cfg.router_score == "sigmoid":
                 specs.append(ParamSpec(p + "mlp.gate.e_score_correction_bias", (E,), "zeros"))
+            if cfg.shared_expert_intermediate_size:  # Qwen3-Next: one gated shared expert
+                Is = cfg.shared_expert_intermediate_size // t
+                specs += [ParamSpec(p + "mlp.shared_expert.gate_up_proj.weight", (2 * Is, H), "normal"),
+                          ParamSpec(p + "mlp.shared_expert.down_proj.weight", (H, Is), "normal"),
+                          ParamSpec(p + "mlp.shared_expert_gate.weight", (1, H), "normal")]
             if cfg.num_shared_experts:
                 Is = cfg.moe_intermediate_size * cfg.num_shared_experts // t
                 specs += [ParamSpec(p + "mlp.shared_experts.gate_up_proj.weight", (2 * Is, H), "normal"),
@@ -258,6 +267,13 @@ class Transformer(torch.nn.Module):
             if self.tp is not None or self.sequence_parallel:
                 raise ValueError("linear-attention layers run without TP / SP")
             self.gdn = GDN(self)
+        self.gattn = None
+        if cfg.attn_output_gate:
+            from miles_b200.models.qwen3_next import GatedAttention
+
+            if self.tp is not None:
+                raise ValueError("gated attention layers run without TP")
+            self.gattn = GatedAttention(self)
         self.mla = None
         if cfg.kv_lora_rank:
             from miles_b200.models.mla import MLA
@@ -307,6 +323,8 @@ class Transformer(torch.nn.Module):
         cfg = self.cfg
         if self.gdn is not None and cfg.layer_is_linear(i):
             return self.gdn.attn(i, x, meta)
+        if self.gattn is not None:
+            return self.gattn.attn(i, x, meta)
         if self.mla is not None:
             return self.mla.attn(i, x, meta)
         pre = f"layers.{i}.self_attn."
@@ -338,6 +356,10 @@ class Transformer(torch.nn.Module):
             if self.cfg.num_shared_experts:
                 s = G.linear_swiglu(x, self.params[pre + "shared_experts.gate_up_proj.weight"])
                 y = y + G.linear(s, self.params[pre + "shared_experts.down_proj.weight"])
+            if self.cfg.shared_expert_intermediate_size:
+                s = G.linear_swiglu(x, self.params[pre + "shared_expert.gate_up_proj.weight"])
+                gate = torch.sigmoid((x.float() @ self.params[pre + "shared_expert_gate.weight"].float().t()))
+                y = y + (gate * G.linear(s, self.params[pre + "shared_expert.down_proj.weight"]).float()).to(y.dtype)
             return y
         return self._lin(self._lin_swiglu(x, pre + "gate_up_proj.weight"), pre + "down_proj.weight")
 
@@ -450,6 +472,16 @@ class Transformer(torch.nn.Module):
             x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
             return self._mlp(i, x2, replay=replay), r
         pre = f"layers.{i}.self_attn."
+        if self.gattn is not None:  # gated attention (Qwen3-Next): same head exchange
+            q, k, v, gate = self.gattn._qkv(i, x, pos)
+            qh, kh, vh = tokens_to_heads(q, cp), tokens_to_heads(k, cp), tokens_to_heads(v, cp)
+            if self.gattn._native(x):
+                oh = varlen_attention(qh, kh, vh, meta)
+            else:
+                oh = self.gattn._sdpa(qh, kh, vh, meta.cu_list)
+            a = self.gattn._out(i, heads_to_tokens(oh, cp), gate)
+            x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
+            return self._mlp(i, x2, replay=replay), r
         qkv = self._lin(x, pre + "qkv_proj.weight")
         q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
                                self.params.get(pre + "k_norm.weight"), pos,
@@ -602,6 +634,8 @@ class Transformer(torch.nn.Module):
             post = self.params[f"layers.{i}.post_attention_layernorm.weight"]
             if self.gdn is not None and cfg.layer_is_linear(i):
                 x2, r = self._add_norm(self.gdn.attn(i, x, meta, cache, state_rows), r, post)
+            elif self.gattn is not None:
+                x2, r = self._add_norm(self.gattn.attn(i, x, meta, cache, slots), r, post)
             elif self.mla is not None:
                 x2, r = self._add_norm(self.mla.attn(i, x, meta, cache, slots, pending=True), r, post)
             else:
@@ -637,6 +671,8 @@ class Transformer(torch.nn.Module):
             post = self.params[f"layers.{i}.post_attention_layernorm.weight"]
             if self.gdn is not None and cfg.layer_is_linear(i):
                 a = self.gdn.decode(i, x, cache, state_rows)
+            elif self.gattn is not None:
+                a = self.gattn.decode(i, x, positions, cache, page_table, ctx_lens, slots)
             elif self.mla is not None:
                 a = self.mla.decode(i, x, positions, cache, page_table, ctx_lens, slots, pending=True)
             else:

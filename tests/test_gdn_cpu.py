@@ -24,7 +24,7 @@ def test_gdn_decode_matches_full_forward():
     cfg = preset("tiny-gdn")
     m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=0)
     assert m.gdn is not None and "layers.0.linear_attn.in_proj_qkvz.weight" in m.params
-    assert "layers.3.self_attn.qkv_proj.weight" in m.params
+    assert "layers.3.self_attn.q_proj.weight" in m.params
     eng = RolloutEngine(m, max_batch=4, num_pages=64, max_pages_per_seq=8, use_cuda_graph=False)
     rng = np.random.default_rng(2)
     prompts = [rng.integers(0, cfg.vocab_size, n).tolist() for n in (7, 33, 18)]
@@ -70,7 +70,7 @@ def test_gdn_recurrence_reference_and_backward():
     h = m.forward_train(toks, VarlenMeta([0, 11, 30], "cpu"))
     h.pow(2).mean().backward()
     for n in ("layers.0.linear_attn.A_log", "layers.1.linear_attn.conv1d.weight",
-              "layers.2.linear_attn.in_proj_qkvz.weight", "layers.3.self_attn.qkv_proj.weight"):
+              "layers.2.linear_attn.in_proj_qkvz.weight", "layers.3.self_attn.q_proj.weight"):
         assert m.params[n].grad is not None and m.params[n].grad.abs().sum() > 0, n
 
 

@@ -61,3 +61,46 @@ def test_matches_transformers(tmp_path, name):
     with torch.no_grad():
         back = hf2(toks).logits[0].float()
     assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
+
+
+def test_qwen3_next_matches_transformers(tmp_path):
+    """Qwen3-Next hybrid: Gated DeltaNet layers (HF's torch fallback of the chunked gated delta
+    rule), gated full attention with partial rotary, zero-centred norms, MoE with a gated shared
+    expert."""
+    from transformers import Qwen3NextConfig, Qwen3NextForCausalLM
+
+    from miles_b200.checkpoint.hf import load_hf, save_hf
+    from miles_b200.models.config import ModelConfig
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops.attention import VarlenMeta
+
+    torch.manual_seed(0)
+    hc = Qwen3NextConfig(vocab_size=512, hidden_size=256, intermediate_size=512, moe_intermediate_size=128,
+                         shared_expert_intermediate_size=192, num_hidden_layers=4, num_attention_heads=4,
+                         num_key_value_heads=2, head_dim=128, num_experts=8, num_experts_per_tok=2,
+                         linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=32,
+                         linear_value_head_dim=32, linear_conv_kernel_dim=4, full_attention_interval=4,
+                         decoder_sparse_step=1, norm_topk_prob=True, tie_word_embeddings=False)
+    hf = Qwen3NextForCausalLM(hc).eval()
+    with torch.no_grad():  # non-trivial zero-centred norm offsets and decays
+        for n, p in hf.named_parameters():
+            if n.endswith(("layernorm.weight", "q_norm.weight", "k_norm.weight", "model.norm.weight")):
+                p.normal_(0, 0.1)
+            if n.endswith("A_log"):
+                p.uniform_(-1, 1)
+    hf.save_pretrained(str(tmp_path / "hf"))
+    cfg = ModelConfig.from_hf(str(tmp_path / "hf"))
+    assert cfg.layer_is_linear(0) and not cfg.layer_is_linear(3) and cfg.partial_rotary_factor == 0.25
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=1)
+    load_hf(m, str(tmp_path / "hf"))
+    toks = torch.randint(0, cfg.vocab_size, (1, 37))
+    with torch.no_grad():
+        ref = hf(toks).logits[0].float()
+        h = m.forward_train(toks[0].int(), VarlenMeta([0, 37], "cpu"))
+        ours = h.float() @ m.lm_head_weight().float().t()
+    assert (ref - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item()), (ref - ours).abs().max()
+    save_hf(m, str(tmp_path / "ours"))
+    hf2 = Qwen3NextForCausalLM.from_pretrained(str(tmp_path / "ours"), torch_dtype=torch.float32).eval()
+    with torch.no_grad():
+        back = hf2(toks).logits[0].float()
+    assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
