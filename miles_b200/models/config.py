@@ -157,13 +157,16 @@ class ModelConfig:
             c.topk = d["num_experts_per_tok"]
             c.moe_intermediate_size = d["moe_intermediate_size"]
             c.norm_topk_prob = d.get("norm_topk_prob", True)
-        elif mt in ("deepseek_v3", "deepseek_v2", "deepseek_v32", "kimi_k2", "glm4_moe_lite"):
+        elif mt in ("deepseek_v3", "deepseek_v2", "deepseek_v32", "kimi_k2", "glm4_moe_lite", "glm_moe_dsa"):
             c.arch = "deepseek_v3"
             c.num_experts = d["n_routed_experts"]
             c.topk = d["num_experts_per_tok"]
             c.moe_intermediate_size = d["moe_intermediate_size"]
             c.num_shared_experts = d.get("n_shared_experts", 0)
             c.first_k_dense = d.get("first_k_dense_replace", 0)
+            if "mlp_layer_types" in d:  # GLM-5: leading dense layers named per layer
+                kinds = d["mlp_layer_types"]
+                c.first_k_dense = next((i for i, t in enumerate(kinds) if t == "sparse"), len(kinds))
             c.router_score = d.get("scoring_func", "sigmoid")
             c.n_group = d.get("n_group", 1)
             c.topk_group = d.get("topk_group", 1)

@@ -113,7 +113,7 @@ class MLA:
     # ------------------------------------------------------------------ projections
     # ------------------------------------------------------------------ DSA indexer
     def _index_q(self, i: int, qa: torch.Tensor, pos: torch.Tensor):
-        """Indexer queries [T, nI, dI] (rotary on the last qk_rope_head_dim dims)."""
+        """Indexer queries [T, nI, dI] (rotary on the first qk_rope_head_dim dims)."""
         cfg = self.cfg
         p = f"layers.{i}.self_attn.indexer."
         q = F.linear(qa.float(), self.m.params[p + "wq_b.weight"].float())
@@ -121,7 +121,7 @@ class MLA:
         return self._index_rope(q, pos)
 
     def _index_k(self, i: int, x: torch.Tensor, pos: torch.Tensor):
-        """Indexer keys [T, dI] (LayerNorm, rotary on the last qk_rope_head_dim dims)."""
+        """Indexer keys [T, dI] (LayerNorm, rotary on the first qk_rope_head_dim dims)."""
         cfg, P = self.cfg, self.m.params
         p = f"layers.{i}.self_attn.indexer."
         k = F.linear(x.float(), P[p + "wk.weight"].float())
@@ -130,8 +130,9 @@ class MLA:
         return self._index_rope(k, pos)
 
     def _index_rope(self, t: torch.Tensor, pos: torch.Tensor):
+        """Rotary (rotate-half) on the first qk_rope_head_dim dims of the indexer heads."""
         dr = self.cfg.qk_rope_head_dim
-        return torch.cat([t[..., :-dr], _rope(t[..., -dr:], pos, self.cos, self.sin)], -1)
+        return torch.cat([_rope(t[..., :dr], pos, self.cos, self.sin), t[..., dr:]], -1)
 
     def _index_weights(self, i: int, x: torch.Tensor):
         cfg = self.cfg

@@ -104,3 +104,38 @@ def test_qwen3_next_matches_transformers(tmp_path):
     with torch.no_grad():
         back = hf2(toks).logits[0].float()
     assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
+
+
+def test_glm5_dsa_matches_transformers(tmp_path):
+    """GLM-5 (DSA): MLA + lightning indexer top-k sparse attention + grouped sigmoid MoE, with
+    sequences longer than index_topk so the key selection is active."""
+    from transformers import GlmMoeDsaConfig, GlmMoeDsaForCausalLM
+
+    from miles_b200.checkpoint.hf import load_hf
+    from miles_b200.models.config import ModelConfig
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops.attention import VarlenMeta
+
+    torch.manual_seed(0)
+    hc = GlmMoeDsaConfig(vocab_size=512, hidden_size=256, intermediate_size=512, moe_intermediate_size=128,
+                         num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=4,
+                         n_routed_experts=8, num_experts_per_tok=2, n_shared_experts=1, n_group=1,
+                         topk_group=1, routed_scaling_factor=2.5, kv_lora_rank=64, q_lora_rank=96,
+                         qk_nope_head_dim=32, qk_rope_head_dim=16, v_head_dim=32, index_n_heads=16,
+                         index_head_dim=32, index_topk=12, mlp_layer_types=["dense", "sparse"],
+                         tie_word_embeddings=False)
+    # eager attention: transformers' SDPA path for this model combines the index mask with no
+    # causal mask when it has none to pass (non-causal attention)
+    hc._attn_implementation = "eager"
+    hf = GlmMoeDsaForCausalLM(hc).eval()
+    hf.save_pretrained(str(tmp_path / "hf"))
+    cfg = ModelConfig.from_hf(str(tmp_path / "hf"))
+    assert cfg.index_topk == 12 and cfg.first_k_dense == 1
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=1)
+    load_hf(m, str(tmp_path / "hf"))
+    toks = torch.randint(0, cfg.vocab_size, (1, 40))
+    with torch.no_grad():
+        ref = hf(toks).logits[0].float()
+        h = m.forward_train(toks[0].int(), VarlenMeta([0, 40], "cpu"))
+        ours = h.float() @ m.lm_head_weight().float().t()
+    assert (ref - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item()), (ref - ours).abs().max()
