@@ -41,7 +41,7 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
             for n in P:
                 if n.startswith(L + "linear_attn."):
                     yield pre + n, P[n].data
-        elif cfg.kv_lora_rank or cfg.attn_output_gate:  # MLA / gated attention: HF names already
+        elif cfg.kv_lora_rank or cfg.uses_torch_attention:  # MLA / separate q,k,v: HF names already
             for n in P:
                 if n.startswith(L + "self_attn."):
                     yield pre + n, P[n].data
@@ -52,7 +52,7 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
             yield pre + L + "self_attn.k_proj.weight", k
             yield pre + L + "self_attn.v_proj.weight", v
             yield pre + L + "self_attn.o_proj.weight", P[L + "self_attn.o_proj.weight"].data
-        if cfg.qk_norm and not cfg.kv_lora_rank and not cfg.layer_is_linear(i) and not cfg.attn_output_gate:
+        if cfg.qk_norm and not cfg.kv_lora_rank and not cfg.layer_is_linear(i) and not cfg.uses_torch_attention:
             yield pre + L + "self_attn.q_norm.weight", P[L + "self_attn.q_norm.weight"].data
             yield pre + L + "self_attn.k_norm.weight", P[L + "self_attn.k_norm.weight"].data
         if cfg.layer_is_moe(i):
@@ -164,6 +164,15 @@ def hf_config_dict(cfg: ModelConfig) -> dict:
             d.update(model_type="deepseek_v32", architectures=["DeepseekV32ForCausalLM"],
                      index_n_heads=cfg.index_n_heads, index_head_dim=cfg.index_head_dim,
                      index_topk=cfg.index_topk)
+    elif cfg.arch == "glm4_moe":
+        d.update(model_type="glm4_moe", architectures=["Glm4MoeForCausalLM"],
+                 n_routed_experts=cfg.num_experts, num_experts_per_tok=cfg.topk,
+                 moe_intermediate_size=cfg.moe_intermediate_size, n_shared_experts=cfg.num_shared_experts,
+                 first_k_dense_replace=cfg.first_k_dense, n_group=cfg.n_group, topk_group=cfg.topk_group,
+                 routed_scaling_factor=cfg.routed_scaling_factor, norm_topk_prob=cfg.norm_topk_prob,
+                 attention_bias=cfg.attention_bias, use_qk_norm=cfg.qk_norm,
+                 partial_rotary_factor=cfg.partial_rotary_factor)
+        d["rope_parameters"]["partial_rotary_factor"] = cfg.partial_rotary_factor
     elif cfg.arch == "qwen3_next":
         d.update(model_type="qwen3_next", architectures=["Qwen3NextForCausalLM"],
                  full_attention_interval=cfg.linear_attn_interval,

@@ -62,11 +62,19 @@ class ModelConfig:
     partial_rotary_factor: float = 1.0
     norm_offset: bool = False          # checkpoint RMSNorm weights are w in y = x_hat * (1 + w)
     shared_expert_intermediate_size: int = 0
+    attention_bias: bool = False       # q / k / v projection biases (GLM-4.5)
     extra: dict = field(default_factory=dict)
 
     @property
     def is_moe(self) -> bool:
         return self.num_experts > 0
+
+    @property
+    def uses_torch_attention(self) -> bool:
+        """Softmax attention with an output gate, projection biases or partial rotary: the
+        separate q / k / v projection path of models/qwen3_next.py instead of the fused
+        qkv + QK-norm/RoPE kernel."""
+        return self.attn_output_gate or self.attention_bias or self.partial_rotary_factor != 1.0
 
     def layer_is_linear(self, i: int) -> bool:
         return self.linear_attn_interval > 0 and (i + 1) % self.linear_attn_interval != 0
@@ -132,6 +140,22 @@ class ModelConfig:
             c.rope_scaling = {k: v for k, v in rp.items() if k != "rope_theta"}
         c.max_position = d.get("max_position_embeddings", 32768)
         c.tie_embeddings = d.get("tie_word_embeddings", False)
+        if mt == "glm4_moe":  # GLM-4.5: GQA with biases / partial rotary, DeepSeek-style MoE
+            c.arch = "glm4_moe"
+            c.num_experts = d["n_routed_experts"]
+            c.topk = d["num_experts_per_tok"]
+            c.moe_intermediate_size = d["moe_intermediate_size"]
+            c.num_shared_experts = d.get("n_shared_experts", 0)
+            c.first_k_dense = d.get("first_k_dense_replace", 0)
+            c.router_score = "sigmoid"
+            c.n_group = d.get("n_group", 1)
+            c.topk_group = d.get("topk_group", 1)
+            c.routed_scaling_factor = d.get("routed_scaling_factor", 1.0)
+            c.norm_topk_prob = d.get("norm_topk_prob", True)
+            c.attention_bias = bool(d.get("attention_bias", False))
+            c.qk_norm = bool(d.get("use_qk_norm", False))
+            c.partial_rotary_factor = d.get("partial_rotary_factor", rp.get("partial_rotary_factor", 1.0))
+            return c
         if mt == "qwen3_next":
             c.arch = "qwen3_next"
             c.num_experts = d.get("num_experts", d.get("num_local_experts", 0))

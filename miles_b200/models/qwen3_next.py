@@ -1,4 +1,6 @@
-"""Full-attention layers of Qwen3-Next-style hybrids: gated softmax attention.
+"""Softmax attention with separate q / k / v projections, for the families whose attention the
+fused qkv + QK-norm/RoPE kernel path does not cover: Qwen3-Next's gated attention and GLM-4.5's
+attention with projection biases and half-width rotary.
 
 Every `linear_attn_interval`-th layer of a Qwen3-Next model keeps softmax attention with three
 differences from Qwen3's:
@@ -26,10 +28,15 @@ from miles_b200.models.mla import _rope
 
 def gated_attn_param_shapes(cfg, p: str):
     H, D, nq, nkv = cfg.hidden_size, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads
-    return [(p + "q_proj.weight", (2 * nq * D, H), "normal"),
-            (p + "k_proj.weight", (nkv * D, H), "normal"),
-            (p + "v_proj.weight", (nkv * D, H), "normal"),
-            (p + "o_proj.weight", (H, nq * D), "normal")]
+    g = 2 if cfg.attn_output_gate else 1
+    out = [(p + "q_proj.weight", (g * nq * D, H), "normal"),
+           (p + "k_proj.weight", (nkv * D, H), "normal"),
+           (p + "v_proj.weight", (nkv * D, H), "normal"),
+           (p + "o_proj.weight", (H, nq * D), "normal")]
+    if cfg.attention_bias:
+        out += [(p + "q_proj.bias", (g * nq * D,), "zeros"), (p + "k_proj.bias", (nkv * D,), "zeros"),
+                (p + "v_proj.bias", (nkv * D,), "zeros")]
+    return out
 
 
 def _head_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
@@ -57,19 +64,31 @@ class GatedAttention:
         cfg, m, D = self.cfg, self.m, self.D
         p = f"layers.{i}.self_attn."
         T = x.shape[0]
-        qg = m._lin(x, p + "q_proj.weight").view(T, cfg.num_heads, 2 * D)
-        q, gate = qg[..., :D], qg[..., D:].reshape(T, cfg.num_heads * D)
-        k = m._lin(x, p + "k_proj.weight").view(T, cfg.num_kv_heads, D)
-        v = m._lin(x, p + "v_proj.weight").view(T, cfg.num_kv_heads, D)
-        q = _head_norm(q, m.params[p + "q_norm.weight"], cfg.rms_eps)
-        k = _head_norm(k, m.params[p + "k_norm.weight"], cfg.rms_eps)
+
+        def proj(name):
+            y = m._lin(x, p + name + ".weight")
+            b = m.params.get(p + name + ".bias")
+            return y if b is None else y + b.to(y.dtype)
+
+        if cfg.attn_output_gate:
+            qg = proj("q_proj").view(T, cfg.num_heads, 2 * D)
+            q, gate = qg[..., :D], qg[..., D:].reshape(T, cfg.num_heads * D)
+        else:
+            q, gate = proj("q_proj").view(T, cfg.num_heads, D), None
+        k = proj("k_proj").view(T, cfg.num_kv_heads, D)
+        v = proj("v_proj").view(T, cfg.num_kv_heads, D)
+        if cfg.qk_norm:
+            q = _head_norm(q, m.params[p + "q_norm.weight"], cfg.rms_eps)
+            k = _head_norm(k, m.params[p + "k_norm.weight"], cfg.rms_eps)
         r = self.rot
         q = torch.cat([_rope(q[..., :r], pos, self.cos, self.sin), q[..., r:]], -1).contiguous()
         k = torch.cat([_rope(k[..., :r], pos, self.cos, self.sin), k[..., r:]], -1).contiguous()
         return q, k, v.contiguous(), gate
 
-    def _out(self, i: int, o: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
-        o = o.reshape(gate.shape) * torch.sigmoid(gate.float()).to(o.dtype)
+    def _out(self, i: int, o: torch.Tensor, gate) -> torch.Tensor:
+        o = o.reshape(o.shape[0], -1)
+        if gate is not None:
+            o = o * torch.sigmoid(gate.float()).to(o.dtype)
         return self.m._lin(o, f"layers.{i}.self_attn.o_proj.weight")
 
     def _sdpa(self, q, k, v, cu):

@@ -71,7 +71,7 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=Non
             from miles_b200.models.gdn import gdn_param_shapes
 
             specs += [ParamSpec(n, shp, init) for n, shp, init in gdn_param_shapes(cfg, p + "linear_attn.")]
-        elif cfg.attn_output_gate:  # Qwen3-Next gated full attention (models/qwen3_next.py)
+        elif cfg.uses_torch_attention:  # gated / biased / partial-rotary attention (models/qwen3_next.py)
             from miles_b200.models.qwen3_next import gated_attn_param_shapes
 
             specs += [ParamSpec(n, shp, init) for n, shp, init in gated_attn_param_shapes(cfg, p + "self_attn.")]
@@ -268,7 +268,7 @@ class Transformer(torch.nn.Module):
                 raise ValueError("linear-attention layers run without TP / SP")
             self.gdn = GDN(self)
         self.gattn = None
-        if cfg.attn_output_gate:
+        if cfg.uses_torch_attention and not cfg.kv_lora_rank:
             from miles_b200.models.qwen3_next import GatedAttention
 
             if self.tp is not None:

@@ -139,3 +139,45 @@ def test_glm5_dsa_matches_transformers(tmp_path):
         h = m.forward_train(toks[0].int(), VarlenMeta([0, 40], "cpu"))
         ours = h.float() @ m.lm_head_weight().float().t()
     assert (ref - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item()), (ref - ours).abs().max()
+
+
+def test_glm45_moe_matches_transformers(tmp_path):
+    """GLM-4.5 (glm4_moe): attention with q/k/v biases, QK-norm and half-width rotary; grouped
+    sigmoid MoE with a shared expert after one dense layer."""
+    from transformers import Glm4MoeConfig, Glm4MoeForCausalLM
+
+    from miles_b200.checkpoint.hf import load_hf, save_hf
+    from miles_b200.models.config import ModelConfig
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops.attention import VarlenMeta
+
+    torch.manual_seed(0)
+    hc = Glm4MoeConfig(vocab_size=512, hidden_size=256, intermediate_size=512, moe_intermediate_size=128,
+                       num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                       n_routed_experts=8, num_experts_per_tok=2, n_shared_experts=1, first_k_dense_replace=1,
+                       n_group=2, topk_group=1, routed_scaling_factor=2.5, attention_bias=True,
+                       use_qk_norm=True, partial_rotary_factor=0.5, tie_word_embeddings=False)
+    hf = Glm4MoeForCausalLM(hc).eval()
+    with torch.no_grad():
+        for n, p in hf.named_parameters():
+            if n.endswith("_proj.bias"):
+                p.normal_(0, 0.1)
+        for mod in hf.modules():
+            if hasattr(mod, "e_score_correction_bias"):
+                mod.e_score_correction_bias.normal_(0, 0.1)
+    hf.save_pretrained(str(tmp_path / "hf"))
+    cfg = ModelConfig.from_hf(str(tmp_path / "hf"))
+    assert cfg.attention_bias and cfg.partial_rotary_factor == 0.5 and cfg.uses_torch_attention
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=1)
+    load_hf(m, str(tmp_path / "hf"))
+    toks = torch.randint(0, cfg.vocab_size, (1, 33))
+    with torch.no_grad():
+        ref = hf(toks).logits[0].float()
+        h = m.forward_train(toks[0].int(), VarlenMeta([0, 33], "cpu"))
+        ours = h.float() @ m.lm_head_weight().float().t()
+    assert (ref - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item()), (ref - ours).abs().max()
+    save_hf(m, str(tmp_path / "ours"))
+    hf2 = Glm4MoeForCausalLM.from_pretrained(str(tmp_path / "ours"), torch_dtype=torch.float32).eval()
+    with torch.no_grad():
+        back = hf2(toks).logits[0].float()
+    assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
