@@ -189,6 +189,11 @@ def hf_config_dict(cfg: ModelConfig) -> dict:
                  layer_types=["linear_attention" if cfg.layer_is_linear(i) else "full_attention"
                               for i in range(cfg.num_layers)])
         d["rope_parameters"]["partial_rotary_factor"] = cfg.partial_rotary_factor
+    elif cfg.arch in ("qwen2", "llama", "mistral"):
+        cls = {"qwen2": "Qwen2ForCausalLM", "llama": "LlamaForCausalLM", "mistral": "MistralForCausalLM"}
+        d.update(model_type=cfg.arch, architectures=[cls[cfg.arch]])
+        if cfg.arch != "qwen2":
+            d.update(attention_bias=cfg.attention_bias, mlp_bias=False)
     else:
         d.update(model_type="qwen3", architectures=["Qwen3ForCausalLM"])
     return d

@@ -209,6 +209,8 @@ class ModelConfig:
         else:
             c.arch = "qwen3" if mt == "qwen3" else mt
             c.qk_norm = mt == "qwen3"
+            # Qwen2 / Qwen2.5 carry q/k/v biases without a config flag; Llama-style configs say
+            c.attention_bias = bool(d.get("attention_bias", mt == "qwen2"))
         return c
 
 

@@ -102,7 +102,8 @@ _ROPE_CACHE: dict = {}
 
 def rope_tables(max_pos: int, head_dim: int, theta: float, device, scaling: dict | None = None):
     """cos/sin tables [max_pos, head_dim/2] fp32 (rotate-half convention). `scaling` accepts
-    the HF rope_scaling dict for 'yarn' (DeepSeek/MLA) and 'linear'."""
+    the HF rope_scaling dict for 'yarn' (DeepSeek/MLA), 'llama3' (Llama 3.1 frequency bands)
+    and 'linear'."""
     key = (max_pos, head_dim, theta, str(device), repr(scaling))
     t = _ROPE_CACHE.get(key)
     if t is not None:
@@ -115,6 +116,15 @@ def rope_tables(max_pos: int, head_dim: int, theta: float, device, scaling: dict
         factor = float(scaling.get("factor", 1.0))
         if typ == "linear":
             inv = inv / factor
+        elif typ == "llama3":
+            # long wavelengths divided by `factor`, short ones kept, a linear blend between
+            orig = float(scaling.get("original_max_position_embeddings", 8192))
+            lo, hi = float(scaling.get("low_freq_factor", 1.0)), float(scaling.get("high_freq_factor", 4.0))
+            wavelen = 2 * math.pi / inv
+            smooth = ((orig / wavelen - lo) / (hi - lo)).clamp(0, 1)
+            inv = torch.where(wavelen < orig / hi, inv,
+                              torch.where(wavelen > orig / lo, inv / factor,
+                                          (1 - smooth) * inv / factor + smooth * inv))
         elif typ == "yarn":
             orig = float(scaling.get("original_max_position_embeddings", 4096))
             beta_fast = float(scaling.get("beta_fast", 32))

@@ -181,3 +181,44 @@ def test_glm45_moe_matches_transformers(tmp_path):
     with torch.no_grad():
         back = hf2(toks).logits[0].float()
     assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("name", ["qwen2", "llama3"])
+def test_dense_classics_match_transformers(tmp_path, name):
+    """Qwen2.5 (q/k/v biases, no QK-norm) and Llama 3.1 (frequency-band rotary scaling)."""
+    from transformers import LlamaConfig, LlamaForCausalLM, Qwen2Config, Qwen2ForCausalLM
+
+    from miles_b200.checkpoint.hf import load_hf, save_hf
+    from miles_b200.models.config import ModelConfig
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops.attention import VarlenMeta
+
+    torch.manual_seed(0)
+    if name == "qwen2":
+        cls = Qwen2ForCausalLM
+        hf = cls(Qwen2Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                             num_attention_heads=4, num_key_value_heads=2, tie_word_embeddings=True)).eval()
+        with torch.no_grad():
+            for n, p in hf.named_parameters():
+                if n.endswith("bias"):
+                    p.normal_(0, 0.1)
+    else:
+        cls = LlamaForCausalLM
+        hf = cls(LlamaConfig(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                             num_attention_heads=4, num_key_value_heads=2,
+                             rope_parameters={"rope_type": "llama3", "rope_theta": 500000.0, "factor": 8.0,
+                                              "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                                              "original_max_position_embeddings": 64})).eval()
+    hf.save_pretrained(str(tmp_path / "hf"))
+    cfg = ModelConfig.from_hf(str(tmp_path / "hf"))
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=1)
+    load_hf(m, str(tmp_path / "hf"))
+    toks = torch.randint(0, cfg.vocab_size, (1, 31))
+    with torch.no_grad():
+        ref = hf(toks).logits[0].float()
+        ours = m.forward_train(toks[0].int(), VarlenMeta([0, 31], "cpu")).float() @ m.lm_head_weight().float().t()
+    assert (ref - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
+    save_hf(m, str(tmp_path / "ours"))
+    with torch.no_grad():
+        back = cls.from_pretrained(str(tmp_path / "ours"), torch_dtype=torch.float32).eval()(toks).logits[0].float()
+    assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
