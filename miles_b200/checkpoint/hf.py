@@ -39,8 +39,21 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
         yield pre + L + "post_attention_layernorm.weight", P[L + "post_attention_layernorm.weight"].data
         if cfg.layer_is_linear(i):  # Gated DeltaNet parameters carry their HF names
             for n in P:
-                if n.startswith(L + "linear_attn."):
-                    yield pre + n, P[n].data
+                if not n.startswith(L + "linear_attn."):
+                    continue
+                if cfg.arch == "qwen3_5" and n.endswith(("in_proj_qkvz.weight", "in_proj_ba.weight")):
+                    # Qwen3.5 stores the projections separately: [q; k; v], z, b, a
+                    w = P[n].data
+                    if n.endswith("qkvz.weight"):
+                        vd = cfg.linear_num_value_heads * cfg.linear_value_head_dim
+                        yield pre + L + "linear_attn.in_proj_qkv.weight", w[: w.shape[0] - vd]
+                        yield pre + L + "linear_attn.in_proj_z.weight", w[w.shape[0] - vd:]
+                    else:
+                        nv = cfg.linear_num_value_heads
+                        yield pre + L + "linear_attn.in_proj_b.weight", w[:nv]
+                        yield pre + L + "linear_attn.in_proj_a.weight", w[nv:]
+                    continue
+                yield pre + n, P[n].data
         elif cfg.kv_lora_rank or cfg.uses_torch_attention:  # MLA / separate q,k,v: HF names already
             for n in P:
                 if n.startswith(L + "self_attn."):
@@ -173,8 +186,13 @@ def hf_config_dict(cfg: ModelConfig) -> dict:
                  attention_bias=cfg.attention_bias, use_qk_norm=cfg.qk_norm,
                  partial_rotary_factor=cfg.partial_rotary_factor)
         d["rope_parameters"]["partial_rotary_factor"] = cfg.partial_rotary_factor
-    elif cfg.arch == "qwen3_next":
-        d.update(model_type="qwen3_next", architectures=["Qwen3NextForCausalLM"],
+    elif cfg.arch in ("qwen3_next", "qwen3_5"):
+        if cfg.arch == "qwen3_5":
+            d.update(model_type="qwen3_5_moe_text" if cfg.is_moe else "qwen3_5_text",
+                     architectures=["Qwen3_5MoeForCausalLM" if cfg.is_moe else "Qwen3_5ForCausalLM"])
+        else:
+            d.update(model_type="qwen3_next", architectures=["Qwen3NextForCausalLM"])
+        d.update(
                  full_attention_interval=cfg.linear_attn_interval,
                  linear_num_key_heads=cfg.linear_num_key_heads,
                  linear_num_value_heads=cfg.linear_num_value_heads,
@@ -230,6 +248,8 @@ def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> No
         if not writer or name in skip:
             continue
         t = to_hf_layout(model.cfg, name, t)
+        if model.cfg.arch == "qwen3_5" and name.startswith("model."):
+            name = "model.language_model." + name[len("model."):]  # the layout HF Qwen3.5 reads
         t = t.to("cpu").contiguous().clone()
         nb = t.numel() * t.element_size()
         if size + nb > max_shard_bytes:
@@ -285,6 +305,11 @@ def load_hf(model: Transformer, path: str) -> None:
         src_name = name
         if src_name not in wmap and src_name.startswith("model.") is False and ("model." + src_name) in wmap:
             src_name = "model." + src_name
+        if src_name not in wmap and name.startswith("model."):
+            # multimodal checkpoints (Qwen3.5) keep the text model under model.language_model.
+            alt = "model.language_model." + name[len("model."):]
+            if alt in wmap:
+                src_name = alt
         if src_name not in wmap:
             if name == "lm_head.weight" and cfg.tie_embeddings:
                 continue

@@ -156,13 +156,16 @@ class ModelConfig:
             c.qk_norm = bool(d.get("use_qk_norm", False))
             c.partial_rotary_factor = d.get("partial_rotary_factor", rp.get("partial_rotary_factor", 1.0))
             return c
-        if mt == "qwen3_next":
-            c.arch = "qwen3_next"
+        if mt in ("qwen3_next", "qwen3_5_text", "qwen3_5_moe_text"):
+            # Qwen3.5 keeps the Qwen3-Next hybrid with separate in_proj_qkv / z / b / a tensors
+            c.arch = "qwen3_next" if mt == "qwen3_next" else "qwen3_5"
             c.num_experts = d.get("num_experts", d.get("num_local_experts", 0))
             c.topk = d.get("num_experts_per_tok", 0)
             c.moe_intermediate_size = d.get("moe_intermediate_size", 0)
             c.norm_topk_prob = d.get("norm_topk_prob", True)
             c.linear_attn_interval = d.get("full_attention_interval", 4)
+            if "layer_types" in d:
+                c.linear_attn_interval = d["layer_types"].index("full_attention") + 1
             c.linear_num_key_heads = d["linear_num_key_heads"]
             c.linear_num_value_heads = d["linear_num_value_heads"]
             c.linear_key_head_dim = d["linear_key_head_dim"]

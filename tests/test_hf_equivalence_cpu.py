@@ -222,3 +222,41 @@ def test_dense_classics_match_transformers(tmp_path, name):
     with torch.no_grad():
         back = cls.from_pretrained(str(tmp_path / "ours"), torch_dtype=torch.float32).eval()(toks).logits[0].float()
     assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
+
+
+def test_qwen35_moe_matches_transformers(tmp_path):
+    """Qwen3.5 MoE (text): the Qwen3-Next hybrid with separate in_proj_qkv / z / b / a."""
+    from transformers import Qwen3_5MoeForCausalLM, Qwen3_5MoeTextConfig
+
+    from miles_b200.checkpoint.hf import load_hf, save_hf
+    from miles_b200.models.config import ModelConfig
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops.attention import VarlenMeta
+
+    torch.manual_seed(0)
+    hc = Qwen3_5MoeTextConfig(vocab_size=512, hidden_size=256, num_hidden_layers=4, num_attention_heads=4,
+                              num_key_value_heads=2, head_dim=128, linear_num_key_heads=2,
+                              linear_num_value_heads=4, linear_key_head_dim=32, linear_value_head_dim=32,
+                              moe_intermediate_size=128, shared_expert_intermediate_size=192, num_experts=8,
+                              num_experts_per_tok=2, tie_word_embeddings=False,
+                              layer_types=["linear_attention"] * 3 + ["full_attention"])
+    hf = Qwen3_5MoeForCausalLM(hc).eval()
+    with torch.no_grad():
+        for n, p in hf.named_parameters():
+            if n.endswith(("layernorm.weight", "q_norm.weight", "k_norm.weight", "model.norm.weight")):
+                p.normal_(0, 0.1)
+    hf.save_pretrained(str(tmp_path / "hf"))
+    cfg = ModelConfig.from_hf(str(tmp_path / "hf"))
+    assert cfg.arch == "qwen3_5" and cfg.layer_is_linear(2) and not cfg.layer_is_linear(3)
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=1)
+    load_hf(m, str(tmp_path / "hf"))
+    toks = torch.randint(0, cfg.vocab_size, (1, 29))
+    with torch.no_grad():
+        ref = hf(toks).logits[0].float()
+        ours = m.forward_train(toks[0].int(), VarlenMeta([0, 29], "cpu")).float() @ m.lm_head_weight().float().t()
+    assert (ref - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item()), (ref - ours).abs().max()
+    save_hf(m, str(tmp_path / "ours"))
+    with torch.no_grad():
+        back = Qwen3_5MoeForCausalLM.from_pretrained(str(tmp_path / "ours"),
+                                                     torch_dtype=torch.float32).eval()(toks).logits[0].float()
+    assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
