@@ -290,7 +290,6 @@ def _open_all(path: str) -> dict[str, str]:
 @torch.no_grad()
 def load_hf(model: Transformer, path: str) -> None:
     """Load an HF checkpoint into the flat parameter buffer (joins fused projections)."""
-    cfg = model.cfg
     wmap = _open_all(path)
     handles: dict[str, object] = {}
 
@@ -299,6 +298,18 @@ def load_hf(model: Transformer, path: str) -> None:
         if fn not in handles:
             handles[fn] = safe_open(os.path.join(path, fn), "pt")
         return handles[fn].get_tensor(name)
+
+    _load(model, wmap, get, path)
+
+
+@torch.no_grad()
+def load_hf_tensors(model: Transformer, tensors: dict[str, torch.Tensor]) -> None:
+    """Load HF-named tensors held in memory (e.g. gathered from an FSDP-trained HF model)."""
+    _load(model, tensors, tensors.__getitem__, "the given tensors")
+
+
+def _load(model: Transformer, wmap, get, path: str) -> None:
+    cfg = model.cfg
 
     targets = dict(to_hf_tensors(model))  # views into model.flat
     for name, dst in targets.items():

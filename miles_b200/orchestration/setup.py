@@ -201,6 +201,21 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                       grad_dtype=torch.float32 if (ctx.device.type != "cuda" or args.accumulate_allreduce_grads_in_fp32) else torch.bfloat16,
                       optimizer_placement=placement,
                       logprob_chunk=args.log_probs_chunk_size if args.log_probs_chunk_size > 0 else 4096)
+    if getattr(args, "train_backend", "b200") == "fsdp":
+        # HF model under FSDP2 (trainer/fsdp_actor.py); `model` is then the engine's Transformer,
+        # refreshed from the gathered HF state after every step
+        from miles_b200.checkpoint.hf import load_hf_tensors
+        from miles_b200.trainer.fsdp_actor import FSDPActor
+
+        if args.use_kl_loss or args.kl_coef or args.use_routing_replay:
+            raise ValueError("--train-backend fsdp supports no reference-model KL and no routing replay")
+        if not args.hf_checkpoint:
+            raise ValueError("--train-backend fsdp loads the policy from --hf-checkpoint")
+        actor = FSDPActor(args.hf_checkpoint, cfg, dp_group=ctx.dp_group, device=ctx.device,
+                          dtype=model.dtype)
+        load_hf_tensors(model, actor.export_hf_state())
+        actor.engine_model = model
+        return actor
     actor = Actor(model, cfg, dp_group=ctx.dp_group)
     actor.expert_dp_group = ctx.expert_dp_group
     return actor

@@ -54,7 +54,7 @@ def setup(args):
     trainer = TrainActor(args, actor, ctx.dp_group, critic=build_critic(args, ctx),
                          data_parallel_size=ctx.dp_size)
     start = 0
-    if args.load and is_torch_dist(args.load):
+    if args.load and is_torch_dist(args.load) and args.train_backend != "fsdp":
         actor._ensure_grads()
         info = load_checkpoint(args.load, model, actor.opt, load_optim=not args.no_load_optim)
         start = info.get("extra", {}).get("rollout_id", info["iteration"]) + 1
@@ -83,6 +83,11 @@ def train(args):
             continue
         profiler.start("train_overall")
         m = trainer.train(rollout_id, data)
+        if args.train_backend == "fsdp":  # HF policy under FSDP2 -> the engine's Transformer
+            from miles_b200.checkpoint.hf import load_hf_tensors
+
+            load_hf_tensors(model, actor.export_hf_state())
+            model.weight_version += 1
         if engine.model is not model:  # pipeline stages -> the engine's full-depth copy
             from miles_b200.parallel.pp import gather_full_weights
 
@@ -90,7 +95,8 @@ def train(args):
         profiler.stop("train_overall")
         profiler.step()
         m.update(data["metrics"])
-        if should_run_periodic_action(rollout_id, args.save_interval, num_rollout) and args.save:
+        if (should_run_periodic_action(rollout_id, args.save_interval, num_rollout) and args.save
+                and args.train_backend != "fsdp"):
             save_checkpoint(args.save, rollout_id, model, actor.opt, extra={"rollout_id": rollout_id},
                             save_optim=not args.no_save_optim, async_save=args.async_save)
             data_source.save(rollout_id)
