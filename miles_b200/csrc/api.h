@@ -210,3 +210,14 @@ int mb_ep_gather_bwd(const long long* dxs_ptrs, int world, const int* idx, const
 #ifdef __cplusplus
 }
 #endif
+
+// Gated DeltaNet decode step (gdn.cu).
+#ifdef __cplusplus
+extern "C" {
+#endif
+int mb_gdn_decode(const float* q, const float* k, const float* v, const float* beta,
+                  const float* g, const long long* rows, float* S, float* out, int B, int nv,
+                  int dk, int dv, float scale, cudaStream_t st);
+#ifdef __cplusplus
+}
+#endif

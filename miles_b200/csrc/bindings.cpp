@@ -485,7 +485,23 @@ int64_t ep_gather_bwd(std::vector<int64_t> dxs_ptrs, torch::Tensor idx, torch::T
                           idx.size(1), H, E_local, P(dx), cur_stream());
 }
 
+// ------------------------------------------------------------------ Gated DeltaNet decode
+int64_t gdn_decode(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor beta,
+                   torch::Tensor g, torch::Tensor rows, torch::Tensor S, torch::Tensor out,
+                   double scale) {
+  for (auto* t : {&q, &k, &v, &beta, &g, &S, &out}) {
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kFloat,
+                "gdn_decode: fp32 contiguous CUDA tensors expected");
+  }
+  TORCH_CHECK(rows.scalar_type() == at::kLong && rows.is_contiguous());
+  TORCH_CHECK(q.dim() == 3 && S.dim() == 4 && S.size(1) == q.size(1) && S.size(2) == q.size(2));
+  return mb_gdn_decode(PT<float>(q), PT<float>(k), PT<float>(v), PT<float>(beta), PT<float>(g),
+                       (const long long*)rows.data_ptr(), PT<float>(S), PT<float>(out), q.size(0),
+                       q.size(1), q.size(2), S.size(3), (float)scale, cur_stream());
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("gdn_decode", &gdn_decode, "Gated DeltaNet decode step (state updated in place)");
   m.def("ep_publish", &ep_publish);
   m.def("ep_offsets", &ep_offsets);
   m.def("ep_dispatch", &ep_dispatch);

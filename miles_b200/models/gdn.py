@@ -14,8 +14,9 @@ Training and prefill run the recurrence over each packed sequence from a zero st
 64 steps in matrix form (a unit-triangular solve per chunk, `_recur_chunked`); the rollout
 engine keeps, per live sequence, the last K-1 conv inputs and the state S (`KVCache.lin_conv`,
 `KVCache.lin_state`, one row per engine batch slot) and advances them one token per decode step,
-so decode reproduces the training forward. This is a PyTorch implementation (fp32 recurrence);
-there is no sm_100a kernel for it yet.
+so decode reproduces the training forward. The decode step's state update runs in a CUDA
+kernel (csrc/gdn.cu) on GPUs; projections use the native GEMMs; the rest is PyTorch (fp32
+recurrence).
 
 Parameter names follow HF Qwen3-Next (`linear_attn.*`), except that in_proj_qkvz holds
 [q; k; v; z] as contiguous blocks (HF interleaves them per key-head group) and conv1d.weight is
@@ -56,6 +57,15 @@ def gdn_state_shapes(cfg):
 def _l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """x / sqrt(sum(x^2) + eps) over the last dim (the eps inside the root, as the HF layer)."""
     return x * torch.rsqrt(x.pow(2).sum(-1, keepdim=True) + eps)
+
+
+def gdn_step_ref(q, k, v, beta, g, S, dk):
+    """One decode step of the gated delta rule for B rows (PyTorch reference of csrc/gdn.cu):
+    q, k [B, nv, dk], v [B, nv, dv], beta, g [B, nv], S [B, nv, dk, dv] -> (o, new S)."""
+    S = S * torch.exp(g)[:, :, None, None]
+    err = v - torch.einsum("bhk,bhkv->bhv", k, S)
+    S = S + k[:, :, :, None] * (beta[:, :, None] * err)[:, :, None, :]
+    return torch.einsum("bhk,bhkv->bhv", q, S) / math.sqrt(dk), S
 
 
 class GDN:
@@ -195,11 +205,16 @@ class GDN:
         q = _l2norm(q.view(B, nk, dk)).repeat_interleave(r, 1)
         k = _l2norm(k.view(B, nk, dk)).repeat_interleave(r, 1)
         v = v.view(B, nv, dv)
-        S = S * torch.exp(g)[:, :, None, None]
-        err = v - torch.einsum("bhk,bhkv->bhv", k, S)
-        S = S + k[:, :, :, None] * (beta[:, :, None] * err)[:, :, None, :]
-        o = torch.einsum("bhk,bhkv->bhv", q, S) / math.sqrt(dk)
         cache.lin_conv[i].index_copy_(0, rows, window[:, :, 1:].contiguous())
+        from miles_b200.ops._lib import lib, use_native
+
+        if use_native(x):
+            # csrc/gdn.cu: the state rows are advanced in place
+            o = torch.empty(B, nv, dv, dtype=torch.float32, device=x.device)
+            lib().gdn_decode(q.contiguous(), k.contiguous(), v.contiguous(), beta.contiguous(),
+                             g.contiguous(), rows.contiguous(), cache.lin_state[i], o, 1.0 / math.sqrt(dk))
+            return self._out(i, o, z, x.dtype)
+        o, S = gdn_step_ref(q, k, v, beta, g, S, dk)
         cache.lin_state[i].index_copy_(0, rows, S)
         return self._out(i, o, z, x.dtype)
 
