@@ -221,3 +221,15 @@ int mb_gdn_decode(const float* q, const float* k, const float* v, const float* b
 #ifdef __cplusplus
 }
 #endif
+
+// Absorbed MLA decode over the paged latent cache (mla_decode.cu).
+#ifdef __cplusplus
+extern "C" {
+#endif
+int mb_mla_decode(const float* q_lat, const float* q_pe, const void* cache, long long row_stride,
+                  const int* page_table, int max_pages, const int* ctx_lens, const float* bias,
+                  long long bias_stride, int B, int nh, int r, int dr, float scale, float* out,
+                  cudaStream_t st);
+#ifdef __cplusplus
+}
+#endif

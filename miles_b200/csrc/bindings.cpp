@@ -500,7 +500,25 @@ int64_t gdn_decode(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
                        q.size(1), q.size(2), S.size(3), (float)scale, cur_stream());
 }
 
+// ------------------------------------------------------------------ MLA decode
+int64_t mla_decode(torch::Tensor q_lat, torch::Tensor q_pe, torch::Tensor cache,
+                   torch::Tensor page_table, torch::Tensor ctx_lens, OT bias, double scale,
+                   torch::Tensor out) {
+  TORCH_CHECK(q_lat.is_contiguous() && q_pe.is_contiguous() && out.is_contiguous());
+  TORCH_CHECK(q_lat.scalar_type() == at::kFloat && q_pe.scalar_type() == at::kFloat &&
+              out.scalar_type() == at::kFloat && cache.scalar_type() == at::kBFloat16);
+  TORCH_CHECK(page_table.scalar_type() == at::kInt && ctx_lens.scalar_type() == at::kInt &&
+              page_table.is_contiguous());
+  if (bias.has_value()) TORCH_CHECK(bias.value().scalar_type() == at::kFloat && bias.value().stride(-1) == 1);
+  const long long row_stride = cache.stride(0);
+  return mb_mla_decode(PT<float>(q_lat), PT<float>(q_pe), cache.data_ptr(), row_stride,
+                       PT<int>(page_table), page_table.size(1), PT<int>(ctx_lens), PT<float>(bias),
+                       bias.has_value() ? bias.value().stride(0) : 0, q_lat.size(0), q_lat.size(1),
+                       q_lat.size(2), q_pe.size(2), (float)scale, PT<float>(out), cur_stream());
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("mla_decode", &mla_decode, "absorbed MLA decode over the paged latent cache");
   m.def("gdn_decode", &gdn_decode, "Gated DeltaNet decode step (state updated in place)");
   m.def("ep_publish", &ep_publish);
   m.def("ep_offsets", &ep_offsets);

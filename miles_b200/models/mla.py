@@ -9,7 +9,8 @@ heads: [k_nope | v] = c Wkv_b per head, k = [k_nope | k_pe].
     (head dims qk = nope + rope, v = v_head_dim, which the head-dim-128 tcgen05 kernels do not
     cover: this path uses PyTorch's scaled_dot_product_attention);
   * the KV cache stores only [c | k_pe] (kv_lora_rank + qk_rope_head_dim values per token, one
-    "head"), and decode runs the absorbed form: q_nope is mapped into latent space by the key
+    "head"), and decode runs the absorbed form (on GPUs in csrc/mla_decode.cu, straight from the
+    paged cache): q_nope is mapped into latent space by the key
     half of Wkv_b, scores are q_lat . c + q_pe . k_pe, the value is read in latent space and
     mapped out by the value half of Wkv_b. Decode therefore never expands the cache.
 
@@ -156,6 +157,20 @@ class MLA:
         keep = torch.zeros_like(valid).scatter_(-1, top, True)
         return keep & valid
 
+    def _dsa_bias(self, i, x, qa, positions, cache, page_table, ctx_lens):
+        """[B, maxk] additive bias of the DSA key selection over the cached indexer keys."""
+        cfg = self.cfg
+        B, page = x.shape[0], 64
+        maxk = page_table.shape[1] * page
+        t = torch.arange(maxk, device=x.device)
+        rows = page_table.long()[:, t // page] * page + (t % page)[None, :]
+        off = cfg.kv_lora_rank + cfg.qk_rope_head_dim
+        kI = cache.k[i][:, 0, off:].index_select(0, rows.reshape(-1)).view(B, maxk, -1).double()
+        qI, wI = self._index_q(i, qa, positions).double(), self._index_weights(i, x).double()
+        scI = torch.einsum("bh,bhs->bs", wI, torch.relu(torch.einsum("bhd,bsd->bhs", qI, kI)))
+        keep = self._topk_keep(scI, t[None, :] < ctx_lens[:, None].long())
+        return torch.zeros(B, maxk, dtype=torch.float32, device=x.device).masked_fill(~keep, float("-inf"))
+
     def _q(self, i: int, x: torch.Tensor, pos: torch.Tensor, want_qa: bool = False):
         cfg, m = self.cfg, self.m
         p = f"layers.{i}.self_attn."
@@ -245,6 +260,20 @@ class MLA:
         w = self.m.params[f"layers.{i}.self_attn.kv_b_proj.weight"].view(nh, dn + dv, r)
         w_uk, w_uv = w[:, :dn, :], w[:, dn:, :]
         q_lat = torch.einsum("bhn,hnc->bhc", q_nope.float(), w_uk.float())
+        from miles_b200.ops._lib import lib, use_native
+
+        if use_native(x):
+            # csrc/mla_decode.cu reads the paged latent cache directly; DSA passes its key
+            # selection as an additive bias (0 kept, -inf dropped)
+            bias = None
+            if dsa:
+                bias = self._dsa_bias(i, x, qa, positions, cache, page_table, ctx_lens)
+            o_lat = torch.empty(B, nh, r, dtype=torch.float32, device=x.device)
+            lib().mla_decode(q_lat.contiguous(), q_pe.float().contiguous(), cache.k[i][:, 0, :],
+                             page_table.int().contiguous(), ctx_lens.int().contiguous(), bias,
+                             self.scale, o_lat)
+            o = torch.einsum("bhc,hvc->bhv", o_lat, w_uv.float()).to(x.dtype)
+            return self._out(i, o.reshape(B, -1), pending)
         page = 64
         maxk = page_table.shape[1] * page
         t = torch.arange(maxk, device=x.device)

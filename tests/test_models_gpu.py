@@ -68,3 +68,38 @@ def test_gdn_decode_kernel_matches_reference():
         torch.cuda.synchronize()
         assert torch.allclose(o, o_ref, atol=1e-4, rtol=1e-4)
         assert torch.allclose(S, S_ref, atol=1e-5, rtol=1e-4)
+
+
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_mla_decode_kernel_matches_reference(with_bias):
+    """csrc/mla_decode.cu against the PyTorch absorbed decode over gathered cache rows."""
+    from miles_b200.ops._lib import lib
+
+    torch.manual_seed(0)
+    B, nh, r, dr, extra, P = 3, 4, 512, 64, 32, 5
+    width = r + dr + extra
+    slots = 16 * 64
+    cache = (torch.randn(slots, 1, width, device="cuda") * 0.5).to(torch.bfloat16)
+    pt = torch.stack([torch.randperm(16, device="cuda")[:P] for _ in range(B)]).int()
+    ctx = torch.tensor([1, 200, P * 64], dtype=torch.int32, device="cuda")
+    q_lat = torch.randn(B, nh, r, device="cuda")
+    q_pe = torch.randn(B, nh, dr, device="cuda")
+    maxk = P * 64
+    bias = None
+    if with_bias:
+        bias = torch.zeros(B, maxk, device="cuda")
+        bias[:, 1::3] = float("-inf")
+    out = torch.empty(B, nh, r, device="cuda")
+    scale = 0.07
+    lib().mla_decode(q_lat, q_pe, cache[:, 0, :], pt, ctx, bias, scale, out)
+    t = torch.arange(maxk, device="cuda")
+    rows = pt.long()[:, t // 64] * 64 + (t % 64)[None, :]
+    lat = cache[:, 0, :].index_select(0, rows.reshape(-1)).view(B, maxk, width).float()
+    sc = (torch.einsum("bhc,btc->bht", q_lat, lat[..., :r]) +
+          torch.einsum("bhd,btd->bht", q_pe, lat[..., r:r + dr])) * scale
+    if bias is not None:
+        sc = sc + bias[:, None, :]
+    sc = sc.masked_fill((t[None, :] >= ctx[:, None].long())[:, None, :], float("-inf"))
+    ref = torch.einsum("bht,btc->bhc", torch.softmax(sc, -1), lat[..., :r])
+    torch.cuda.synchronize()
+    assert torch.allclose(out, ref, atol=2e-4, rtol=1e-3), (out - ref).abs().max()
