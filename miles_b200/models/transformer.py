@@ -190,6 +190,9 @@ class Transformer(torch.nn.Module):
         self.tp_size = self.tp.size if self.tp else 1
         # sequence parallelism (training forward): residual stream sharded over TP ranks by rows
         self.sequence_parallel = False
+        # TP trainer log-probs with the vocabulary split over the TP ranks (opt-in: the rollout
+        # engine samples from full logits, so train / rollout log-probs then differ by rounding)
+        self.vocab_parallel_logprob = False
         self.cp = None  # context parallelism (training forward), miles_b200/parallel/cp.py
         if cp_group is not None:
             from miles_b200.parallel.cp import CPContext
@@ -521,6 +524,13 @@ class Transformer(torch.nn.Module):
 
         W = self.lm_head_weight()
         h = self.forward_train(tokens, meta, replay_experts=replay_experts)
+        if self.tp is not None and self.vocab_parallel_logprob:
+            from miles_b200.parallel.tp import vocab_parallel_logprob
+
+            if self.cfg.tie_embeddings:
+                raise ValueError("vocab-parallel log-probs need an untied LM head")
+
+            return vocab_parallel_logprob(h.index_select(0, sel), W, targets, temperature, self.tp, chunk)
         if self.cp is None:
             return lm_head_logprob(h.index_select(0, sel), W, targets, temperature, chunk)
         from miles_b200.parallel.cp import gather_parts

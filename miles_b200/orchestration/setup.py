@@ -154,6 +154,8 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
                         tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
     if getattr(args, "sequence_parallel", False) and model.tp is not None and model.mla is None:
         model.sequence_parallel = True
+    if getattr(args, "vocab_parallel_logprob", False) and model.tp is not None:
+        model.vocab_parallel_logprob = True
     loaded = False
     if args.load:
         from miles_b200.checkpoint.torch_dist import is_torch_dist

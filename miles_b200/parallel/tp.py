@@ -188,6 +188,8 @@ def tp_partial_param_names(model) -> list[str]:
             out.append(name)
         elif model.sequence_parallel and (name.endswith(sp_norms) or name == "norm.weight"):
             out.append(name)
+        elif model.vocab_parallel_logprob and name == "lm_head.weight":
+            out.append(name)  # each rank's gradient covers its vocabulary rows
         elif name.endswith("mlp.gate.weight"):
             out.append(name)  # router logits feed a combine of partial expert outputs
     return out
@@ -342,3 +344,83 @@ def row_parallel_rs(x, w, tp, lin):
             and x.shape[0] // tp.size <= tp.cap_rows and w.shape[0] == tp.hidden:
         return _RowParallelRS.apply(x, w, tp)
     return sp_reduce_scatter(lin(x, w), tp)
+
+
+# ------------------------------------------------------------------ vocab-parallel log-prob
+class _VocabParallelLogProb(torch.autograd.Function):
+    """log softmax(h W^T / T)[target] and the entropy with every TP rank computing the logits of
+    its vocabulary slice only: the row max, the sum of exponentials, the target logit and
+    sum(p z) are combined over the TP group (max / sum all-reduces), so no rank holds [n, V]
+    logits. Backward: each rank forms the logit gradient of its slice; the hidden-state gradient
+    is a partial sum (the caller's copy_to_tp all-reduces it) and the LM-head gradient lands in
+    this rank's rows (tp_partial_param_names all-reduces it)."""
+
+    @staticmethod
+    def forward(ctx, h, W, targets, inv_temp, tp, lo, hi, chunk):
+        from miles_b200.ops import gemm as G
+
+        n = h.shape[0]
+        lp = torch.empty(n, dtype=torch.float32, device=h.device)
+        ent = torch.empty_like(lp)
+        lse = torch.empty_like(lp)
+        Wl = W[lo:hi]
+        for s in range(0, n, chunk):
+            e = min(n, s + chunk)
+            z = G.matmul_nt(h[s:e].contiguous(), Wl, out_dtype=torch.float32) * inv_temp
+            m = z.max(-1).values
+            dist.all_reduce(m, op=dist.ReduceOp.MAX, group=tp.group)
+            ex = torch.exp(z - m[:, None])
+            se = ex.sum(-1)
+            tgt = targets[s:e].long()
+            inr = (tgt >= lo) & (tgt < hi)
+            tz = torch.where(inr, z.gather(1, (tgt - lo).clamp(0, hi - lo - 1)[:, None])[:, 0],
+                             torch.zeros_like(m))
+            pz = (ex * z).sum(-1)
+            red = torch.stack([se, tz, pz], 0)
+            dist.all_reduce(red, group=tp.group)
+            l = m + torch.log(red[0])
+            lse[s:e] = l
+            lp[s:e] = red[1] - l
+            ent[s:e] = l - red[2] / red[0]
+        ctx.save_for_backward(h, W, targets, lse, ent)
+        ctx.cfg = (inv_temp, lo, hi, chunk)
+        return lp, ent
+
+    @staticmethod
+    def backward(ctx, g_lp, g_ent):
+        from miles_b200.ops import gemm as G
+
+        h, W, targets, lse, ent = ctx.saved_tensors
+        inv_temp, lo, hi, chunk = ctx.cfg
+        n = h.shape[0]
+        Wl = W[lo:hi]
+        dh = torch.empty(h.shape, dtype=torch.float32, device=h.device)
+        dW = torch.zeros(W.shape, dtype=torch.float32, device=h.device) if ctx.needs_input_grad[1] else None
+        for s in range(0, n, chunk):
+            e = min(n, s + chunk)
+            hs = h[s:e].contiguous()
+            z = G.matmul_nt(hs, Wl, out_dtype=torch.float32) * inv_temp
+            p = torch.exp(z - lse[s:e, None])
+            dz = torch.zeros_like(z)
+            if g_lp is not None:
+                tgt = targets[s:e].long()
+                inr = (tgt >= lo) & (tgt < hi)
+                onehot = torch.zeros_like(z)
+                idx = (tgt - lo).clamp(0, hi - lo - 1)
+                onehot.scatter_(1, idx[:, None], inr[:, None].float())
+                dz += g_lp[s:e, None] * (onehot - p)
+            if g_ent is not None:
+                dz += g_ent[s:e, None] * (-p * (z - lse[s:e, None] + ent[s:e, None]))
+            dz = dz * inv_temp
+            dh[s:e] = dz @ Wl.float()
+            if dW is not None:
+                dW[lo:hi] += dz.t() @ hs.float()
+        return dh.to(h.dtype), (dW.to(W.dtype) if dW is not None else None), None, None, None, None, None, None
+
+
+def vocab_parallel_logprob(h, W, targets, temperature: float, tp: TPContext, chunk: int = 4096):
+    """(log-prob, entropy) of `targets` with the vocabulary split over the TP group; `h` must be
+    identical on every TP rank (it is passed through copy_to_tp here)."""
+    lo, hi = tp.shard(W.shape[0])
+    return _VocabParallelLogProb.apply(copy_to_tp(h, tp), W, targets.int().contiguous(),
+                                       1.0 / temperature, tp, lo, hi, chunk)

@@ -65,6 +65,8 @@ def add_train_args(p):
     g.add_argument("--expert-model-parallel-size", type=int, default=1)
     g.add_argument("--expert-tensor-parallel-size", type=int, default=1)
     g.add_argument("--sequence-parallel", action="store_true", default=False)
+    g.add_argument("--vocab-parallel-logprob", action="store_true", default=False,
+                   help="under TP, split the LM-head logits of the trainer's log-probs over the TP ranks")
     g.add_argument("--lr", type=float, default=1e-6)
     g.add_argument("--min-lr", type=float, default=0.0)
     g.add_argument("--lr-decay-style", default="constant", choices=["constant", "linear", "cosine"])

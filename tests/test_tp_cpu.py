@@ -164,3 +164,53 @@ def test_tp2_matches_tp1(tmp_path, preset_name, port):
     for k in src:
         assert torch.equal(src[k], back[k]), k
     assert any(hf_shard_dim(k) is not None for k in src)
+
+
+def _run_vp(rank, world, port, out):
+    os.environ["MILES_B200_FORCE_CPU"] = "1"
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops.attention import VarlenMeta
+    from miles_b200.parallel.tp import tp_partial_param_names
+
+    cfg = preset("tiny-moe")  # untied LM head
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=5, tp_group=dist.group.WORLD)
+    m.recompute = False
+    g = torch.Generator().manual_seed(0)
+    toks = torch.randint(0, cfg.vocab_size, (30,), generator=g, dtype=torch.int32)
+    meta = VarlenMeta([0, 12, 30], "cpu")
+    sel = torch.arange(3, 28)
+    tgt = toks[sel + 1]
+    res = {}
+    for vp in (False, True):
+        m.vocab_parallel_logprob = vp
+        for p in m.params.values():
+            p.grad = None
+        lp, ent = m.selected_logprob(toks, meta, sel, tgt, 1.3, 8)
+        (lp.sum() + 0.3 * ent.sum()).backward()
+        grads = {}
+        partial = set(tp_partial_param_names(m))
+        for n, p in m.params.items():
+            if p.grad is not None:
+                gr = p.grad.clone()
+                if n in partial:
+                    dist.all_reduce(gr)
+                grads[n] = gr
+        res[vp] = (lp.detach(), ent.detach(), grads)
+    if rank == 0:
+        torch.save(res, out)
+    dist.destroy_process_group()
+
+
+def test_vocab_parallel_logprob(tmp_path):
+    """TP2 log-probs / entropies with the vocabulary split over the ranks equal the replicated
+    LM head's, and so do all gradients (LM head rows all-reduced)."""
+    out = str(tmp_path / "vp.pt")
+    mp.spawn(_run_vp, args=(2, 29675, out), nprocs=2, join=True)
+    r = torch.load(out)
+    (lp0, e0, g0), (lp1, e1, g1) = r[False], r[True]
+    assert torch.allclose(lp0, lp1, atol=1e-5) and torch.allclose(e0, e1, atol=1e-5)
+    assert set(g0) == set(g1)
+    for n in g0:
+        assert torch.allclose(g0[n], g1[n], atol=1e-5, rtol=1e-4), (n, (g0[n] - g1[n]).abs().max())
