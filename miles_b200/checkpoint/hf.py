@@ -37,6 +37,9 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
         L = f"layers.{i}."
         yield pre + L + "input_layernorm.weight", P[L + "input_layernorm.weight"].data
         yield pre + L + "post_attention_layernorm.weight", P[L + "post_attention_layernorm.weight"].data
+        if cfg.sandwich_norm:
+            yield pre + L + "post_self_attn_layernorm.weight", P[L + "post_self_attn_layernorm.weight"].data
+            yield pre + L + "post_mlp_layernorm.weight", P[L + "post_mlp_layernorm.weight"].data
         if cfg.layer_is_linear(i):  # Gated DeltaNet parameters carry their HF names
             for n in P:
                 if not n.startswith(L + "linear_attn."):
@@ -92,6 +95,9 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
                 yield pre + L + "mlp.shared_experts.gate_proj.weight", gu[:Is]
                 yield pre + L + "mlp.shared_experts.up_proj.weight", gu[Is:]
                 yield pre + L + "mlp.shared_experts.down_proj.weight", P[L + "mlp.shared_experts.down_proj.weight"].data
+        elif cfg.arch == "glm4":  # fused [gate; up] under its HF name
+            yield pre + L + "mlp.gate_up_proj.weight", P[L + "mlp.gate_up_proj.weight"].data
+            yield pre + L + "mlp.down_proj.weight", P[L + "mlp.down_proj.weight"].data
         else:
             gu = P[L + "mlp.gate_up_proj.weight"].data
             I = gu.shape[0] // 2
@@ -157,6 +163,8 @@ def hf_config_dict(cfg: ModelConfig) -> dict:
                                  **(cfg.rope_scaling or {})),
          "max_position_embeddings": cfg.max_position, "tie_word_embeddings": cfg.tie_embeddings,
          "torch_dtype": "bfloat16"}
+    d.update({k: None for k in ("pad_token_id", "bos_token_id", "eos_token_id")})
+    d.update(cfg.extra.get("token_ids", {}))
     if cfg.arch == "qwen3_moe":
         d.update(model_type="qwen3_moe", architectures=["Qwen3MoeForCausalLM"],
                  num_experts=cfg.num_experts, num_local_experts=cfg.num_experts,
@@ -177,6 +185,10 @@ def hf_config_dict(cfg: ModelConfig) -> dict:
             d.update(model_type="deepseek_v32", architectures=["DeepseekV32ForCausalLM"],
                      index_n_heads=cfg.index_n_heads, index_head_dim=cfg.index_head_dim,
                      index_topk=cfg.index_topk)
+    elif cfg.arch == "glm4":
+        d.update(model_type="glm4", architectures=["Glm4ForCausalLM"], attention_bias=cfg.attention_bias,
+                 partial_rotary_factor=cfg.partial_rotary_factor)
+        d["rope_parameters"]["partial_rotary_factor"] = cfg.partial_rotary_factor
     elif cfg.arch == "glm4_moe":
         d.update(model_type="glm4_moe", architectures=["Glm4MoeForCausalLM"],
                  n_routed_experts=cfg.num_experts, num_experts_per_tok=cfg.topk,

@@ -63,6 +63,7 @@ class ModelConfig:
     norm_offset: bool = False          # checkpoint RMSNorm weights are w in y = x_hat * (1 + w)
     shared_expert_intermediate_size: int = 0
     attention_bias: bool = False       # q / k / v projection biases (GLM-4.5)
+    sandwich_norm: bool = False        # GLM-4: RMSNorm on the attention and MLP outputs as well
     extra: dict = field(default_factory=dict)
 
     @property
@@ -74,7 +75,8 @@ class ModelConfig:
         """Softmax attention with an output gate, projection biases or partial rotary: the
         separate q / k / v projection path of models/qwen3_next.py instead of the fused
         qkv + QK-norm/RoPE kernel."""
-        return self.attn_output_gate or self.attention_bias or self.partial_rotary_factor != 1.0
+        return (self.attn_output_gate or self.attention_bias or self.partial_rotary_factor != 1.0
+                or (self.rope_interleave and not self.kv_lora_rank))
 
     def layer_is_linear(self, i: int) -> bool:
         return self.linear_attn_interval > 0 and (i + 1) % self.linear_attn_interval != 0
@@ -140,6 +142,15 @@ class ModelConfig:
             c.rope_scaling = {k: v for k, v in rp.items() if k != "rope_theta"}
         c.max_position = d.get("max_position_embeddings", 32768)
         c.tie_embeddings = d.get("tie_word_embeddings", False)
+        c.extra["token_ids"] = {k: d.get(k) for k in ("pad_token_id", "bos_token_id", "eos_token_id")}
+        if mt == "glm4":  # GLM-4 dense: sandwich norms, interleaved half-width rotary, biases
+            c.arch = "glm4"
+            c.sandwich_norm = True
+            c.rope_interleave = True
+            c.qk_norm = False
+            c.attention_bias = bool(d.get("attention_bias", True))
+            c.partial_rotary_factor = d.get("partial_rotary_factor", rp.get("partial_rotary_factor", 0.5))
+            return c
         if mt == "glm4_moe":  # GLM-4.5: GQA with biases / partial rotary, DeepSeek-style MoE
             c.arch = "glm4_moe"
             c.num_experts = d["n_routed_experts"]

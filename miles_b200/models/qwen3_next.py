@@ -81,8 +81,9 @@ class GatedAttention:
             q = _head_norm(q, m.params[p + "q_norm.weight"], cfg.rms_eps)
             k = _head_norm(k, m.params[p + "k_norm.weight"], cfg.rms_eps)
         r = self.rot
-        q = torch.cat([_rope(q[..., :r], pos, self.cos, self.sin), q[..., r:]], -1).contiguous()
-        k = torch.cat([_rope(k[..., :r], pos, self.cos, self.sin), k[..., r:]], -1).contiguous()
+        il = cfg.rope_interleave  # GLM-4: adjacent-pair rotary (same scores, permuted layout)
+        q = torch.cat([_rope(q[..., :r], pos, self.cos, self.sin, il), q[..., r:]], -1).contiguous()
+        k = torch.cat([_rope(k[..., :r], pos, self.cos, self.sin, il), k[..., r:]], -1).contiguous()
         return q, k, v.contiguous(), gate
 
     def _out(self, i: int, o: torch.Tensor, gate) -> torch.Tensor:

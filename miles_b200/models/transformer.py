@@ -83,6 +83,9 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=Non
             specs += [ParamSpec(p + "self_attn.qkv_proj.weight", ((nq + 2 * nkv) * D, H), "normal"),
                       ParamSpec(p + "self_attn.o_proj.weight", (H, nq * D), "normal")]
         specs.append(ParamSpec(p + "post_attention_layernorm.weight", (H,), "ones"))
+        if cfg.sandwich_norm:  # GLM-4: norms on the attention and MLP outputs too
+            specs += [ParamSpec(p + "post_self_attn_layernorm.weight", (H,), "ones"),
+                      ParamSpec(p + "post_mlp_layernorm.weight", (H,), "ones")]
         if cfg.qk_norm and not cfg.kv_lora_rank and not cfg.layer_is_linear(i):
             specs += [ParamSpec(p + "self_attn.q_norm.weight", (D,), "ones"),
                       ParamSpec(p + "self_attn.k_norm.weight", (D,), "ones")]
@@ -171,6 +174,12 @@ class KVCache:
         return sum(t.numel() * t.element_size() for t in ts)
 
 
+def dist_world(group) -> int:
+    import torch.distributed as dist
+
+    return dist.get_world_size(group)
+
+
 class Transformer(torch.nn.Module):
     def __init__(self, cfg: ModelConfig, device="cuda", dtype=torch.bfloat16, seed: int = 0,
                  init_std: float = 0.02, materialize: bool = True, ep_group=None, tp_group=None,
@@ -214,6 +223,8 @@ class Transformer(torch.nn.Module):
                                 cap_tokens=ep_cap_tokens)
             if self.ep.size == 1:
                 self.ep = None
+        if cfg.sandwich_norm and tp_group is not None and dist_world(tp_group) > 1:
+            raise ValueError("sandwich-norm (GLM-4) models run without TP")
         if self.ep is not None and self.tp is not None:
             raise ValueError("expert parallelism combined with tensor parallelism is not supported")
         self.pp = None  # pipeline parallelism (training), miles_b200/parallel/pp.py
@@ -323,6 +334,9 @@ class Transformer(torch.nn.Module):
 
     # -------------------------------------------------------------------------------- blocks
     def _attn_train(self, i: int, x: torch.Tensor, meta: VarlenMeta) -> torch.Tensor:
+        return self._sw(i, "post_self_attn_layernorm", self._attn_train_raw(i, x, meta))
+
+    def _attn_train_raw(self, i: int, x: torch.Tensor, meta: VarlenMeta) -> torch.Tensor:
         cfg = self.cfg
         if self.gdn is not None and cfg.layer_is_linear(i):
             return self.gdn.attn(i, x, meta)
@@ -339,8 +353,15 @@ class Transformer(torch.nn.Module):
         o = varlen_attention(q, k, v, meta)
         return reduce_from_tp(self._lin(o.reshape(x.shape[0], -1), pre + "o_proj.weight"), self.tp)
 
+    def _sw(self, i: int, name: str, t):
+        """GLM-4 sandwich norm of a branch output (identity for other families)."""
+        if not self.cfg.sandwich_norm:
+            return t
+        return rms_norm(t, self.params[f"layers.{i}.{name}.weight"], self.cfg.rms_eps)
+
     def _mlp(self, i: int, x: torch.Tensor, replay=None, record=None) -> torch.Tensor:
-        return reduce_from_tp(self._mlp_partial(i, copy_to_tp(x, self.tp), replay, record), self.tp)
+        m = reduce_from_tp(self._mlp_partial(i, copy_to_tp(x, self.tp), replay, record), self.tp)
+        return self._sw(i, "post_mlp_layernorm", m)
 
     def _mlp_partial(self, i: int, x: torch.Tensor, replay=None, record=None) -> torch.Tensor:
         """MLP / MoE output before the tensor-parallel all-reduce (the full output at TP 1)."""
@@ -472,7 +493,8 @@ class Transformer(torch.nn.Module):
 
             _, lo, hi = cp.rows(meta.total)
             a = gdn_attn_cp(self.gdn, i, x, meta, lo, hi, cp)
-            x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
+            x2, r = add_rms_norm(self._sw(i, "post_self_attn_layernorm", a), r,
+                                 self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
             return self._mlp(i, x2, replay=replay), r
         pre = f"layers.{i}.self_attn."
         if self.gattn is not None:  # gated attention (Qwen3-Next): same head exchange
@@ -483,7 +505,8 @@ class Transformer(torch.nn.Module):
             else:
                 oh = self.gattn._sdpa(qh, kh, vh, meta.cu_list)
             a = self.gattn._out(i, heads_to_tokens(oh, cp), gate)
-            x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
+            x2, r = add_rms_norm(self._sw(i, "post_self_attn_layernorm", a), r,
+                                 self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
             return self._mlp(i, x2, replay=replay), r
         qkv = self._lin(x, pre + "qkv_proj.weight")
         q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
@@ -491,7 +514,8 @@ class Transformer(torch.nn.Module):
                                self.rope_cos, self.rope_sin, self.nq, self.nkv, cfg.rms_eps, cfg.qk_norm)
         o = varlen_attention(tokens_to_heads(q, cp), tokens_to_heads(k, cp), tokens_to_heads(v, cp), meta)
         a = self._lin(heads_to_tokens(o, cp).reshape(x.shape[0], -1), pre + "o_proj.weight")
-        x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
+        x2, r = add_rms_norm(self._sw(i, "post_self_attn_layernorm", a), r,
+                                 self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
         return self._mlp(i, x2, replay=replay), r
 
     def _forward_train_cp(self, tokens, meta, replay_experts):
@@ -643,9 +667,9 @@ class Transformer(torch.nn.Module):
             pre = f"layers.{i}.self_attn."
             post = self.params[f"layers.{i}.post_attention_layernorm.weight"]
             if self.gdn is not None and cfg.layer_is_linear(i):
-                x2, r = self._add_norm(self.gdn.attn(i, x, meta, cache, state_rows), r, post)
+                x2, r = self._add_norm(self._sw(i, "post_self_attn_layernorm", self.gdn.attn(i, x, meta, cache, state_rows)), r, post)
             elif self.gattn is not None:
-                x2, r = self._add_norm(self.gattn.attn(i, x, meta, cache, slots), r, post)
+                x2, r = self._add_norm(self._sw(i, "post_self_attn_layernorm", self.gattn.attn(i, x, meta, cache, slots)), r, post)
             elif self.mla is not None:
                 x2, r = self._add_norm(self.mla.attn(i, x, meta, cache, slots, pending=True), r, post)
             else:
@@ -661,6 +685,7 @@ class Transformer(torch.nn.Module):
                                        r, post)
             rec = record.append if (record is not None and i in self.router_cfgs) else None
             pend = self._mlp_partial(i, x2, record=rec) if rec is not None else self._pending_mlp(i, x2)
+            pend = self._sw(i, "post_mlp_layernorm", pend)
         y, _ = self._add_norm(pend, r, self.params["norm.weight"])
         return y
 
@@ -694,9 +719,10 @@ class Transformer(torch.nn.Module):
                                           cfg.rms_eps, cfg.qk_norm)
                 o = decode_attention(q, cache.k[i], cache.v[i], page_table, ctx_lens)
                 a = self._pending_out(o.reshape(B, -1), pre + "o_proj.weight")
-            x2, r = self._add_norm(a, r, post)
+            x2, r = self._add_norm(self._sw(i, "post_self_attn_layernorm", a), r, post)
             rec = record.append if (record is not None and i in self.router_cfgs) else None
             pend = self._mlp_partial(i, x2, record=rec) if rec is not None else self._pending_mlp(i, x2)
+            pend = self._sw(i, "post_mlp_layernorm", pend)
         y, _ = self._add_norm(pend, r, self.params["norm.weight"])
         return y
 

@@ -260,3 +260,38 @@ def test_qwen35_moe_matches_transformers(tmp_path):
         back = Qwen3_5MoeForCausalLM.from_pretrained(str(tmp_path / "ours"),
                                                      torch_dtype=torch.float32).eval()(toks).logits[0].float()
     assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
+
+
+def test_glm4_dense_matches_transformers(tmp_path):
+    """GLM-4 dense: sandwich norms, adjacent-pair half-width rotary, q/k/v biases, fused gate_up."""
+    from transformers import Glm4Config, Glm4ForCausalLM
+
+    from miles_b200.checkpoint.hf import load_hf, save_hf
+    from miles_b200.models.config import ModelConfig
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops.attention import VarlenMeta
+
+    torch.manual_seed(0)
+    hf = Glm4ForCausalLM(Glm4Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                                    num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                                    tie_word_embeddings=False, pad_token_id=0)).eval()
+    with torch.no_grad():
+        for n, p in hf.named_parameters():
+            if n.endswith("bias"):
+                p.normal_(0, 0.1)
+            if n.endswith("layernorm.weight"):
+                p.normal_(1.0, 0.1)
+    hf.save_pretrained(str(tmp_path / "hf"))
+    cfg = ModelConfig.from_hf(str(tmp_path / "hf"))
+    assert cfg.sandwich_norm and cfg.rope_interleave
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=1)
+    load_hf(m, str(tmp_path / "hf"))
+    toks = torch.randint(0, cfg.vocab_size, (1, 27))
+    with torch.no_grad():
+        ref = hf(toks).logits[0].float()
+        ours = m.forward_train(toks[0].int(), VarlenMeta([0, 27], "cpu")).float() @ m.lm_head_weight().float().t()
+    assert (ref - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item()), (ref - ours).abs().max()
+    save_hf(m, str(tmp_path / "ours"))
+    with torch.no_grad():
+        back = Glm4ForCausalLM.from_pretrained(str(tmp_path / "ours"), torch_dtype=torch.float32).eval()(toks).logits[0].float()
+    assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
