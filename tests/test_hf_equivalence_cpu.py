@@ -295,3 +295,53 @@ def test_glm4_dense_matches_transformers(tmp_path):
     with torch.no_grad():
         back = Glm4ForCausalLM.from_pretrained(str(tmp_path / "ours"), torch_dtype=torch.float32).eval()(toks).logits[0].float()
     assert (back - ours).abs().max() < 1e-4 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("family", ["qwen2", "glm4", "glm45", "qwen3_next"])
+def test_engine_decode_matches_forward_for_hf_families(tmp_path, family):
+    """The rollout engine's prefill + decode path (paged cache, separate-projection attention,
+    sandwich norms, gated attention / GDN state) reproduces the training forward."""
+    import numpy as np
+    from transformers import (Glm4Config, Glm4ForCausalLM, Glm4MoeConfig, Glm4MoeForCausalLM, Qwen2Config,
+                              Qwen2ForCausalLM, Qwen3NextConfig, Qwen3NextForCausalLM)
+
+    from miles_b200.checkpoint.hf import load_hf
+    from miles_b200.engine.engine import GenRequest, RolloutEngine
+    from miles_b200.models.config import ModelConfig
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops.attention import VarlenMeta
+
+    torch.manual_seed(0)
+    base = dict(vocab_size=512, hidden_size=256, num_hidden_layers=4, num_attention_heads=4,
+                num_key_value_heads=2, tie_word_embeddings=False)
+    if family == "qwen2":
+        hf = Qwen2ForCausalLM(Qwen2Config(intermediate_size=512, **base))
+    elif family == "glm4":
+        hf = Glm4ForCausalLM(Glm4Config(intermediate_size=512, head_dim=64, pad_token_id=0, **base))
+    elif family == "glm45":
+        hf = Glm4MoeForCausalLM(Glm4MoeConfig(intermediate_size=512, moe_intermediate_size=128, head_dim=64,
+                                              n_routed_experts=8, num_experts_per_tok=2, first_k_dense_replace=1,
+                                              attention_bias=True, use_qk_norm=True, **base))
+    else:
+        hf = Qwen3NextForCausalLM(Qwen3NextConfig(intermediate_size=512, moe_intermediate_size=128,
+                                                  shared_expert_intermediate_size=128, head_dim=128,
+                                                  num_experts=8, num_experts_per_tok=2, linear_num_key_heads=2,
+                                                  linear_num_value_heads=4, linear_key_head_dim=32,
+                                                  linear_value_head_dim=32, full_attention_interval=2, **base))
+    hf.save_pretrained(str(tmp_path / "hf"))
+    cfg = ModelConfig.from_hf(str(tmp_path / "hf"))
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=1)
+    load_hf(m, str(tmp_path / "hf"))
+    eng = RolloutEngine(m, max_batch=2, num_pages=32, max_pages_per_seq=4, use_cuda_graph=False)
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(0, 512, n).tolist() for n in (7, 40, 19)]
+    outs = eng.generate([GenRequest(p, 6, temperature=0.0, rid=i) for i, p in enumerate(prompts)])
+    for p, o in zip(prompts, outs):
+        toks = p + o.tokens
+        with torch.no_grad():
+            h = m.forward_train(torch.tensor(toks, dtype=torch.int32), VarlenMeta([0, len(toks)], "cpu"))
+        logits = h.float() @ m.lm_head_weight().float().t()
+        assert logits[len(p) - 1:len(toks) - 1].argmax(-1).tolist() == o.tokens
+        lp = torch.log_softmax(logits[len(p) - 1:len(toks) - 1], -1)
+        ref = lp.gather(1, torch.tensor(o.tokens)[:, None])[:, 0].detach().numpy()
+        assert np.abs(ref - np.asarray(o.logprobs)).max() < 1e-4
