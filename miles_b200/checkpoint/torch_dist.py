@@ -129,7 +129,8 @@ def _mp_suffix(model) -> str:
     if getattr(model, "tp", None) is not None:
         return f".tp{model.tp.rank}of{model.tp.size}"
     if getattr(model, "pp", None) is not None:
-        return f".pp{model.pp.stage}of{model.pp.size}"
+        v = getattr(model.pp, "vpp", 1)
+        return f".pp{model.pp.stage}of{model.pp.size}" + (f"v{v}" if v > 1 else "")
     return ""
 
 

@@ -184,7 +184,7 @@ class Transformer(torch.nn.Module):
     def __init__(self, cfg: ModelConfig, device="cuda", dtype=torch.bfloat16, seed: int = 0,
                  init_std: float = 0.02, materialize: bool = True, ep_group=None, tp_group=None,
                  tp_backend: str = "auto", tp_cap_rows: int = 16384, cp_group=None,
-                 pp_group=None, ep_cap_tokens: int = 16384):
+                 pp_group=None, ep_cap_tokens: int = 16384, vpp: int = 1):
         super().__init__()
         self.cfg = cfg
         self.device = torch.device(device)
@@ -231,12 +231,12 @@ class Transformer(torch.nn.Module):
         if pp_group is not None:
             from miles_b200.parallel.pp import PPContext
 
-            self.pp = PPContext(pp_group, cfg.num_layers)
+            self.pp = PPContext(pp_group, cfg.num_layers, vpp)
             if self.pp.size == 1:
                 self.pp = None
             elif self.tp is not None or self.cp is not None or self.ep is not None:
                 raise ValueError("pipeline parallelism is supported with data parallelism only")
-        self.layer_ids = list(range(self.pp.lo, self.pp.hi)) if self.pp else list(range(cfg.num_layers))
+        self.layer_ids = list(self.pp.layer_ids) if self.pp else list(range(cfg.num_layers))
         self.is_first = self.pp is None or self.pp.is_first
         self.is_last = self.pp is None or self.pp.is_last
         self.specs = param_specs(cfg, self.ep.size if self.ep else 1, self.tp_size, self.layer_ids,
@@ -401,12 +401,12 @@ class Transformer(torch.nn.Module):
         return m, r
 
     # -------------------------------------------------------------------------------- layer loop
-    def _run_layers(self, layer_fn, r, replay_experts, rows=None):
+    def _run_layers(self, layer_fn, r, replay_experts, rows=None, layers=None):
         """Run this rank's layers: layer_fn(i, m_prev, r_prev, replay) -> (m, r), with per-layer
         activation recompute when training. `replay_experts` [T, L_moe, k] is sliced to layer i's
         MoE column (and to `rows`, a slice of this rank's rows, if given)."""
         m = None
-        for i in self.layer_ids:
+        for i in (self.layer_ids if layers is None else layers):
             replay = None
             if i in self.router_cfgs and replay_experts is not None:
                 col = replay_experts[:, self.moe_index[i]]
@@ -579,12 +579,14 @@ class Transformer(torch.nn.Module):
     def forward_train(self, tokens: torch.Tensor, meta: VarlenMeta,
                       replay_experts: torch.Tensor | None = None,
                       record_experts: list | None = None,
-                      hidden_in: torch.Tensor | None = None) -> torch.Tensor:
+                      hidden_in: torch.Tensor | None = None, chunk: int | None = None) -> torch.Tensor:
         """tokens int [T] packed; returns final hidden [T, H] (after the final norm).
         replay_experts: int32 [T, L_moe, k] routing to replay (R3).
         Pipeline stages: a stage after the first takes the residual stream `hidden_in`, a stage
         before the last returns its residual stream (bitwise what the next layer's fused
-        residual add would have formed)."""
+        residual add would have formed). With interleaved stages (`vpp` > 1) `chunk` selects the
+        model chunk to run: the embedding belongs to chunk 0 of the first rank, the final norm to
+        the last chunk of the last rank."""
         cfg = self.cfg
         if self.tp is not None and self.sequence_parallel and record_experts is None:
             return self._forward_train_sp(tokens, meta, replay_experts)
@@ -592,7 +594,12 @@ class Transformer(torch.nn.Module):
             if record_experts is not None:
                 raise NotImplementedError("routing capture under context parallelism")
             return self._forward_train_cp(tokens, meta, replay_experts)
-        r = F.embedding(tokens.long(), self.params["embed_tokens.weight"]) if self.is_first else hidden_in
+        layers, first, last = None, self.is_first, self.is_last
+        if chunk is not None and self.pp is not None:
+            lo, hi = self.pp.chunks[chunk]
+            layers = list(range(lo, hi))
+            first, last = first and chunk == 0, last and chunk == self.pp.vpp - 1
+        r = F.embedding(tokens.long(), self.params["embed_tokens.weight"]) if first else hidden_in
 
         def layer(i, m, r, replay):
             if (record_experts is not None and i in self.router_cfgs
@@ -605,8 +612,8 @@ class Transformer(torch.nn.Module):
                 return self._mlp(i, x2, replay=replay, record=record_experts.append), r
             return self._layer_train(i, m, r, meta, replay)
 
-        m, r = self._run_layers(layer, r, replay_experts)
-        if not self.is_last:
+        m, r = self._run_layers(layer, r, replay_experts, layers=layers)
+        if not last:
             return r if m is None else m + r
         y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
         return y

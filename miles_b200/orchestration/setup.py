@@ -151,6 +151,7 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
     dtype = torch.bfloat16 if ctx.device.type == "cuda" else torch.float32
     model = Transformer(cfg, device=ctx.device, dtype=dtype, seed=args.seed, tp_group=ctx.tp_group,
                         ep_group=ctx.ep_group, cp_group=ctx.cp_group, pp_group=ctx.pp_group,
+                        vpp=getattr(args, "virtual_pipeline_model_parallel_size", None) or 1,
                         tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
     if getattr(args, "sequence_parallel", False) and model.tp is not None and model.mla is None:
         model.sequence_parallel = True

@@ -12,7 +12,11 @@ send and receive in one batched isend/irecv (send the forward output while recei
 gradient of an earlier micro-batch, and the reverse), so no ordering of blocking sends can
 deadlock. The loss lives on the last stage.
 
-Reference: Megatron get_forward_backward_func 1F1B (megatron_utils/model.py:440-450),
+Interleaved schedule (`vpp` > 1, `run_interleaved`): each rank holds vpp model chunks, a
+micro-batch passes every rank vpp times, and the bubble shrinks to (P - 1) / vpp stage-times.
+
+Reference: Megatron get_forward_backward_func 1F1B (megatron_utils/model.py:440-450), virtual
+pipeline size (megatron_utils/initialize.py:44),
 --pipeline-model-parallel-size, loss on the last stage (model.py:487-490), PP shards gathered
 at refit (update_weight/common.py).
 """
@@ -28,16 +32,29 @@ _TIED_GROUPS: dict = {}
 
 
 class PPContext:
-    def __init__(self, group, num_layers: int):
+    """Stage layout of one pipeline. With `vpp` > 1 (interleaved / virtual pipeline) the layers
+    are cut into size * vpp chunks; rank s owns chunks c * size + s for c < vpp, so a
+    micro-batch visits every rank vpp times (model chunk c of rank s is virtual stage
+    c * size + s)."""
+
+    def __init__(self, group, num_layers: int, vpp: int = 1):
         self.group = group
         self.size = dist.get_world_size(group)
         self.stage = dist.get_rank(group)
-        base, extra = divmod(num_layers, self.size)
-        counts = [base + (1 if s < extra else 0) for s in range(self.size)]
+        self.vpp = vpp
+        nv = self.size * vpp
+        base, extra = divmod(num_layers, nv)
+        counts = [base + (1 if v < extra else 0) for v in range(nv)]
         if min(counts) == 0:
-            raise ValueError(f"{num_layers} layers do not fill {self.size} pipeline stages")
-        self.bounds = [sum(counts[:s]) for s in range(self.size + 1)]
-        self.lo, self.hi = self.bounds[self.stage], self.bounds[self.stage + 1]
+            raise ValueError(f"{num_layers} layers do not fill {nv} (virtual) pipeline stages")
+        self.vbounds = [sum(counts[:v]) for v in range(nv + 1)]
+        # layer ranges of this rank's model chunks, in chunk order
+        self.chunks = [(self.vbounds[c * self.size + self.stage], self.vbounds[c * self.size + self.stage + 1])
+                       for c in range(vpp)]
+        self.layer_ids = [i for lo, hi in self.chunks for i in range(lo, hi)]
+        if vpp == 1:
+            self.bounds = self.vbounds
+            self.lo, self.hi = self.chunks[0]
         self.is_first = self.stage == 0
         self.is_last = self.stage == self.size - 1
         self.ranks = [dist.get_global_rank(group, s) for s in range(self.size)]
@@ -48,9 +65,10 @@ class PPContext:
             _TIED_GROUPS[key] = dist.new_group([self.ranks[0], self.ranks[-1]])
 
     def stage_of_layer(self, i: int) -> int:
-        for s in range(self.size):
-            if self.bounds[s] <= i < self.bounds[s + 1]:
-                return s
+        """Rank (within the pipeline group) that owns layer i."""
+        for v in range(self.size * self.vpp):
+            if self.vbounds[v] <= i < self.vbounds[v + 1]:
+                return v % self.size
         raise IndexError(i)
 
     @property
@@ -139,6 +157,136 @@ def run_1f1b(pp: PPContext, n_mb: int, shapes: list[tuple], dtype, device,
         dh = run_bwd(i, g)
         if not first:
             _p2p([dist.P2POp(dist.isend, dh.contiguous(), pp.prev, group=pp.group)])
+
+
+def _virtual_order(P: int, V: int, n_mb: int, reverse: bool) -> list[tuple[int, int]]:
+    """(micro-batch, chunk) visit order of one rank: groups of P micro-batches go through chunk
+    0, 1, ..., V-1 (backwards: V-1, ..., 0) before the next group starts."""
+    out = []
+    for g in range(0, n_mb, P):
+        grp = range(g, min(g + P, n_mb))
+        for c in (reversed(range(V)) if reverse else range(V)):
+            out += [(j, c) for j in grp]
+    return out
+
+
+def interleaved_schedule(P: int, V: int, n_mb: int, train: bool = True):
+    """Plan of the interleaved 1F1B schedule for every rank of a P-stage pipeline with V model
+    chunks per rank, as a list of ticks.
+
+    Each rank runs its own op sequence: forwards in `_virtual_order`, of which the first
+    (P - s - 1) * 2 + (V - 1) * P are warm-up, then alternating one forward / one backward,
+    then the remaining backwards. The plan is found by simulating all ranks in lockstep: in a
+    tick each rank runs its next op if its input was produced in an earlier tick. An op's
+    message (activation to virtual stage v+1, gradient to v-1) is exchanged at the end of the
+    tick that produced it, so every rank derives the same (sender, receiver) pairs per tick
+    and posts them in one batched send/recv: no ordering of point-to-point calls can
+    deadlock. If the warm-up depth of the 1F1B order stalls (possible when n_mb is not a
+    multiple of P), every rank falls back to all forwards, then all backwards.
+
+    Returns ticks: list of (ops, msgs) with ops {rank: ("F" | "B", mb, chunk)} and msgs
+    [(src, dst, "F" | "B", mb, v_dst)], v_dst the virtual stage that consumes the message."""
+    NV = P * V
+
+    def seqs(warm_fn):
+        out = []
+        for s in range(P):
+            fw = _virtual_order(P, V, n_mb, False)
+            if not train:
+                out.append([("F", j, c) for j, c in fw])
+                continue
+            bw = _virtual_order(P, V, n_mb, True)
+            w = min(warm_fn(s), len(fw))
+            ops = [("F", j, c) for j, c in fw[:w]]
+            fi, bi = w, 0
+            while fi < len(fw):
+                ops.append(("F",) + fw[fi]); fi += 1
+                ops.append(("B",) + bw[bi]); bi += 1
+            ops += [("B",) + x for x in bw[bi:]]
+            out.append(ops)
+        return out
+
+    def simulate(per_rank):
+        done: dict = {}
+        pos = [0] * P
+        ticks = []
+        t = 0
+        while any(pos[s] < len(per_rank[s]) for s in range(P)):
+            ops, msgs = {}, []
+            for s in range(P):
+                if pos[s] >= len(per_rank[s]):
+                    continue
+                kind, j, c = per_rank[s][pos[s]]
+                v = c * P + s
+                if kind == "F":
+                    dep = [("F", j, v - 1)] if v > 0 else []
+                else:
+                    dep = [("F", j, v)] + ([("B", j, v + 1)] if v < NV - 1 else [])
+                if all(done.get(d, t) < t for d in dep):
+                    ops[s] = (kind, j, c)
+            if not ops:
+                return None
+            for s, (kind, j, c) in ops.items():
+                v = c * P + s
+                done[(kind, j, v)] = t
+                pos[s] += 1
+                if kind == "F" and v < NV - 1:
+                    msgs.append((s, (v + 1) % P, "F", j, v + 1))
+                if kind == "B" and v > 0:
+                    msgs.append((s, (v - 1) % P, "B", j, v - 1))
+            ticks.append((ops, msgs))
+            t += 1
+        return ticks
+
+    warm = (lambda s: (P - s - 1) * 2 + (V - 1) * P) if V > 1 else (lambda s: P - s - 1)
+    plan = simulate(seqs(warm))
+    if plan is None:
+        plan = simulate(seqs(lambda s: n_mb * V))
+    return plan
+
+
+def run_interleaved(pp: PPContext, n_mb: int, shapes: list[tuple], dtype, device,
+                    forward: Callable[[int, int, torch.Tensor | None], torch.Tensor],
+                    backward: Callable[[int, int, torch.Tensor, torch.Tensor | None], None] | None) -> None:
+    """Drive `n_mb` micro-batches through this rank's `pp.vpp` model chunks.
+
+    forward(j, c, h_in) -> output of chunk c for micro-batch j (the loss on the last virtual
+    stage); h_in None on virtual stage 0. backward(j, c, output, grad) (grad None on the last
+    virtual stage); backward None runs the forward-only schedule (log-probs)."""
+    P, V, me = pp.size, pp.vpp, pp.stage
+    plan = interleaved_schedule(P, V, n_mb, train=backward is not None)
+    mail: dict = {}
+    saved: dict = {}
+    pending: dict = {}
+    for ops, msgs in plan:
+        op = ops.get(me)
+        if op is not None:
+            kind, j, c = op
+            v = c * P + me
+            if kind == "F":
+                h = mail.pop(("F", j, v), None)
+                if h is not None and backward is not None:
+                    h.requires_grad_(True)
+                out = forward(j, c, h)
+                if backward is not None:
+                    saved[(j, c)] = (h, out)
+                pending[("F", j, v + 1)] = out
+            else:
+                h, out = saved.pop((j, c))
+                backward(j, c, out, mail.pop(("B", j, v), None))
+                pending[("B", j, v - 1)] = h.grad if h is not None else None
+        p2p = []
+        for src, dst, kind, j, vd in msgs:
+            if src == me:
+                t = pending.pop((kind, j, vd))
+                t = (t.detach() if kind == "F" else t).contiguous()
+                p2p.append(dist.P2POp(dist.isend, t, pp.ranks[dst], group=pp.group))
+            elif dst == me:
+                t = torch.empty(shapes[j], dtype=dtype, device=device)
+                mail[(kind, j, vd)] = t
+                p2p.append(dist.P2POp(dist.irecv, t, pp.ranks[src], group=pp.group))
+        _p2p(p2p)
+        pending = {k: t for k, t in pending.items() if t is not None and k[2] not in (-1, P * V)}
 
 
 def run_forward_only(pp: PPContext, n_mb: int, shapes: list[tuple], dtype, device,

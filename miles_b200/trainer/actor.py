@@ -217,7 +217,7 @@ class Actor:
     @torch.no_grad()
     def _logprobs_pp(self, items):
         from miles_b200.ops.logprob import lm_head_logprob
-        from miles_b200.parallel.pp import run_forward_only
+        from miles_b200.parallel.pp import run_forward_only, run_interleaved
 
         model, cfg = self.model, self.cfg
         mbs = pack_microbatches([len(it.tokens) for it in items], cfg.max_tokens_per_gpu)
@@ -226,10 +226,13 @@ class Actor:
         shapes = [(x[0].shape[0], model.cfg.hidden_size) for x in ins]
         out: list = [None] * len(items)
 
-        def forward(j, h):
+        V = model.pp.vpp
+
+        def forward(j, h, c=None):
             tok, meta, sel, tgt = ins[j]
-            y = model.forward_train(tok, meta, replay_experts=self._replay(subs[j]), hidden_in=h)
-            if model.is_last:
+            y = model.forward_train(tok, meta, replay_experts=self._replay(subs[j]), hidden_in=h,
+                                    chunk=c)
+            if model.is_last and (c is None or c == V - 1):
                 lp, _ = lm_head_logprob(y.index_select(0, sel), model.lm_head_weight(), tgt,
                                         cfg.temperature, cfg.logprob_chunk)
                 lp = lp.float().cpu().numpy()
@@ -240,7 +243,11 @@ class Actor:
                     o += n
             return y
 
-        run_forward_only(model.pp, len(ins), shapes, model.dtype, self.dev, forward)
+        if V > 1:
+            run_interleaved(model.pp, len(ins), shapes, model.dtype, self.dev,
+                            lambda j, c, h: forward(j, h, c), None)
+        else:
+            run_forward_only(model.pp, len(ins), shapes, model.dtype, self.dev, forward)
         box = [out]
         dist.broadcast_object_list(box, model.pp.ranks[-1], group=model.pp.group)
         return box[0]
@@ -334,18 +341,20 @@ class Actor:
         """One training pass over the micro-batches through the 1F1B pipeline; the loss and the
         metrics live on the last stage, which broadcasts the metrics to the other stages."""
         from miles_b200.ops.logprob import lm_head_logprob
-        from miles_b200.parallel.pp import reduce_tied_embedding, run_1f1b
+        from miles_b200.parallel.pp import reduce_tied_embedding, run_1f1b, run_interleaved
 
         model, cfg = self.model, self.cfg
         subs = [[items[i] for i in mb] for mb in mbs]
         preps = [self._mb_prepare(sub, n_samples, n_tokens) for sub in subs]
         shapes = [(p["tok"].shape[0], model.cfg.hidden_size) for p in preps]
 
-        def forward(j, h):
+        V = model.pp.vpp
+
+        def forward(j, h, c=None):
             p = preps[j]
             out = model.forward_train(p["tok"], p["meta"], replay_experts=self._replay(subs[j]),
-                                      hidden_in=h)
-            if not model.is_last:
+                                      hidden_in=h, chunk=c)
+            if not (model.is_last and (c is None or c == V - 1)):
                 return out
             lp, ent = lm_head_logprob(out.index_select(0, p["sel"]), model.lm_head_weight(), p["tgt"],
                                       cfg.temperature, cfg.logprob_chunk)
@@ -357,7 +366,11 @@ class Actor:
             else:
                 out.backward(g)
 
-        run_1f1b(model.pp, len(preps), shapes, model.dtype, self.dev, forward, backward)
+        if V > 1:
+            run_interleaved(model.pp, len(preps), shapes, model.dtype, self.dev,
+                            lambda j, c, h: forward(j, h, c), lambda j, c, out, g: backward(j, out, g))
+        else:
+            run_1f1b(model.pp, len(preps), shapes, model.dtype, self.dev, forward, backward)
         for name, p in model.params.items():  # autograd-held grads -> flat buffer before the tie
             if p.grad is not None:
                 p.main_grad.add_(p.grad.to(p.main_grad.dtype))

@@ -61,6 +61,8 @@ def add_train_args(p):
     # model / optimizer (Megatron-compatible names)
     g.add_argument("--tensor-model-parallel-size", type=int, default=1)
     g.add_argument("--pipeline-model-parallel-size", type=int, default=1)
+    g.add_argument("--virtual-pipeline-model-parallel-size", type=int, default=None,
+                   help="model chunks per pipeline rank (interleaved 1F1B schedule)")
     g.add_argument("--context-parallel-size", type=int, default=1)
     g.add_argument("--expert-model-parallel-size", type=int, default=1)
     g.add_argument("--expert-tensor-parallel-size", type=int, default=1)
