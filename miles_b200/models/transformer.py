@@ -184,7 +184,8 @@ class Transformer(torch.nn.Module):
     def __init__(self, cfg: ModelConfig, device="cuda", dtype=torch.bfloat16, seed: int = 0,
                  init_std: float = 0.02, materialize: bool = True, ep_group=None, tp_group=None,
                  tp_backend: str = "auto", tp_cap_rows: int = 16384, cp_group=None,
-                 pp_group=None, ep_cap_tokens: int = 16384, vpp: int = 1):
+                 pp_group=None, ep_cap_tokens: int = 16384, vpp: int = 1,
+                 pp_first_layers: int | None = None, pp_last_layers: int | None = None):
         super().__init__()
         self.cfg = cfg
         self.device = torch.device(device)
@@ -231,7 +232,7 @@ class Transformer(torch.nn.Module):
         if pp_group is not None:
             from miles_b200.parallel.pp import PPContext
 
-            self.pp = PPContext(pp_group, cfg.num_layers, vpp)
+            self.pp = PPContext(pp_group, cfg.num_layers, vpp, pp_first_layers, pp_last_layers)
             if self.pp.size == 1:
                 self.pp = None
             elif self.tp is not None or self.cp is not None or self.ep is not None:

@@ -152,6 +152,8 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
     model = Transformer(cfg, device=ctx.device, dtype=dtype, seed=args.seed, tp_group=ctx.tp_group,
                         ep_group=ctx.ep_group, cp_group=ctx.cp_group, pp_group=ctx.pp_group,
                         vpp=getattr(args, "virtual_pipeline_model_parallel_size", None) or 1,
+                        pp_first_layers=getattr(args, "decoder_first_pipeline_num_layers", None),
+                        pp_last_layers=getattr(args, "decoder_last_pipeline_num_layers", None),
                         tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
     if getattr(args, "sequence_parallel", False) and model.tp is not None and model.mla is None:
         model.sequence_parallel = True

@@ -31,20 +31,36 @@ import torch.distributed as dist
 _TIED_GROUPS: dict = {}
 
 
+def stage_layer_counts(num_layers: int, n_stages: int, first: int | None = None,
+                       last: int | None = None) -> list[int]:
+    """Layers per (virtual) stage: `first` / `last` pin the first and last stage's counts (the
+    embedding / LM-head stages often take fewer layers), the rest are split evenly with the
+    remainder on the earlier stages."""
+    head = [first] if first is not None else []
+    tail = [last] if last is not None else []
+    mid_n = n_stages - len(head) - len(tail)
+    rest = num_layers - sum(head) - sum(tail)
+    if mid_n < 0 or rest < 0 or (mid_n == 0 and rest != 0):
+        raise ValueError(f"first={first} / last={last} layers do not fit {num_layers} layers "
+                         f"in {n_stages} stages")
+    base, extra = divmod(rest, mid_n) if mid_n else (0, 0)
+    return head + [base + (1 if v < extra else 0) for v in range(mid_n)] + tail
+
+
 class PPContext:
     """Stage layout of one pipeline. With `vpp` > 1 (interleaved / virtual pipeline) the layers
     are cut into size * vpp chunks; rank s owns chunks c * size + s for c < vpp, so a
     micro-batch visits every rank vpp times (model chunk c of rank s is virtual stage
     c * size + s)."""
 
-    def __init__(self, group, num_layers: int, vpp: int = 1):
+    def __init__(self, group, num_layers: int, vpp: int = 1, first_layers: int | None = None,
+                 last_layers: int | None = None):
         self.group = group
         self.size = dist.get_world_size(group)
         self.stage = dist.get_rank(group)
         self.vpp = vpp
         nv = self.size * vpp
-        base, extra = divmod(num_layers, nv)
-        counts = [base + (1 if v < extra else 0) for v in range(nv)]
+        counts = stage_layer_counts(num_layers, nv, first_layers, last_layers)
         if min(counts) == 0:
             raise ValueError(f"{num_layers} layers do not fill {nv} (virtual) pipeline stages")
         self.vbounds = [sum(counts[:v]) for v in range(nv + 1)]

@@ -63,6 +63,10 @@ def add_train_args(p):
     g.add_argument("--pipeline-model-parallel-size", type=int, default=1)
     g.add_argument("--virtual-pipeline-model-parallel-size", type=int, default=None,
                    help="model chunks per pipeline rank (interleaved 1F1B schedule)")
+    g.add_argument("--decoder-first-pipeline-num-layers", type=int, default=None,
+                   help="layers on the first pipeline stage (the rest split evenly)")
+    g.add_argument("--decoder-last-pipeline-num-layers", type=int, default=None,
+                   help="layers on the last pipeline stage")
     g.add_argument("--context-parallel-size", type=int, default=1)
     g.add_argument("--expert-model-parallel-size", type=int, default=1)
     g.add_argument("--expert-tensor-parallel-size", type=int, default=1)
@@ -525,6 +529,12 @@ def validate_args(args) -> None:
         raise ValueError(f"world size {world} not divisible by TP*PP*CP = {mp}")
     args.data_parallel_size = world // mp
     args.world_size = world
+    if args.pipeline_model_parallel_size == 1 and (
+            args.decoder_first_pipeline_num_layers is not None
+            or args.decoder_last_pipeline_num_layers is not None
+            or (args.virtual_pipeline_model_parallel_size or 1) > 1):
+        raise ValueError("--decoder-first/last-pipeline-num-layers and "
+                         "--virtual-pipeline-model-parallel-size need --pipeline-model-parallel-size > 1")
 
 
 def reset_arg(parser: argparse.ArgumentParser, name: str, **kwargs) -> None:

@@ -144,7 +144,7 @@ def test_interleaved_schedule_plan():
     assert all(op[0] == "F" for ops, _ in fo for op in ops.values())
 
 
-def _run_vpp(rank, world, port, name, ckpt, out, vpp):
+def _run_vpp(rank, world, port, name, ckpt, out, vpp, first=None, last=None):
     os.environ["MILES_B200_FORCE_CPU"] = "1"
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     from miles_b200.checkpoint.hf import load_hf
@@ -152,7 +152,8 @@ def _run_vpp(rank, world, port, name, ckpt, out, vpp):
     from miles_b200.models.transformer import Transformer
 
     cfg = dataclasses.replace(preset(name), num_layers=4)
-    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=7, pp_group=dist.group.WORLD, vpp=vpp)
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=7, pp_group=dist.group.WORLD, vpp=vpp,
+                    pp_first_layers=first, pp_last_layers=last)
     assert len(m.pp.chunks) == vpp
     load_hf(m, ckpt)
     old, met = _step(m, cfg)
@@ -161,8 +162,10 @@ def _run_vpp(rank, world, port, name, ckpt, out, vpp):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name,world,vpp,port", [("tiny", 2, 2, 29663), ("tiny-moe", 2, 2, 29664)])
-def test_interleaved_pp_matches_single(tmp_path, name, world, vpp, port):
+@pytest.mark.parametrize("name,world,vpp,port,first,last", [
+    ("tiny", 2, 2, 29663, None, None), ("tiny-moe", 2, 2, 29664, None, None),
+    ("tiny", 2, 1, 29665, 1, 3)])
+def test_interleaved_pp_matches_single(tmp_path, name, world, vpp, port, first, last):
     """Interleaved (virtual) pipeline: each of 2 ranks holds 2 model chunks (4 layers -> virtual
     stages of one layer, rank 0 layers {0, 2}, rank 1 layers {1, 3}); the step equals one rank's."""
     from miles_b200.checkpoint.hf import save_hf
@@ -175,7 +178,7 @@ def test_interleaved_pp_matches_single(tmp_path, name, world, vpp, port):
     save_hf(m, ckpt)
     old1, met1 = _step(m, cfg)
     out = str(tmp_path / "vpp")
-    mp.spawn(_run_vpp, args=(world, port, name, ckpt, out, vpp), nprocs=world, join=True)
+    mp.spawn(_run_vpp, args=(world, port, name, ckpt, out, vpp, first, last), nprocs=world, join=True)
     seen = set()
     for r in range(world):
         res = torch.load(f"{out}.{r}", weights_only=False)
@@ -188,3 +191,14 @@ def test_interleaved_pp_matches_single(tmp_path, name, world, vpp, port):
             assert torch.allclose(v, m.params[k].detach(), atol=1e-5), (r, k, (v - m.params[k]).abs().max())
             seen.add(k)
     assert seen == set(m.params)
+
+
+def test_stage_layer_counts():
+    from miles_b200.parallel.pp import stage_layer_counts
+
+    assert stage_layer_counts(10, 4) == [3, 3, 2, 2]
+    assert stage_layer_counts(10, 4, first=1) == [1, 3, 3, 3]
+    assert stage_layer_counts(10, 4, first=1, last=2) == [1, 4, 3, 2]
+    assert stage_layer_counts(4, 2, first=1, last=3) == [1, 3]
+    with pytest.raises(ValueError):
+        stage_layer_counts(4, 2, first=1, last=1)
