@@ -21,7 +21,7 @@ from safetensors.torch import save_file
 
 from miles_b200.models.config import ModelConfig
 from miles_b200.models.transformer import Transformer
-from miles_b200.parallel.tp import tp_gather, tp_slice
+from miles_b200.parallel.tp import model_tp, tp_gather, tp_slice
 
 
 def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
@@ -78,10 +78,11 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
             w1 = P[L + "mlp.experts.w1"].data
             w2 = P[L + "mlp.experts.w2"].data
             I = w1.shape[1] // 2
+            e0 = model.ep.first if getattr(model, "ep", None) is not None else 0  # global expert ids
             for e in range(w1.shape[0]):
-                yield pre + L + f"mlp.experts.{e}.gate_proj.weight", w1[e, :I]
-                yield pre + L + f"mlp.experts.{e}.up_proj.weight", w1[e, I:]
-                yield pre + L + f"mlp.experts.{e}.down_proj.weight", w2[e]
+                yield pre + L + f"mlp.experts.{e0 + e}.gate_proj.weight", w1[e, :I]
+                yield pre + L + f"mlp.experts.{e0 + e}.up_proj.weight", w1[e, I:]
+                yield pre + L + f"mlp.experts.{e0 + e}.down_proj.weight", w2[e]
             if cfg.shared_expert_intermediate_size:
                 gu = P[L + "mlp.shared_expert.gate_up_proj.weight"].data
                 Is = gu.shape[0] // 2
@@ -241,23 +242,38 @@ def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> No
         if not shard:
             return
         idx += 1
-        fn = f"model-{idx:05d}.safetensors" if stage is None else f"model-pp{stage:02d}-{idx:05d}.safetensors"
+        fn = (f"model-{idx:05d}.safetensors" if stage is None else f"model-pp{stage:02d}-{idx:05d}.safetensors")
+        if ep is not None:
+            fn = fn.replace("model-", f"model-ep{ep.rank:02d}-")
         save_file(shard, os.path.join(path, fn), metadata={"format": "pt"})
         for n in shard:
             weight_map[n] = fn
         shard, size = {}, 0
 
     # tensor parallel: every TP rank takes part in the gathers, TP rank 0 writes;
-    # pipeline parallel: every stage writes its own files, stage 0 writes the merged index
+    # pipeline parallel: every stage writes its own files, stage 0 writes the merged index;
+    # expert parallel: every EP rank writes its experts, EP rank 0 the rest and the index
     writer = model.tp is None or model.tp.rank == 0
     stage = model.pp.stage if model.pp is not None else None
+    ep = getattr(model, "ep", None)
     if stage is not None and stage > 0 and model.cfg.tie_embeddings:
         skip = {"model.embed_tokens.weight"}  # stage 0 writes the tied embedding
     else:
         skip = set()
+    if ep is not None:
+        import torch.distributed as dist
+
+        ep_first = 0 in dist.get_process_group_ranks(ep.group)  # the EP group rank 0 is in
     for name, t in to_hf_tensors(model):
-        t = tp_gather(name, t.detach(), model.tp)
-        if not writer or name in skip:
+        tpc = model_tp(model, name)
+        t = tp_gather(name, t.detach(), tpc)
+        if name in skip:
+            continue
+        if ep is not None and ".mlp.experts." in name:
+            # experts: every EP rank of the first EP group (TP rank 0 when TP splits them)
+            if not ep_first or (tpc is not None and tpc.rank != 0):
+                continue
+        elif not writer or (ep is not None and ep.rank != 0):
             continue
         t = to_hf_layout(model.cfg, name, t)
         if model.cfg.arch == "qwen3_5" and name.startswith("model."):
@@ -270,6 +286,17 @@ def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> No
         size += nb
         total += nb
     flush()
+    if ep is not None:
+        import torch.distributed as dist
+
+        parts: list = [None] * ep.size
+        dist.all_gather_object(parts, (weight_map, total), group=ep.group)
+        if dist.get_rank() != 0:
+            return
+        weight_map, total = {}, 0
+        for wm, tt in parts:
+            weight_map.update(wm)
+            total += tt
     if model.pp is not None:
         import torch.distributed as dist
 
@@ -338,4 +365,4 @@ def _load(model: Transformer, wmap, get, path: str) -> None:
                 continue
             raise KeyError(f"{name} missing from {path}")
         src = from_hf_layout(cfg, name, get(src_name))
-        dst.copy_(tp_slice(name, src, model.tp).to(dst.dtype))
+        dst.copy_(tp_slice(name, src, model_tp(model, name)).to(dst.dtype))

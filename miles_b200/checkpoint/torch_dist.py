@@ -87,10 +87,13 @@ def _key(model: Transformer, name: str) -> str:
     (the HF path reshards between sizes)."""
     k = megatron_name(name, model.cfg)
     if model.tp is not None:
-        from miles_b200.parallel.tp import is_tp_sharded
+        from miles_b200.parallel.tp import is_tp_sharded, model_tp
 
-        if is_tp_sharded(name):
+        if is_tp_sharded(name) and model_tp(model, name) is not None:
             k += f".tp{model.tp.rank}of{model.tp.size}"
+    ep = getattr(model, "ep", None)
+    if ep is not None and ".mlp.experts." in "." + name:
+        k += f".ep{ep.rank}of{ep.size}"  # each EP rank holds a different expert slice
     return k
 
 
@@ -123,15 +126,18 @@ _ASYNC: threading.Thread | None = None
 
 
 def _mp_suffix(model) -> str:
-    """Key suffix of this rank's model-parallel part (TP rank / pipeline stage)."""
+    """Key suffix of this rank's model-parallel part (TP rank / pipeline stage / EP rank)."""
     if model is None:
         return ""
+    out = ""
     if getattr(model, "tp", None) is not None:
-        return f".tp{model.tp.rank}of{model.tp.size}"
+        out += f".tp{model.tp.rank}of{model.tp.size}"
     if getattr(model, "pp", None) is not None:
         v = getattr(model.pp, "vpp", 1)
-        return f".pp{model.pp.stage}of{model.pp.size}" + (f"v{v}" if v > 1 else "")
-    return ""
+        out += f".pp{model.pp.stage}of{model.pp.size}" + (f"v{v}" if v > 1 else "")
+    if getattr(model, "ep", None) is not None:
+        out += f".ep{model.ep.rank}of{model.ep.size}"
+    return out
 
 
 def _optim_state(optimizer, model=None) -> dict:

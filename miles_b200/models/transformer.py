@@ -21,6 +21,7 @@ import math
 from dataclasses import dataclass
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 from torch.utils.checkpoint import checkpoint
 
@@ -50,11 +51,12 @@ class ParamSpec:
 
 
 def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=None,
-                first: bool = True, last: bool = True) -> list[ParamSpec]:
+                first: bool = True, last: bool = True, expert_tp: int | None = None) -> list[ParamSpec]:
     """Parameter layout; with expert parallelism each rank holds E / ep_size experts, with
     tensor parallelism each rank holds 1 / tp_size of the heads and intermediate dimensions
     (miles_b200/parallel/tp.py); a pipeline stage holds `layers` only, the embedding on the first
-    stage and the final norm + LM head on the last (tied embeddings: a copy on the last stage)."""
+    stage and the final norm + LM head on the last (tied embeddings: a copy on the last stage).
+    Routed experts split their intermediate dimension over `expert_tp` ranks (default: TP)."""
     H, D = cfg.hidden_size, cfg.head_dim
     t = tp_size
     if cfg.num_heads % t or cfg.num_kv_heads % t:
@@ -90,7 +92,7 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=Non
             specs += [ParamSpec(p + "self_attn.q_norm.weight", (D,), "ones"),
                       ParamSpec(p + "self_attn.k_norm.weight", (D,), "ones")]
         if cfg.layer_is_moe(i):
-            E, I = cfg.num_experts, cfg.moe_intermediate_size // t
+            E, I = cfg.num_experts, cfg.moe_intermediate_size // (t if expert_tp is None else expert_tp)
             El = E // ep_size
             specs += [ParamSpec(p + "mlp.gate.weight", (E, H), "normal"),
                       ParamSpec(p + "mlp.experts.w1", (El, 2 * I, H), "normal"),
@@ -185,7 +187,8 @@ class Transformer(torch.nn.Module):
                  init_std: float = 0.02, materialize: bool = True, ep_group=None, tp_group=None,
                  tp_backend: str = "auto", tp_cap_rows: int = 16384, cp_group=None,
                  pp_group=None, ep_cap_tokens: int = 16384, vpp: int = 1,
-                 pp_first_layers: int | None = None, pp_last_layers: int | None = None):
+                 pp_first_layers: int | None = None, pp_last_layers: int | None = None,
+                 etp: int | None = None):
         super().__init__()
         self.cfg = cfg
         self.device = torch.device(device)
@@ -226,8 +229,6 @@ class Transformer(torch.nn.Module):
                 self.ep = None
         if cfg.sandwich_norm and tp_group is not None and dist_world(tp_group) > 1:
             raise ValueError("sandwich-norm (GLM-4) models run without TP")
-        if self.ep is not None and self.tp is not None:
-            raise ValueError("expert parallelism combined with tensor parallelism is not supported")
         self.pp = None  # pipeline parallelism (training), miles_b200/parallel/pp.py
         if pp_group is not None:
             from miles_b200.parallel.pp import PPContext
@@ -240,8 +241,13 @@ class Transformer(torch.nn.Module):
         self.layer_ids = list(self.pp.layer_ids) if self.pp else list(range(cfg.num_layers))
         self.is_first = self.pp is None or self.pp.is_first
         self.is_last = self.pp is None or self.pp.is_last
+        # expert-tensor parallelism: routed experts split over the TP ranks (etp = TP, default)
+        # or whole on every rank (etp = 1: each TP rank routes its 1 / TP of the tokens)
+        if etp not in (None, 1, self.tp_size):
+            raise ValueError(f"expert-tensor-parallel size {etp} must be 1 or the TP size {self.tp_size}")
+        self.expert_tp = self.tp_size if etp is None else etp
         self.specs = param_specs(cfg, self.ep.size if self.ep else 1, self.tp_size, self.layer_ids,
-                                 self.is_first, self.is_last)
+                                 self.is_first, self.is_last, self.expert_tp)
         total = self.specs[-1].offset + self.specs[-1].numel
         self.numel = total
         ex = [sp.offset for sp in self.specs if is_expert_param(sp.name)]
@@ -368,16 +374,7 @@ class Transformer(torch.nn.Module):
         """MLP / MoE output before the tensor-parallel all-reduce (the full output at TP 1)."""
         pre = f"layers.{i}.mlp."
         if i in self.router_cfgs:
-            if self.ep is not None:
-                from miles_b200.parallel.ep import moe_experts_ep
-
-                y = moe_experts_ep(x, self.params[pre + "gate.weight"], self.params[pre + "experts.w1"],
-                                   self.params[pre + "experts.w2"], self.router_cfgs[i], self.ep,
-                                   self.params.get(pre + "gate.e_score_correction_bias"), replay, record)
-            else:
-                y = moe_experts(x, self.params[pre + "gate.weight"], self.params[pre + "experts.w1"],
-                                self.params[pre + "experts.w2"], self.router_cfgs[i],
-                                self.params.get(pre + "gate.e_score_correction_bias"), replay, record)
+            y = self._routed(i, x, replay, record)
             if self.cfg.num_shared_experts:
                 s = G.linear_swiglu(x, self.params[pre + "shared_experts.gate_up_proj.weight"])
                 y = y + G.linear(s, self.params[pre + "shared_experts.down_proj.weight"])
@@ -387,6 +384,41 @@ class Transformer(torch.nn.Module):
                 y = y + (gate * G.linear(s, self.params[pre + "shared_expert.down_proj.weight"]).float()).to(y.dtype)
             return y
         return self._lin(self._lin_swiglu(x, pre + "gate_up_proj.weight"), pre + "down_proj.weight")
+
+    def _routed(self, i: int, x: torch.Tensor, replay=None, record=None) -> torch.Tensor:
+        """Routed experts of layer i. With whole experts under TP (expert_tp = 1) each TP rank
+        routes rows [T r / tp, T (r+1) / tp) of the replicated input and returns them in a
+        zero-filled [T, H] block, so the TP all-reduce that follows completes the output (and
+        the backward of the TP copy sums the row gradients)."""
+        pre = f"layers.{i}.mlp."
+        args = (self.params[pre + "gate.weight"], self.params[pre + "experts.w1"],
+                self.params[pre + "experts.w2"], self.router_cfgs[i])
+        bias = self.params.get(pre + "gate.e_score_correction_bias")
+
+        def run(xr, rp, rec):
+            if self.ep is not None:
+                from miles_b200.parallel.ep import moe_experts_ep
+
+                return moe_experts_ep(xr, *args, self.ep, bias, rp, rec)
+            return moe_experts(xr, *args, bias, rp, rec)
+
+        if self.tp is None or self.expert_tp > 1:
+            return run(x, replay, record)
+        T, tp = x.shape[0], self.tp
+        lo, hi = T * tp.rank // tp.size, T * (tp.rank + 1) // tp.size
+        got = []
+        y = run(x[lo:hi], None if replay is None else replay[lo:hi],
+                None if record is None else got.append)
+        if record is not None:  # the full routing: every rank's rows, gathered
+            idx = got[0]
+            n = -(-T // tp.size) + 1
+            buf = torch.full((n, idx.shape[1]), -1, dtype=idx.dtype, device=idx.device)
+            buf[:hi - lo] = idx
+            parts = [torch.empty_like(buf) for _ in range(tp.size)]
+            dist.all_gather(parts, buf, group=tp.group)
+            record(torch.cat([p[:(T * (r + 1) // tp.size) - (T * r // tp.size)]
+                              for r, p in enumerate(parts)], 0))
+        return F.pad(y, (0, 0, lo, T - hi))
 
     def _layer_train(self, i, m_prev, r_prev, meta, replay):
         cfg = self.cfg

@@ -89,8 +89,6 @@ def init_distributed(args) -> ProcessContext:
                     ctx.dp_group = g
             register_tied_embedding_groups(world, pp)
             ctx.dp_rank, ctx.dp_size = rank % D, D
-        if tp > 1 and ep > 1:
-            raise ValueError("tensor and expert parallelism cannot be combined")
         if cp > 1 and (tp > 1 or ep > 1):
             raise ValueError("context parallelism is supported with data parallelism only")
         if cp > 1:
@@ -114,7 +112,30 @@ def init_distributed(args) -> ProcessContext:
                 if rank in ranks:
                     ctx.dp_group = g
             ctx.dp_rank, ctx.dp_size = rank // tp, world // tp
-        if ep > 1:
+        etp = getattr(args, "expert_tensor_parallel_size", None)
+        if ep > 1 and tp > 1 and etp == 1 and ep % tp and tp % ep:
+            raise ValueError(f"whole experts under TP need EP ({ep}) and TP ({tp}) to divide one another")
+        if ep > 1 and tp > 1 and etp != 1:
+            # TP x EP: attention heads and every expert's FFN width split over the TP group
+            # (expert-tensor parallel = TP); experts split over EP groups of the ranks with the
+            # same TP rank (consecutive data-parallel replicas); expert gradients reduce over
+            # the replicas of the same (TP rank, EP rank)
+            D = world // tp
+            if D % ep:
+                raise ValueError(f"{D} data-parallel replicas do not split into EP groups of {ep}")
+            for t in range(tp):
+                for b in range(0, D, ep):
+                    ranks = [t + tp * (b + e) for e in range(ep)]
+                    g = dist.new_group(ranks)
+                    if rank in ranks:
+                        ctx.ep_group = g
+                for e in range(ep):
+                    ranks = [t + tp * (b + e) for b in range(0, D, ep)]
+                    g = dist.new_group(ranks)
+                    if rank in ranks:
+                        ctx.expert_dp_group = g
+        elif ep > 1:
+            # EP alone, or with whole experts under TP: EP groups of consecutive ranks
             blocks, strided = _groups(world, ep)
             for ranks in blocks:
                 g = dist.new_group(ranks)
@@ -154,6 +175,7 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
                         vpp=getattr(args, "virtual_pipeline_model_parallel_size", None) or 1,
                         pp_first_layers=getattr(args, "decoder_first_pipeline_num_layers", None),
                         pp_last_layers=getattr(args, "decoder_last_pipeline_num_layers", None),
+                        etp=getattr(args, "expert_tensor_parallel_size", None),
                         tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
     if getattr(args, "sequence_parallel", False) and model.tp is not None and model.mla is None:
         model.sequence_parallel = True

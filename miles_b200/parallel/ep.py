@@ -15,11 +15,15 @@ csrc/moe_ep.cu): the dispatch kernel stores every row straight into its owner's 
 buffer and the combine kernel loads the expert outputs from the owners, with device barriers
 instead of host synchronisation. Either way the order of every row is a pure function of
 (source rank, token, slot), so results do not depend on timing, and both equal the single-GPU
-layer bit for bit.
+layer bit for bit. On CPU ranks (gloo) `moe_ep_ref` runs the same exchange in PyTorch autograd.
+
+Under TP the experts are either split over the TP ranks as well (expert-tensor parallel size =
+TP; the EP group is the ranks with the same TP rank) or whole (size 1; each TP rank routes its
+share of the replicated rows): `Transformer._routed`.
 
 Reference: Megatron MoE alltoall token dispatcher (--moe-token-dispatcher-type alltoall),
 DeepEP flex dispatcher (--moe-enable-deepep), expert index offsets for naming
-(update_weight/common.py:186-190).
+(update_weight/common.py:186-190), --expert-tensor-parallel-size (utils/arguments.py).
 """
 from __future__ import annotations
 
@@ -290,10 +294,66 @@ class _MoEEP(torch.autograd.Function):
         return dx, dwr, dw1, dw2, None, None, None, None, None, None
 
 
+class _A2A(torch.autograd.Function):
+    """Differentiable all-to-all of rows: the backward sends the gradients the reverse way."""
+
+    @staticmethod
+    def forward(ctx, x, send_splits, recv_splits, ep):
+        ctx.misc = (send_splits, recv_splits, ep)
+        return _a2a(x, send_splits, recv_splits, ep)
+
+    @staticmethod
+    def backward(ctx, g):
+        ss, rs, ep = ctx.misc
+        return _a2a(g, rs, ss, ep), None, None, None
+
+
+def moe_ep_ref(x, router_w, w1_local, w2_local, cfg: RouterCfg, ep: EPContext, bias=None,
+               replay_idx=None, record=None):
+    """PyTorch expert-parallel layer (CPU ranks, gloo): the same exchange as the kernel path
+    (rows ordered by destination rank, then token, then slot; counts, rows and local expert
+    ids all-to-all; reverse all-to-all of the expert outputs; weighted combine) in autograd
+    ops, experts in fp32. Equals `moe_ref` over the global expert set."""
+    from miles_b200.ops.moe import route_ref, swiglu_ref
+
+    T, H = x.shape
+    logits = x.float() @ router_w.float().t()
+    idx, w = route_ref(logits, cfg, bias, replay_idx)
+    if record is not None:
+        record(idx)
+    dest = torch.div(idx.long(), ep.E_local, rounding_mode="floor").view(-1)
+    # stable sort by destination keeps (token, slot) order inside each destination
+    order = torch.sort(dest, stable=True).indices
+    tok = torch.div(order, cfg.k, rounding_mode="floor")
+    send_counts = torch.bincount(dest, minlength=ep.size).to(torch.int64)
+    recv_counts = _exchange_counts(send_counts, ep)
+    ss, rs = send_counts.tolist(), recv_counts.tolist()
+    send_eid = (idx.long().view(-1) - dest * ep.E_local)[order]
+    recv_x = _A2A.apply(x[tok].float(), ss, rs, ep)
+    recv_eid = _a2a(send_eid, ss, rs, ep)
+    rd = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
+    out = torch.zeros(recv_x.shape[0], H, dtype=torch.float32, device=x.device)
+    for e in range(ep.E_local):
+        rows = (recv_eid == e).nonzero(as_tuple=True)[0]
+        if rows.numel() == 0:
+            continue
+        gu = (recv_x[rows] @ w1_local[e].float().t()).to(rd)
+        o = (swiglu_ref(gu).float() @ w2_local[e].float().t()).to(rd)
+        out = out.index_add(0, rows, o.float())
+    ret = _A2A.apply(out, rs, ss, ep)
+    wf = w.view(-1)[order]
+    y = torch.zeros(T, H, dtype=torch.float32, device=x.device).index_add(0, tok, wf[:, None] * ret)
+    return y.to(x.dtype)
+
+
 def moe_experts_ep(x, router_w, w1_local, w2_local, cfg: RouterCfg, ep: EPContext, bias=None,
                    replay_idx=None, record=None):
     """Expert-parallel MoE: w1_local [E/ep, 2I, H], w2_local [E/ep, H, I] hold this rank's
     experts; routing and the output are over the global expert set."""
+    from miles_b200.ops._lib import use_native
+
+    if not use_native(x):
+        return moe_ep_ref(x, router_w, w1_local, w2_local, cfg, ep, bias, replay_idx, record)
     fn = _MoEEPPeer if (ep.transport == "peer" and x.is_cuda) else _MoEEP
     return fn.apply(x, router_w, w1_local, w2_local, bias, cfg, ep, replay_idx, record,
                     torch.is_grad_enabled())

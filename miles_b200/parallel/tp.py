@@ -176,6 +176,17 @@ def tp_slice(hf_name: str, full: torch.Tensor, tp: TPContext | None) -> torch.Te
     return full.narrow(d, lo, hi - lo)
 
 
+def _whole_expert(model, name: str) -> bool:
+    """Routed-expert tensor (internal or HF name) that is not split over TP (expert_tp = 1)."""
+    return (getattr(model, "expert_tp", 0) == 1 and ".experts." in name
+            and "shared_experts" not in name)
+
+
+def model_tp(model, name: str):
+    """The TP context that splits parameter `name` of `model` (None: not split)."""
+    return None if _whole_expert(model, name) else model.tp
+
+
 def tp_partial_param_names(model) -> list[str]:
     """Replicated parameters whose gradient on one TP rank covers only its own slice (its heads,
     its intermediate slice, or under sequence parallelism its rows)."""
@@ -192,6 +203,8 @@ def tp_partial_param_names(model) -> list[str]:
             out.append(name)  # each rank's gradient covers its vocabulary rows
         elif name.endswith("mlp.gate.weight"):
             out.append(name)  # router logits feed a combine of partial expert outputs
+        elif model.ep is None and _whole_expert(model, name):
+            out.append(name)  # whole experts on every TP rank, each fed its own rows
     return out
 
 
@@ -224,7 +237,7 @@ def tp_replicated_ranges(model) -> list[tuple[int, int]]:
     if model.tp is None or model.tp.size == 1:
         return []
     return [(s.offset, s.offset + s.numel) for s in model.specs
-            if not s.name.endswith(_SHARDED_INTERNAL)]
+            if not s.name.endswith(_SHARDED_INTERNAL) or (model.ep is None and _whole_expert(model, s.name))]
 
 
 

@@ -135,11 +135,19 @@ class Actor:
                                 **self._norm_scope())
 
     def _norm_scope(self) -> dict:
-        """Gradient-norm group of model-parallel ranks and the flat ranges this rank leaves out."""
+        """Gradient-norm group of model-parallel ranks and the flat ranges this rank leaves out;
+        under expert parallelism the experts' part is summed over the groups that split them."""
         m = self.model
+        out = {}
+        if m.ep is not None:
+            groups = ([m.tp.group] if m.tp is not None and m.expert_tp > 1 else []) + [m.ep.group]
+            out["expert_norm"] = (m.dense_numel, groups)
         if m.tp is not None:
-            return {"norm_group": m.tp.group,
-                    "norm_exclude": tp_replicated_ranges(m) if m.tp.rank != 0 else []}
+            out.update({"norm_group": m.tp.group,
+                        "norm_exclude": tp_replicated_ranges(m) if m.tp.rank != 0 else []})
+            return out
+        if m.ep is not None:
+            return out
         if m.pp is not None:
             ex = []
             if m.cfg.tie_embeddings and m.pp.is_last and not m.pp.is_first:

@@ -41,13 +41,17 @@ class FlatAdam:
     def __init__(self, params_flat: torch.Tensor, grads_flat: torch.Tensor, lr: float = 1e-6,
                  betas=(0.9, 0.98), eps: float = 1e-8, weight_decay: float = 0.0,
                  clip_grad: float = 1.0, placement: str = "auto", chunk: int = 1 << 28,
-                 seed: int = 1234, dp_group=None, norm_group=None, norm_exclude=None):
+                 seed: int = 1234, dp_group=None, norm_group=None, norm_exclude=None,
+                 expert_norm=None):
         """norm_group / norm_exclude: under model parallelism (TP, PP) every rank runs its own
         optimizer over its part of the model; the gradient norm sums the squares over
         `norm_group`, leaving out this rank's flat ranges `norm_exclude` (parameters another
         rank of the group already counts: TP-replicated ones on TP ranks > 0, the last pipeline
-        stage's copy of tied embeddings)."""
+        stage's copy of tied embeddings). expert_norm = (offset, groups): under expert
+        parallelism the flat tail from `offset` (this rank's experts) is summed over each of
+        `groups` in turn (TP when experts are TP-split, then EP) instead of `norm_group`."""
         self.p = params_flat
+        self.expert_norm = expert_norm
         self.norm_group = norm_group
         self.norm_world = dist.get_world_size(norm_group) if norm_group is not None else 1
         self.norm_exclude = list(norm_exclude or [])
@@ -135,10 +139,22 @@ class FlatAdam:
                 if a < b:
                     sqnorm_(self.g[a:b], sq_x)
             self.sq.sub_(sq_x)
+        sq_e = None
+        if self.expert_norm is not None:
+            off, _ = self.expert_norm
+            sq_e = torch.zeros_like(self.sq)
+            if max(off, lo) < hi:
+                sqnorm_(self.g[max(off, lo):hi], sq_e)
+            self.sq.sub_(sq_e)
         if self.world > 1:
             dist.all_reduce(self.sq, group=self.group)
         if self.norm_world > 1:
             dist.all_reduce(self.sq, group=self.norm_group)
+        if sq_e is not None:
+            for grp in self.expert_norm[1]:
+                if dist.get_world_size(grp) > 1:
+                    dist.all_reduce(sq_e, group=grp)
+            self.sq.add_(sq_e)
         nonfinite_(self.sq, self.skip)
         common = dict(lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.wd,
                       step=self.step_id, sqnorm=self.sq, max_norm=self.clip,

@@ -69,7 +69,9 @@ def add_train_args(p):
                    help="layers on the last pipeline stage")
     g.add_argument("--context-parallel-size", type=int, default=1)
     g.add_argument("--expert-model-parallel-size", type=int, default=1)
-    g.add_argument("--expert-tensor-parallel-size", type=int, default=1)
+    g.add_argument("--expert-tensor-parallel-size", type=int, default=None,
+                   help="TP ranks that split each routed expert: 1 (whole experts, each TP rank "
+                        "routes its share of the tokens) or the TP size (default)")
     g.add_argument("--sequence-parallel", action="store_true", default=False)
     g.add_argument("--vocab-parallel-logprob", action="store_true", default=False,
                    help="under TP, split the LM-head logits of the trainer's log-probs over the TP ranks")

@@ -1,0 +1,106 @@
+"""Expert parallelism on CPU (gloo): EP alone, TP x EP with TP-split experts, TP x EP and TP
+alone with whole experts (expert-tensor-parallel size 1). Each layout's groups come from
+`init_distributed`; one actor step over data-parallel shards of a batch, then `save_hf`, gives
+the same HF tensors as one process stepping on the whole batch; the gradient norm is the
+global one on every rank."""
+import argparse
+import dataclasses
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
+
+
+def _cfg():
+    from miles_b200.models.config import preset
+
+    return dataclasses.replace(preset("tiny-moe"), num_experts=8)
+
+
+def _items(cfg, n=8):
+    from miles_b200.trainer.actor import TrainItem
+
+    rng = np.random.default_rng(3)
+    out = []
+    for _ in range(n):
+        P, R = int(rng.integers(5, 14)), int(rng.integers(3, 9))
+        toks = rng.integers(0, cfg.vocab_size, P + R).tolist()
+        out.append(TrainItem(toks, P, advantage=float(rng.normal()),
+                             rollout_logp=(-rng.random(R)).tolist()))
+    return out
+
+
+def _actor_cfg():
+    from miles_b200.trainer.actor import ActorConfig
+
+    return ActorConfig(lr=1e-3, max_tokens_per_gpu=48, grad_dtype=torch.float32,
+                       optimizer_placement="device")
+
+
+def _run(rank, world, port, layout, ckpt, out):
+    os.environ.update(MILES_B200_FORCE_CPU="1", RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from miles_b200.checkpoint.hf import load_hf, save_hf
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.orchestration.setup import init_distributed
+    from miles_b200.trainer.actor import Actor
+
+    tp, ep, etp = layout
+    args = argparse.Namespace(distributed_timeout_minutes=5, tensor_model_parallel_size=tp,
+                              expert_model_parallel_size=ep, context_parallel_size=1,
+                              pipeline_model_parallel_size=1, expert_tensor_parallel_size=etp)
+    ctx = init_distributed(args)
+    cfg = _cfg()
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=7, tp_group=ctx.tp_group,
+                    ep_group=ctx.ep_group, etp=etp)
+    load_hf(m, ckpt)
+    a = Actor(m, _actor_cfg(), dp_group=ctx.dp_group if ctx.dp_size > 1 else None)
+    a.expert_dp_group = ctx.expert_dp_group
+    items = _items(cfg)
+    n_tok = sum(it.resp_len for it in items)
+    mine = items[ctx.dp_rank::ctx.dp_size]
+    met = a.train_step(mine, global_num_samples=len(items), global_num_tokens=n_tok)
+    if rank < (tp * ep if (etp or tp) > 1 else max(tp, ep)):
+        save_hf(m, out)
+    torch.save(met["grad_norm"], f"{out}.gn{rank}")
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("layout,world,port", [
+    ((1, 2, None), 2, 29681),     # EP2
+    ((2, 2, None), 4, 29682),     # TP2 x EP2, experts split over TP
+    ((2, 2, 1), 4, 29683),        # TP2 x EP2, whole experts (EP group = TP group)
+    ((2, 1, 1), 2, 29684),        # TP2, whole experts on both ranks
+])
+def test_ep_layouts_match_single(tmp_path, layout, world, port):
+    from safetensors import safe_open
+
+    from miles_b200.checkpoint.hf import save_hf, to_hf_tensors
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.trainer.actor import Actor
+
+    cfg = _cfg()
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=7)
+    ckpt = str(tmp_path / "hf")
+    save_hf(m, ckpt)
+    a = Actor(m, _actor_cfg())
+    met = a.train_step(_items(cfg))
+    ref = {k: v.detach().clone() for k, v in to_hf_tensors(m)}
+    out = str(tmp_path / "out")
+    mp.spawn(_run, args=(world, port, layout, ckpt, out), nprocs=world, join=True)
+    import json
+
+    wm = json.load(open(os.path.join(out, "model.safetensors.index.json")))["weight_map"]
+    assert set(wm) == set(ref), set(ref) ^ set(wm)
+    for name, fn in wm.items():
+        with safe_open(os.path.join(out, fn), "pt") as f:
+            got = f.get_tensor(name)
+        assert torch.allclose(got, ref[name], atol=2e-5), (name, (got - ref[name]).abs().max())
+    for r in range(world):
+        gn = torch.load(f"{out}.gn{r}")
+        assert abs(gn - met["grad_norm"]) < 1e-4 * max(1.0, met["grad_norm"]), (r, gn, met["grad_norm"])

@@ -103,7 +103,15 @@ def train(args):
             if args.save_hf:
                 from miles_b200.checkpoint.hf import save_hf
 
-                if ctx.dp_rank == 0:  # the TP group of replica 0 (save_hf gathers over it)
+                # the TP group of replica 0 (save_hf gathers over it); under EP the ranks that
+                # hold one copy of every expert too (the first tp * ep ranks with TP-split
+                # experts, the first max(tp, ep) with whole experts)
+                if model.ep is None:
+                    saver = ctx.dp_rank == 0
+                else:
+                    tp_n, ep_n = model.tp_size, model.ep.size
+                    saver = ctx.rank < (tp_n * ep_n if model.expert_tp > 1 else max(tp_n, ep_n))
+                if saver:
                     save_hf(model, args.save_hf.format(rollout_id=rollout_id))
         # colocated refit: the engine reads the trainer's parameter buffer in place
         m["rollout/weight_version"] = model.weight_version
