@@ -213,10 +213,12 @@ class Transformer(torch.nn.Module):
             self.cp = CPContext(cp_group)
             if self.cp.size == 1:
                 self.cp = None
-            elif self.tp is not None:
-                raise ValueError("context parallelism combined with tensor parallelism is not supported")
-            elif cfg.num_kv_heads % self.cp.size:
-                raise ValueError(f"{cfg.num_kv_heads} KV heads do not split over CP {self.cp.size}")
+            elif self.tp is not None and (cfg.uses_torch_attention or cfg.linear_attn_interval
+                                          or cfg.kv_lora_rank):
+                raise ValueError("TP x CP is implemented for the fused-qkv attention families")
+            elif (cfg.num_kv_heads // self.tp_size) % self.cp.size:
+                raise ValueError(f"{cfg.num_kv_heads // self.tp_size} KV heads per TP rank do not "
+                                 f"split over CP {self.cp.size}")
         self.nq = cfg.num_heads // self.tp_size      # this rank's query heads
         self.nkv = cfg.num_kv_heads // self.tp_size  # this rank's KV heads
         self.ep = None
@@ -541,12 +543,14 @@ class Transformer(torch.nn.Module):
             x2, r = add_rms_norm(self._sw(i, "post_self_attn_layernorm", a), r,
                                  self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
             return self._mlp(i, x2, replay=replay), r
-        qkv = self._lin(x, pre + "qkv_proj.weight")
+        # under TP the projections hold this TP rank's heads; the CP exchange splits those
+        qkv = self._lin(copy_to_tp(x, self.tp), pre + "qkv_proj.weight")
         q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
                                self.params.get(pre + "k_norm.weight"), pos,
                                self.rope_cos, self.rope_sin, self.nq, self.nkv, cfg.rms_eps, cfg.qk_norm)
         o = varlen_attention(tokens_to_heads(q, cp), tokens_to_heads(k, cp), tokens_to_heads(v, cp), meta)
-        a = self._lin(heads_to_tokens(o, cp).reshape(x.shape[0], -1), pre + "o_proj.weight")
+        a = reduce_from_tp(self._lin(heads_to_tokens(o, cp).reshape(x.shape[0], -1), pre + "o_proj.weight"),
+                           self.tp)
         x2, r = add_rms_norm(self._sw(i, "post_self_attn_layernorm", a), r,
                                  self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
         return self._mlp(i, x2, replay=replay), r
@@ -581,7 +585,7 @@ class Transformer(torch.nn.Module):
 
         W = self.lm_head_weight()
         h = self.forward_train(tokens, meta, replay_experts=replay_experts)
-        if self.tp is not None and self.vocab_parallel_logprob:
+        if self.tp is not None and self.vocab_parallel_logprob and self.cp is None:
             from miles_b200.parallel.tp import vocab_parallel_logprob
 
             if self.cfg.tie_embeddings:
@@ -621,7 +625,7 @@ class Transformer(torch.nn.Module):
         model chunk to run: the embedding belongs to chunk 0 of the first rank, the final norm to
         the last chunk of the last rank."""
         cfg = self.cfg
-        if self.tp is not None and self.sequence_parallel and record_experts is None:
+        if self.tp is not None and self.sequence_parallel and record_experts is None and self.cp is None:
             return self._forward_train_sp(tokens, meta, replay_experts)
         if self.cp is not None:
             if record_experts is not None:

@@ -89,9 +89,20 @@ def init_distributed(args) -> ProcessContext:
                     ctx.dp_group = g
             register_tied_embedding_groups(world, pp)
             ctx.dp_rank, ctx.dp_size = rank % D, D
-        if cp > 1 and (tp > 1 or ep > 1):
-            raise ValueError("context parallelism is supported with data parallelism only")
-        if cp > 1:
+        if cp > 1 and ep > 1:
+            raise ValueError("context parallelism combined with expert parallelism is not supported")
+        if cp > 1 and tp > 1:
+            # TP x CP (rank = replica * tp * cp + c * tp + t): a CP group is the ranks with the
+            # same TP rank in one replica; gradients reduce over all ranks of the same TP rank
+            # (the TP block below), data is sharded over replicas of tp * cp ranks
+            blk = tp * cp
+            for b in range(0, world, blk):
+                for t in range(tp):
+                    ranks = [b + c * tp + t for c in range(cp)]
+                    g = dist.new_group(ranks)
+                    if rank in ranks:
+                        ctx.cp_group = g
+        elif cp > 1:
             # CP groups are consecutive ranks; gradients reduce over every rank (DP x CP),
             # data is sharded over DP replicas only
             blocks, _ = _groups(world, cp)
@@ -112,6 +123,8 @@ def init_distributed(args) -> ProcessContext:
                 if rank in ranks:
                     ctx.dp_group = g
             ctx.dp_rank, ctx.dp_size = rank // tp, world // tp
+            if cp > 1:
+                ctx.dp_rank, ctx.dp_size = rank // (tp * cp), world // (tp * cp)
         etp = getattr(args, "expert_tensor_parallel_size", None)
         if ep > 1 and tp > 1 and etp == 1 and ep % tp and tp % ep:
             raise ValueError(f"whole experts under TP need EP ({ep}) and TP ({tp}) to divide one another")

@@ -197,9 +197,10 @@ def tp_partial_param_names(model) -> list[str]:
     for name in model.params:
         if name.endswith(("self_attn.q_norm.weight", "self_attn.k_norm.weight")):
             out.append(name)
-        elif model.sequence_parallel and (name.endswith(sp_norms) or name == "norm.weight"):
+        elif (model.sequence_parallel and model.cp is None
+              and (name.endswith(sp_norms) or name == "norm.weight")):
             out.append(name)
-        elif model.vocab_parallel_logprob and name == "lm_head.weight":
+        elif model.vocab_parallel_logprob and model.cp is None and name == "lm_head.weight":
             out.append(name)  # each rank's gradient covers its vocabulary rows
         elif name.endswith("mlp.gate.weight"):
             out.append(name)  # router logits feed a combine of partial expert outputs

@@ -1,5 +1,5 @@
-"""Expert parallelism on CPU (gloo): EP alone, TP x EP with TP-split experts, TP x EP and TP
-alone with whole experts (expert-tensor-parallel size 1). Each layout's groups come from
+"""Model-parallel layouts on CPU (gloo): EP alone, TP x EP with TP-split experts, TP x EP and TP
+alone with whole experts (expert-tensor-parallel size 1), TP x CP. Each layout's groups come from
 `init_distributed`; one actor step over data-parallel shards of a batch, then `save_hf`, gives
 the same HF tensors as one process stepping on the whole batch; the gradient norm is the
 global one on every rank."""
@@ -19,7 +19,8 @@ os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
 def _cfg():
     from miles_b200.models.config import preset
 
-    return dataclasses.replace(preset("tiny-moe"), num_experts=8)
+    # 4 KV heads: 2 per TP rank, split again over 2 CP ranks
+    return dataclasses.replace(preset("tiny-moe"), num_experts=8, num_heads=8, num_kv_heads=4)
 
 
 def _items(cfg, n=8):
@@ -50,32 +51,37 @@ def _run(rank, world, port, layout, ckpt, out):
     from miles_b200.orchestration.setup import init_distributed
     from miles_b200.trainer.actor import Actor
 
-    tp, ep, etp = layout
+    tp, ep, etp, cp = layout
     args = argparse.Namespace(distributed_timeout_minutes=5, tensor_model_parallel_size=tp,
-                              expert_model_parallel_size=ep, context_parallel_size=1,
+                              expert_model_parallel_size=ep, context_parallel_size=cp,
                               pipeline_model_parallel_size=1, expert_tensor_parallel_size=etp)
     ctx = init_distributed(args)
     cfg = _cfg()
     m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=7, tp_group=ctx.tp_group,
-                    ep_group=ctx.ep_group, etp=etp)
+                    ep_group=ctx.ep_group, cp_group=ctx.cp_group, etp=etp)
     load_hf(m, ckpt)
-    a = Actor(m, _actor_cfg(), dp_group=ctx.dp_group if ctx.dp_size > 1 else None)
+    a = Actor(m, _actor_cfg(), dp_group=ctx.dp_group)  # as build_actor: gradients over DP x CP
     a.expert_dp_group = ctx.expert_dp_group
     items = _items(cfg)
     n_tok = sum(it.resp_len for it in items)
     mine = items[ctx.dp_rank::ctx.dp_size]
     met = a.train_step(mine, global_num_samples=len(items), global_num_tokens=n_tok)
-    if rank < (tp * ep if (etp or tp) > 1 else max(tp, ep)):
+    if ctx.cp_group is not None:
+        saver = ctx.dp_rank == 0 and dist.get_rank(ctx.cp_group) == 0
+    else:
+        saver = rank < (tp * ep if (etp or tp) > 1 else max(tp, ep))
+    if saver:
         save_hf(m, out)
     torch.save(met["grad_norm"], f"{out}.gn{rank}")
     dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("layout,world,port", [
-    ((1, 2, None), 2, 29681),     # EP2
-    ((2, 2, None), 4, 29682),     # TP2 x EP2, experts split over TP
-    ((2, 2, 1), 4, 29683),        # TP2 x EP2, whole experts (EP group = TP group)
-    ((2, 1, 1), 2, 29684),        # TP2, whole experts on both ranks
+    ((1, 2, None, 1), 2, 29681),     # EP2
+    ((2, 2, None, 1), 4, 29682),     # TP2 x EP2, experts split over TP
+    ((2, 2, 1, 1), 4, 29683),        # TP2 x EP2, whole experts (EP group = TP group)
+    ((2, 1, 1, 1), 2, 29684),        # TP2, whole experts on both ranks
+    ((2, 1, None, 2), 4, 29685),     # TP2 x CP2
 ])
 def test_ep_layouts_match_single(tmp_path, layout, world, port):
     from safetensors import safe_open
@@ -97,10 +103,13 @@ def test_ep_layouts_match_single(tmp_path, layout, world, port):
 
     wm = json.load(open(os.path.join(out, "model.safetensors.index.json")))["weight_map"]
     assert set(wm) == set(ref), set(ref) ^ set(wm)
+    bad = []
     for name, fn in wm.items():
         with safe_open(os.path.join(out, fn), "pt") as f:
             got = f.get_tensor(name)
-        assert torch.allclose(got, ref[name], atol=2e-5), (name, (got - ref[name]).abs().max())
+        if not torch.allclose(got, ref[name], atol=2e-5):
+            bad.append((name, float((got - ref[name]).abs().max())))
+    assert not bad, bad
     for r in range(world):
         gn = torch.load(f"{out}.gn{r}")
         assert abs(gn - met["grad_norm"]) < 1e-4 * max(1.0, met["grad_norm"]), (r, gn, met["grad_norm"])
