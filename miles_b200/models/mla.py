@@ -225,24 +225,52 @@ class MLA:
             cache.k[i].index_copy_(0, slots, torch.cat(row, -1).unsqueeze(1).to(cache.k[i].dtype))
         k, v = self._expand(i, c, k_pe)
         q = torch.cat([q_nope, q_pe], -1)
-        o = torch.empty(x.shape[0], self.nh, cfg.v_head_dim, dtype=x.dtype, device=x.device)
+        o = self._sdpa(q, k, v, meta.cu_list, (qI, kI, wI) if dsa else None)
+        return self._out(i, o.reshape(x.shape[0], -1), pending)
+
+    def _sdpa(self, q, k, v, cu, index=None):
+        """Causal attention per sequence of the packed rows (q, k, v [T, heads, D]); with the
+        DSA indexer inputs (qI, kI, wI over the same rows) only each query's top-k keys."""
+        o = torch.empty(q.shape[0], q.shape[1], v.shape[-1], dtype=q.dtype, device=q.device)
         outs = []
-        cu = meta.cu_list
         for b in range(len(cu) - 1):
             s, e = cu[b], cu[b + 1]
             if e == s:
                 continue
             qs, ks, vs = (t[s:e].transpose(0, 1).unsqueeze(0) for t in (q, k, v))
-            if dsa:
+            if index is not None:
+                qI, kI, wI = index
                 L = e - s
-                causal = torch.ones(L, L, dtype=torch.bool, device=x.device).tril()
+                causal = torch.ones(L, L, dtype=torch.bool, device=q.device).tril()
                 keep = self._topk_keep(self._index_scores(qI[s:e], wI[s:e], kI[s:e]), causal)
                 o_b = F.scaled_dot_product_attention(qs, ks, vs, attn_mask=keep, scale=self.scale)
             else:
                 o_b = F.scaled_dot_product_attention(qs, ks, vs, is_causal=True, scale=self.scale)
             outs.append(o_b[0].transpose(0, 1))
-        o = torch.cat(outs, 0) if outs else o
-        return self._out(i, o.reshape(x.shape[0], -1), pending)
+        return torch.cat(outs, 0) if outs else o
+
+    def attn_cp(self, i: int, x: torch.Tensor, meta, pos: torch.Tensor, cp) -> torch.Tensor:
+        """Context-parallel training attention: x holds this CP rank's rows of the padded batch.
+        The per-head q / k / v (after the latent up-projection) go through the head all-to-all
+        (all rows, 1 / CP of the heads per rank); the DSA indexer's inputs, computed without
+        gradient, are all-gathered so that every rank selects the same top-k keys over the
+        whole sequence (the reference's allgather-CP keeps the indexer global the same way)."""
+        from miles_b200.parallel.cp import all_gather_rows, heads_to_tokens, tokens_to_heads
+
+        cfg = self.cfg
+        q_nope, q_pe, qa = self._q(i, x, pos, want_qa=True)
+        c, k_pe = self._latent(i, x, pos)
+        index = None
+        if cfg.index_topk > 0:
+            with torch.no_grad():
+                index = tuple(all_gather_rows(t, cp) for t in (
+                    self._index_q(i, qa.detach(), pos), self._index_k(i, x.detach(), pos),
+                    self._index_weights(i, x.detach())))
+        k, v = self._expand(i, c, k_pe)
+        q = torch.cat([q_nope, q_pe], -1)
+        oh = self._sdpa(tokens_to_heads(q, cp), tokens_to_heads(k, cp), tokens_to_heads(v, cp),
+                        meta.cu_list, index)
+        return self._out(i, heads_to_tokens(oh, cp).reshape(x.shape[0], -1), False)
 
     # ------------------------------------------------------------------ decode (absorbed)
     def decode(self, i: int, x: torch.Tensor, positions: torch.Tensor, cache, page_table: torch.Tensor,

@@ -532,6 +532,11 @@ class Transformer(torch.nn.Module):
                                  self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
             return self._mlp(i, x2, replay=replay), r
         pre = f"layers.{i}.self_attn."
+        if self.mla is not None:  # multi-head latent attention (+ DSA): models/mla.py
+            a = self.mla.attn_cp(i, x, meta, pos, cp)
+            x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"],
+                                 cfg.rms_eps)
+            return self._mlp(i, x2, replay=replay), r
         if self.gattn is not None:  # gated attention (Qwen3-Next): same head exchange
             q, k, v, gate = self.gattn._qkv(i, x, pos)
             qh, kh, vh = tokens_to_heads(q, cp), tokens_to_heads(k, cp), tokens_to_heads(v, cp)
@@ -560,8 +565,6 @@ class Transformer(torch.nn.Module):
         from miles_b200.ops.attention import VarlenMeta
 
         cfg, cp = self.cfg, self.cp
-        if self.mla is not None:
-            raise NotImplementedError("context parallelism is not implemented for MLA models")
         T = tokens.shape[0]
         Tp, lo, hi = cp.rows(T)
         if Tp > T:

@@ -92,6 +92,14 @@ def tokens_to_heads(x, cp):
     return _tokens_to_heads(x, cp)
 
 
+@torch.no_grad()
+def all_gather_rows(x: torch.Tensor, cp) -> torch.Tensor:
+    """Every CP rank's rows of x, concatenated in rank order (no gradient)."""
+    parts = [torch.empty_like(x) for _ in range(cp.size)]
+    dist.all_gather(parts, x.contiguous(), group=cp.group)
+    return torch.cat(parts, 0)
+
+
 def heads_to_tokens(x, cp):
     if torch.is_grad_enabled() and x.requires_grad:
         return _HeadsToTokens.apply(x, cp)

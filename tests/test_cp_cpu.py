@@ -1,7 +1,7 @@
 """Context parallelism on CPU (gloo, 2 ranks): the per-token log-probs of a CP2 forward equal
 the single-rank ones, and the CP ranks' gradients sum to the single-rank gradients (softmax
-attention through the head all-to-all; Gated DeltaNet layers through the state hand-over
-between ranks); then one train.py GRPO step with --context-parallel-size 2."""
+attention, MLA and DSA (global top-k selection) through the head all-to-all; Gated DeltaNet
+layers through the state hand-over between ranks); then one train.py GRPO step with --context-parallel-size 2."""
 import os
 import subprocess
 import sys
@@ -50,7 +50,8 @@ def _run(rank, world, port, name, out):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name,port", [("tiny", 29681), ("tiny-moe", 29682), ("tiny-gdn", 29683)])
+@pytest.mark.parametrize("name,port", [("tiny", 29681), ("tiny-moe", 29682), ("tiny-gdn", 29683),
+                                       ("tiny-mla", 29686), ("tiny-dsa", 29687)])
 def test_cp2_matches_single(tmp_path, name, port):
     from miles_b200.models.config import preset
     from miles_b200.models.transformer import Transformer

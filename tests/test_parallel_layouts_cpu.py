@@ -77,11 +77,11 @@ def _run(rank, world, port, layout, ckpt, out):
 
 
 @pytest.mark.parametrize("layout,world,port", [
-    ((1, 2, None, 1), 2, 29681),     # EP2
-    ((2, 2, None, 1), 4, 29682),     # TP2 x EP2, experts split over TP
-    ((2, 2, 1, 1), 4, 29683),        # TP2 x EP2, whole experts (EP group = TP group)
-    ((2, 1, 1, 1), 2, 29684),        # TP2, whole experts on both ranks
-    ((2, 1, None, 2), 4, 29685),     # TP2 x CP2
+    ((1, 2, None, 1), 2, 29691),     # EP2
+    ((2, 2, None, 1), 4, 29692),     # TP2 x EP2, experts split over TP
+    ((2, 2, 1, 1), 4, 29693),        # TP2 x EP2, whole experts (EP group = TP group)
+    ((2, 1, 1, 1), 2, 29694),        # TP2, whole experts on both ranks
+    ((2, 1, None, 2), 4, 29695),     # TP2 x CP2
 ])
 def test_ep_layouts_match_single(tmp_path, layout, world, port):
     from safetensors import safe_open
