@@ -249,6 +249,50 @@ class MLA:
             outs.append(o_b[0].transpose(0, 1))
         return torch.cat(outs, 0) if outs else o
 
+    def attn_sp(self, i: int, x: torch.Tensor, meta) -> torch.Tensor:
+        """Sequence-parallel training attention: x holds this TP rank's rows, the result is
+        this rank's rows of the o_proj output (reduce-scattered). The replicated down
+        projections run on the local rows and the low-rank latents (q_a output, compressed KV
+        and the shared rotary key: q_lora_rank + kv_lora_rank + qk_rope_head_dim wide) are
+        all-gathered instead of the hidden state; the up projections then run on all rows for
+        this rank's heads. The gather's backward reduce-scatters the latent gradients."""
+        from miles_b200.parallel.tp import sp_gather
+
+        cfg, m, tp = self.cfg, self.m, self.m.tp
+        p = f"layers.{i}.self_attn."
+        pos = meta.positions
+        R = x.shape[0]
+        T = R * tp.size
+        lo = tp.rank * R
+        dn, dr = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim
+        qa = None
+        if cfg.q_lora_rank:
+            qa = sp_gather(rms_norm(m._lin(x, p + "q_a_proj.weight"), m.params[p + "q_a_layernorm.weight"],
+                                    cfg.rms_eps), tp)
+            q = m._lin(qa, p + "q_b_proj.weight")
+        else:
+            q = m._lin(sp_gather(x, tp), p + "q_proj.weight")
+        q_nope, q_pe = q.view(T, self.nh, dn + dr).split([dn, dr], -1)
+        q = torch.cat([q_nope, _rope(q_pe, pos, self.cos, self.sin, cfg.rope_interleave)], -1)
+        kva = m._lin(x, p + "kv_a_proj_with_mqa.weight")
+        c, k_pe = kva.split([cfg.kv_lora_rank, dr], -1)
+        c = rms_norm(c.contiguous(), m.params[p + "kv_a_layernorm.weight"], cfg.rms_eps)
+        lat = sp_gather(torch.cat([c, k_pe], -1), tp)
+        c, k_pe = lat.split([cfg.kv_lora_rank, dr], -1)
+        k_pe = _rope(k_pe, pos, self.cos, self.sin, cfg.rope_interleave)
+        kv = m._lin(c.contiguous(), p + "kv_b_proj.weight").view(T, self.nh, dn + cfg.v_head_dim)
+        k_nope, v = kv.split([dn, cfg.v_head_dim], -1)
+        k = torch.cat([k_nope, k_pe[:, None, :].expand(-1, self.nh, -1)], -1)
+        index = None
+        if cfg.index_topk > 0:
+            with torch.no_grad():
+                pl = pos[lo:lo + R]
+                index = (self._index_q(i, qa.detach(), pos),
+                         sp_gather(self._index_k(i, x.detach(), pl), tp),
+                         sp_gather(self._index_weights(i, x.detach()), tp))
+        o = self._sdpa(q, k, v.contiguous(), meta.cu_list, index)
+        return m._row_rs(o.reshape(T, -1), p + "o_proj.weight")
+
     def attn_cp(self, i: int, x: torch.Tensor, meta, pos: torch.Tensor, cp) -> torch.Tensor:
         """Context-parallel training attention: x holds this CP rank's rows of the padded batch.
         The per-head q / k / v (after the latent up-projection) go through the head all-to-all

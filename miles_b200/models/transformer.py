@@ -471,13 +471,16 @@ class Transformer(torch.nn.Module):
         else:
             x, r = add_rms_norm(m_prev, r_prev, ln1, cfg.rms_eps)
         pre = f"layers.{i}.self_attn."
-        xf = sp_gather(x, tp)
-        qkv = self._lin(xf, pre + "qkv_proj.weight")
-        q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
-                               self.params.get(pre + "k_norm.weight"), meta.positions,
-                               self.rope_cos, self.rope_sin, self.nq, self.nkv, cfg.rms_eps, cfg.qk_norm)
-        o = varlen_attention(q, k, v, meta)
-        a = self._row_rs(o.reshape(xf.shape[0], -1), pre + "o_proj.weight")
+        if self.mla is not None:  # latents gathered instead of the hidden rows (models/mla.py)
+            a = self.mla.attn_sp(i, x, meta)
+        else:
+            xf = sp_gather(x, tp)
+            qkv = self._lin(xf, pre + "qkv_proj.weight")
+            q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
+                                   self.params.get(pre + "k_norm.weight"), meta.positions,
+                                   self.rope_cos, self.rope_sin, self.nq, self.nkv, cfg.rms_eps, cfg.qk_norm)
+            o = varlen_attention(q, k, v, meta)
+            a = self._row_rs(o.reshape(xf.shape[0], -1), pre + "o_proj.weight")
         x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
         x2f = sp_gather(x2, tp)
         if i in self.router_cfgs:
@@ -496,8 +499,6 @@ class Transformer(torch.nn.Module):
         from miles_b200.ops.attention import VarlenMeta
 
         cfg, tp = self.cfg, self.tp
-        if self.mla is not None:
-            raise NotImplementedError("sequence parallelism is not implemented for MLA models")
         T = tokens.shape[0]
         pad = (-T) % tp.size
         if pad:

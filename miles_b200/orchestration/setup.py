@@ -190,7 +190,7 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
                         pp_last_layers=getattr(args, "decoder_last_pipeline_num_layers", None),
                         etp=getattr(args, "expert_tensor_parallel_size", None),
                         tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
-    if getattr(args, "sequence_parallel", False) and model.tp is not None and model.mla is None:
+    if getattr(args, "sequence_parallel", False) and model.tp is not None:
         model.sequence_parallel = True
     if getattr(args, "vocab_parallel_logprob", False) and model.tp is not None:
         model.vocab_parallel_logprob = True

@@ -193,7 +193,9 @@ def tp_partial_param_names(model) -> list[str]:
     if model.tp is None or model.tp.size == 1:
         return []
     out = []
-    sp_norms = ("input_layernorm.weight", "post_attention_layernorm.weight")
+    # under SP these see only this rank's rows: the norms, and MLA's replicated down projections
+    sp_norms = ("input_layernorm.weight", "post_attention_layernorm.weight", "q_a_proj.weight",
+                "q_a_layernorm.weight", "kv_a_proj_with_mqa.weight", "kv_a_layernorm.weight")
     for name in model.params:
         if name.endswith(("self_attn.q_norm.weight", "self_attn.k_norm.weight")):
             out.append(name)

@@ -48,23 +48,22 @@ def _run(rank, world, port, preset_name, ckpt, out_dir):
         grads[name] = gr
     # sequence parallel: same forward, same gradients (37 rows: exercises the padding)
     sp = {}
-    if cfg.kv_lora_rank == 0:
-        for p in m.params.values():
-            p.grad = None
-        m.sequence_parallel = True
-        hs = m.forward_train(toks, meta)
-        hs.pow(2).mean().backward()
-        sp["h"] = hs.detach()
-        partial_sp = set(tp_partial_param_names(m))
-        sp["grads"] = {}
-        for name, p in m.params.items():
-            if p.grad is None:
-                continue
-            gr = p.grad.clone()
-            if name in partial_sp:
-                dist.all_reduce(gr)
-            sp["grads"][name] = gr
-        m.sequence_parallel = False
+    for p in m.params.values():
+        p.grad = None
+    m.sequence_parallel = True
+    hs = m.forward_train(toks, meta)
+    hs.pow(2).mean().backward()
+    sp["h"] = hs.detach()
+    partial_sp = set(tp_partial_param_names(m))
+    sp["grads"] = {}
+    for name, p in m.params.items():
+        if p.grad is None:
+            continue
+        gr = p.grad.clone()
+        if name in partial_sp:
+            dist.all_reduce(gr)
+        sp["grads"][name] = gr
+    m.sequence_parallel = False
     # engine decode (prefill + 4 greedy steps)
     from miles_b200.engine.engine import GenRequest, RolloutEngine
 
@@ -122,7 +121,8 @@ def _rank0_slice(name, full, cfg, t):
     return full
 
 
-@pytest.mark.parametrize("preset_name,port", [("tiny", 29671), ("tiny-moe", 29672), ("tiny-mla", 29673)])
+@pytest.mark.parametrize("preset_name,port", [("tiny", 29671), ("tiny-moe", 29672), ("tiny-mla", 29673),
+                                              ("tiny-dsa", 29674)])
 def test_tp2_matches_tp1(tmp_path, preset_name, port):
     from safetensors.torch import load_file
 
