@@ -21,7 +21,7 @@ from safetensors.torch import save_file
 
 from miles_b200.models.config import ModelConfig
 from miles_b200.models.transformer import Transformer
-from miles_b200.parallel.tp import model_tp, tp_gather, tp_slice
+from miles_b200.parallel.tp import model_tp, tp_gather_for, tp_slice_for
 
 
 def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
@@ -48,11 +48,11 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
                     # Qwen3.5 stores the projections separately: [q; k; v], z, b, a
                     w = P[n].data
                     if n.endswith("qkvz.weight"):
-                        vd = cfg.linear_num_value_heads * cfg.linear_value_head_dim
+                        vd = model.gdn.nv * cfg.linear_value_head_dim  # this TP rank's heads
                         yield pre + L + "linear_attn.in_proj_qkv.weight", w[: w.shape[0] - vd]
                         yield pre + L + "linear_attn.in_proj_z.weight", w[w.shape[0] - vd:]
                     else:
-                        nv = cfg.linear_num_value_heads
+                        nv = model.gdn.nv
                         yield pre + L + "linear_attn.in_proj_b.weight", w[:nv]
                         yield pre + L + "linear_attn.in_proj_a.weight", w[nv:]
                     continue
@@ -266,7 +266,7 @@ def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> No
         ep_first = 0 in dist.get_process_group_ranks(ep.group)  # the EP group rank 0 is in
     for name, t in to_hf_tensors(model):
         tpc = model_tp(model, name)
-        t = tp_gather(name, t.detach(), tpc)
+        t = tp_gather_for(model, name, t.detach())
         if name in skip:
             continue
         if ep is not None and ".mlp.experts." in name:
@@ -365,4 +365,4 @@ def _load(model: Transformer, wmap, get, path: str) -> None:
                 continue
             raise KeyError(f"{name} missing from {path}")
         src = from_hf_layout(cfg, name, get(src_name))
-        dst.copy_(tp_slice(name, src, model_tp(model, name)).to(dst.dtype))
+        dst.copy_(tp_slice_for(model, name, src).to(dst.dtype))

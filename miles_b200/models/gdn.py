@@ -33,10 +33,11 @@ import torch
 import torch.nn.functional as F
 
 
-def gdn_param_shapes(cfg, p: str):
+def gdn_param_shapes(cfg, p: str, tp: int = 1):
+    """This TP rank's slice: 1 / tp of the key heads and of their value heads in every block."""
     H = cfg.hidden_size
-    nk, nv, dk, dv, K = (cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim,
-                         cfg.linear_value_head_dim, cfg.linear_conv_kernel)
+    nk, nv, dk, dv, K = (cfg.linear_num_key_heads // tp, cfg.linear_num_value_heads // tp,
+                         cfg.linear_key_head_dim, cfg.linear_value_head_dim, cfg.linear_conv_kernel)
     C = 2 * nk * dk + nv * dv
     return [(p + "in_proj_qkvz.weight", (2 * nk * dk + 2 * nv * dv, H), "normal"),
             (p + "in_proj_ba.weight", (2 * nv, H), "normal"),
@@ -47,10 +48,11 @@ def gdn_param_shapes(cfg, p: str):
             (p + "out_proj.weight", (H, nv * dv), "normal")]
 
 
-def gdn_state_shapes(cfg):
-    """(conv state [C, K-1], recurrent state [nv, dk, dv]) of one sequence in one layer."""
-    nk, nv, dk, dv, K = (cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim,
-                         cfg.linear_value_head_dim, cfg.linear_conv_kernel)
+def gdn_state_shapes(cfg, tp: int = 1):
+    """(conv state [C, K-1], recurrent state [nv, dk, dv]) of one sequence in one layer (this
+    TP rank's heads)."""
+    nk, nv, dk, dv, K = (cfg.linear_num_key_heads // tp, cfg.linear_num_value_heads // tp,
+                         cfg.linear_key_head_dim, cfg.linear_value_head_dim, cfg.linear_conv_kernel)
     return (2 * nk * dk + nv * dv, K - 1), (nv, dk, dv)
 
 
@@ -72,7 +74,11 @@ class GDN:
     def __init__(self, model):
         self.m = model
         self.cfg = cfg = model.cfg
-        self.nk, self.nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+        self.tp = model.tp_size
+        if cfg.linear_num_key_heads % self.tp:
+            raise ValueError(f"{cfg.linear_num_key_heads} linear key heads do not split over TP {self.tp}")
+        # this TP rank's key heads and the value heads they serve
+        self.nk, self.nv = cfg.linear_num_key_heads // self.tp, cfg.linear_num_value_heads // self.tp
         self.dk, self.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
         self.K = cfg.linear_conv_kernel
         if self.nv % self.nk:
@@ -82,7 +88,10 @@ class GDN:
         return self.m.params[f"layers.{i}.linear_attn.{name}"]
 
     def _project(self, i, x):
+        from miles_b200.parallel.tp import copy_to_tp
+
         nk, nv, dk, dv = self.nk, self.nv, self.dk, self.dv
+        x = copy_to_tp(x, self.m.tp)
         qkvz = self.m._lin(x, f"layers.{i}.linear_attn.in_proj_qkvz.weight").float()
         mixed, z = qkvz.split([2 * nk * dk + nv * dv, nv * dv], -1)
         ba = self.m._lin(x, f"layers.{i}.linear_attn.in_proj_ba.weight").float()
@@ -154,19 +163,27 @@ class GDN:
                 "hjd,hjv->hdv", kc * torch.exp(last[:, None] - gam)[:, :, None], u)
         return torch.cat(outs, 0), S
 
-    def _out(self, i, o, z, dtype):
+    def _out(self, i, o, z, dtype, pending: bool = False):
+        """Gated norm + out_proj (row parallel under TP): reduced, or (pending) what the
+        caller's residual add + norm reduces."""
+        from miles_b200.parallel.tp import reduce_from_tp
+
         T = o.shape[0]
         o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + self.cfg.rms_eps)
         o = o * self._p(i, "norm.weight").float() * F.silu(z.view(T, self.nv, self.dv))
-        return self.m._lin(o.reshape(T, -1).to(dtype), f"layers.{i}.linear_attn.out_proj.weight")
+        o, name = o.reshape(T, -1).to(dtype), f"layers.{i}.linear_attn.out_proj.weight"
+        if pending:
+            return self.m._pending_out(o, name)
+        return reduce_from_tp(self.m._lin(o, name), self.m.tp)
 
     def _zero_states(self, device):
-        (C, Km1), (nv, dk, dv) = gdn_state_shapes(self.cfg)
+        (C, Km1), (nv, dk, dv) = gdn_state_shapes(self.cfg, self.tp)
         return (torch.zeros(C, Km1, dtype=torch.float32, device=device),
                 torch.zeros(nv, dk, dv, dtype=torch.float32, device=device))
 
     # ------------------------------------------------------------------ training / prefill
-    def attn(self, i: int, x: torch.Tensor, meta, cache=None, state_rows=None) -> torch.Tensor:
+    def attn(self, i: int, x: torch.Tensor, meta, cache=None, state_rows=None,
+             pending: bool = False) -> torch.Tensor:
         """Packed sequences from zero states; with `cache` the final states of sequence b are
         written to row state_rows[b]."""
         mixed, z, beta, g = self._project(i, x)
@@ -186,10 +203,11 @@ class GDN:
                 cache.lin_conv[i][row].copy_(cst)
                 cache.lin_state[i][row].copy_(S)
         o = torch.cat(outs, 0)
-        return self._out(i, o, z, x.dtype)
+        return self._out(i, o, z, x.dtype, pending)
 
     # ------------------------------------------------------------------ decode
-    def decode(self, i: int, x: torch.Tensor, cache, state_rows: torch.Tensor) -> torch.Tensor:
+    def decode(self, i: int, x: torch.Tensor, cache, state_rows: torch.Tensor,
+               pending: bool = False) -> torch.Tensor:
         """One token per row; advances the states in rows `state_rows` of the cache."""
         mixed, z, beta, g = self._project(i, x)                  # [B, ...]
         rows = state_rows.long()
@@ -213,10 +231,10 @@ class GDN:
             o = torch.empty(B, nv, dv, dtype=torch.float32, device=x.device)
             lib().gdn_decode(q.contiguous(), k.contiguous(), v.contiguous(), beta.contiguous(),
                              g.contiguous(), rows.contiguous(), cache.lin_state[i], o, 1.0 / math.sqrt(dk))
-            return self._out(i, o, z, x.dtype)
+            return self._out(i, o, z, x.dtype, pending)
         o, S = gdn_step_ref(q, k, v, beta, g, S, dk)
         cache.lin_state[i].index_copy_(0, rows, S)
-        return self._out(i, o, z, x.dtype)
+        return self._out(i, o, z, x.dtype, pending)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -276,7 +294,7 @@ def gdn_attn_cp(gdn: GDN, i: int, x: torch.Tensor, meta, lo: int, hi: int, cp) -
         if e <= s:
             continue
         if cu[b] < lo:  # continues a sequence from the previous rank
-            (C, Km1), ss = gdn_state_shapes(gdn.cfg)
+            (C, Km1), ss = gdn_state_shapes(gdn.cfg, gdn.tp)
             anchor = mixed[:0].sum()
             cst, S = _RecvState.apply(anchor, (C, Km1), ss, dist.get_global_rank(cp.group, cp.rank - 1), cp.group)
         else:

@@ -9,7 +9,9 @@ differences from Qwen3's:
   * rotary embedding on the first D * partial_rotary_factor dims of each head only;
   * the model's RMSNorms are zero-centred in the checkpoint (y = x_hat * (1 + w)); the HF
     loader stores 1 + w, so the ordinary norm kernels apply unchanged.
-q / k / v are separate projections (HF names); QK-norm per head. Attention uses the tcgen05
+q / k / v are separate projections (HF names); QK-norm per head. Under TP each rank holds
+1 / TP of the query and KV heads (column-parallel q / k / v with their biases, row-parallel
+o_proj). Attention uses the tcgen05
 varlen / paged-decode kernels when the head size is 128 and the device is a GPU, PyTorch
 otherwise (Qwen3-Next's 256-wide heads).
 
@@ -26,8 +28,9 @@ import torch.nn.functional as F
 from miles_b200.models.mla import _rope
 
 
-def gated_attn_param_shapes(cfg, p: str):
-    H, D, nq, nkv = cfg.hidden_size, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads
+def gated_attn_param_shapes(cfg, p: str, tp: int = 1):
+    """Shapes of this TP rank's slice: q / k / v / o projections hold 1 / tp of the heads."""
+    H, D, nq, nkv = cfg.hidden_size, cfg.head_dim, cfg.num_heads // tp, cfg.num_kv_heads // tp
     g = 2 if cfg.attn_output_gate else 1
     out = [(p + "q_proj.weight", (g * nq * D, H), "normal"),
            (p + "k_proj.weight", (nkv * D, H), "normal"),
@@ -60,23 +63,27 @@ class GatedAttention:
 
         return self.D == 128 and use_native(x)
 
-    def _qkv(self, i: int, x: torch.Tensor, pos: torch.Tensor):
+    def _qkv(self, i: int, x: torch.Tensor, pos: torch.Tensor, tp_copy: bool = True):
+        from miles_b200.parallel.tp import copy_to_tp
+
         cfg, m, D = self.cfg, self.m, self.D
+        nq, nkv = m.nq, m.nkv  # this TP rank's heads
         p = f"layers.{i}.self_attn."
         T = x.shape[0]
+        xt = copy_to_tp(x, m.tp) if tp_copy else x
 
         def proj(name):
-            y = m._lin(x, p + name + ".weight")
+            y = m._lin(xt, p + name + ".weight")
             b = m.params.get(p + name + ".bias")
             return y if b is None else y + b.to(y.dtype)
 
         if cfg.attn_output_gate:
-            qg = proj("q_proj").view(T, cfg.num_heads, 2 * D)
-            q, gate = qg[..., :D], qg[..., D:].reshape(T, cfg.num_heads * D)
+            qg = proj("q_proj").view(T, nq, 2 * D)
+            q, gate = qg[..., :D], qg[..., D:].reshape(T, nq * D)
         else:
-            q, gate = proj("q_proj").view(T, cfg.num_heads, D), None
-        k = proj("k_proj").view(T, cfg.num_kv_heads, D)
-        v = proj("v_proj").view(T, cfg.num_kv_heads, D)
+            q, gate = proj("q_proj").view(T, nq, D), None
+        k = proj("k_proj").view(T, nkv, D)
+        v = proj("v_proj").view(T, nkv, D)
         if cfg.qk_norm:
             q = _head_norm(q, m.params[p + "q_norm.weight"], cfg.rms_eps)
             k = _head_norm(k, m.params[p + "k_norm.weight"], cfg.rms_eps)
@@ -86,15 +93,21 @@ class GatedAttention:
         k = torch.cat([_rope(k[..., :r], pos, self.cos, self.sin, il), k[..., r:]], -1).contiguous()
         return q, k, v.contiguous(), gate
 
-    def _out(self, i: int, o: torch.Tensor, gate) -> torch.Tensor:
+    def _out(self, i: int, o: torch.Tensor, gate, pending: bool = False):
+        """o_proj (row parallel under TP): the reduced output, or (pending) the partial /
+        deferred product that the caller's residual add + norm reduces."""
+        from miles_b200.parallel.tp import reduce_from_tp
+
         o = o.reshape(o.shape[0], -1)
         if gate is not None:
             o = o * torch.sigmoid(gate.float()).to(o.dtype)
-        return self.m._lin(o, f"layers.{i}.self_attn.o_proj.weight")
+        name = f"layers.{i}.self_attn.o_proj.weight"
+        if pending:
+            return self.m._pending_out(o, name)
+        return reduce_from_tp(self.m._lin(o, name), self.m.tp)
 
     def _sdpa(self, q, k, v, cu):
-        cfg = self.cfg
-        rep = cfg.num_heads // cfg.num_kv_heads
+        rep = self.m.nq // self.m.nkv
         outs = []
         for b in range(len(cu) - 1):
             s, e = cu[b], cu[b + 1]
@@ -107,7 +120,8 @@ class GatedAttention:
                                                        scale=1.0 / math.sqrt(self.D))[0].transpose(0, 1))
         return torch.cat(outs, 0)
 
-    def attn(self, i: int, x: torch.Tensor, meta, cache=None, slots=None) -> torch.Tensor:
+    def attn(self, i: int, x: torch.Tensor, meta, cache=None, slots=None,
+             pending: bool = False) -> torch.Tensor:
         q, k, v, gate = self._qkv(i, x, meta.positions)
         if cache is not None:
             cache.k[i].index_copy_(0, slots, k.to(cache.k[i].dtype))
@@ -118,9 +132,28 @@ class GatedAttention:
             o = varlen_attention(q, k, v, meta)
         else:
             o = self._sdpa(q, k, v, meta.cu_list)
-        return self._out(i, o, gate)
+        return self._out(i, o, gate, pending)
 
-    def decode(self, i: int, x: torch.Tensor, positions, cache, page_table, ctx_lens, slots):
+    def attn_sp(self, i: int, x: torch.Tensor, meta) -> torch.Tensor:
+        """Sequence parallel: x holds this TP rank's rows; projections on the all-gathered rows
+        (the gather's backward reduce-scatters), o_proj ends in a reduce-scatter."""
+        from miles_b200.parallel.tp import sp_gather
+
+        xf = sp_gather(x, self.m.tp)
+        q, k, v, gate = self._qkv(i, xf, meta.positions, tp_copy=False)
+        if self._native(x):
+            from miles_b200.ops.attention import varlen_attention
+
+            o = varlen_attention(q, k, v, meta)
+        else:
+            o = self._sdpa(q, k, v, meta.cu_list)
+        o = o.reshape(xf.shape[0], -1)
+        if gate is not None:
+            o = o * torch.sigmoid(gate.float()).to(o.dtype)
+        return self.m._row_rs(o, f"layers.{i}.self_attn.o_proj.weight")
+
+    def decode(self, i: int, x: torch.Tensor, positions, cache, page_table, ctx_lens, slots,
+               pending: bool = False):
         cfg = self.cfg
         q, k, v, gate = self._qkv(i, x, positions)
         cache.k[i].index_copy_(0, slots, k.to(cache.k[i].dtype))
@@ -135,11 +168,12 @@ class GatedAttention:
             maxk = page_table.shape[1] * page
             t = torch.arange(maxk, device=x.device)
             rows = (page_table.long()[:, t // page] * page + (t % page)[None, :]).reshape(-1)
-            kc = cache.k[i].index_select(0, rows).view(B, maxk, cfg.num_kv_heads, self.D).float()
-            vc = cache.v[i].index_select(0, rows).view(B, maxk, cfg.num_kv_heads, self.D).float()
-            rep = cfg.num_heads // cfg.num_kv_heads
+            nkv = self.m.nkv
+            kc = cache.k[i].index_select(0, rows).view(B, maxk, nkv, self.D).float()
+            vc = cache.v[i].index_select(0, rows).view(B, maxk, nkv, self.D).float()
+            rep = self.m.nq // nkv
             kc, vc = kc.repeat_interleave(rep, 2), vc.repeat_interleave(rep, 2)
             sc = torch.einsum("bhd,bthd->bht", q.float(), kc) / math.sqrt(self.D)
             sc = sc.masked_fill((t[None, :] >= ctx_lens[:, None].long())[:, None, :], float("-inf"))
             o = torch.einsum("bht,bthd->bhd", torch.softmax(sc, -1), vc).to(x.dtype)
-        return self._out(i, o, gate)
+        return self._out(i, o, gate, pending)

@@ -72,11 +72,11 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=Non
         if cfg.layer_is_linear(i):  # Gated DeltaNet linear attention (models/gdn.py)
             from miles_b200.models.gdn import gdn_param_shapes
 
-            specs += [ParamSpec(n, shp, init) for n, shp, init in gdn_param_shapes(cfg, p + "linear_attn.")]
+            specs += [ParamSpec(n, shp, init) for n, shp, init in gdn_param_shapes(cfg, p + "linear_attn.", t)]
         elif cfg.uses_torch_attention:  # gated / biased / partial-rotary attention (models/qwen3_next.py)
             from miles_b200.models.qwen3_next import gated_attn_param_shapes
 
-            specs += [ParamSpec(n, shp, init) for n, shp, init in gated_attn_param_shapes(cfg, p + "self_attn.")]
+            specs += [ParamSpec(n, shp, init) for n, shp, init in gated_attn_param_shapes(cfg, p + "self_attn.", t)]
         elif cfg.kv_lora_rank:  # multi-head latent attention (models/mla.py)
             from miles_b200.models.mla import mla_param_shapes
 
@@ -165,7 +165,7 @@ class KVCache:
         if any(lin):
             from miles_b200.models.gdn import gdn_state_shapes
 
-            cs, ss = gdn_state_shapes(cfg)
+            cs, ss = gdn_state_shapes(cfg, tp_size)
             for i in range(cfg.num_layers):
                 if lin[i]:
                     self.lin_conv[i] = torch.zeros((max_seqs,) + cs, dtype=torch.float32, device=device)
@@ -213,9 +213,8 @@ class Transformer(torch.nn.Module):
             self.cp = CPContext(cp_group)
             if self.cp.size == 1:
                 self.cp = None
-            elif self.tp is not None and (cfg.uses_torch_attention or cfg.linear_attn_interval
-                                          or cfg.kv_lora_rank):
-                raise ValueError("TP x CP is implemented for the fused-qkv attention families")
+            elif self.tp is not None and cfg.linear_attn_interval:
+                raise ValueError("linear-attention (Gated DeltaNet) layers run without TP")
             elif (cfg.num_kv_heads // self.tp_size) % self.cp.size:
                 raise ValueError(f"{cfg.num_kv_heads // self.tp_size} KV heads per TP rank do not "
                                  f"split over CP {self.cp.size}")
@@ -287,15 +286,11 @@ class Transformer(torch.nn.Module):
         if cfg.linear_attn_interval:
             from miles_b200.models.gdn import GDN
 
-            if self.tp is not None or self.sequence_parallel:
-                raise ValueError("linear-attention layers run without TP / SP")
             self.gdn = GDN(self)
         self.gattn = None
         if cfg.uses_torch_attention and not cfg.kv_lora_rank:
             from miles_b200.models.qwen3_next import GatedAttention
 
-            if self.tp is not None:
-                raise ValueError("gated attention layers run without TP")
             self.gattn = GatedAttention(self)
         self.mla = None
         if cfg.kv_lora_rank:
@@ -473,6 +468,8 @@ class Transformer(torch.nn.Module):
         pre = f"layers.{i}.self_attn."
         if self.mla is not None:  # latents gathered instead of the hidden rows (models/mla.py)
             a = self.mla.attn_sp(i, x, meta)
+        elif self.gattn is not None:  # separate q / k / v (models/qwen3_next.py)
+            a = self.gattn.attn_sp(i, x, meta)
         else:
             xf = sp_gather(x, tp)
             qkv = self._lin(xf, pre + "qkv_proj.weight")
@@ -499,6 +496,8 @@ class Transformer(torch.nn.Module):
         from miles_b200.ops.attention import VarlenMeta
 
         cfg, tp = self.cfg, self.tp
+        if self.gdn is not None:
+            raise NotImplementedError("sequence parallelism with linear-attention layers")
         T = tokens.shape[0]
         pad = (-T) % tp.size
         if pad:
@@ -715,9 +714,11 @@ class Transformer(torch.nn.Module):
             pre = f"layers.{i}.self_attn."
             post = self.params[f"layers.{i}.post_attention_layernorm.weight"]
             if self.gdn is not None and cfg.layer_is_linear(i):
-                x2, r = self._add_norm(self._sw(i, "post_self_attn_layernorm", self.gdn.attn(i, x, meta, cache, state_rows)), r, post)
+                x2, r = self._add_norm(self._sw(i, "post_self_attn_layernorm",
+                                               self.gdn.attn(i, x, meta, cache, state_rows, pending=True)), r, post)
             elif self.gattn is not None:
-                x2, r = self._add_norm(self._sw(i, "post_self_attn_layernorm", self.gattn.attn(i, x, meta, cache, slots)), r, post)
+                x2, r = self._add_norm(self._sw(i, "post_self_attn_layernorm",
+                                               self.gattn.attn(i, x, meta, cache, slots, pending=True)), r, post)
             elif self.mla is not None:
                 x2, r = self._add_norm(self.mla.attn(i, x, meta, cache, slots, pending=True), r, post)
             else:
@@ -753,9 +754,9 @@ class Transformer(torch.nn.Module):
             pre = f"layers.{i}.self_attn."
             post = self.params[f"layers.{i}.post_attention_layernorm.weight"]
             if self.gdn is not None and cfg.layer_is_linear(i):
-                a = self.gdn.decode(i, x, cache, state_rows)
+                a = self.gdn.decode(i, x, cache, state_rows, pending=True)
             elif self.gattn is not None:
-                a = self.gattn.decode(i, x, positions, cache, page_table, ctx_lens, slots)
+                a = self.gattn.decode(i, x, positions, cache, page_table, ctx_lens, slots, pending=True)
             elif self.mla is not None:
                 a = self.mla.decode(i, x, positions, cache, page_table, ctx_lens, slots, pending=True)
             else:

@@ -147,8 +147,11 @@ def reduce_from_tp(x: torch.Tensor, tp: TPContext | None) -> torch.Tensor:
 # ------------------------------------------------------------------ parameter layout
 _COL = ("self_attn.q_proj.weight", "self_attn.q_b_proj.weight", "self_attn.kv_b_proj.weight",
         "mlp.gate_proj.weight", "mlp.up_proj.weight", "shared_experts.gate_proj.weight",
-        "shared_experts.up_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight")
-_ROW = ("self_attn.o_proj.weight", "mlp.down_proj.weight", "shared_experts.down_proj.weight")
+        "shared_experts.up_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+        "self_attn.q_proj.bias", "self_attn.k_proj.bias", "self_attn.v_proj.bias",
+        "shared_expert.gate_proj.weight", "shared_expert.up_proj.weight")
+_ROW = ("self_attn.o_proj.weight", "mlp.down_proj.weight", "shared_experts.down_proj.weight",
+        "shared_expert.down_proj.weight")
 
 
 def hf_shard_dim(hf_name: str) -> int | None:
@@ -187,6 +190,55 @@ def model_tp(model, name: str):
     return None if _whole_expert(model, name) else model.tp
 
 
+def _gdn_blocks(hf_name: str, cfg):
+    """(dim, block sizes) of a Gated DeltaNet tensor in this framework's layout: each block is
+    split over TP ranks by heads (key heads, and the value heads each key head serves)."""
+    if ".linear_attn." not in hf_name:
+        return None
+    qk, v = cfg.linear_num_key_heads * cfg.linear_key_head_dim, \
+        cfg.linear_num_value_heads * cfg.linear_value_head_dim
+    nv = cfg.linear_num_value_heads
+    table = {"in_proj_qkvz.weight": (0, [qk, qk, v, v]), "in_proj_qkv.weight": (0, [qk, qk, v]),
+             "in_proj_z.weight": (0, [v]), "in_proj_ba.weight": (0, [nv, nv]),
+             "in_proj_b.weight": (0, [nv]), "in_proj_a.weight": (0, [nv]),
+             "conv1d.weight": (0, [qk, qk, v]), "dt_bias": (0, [nv]), "A_log": (0, [nv]),
+             "out_proj.weight": (1, [v])}
+    return table.get(hf_name.split(".linear_attn.")[1])
+
+
+def tp_slice_for(model, hf_name: str, full: torch.Tensor) -> torch.Tensor:
+    """This rank's TP slice of a full tensor of `model` (named by its HF name)."""
+    tp = model_tp(model, hf_name)
+    if tp is None or tp.size == 1:
+        return full
+    blk = _gdn_blocks(hf_name, model.cfg)
+    if blk is None:
+        return tp_slice(hf_name, full, tp)
+    d, sizes = blk
+    parts, off = [], 0
+    for n in sizes:
+        lo, hi = tp.shard(n)
+        parts.append(full.narrow(d, off + lo, hi - lo))
+        off += n
+    return torch.cat(parts, d)
+
+
+def tp_gather_for(model, hf_name: str, local: torch.Tensor) -> torch.Tensor:
+    """Full tensor of `model` from every TP rank's slice (collective over the TP group)."""
+    tp = model_tp(model, hf_name)
+    if tp is None or tp.size == 1:
+        return local
+    blk = _gdn_blocks(hf_name, model.cfg)
+    if blk is None:
+        return tp_gather(hf_name, local, tp)
+    d, sizes = blk
+    ranks = [torch.empty_like(local) for _ in range(tp.size)]
+    dist.all_gather(ranks, local.contiguous(), group=tp.group)
+    split = [n // tp.size for n in sizes]
+    per_rank = [r.split(split, d) for r in ranks]
+    return torch.cat([per_rank[r][b] for b in range(len(sizes)) for r in range(tp.size)], d)
+
+
 def tp_partial_param_names(model) -> list[str]:
     """Replicated parameters whose gradient on one TP rank covers only its own slice (its heads,
     its intermediate slice, or under sequence parallelism its rows)."""
@@ -197,15 +249,15 @@ def tp_partial_param_names(model) -> list[str]:
     sp_norms = ("input_layernorm.weight", "post_attention_layernorm.weight", "q_a_proj.weight",
                 "q_a_layernorm.weight", "kv_a_proj_with_mqa.weight", "kv_a_layernorm.weight")
     for name in model.params:
-        if name.endswith(("self_attn.q_norm.weight", "self_attn.k_norm.weight")):
+        if name.endswith(("self_attn.q_norm.weight", "self_attn.k_norm.weight", "linear_attn.norm.weight")):
             out.append(name)
         elif (model.sequence_parallel and model.cp is None
               and (name.endswith(sp_norms) or name == "norm.weight")):
             out.append(name)
         elif model.vocab_parallel_logprob and model.cp is None and name == "lm_head.weight":
             out.append(name)  # each rank's gradient covers its vocabulary rows
-        elif name.endswith("mlp.gate.weight"):
-            out.append(name)  # router logits feed a combine of partial expert outputs
+        elif name.endswith(("mlp.gate.weight", "mlp.shared_expert_gate.weight")):
+            out.append(name)  # gate logits scale partial expert outputs
         elif model.ep is None and _whole_expert(model, name):
             out.append(name)  # whole experts on every TP rank, each fed its own rows
     return out
@@ -227,7 +279,12 @@ _SHARDED_INTERNAL = ("self_attn.qkv_proj.weight", "self_attn.o_proj.weight", "ml
                      "mlp.down_proj.weight", "mlp.experts.w1", "mlp.experts.w2",
                      "shared_experts.gate_up_proj.weight", "shared_experts.down_proj.weight",
                      "self_attn.q_proj.weight", "self_attn.q_b_proj.weight",
-                     "self_attn.kv_b_proj.weight")
+                     "self_attn.kv_b_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                     "self_attn.q_proj.bias", "self_attn.k_proj.bias", "self_attn.v_proj.bias",
+                     "shared_expert.gate_up_proj.weight", "shared_expert.down_proj.weight",
+                     "linear_attn.in_proj_qkvz.weight", "linear_attn.in_proj_ba.weight",
+                     "linear_attn.conv1d.weight", "linear_attn.dt_bias", "linear_attn.A_log",
+                     "linear_attn.out_proj.weight")
 
 
 def is_tp_sharded(name: str) -> bool:

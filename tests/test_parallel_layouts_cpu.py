@@ -16,11 +16,16 @@ import torch.multiprocessing as mp
 os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
 
 
-def _cfg():
+def _cfg(variant="moe"):
     from miles_b200.models.config import preset
 
     # 4 KV heads: 2 per TP rank, split again over 2 CP ranks
-    return dataclasses.replace(preset("tiny-moe"), num_experts=8, num_heads=8, num_kv_heads=4)
+    base = dataclasses.replace(preset("tiny-moe"), num_experts=8, num_heads=8, num_kv_heads=4)
+    if variant == "biased":  # separate q / k / v with biases, half-width rotary (GLM-4.5-like)
+        return dataclasses.replace(base, attention_bias=True, partial_rotary_factor=0.5)
+    if variant == "mla":
+        return preset("tiny-dsa")
+    return base
 
 
 def _items(cfg, n=8):
@@ -43,7 +48,7 @@ def _actor_cfg():
                        optimizer_placement="device")
 
 
-def _run(rank, world, port, layout, ckpt, out):
+def _run(rank, world, port, layout, ckpt, out, variant):
     os.environ.update(MILES_B200_FORCE_CPU="1", RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     from miles_b200.checkpoint.hf import load_hf, save_hf
@@ -56,7 +61,7 @@ def _run(rank, world, port, layout, ckpt, out):
                               expert_model_parallel_size=ep, context_parallel_size=cp,
                               pipeline_model_parallel_size=1, expert_tensor_parallel_size=etp)
     ctx = init_distributed(args)
-    cfg = _cfg()
+    cfg = _cfg(variant)
     m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=7, tp_group=ctx.tp_group,
                     ep_group=ctx.ep_group, cp_group=ctx.cp_group, etp=etp)
     load_hf(m, ckpt)
@@ -82,15 +87,19 @@ def _run(rank, world, port, layout, ckpt, out):
     ((2, 2, 1, 1), 4, 29693),        # TP2 x EP2, whole experts (EP group = TP group)
     ((2, 1, 1, 1), 2, 29694),        # TP2, whole experts on both ranks
     ((2, 1, None, 2), 4, 29695),     # TP2 x CP2
+    ((2, 1, None, 2, "biased"), 4, 29696),   # TP2 x CP2, separate biased q / k / v
+    ((2, 1, None, 2, "mla"), 4, 29698),      # TP2 x CP2, MLA + DSA
 ])
-def test_ep_layouts_match_single(tmp_path, layout, world, port):
+def test_layouts_match_single(tmp_path, layout, world, port):
     from safetensors import safe_open
 
     from miles_b200.checkpoint.hf import save_hf, to_hf_tensors
     from miles_b200.models.transformer import Transformer
     from miles_b200.trainer.actor import Actor
 
-    cfg = _cfg()
+    variant = layout[4] if len(layout) > 4 else "moe"
+    layout = layout[:4]
+    cfg = _cfg(variant)
     m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=7)
     ckpt = str(tmp_path / "hf")
     save_hf(m, ckpt)
@@ -98,7 +107,7 @@ def test_ep_layouts_match_single(tmp_path, layout, world, port):
     met = a.train_step(_items(cfg))
     ref = {k: v.detach().clone() for k, v in to_hf_tensors(m)}
     out = str(tmp_path / "out")
-    mp.spawn(_run, args=(world, port, layout, ckpt, out), nprocs=world, join=True)
+    mp.spawn(_run, args=(world, port, layout, ckpt, out, variant), nprocs=world, join=True)
     import json
 
     wm = json.load(open(os.path.join(out, "model.safetensors.index.json")))["weight_map"]

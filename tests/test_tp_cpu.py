@@ -13,6 +13,21 @@ import torch.multiprocessing as mp
 os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
 
 
+def _cfg(name):
+    """Presets, plus attention variants that run through the separate-q/k/v path: GLM-4.5-like
+    (projection biases, half-width rotary, MoE) and Qwen3-Next-like (output gate, quarter-width
+    rotary)."""
+    import dataclasses
+
+    from miles_b200.models.config import preset
+
+    if name == "tiny-biased":
+        return dataclasses.replace(preset("tiny-moe"), attention_bias=True, partial_rotary_factor=0.5)
+    if name == "tiny-gated":
+        return dataclasses.replace(preset("tiny"), attn_output_gate=True, partial_rotary_factor=0.25)
+    return preset(name)
+
+
 def _run(rank, world, port, preset_name, ckpt, out_dir):
     os.environ["MILES_B200_FORCE_CPU"] = "1"
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
@@ -22,7 +37,7 @@ def _run(rank, world, port, preset_name, ckpt, out_dir):
     from miles_b200.ops.attention import VarlenMeta
     from miles_b200.parallel.tp import tp_gather
 
-    cfg = preset(preset_name)
+    cfg = _cfg(preset_name)
     from miles_b200.models.transformer import Transformer
 
     m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=5, tp_group=dist.group.WORLD)
@@ -48,22 +63,23 @@ def _run(rank, world, port, preset_name, ckpt, out_dir):
         grads[name] = gr
     # sequence parallel: same forward, same gradients (37 rows: exercises the padding)
     sp = {}
-    for p in m.params.values():
-        p.grad = None
-    m.sequence_parallel = True
-    hs = m.forward_train(toks, meta)
-    hs.pow(2).mean().backward()
-    sp["h"] = hs.detach()
-    partial_sp = set(tp_partial_param_names(m))
-    sp["grads"] = {}
-    for name, p in m.params.items():
-        if p.grad is None:
-            continue
-        gr = p.grad.clone()
-        if name in partial_sp:
-            dist.all_reduce(gr)
-        sp["grads"][name] = gr
-    m.sequence_parallel = False
+    if not cfg.linear_attn_interval:  # no SP for linear-attention layers
+        for p in m.params.values():
+            p.grad = None
+        m.sequence_parallel = True
+        hs = m.forward_train(toks, meta)
+        hs.pow(2).mean().backward()
+        sp["h"] = hs.detach()
+        partial_sp = set(tp_partial_param_names(m))
+        sp["grads"] = {}
+        for name, p in m.params.items():
+            if p.grad is None:
+                continue
+            gr = p.grad.clone()
+            if name in partial_sp:
+                dist.all_reduce(gr)
+            sp["grads"][name] = gr
+        m.sequence_parallel = False
     # engine decode (prefill + 4 greedy steps)
     from miles_b200.engine.engine import GenRequest, RolloutEngine
 
@@ -84,7 +100,7 @@ def _single(preset_name, ckpt):
     from miles_b200.models.transformer import Transformer
     from miles_b200.ops.attention import VarlenMeta
 
-    cfg = preset(preset_name)
+    cfg = _cfg(preset_name)
     m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=11)
     save_hf(m, ckpt)
     m.recompute = False
@@ -104,6 +120,16 @@ def _rank0_slice(name, full, cfg, t):
         a, b = x.chunk(2, d)
         return torch.cat([a.narrow(d, 0, a.shape[d] // t), b.narrow(d, 0, b.shape[d] // t)], d)
 
+    from miles_b200.parallel.tp import _gdn_blocks
+
+    blk = _gdn_blocks(name, cfg)  # Gated DeltaNet: every block split by heads
+    if blk is not None:
+        d, sizes = blk
+        parts, off = [], 0
+        for n in sizes:
+            parts.append(full.narrow(d, off, n // t))
+            off += n
+        return torch.cat(parts, d)
     if name.endswith("qkv_proj.weight"):
         D = cfg.head_dim
         q, k, v = full.split([cfg.num_heads * D, cfg.num_kv_heads * D, cfg.num_kv_heads * D], 0)
@@ -116,13 +142,15 @@ def _rank0_slice(name, full, cfg, t):
         return full.narrow(2, 0, full.shape[2] // t)
     if name.endswith(("o_proj.weight", "down_proj.weight")):
         return full.narrow(1, 0, full.shape[1] // t)
-    if name.endswith(("q_proj.weight", "q_b_proj.weight", "kv_b_proj.weight")):
+    if name.endswith(("q_proj.weight", "q_b_proj.weight", "kv_b_proj.weight", "k_proj.weight",
+                      "v_proj.weight", "q_proj.bias", "k_proj.bias", "v_proj.bias")):
         return full.narrow(0, 0, full.shape[0] // t)
     return full
 
 
 @pytest.mark.parametrize("preset_name,port", [("tiny", 29671), ("tiny-moe", 29672), ("tiny-mla", 29673),
-                                              ("tiny-dsa", 29674)])
+                                              ("tiny-dsa", 29674), ("tiny-biased", 29675),
+                                              ("tiny-gated", 29676), ("tiny-gdn", 29677)])
 def test_tp2_matches_tp1(tmp_path, preset_name, port):
     from safetensors.torch import load_file
 
