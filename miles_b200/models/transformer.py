@@ -228,8 +228,6 @@ class Transformer(torch.nn.Module):
                                 cap_tokens=ep_cap_tokens)
             if self.ep.size == 1:
                 self.ep = None
-        if cfg.sandwich_norm and tp_group is not None and dist_world(tp_group) > 1:
-            raise ValueError("sandwich-norm (GLM-4) models run without TP")
         self.pp = None  # pipeline parallelism (training), miles_b200/parallel/pp.py
         if pp_group is not None:
             from miles_b200.parallel.pp import PPContext
@@ -496,8 +494,8 @@ class Transformer(torch.nn.Module):
         from miles_b200.ops.attention import VarlenMeta
 
         cfg, tp = self.cfg, self.tp
-        if self.gdn is not None:
-            raise NotImplementedError("sequence parallelism with linear-attention layers")
+        if self.gdn is not None or cfg.sandwich_norm:
+            raise NotImplementedError("sequence parallelism with linear-attention layers or sandwich norms")
         T = tokens.shape[0]
         pad = (-T) % tp.size
         if pad:
@@ -669,10 +667,26 @@ class Transformer(torch.nn.Module):
         return (self.tp is not None and self.tp.backend == "symm" and self.device.type == "cuda"
                 and self.lora is None and rows <= self.tp.cap_rows)
 
+    def _sw_pend(self, i: int, name: str, pend):
+        """GLM-4 sandwich norm of a pending (inference) branch output: under TP the output is
+        reduced first and returned as ("full", y) so that `_add_norm` does not reduce again."""
+        if not self.cfg.sandwich_norm:
+            return pend
+        if isinstance(pend, tuple):
+            pend = G.linear(pend[1], pend[2])
+        if self.tp is not None:
+            pend = self.tp.all_reduce(pend)
+        y = rms_norm(pend, self.params[f"layers.{i}.{name}.weight"], self.cfg.rms_eps)
+        return ("full", y) if self.tp is not None else y
+
     def _add_norm(self, pending, r, w):
         """(x, r') = add_rms_norm(allreduce(pending), r, w); pending is a tensor (partial or
-        full output) or ("gemm", a, W) meaning a @ W^T still to be computed."""
+        full output), ("gemm", a, W) meaning a @ W^T still to be computed, or ("full", y) an
+        output already reduced over TP."""
         eps = self.cfg.rms_eps
+        if isinstance(pending, tuple) and pending[0] == "full":
+            y = pending[1]
+            return (rms_norm(y, w, eps), y) if r is None else add_rms_norm(y, r, w, eps)
         if isinstance(pending, tuple):
             _, a, W = pending
             if self._tp_fused(a.shape[0]):
@@ -714,10 +728,10 @@ class Transformer(torch.nn.Module):
             pre = f"layers.{i}.self_attn."
             post = self.params[f"layers.{i}.post_attention_layernorm.weight"]
             if self.gdn is not None and cfg.layer_is_linear(i):
-                x2, r = self._add_norm(self._sw(i, "post_self_attn_layernorm",
+                x2, r = self._add_norm(self._sw_pend(i, "post_self_attn_layernorm",
                                                self.gdn.attn(i, x, meta, cache, state_rows, pending=True)), r, post)
             elif self.gattn is not None:
-                x2, r = self._add_norm(self._sw(i, "post_self_attn_layernorm",
+                x2, r = self._add_norm(self._sw_pend(i, "post_self_attn_layernorm",
                                                self.gattn.attn(i, x, meta, cache, slots, pending=True)), r, post)
             elif self.mla is not None:
                 x2, r = self._add_norm(self.mla.attn(i, x, meta, cache, slots, pending=True), r, post)
@@ -734,7 +748,7 @@ class Transformer(torch.nn.Module):
                                        r, post)
             rec = record.append if (record is not None and i in self.router_cfgs) else None
             pend = self._mlp_partial(i, x2, record=rec) if rec is not None else self._pending_mlp(i, x2)
-            pend = self._sw(i, "post_mlp_layernorm", pend)
+            pend = self._sw_pend(i, "post_mlp_layernorm", pend)
         y, _ = self._add_norm(pend, r, self.params["norm.weight"])
         return y
 
@@ -768,10 +782,10 @@ class Transformer(torch.nn.Module):
                                           cfg.rms_eps, cfg.qk_norm)
                 o = decode_attention(q, cache.k[i], cache.v[i], page_table, ctx_lens)
                 a = self._pending_out(o.reshape(B, -1), pre + "o_proj.weight")
-            x2, r = self._add_norm(self._sw(i, "post_self_attn_layernorm", a), r, post)
+            x2, r = self._add_norm(self._sw_pend(i, "post_self_attn_layernorm", a), r, post)
             rec = record.append if (record is not None and i in self.router_cfgs) else None
             pend = self._mlp_partial(i, x2, record=rec) if rec is not None else self._pending_mlp(i, x2)
-            pend = self._sw(i, "post_mlp_layernorm", pend)
+            pend = self._sw_pend(i, "post_mlp_layernorm", pend)
         y, _ = self._add_norm(pend, r, self.params["norm.weight"])
         return y
 

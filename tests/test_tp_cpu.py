@@ -23,6 +23,9 @@ def _cfg(name):
 
     if name == "tiny-biased":
         return dataclasses.replace(preset("tiny-moe"), attention_bias=True, partial_rotary_factor=0.5)
+    if name == "tiny-sandwich":  # GLM-4-like: sandwich norms, biases, half interleaved rotary
+        return dataclasses.replace(preset("tiny"), sandwich_norm=True, attention_bias=True,
+                                   partial_rotary_factor=0.5, rope_interleave=True)
     if name == "tiny-gated":
         return dataclasses.replace(preset("tiny"), attn_output_gate=True, partial_rotary_factor=0.25)
     return preset(name)
@@ -63,7 +66,7 @@ def _run(rank, world, port, preset_name, ckpt, out_dir):
         grads[name] = gr
     # sequence parallel: same forward, same gradients (37 rows: exercises the padding)
     sp = {}
-    if not cfg.linear_attn_interval:  # no SP for linear-attention layers
+    if not cfg.linear_attn_interval and not cfg.sandwich_norm:  # no SP for these
         for p in m.params.values():
             p.grad = None
         m.sequence_parallel = True
@@ -150,7 +153,8 @@ def _rank0_slice(name, full, cfg, t):
 
 @pytest.mark.parametrize("preset_name,port", [("tiny", 29671), ("tiny-moe", 29672), ("tiny-mla", 29673),
                                               ("tiny-dsa", 29674), ("tiny-biased", 29675),
-                                              ("tiny-gated", 29676), ("tiny-gdn", 29677)])
+                                              ("tiny-gated", 29676), ("tiny-gdn", 29677),
+                                              ("tiny-sandwich", 29678)])
 def test_tp2_matches_tp1(tmp_path, preset_name, port):
     from safetensors.torch import load_file
 
