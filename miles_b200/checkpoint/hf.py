@@ -33,7 +33,7 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
     pre = "model."
     if "embed_tokens.weight" in P:
         yield pre + "embed_tokens.weight", P["embed_tokens.weight"].data
-    for i in model.layer_ids:
+    for i in list(model.layer_ids) + list(getattr(model, "mtp_ids", [])):
         L = f"layers.{i}."
         yield pre + L + "input_layernorm.weight", P[L + "input_layernorm.weight"].data
         yield pre + L + "post_attention_layernorm.weight", P[L + "post_attention_layernorm.weight"].data
@@ -105,6 +105,9 @@ def to_hf_tensors(model: Transformer) -> Iterator[tuple[str, torch.Tensor]]:
             yield pre + L + "mlp.gate_proj.weight", gu[:I]
             yield pre + L + "mlp.up_proj.weight", gu[I:]
             yield pre + L + "mlp.down_proj.weight", P[L + "mlp.down_proj.weight"].data
+    for j in getattr(model, "mtp_ids", []):  # multi-token prediction extras (DeepSeek-V3 names)
+        for n in ("enorm.weight", "hnorm.weight", "eh_proj.weight", "shared_head.norm.weight"):
+            yield pre + f"layers.{j}." + n, P[f"layers.{j}." + n].data
     if "norm.weight" in P:
         yield pre + "norm.weight", P["norm.weight"].data
     if not cfg.tie_embeddings and "lm_head.weight" in P:
@@ -227,6 +230,8 @@ def hf_config_dict(cfg: ModelConfig) -> dict:
             d.update(attention_bias=cfg.attention_bias, mlp_bias=False)
     else:
         d.update(model_type="qwen3", architectures=["Qwen3ForCausalLM"])
+    if cfg.mtp_num_layers:
+        d["num_nextn_predict_layers"] = cfg.mtp_num_layers
     return d
 
 

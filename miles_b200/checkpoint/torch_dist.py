@@ -44,6 +44,16 @@ def _qkv_from_megatron(t, nq, nkv, D):
     return torch.cat([q.reshape(nq * D, -1), k.reshape(nkv * D, -1), v.reshape(nkv * D, -1)], 0)
 
 
+class _NoMTP:
+    """cfg view whose main stack covers every layer index (names an MTP layer's body)."""
+
+    def __init__(self, cfg):
+        self._c = cfg
+
+    def __getattr__(self, k):
+        return 1 << 30 if k == "num_layers" else getattr(self._c, k)
+
+
 def megatron_name(name: str, cfg) -> str:
     m = re.match(r"layers\.(\d+)\.(.*)", name)
     if not m:
@@ -52,6 +62,13 @@ def megatron_name(name: str, cfg) -> str:
                 "lm_head.weight": "output_layer.weight"}[name]
     i, rest = int(m.group(1)), m.group(2)
     L = f"decoder.layers.{i}."
+    if i >= cfg.num_layers:  # multi-token prediction depth (Megatron MTP block names)
+        mp = f"mtp.layers.{i - cfg.num_layers}."
+        extra = {"enorm.weight": "enorm.weight", "hnorm.weight": "hnorm.weight",
+                 "eh_proj.weight": "eh_proj.weight", "shared_head.norm.weight": "final_layernorm.weight"}
+        if rest in extra:
+            return mp + extra[rest]
+        return mp + "transformer_layer." + megatron_name(f"layers.{i}.{rest}", _NoMTP(cfg))[len(L):]
     moe = cfg.layer_is_moe(i)
     table = {
         "input_layernorm.weight": ("input_layernorm.weight" if cfg.kv_lora_rank

@@ -37,6 +37,7 @@ class ModelConfig:
     routed_scaling_factor: float = 1.0
     num_shared_experts: int = 0
     first_k_dense: int = 0            # leading dense layers (DeepSeek)
+    mtp_num_layers: int = 0           # multi-token prediction depths (layers num_layers .. + mtp - 1)
     moe_layer_freq: int = 1
     # MLA (DeepSeek-V3 style)
     kv_lora_rank: int = 0

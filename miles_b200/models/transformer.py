@@ -66,7 +66,10 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=Non
     specs = []
     if first or (last and cfg.tie_embeddings):
         specs.append(ParamSpec("embed_tokens.weight", (cfg.vocab_size, H), "normal"))
-    for i in layers:
+    # multi-token prediction layers (on the last stage): ordinary decoder layers numbered after
+    # the main stack, plus their input norms / projection and head norm (HF DeepSeek-V3 names)
+    mtp_ids = list(range(cfg.num_layers, cfg.num_layers + cfg.mtp_num_layers)) if last else []
+    for i in list(layers) + mtp_ids:
         p = f"layers.{i}."
         specs.append(ParamSpec(p + "input_layernorm.weight", (H,), "ones"))
         if cfg.layer_is_linear(i):  # Gated DeltaNet linear attention (models/gdn.py)
@@ -112,6 +115,11 @@ def param_specs(cfg: ModelConfig, ep_size: int = 1, tp_size: int = 1, layers=Non
             I = cfg.intermediate_size // t
             specs += [ParamSpec(p + "mlp.gate_up_proj.weight", (2 * I, H), "normal"),
                       ParamSpec(p + "mlp.down_proj.weight", (H, I), "normal")]
+    for i in mtp_ids:
+        p = f"layers.{i}."
+        specs += [ParamSpec(p + "enorm.weight", (H,), "ones"), ParamSpec(p + "hnorm.weight", (H,), "ones"),
+                  ParamSpec(p + "eh_proj.weight", (H, 2 * H), "normal"),
+                  ParamSpec(p + "shared_head.norm.weight", (H,), "ones")]
     if last:
         specs.append(ParamSpec("norm.weight", (H,), "ones"))
         if not cfg.tie_embeddings:
@@ -238,6 +246,12 @@ class Transformer(torch.nn.Module):
             elif self.tp is not None or self.cp is not None or self.ep is not None:
                 raise ValueError("pipeline parallelism is supported with data parallelism only")
         self.layer_ids = list(self.pp.layer_ids) if self.pp else list(range(cfg.num_layers))
+        self.mtp_ids = list(range(cfg.num_layers, cfg.num_layers + cfg.mtp_num_layers))
+        if self.mtp_ids and (self.pp is not None or self.tp is not None or self.cp is not None
+                             or self.ep is not None):
+            raise ValueError("multi-token prediction layers run with data parallelism only")
+        self.mtp_train = False  # add the MTP loss in training (Actor)
+        self._mtp_h = None
         self.is_first = self.pp is None or self.pp.is_first
         self.is_last = self.pp is None or self.pp.is_last
         # expert-tensor parallelism: routed experts split over the TP ranks (etp = TP, default)
@@ -272,7 +286,7 @@ class Transformer(torch.nn.Module):
         if cfg.is_moe:
             rc = RouterCfg(cfg.num_experts, cfg.topk, cfg.router_score, cfg.norm_topk_prob,
                            cfg.n_group, cfg.topk_group, cfg.routed_scaling_factor)
-            for i in self.layer_ids:
+            for i in self.layer_ids + self.mtp_ids:
                 if cfg.layer_is_moe(i):
                     self.router_cfgs[i] = rc
         # global ordinal of every MoE layer (column of the R3 routing tensors)
@@ -577,6 +591,49 @@ class Transformer(torch.nn.Module):
         y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
         return y
 
+    def mtp_loss(self, tokens, meta, sel, targets, weights, temperature: float = 1.0,
+                 chunk: int = 4096) -> torch.Tensor:
+        """Multi-token prediction loss of the last training forward (`selected_logprob` keeps
+        its final hidden h). Depth k (1-based) at row t: layer num_layers + k - 1 over
+        eh_proj([enorm(emb(token t + k)); hnorm(h_{k-1}[t])]) (the token embedding detached,
+        h_0 = h), then the shared LM head after shared_head.norm predicts token t + k + 1. The
+        main forward scores target tokens[s + 1] at rows `sel`; depth k scores the same targets
+        at rows s - k of the same sequence. Returns the mean over depths of
+        -sum(weights * log p) over the rows that exist.
+
+        Reference: Megatron MTP block (model_provider.py, --enable-mtp-training, MTP loss scaled
+        by --mtp-loss-scaling-factor), embeddings detached in the MTP input (megatron.patch)."""
+        from miles_b200.ops.logprob import lm_head_logprob
+
+        cfg = self.cfg
+        h = self._mtp_h
+        T = tokens.shape[0]
+        dev = tokens.device
+        cu = torch.tensor(meta.cu_list, device=dev)
+        row = torch.arange(T, device=dev)
+        seq = torch.searchsorted(cu, row, right=True) - 1
+        start, end = cu[seq], cu[seq + 1]
+        emb = F.embedding(tokens.long(), self.params["embed_tokens.weight"]).detach()
+        W = self.lm_head_weight()
+        prev, total = h, h.new_zeros((), dtype=torch.float32)
+        for k, j in enumerate(self.mtp_ids, 1):
+            p = f"layers.{j}."
+            ahead = row + k
+            ok = ahead < end
+            e = emb[torch.where(ok, ahead, row)] * ok[:, None].to(emb.dtype)
+            x = torch.cat([rms_norm(e, self.params[p + "enorm.weight"], cfg.rms_eps),
+                           rms_norm(prev, self.params[p + "hnorm.weight"], cfg.rms_eps)], -1)
+            x = self._lin(x, p + "eh_proj.weight")
+            m, r = self._layer_train(j, None, x, meta, None)
+            prev = m + r
+            y = rms_norm(prev, self.params[p + "shared_head.norm.weight"], cfg.rms_eps)
+            rows = sel - k
+            valid = rows >= start[sel]
+            rows = torch.where(valid, rows, sel)
+            lp, _ = lm_head_logprob(y.index_select(0, rows), W, targets, temperature, chunk)
+            total = total - (weights * valid.to(weights.dtype) * lp.float()).sum()
+        return total / max(1, len(self.mtp_ids))
+
     def selected_logprob(self, tokens, meta, sel, targets, temperature: float, chunk: int,
                          replay_experts=None):
         """(log-prob, entropy) of `targets` at hidden rows `sel` (ascending) of the training
@@ -586,6 +643,7 @@ class Transformer(torch.nn.Module):
 
         W = self.lm_head_weight()
         h = self.forward_train(tokens, meta, replay_experts=replay_experts)
+        self._mtp_h = h if (self.mtp_train and torch.is_grad_enabled()) else None
         if self.tp is not None and self.vocab_parallel_logprob and self.cp is None:
             from miles_b200.parallel.tp import vocab_parallel_logprob
 

@@ -163,10 +163,16 @@ def init_distributed(args) -> ProcessContext:
 
 def model_config(args) -> ModelConfig:
     if args.model_name:
-        return preset(args.model_name)
-    if args.hf_checkpoint:
-        return ModelConfig.from_hf(args.hf_checkpoint)
-    raise ValueError("pass --model-name <preset> or --hf-checkpoint <dir>")
+        cfg = preset(args.model_name)
+    elif args.hf_checkpoint:
+        cfg = ModelConfig.from_hf(args.hf_checkpoint)
+    else:
+        raise ValueError("pass --model-name <preset> or --hf-checkpoint <dir>")
+    if getattr(args, "enable_mtp_training", False):
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, mtp_num_layers=getattr(args, "mtp_num_layers", None) or 1)
+    return cfg
 
 
 def load_tokenizer(args):
@@ -190,6 +196,7 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
                         pp_last_layers=getattr(args, "decoder_last_pipeline_num_layers", None),
                         etp=getattr(args, "expert_tensor_parallel_size", None),
                         tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
+    model.mtp_train = bool(getattr(args, "enable_mtp_training", False))
     if getattr(args, "sequence_parallel", False) and model.tp is not None:
         model.sequence_parallel = True
     if getattr(args, "vocab_parallel_logprob", False) and model.tp is not None:
@@ -240,7 +247,9 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                       use_routing_replay=args.use_routing_replay,
                       grad_dtype=torch.float32 if (ctx.device.type != "cuda" or args.accumulate_allreduce_grads_in_fp32) else torch.bfloat16,
                       optimizer_placement=placement,
-                      logprob_chunk=args.log_probs_chunk_size if args.log_probs_chunk_size > 0 else 4096)
+                      logprob_chunk=args.log_probs_chunk_size if args.log_probs_chunk_size > 0 else 4096,
+                      mtp_loss_scale=(args.mtp_loss_scaling_factor
+                                      if getattr(args, "enable_mtp_training", False) else 0.0))
     if getattr(args, "train_backend", "b200") == "fsdp":
         # HF model under FSDP2 (trainer/fsdp_actor.py); `model` is then the engine's Transformer,
         # refreshed from the gathered HF state after every step

@@ -61,6 +61,7 @@ class ActorConfig:
     loss: PolicyLossCfg = field(default_factory=PolicyLossCfg)
     entropy_coef: float = 0.0
     per_token_loss: bool = False
+    mtp_loss_scale: float = 0.0      # weight of the multi-token prediction loss (model.mtp_train)
     temperature: float = 1.0
     use_rollout_logprobs: bool = False
     use_routing_replay: bool = False
@@ -274,6 +275,7 @@ class Actor:
             (sum(it.loss_mask) if it.loss_mask is not None else it.resp_len) for it in items)
         metrics = torch.zeros(len(METRIC_NAMES) + 1, dtype=torch.float64, device=self.dev)
         mbs = pack_microbatches([len(it.tokens) for it in items], cfg.max_tokens_per_gpu)
+        mtp_total = 0.0
         if model.pp is not None:
             self._train_pp(items, mbs, n_samples, n_tokens, metrics)
         for mb in ([] if model.pp is not None else mbs):
@@ -282,6 +284,11 @@ class Actor:
             lp, ent = model.selected_logprob(prep["tok"], prep["meta"], prep["sel"], prep["tgt"],
                                              cfg.temperature, cfg.logprob_chunk, self._replay(sub))
             loss = self._mb_loss(prep, lp, ent, metrics)
+            if model.mtp_train and cfg.mtp_loss_scale:
+                lm = model.mtp_loss(prep["tok"], prep["meta"], prep["sel"], prep["tgt"], prep["wgt"],
+                                    cfg.temperature, cfg.logprob_chunk)
+                loss = loss + cfg.mtp_loss_scale * lm
+                mtp_total += float(lm.detach())
             loss.backward()
         # parameters whose gradient came through autograd (embedding, norms) -> flat buffer
         for name, p in model.params.items():
@@ -299,6 +306,8 @@ class Actor:
         model.weight_version += 1
         out = {k: float(v) for k, v in zip(METRIC_NAMES + ["entropy"], metrics.tolist())}
         out["grad_norm"] = float(self.opt.grad_norm())
+        if model.mtp_train and cfg.mtp_loss_scale:
+            out["mtp_loss"] = mtp_total
         out["num_microbatches"] = len(mbs)
         self.timers["train_fwd_bwd"] = t1 - t0
         self.timers["train_total"] = time.perf_counter() - t0
