@@ -53,8 +53,18 @@ class RolloutManager:
         self.data_source = ShardedDataSource(data_source, rank, world) if world > 1 else data_source
         self.state = GenerateState(args, client=client, tokenizer=tokenizer)
         GenerateState.set(self.state)
-        self.rollout_fn = load_function(args.rollout_function_path)
-        self.eval_fn = load_function(args.eval_function_path) if args.eval_function_path else self.rollout_fn
+        from miles_b200.rollout.base_types import (RolloutFnConstructorInput,
+                                                   enable_experimental_rollout_refactor,
+                                                   load_rollout_callable)
+
+        if enable_experimental_rollout_refactor():
+            # class-based rollout functions, constructed once with this rank's arguments
+            ctor = RolloutFnConstructorInput(self._local_args(), self.data_source)
+            load = lambda path: load_rollout_callable(path, ctor)  # noqa: E731
+        else:
+            load = load_function
+        self.rollout_fn = load(args.rollout_function_path)
+        self.eval_fn = load(args.eval_function_path) if args.eval_function_path else self.rollout_fn
         self.custom_convert = (load_function(args.custom_convert_samples_to_train_data_path)
                                if args.custom_convert_samples_to_train_data_path else None)
         self.custom_reward_post = (load_function(args.custom_reward_post_process_path)

@@ -18,6 +18,7 @@ from miles_b200.engine.engine import RolloutEngine
 from miles_b200.models.config import ModelConfig, preset
 from miles_b200.models.transformer import Transformer
 from miles_b200.ops.rl import PolicyLossCfg
+from miles_b200.parallel.reloadable import REGISTRY as _RG
 from miles_b200.trainer.actor import Actor, ActorConfig
 
 
@@ -65,7 +66,7 @@ def init_distributed(args) -> ProcessContext:
     ctx = ProcessContext(rank, world, local, dev)
     if world > 1:
         dp = dist.group.WORLD
-        gloo = dist.new_group(backend="gloo") if use_cuda else dp
+        gloo = _RG.new_group(backend="gloo", tag="keep") if use_cuda else dp
         ctx.dp_group, ctx.gloo_group, ctx.dp_rank, ctx.dp_size = dp, gloo, rank, world
         tp = getattr(args, "tensor_model_parallel_size", 1)
         ep = getattr(args, "expert_model_parallel_size", 1)
@@ -79,12 +80,12 @@ def init_distributed(args) -> ProcessContext:
             # stage s holds ranks [s*D, (s+1)*D) (its DP group); pipeline d is {d + s*D}
             D = world // pp
             for d in range(D):
-                g = dist.new_group([d + s_ * D for s_ in range(pp)])
+                g = _RG.new_group([d + s_ * D for s_ in range(pp)])
                 if rank % D == d:
                     ctx.pp_group = g
             for s_ in range(pp):
                 ranks = list(range(s_ * D, (s_ + 1) * D))
-                g = dist.new_group(ranks)
+                g = _RG.new_group(ranks)
                 if rank in ranks:
                     ctx.dp_group = g
             register_tied_embedding_groups(world, pp)
@@ -99,7 +100,7 @@ def init_distributed(args) -> ProcessContext:
             for b in range(0, world, blk):
                 for t in range(tp):
                     ranks = [b + c * tp + t for c in range(cp)]
-                    g = dist.new_group(ranks)
+                    g = _RG.new_group(ranks)
                     if rank in ranks:
                         ctx.cp_group = g
         elif cp > 1:
@@ -107,7 +108,7 @@ def init_distributed(args) -> ProcessContext:
             # data is sharded over DP replicas only
             blocks, _ = _groups(world, cp)
             for ranks in blocks:
-                g = dist.new_group(ranks)
+                g = _RG.new_group(ranks)
                 if rank in ranks:
                     ctx.cp_group = g
             ctx.dp_rank, ctx.dp_size = rank // cp, world // cp
@@ -115,11 +116,11 @@ def init_distributed(args) -> ProcessContext:
             # TP groups are consecutive ranks (one NVSwitch domain); DP across them
             blocks, strided = _groups(world, tp)
             for ranks in blocks:
-                g = dist.new_group(ranks)
+                g = _RG.new_group(ranks, tag="rollout")
                 if rank in ranks:
                     ctx.tp_group = g
             for ranks in strided:
-                g = dist.new_group(ranks)
+                g = _RG.new_group(ranks)
                 if rank in ranks:
                     ctx.dp_group = g
             ctx.dp_rank, ctx.dp_size = rank // tp, world // tp
@@ -139,23 +140,23 @@ def init_distributed(args) -> ProcessContext:
             for t in range(tp):
                 for b in range(0, D, ep):
                     ranks = [t + tp * (b + e) for e in range(ep)]
-                    g = dist.new_group(ranks)
+                    g = _RG.new_group(ranks, tag="rollout")
                     if rank in ranks:
                         ctx.ep_group = g
                 for e in range(ep):
                     ranks = [t + tp * (b + e) for b in range(0, D, ep)]
-                    g = dist.new_group(ranks)
+                    g = _RG.new_group(ranks)
                     if rank in ranks:
                         ctx.expert_dp_group = g
         elif ep > 1:
             # EP alone, or with whole experts under TP: EP groups of consecutive ranks
             blocks, strided = _groups(world, ep)
             for ranks in blocks:
-                g = dist.new_group(ranks)
+                g = _RG.new_group(ranks, tag="rollout")
                 if rank in ranks:
                     ctx.ep_group = g
             for ranks in strided:
-                g = dist.new_group(ranks)
+                g = _RG.new_group(ranks)
                 if rank in ranks:
                     ctx.expert_dp_group = g
     return ctx

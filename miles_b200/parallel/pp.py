@@ -78,7 +78,9 @@ class PPContext:
         if key not in _TIED_GROUPS and self.size > 1 and self.size == dist.get_world_size():
             # one pipeline spans the job: create its first/last-stage group here (new_group is
             # collective over the job; with several pipelines the launcher creates them all)
-            _TIED_GROUPS[key] = dist.new_group([self.ranks[0], self.ranks[-1]])
+            from miles_b200.parallel.reloadable import REGISTRY
+
+            _TIED_GROUPS[key] = REGISTRY.new_group([self.ranks[0], self.ranks[-1]])
 
     def stage_of_layer(self, i: int) -> int:
         """Rank (within the pipeline group) that owns layer i."""
@@ -352,7 +354,9 @@ def register_tied_embedding_groups(world: int, pp_size: int) -> None:
     D = world // pp_size
     for d in range(D):
         ranks = [d + s * D for s in range(pp_size)]
-        _TIED_GROUPS[tuple(ranks)] = dist.new_group([ranks[0], ranks[-1]])
+        from miles_b200.parallel.reloadable import REGISTRY
+
+        _TIED_GROUPS[tuple(ranks)] = REGISTRY.new_group([ranks[0], ranks[-1]])
 
 
 @torch.no_grad()

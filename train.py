@@ -17,6 +17,7 @@ import sys
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
 
 from miles_b200.checkpoint.torch_dist import (get_checkpoint_iteration, is_torch_dist,  # noqa: E402
                                               load_checkpoint, save_checkpoint, wait_async_save)
@@ -76,8 +77,18 @@ def train(args):
         tracker.log(manager.eval(start), start)
     for rollout_id in range(start, num_rollout):
         actor.release_grads()
+        reload_groups = args.offload_train and dist.is_initialized() and dist.get_world_size() > 1
+        if reload_groups:
+            # the trainer's DP / CP / pipeline communicators are idle during the rollout: free
+            # their device buffers and rebuild them (rebinding every holder) before training
+            from miles_b200.parallel import pp as _pp
+            from miles_b200.parallel.reloadable import REGISTRY
+
+            REGISTRY.destroy()
         data = manager.generate(rollout_id)
         engine.release_memory()
+        if reload_groups:
+            REGISTRY.reload([ctx, model, actor, trainer, _pp._TIED_GROUPS])
         if args.debug_rollout_only:
             tracker.log(data["metrics"], rollout_id)
             continue
