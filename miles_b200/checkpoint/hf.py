@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import json
 import os
+import warnings
 from typing import Iterator
 
 import torch
@@ -356,6 +357,7 @@ def _load(model: Transformer, wmap, get, path: str) -> None:
     cfg = model.cfg
 
     targets = dict(to_hf_tensors(model))  # views into model.flat
+    missing_mtp: list[str] = []
     for name, dst in targets.items():
         src_name = name
         if src_name not in wmap and src_name.startswith("model.") is False and ("model." + src_name) in wmap:
@@ -368,6 +370,26 @@ def _load(model: Transformer, wmap, get, path: str) -> None:
         if src_name not in wmap:
             if name == "lm_head.weight" and cfg.tie_embeddings:
                 continue
+            if _is_mtp_name(model, name):
+                # a base checkpoint without multi-token prediction weights: keep the freshly
+                # initialised MTP parameters
+                missing_mtp.append(name)
+                continue
             raise KeyError(f"{name} missing from {path}")
         src = from_hf_layout(cfg, name, get(src_name))
         dst.copy_(tp_slice_for(model, name, src).to(dst.dtype))
+    if missing_mtp:
+        warnings.warn(f"{path} has no multi-token prediction weights ({len(missing_mtp)} tensors, "
+                      f"e.g. {missing_mtp[0]}); keeping the initialised MTP layers")
+
+
+def _is_mtp_name(model: Transformer, name: str) -> bool:
+    """True for a tensor of a multi-token prediction depth (layers numbered past the main stack)."""
+    mtp = set(getattr(model, "mtp_ids", []))
+    if not mtp:
+        return False
+    parts = name.split(".")
+    for a, b in zip(parts, parts[1:]):
+        if a == "layers" and b.isdigit():
+            return int(b) in mtp
+    return False

@@ -148,6 +148,9 @@ int mb_attn_decode_noalloc(const void* q, const void* kc, const void* vc, void* 
                            const int* page_table, const int* ctx_lens, int B, int max_pages,
                            long long num_slots, int nq, int nkv, float softmax_scale,
                            cudaStream_t st);
+// Error word of the allocation-free entry point on the current device (0 = none, 2 = a bounded
+// wait inside the kernel ran out and the output is incomplete); reading it clears it.
+int mb_attn_decode_noalloc_error(int* code, cudaStream_t st);
 #ifdef __cplusplus
 }
 #endif
@@ -230,6 +233,25 @@ int mb_mla_decode(const float* q_lat, const float* q_pe, const void* cache, long
                   const int* page_table, int max_pages, const int* ctx_lens, const float* bias,
                   long long bias_stride, int B, int nh, int r, int dr, float scale, float* out,
                   cudaStream_t st);
+#ifdef __cplusplus
+}
+#endif
+
+// Device-resident decode loop state (engine_step.cu): gather a bucket's inputs from the
+// sequence slots, and commit the sampled tokens back into them.
+#ifdef __cplusplus
+extern "C" {
+#endif
+int mb_decode_prep(const int* rows, int B, int spare, const int* s_tok, const int* s_pos,
+                   const int* s_done, const int* s_pt, int max_pages, const float* s_invt,
+                   const long long* s_seed, int* tokens, int* positions, int* ctx,
+                   long long* slots, int* pt, float* invt, long long* seeds,
+                   long long* state_rows, int state_spare, cudaStream_t st);
+int mb_decode_commit(const int* rows, int B, int spare, const int* tok, const float* lp,
+                     const int* experts, int nk, int* s_tok, int* s_pos, int* s_done, int* s_nout,
+                     const int* s_maxnew, const int* s_stop, int nstop, int* out_tok,
+                     float* out_lp, int max_new, unsigned char* out_exp, const int* s_rec,
+                     int max_len, cudaStream_t st);
 #ifdef __cplusplus
 }
 #endif

@@ -179,27 +179,58 @@ extern "C" int mb_attn_bwd(const void* q, const void* k, const void* v, const vo
 //    to start at zero (each call writes every slot it later reads), but calls whose kernels
 //    overlap on the GPU (different streams, no ordering) race on it: order them.
 // =============================================================================================
+//  * Errors inside the kernels (a bounded wait that ran out: code 2) are recorded in a fixed
+//    device int beside the workspace; read it with mb_attn_decode_noalloc_error (which also
+//    clears it). It is zero until a kernel reports something.
 constexpr long long kNoAllocWsFloats = 1ll << 20;
 static __device__ __align__(256) float g_noalloc_ws[kNoAllocWsFloats];
+static __device__ int g_noalloc_err;
 static float* g_noalloc_ws_ptr[128] = {nullptr};
+static int* g_noalloc_err_ptr[128] = {nullptr};
+
+// Resolves (once per device, with that device current) the device addresses of the fixed
+// workspace and error word. Returns 0, or -10 / -11 on a device or symbol lookup failure.
+static int noalloc_setup(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return -10;
+  if (g_noalloc_ws_ptr[dev] == nullptr) {
+    void* ws = nullptr;
+    void* e = nullptr;
+    if (cudaGetSymbolAddress(&ws, g_noalloc_ws) != cudaSuccess || ws == nullptr) return -11;
+    if (cudaGetSymbolAddress(&e, g_noalloc_err) != cudaSuccess || e == nullptr) return -11;
+    g_noalloc_err_ptr[dev] = static_cast<int*>(e);
+    g_noalloc_ws_ptr[dev] = static_cast<float*>(ws);
+  }
+  *dev_out = dev;
+  return 0;
+}
+
+// Copies the error word of the current device into *code (0 = no error) and clears it. Ordered
+// on stream `st` and synchronous with it (it waits for the stream's earlier work).
+extern "C" int mb_attn_decode_noalloc_error(int* code, cudaStream_t st) {
+  int dev = 0;
+  const int rc = noalloc_setup(&dev);
+  if (rc) return rc;
+  if (cudaMemcpyAsync(code, g_noalloc_err_ptr[dev], sizeof(int), cudaMemcpyDeviceToHost, st) !=
+      cudaSuccess)
+    return -12;
+  if (cudaMemsetAsync(g_noalloc_err_ptr[dev], 0, sizeof(int), st) != cudaSuccess) return -12;
+  return cudaStreamSynchronize(st) == cudaSuccess ? 0 : -12;
+}
 
 extern "C" int mb_attn_decode_noalloc(const void* q, const void* kc, const void* vc, void* o,
                                       const int* page_table, const int* ctx_lens, int B,
                                       int max_pages, long long num_slots, int nq, int nkv,
                                       float softmax_scale, cudaStream_t st) {
   if (B == 0) return 0;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return -10;
   const long long nsplit = mb_attn_decode_nsplit(max_pages);
   const long long need = nsplit > 1 ? (long long)B * nq * nsplit * (D + 2) : 0;
   if (need > kNoAllocWsFloats) return -9;  // MB_NOALLOC_TOO_LARGE
-  if (g_noalloc_ws_ptr[dev] == nullptr) {
-    void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_ws) != cudaSuccess || ptr == nullptr) return -11;
-    g_noalloc_ws_ptr[dev] = static_cast<float*>(ptr);
-  }
+  int dev = 0;
+  const int rc = noalloc_setup(&dev);
+  if (rc) return rc;
   float* ws_o = g_noalloc_ws_ptr[dev];
   float* ws_ml = ws_o + (long long)B * nq * nsplit * D;
   return mb_attn_decode(q, kc, vc, o, page_table, ctx_lens, B, max_pages, num_slots, nq, nkv,
-                        softmax_scale, ws_o, ws_ml, nullptr, st);
+                        softmax_scale, ws_o, ws_ml, g_noalloc_err_ptr[dev], st);
 }

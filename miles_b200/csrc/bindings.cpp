@@ -517,6 +517,52 @@ int64_t mla_decode(torch::Tensor q_lat, torch::Tensor q_pe, torch::Tensor cache,
                        q_lat.size(2), q_pe.size(2), (float)scale, PT<float>(out), cur_stream());
 }
 
+
+// ------------------------------------------------------------------ device-resident decode
+// st: dict-free positional state (see engine/engine.py DecodeState): slot arrays [S+1, ...]
+int64_t decode_prep(torch::Tensor rows, int64_t spare, torch::Tensor s_tok, torch::Tensor s_pos,
+                    torch::Tensor s_done, torch::Tensor s_pt, torch::Tensor s_invt,
+                    torch::Tensor s_seed, torch::Tensor tokens, torch::Tensor positions,
+                    torch::Tensor ctx, torch::Tensor slots, torch::Tensor pt, torch::Tensor invt,
+                    torch::Tensor seeds, OT state_rows, int64_t state_spare) {
+  CHECK_DT(rows, at::kInt); CHECK_DT(s_tok, at::kInt); CHECK_DT(s_pos, at::kInt);
+  CHECK_DT(s_done, at::kInt); CHECK_DT(s_pt, at::kInt); CHECK_DT(s_seed, at::kLong);
+  CHECK_DT(slots, at::kLong); CHECK_DT(pt, at::kInt); CHECK_DT(seeds, at::kLong);
+  const int B = rows.numel();
+  TORCH_CHECK(pt.size(0) >= B && pt.size(1) == s_pt.size(1), "page-table shapes");
+  TORCH_CHECK(rows.is_contiguous() && s_pt.is_contiguous() && pt.is_contiguous());
+  if (state_rows.has_value()) CHECK_DT(state_rows.value(), at::kLong);
+  return mb_decode_prep(PT<int>(rows), B, (int)spare, PT<int>(s_tok), PT<int>(s_pos),
+                        PT<int>(s_done), PT<int>(s_pt), (int)s_pt.size(1), PT<float>(s_invt),
+                        PT<long long>(s_seed), PT<int>(tokens), PT<int>(positions), PT<int>(ctx),
+                        PT<long long>(slots), PT<int>(pt), PT<float>(invt), PT<long long>(seeds),
+                        PT<long long>(state_rows), (int)state_spare, cur_stream());
+}
+int64_t decode_commit(torch::Tensor rows, int64_t spare, torch::Tensor tok, torch::Tensor lp,
+                      OT experts, torch::Tensor s_tok, torch::Tensor s_pos, torch::Tensor s_done,
+                      torch::Tensor s_nout, torch::Tensor s_maxnew, torch::Tensor s_stop,
+                      torch::Tensor out_tok, torch::Tensor out_lp, OT out_exp, torch::Tensor s_rec) {
+  CHECK_DT(tok, at::kInt); CHECK_DT(lp, at::kFloat); CHECK_DT(out_tok, at::kInt);
+  CHECK_DT(out_lp, at::kFloat); CHECK_DT(s_stop, at::kInt); CHECK_DT(s_rec, at::kInt);
+  const int B = rows.numel();
+  int nk = 0, max_len = 0;
+  if (experts.has_value() && out_exp.has_value()) {
+    CHECK_DT(experts.value(), at::kInt);
+    CHECK_DT(out_exp.value(), at::kByte);
+    TORCH_CHECK(experts.value().is_contiguous() && out_exp.value().is_contiguous());
+    nk = experts.value().numel() / std::max<int64_t>(experts.value().size(0), 1);
+    max_len = out_exp.value().size(1);
+    TORCH_CHECK(out_exp.value().numel() == out_exp.value().size(0) * (int64_t)max_len * nk,
+                "out_exp must be [slots, max_len, n_moe, k]");
+  }
+  return mb_decode_commit(PT<int>(rows), B, (int)spare, PT<int>(tok), PT<float>(lp),
+                          nk ? PT<int>(experts) : nullptr, nk, PT<int>(s_tok), PT<int>(s_pos),
+                          PT<int>(s_done), PT<int>(s_nout), PT<int>(s_maxnew), PT<int>(s_stop),
+                          (int)s_stop.size(1), PT<int>(out_tok), PT<float>(out_lp),
+                          (int)out_tok.size(1), nk ? PT<unsigned char>(out_exp) : nullptr,
+                          PT<int>(s_rec), max_len, cur_stream());
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_decode", &mla_decode, "absorbed MLA decode over the paged latent cache");
   m.def("gdn_decode", &gdn_decode, "Gated DeltaNet decode step (state updated in place)");
@@ -576,4 +622,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sqnorm", &sqnorm);
   m.def("nonfinite", &nonfinite);
   m.def("adam", &adam);
+  m.def("decode_prep", &decode_prep);
+  m.def("decode_commit", &decode_commit);
 }

@@ -33,7 +33,7 @@ __global__ void mla_decode_kernel(const float* __restrict__ q_lat, const float* 
   for (int i = tid; i < r; i += nt) q[i] = q_lat[bh * r + i];
   for (int i = tid; i < dr; i += nt) q[r + i] = q_pe[bh * dr + i];
   __syncthreads();
-  const int L = ctx_lens[b];
+  const int L = min(ctx_lens[b], max_pages * 64);  // never past the page-table row
   const int* pt = page_table + (long long)b * max_pages;
   // pass 1: scores and their max
   float mx = -INFINITY;

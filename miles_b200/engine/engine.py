@@ -56,38 +56,125 @@ class GenResult:
 
 
 class _Seq:
-    __slots__ = ("req", "pages", "out", "lps", "pos", "done", "reason", "experts", "wave_idx")
+    __slots__ = ("req", "pages", "slot", "done", "reason", "prompt_experts")
 
     def __init__(self, req: GenRequest, pages: list[int]):
         self.req = req
         self.pages = pages
-        self.out: list[int] = []
-        self.lps: list[float] = []
-        self.pos = len(req.prompt)  # position of the next token to be written
+        self.slot = -1           # sequence slot: row of the device decode state (and GDN state)
         self.done = False
         self.reason = ""
-        self.experts: list[np.ndarray] = []
-        self.wave_idx = 0  # row of this sequence in the linear-attention state cache
+
+
+_NSTOP = 4  # stop token ids kept per sequence on the device
+
+
+class DecodeState:
+    """Per-slot decode state on the device (slots 0..S-1, slot S = spare for padding rows).
+
+    s_tok: last sampled token (next step's input); s_pos: its position; s_done: frozen flag;
+    s_nout / s_maxnew: generated / allowed tokens; s_pt: page-table row; s_invt, s_seed:
+    sampling parameters; s_stop: up to 4 stop ids (-1 = none); s_rec: record routed experts.
+    out_tok / out_lp [S+1, max_new]: generated tokens and their log-probs; out_exp
+    [S+1, max_len, n_moe, k] uint8 (allocated on first use): routed experts of every fed
+    position (prompt rows written at prefill)."""
+
+    def __init__(self, S: int, max_pages: int, n_moe: int, topk: int, dev):
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.S = S
+        self.max_len = max_pages * PAGE
+        self.s_tok = torch.zeros(S + 1, **i32)
+        self.s_pos = torch.zeros(S + 1, **i32)
+        self.s_done = torch.ones(S + 1, **i32)
+        self.s_nout = torch.zeros(S + 1, **i32)
+        self.s_maxnew = torch.zeros(S + 1, **i32)
+        self.s_pt = torch.zeros(S + 1, max_pages, **i32)
+        self.s_invt = torch.ones(S + 1, dtype=torch.float32, device=dev)
+        self.s_seed = torch.zeros(S + 1, dtype=torch.int64, device=dev)
+        self.s_stop = torch.full((S + 1, _NSTOP), -1, **i32)
+        self.s_rec = torch.zeros(S + 1, **i32)
+        self.out_tok = torch.zeros(S + 1, self.max_len, **i32)
+        self.out_lp = torch.zeros(S + 1, self.max_len, dtype=torch.float32, device=dev)
+        self.n_moe, self.topk = n_moe, topk
+        self.out_exp: torch.Tensor | None = None
+        self.dev = dev
+        self.host_flags = (torch.zeros(2, S + 1, dtype=torch.int32).pin_memory()
+                           if dev.type == "cuda" else torch.zeros(2, S + 1, dtype=torch.int32))
+
+    def ensure_exp(self):
+        if self.out_exp is None and self.n_moe:
+            self.out_exp = torch.zeros(self.S + 1, self.max_len, self.n_moe, self.topk,
+                                       dtype=torch.uint8, device=self.dev)
+        return self.out_exp
+
+
+def _prep_ref(ds: DecodeState, st: dict):
+    """PyTorch form of csrc/engine_step.cu decode_prep (CPU path)."""
+    rows = st["rows"].long()
+    live = (rows != ds.S) & (ds.s_done[rows] == 0)
+    p = torch.where(live, ds.s_pos[rows], torch.zeros_like(rows, dtype=torch.int32))
+    live = live & (p > 0) & ((p // PAGE) < ds.s_pt.shape[1])
+    p = torch.where(live, p, torch.zeros_like(p))
+    pt = torch.where(live[:, None], ds.s_pt[rows], torch.zeros_like(ds.s_pt[rows]))
+    st["pt"].copy_(pt)
+    st["tokens"].copy_(torch.where(live, ds.s_tok[rows], torch.zeros_like(p)))
+    st["positions"].copy_(p)
+    st["ctx"].copy_(p + 1)
+    j = torch.arange(rows.numel(), device=rows.device)
+    page = pt.gather(1, (p // PAGE).long()[:, None])[:, 0].long()
+    st["slots"].copy_(torch.where(live, page * PAGE + (p % PAGE).long(), j % PAGE))
+    st["inv_t"].copy_(torch.where(live, ds.s_invt[rows], torch.ones_like(ds.s_invt[rows])))
+    st["seeds"].copy_(torch.where(live, ds.s_seed[rows], torch.zeros_like(ds.s_seed[rows])))
+    st["state_rows"].copy_(torch.where(live, rows, torch.full_like(rows, ds.S)))
+
+
+def _commit_ref(ds: DecodeState, st: dict, tok, lp, experts):
+    """PyTorch form of csrc/engine_step.cu decode_commit (CPU path)."""
+    rows = st["rows"].long()
+    live = (rows != ds.S) & (ds.s_done[rows] == 0) & (ds.s_pos[rows] > 0)
+    r = rows[live]
+    if r.numel() == 0:
+        return
+    t = tok[live].int()
+    n = ds.s_nout[r].long()
+    p = ds.s_pos[r].long()
+    if experts is not None and ds.out_exp is not None:
+        rec = (ds.s_rec[r] != 0) & (p < ds.max_len)
+        ds.out_exp[r[rec], p[rec]] = experts[live][rec].to(torch.uint8)
+    ok = n < ds.max_len
+    ds.out_tok[r[ok], n[ok]] = t[ok]
+    ds.out_lp[r[ok], n[ok]] = lp[live][ok].float()
+    stop = (n + 1 >= ds.s_maxnew[r].long()) | (n + 1 >= ds.max_len)
+    stop = stop | (ds.s_stop[r] == t[:, None]).any(1)
+    ds.s_nout[r] = (n + 1).int()
+    ds.s_tok[r] = t
+    ds.s_pos[r] = (p + 1).int()
+    ds.s_done[r] = torch.where(stop, torch.ones_like(t), ds.s_done[r])
 
 
 class RolloutEngine:
     def __init__(self, model: Transformer, max_batch: int = 64, num_pages: int | None = None,
-                 mem_fraction: float = 0.9, use_cuda_graph: bool = True, max_pages_per_seq: int = 160):
+                 mem_fraction: float = 0.9, use_cuda_graph: bool = True, max_pages_per_seq: int = 160,
+                 steps_per_sync: int = 8):
         self.model = model
         self.cfg = model.cfg
         self.dev = model.device
         self.max_batch = max_batch
         self.use_graph = use_cuda_graph and self.dev.type == "cuda"
         self.max_pages_per_seq = max_pages_per_seq
+        # decode steps run back to back on the device between two host visits (one graph)
+        self.steps_per_sync = max(1, steps_per_sync)
         self._num_pages_req = num_pages
         self._mem_fraction = mem_fraction
         self.cache: KVCache | None = None
+        self.ds: DecodeState | None = None
         self.graphs: dict[int, tuple] = {}
         self.graph_launches: dict[int, int] = {}
         self.pool = None
         self.aborted = False
         self.stats = {}
         self.n_moe = sum(1 for i in range(self.cfg.num_layers) if self.cfg.layer_is_moe(i))
+        self.native = _lib.use_native(torch.empty(0, device=self.dev))
 
     # ------------------------------------------------------------------ memory
     def kv_bytes_per_page(self) -> int:
@@ -98,14 +185,19 @@ class RolloutEngine:
         return (1 if c.kv_lora_rank else 2) * c.num_layers * PAGE * nkv * hd * 2
 
     def resume_memory(self):
-        """Allocate the KV cache (and lazily the decode graphs). Mirrors resume_memory_occupation."""
+        """Allocate the KV cache and the decode state (graphs are captured lazily). Mirrors
+        resume_memory_occupation."""
         if self.cache is not None:
             return
+        self.ds = DecodeState(self.max_batch, self.max_pages_per_seq, self.n_moe,
+                              max(self.cfg.topk, 1), self.dev)
         n = self._num_pages_req
         if n is None:
             if self.dev.type == "cuda":
                 free, _ = torch.cuda.mem_get_info(self.dev)
-                n = int(free * self._mem_fraction) // self.kv_bytes_per_page()
+                # the routed-expert record buffer is allocated on first use: leave room for it
+                reserve = (self.max_batch + 1) * self.ds.max_len * self.n_moe * max(self.cfg.topk, 1)
+                n = int(max(free - reserve, 0) * self._mem_fraction) // self.kv_bytes_per_page()
             else:
                 n = 1024
         n = max(n, 2)
@@ -114,10 +206,12 @@ class RolloutEngine:
         self.free_pages = list(range(n - 1, 0, -1))  # page 0 = trash page for padded rows
 
     def release_memory(self):
-        """Free KV cache and graphs (mirrors release_memory_occupation(kv_cache, cuda_graph))."""
+        """Free KV cache, decode state and graphs (mirrors release_memory_occupation(kv_cache,
+        cuda_graph))."""
         self.graphs.clear()
         self.pool = None
         self.cache = None
+        self.ds = None
         if self.dev.type == "cuda":
             torch.cuda.empty_cache()
 
@@ -131,6 +225,7 @@ class RolloutEngine:
     def _static(self, B: int):
         dev = self.dev
         return {
+            "rows": torch.full((B,), self.max_batch, dtype=torch.int32, device=dev),
             "tokens": torch.zeros(B, dtype=torch.int32, device=dev),
             "positions": torch.zeros(B, dtype=torch.int32, device=dev),
             "ctx": torch.ones(B, dtype=torch.int32, device=dev),
@@ -139,30 +234,49 @@ class RolloutEngine:
             "inv_t": torch.ones(B, dtype=torch.float32, device=dev),
             "seeds": torch.zeros(B, dtype=torch.int64, device=dev),
             "experts": torch.zeros(B, max(self.n_moe, 1), max(self.cfg.topk, 1), dtype=torch.int32, device=dev),
-            # linear-attention state row of every batch row (padding rows: the spare last row)
+            # linear-attention state row of every batch row (= its slot; padding: the spare row)
             "state_rows": torch.full((B,), self.max_batch, dtype=torch.int64, device=dev),
         }
 
     def _step_fn(self, st):
+        """One decode step of the bucket: gather inputs from the slots, forward, sample, commit."""
+        ds = self.ds
+        rec_on = self.n_moe and ds.out_exp is not None
+        if self.native:
+            _lib.lib().decode_prep(st["rows"], ds.S, ds.s_tok, ds.s_pos, ds.s_done, ds.s_pt,
+                                   ds.s_invt, ds.s_seed, st["tokens"], st["positions"], st["ctx"],
+                                   st["slots"], st["pt"], st["inv_t"], st["seeds"],
+                                   st["state_rows"], ds.S)
+        else:
+            _prep_ref(ds, st)
         rec = []
         h = self.model.forward_decode(st["tokens"], st["positions"], self.cache, st["pt"], st["ctx"],
-                                      st["slots"], record=rec if self.n_moe else None,
+                                      st["slots"], record=rec if rec_on else None,
                                       state_rows=st["state_rows"])
         for j, idx in enumerate(rec):
             st["experts"][:, j].copy_(idx)
         # the sampled token sits at position `positions + 1`
         tok, lp = sample_from_hidden(h, self.model.lm_head_weight(), st["inv_t"], st["seeds"],
                                      st["positions"] + 1)
-        return tok, lp
+        if self.native:
+            _lib.lib().decode_commit(st["rows"], ds.S, tok, lp, st["experts"] if rec_on else None,
+                                     ds.s_tok, ds.s_pos, ds.s_done, ds.s_nout, ds.s_maxnew,
+                                     ds.s_stop, ds.out_tok, ds.out_lp,
+                                     ds.out_exp if rec_on else None, ds.s_rec)
+        else:
+            _commit_ref(ds, st, tok, lp, st["experts"] if rec_on else None)
 
-    def _get_step(self, B: int):
-        if B in self.graphs:
-            return self.graphs[B]
+    def _get_steps(self, B: int):
+        """(graph or None, static inputs) running `steps_per_sync` decode steps of bucket B."""
+        key = (B, self.ds.out_exp is not None)
+        if key in self.graphs:
+            return self.graphs[key]
         st = self._static(B)
         if not self.use_graph:
-            entry = (None, st, None)
-            self.graphs[B] = entry
+            entry = (None, st)
+            self.graphs[key] = entry
             return entry
+        # warm-up on a side stream with every row padding (writes only the trash page)
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(s):
@@ -174,10 +288,11 @@ class RolloutEngine:
         g = torch.cuda.CUDAGraph()
         n0 = _lib.launch_count()
         with torch.cuda.graph(g, pool=self.pool):
-            out = self._step_fn(st)
-        self.graph_launches[B] = _lib.launch_count() - n0
-        entry = (g, st, out)
-        self.graphs[B] = entry
+            for _ in range(self.steps_per_sync):
+                self._step_fn(st)
+        self.graph_launches[key] = _lib.launch_count() - n0
+        entry = (g, st)
+        self.graphs[key] = entry
         return entry
 
     # ------------------------------------------------------------------ generation
@@ -185,51 +300,84 @@ class RolloutEngine:
         self.aborted = True
 
     def generate(self, reqs: list[GenRequest]) -> list[GenResult]:
-        """Continuous batching: requests are admitted whenever a batch slot and enough KV pages
-        are free (prefilled as a packed batch, then joined to the running decode batch), and
-        leave the batch as soon as they finish."""
+        """Continuous batching with the decode loop on the device: requests are admitted whenever
+        a slot and enough KV pages are free (prefilled as a packed batch; their slots join the
+        running batch), the batch runs `steps_per_sync` decode steps per host visit (finished
+        sequences freeze on the device), and finished sequences leave at the next visit."""
         self.resume_memory()
+        ds = self.ds
+        if self.n_moe and any(r.return_routed_experts for r in reqs):
+            if self.cfg.num_experts > 256:
+                raise ValueError("routed-expert recording stores expert ids as uint8 (<= 256 experts)")
+            ds.ensure_exp()
         self.aborted = False
         results: dict[int, GenResult] = {}
         pending = list(reqs)
-        live: list[_Seq] = []
-        free_rows = list(range(self.max_batch - 1, -1, -1))  # linear-attention state rows
+        live: dict[int, _Seq] = {}           # slot -> sequence
+        free_slots = list(range(self.max_batch - 1, -1, -1))
         t0 = time.perf_counter()
-        n_decode_steps = n_prefills = 0
+        n_decode_steps = n_prefills = n_syncs = 0
+        cur_rows: tuple | None = None
+        cur_key = None
         while (pending or live) and not self.aborted:
-            if pending and len(live) < self.max_batch:
-                new, pending = self._admit(pending, self.max_batch - len(live))
+            if pending and free_slots:
+                new, pending = self._admit(pending, len(free_slots))
                 if new:
                     for sq in new:
-                        sq.wave_idx = free_rows.pop()
+                        sq.slot = free_slots.pop()
+                        live[sq.slot] = sq
                     self._prefill(new)
                     n_prefills += 1
-                    live += new
                 elif not live:
                     raise RuntimeError("KV cache too small for a single request")
-            running = [sq for sq in live if not sq.done]
-            if running:
-                self._decode_step(running)
-                n_decode_steps += 1
-            still = []
-            for sq in live:
-                if sq.done:
-                    results[sq.req.rid] = self._result(sq)
+            slots = sorted(live)
+            Bb = self._bucket(len(slots))
+            g, st = self._get_steps(Bb)
+            rows = tuple(slots) + (self.max_batch,) * (Bb - len(slots))
+            if rows != cur_rows or (Bb, ds.out_exp is not None) != cur_key:
+                st["rows"].copy_(torch.tensor(rows, dtype=torch.int32), non_blocking=False)
+                cur_rows, cur_key = rows, (Bb, ds.out_exp is not None)
+            if self.dev.type == "cuda":
+                torch.cuda.nvtx.range_push("decode_steps")
+            if g is not None:
+                g.replay()
+                _lib.add_launches(self.graph_launches[cur_key])
+            else:
+                for _ in range(self.steps_per_sync):
+                    self._step_fn(st)
+            if self.dev.type == "cuda":
+                torch.cuda.nvtx.range_pop()
+            n_decode_steps += self.steps_per_sync
+            n_syncs += 1
+            done, nout = self._read_flags()
+            for sl in slots:
+                if done[sl]:
+                    sq = live.pop(sl)
+                    sq.done = True
+                    results[sq.req.rid] = self._result(sq, int(nout[sl]))
                     self.free_pages.extend(sq.pages)
-                    free_rows.append(sq.wave_idx)
-                else:
-                    still.append(sq)
-            live = still
+                    free_slots.append(sl)
         if self.aborted:
-            for sq in live:
-                sq.done, sq.reason = True, "abort"
-                results[sq.req.rid] = self._result(sq)
+            done, nout = self._read_flags()
+            for sl, sq in list(live.items()):
+                results[sq.req.rid] = self._result(sq, int(nout[sl]), reason="abort")
                 self.free_pages.extend(sq.pages)
+                ds.s_done[sl] = 1
             for r in pending:
                 results[r.rid] = GenResult(r.rid, [], [], "abort", None, self.model.weight_version)
         self.stats = {"wall_s": time.perf_counter() - t0, "decode_steps": n_decode_steps,
-                      "prefills": n_prefills}
+                      "prefills": n_prefills, "host_syncs": n_syncs}
         return [results[r.rid] for r in reqs]
+
+    def _read_flags(self):
+        """Done flags and generated counts of every slot (one small device->host copy)."""
+        ds = self.ds
+        hf = ds.host_flags
+        hf[0].copy_(ds.s_done, non_blocking=True)
+        hf[1].copy_(ds.s_nout, non_blocking=True)
+        if self.dev.type == "cuda":
+            torch.cuda.current_stream(self.dev).synchronize()
+        return hf[0].numpy(), hf[1].numpy()
 
     def _admit(self, pending, room: int):
         """Take requests in order while batch slots (`room`) and KV pages last."""
@@ -248,8 +396,9 @@ class RolloutEngine:
         return s.pages[pos // PAGE] * PAGE + pos % PAGE
 
     def _prefill(self, wave: list[_Seq]) -> None:
-        """Packed prefill of newly admitted sequences; samples and accepts their first token."""
-        dev = self.dev
+        """Packed prefill of newly admitted sequences; samples their first token and writes
+        their slots' device state (nothing is read back)."""
+        dev, ds = self.dev, self.ds
         cu = [0]
         toks, slots = [], []
         for s in wave:
@@ -257,92 +406,65 @@ class RolloutEngine:
             slots.extend(self._slot(s, p) for p in range(len(s.req.prompt)))
             cu.append(len(toks))
         meta = VarlenMeta(cu, dev)
-        rec = [] if self.n_moe else None
+        rec = [] if (self.n_moe and ds.out_exp is not None) else None
         nvtx = dev.type == "cuda"
         if nvtx:
             torch.cuda.nvtx.range_push("prefill")
+        sl = torch.tensor([s.slot for s in wave], dtype=torch.int64, device=dev)
         h = self.model.forward_prefill(torch.tensor(toks, dtype=torch.int32, device=dev), meta,
                                        self.cache, torch.tensor(slots, dtype=torch.int64, device=dev),
-                                       record=rec,
-                                       state_rows=torch.tensor([s.wave_idx for s in wave],
-                                                               dtype=torch.int64, device=dev))
+                                       record=rec, state_rows=sl)
         last = torch.tensor([c - 1 for c in cu[1:]], dtype=torch.long, device=dev)
-        inv_t = torch.tensor([1.0 / s.req.temperature if s.req.temperature > 0 else 0.0 for s in wave],
-                             dtype=torch.float32, device=dev)
-        seeds = torch.tensor([s.req.seed for s in wave], dtype=torch.int64, device=dev)
-        posn = torch.tensor([len(s.req.prompt) for s in wave], dtype=torch.int32, device=dev)
+        invt_h = [1.0 / s.req.temperature if s.req.temperature > 0 else 0.0 for s in wave]
+        seed_h = [s.req.seed for s in wave]
+        plen_h = [len(s.req.prompt) for s in wave]
+        inv_t = torch.tensor(invt_h, dtype=torch.float32, device=dev)
+        seeds = torch.tensor(seed_h, dtype=torch.int64, device=dev)
+        posn = torch.tensor(plen_h, dtype=torch.int32, device=dev)
         tok, lp = sample_from_hidden(h.index_select(0, last).contiguous(), self.model.lm_head_weight(),
                                      inv_t, seeds, posn)
+        n = len(wave)
+        pt = np.zeros((n, self.max_pages_per_seq), np.int32)
+        stop = np.full((n, _NSTOP), -1, np.int32)
+        for b, s in enumerate(wave):
+            pt[b, :len(s.pages)] = s.pages
+            ids = list(s.req.stop_token_ids)
+            if len(ids) > _NSTOP:
+                raise ValueError(f"at most {_NSTOP} stop token ids per request")
+            stop[b, :len(ids)] = ids
+        maxnew = torch.tensor([s.req.max_new_tokens for s in wave], dtype=torch.int32, device=dev)
+        stop_d = torch.from_numpy(stop).to(dev)
+        ds.s_pt[sl] = torch.from_numpy(pt).to(dev)
+        ds.s_stop[sl] = stop_d
+        ds.s_invt[sl] = inv_t
+        ds.s_seed[sl] = seeds
+        ds.s_maxnew[sl] = maxnew
+        ds.s_rec[sl] = torch.tensor([int(s.req.return_routed_experts) for s in wave],
+                                    dtype=torch.int32, device=dev)
+        ds.s_tok[sl] = tok
+        ds.s_pos[sl] = posn
+        ds.s_nout[sl] = 1
+        ds.out_tok[sl, 0] = tok
+        ds.out_lp[sl, 0] = lp
+        first_done = (maxnew <= 1) | (stop_d == tok[:, None]).any(1)
+        ds.s_done[sl] = first_done.int()
         if rec:
-            ex = torch.stack(rec, 1).cpu().numpy()  # [T, L_moe, k]
+            ex = torch.stack(rec, 1).to(torch.uint8)  # [T, L_moe, k]
             for b, s in enumerate(wave):
                 if s.req.return_routed_experts:
-                    s.experts.append(ex[cu[b]:cu[b + 1]])
-        self._accept(wave, tok.tolist(), lp.tolist())
+                    ds.out_exp[s.slot, :plen_h[b]] = ex[cu[b]:cu[b + 1]]
         if nvtx:
             torch.cuda.nvtx.range_pop()
 
-    def _decode_step(self, live: list[_Seq]) -> None:
-        """One token for every running sequence (CUDA graph of the batch bucket)."""
-        nvtx = self.dev.type == "cuda"
-        Bb = self._bucket(len(live))
-        g, st, out = self._get_step(Bb)
-        n = len(live)
-        tokens = np.zeros(Bb, np.int32)
-        pos = np.zeros(Bb, np.int32)
-        ctx = np.ones(Bb, np.int32)
-        slot = np.arange(Bb, dtype=np.int64) % PAGE  # trash page 0 for padding rows
-        pt = np.zeros((Bb, self.max_pages_per_seq), np.int32)
-        invt = np.ones(Bb, np.float32)
-        seed = np.zeros(Bb, np.int64)
-        srow = np.full(Bb, self.max_batch, np.int64)
-        for j, s in enumerate(live):
-            srow[j] = s.wave_idx
-            p = len(s.req.prompt) + len(s.out) - 1  # position of the token being fed
-            tokens[j] = s.out[-1]
-            pos[j] = p
-            ctx[j] = p + 1
-            slot[j] = self._slot(s, p)
-            pt[j, :len(s.pages)] = s.pages
-            invt[j] = 1.0 / s.req.temperature if s.req.temperature > 0 else 0.0
-            seed[j] = s.req.seed
-        st["tokens"].copy_(torch.from_numpy(tokens), non_blocking=True)
-        st["positions"].copy_(torch.from_numpy(pos), non_blocking=True)
-        st["ctx"].copy_(torch.from_numpy(ctx), non_blocking=True)
-        st["slots"].copy_(torch.from_numpy(slot), non_blocking=True)
-        st["pt"].copy_(torch.from_numpy(pt), non_blocking=True)
-        st["inv_t"].copy_(torch.from_numpy(invt), non_blocking=True)
-        st["seeds"].copy_(torch.from_numpy(seed), non_blocking=True)
-        st["state_rows"].copy_(torch.from_numpy(srow), non_blocking=True)
-        if nvtx:
-            torch.cuda.nvtx.range_push("decode_step")
-        if g is not None:
-            g.replay()
-            _lib.add_launches(self.graph_launches[Bb])
-            tok, lp = out
-        else:
-            tok, lp = self._step_fn(st)
-        if self.n_moe and any(s.req.return_routed_experts for s in live):
-            ex = st["experts"][:n].cpu().numpy().copy()
-            for j, s in enumerate(live):
-                if s.req.return_routed_experts:
-                    s.experts.append(ex[j:j + 1])
-        self._accept(live, tok[:n].tolist(), lp[:n].tolist())
-        if nvtx:
-            torch.cuda.nvtx.range_pop()
-
-    def _accept(self, seqs, toks, lps):
-        for s, t, l in zip(seqs, toks, lps):
-            s.out.append(int(t))
-            s.lps.append(float(l))
-            if int(t) in s.req.stop_token_ids:
-                s.done, s.reason = True, "stop"
-            elif len(s.out) >= s.req.max_new_tokens:
-                s.done, s.reason = True, "length"
-
-    def _result(self, s: _Seq) -> GenResult:
+    def _result(self, s: _Seq, n: int, reason: str | None = None) -> GenResult:
+        ds = self.ds
+        n = max(0, min(n, ds.max_len))
+        toks = ds.out_tok[s.slot, :n].tolist()
+        lps = ds.out_lp[s.slot, :n].tolist()
+        if reason is None:
+            reason = "stop" if (toks and toks[-1] in s.req.stop_token_ids) else "length"
         ex = None
-        if s.req.return_routed_experts and s.experts:
-            ex = np.concatenate(s.experts, 0)
-            ex = ex[: len(s.req.prompt) + len(s.out) - 1]
-        return GenResult(s.req.rid, s.out, s.lps, s.reason, ex, self.model.weight_version)
+        if s.req.return_routed_experts and ds.out_exp is not None and n > 0:
+            rows = len(s.req.prompt) + n - 1
+            ex = ds.out_exp[s.slot, :rows].to(torch.int32).cpu().numpy()
+        return GenResult(s.req.rid, toks, lps, reason, ex, self.model.weight_version)

@@ -80,7 +80,9 @@ class ModelConfig:
                 or (self.rope_interleave and not self.kv_lora_rank))
 
     def layer_is_linear(self, i: int) -> bool:
-        return self.linear_attn_interval > 0 and (i + 1) % self.linear_attn_interval != 0
+        # layers numbered past the main stack are multi-token prediction depths: full attention
+        return (self.linear_attn_interval > 0 and i < self.num_layers
+                and (i + 1) % self.linear_attn_interval != 0)
 
     def layer_is_moe(self, i: int) -> bool:
         return self.is_moe and i >= self.first_k_dense and (i - self.first_k_dense) % self.moe_layer_freq == 0
@@ -144,6 +146,7 @@ class ModelConfig:
         c.max_position = d.get("max_position_embeddings", 32768)
         c.tie_embeddings = d.get("tie_word_embeddings", False)
         c.extra["token_ids"] = {k: d.get(k) for k in ("pad_token_id", "bos_token_id", "eos_token_id")}
+        c.extra["num_nextn_predict_layers"] = int(d.get("num_nextn_predict_layers") or 0)
         if mt == "glm4":  # GLM-4 dense: sandwich norms, interleaved half-width rotary, biases
             c.arch = "glm4"
             c.sandwich_norm = True

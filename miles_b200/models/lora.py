@@ -126,6 +126,15 @@ class LoRAOptimizer:
         self.step_id = 0
         self._norm = torch.zeros(())
 
+    @property
+    def lr(self) -> float:
+        return self.opt.param_groups[0]["lr"]
+
+    @lr.setter
+    def lr(self, v: float) -> None:
+        for g in self.opt.param_groups:
+            g["lr"] = v
+
     def grad_norm(self) -> torch.Tensor:
         return self._norm
 

@@ -250,6 +250,11 @@ class Transformer(torch.nn.Module):
         if self.mtp_ids and (self.pp is not None or self.tp is not None or self.cp is not None
                              or self.ep is not None):
             raise ValueError("multi-token prediction layers run with data parallelism only")
+        if self.mtp_ids and cfg.linear_attn_interval > 0:
+            # Qwen3-Next / Qwen3.5 keep their MTP block under mtp.fc / mtp.pre_fc_norm_* with
+            # gated full attention; that layout is not mapped here
+            raise ValueError("multi-token prediction is not supported on Gated DeltaNet hybrid "
+                             "families (Qwen3-Next / Qwen3.5)")
         self.mtp_train = False  # add the MTP loss in training (Actor)
         self._mtp_h = None
         self.is_first = self.pp is None or self.pp.is_first

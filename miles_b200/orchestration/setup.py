@@ -20,6 +20,7 @@ from miles_b200.models.transformer import Transformer
 from miles_b200.ops.rl import PolicyLossCfg
 from miles_b200.parallel.reloadable import REGISTRY as _RG
 from miles_b200.trainer.actor import Actor, ActorConfig
+from miles_b200.trainer.lr_scheduler import schedule_from_args
 
 
 @dataclass
@@ -172,7 +173,9 @@ def model_config(args) -> ModelConfig:
     if getattr(args, "enable_mtp_training", False):
         import dataclasses
 
-        cfg = dataclasses.replace(cfg, mtp_num_layers=getattr(args, "mtp_num_layers", None) or 1)
+        depth = (getattr(args, "mtp_num_layers", None) or cfg.extra.get("num_nextn_predict_layers")
+                 or 1)
+        cfg = dataclasses.replace(cfg, mtp_num_layers=depth)
     return cfg
 
 
@@ -250,7 +253,8 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                       optimizer_placement=placement,
                       logprob_chunk=args.log_probs_chunk_size if args.log_probs_chunk_size > 0 else 4096,
                       mtp_loss_scale=(args.mtp_loss_scaling_factor
-                                      if getattr(args, "enable_mtp_training", False) else 0.0))
+                                      if getattr(args, "enable_mtp_training", False) else 0.0),
+                      adam_eps=args.adam_eps, lr_schedule=schedule_from_args(args))
     if getattr(args, "train_backend", "b200") == "fsdp":
         # HF model under FSDP2 (trainer/fsdp_actor.py); `model` is then the engine's Transformer,
         # refreshed from the gathered HF state after every step
@@ -298,6 +302,9 @@ def build_critic(args, ctx: ProcessContext):
         if is_torch_dist(args.critic_load):
             load_checkpoint(args.critic_load, body)
     acfg = ActorConfig(lr=args.critic_lr, betas=(args.adam_beta1, args.adam_beta2),
+                       adam_eps=args.adam_eps,
+                       lr_schedule=schedule_from_args(args, lr=args.critic_lr,
+                                                      warmup_iters=args.critic_lr_warmup_iters),
                        weight_decay=args.weight_decay, clip_grad=args.clip_grad,
                        max_tokens_per_gpu=args.max_tokens_per_gpu or 16384,
                        grad_dtype=torch.float32 if ctx.device.type != "cuda" else torch.bfloat16,

@@ -31,6 +31,7 @@ from miles_b200.ops.gemm import clear_main_grads, register_main_grad
 from miles_b200.parallel.tp import tp_partial_param_names, tp_replicated_ranges
 from miles_b200.ops.attention import VarlenMeta
 from miles_b200.ops.rl import METRIC_NAMES, PolicyLossCfg, policy_loss
+from miles_b200.trainer.lr_scheduler import LRSchedule
 from miles_b200.trainer.optimizer import FlatAdam
 from miles_b200.utils.misc import load_function
 
@@ -68,6 +69,8 @@ class ActorConfig:
     grad_dtype: torch.dtype = torch.bfloat16
     optimizer_placement: str = "auto"
     logprob_chunk: int = 4096
+    adam_eps: float = 1e-8
+    lr_schedule: "LRSchedule | None" = None   # None: constant `lr`
 
 
 def pack_microbatches(lengths: list[int], max_tokens: int) -> list[list[int]]:
@@ -130,7 +133,8 @@ class Actor:
             self.opt.g = self.grad_flat
         else:
             self.opt = FlatAdam(self.model.flat, self.grad_flat, lr=self.cfg.lr,
-                                betas=self.cfg.betas, weight_decay=self.cfg.weight_decay,
+                                betas=self.cfg.betas, eps=self.cfg.adam_eps,
+                                weight_decay=self.cfg.weight_decay,
                                 clip_grad=self.cfg.clip_grad, placement=self.cfg.optimizer_placement,
                                 dp_group=self.dp_group if self._sharded() else None,
                                 **self._norm_scope())
@@ -275,7 +279,7 @@ class Actor:
             (sum(it.loss_mask) if it.loss_mask is not None else it.resp_len) for it in items)
         metrics = torch.zeros(len(METRIC_NAMES) + 1, dtype=torch.float64, device=self.dev)
         mbs = pack_microbatches([len(it.tokens) for it in items], cfg.max_tokens_per_gpu)
-        mtp_total = 0.0
+        mtp_total = torch.zeros((), dtype=torch.float32, device=self.dev)
         if model.pp is not None:
             self._train_pp(items, mbs, n_samples, n_tokens, metrics)
         for mb in ([] if model.pp is not None else mbs):
@@ -288,8 +292,9 @@ class Actor:
                 lm = model.mtp_loss(prep["tok"], prep["meta"], prep["sel"], prep["tgt"], prep["wgt"],
                                     cfg.temperature, cfg.logprob_chunk)
                 loss = loss + cfg.mtp_loss_scale * lm
-                mtp_total += float(lm.detach())
+                mtp_total += lm.detach().float()
             loss.backward()
+        model._mtp_h = None  # the last microbatch's final hidden is not kept past the step
         # parameters whose gradient came through autograd (embedding, norms) -> flat buffer
         for name, p in model.params.items():
             if p.grad is not None:
@@ -302,12 +307,17 @@ class Actor:
         if (self.dp_group is not None and dist.get_world_size(self.dp_group) > 1
                 and not self._sharded() and model.lora is None):
             self._reduce_grads()
+        if cfg.lr_schedule is not None:
+            # the LR of this step from the samples consumed before it (Megatron order)
+            self.opt.lr = cfg.lr_schedule.lr()
+            cfg.lr_schedule.advance(n_samples)
         self.opt.step()  # sharded: reduce-scatter + shard update + all-gather inside
         model.weight_version += 1
         out = {k: float(v) for k, v in zip(METRIC_NAMES + ["entropy"], metrics.tolist())}
         out["grad_norm"] = float(self.opt.grad_norm())
+        out["lr"] = float(self.opt.lr)
         if model.mtp_train and cfg.mtp_loss_scale:
-            out["mtp_loss"] = mtp_total
+            out["mtp_loss"] = float(mtp_total)
         out["num_microbatches"] = len(mbs)
         self.timers["train_fwd_bwd"] = t1 - t0
         self.timers["train_total"] = time.perf_counter() - t0

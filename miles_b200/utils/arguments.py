@@ -77,7 +77,9 @@ def add_train_args(p):
                    help="under TP, split the LM-head logits of the trainer's log-probs over the TP ranks")
     g.add_argument("--lr", type=float, default=1e-6)
     g.add_argument("--min-lr", type=float, default=0.0)
-    g.add_argument("--lr-decay-style", default="constant", choices=["constant", "linear", "cosine"])
+    g.add_argument("--lr-decay-style", default="constant",
+                   choices=["constant", "linear", "cosine", "inverse-square-root"])
+    g.add_argument("--lr-warmup-init", type=float, default=0.0)
     g.add_argument("--lr-warmup-iters", type=int, default=0)
     g.add_argument("--lr-warmup-fraction", type=float, default=None)
     g.add_argument("--lr-decay-iters", type=int, default=None)

@@ -87,3 +87,35 @@ def test_mtp_checkpoints(tmp_path):
     keys = set(model_state_dict(m))
     assert "mtp.layers.0.eh_proj.weight" in keys and "mtp.layers.0.final_layernorm.weight" in keys
     assert any(k.startswith("mtp.layers.0.transformer_layer.") for k in keys)
+
+
+def test_mtp_rejected_on_gated_deltanet_hybrid():
+    from miles_b200.models.config import preset
+
+    cfg = dataclasses.replace(preset("tiny-gdn"), mtp_num_layers=1)
+    # MTP depths numbered past the main stack are never linear-attention layers
+    assert not cfg.layer_is_linear(cfg.num_layers)
+    with pytest.raises(ValueError, match="Gated DeltaNet"):
+        _model("tiny-gdn", 1)
+
+
+def test_mtp_kept_when_base_checkpoint_has_none(tmp_path):
+    from miles_b200.checkpoint.hf import load_hf, save_hf
+
+    base = _model("tiny", 0, seed=3)
+    save_hf(base, str(tmp_path))
+    m = _model("tiny", 1, seed=9)
+    before = m.p("layers.%d.eh_proj.weight" % m.cfg.num_layers).clone()
+    with pytest.warns(UserWarning, match="multi-token prediction"):
+        load_hf(m, str(tmp_path))
+    assert torch.equal(m.p("layers.0.mlp.down_proj.weight"), base.p("layers.0.mlp.down_proj.weight"))
+    assert torch.equal(m.p("layers.%d.eh_proj.weight" % m.cfg.num_layers), before)
+
+
+def test_mtp_depth_from_hf_config():
+    from miles_b200.models.config import ModelConfig
+
+    c = ModelConfig.from_hf({"model_type": "qwen3", "vocab_size": 64, "hidden_size": 32,
+                             "num_hidden_layers": 2, "num_attention_heads": 2,
+                             "num_nextn_predict_layers": 2})
+    assert c.extra["num_nextn_predict_layers"] == 2

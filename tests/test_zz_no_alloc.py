@@ -33,6 +33,22 @@ def _lib():
     return f
 
 
+def _err_fn():
+    import miles_b200._C  # noqa: F401
+
+    lib = ctypes.CDLL(glob.glob(os.path.join(ROOT, "miles_b200", "_C*.so"))[0])
+    f = lib.mb_attn_decode_noalloc_error
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
+    return f
+
+
+def _device_error() -> int:
+    code = ctypes.c_int(-1)
+    assert _err_fn()(ctypes.byref(code), torch.cuda.current_stream().cuda_stream) == 0
+    return code.value
+
+
 def _inputs(B, nq, nkv, lens, max_pages, seed=0):
     g = torch.Generator(device="cuda").manual_seed(seed)
     slots = B * max_pages * 64
@@ -63,6 +79,7 @@ def test_noalloc_matches_regular_entry_point():
         err = (out.float() - ref.float()).abs().max() / ref.float().abs().max()
         assert err < 2e-2
         assert torch.equal(out, ref)
+        assert _device_error() == 0  # no bounded wait inside the kernels ran out
 
 
 def test_noalloc_rejects_oversized_workspace():

@@ -27,6 +27,7 @@ from miles_b200.orchestration.setup import (build_actor, build_critic, build_eng
                                             load_tokenizer)
 from miles_b200.rollout.engine_client import LocalEngineClient  # noqa: E402
 from miles_b200.trainer.train_actor import TrainActor  # noqa: E402
+from miles_b200.trainer.lr_scheduler import restore_schedule, schedule_state  # noqa: E402
 from miles_b200.utils.arguments import parse_args  # noqa: E402
 from miles_b200.utils.misc import load_function, should_run_periodic_action  # noqa: E402
 from miles_b200.utils.tracking import Tracker  # noqa: E402
@@ -58,6 +59,7 @@ def setup(args):
     if args.load and is_torch_dist(args.load) and args.train_backend != "fsdp":
         actor._ensure_grads()
         info = load_checkpoint(args.load, model, actor.opt, load_optim=not args.no_load_optim)
+        restore_schedule(actor, info)
         start = info.get("extra", {}).get("rollout_id", info["iteration"]) + 1
         data_source.load(start - 1)
     if args.start_rollout_id is not None:
@@ -108,7 +110,7 @@ def train(args):
         m.update(data["metrics"])
         if (should_run_periodic_action(rollout_id, args.save_interval, num_rollout) and args.save
                 and args.train_backend != "fsdp"):
-            save_checkpoint(args.save, rollout_id, model, actor.opt, extra={"rollout_id": rollout_id},
+            save_checkpoint(args.save, rollout_id, model, actor.opt, extra={"rollout_id": rollout_id, **schedule_state(actor)},
                             save_optim=not args.no_save_optim, async_save=args.async_save)
             data_source.save(rollout_id)
             if args.save_hf:

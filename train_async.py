@@ -42,6 +42,7 @@ from miles_b200.orchestration.setup import (ProcessContext, build_actor, build_e
 from miles_b200.parallel.refit import make_refit  # noqa: E402
 from miles_b200.rollout.engine_client import LocalEngineClient  # noqa: E402
 from miles_b200.trainer.train_actor import TrainActor  # noqa: E402
+from miles_b200.trainer.lr_scheduler import restore_schedule, schedule_state  # noqa: E402
 from miles_b200.utils.arguments import parse_args  # noqa: E402
 from miles_b200.utils.misc import load_function, should_run_periodic_action  # noqa: E402
 from miles_b200.utils.tracking import Tracker  # noqa: E402
@@ -145,7 +146,7 @@ def run_trainer(args, ctx, T, train_gloo, refit_group, data_gloo):
         if should_run_periodic_action(j, args.save_interval, N) and args.save:
             from miles_b200.checkpoint.torch_dist import save_checkpoint
 
-            save_checkpoint(args.save, j, model, actor.opt, extra={"rollout_id": j},
+            save_checkpoint(args.save, j, model, actor.opt, extra={"rollout_id": j, **schedule_state(actor)},
                             save_optim=not args.no_save_optim, process_group=ctx.dp_group)
         tracker.log(m, j)
     tracker.finish()
