@@ -255,3 +255,17 @@ int mb_decode_commit(const int* rows, int B, int spare, const int* tok, const fl
 #ifdef __cplusplus
 }
 #endif
+
+// Virtual-memory arenas (vmm.cu): reserved device address ranges with physical memory mapped in
+// and out (addresses stay fixed across release / resume).
+#ifdef __cplusplus
+extern "C" {
+#endif
+int mb_vmm_granularity(int device, size_t* gran);
+int mb_vmm_reserve(size_t bytes, unsigned long long* ptr);
+int mb_vmm_free(unsigned long long ptr, size_t bytes);
+int mb_vmm_map(unsigned long long ptr, size_t bytes, int device, unsigned long long* handle);
+int mb_vmm_unmap(unsigned long long ptr, size_t bytes, unsigned long long handle);
+#ifdef __cplusplus
+}
+#endif

@@ -563,6 +563,34 @@ int64_t decode_commit(torch::Tensor rows, int64_t spare, torch::Tensor tok, torc
                           PT<int>(s_rec), max_len, cur_stream());
 }
 
+
+// ------------------------------------------------------------------ virtual-memory arenas
+// Status codes are returned first; values follow (ptr / handle as int64).
+std::tuple<int64_t, int64_t> vmm_granularity(int64_t device) {
+  size_t g = 0;
+  const int rc = mb_vmm_granularity((int)device, &g);
+  return {rc, (int64_t)g};
+}
+std::tuple<int64_t, int64_t> vmm_reserve(int64_t bytes) {
+  unsigned long long p = 0;
+  const int rc = mb_vmm_reserve((size_t)bytes, &p);
+  return {rc, (int64_t)p};
+}
+int64_t vmm_free(int64_t ptr, int64_t bytes) { return mb_vmm_free((unsigned long long)ptr, (size_t)bytes); }
+std::tuple<int64_t, int64_t> vmm_map(int64_t ptr, int64_t bytes, int64_t device) {
+  unsigned long long h = 0;
+  const int rc = mb_vmm_map((unsigned long long)ptr, (size_t)bytes, (int)device, &h);
+  return {rc, (int64_t)h};
+}
+int64_t vmm_unmap(int64_t ptr, int64_t bytes, int64_t handle) {
+  return mb_vmm_unmap((unsigned long long)ptr, (size_t)bytes, (unsigned long long)handle);
+}
+// A tensor view of `numel` elements at device address `ptr` (no ownership: the arena owns it).
+torch::Tensor vmm_tensor(int64_t ptr, int64_t numel, at::ScalarType dtype, int64_t device) {
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {numel},
+                          torch::TensorOptions().dtype(dtype).device(torch::kCUDA, (int)device));
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_decode", &mla_decode, "absorbed MLA decode over the paged latent cache");
   m.def("gdn_decode", &gdn_decode, "Gated DeltaNet decode step (state updated in place)");
@@ -623,5 +651,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nonfinite", &nonfinite);
   m.def("adam", &adam);
   m.def("decode_prep", &decode_prep);
+  m.def("vmm_granularity", &vmm_granularity);
+  m.def("vmm_reserve", &vmm_reserve);
+  m.def("vmm_free", &vmm_free);
+  m.def("vmm_map", &vmm_map);
+  m.def("vmm_unmap", &vmm_unmap);
+  m.def("vmm_tensor", &vmm_tensor);
   m.def("decode_commit", &decode_commit);
 }

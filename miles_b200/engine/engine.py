@@ -155,7 +155,7 @@ def _commit_ref(ds: DecodeState, st: dict, tok, lp, experts):
 class RolloutEngine:
     def __init__(self, model: Transformer, max_batch: int = 64, num_pages: int | None = None,
                  mem_fraction: float = 0.9, use_cuda_graph: bool = True, max_pages_per_seq: int = 160,
-                 steps_per_sync: int = 8):
+                 steps_per_sync: int = 8, persistent_kv: bool = True):
         self.model = model
         self.cfg = model.cfg
         self.dev = model.device
@@ -175,6 +175,12 @@ class RolloutEngine:
         self.stats = {}
         self.n_moe = sum(1 for i in range(self.cfg.num_layers) if self.cfg.layer_is_moe(i))
         self.native = _lib.use_native(torch.empty(0, device=self.dev))
+        # fixed-address KV cache: graphs survive release / resume (GPU only)
+        self.use_arena = persistent_kv and self.use_graph and self.native
+        self.arena = None
+        self._arena_pages = 0
+        self._num_pages = 0
+        self._free_pages: list[int] | None = None
 
     # ------------------------------------------------------------------ memory
     def kv_bytes_per_page(self) -> int:
@@ -186,11 +192,18 @@ class RolloutEngine:
 
     def resume_memory(self):
         """Allocate the KV cache and the decode state (graphs are captured lazily). Mirrors
-        resume_memory_occupation."""
+        resume_memory_occupation. On GPUs the cache lives in a fixed-address arena
+        (engine/arena.py): after the first call, resuming maps fresh memory at the same
+        addresses, so decode graphs captured earlier stay valid."""
         if self.cache is not None:
             return
-        self.ds = DecodeState(self.max_batch, self.max_pages_per_seq, self.n_moe,
-                              max(self.cfg.topk, 1), self.dev)
+        if self.ds is None:
+            self.ds = DecodeState(self.max_batch, self.max_pages_per_seq, self.n_moe,
+                                  max(self.cfg.topk, 1), self.dev)
+        kw = dict(dtype=self.model.dtype, tp_size=self.model.tp_size, max_seqs=self.max_batch + 1)
+        if self.arena is not None:
+            self.cache = KVCache(self.cfg, self._arena_pages, self.dev, buffer=self.arena.map(), **kw)
+            return
         n = self._num_pages_req
         if n is None:
             if self.dev.type == "cuda":
@@ -201,17 +214,35 @@ class RolloutEngine:
             else:
                 n = 1024
         n = max(n, 2)
-        self.cache = KVCache(self.cfg, n, self.dev, self.model.dtype, self.model.tp_size,
-                             max_seqs=self.max_batch + 1)
-        self.free_pages = list(range(n - 1, 0, -1))  # page 0 = trash page for padded rows
+        if self.use_arena:
+            from miles_b200.engine.arena import DeviceArena
+
+            self.arena = DeviceArena(KVCache.required_bytes(self.cfg, n, **kw), self.dev)
+            self._arena_pages = n
+            self.cache = KVCache(self.cfg, n, self.dev, buffer=self.arena.map(), **kw)
+        else:
+            self.cache = KVCache(self.cfg, n, self.dev, **kw)
+        self._num_pages = n
+
+    @property
+    def free_pages(self) -> list[int]:
+        if self._free_pages is None:
+            self._free_pages = list(range(self._num_pages - 1, 0, -1))  # page 0 = trash page
+        return self._free_pages
 
     def release_memory(self):
-        """Free KV cache, decode state and graphs (mirrors release_memory_occupation(kv_cache,
-        cuda_graph))."""
-        self.graphs.clear()
-        self.pool = None
+        """Free the KV cache (mirrors release_memory_occupation(kv_cache, cuda_graph)). With the
+        arena its physical memory is unmapped and the decode graphs, their pool and the decode
+        state are kept (they are small and their addresses stay valid); otherwise the graphs
+        go too."""
         self.cache = None
-        self.ds = None
+        self._free_pages = None
+        if self.arena is not None:
+            self.arena.unmap()
+        else:
+            self.graphs.clear()
+            self.pool = None
+            self.ds = None
         if self.dev.type == "cuda":
             torch.cuda.empty_cache()
 

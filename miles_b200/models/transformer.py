@@ -157,27 +157,60 @@ class KVCache:
     they must hold finite values."""
 
     def __init__(self, cfg: ModelConfig, num_pages: int, device, dtype=torch.bfloat16,
-                 tp_size: int = 1, max_seqs: int = 0):
+                 tp_size: int = 1, max_seqs: int = 0, buffer: torch.Tensor | None = None):
+        """buffer: optional flat uint8 device tensor of at least `required_bytes(...)` that
+        backs every cache tensor (e.g. a fixed-address arena); it is zeroed here."""
         self.num_pages = num_pages
+        shapes = self.tensor_shapes(cfg, num_pages, tp_size, max_seqs, dtype)
+        if buffer is not None:
+            buffer.zero_()
+            out, off = [], 0
+            for shape, dt in shapes:
+                n = math.prod(shape) * torch.empty((), dtype=dt).element_size()
+                out.append(buffer[off:off + n].view(dt).view(shape) if n else
+                           torch.zeros(shape, dtype=dt, device=device))
+                off = (off + n + 255) // 256 * 256
+        else:
+            out = [torch.zeros(shape, dtype=dt, device=device) for shape, dt in shapes]
+        L = cfg.num_layers
+        self.k, self.v = out[:L], out[L:2 * L]
+        # linear-attention layers: conv + recurrent state per engine batch slot (fp32)
+        lin = [cfg.layer_is_linear(i) for i in range(L)]
+        rest = iter(out[2 * L:])
+        self.lin_conv, self.lin_state = [None] * L, [None] * L
+        for i in range(L):
+            if lin[i]:
+                self.lin_conv[i], self.lin_state[i] = next(rest), next(rest)
+
+    @staticmethod
+    def tensor_shapes(cfg: ModelConfig, num_pages: int, tp_size: int = 1, max_seqs: int = 0,
+                      dtype=torch.bfloat16) -> list:
+        """[(shape, dtype)] of K per layer, V per layer, then (conv, state) per linear layer."""
         slots = num_pages * PAGE
         nkv, hd = kv_cache_shape(cfg, tp_size)
         lin = [cfg.layer_is_linear(i) for i in range(cfg.num_layers)]
-        self.k = [torch.zeros(0 if lin[i] else slots, nkv, hd, dtype=dtype, device=device)
-                  for i in range(cfg.num_layers)]
+        ks = [((0 if lin[i] else slots, nkv, hd), dtype) for i in range(cfg.num_layers)]
         # MLA caches only the latent (+ rotary key) in `k`
         vs = 1 if cfg.kv_lora_rank else slots
-        self.v = [torch.zeros(0 if lin[i] else vs, nkv, hd, dtype=dtype, device=device)
-                  for i in range(cfg.num_layers)]
-        # linear-attention layers: conv + recurrent state per engine batch slot (fp32)
-        self.lin_conv, self.lin_state = [None] * cfg.num_layers, [None] * cfg.num_layers
+        vv = [((0 if lin[i] else vs, nkv, hd), dtype) for i in range(cfg.num_layers)]
+        extra = []
         if any(lin):
             from miles_b200.models.gdn import gdn_state_shapes
 
             cs, ss = gdn_state_shapes(cfg, tp_size)
             for i in range(cfg.num_layers):
                 if lin[i]:
-                    self.lin_conv[i] = torch.zeros((max_seqs,) + cs, dtype=torch.float32, device=device)
-                    self.lin_state[i] = torch.zeros((max_seqs,) + ss, dtype=torch.float32, device=device)
+                    extra += [((max_seqs,) + cs, torch.float32), ((max_seqs,) + ss, torch.float32)]
+        return ks + vv + extra
+
+    @classmethod
+    def required_bytes(cls, cfg: ModelConfig, num_pages: int, tp_size: int = 1, max_seqs: int = 0,
+                       dtype=torch.bfloat16) -> int:
+        off = 0
+        for shape, dt in cls.tensor_shapes(cfg, num_pages, tp_size, max_seqs, dtype):
+            n = math.prod(shape) * torch.empty((), dtype=dt).element_size()
+            off = (off + n + 255) // 256 * 256
+        return off
 
     def nbytes(self) -> int:
         ts = self.k + self.v + [t for t in self.lin_conv + self.lin_state if t is not None]

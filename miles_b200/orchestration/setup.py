@@ -254,7 +254,10 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                       logprob_chunk=args.log_probs_chunk_size if args.log_probs_chunk_size > 0 else 4096,
                       mtp_loss_scale=(args.mtp_loss_scaling_factor
                                       if getattr(args, "enable_mtp_training", False) else 0.0),
-                      adam_eps=args.adam_eps, lr_schedule=schedule_from_args(args))
+                      adam_eps=args.adam_eps, lr_schedule=schedule_from_args(args),
+                      micro_batching="balanced" if args.use_dynamic_batch_size else "fixed",
+                      micro_batch_size=args.micro_batch_size,
+                      log_probs_max_tokens_per_gpu=args.log_probs_max_tokens_per_gpu)
     if getattr(args, "train_backend", "b200") == "fsdp":
         # HF model under FSDP2 (trainer/fsdp_actor.py); `model` is then the engine's Transformer,
         # refreshed from the gathered HF state after every step
@@ -308,7 +311,9 @@ def build_critic(args, ctx: ProcessContext):
                        weight_decay=args.weight_decay, clip_grad=args.clip_grad,
                        max_tokens_per_gpu=args.max_tokens_per_gpu or 16384,
                        grad_dtype=torch.float32 if ctx.device.type != "cuda" else torch.bfloat16,
-                       optimizer_placement="host" if args.optimizer_cpu_offload else "auto")
+                       optimizer_placement="host" if args.optimizer_cpu_offload else "auto",
+                       micro_batching="balanced" if args.use_dynamic_batch_size else "fixed",
+                       micro_batch_size=args.micro_batch_size)
     return Critic(body, acfg, value_clip=args.value_clip, dp_group=ctx.dp_group)
 
 

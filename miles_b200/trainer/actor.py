@@ -70,6 +70,12 @@ class ActorConfig:
     optimizer_placement: str = "auto"
     logprob_chunk: int = 4096
     adam_eps: float = 1e-8
+    # micro-batching: "ffd" (first-fit decreasing under max_tokens_per_gpu), "balanced"
+    # (--use-dynamic-batch-size: fewest micro-batches under the budget, Karmarkar-Karp balanced
+    # token totals) or "fixed" (--micro-batch-size samples per micro-batch, in order)
+    micro_batching: str = "ffd"
+    micro_batch_size: int = 1
+    log_probs_max_tokens_per_gpu: int | None = None
     lr_schedule: "LRSchedule | None" = None   # None: constant `lr`
 
 
@@ -89,6 +95,19 @@ def pack_microbatches(lengths: list[int], max_tokens: int) -> list[list[int]]:
             bins.append([i])
             loads.append(L)
     return [sorted(b) for b in bins]
+
+
+def make_micro_batches(lengths: list[int], cfg: "ActorConfig", budget: int | None = None) -> list[list[int]]:
+    """Micro-batches (lists of sample indices) under the configured policy."""
+    budget = budget or cfg.max_tokens_per_gpu
+    if cfg.micro_batching == "balanced":
+        from miles_b200.utils.seqlen_balancing import balanced_micro_batches
+
+        return balanced_micro_batches(lengths, budget)
+    if cfg.micro_batching == "fixed":
+        m = max(1, cfg.micro_batch_size)
+        return [list(range(i, min(i + m, len(lengths)))) for i in range(0, len(lengths), m)]
+    return pack_microbatches(lengths, budget)
 
 
 def _seg_mean(x: torch.Tensor, mask: torch.Tensor, seg: torch.Tensor, nseq: int) -> torch.Tensor:
@@ -214,7 +233,8 @@ class Actor:
         out: list[np.ndarray | None] = [None] * len(items)
         if self.model.pp is not None:
             return self._logprobs_pp(items)
-        for mb in pack_microbatches([len(it.tokens) for it in items], self.cfg.max_tokens_per_gpu):
+        for mb in make_micro_batches([len(it.tokens) for it in items], self.cfg,
+                                     self.cfg.log_probs_max_tokens_per_gpu):
             sub = [items[i] for i in mb]
             tok, meta, sel, tgt = self._mb_inputs(sub)
             lp, _ = self.model.selected_logprob(tok, meta, sel, tgt, self.cfg.temperature,
@@ -233,7 +253,7 @@ class Actor:
         from miles_b200.parallel.pp import run_forward_only, run_interleaved
 
         model, cfg = self.model, self.cfg
-        mbs = pack_microbatches([len(it.tokens) for it in items], cfg.max_tokens_per_gpu)
+        mbs = make_micro_batches([len(it.tokens) for it in items], cfg, cfg.log_probs_max_tokens_per_gpu)
         subs = [[items[i] for i in mb] for mb in mbs]
         ins = [self._mb_inputs(sub) for sub in subs]
         shapes = [(x[0].shape[0], model.cfg.hidden_size) for x in ins]
@@ -278,7 +298,7 @@ class Actor:
         n_tokens = global_num_tokens or sum(
             (sum(it.loss_mask) if it.loss_mask is not None else it.resp_len) for it in items)
         metrics = torch.zeros(len(METRIC_NAMES) + 1, dtype=torch.float64, device=self.dev)
-        mbs = pack_microbatches([len(it.tokens) for it in items], cfg.max_tokens_per_gpu)
+        mbs = make_micro_batches([len(it.tokens) for it in items], cfg)
         mtp_total = torch.zeros((), dtype=torch.float32, device=self.dev)
         if model.pp is not None:
             self._train_pp(items, mbs, n_samples, n_tokens, metrics)

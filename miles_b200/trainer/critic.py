@@ -18,7 +18,7 @@ import torch
 import torch.distributed as dist
 
 from miles_b200.models.transformer import Transformer
-from miles_b200.trainer.actor import Actor, ActorConfig, TrainItem, pack_microbatches
+from miles_b200.trainer.actor import Actor, ActorConfig, TrainItem, make_micro_batches
 
 
 class Critic:
@@ -41,7 +41,7 @@ class Critic:
     @torch.no_grad()
     def values(self, items: list[TrainItem]) -> list[np.ndarray]:
         out: list[np.ndarray | None] = [None] * len(items)
-        for mb in pack_microbatches([len(it.tokens) for it in items], self.cfg.max_tokens_per_gpu):
+        for mb in make_micro_batches([len(it.tokens) for it in items], self.cfg):
             sub = [items[i] for i in mb]
             v = self._values_of(sub).cpu().numpy()
             o = 0
@@ -60,7 +60,7 @@ class Critic:
         n_samples = global_num_samples or len(items)
         c = self.value_clip
         tot = {"value_loss": 0.0, "value_clipfrac": 0.0}
-        for mb in pack_microbatches([len(it.tokens) for it in items], self.cfg.max_tokens_per_gpu):
+        for mb in make_micro_batches([len(it.tokens) for it in items], self.cfg):
             sub = [items[i] for i in mb]
             T = lambda xs: torch.from_numpy(np.concatenate(xs).astype(np.float32)).to(self.model.device)
             R = T([returns[i] for i in mb])

@@ -29,7 +29,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from miles_b200.ops.rl import METRIC_NAMES
-from miles_b200.trainer.actor import Actor, ActorConfig, TrainItem, pack_microbatches
+from miles_b200.trainer.actor import Actor, ActorConfig, TrainItem, make_micro_batches
 
 
 class FSDPActor(Actor):
@@ -99,7 +99,7 @@ class FSDPActor(Actor):
         n_tokens = global_num_tokens or sum(
             (sum(it.loss_mask) if it.loss_mask is not None else it.resp_len) for it in items)
         metrics = torch.zeros(len(METRIC_NAMES) + 1, dtype=torch.float64, device=self.dev)
-        mbs = pack_microbatches([len(it.tokens) for it in items], cfg.max_tokens_per_gpu)
+        mbs = make_micro_batches([len(it.tokens) for it in items], cfg)
         for mb in mbs:
             for i in mb:
                 prep = self._mb_prepare([items[i]], n_samples, n_tokens)

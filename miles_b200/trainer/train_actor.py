@@ -70,9 +70,48 @@ class TrainActor:
         self.metrics: dict = {}
 
     def init_ref(self):
-        """The reference policy is the initial weights (or --ref-load, loaded by the caller)."""
+        """Reference policy for the KL terms: the weights of --ref-load (torch_dist iteration
+        --ref-ckpt-step, or an HF directory) when given, else the initial weights. With
+        --keep-old-actor the initial weights also seed the old-actor / rollout-actor queue
+        (reference megatron_utils/actor.py:151-156, :543-552)."""
+        a = self.args
         if self.need_ref:
+            ref_load = getattr(a, "ref_load", None)
+            if ref_load:
+                self.backuper.backup("actor")
+                self._load_weights(ref_load, getattr(a, "ref_ckpt_step", None))
+                self.backuper.backup("ref")
+                self.backuper.restore("actor")
+            else:
+                self.backuper.backup("ref")
+        if getattr(a, "keep_old_actor", False):
+            self.backuper.backup("old_actor")
+            self.backuper.backup("rollout_actor")
+
+    def _load_weights(self, path: str, step: int | None):
+        from miles_b200.checkpoint.torch_dist import is_torch_dist, load_checkpoint
+
+        if is_torch_dist(path):
+            load_checkpoint(path, self.model, None, load_optim=False, iteration=step)
+        else:
+            from miles_b200.checkpoint.hf import load_hf
+
+            load_hf(self.model, path)
+
+    def after_update(self, rollout_id: int):
+        """Weight bookkeeping after the policy update of `rollout_id`: refresh the reference
+        policy every --ref-update-interval rollouts, and advance the --keep-old-actor queue
+        (the weights that generated the next rollout become the old actor of its training)."""
+        a = self.args
+        iv = getattr(a, "ref_update_interval", None)
+        if self.need_ref and iv and (rollout_id + 1) % iv == 0:
             self.backuper.backup("ref")
+        if getattr(a, "keep_old_actor", False):
+            if (getattr(a, "update_weights_interval", 1) or 1) == 1:
+                self.backuper.backups["old_actor"].copy_(self.backuper.backups["rollout_actor"])
+                self.backuper.backup("rollout_actor")
+            else:
+                self.backuper.backup("old_actor")
 
     def _switch(self, tag: str):
         self.backuper.backup("actor")
@@ -81,10 +120,22 @@ class TrainActor:
     def train(self, rollout_id: int, data: dict) -> dict:
         a = self.args
         t0 = time.perf_counter()
+        if (getattr(a, "balance_data", False) and self.dp_group is not None
+                and torch.distributed.get_world_size(self.dp_group) > 1):
+            if getattr(self.model, "cp", None) is not None:
+                raise ValueError("--balance-data is not supported with context parallelism")
+            from miles_b200.utils.seqlen_balancing import rebalance_over_dp
+
+            data = rebalance_over_dp(data, self.dp_group)
         items = data_to_items(data)
         old = None
         if not a.use_rollout_logprobs:
+            old_actor = getattr(a, "keep_old_actor", False) and "old_actor" in self.backuper.backups
+            if old_actor:  # old log-probs under the weights that generated this rollout
+                self._switch("old_actor")
             old = self.actor.compute_logprobs(items)
+            if old_actor:
+                self.backuper.restore("actor")
             for it, o in zip(items, old):
                 it.old_logp = o
         t1 = time.perf_counter()

@@ -19,3 +19,13 @@ def pytest_collection_modifyitems(config, items):
     for it in items:
         if "gpu" in it.keywords:
             it.add_marker(skip)
+
+
+def free_port() -> int:
+    """A TCP port on 127.0.0.1 that is free right now (for gloo rendezvous in spawned ranks;
+    hard-coded ports collide when tests run in parallel)."""
+    import socket
+
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]

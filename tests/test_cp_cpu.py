@@ -11,6 +11,7 @@ import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+from tests.conftest import free_port
 
 os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -62,7 +63,7 @@ def test_cp2_matches_single(tmp_path, name, port):
     lp, ent = m.selected_logprob(toks, meta, sel, tgt, 1.0, 4096)
     (lp.sum() + 0.1 * ent.sum()).backward()
     out = str(tmp_path / "cp.pt")
-    mp.spawn(_run, args=(2, port, name, out), nprocs=2, join=True)
+    mp.spawn(_run, args=(2, free_port(), name, out), nprocs=2, join=True)
     r = torch.load(out)
     assert torch.allclose(r["lp"], lp.detach(), atol=1e-5), (r["lp"] - lp).abs().max()
     assert torch.allclose(r["ent"], ent.detach(), atol=1e-5)
@@ -84,7 +85,7 @@ def test_train_cp2(tmp_path):
             f.write(json.dumps({"input": rng.integers(0, 4096, 64).tolist(), "label": "1"}) + "\n")
     env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", "29637", os.path.join(ROOT, "train.py"),
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()), os.path.join(ROOT, "train.py"),
            "--model-name", "tiny", "--prompt-data", str(tmp_path / "d.jsonl"), "--label-key", "label",
            "--rollout-batch-size", "4", "--n-samples-per-prompt", "4", "--rollout-max-response-len", "16",
            "--rm-type", "random", "--num-rollout", "1", "--lr", "1e-3", "--max-tokens-per-gpu", "1024",

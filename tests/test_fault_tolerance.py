@@ -7,6 +7,8 @@ import time
 
 import pytest
 
+from tests.conftest import free_port
+
 from miles_b200.utils.health_monitor import RankFailure, RankHeartbeat, RolloutHealthMonitor
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -82,6 +84,6 @@ def test_rank_departure_detected(tmp_path):
     p.write_text(WORKER)
     env = dict(os.environ, ROOT=ROOT)
     r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-                        "--master-addr", "127.0.0.1", "--master-port", "29631", str(p)],
+                        "--master-addr", "127.0.0.1", "--master-port", str(free_port()), str(p)],
                        env=env, capture_output=True, text=True, timeout=110)
     assert "DETECTED rank 1 left the job" in r.stdout, r.stdout + r.stderr[-2000:]

@@ -8,6 +8,7 @@ import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+from tests.conftest import free_port
 
 os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
 pytest.importorskip("transformers")
@@ -73,7 +74,7 @@ def test_fsdp2_step_matches_single_process(tmp_path):
     m1 = _step(single, _items(), 4)
     ref = single.export_hf_state()
     out = str(tmp_path / "r.pt")
-    mp.spawn(_rank, args=(29711, ckpt, out), nprocs=2, join=True)
+    mp.spawn(_rank, args=(free_port(), ckpt, out), nprocs=2, join=True)
     r = torch.load(out)
     assert abs(r["metrics"]["grad_norm"] - m1["grad_norm"]) < 1e-4 * max(1.0, m1["grad_norm"])
     for k, v in ref.items():
@@ -110,7 +111,7 @@ def test_train_fsdp_backend(tmp_path):
             f.write(json.dumps({"input": rng.integers(0, 256, 12).tolist(), "label": "1"}) + "\n")
     env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=root, OMP_NUM_THREADS="2")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", "29657", os.path.join(root, "train.py"),
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()), os.path.join(root, "train.py"),
            "--hf-checkpoint", str(tmp_path / "hf"), "--train-backend", "fsdp",
            "--prompt-data", str(tmp_path / "d.jsonl"), "--label-key", "label",
            "--rollout-batch-size", "2", "--n-samples-per-prompt", "2", "--rollout-max-response-len", "8",

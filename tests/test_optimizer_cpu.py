@@ -6,6 +6,7 @@ import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+from tests.conftest import free_port
 
 
 def _init_params(n):
@@ -45,7 +46,7 @@ def test_sharded_adam_matches_unsharded(tmp_path):
 
     n, world = 8192 * 2, 2
     out = str(tmp_path / "r0.pt")
-    mp.spawn(_worker, args=(world, 29631, n, out), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, free_port(), n, out), nprocs=world, join=True)
     r0 = torch.load(out)
     r1 = torch.load(out + ".1")
     assert torch.equal(r0["p"], r1["p"])  # every rank holds the gathered parameters

@@ -13,6 +13,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from tests.conftest import free_port
+
 os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
 
 
@@ -107,7 +109,7 @@ def test_layouts_match_single(tmp_path, layout, world, port):
     met = a.train_step(_items(cfg))
     ref = {k: v.detach().clone() for k, v in to_hf_tensors(m)}
     out = str(tmp_path / "out")
-    mp.spawn(_run, args=(world, port, layout, ckpt, out, variant), nprocs=world, join=True)
+    mp.spawn(_run, args=(world, free_port(), layout, ckpt, out, variant), nprocs=world, join=True)
     import json
 
     wm = json.load(open(os.path.join(out, "model.safetensors.index.json")))["weight_map"]

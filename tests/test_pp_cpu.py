@@ -12,6 +12,7 @@ import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+from tests.conftest import free_port
 
 os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -76,7 +77,7 @@ def test_pp_matches_single(tmp_path, name, world, port):
     save_hf(m, ckpt)
     old1, met1 = _step(m, cfg)
     out = str(tmp_path / "pp")
-    mp.spawn(_run, args=(world, port, name, ckpt, out), nprocs=world, join=True)
+    mp.spawn(_run, args=(world, free_port(), name, ckpt, out), nprocs=world, join=True)
     seen = set()
     for r in range(world):
         res = torch.load(f"{out}.{r}", weights_only=False)
@@ -99,7 +100,7 @@ def test_train_pp2(tmp_path):
             f.write(json.dumps({"input": rng.integers(0, 4096, 64).tolist(), "label": "1"}) + "\n")
     env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", "29647", os.path.join(ROOT, "train.py"),
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()), os.path.join(ROOT, "train.py"),
            "--model-name", "tiny", "--prompt-data", str(tmp_path / "d.jsonl"), "--label-key", "label",
            "--rollout-batch-size", "4", "--n-samples-per-prompt", "4", "--rollout-max-response-len", "16",
            "--rm-type", "random", "--num-rollout", "2", "--lr", "1e-3", "--max-tokens-per-gpu", "128",
@@ -178,7 +179,7 @@ def test_interleaved_pp_matches_single(tmp_path, name, world, vpp, port, first, 
     save_hf(m, ckpt)
     old1, met1 = _step(m, cfg)
     out = str(tmp_path / "vpp")
-    mp.spawn(_run_vpp, args=(world, port, name, ckpt, out, vpp, first, last), nprocs=world, join=True)
+    mp.spawn(_run_vpp, args=(world, free_port(), name, ckpt, out, vpp, first, last), nprocs=world, join=True)
     seen = set()
     for r in range(world):
         res = torch.load(f"{out}.{r}", weights_only=False)

@@ -9,6 +9,7 @@ import numpy as np
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+from tests.conftest import free_port
 
 os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
 
@@ -49,8 +50,8 @@ def _run(rank, world, port, reload, out):
 
 def test_reload_groups_between_steps(tmp_path):
     a, b = str(tmp_path / "keep"), str(tmp_path / "reload")
-    mp.spawn(_run, args=(4, 29713, False, a), nprocs=4, join=True)
-    mp.spawn(_run, args=(4, 29714, True, b), nprocs=4, join=True)
+    mp.spawn(_run, args=(4, free_port(), False, a), nprocs=4, join=True)
+    mp.spawn(_run, args=(4, free_port(), True, b), nprocs=4, join=True)
     for r in range(4):
         pa, pb = torch.load(f"{a}.{r}"), torch.load(f"{b}.{r}")
         for k in pa:

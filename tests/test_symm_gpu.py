@@ -14,6 +14,7 @@ import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+from tests.conftest import free_port
 
 pytestmark = pytest.mark.gpu
 
@@ -23,7 +24,7 @@ def one_rank_group():
     """A one-rank process group (torn down afterwards so later tests can create their own)."""
     created = not dist.is_initialized()
     if created:
-        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29691", rank=0, world_size=1)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{free_port()}", rank=0, world_size=1)
     yield dist.group.WORLD
     if created:
         dist.destroy_process_group()
@@ -255,7 +256,7 @@ def _two_rank(rank, port, out):
 def test_symm_two_ranks(tmp_path):
     out = str(tmp_path / "r.pt")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    mp.spawn(_two_rank, args=(29693, out), nprocs=2, join=True)
+    mp.spawn(_two_rank, args=(free_port(), out), nprocs=2, join=True)
     r = torch.load(out)
     print({k: v for k, v in r.items() if k != "tokens"})
     assert r["ok"]
@@ -301,7 +302,7 @@ def _two_rank_refit(rank, port, out):
 def test_peer_refit_matches_nccl_refit(tmp_path):
     out = str(tmp_path / "refit.pt")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    mp.spawn(_two_rank_refit, args=(29695, out), nprocs=2, join=True)
+    mp.spawn(_two_rank_refit, args=(free_port(), out), nprocs=2, join=True)
     r = torch.load(out)
     print(r)
     assert r["bf16_equal"] and r["fp8_equal"] and r["bf16_nonzero"]
@@ -353,7 +354,7 @@ def _two_rank_ep(rank, port, out):
 def test_ep_peer_transport_matches_nccl(tmp_path):
     out = str(tmp_path / "ep.pt")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    mp.spawn(_two_rank_ep, args=(29697, out), nprocs=2, join=True)
+    mp.spawn(_two_rank_ep, args=(free_port(), out), nprocs=2, join=True)
     r = torch.load(out)
     print(r)
     assert r["fwd_equal"] and r["grad_equal"] and r["nograd_equal"]

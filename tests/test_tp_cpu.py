@@ -9,6 +9,7 @@ import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+from tests.conftest import free_port
 
 os.environ.setdefault("MILES_B200_FORCE_CPU", "1")
 
@@ -162,7 +163,7 @@ def test_tp2_matches_tp1(tmp_path, preset_name, port):
 
     ckpt = str(tmp_path / "ref")
     m1, h1, outs1 = _single(preset_name, ckpt)
-    mp.spawn(_run, args=(2, port, preset_name, ckpt, str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_run, args=(2, free_port(), preset_name, ckpt, str(tmp_path)), nprocs=2, join=True)
     r = torch.load(tmp_path / "tp2.pt")
     assert torch.allclose(r["h"], h1, atol=2e-5, rtol=1e-4), (r["h"] - h1).abs().max()
     # gradients: rank 0 holds slice 0 of sharded tensors, full replicated ones
@@ -239,7 +240,7 @@ def test_vocab_parallel_logprob(tmp_path):
     """TP2 log-probs / entropies with the vocabulary split over the ranks equal the replicated
     LM head's, and so do all gradients (LM head rows all-reduced)."""
     out = str(tmp_path / "vp.pt")
-    mp.spawn(_run_vp, args=(2, 29675, out), nprocs=2, join=True)
+    mp.spawn(_run_vp, args=(2, free_port(), out), nprocs=2, join=True)
     r = torch.load(out)
     (lp0, e0, g0), (lp1, e1, g1) = r[False], r[True]
     assert torch.allclose(lp0, lp1, atol=1e-5) and torch.allclose(e0, e1, atol=1e-5)

@@ -7,6 +7,7 @@ import sys
 
 import numpy as np
 import pytest
+from tests.conftest import free_port
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -50,7 +51,7 @@ def test_train_gloo_world2(tmp_path):
     _dataset(tmp_path / "d.jsonl")
     env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", "29617", os.path.join(ROOT, "train.py"),
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()), os.path.join(ROOT, "train.py"),
            *_argv(tmp_path, ["--actor-num-gpus-per-node", "2", "--num-rollout", "1"])]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=580)
     assert r.returncode == 0, r.stderr[-3000:]
@@ -63,7 +64,7 @@ def test_train_tp2(tmp_path):
     _dataset(tmp_path / "d.jsonl")
     env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
     base = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-            "--master-addr", "127.0.0.1", "--master-port", "29627", os.path.join(ROOT, "train.py")]
+            "--master-addr", "127.0.0.1", "--master-port", str(free_port()), os.path.join(ROOT, "train.py")]
     tp = ["--actor-num-gpus-per-node", "2", "--tensor-model-parallel-size", "2"]
     r = subprocess.run(base + _argv(tmp_path, tp), env=env, capture_output=True, text=True, timeout=400)
     assert r.returncode == 0, r.stderr[-3000:]
@@ -90,14 +91,14 @@ def _async_run(tmp_path, extra, port):
 @pytest.mark.timeout(600)
 def test_train_async_disaggregated(tmp_path):
     """1 trainer + 1 rollout rank: one-step-ahead pipeline with bf16 broadcast refits."""
-    _async_run(tmp_path, [], 29641)
+    _async_run(tmp_path, [], free_port())
 
 
 @pytest.mark.timeout(600)
 def test_train_async_fully_async_fp8_refit(tmp_path):
     """Continuous generation worker (partial rollout, staleness filter) and fp8 refits."""
     _async_run(tmp_path, ["--fully-async", "--partial-rollout", "--max-weight-staleness", "4",
-                          "--update-weight-quant", "fp8"], 29643)
+                          "--update-weight-quant", "fp8"], free_port())
 
 
 def test_train_ppo_with_critic(tmp_path, monkeypatch):

@@ -96,6 +96,7 @@ def train(args):
             continue
         profiler.start("train_overall")
         m = trainer.train(rollout_id, data)
+        trainer.after_update(rollout_id)
         if args.train_backend == "fsdp":  # HF policy under FSDP2 -> the engine's Transformer
             from miles_b200.checkpoint.hf import load_hf_tensors
 

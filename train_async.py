@@ -136,6 +136,7 @@ def run_trainer(args, ctx, T, train_gloo, refit_group, data_gloo):
     data = recv()
     for j in range(start, N):
         m = trainer.train(j, data)
+        trainer.after_update(j)
         m.update(data.get("metrics", {}))
         if j + 1 < N:
             data = recv()
