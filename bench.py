@@ -10,6 +10,12 @@ Rollout Routing Replay (routing recorded in rollout, replayed in training), Adam
 At N GPUs the global batch is N x 64 samples (N x 8 prompts), i.e. the headline workload's
 64 prompts x 8 samples at N = 8.
 
+Rollout (default): the reference's partial rollout with 2x over-sampling (--partial-rollout,
+--over-sampling-batch-size): 16 groups per GPU are in flight, each step trains the first 8 that
+complete, and the others keep their partial responses for the next step. Every trained sample
+is generated to its full sampled length; in steady state each step generates as many tokens as
+it trains. `--partial-rollout 0` generates every step's 8 groups to the end instead.
+
 Timing: W untimed warm-up steps, then K steps bracketed by barrier + synchronize, device-timed
 with CUDA events; the max over ranks is reported. Inputs are larger than L2 every step (the
 model itself is ~61 GB). `e2e` times the same public API call (ColocatedRL.step) on the host
@@ -43,6 +49,12 @@ def parse():
     ap.add_argument("--resp-max", type=int, default=8192)
     ap.add_argument("--max-tokens-per-gpu", type=int, default=16384)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--partial-rollout", type=int, default=1,
+                    help="1: reference --partial-rollout with over-sampling (unfinished groups "
+                         "continue next step); 0: every step generates its groups to the end")
+    ap.add_argument("--over-sampling", type=int, default=2,
+                    help="groups in flight per trained group under partial rollout")
+    ap.add_argument("--steps-per-sync", type=int, default=8)
     return ap.parse_args()
 
 
@@ -161,8 +173,9 @@ def main():
 
     cfg = preset(args.model)
     model = Transformer(cfg, device=dev, seed=1234)
-    engine = RolloutEngine(model, max_batch=args.prompts_per_gpu * args.samples_per_prompt,
-                           use_cuda_graph=not args.no_graph,
+    inflight = args.prompts_per_gpu * (args.over_sampling if args.partial_rollout else 1)
+    engine = RolloutEngine(model, max_batch=inflight * args.samples_per_prompt,
+                           use_cuda_graph=not args.no_graph, steps_per_sync=args.steps_per_sync,
                            max_pages_per_seq=(args.prompt_len + args.resp_max + 63) // 64 + 1)
     acfg = ActorConfig(lr=1e-6, max_tokens_per_gpu=args.max_tokens_per_gpu,
                        loss=PolicyLossCfg(eps_clip=0.2, eps_clip_high=0.2, use_tis=True,
@@ -170,16 +183,22 @@ def main():
                        use_routing_replay=cfg.is_moe)
     actor = Actor(model, acfg, dp_group=group)
     rl = ColocatedRL(engine, actor, RLConfig(n_samples_per_prompt=args.samples_per_prompt,
-                                             routing_replay=cfg.is_moe, seed=rank))
+                                             routing_replay=cfg.is_moe, seed=rank,
+                                             partial_rollout=bool(args.partial_rollout),
+                                             groups_per_step=args.prompts_per_gpu,
+                                             over_sampling=args.over_sampling))
     rng = np.random.default_rng(1000 + rank)
     nsamp = args.prompts_per_gpu * args.samples_per_prompt
 
     def workload():
-        prompts = [rng.integers(0, cfg.vocab_size, args.prompt_len).tolist()
-                   for _ in range(args.prompts_per_gpu)]
-        lens = rng.integers(args.resp_min, args.resp_max + 1, nsamp).tolist()
-        rewards = (rng.random(nsamp) < 0.5).astype(np.float32).tolist()
-        return prompts, lens, rewards
+        """This step's fresh prompt groups (in pinned host memory, copied to the device by the
+        step), their sampled response lengths and Bernoulli(0.5) rewards."""
+        k = rl.prompts_needed() if args.partial_rollout else args.prompts_per_gpu
+        n = k * args.samples_per_prompt
+        prompts = torch.from_numpy(rng.integers(0, cfg.vocab_size, (k, args.prompt_len)).astype(np.int32))
+        lens = rng.integers(args.resp_min, args.resp_max + 1, n).tolist()
+        rewards = (rng.random(n) < 0.5).astype(np.float32).tolist()
+        return prompts.pin_memory(), lens, rewards
 
     def barrier():
         if world > 1:
@@ -195,7 +214,7 @@ def main():
 
     for i in range(args.warmup):
         prompts, lens, rewards = workload()
-        progress(f"warmup {i}", rl.step(prompts, lens, rewards))
+        progress(f"warmup {i}", rl.step(prompts.to(dev, non_blocking=True), lens, rewards))
     barrier()
     sampler = ClockSampler(local)
     sampler.start()
@@ -206,9 +225,14 @@ def main():
     rollout_s = train_s = lp_s = 0.0
     t_host0 = time.perf_counter()
     ev0.record()
+    h2d = d2h = 0
     for _ in range(args.steps):
         prompts, lens, rewards = workload()
-        m = rl.step(prompts, lens, rewards)
+        # host -> device: this step's prompt ids from pinned memory; device -> host inside the
+        # step: generated tokens / log-probs / routing and the step's metrics
+        m = rl.step(prompts.to(dev, non_blocking=True), lens, rewards)
+        h2d += prompts.numel() * prompts.element_size()
+        d2h += int(m.get("rollout/generated_tokens", 0)) * 8 + 8 * len(m)
         progress("timed", m)
         tokens += m["tokens_total"]
         resp += m["response_tokens"]
@@ -233,8 +257,8 @@ def main():
     step_s = ms / 1e3
     value = tokens / args.steps / step_s
     if rank == 0:
-        h2d = args.prompts_per_gpu * args.prompt_len * 4 * world
-        d2h = int(resp / args.steps) * 8 + 8 * 8
+        h2d = h2d // args.steps * world
+        d2h = d2h // args.steps * world
         out = {
             "metric": METRIC,
             "value": value,
@@ -249,6 +273,11 @@ def main():
                        "prompt_len": args.prompt_len, "response_len": [args.resp_min, args.resp_max],
                        "parallelism": f"dp{world}" if world > 1 else "dp1",
                        "routing_replay": cfg.is_moe, "tis_cap": 2.0,
+                       "rollout": ({"partial_rollout": True, "over_sampling": args.over_sampling,
+                                    "note": "reference --partial-rollout: each step trains the first "
+                                            f"{args.prompts_per_gpu} complete groups per GPU; unfinished "
+                                            "groups continue next step (TIS corrects the off-policy tokens)"}
+                                   if args.partial_rollout else {"partial_rollout": False}),
                        "l2": "inputs larger than L2 (61 GB of weights streamed every step)"},
             "grpo_step_s": step_s,
             "rollout_tok_s": resp / args.steps / (rollout_s / args.steps),

@@ -330,11 +330,15 @@ class RolloutEngine:
     def abort(self):
         self.aborted = True
 
-    def generate(self, reqs: list[GenRequest]) -> list[GenResult]:
+    def generate(self, reqs: list[GenRequest], stop_when=None) -> list[GenResult]:
         """Continuous batching with the decode loop on the device: requests are admitted whenever
         a slot and enough KV pages are free (prefilled as a packed batch; their slots join the
         running batch), the batch runs `steps_per_sync` decode steps per host visit (finished
-        sequences freeze on the device), and finished sequences leave at the next visit."""
+        sequences freeze on the device), and finished sequences leave at the next visit.
+
+        stop_when(results): checked at every host visit with the finished results so far (rid ->
+        GenResult); when it returns True the call aborts the rest (partial rollout: unfinished
+        sequences return their tokens so far with finish_reason "abort")."""
         self.resume_memory()
         ds = self.ds
         if self.n_moe and any(r.return_routed_experts for r in reqs):
@@ -388,6 +392,8 @@ class RolloutEngine:
                     results[sq.req.rid] = self._result(sq, int(nout[sl]))
                     self.free_pages.extend(sq.pages)
                     free_slots.append(sl)
+            if stop_when is not None and stop_when(results):
+                self.aborted = True
         if self.aborted:
             done, nout = self._read_flags()
             for sl, sq in list(live.items()):

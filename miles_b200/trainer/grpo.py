@@ -34,6 +34,14 @@ class RLConfig:
     check_logprob_parity: bool = True
     eos_token_id: int | None = None
     seed: int = 0
+    # partial rollout (reference --partial-rollout with --over-sampling-batch-size): the rollout
+    # stops once `groups_per_step` groups are complete; unfinished groups keep their tokens,
+    # log-probs and routing and continue in the next step's rollout (re-prefilled under the new
+    # weights, like the reference's SGLang engines). The caller keeps `groups_per_step *
+    # over_sampling` groups in flight by feeding `prompts_needed()` fresh prompts per step.
+    partial_rollout: bool = False
+    groups_per_step: int | None = None
+    over_sampling: int = 1
 
 
 class ColocatedRL:
@@ -44,41 +52,108 @@ class ColocatedRL:
         self.reward_fn = reward_fn
         self.rollout_id = 0
         self.last_metrics: dict = {}
+        self.buffer: list[list[Sample]] = []   # unfinished groups (partial rollout)
+        self._next_uid = 0
+        self._next_group = 0
+        self.generated_tokens = 0
 
-    def generate(self, prompts: list[list[int]], max_new: list[int] | None = None) -> list[Sample]:
+    def prompts_needed(self) -> int:
+        """Fresh prompt groups the next step() wants (partial rollout keeps the in-flight count
+        at groups_per_step * over_sampling; without it, whatever the caller passes)."""
+        if not self.cfg.partial_rollout:
+            return self.cfg.groups_per_step or 0
+        return self.cfg.groups_per_step * self.cfg.over_sampling - len(self.buffer)
+
+    def _new_groups(self, prompts, max_new, rewards):
         cfg = self.cfg
-        reqs = []
-        samples = []
+        groups = []
         for gi, p in enumerate(prompts):
+            g = []
             for j in range(cfg.n_samples_per_prompt):
                 idx = gi * cfg.n_samples_per_prompt + j
-                mn = max_new[idx] if max_new is not None else cfg.max_new_tokens
-                reqs.append(GenRequest(prompt=list(p), max_new_tokens=mn,
-                                       temperature=cfg.temperature,
-                                       seed=(cfg.seed * 1_000_003 + self.rollout_id * 65_537 + idx),
+                uid = self._next_uid
+                self._next_uid += 1
+                s = Sample(group_index=self._next_group, index=uid, tokens=list(p),
+                           response_length=0, loss_mask=[], rollout_log_probs=[])
+                s.metadata = {"prompt_len": len(p),
+                              "max_new": max_new[idx] if max_new is not None else cfg.max_new_tokens,
+                              "reward": None if rewards is None else float(rewards[idx]),
+                              "seed": cfg.seed * 1_000_003 + self.rollout_id * 65_537 + idx}
+                g.append(s)
+            self._next_group += 1
+            groups.append(g)
+        return groups
+
+    def generate(self, prompts: list[list[int]], max_new: list[int] | None = None,
+                 rewards: list[float] | None = None) -> list[Sample]:
+        """Roll out the fresh prompt groups (and, with partial rollout, the buffered unfinished
+        groups first). Returns the samples of the groups to train on this step."""
+        cfg = self.cfg
+        groups = self.buffer + self._new_groups(prompts, max_new, rewards)
+        self.buffer = []
+        reqs, owner = [], {}
+        for g in groups:
+            for s in g:
+                md = s.metadata
+                left = md["max_new"] - s.response_length
+                if left <= 0 or md.get("finished"):
+                    continue
+                if s.response_length:
+                    md["resumed"] = md.get("resumed", 0) + 1
+                reqs.append(GenRequest(prompt=list(s.tokens), max_new_tokens=left,
+                                       temperature=cfg.temperature, seed=md["seed"],
                                        stop_token_ids=(cfg.eos_token_id,) if cfg.eos_token_id is not None else (),
-                                       return_routed_experts=cfg.routing_replay, rid=idx))
-                samples.append(Sample(group_index=gi, index=idx, tokens=list(p)))
-        outs = self.engine.generate(reqs)
-        for s, o in zip(samples, outs):
+                                       return_routed_experts=cfg.routing_replay, rid=s.index))
+                owner[s.index] = s
+        by_uid = {s.index: s for g in groups for s in g}
+        gid_of = {s.index: gi for gi, g in enumerate(groups) for s in g}
+        need = {gi: sum(1 for s in g if not s.metadata.get("finished")) for gi, g in enumerate(groups)}
+        target = cfg.groups_per_step if cfg.partial_rollout else None
+
+        def done_enough(results):
+            fin: dict[int, int] = {}
+            for rid in results:
+                gi = gid_of[rid]
+                fin[gi] = fin.get(gi, 0) + 1
+            return sum(1 for gi, n in fin.items() if n >= need[gi]) >= target
+
+        outs = self.engine.generate(reqs, stop_when=done_enough if target else None)
+        self.generated_tokens = 0
+        for o in outs:
+            s = by_uid[o.rid]
+            self.generated_tokens += len(o.tokens)
+            plen = s.metadata["prompt_len"]
             s.tokens = s.tokens + o.tokens
-            s.response_length = len(o.tokens)
-            s.loss_mask = [1] * len(o.tokens)
-            s.rollout_log_probs = o.logprobs
-            s.rollout_routed_experts = o.routed_experts
-            s.update_from_meta_info(o.finish_reason, o.weight_version)
-        return samples
+            s.response_length += len(o.tokens)
+            s.loss_mask = s.loss_mask + [1] * len(o.tokens)
+            s.rollout_log_probs = list(s.rollout_log_probs) + list(o.logprobs)
+            if o.routed_experts is not None:
+                # routing of every token fed so far (prompt and earlier partial response included)
+                s.rollout_routed_experts = o.routed_experts[: plen + s.response_length - 1]
+            if o.finish_reason != "abort":
+                s.metadata["finished"] = True
+                s.update_from_meta_info(o.finish_reason, o.weight_version)
+        complete = [g for g in groups if all(s.metadata.get("finished") for s in g)]
+        if target:
+            train, rest = complete[:target], [g for g in groups if g not in complete[:target]]
+            self.buffer = rest
+        else:
+            train = groups
+        self.last_groups = train
+        return [s for g in train for s in g]
 
     def step(self, prompts: list[list[int]], max_new: list[int] | None = None,
              rewards: list[float] | None = None) -> dict:
         cfg = self.cfg
         t0 = time.perf_counter()
         self.actor.release_grads()
-        samples = self.generate(prompts, max_new)
+        if isinstance(prompts, torch.Tensor):  # [groups, prompt_len] token ids (any device)
+            prompts = prompts.tolist()
+        samples = self.generate(prompts, max_new, rewards)
         t_gen = time.perf_counter()
         self.engine.release_memory()
-        if rewards is None:
-            rewards = [float(self.reward_fn(s)) for s in samples]
+        rewards = [s.metadata["reward"] if s.metadata.get("reward") is not None
+                   else float(self.reward_fn(s)) for s in samples]
         r = torch.tensor(rewards, dtype=torch.float32, device=self.actor.dev)
         adv = grpo_advantages(r, cfg.n_samples_per_prompt, cfg.normalize_std).cpu().numpy()
         items = [TrainItem(tokens=s.tokens, prompt_len=s.prompt_length, advantage=float(a),
@@ -113,7 +188,9 @@ class ColocatedRL:
             "perf/log_probs_time": t_lp - t_gen,
             "perf/actor_train_time": t_train - t_lp,
             "perf/step_time": t_train - t0,
-            "perf/tokens_per_gpu_per_sec": n_resp / max(t_gen - t0, 1e-9),
+            "perf/tokens_per_gpu_per_sec": self.generated_tokens / max(t_gen - t0, 1e-9),
+            "rollout/generated_tokens": self.generated_tokens,
+            "rollout/buffered_groups": len(self.buffer),
             "perf/actor_train_tok_per_s": n_tok / max(t_train - t_lp, 1e-9),
             "tokens_total": n_tok,
             "response_tokens": n_resp,

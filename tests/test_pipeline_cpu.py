@@ -62,3 +62,39 @@ def test_moe_engine_and_replay_cpu():
                    routed_experts=out.routed_experts)
     lp = actor.compute_logprobs([it])[0]
     assert np.allclose(lp, out.logprobs, atol=1e-4)
+
+
+def test_partial_rollout_over_sampling_cpu():
+    """Partial rollout: each step trains the first `groups_per_step` complete groups; the rest
+    keep their partial responses and continue next step. With lr 0 the continued samples equal
+    one uninterrupted generation (the sampler is a function of seed and position)."""
+    m = _model("tiny-moe")
+    eng = RolloutEngine(m, max_batch=16, num_pages=256, use_cuda_graph=False, steps_per_sync=2)
+    actor = Actor(m, ActorConfig(lr=0.0, max_tokens_per_gpu=512, grad_dtype=torch.float32,
+                                 use_routing_replay=True))
+    cfg = RLConfig(n_samples_per_prompt=2, partial_rollout=True, groups_per_step=2,
+                   over_sampling=2, routing_replay=True)
+    rl = ColocatedRL(eng, actor, cfg)
+    rng = np.random.default_rng(0)
+    seen = {}
+    for step in range(4):
+        k = rl.prompts_needed()
+        assert k == (4 if step == 0 else 2)
+        prompts = [rng.integers(0, 4096, 8).tolist() for _ in range(k)]
+        lens = rng.integers(2, 30, 2 * k).tolist()
+        met = rl.step(prompts, lens, rng.integers(0, 2, 2 * k).astype(float).tolist())
+        assert met["rollout/buffered_groups"] == 2
+        for g in rl.last_groups:
+            for s in g:
+                assert s.response_length == s.metadata["max_new"]
+                assert len(s.rollout_log_probs) == s.response_length == len(s.loss_mask)
+                assert s.rollout_routed_experts.shape[0] == len(s.tokens) - 1
+                seen[s.index] = s
+    assert any(s.metadata.get("resumed") for s in seen.values())  # some crossed a step boundary
+    # lr 0: every trained sample equals one uninterrupted generation of the same request
+    for s in list(seen.values())[:6]:
+        plen = s.metadata["prompt_len"]
+        ref = eng.generate([GenRequest(s.tokens[:plen], s.response_length, seed=s.metadata["seed"],
+                                       rid=0)])[0]
+        assert ref.tokens == s.tokens[plen:]
+        assert np.allclose(ref.logprobs, s.rollout_log_probs, atol=1e-5)
