@@ -266,6 +266,8 @@ int mb_vmm_reserve(size_t bytes, unsigned long long* ptr);
 int mb_vmm_free(unsigned long long ptr, size_t bytes);
 int mb_vmm_map(unsigned long long ptr, size_t bytes, int device, unsigned long long* handle);
 int mb_vmm_unmap(unsigned long long ptr, size_t bytes, unsigned long long handle);
+int mb_host_register(void* ptr, size_t bytes);
+int mb_host_unregister(void* ptr);
 #ifdef __cplusplus
 }
 #endif

@@ -591,6 +591,16 @@ torch::Tensor vmm_tensor(int64_t ptr, int64_t numel, at::ScalarType dtype, int64
                           torch::TensorOptions().dtype(dtype).device(torch::kCUDA, (int)device));
 }
 
+// Page-lock / release a byte range of a CPU tensor's storage.
+int64_t host_register(torch::Tensor t, int64_t offset, int64_t bytes) {
+  TORCH_CHECK(t.device().is_cpu() && t.is_contiguous());
+  TORCH_CHECK(offset >= 0 && offset + bytes <= (int64_t)(t.numel() * t.element_size()));
+  return mb_host_register(static_cast<char*>(t.data_ptr()) + offset, (size_t)bytes);
+}
+int64_t host_unregister(torch::Tensor t, int64_t offset) {
+  return mb_host_unregister(static_cast<char*>(t.data_ptr()) + offset);
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_decode", &mla_decode, "absorbed MLA decode over the paged latent cache");
   m.def("gdn_decode", &gdn_decode, "Gated DeltaNet decode step (state updated in place)");
@@ -657,5 +667,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("vmm_map", &vmm_map);
   m.def("vmm_unmap", &vmm_unmap);
   m.def("vmm_tensor", &vmm_tensor);
+  m.def("host_register", &host_register);
+  m.def("host_unregister", &host_unregister);
   m.def("decode_commit", &decode_commit);
 }

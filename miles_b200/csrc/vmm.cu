@@ -123,3 +123,14 @@ extern "C" int mb_vmm_unmap(unsigned long long ptr, size_t bytes, unsigned long 
   if (a.unmap(static_cast<CUdeviceptr>(ptr), bytes) != CUDA_SUCCESS) return -2;
   return a.release(static_cast<CUmemGenericAllocationHandle>(handle)) == CUDA_SUCCESS ? 0 : -3;
 }
+
+// Page-locks [ptr, ptr + bytes) of ordinary host memory so that copies from / to it run as
+// asynchronous DMA (used to pin the host-resident optimizer state chunk by chunk in the
+// background instead of one long cudaHostAlloc before the first optimizer step).
+extern "C" int mb_host_register(void* ptr, size_t bytes) {
+  return cudaHostRegister(ptr, bytes, cudaHostRegisterDefault) == cudaSuccess ? 0 : -1;
+}
+
+extern "C" int mb_host_unregister(void* ptr) {
+  return cudaHostUnregister(ptr) == cudaSuccess ? 0 : -1;
+}

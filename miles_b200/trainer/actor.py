@@ -128,6 +128,7 @@ class Actor:
         self.timers: dict[str, float] = {}
         self._custom_loss = None
         self._custom_tis = None
+        self._host_state = self._prefetch_host_state()
 
     # ------------------------------------------------------------------ memory
     def _ensure_grads(self):
@@ -155,8 +156,28 @@ class Actor:
                                 betas=self.cfg.betas, eps=self.cfg.adam_eps,
                                 weight_decay=self.cfg.weight_decay,
                                 clip_grad=self.cfg.clip_grad, placement=self.cfg.optimizer_placement,
+                                host_state=self._host_state,
                                 dp_group=self.dp_group if self._sharded() else None,
                                 **self._norm_scope())
+
+    def _prefetch_host_state(self):
+        """Start page-locking the host-resident Adam state now (under the first rollout) when
+        the optimizer will keep it on the host: FlatAdam's 'auto' rule with the gradient
+        buffer that _ensure_grads allocates first."""
+        m, cfg = self.model, self.cfg
+        if m.device.type != "cuda" or m.lora is not None or cfg.optimizer_placement == "device":
+            return None
+        n = m.flat.numel()
+        world = dist.get_world_size(self.dp_group) if self._sharded() else 1
+        ns = n // world
+        if cfg.optimizer_placement == "auto":
+            free, _ = torch.cuda.mem_get_info(m.device)
+            grad_bytes = n * torch.empty((), dtype=cfg.grad_dtype).element_size()
+            if not 12 * ns > 0.8 * (free - grad_bytes):
+                return None
+        from miles_b200.utils.host_memory import BackgroundPinned
+
+        return (BackgroundPinned(ns, torch.bfloat16), BackgroundPinned(ns, torch.bfloat16))
 
     def _norm_scope(self) -> dict:
         """Gradient-norm group of model-parallel ranks and the flat ranges this rank leaves out;

@@ -42,7 +42,7 @@ class FlatAdam:
                  betas=(0.9, 0.98), eps: float = 1e-8, weight_decay: float = 0.0,
                  clip_grad: float = 1.0, placement: str = "auto", chunk: int = 1 << 28,
                  seed: int = 1234, dp_group=None, norm_group=None, norm_exclude=None,
-                 expert_norm=None):
+                 expert_norm=None, host_state=None):
         """norm_group / norm_exclude: under model parallelism (TP, PP) every rank runs its own
         optimizer over its part of the model; the gradient norm sums the squares over
         `norm_group`, leaving out this rank's flat ranges `norm_exclude` (parameters another
@@ -87,9 +87,14 @@ class FlatAdam:
             self.v = torch.zeros(ns, dtype=torch.float32, device=dev)
         else:
             self.master = None
-            pin = dev.type == "cuda"
-            self.m = torch.zeros(ns, dtype=torch.bfloat16, pin_memory=pin)
-            self.v = torch.zeros(ns, dtype=torch.bfloat16, pin_memory=pin)
+            # bf16 m / v in host memory, page-locked on a worker thread (possibly started
+            # earlier by the actor: `host_state`); the first step waits for it
+            from miles_b200.utils.host_memory import BackgroundPinned
+
+            if host_state is None or host_state[0].tensor.numel() != ns:
+                host_state = (BackgroundPinned(ns, torch.bfloat16), BackgroundPinned(ns, torch.bfloat16))
+            self._pinning = host_state
+            self.m, self.v = host_state[0].tensor, host_state[1].tensor
             if dev.type == "cuda":
                 c = min(chunk, ns)
                 self.stage = [(torch.empty(c, dtype=torch.bfloat16, device=dev),
@@ -167,6 +172,8 @@ class FlatAdam:
             self._all_gather_params()
 
     def _host_step(self, p: torch.Tensor, g: torch.Tensor, common: dict) -> None:
+        for b in self._pinning:
+            b.wait()
         n = p.numel()
         cur = torch.cuda.current_stream(p.device)
         backs: list[torch.cuda.Event] = []
