@@ -248,7 +248,7 @@ int mb_decode_prep(const int* rows, int B, int spare, const int* s_tok, const in
                    long long* slots, int* pt, float* invt, long long* seeds,
                    long long* state_rows, int state_spare, cudaStream_t st);
 int mb_decode_commit(const int* rows, int B, int spare, const int* tok, const float* lp,
-                     const int* experts, int nk, int* s_tok, int* s_pos, int* s_done, int* s_nout,
+                     const int* experts, int n_moe, int topk, int* s_tok, int* s_pos, int* s_done, int* s_nout,
                      const int* s_maxnew, const int* s_stop, int nstop, int* out_tok,
                      float* out_lp, int max_new, unsigned char* out_exp, const int* s_rec,
                      int max_len, cudaStream_t st);

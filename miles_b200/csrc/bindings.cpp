@@ -545,21 +545,24 @@ int64_t decode_commit(torch::Tensor rows, int64_t spare, torch::Tensor tok, torc
   CHECK_DT(tok, at::kInt); CHECK_DT(lp, at::kFloat); CHECK_DT(out_tok, at::kInt);
   CHECK_DT(out_lp, at::kFloat); CHECK_DT(s_stop, at::kInt); CHECK_DT(s_rec, at::kInt);
   const int B = rows.numel();
-  int nk = 0, max_len = 0;
+  int n_moe = 0, topk = 0, max_len = 0;
   if (experts.has_value() && out_exp.has_value()) {
     CHECK_DT(experts.value(), at::kInt);
     CHECK_DT(out_exp.value(), at::kByte);
     TORCH_CHECK(experts.value().is_contiguous() && out_exp.value().is_contiguous());
-    nk = experts.value().numel() / std::max<int64_t>(experts.value().size(0), 1);
+    TORCH_CHECK(experts.value().dim() == 3 && experts.value().size(1) == B,
+                "experts must be [n_moe, B, k]");
+    n_moe = experts.value().size(0);
+    topk = experts.value().size(2);
     max_len = out_exp.value().size(1);
-    TORCH_CHECK(out_exp.value().numel() == out_exp.value().size(0) * (int64_t)max_len * nk,
+    TORCH_CHECK(out_exp.value().numel() == out_exp.value().size(0) * (int64_t)max_len * n_moe * topk,
                 "out_exp must be [slots, max_len, n_moe, k]");
   }
   return mb_decode_commit(PT<int>(rows), B, (int)spare, PT<int>(tok), PT<float>(lp),
-                          nk ? PT<int>(experts) : nullptr, nk, PT<int>(s_tok), PT<int>(s_pos),
+                          n_moe ? PT<int>(experts) : nullptr, n_moe, topk, PT<int>(s_tok), PT<int>(s_pos),
                           PT<int>(s_done), PT<int>(s_nout), PT<int>(s_maxnew), PT<int>(s_stop),
                           (int)s_stop.size(1), PT<int>(out_tok), PT<float>(out_lp),
-                          (int)out_tok.size(1), nk ? PT<unsigned char>(out_exp) : nullptr,
+                          (int)out_tok.size(1), n_moe ? PT<unsigned char>(out_exp) : nullptr,
                           PT<int>(s_rec), max_len, cur_stream());
 }
 

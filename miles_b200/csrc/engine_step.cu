@@ -57,11 +57,12 @@ __global__ void decode_prep_kernel(const int* __restrict__ rows, int B, int spar
   }
 }
 
-// experts: [B, n_moe, k] int32 routing of the token fed at row j (nullptr without MoE / R3);
-// out_exp: [slots, max_len, n_moe, k] uint8, written at the fed token's position.
+// experts: [n_moe, B, k] int32 routing of the token fed at row j (layer-major, as the router
+// writes it; nullptr without MoE / R3); out_exp: [slots, max_len, n_moe, k] uint8, written at
+// the fed token's position.
 __global__ void decode_commit_kernel(const int* __restrict__ rows, int B, int spare,
                                      const int* __restrict__ tok, const float* __restrict__ lp,
-                                     const int* __restrict__ experts, int nk,
+                                     const int* __restrict__ experts, int n_moe, int topk,
                                      int* __restrict__ s_tok, int* __restrict__ s_pos,
                                      int* __restrict__ s_done, int* __restrict__ s_nout,
                                      const int* __restrict__ s_maxnew,
@@ -84,9 +85,12 @@ __global__ void decode_commit_kernel(const int* __restrict__ rows, int B, int sp
   if (!live_sh) return;
   const int p = pos_sh;
   if (experts && out_exp && s_rec[s] && p < max_len) {
+    const int nk = n_moe * topk;
     unsigned char* dst = out_exp + ((long long)s * max_len + p) * nk;
-    for (int c = threadIdx.x; c < nk; c += blockDim.x)
-      dst[c] = (unsigned char)experts[(long long)j * nk + c];
+    for (int c = threadIdx.x; c < nk; c += blockDim.x) {
+      const int l = c / topk, kk = c - l * topk;
+      dst[c] = (unsigned char)experts[((long long)l * B + j) * topk + kk];
+    }
   }
   __syncthreads();  // every thread has read s_pos before thread 0 advances it
   if (threadIdx.x == 0) {
@@ -120,12 +124,12 @@ extern "C" int mb_decode_prep(const int* rows, int B, int spare, const int* s_to
 }
 
 extern "C" int mb_decode_commit(const int* rows, int B, int spare, const int* tok, const float* lp,
-                                const int* experts, int nk, int* s_tok, int* s_pos, int* s_done,
+                                const int* experts, int n_moe, int topk, int* s_tok, int* s_pos, int* s_done,
                                 int* s_nout, const int* s_maxnew, const int* s_stop, int nstop,
                                 int* out_tok, float* out_lp, int max_new, unsigned char* out_exp,
                                 const int* s_rec, int max_len, cudaStream_t st) {
   if (B == 0) return 0;
-  return (int)mb::mb_launch(es::decode_commit_kernel, B, 128, 0, st, rows, B, spare, tok, lp, experts, nk, s_tok,
+  return (int)mb::mb_launch(es::decode_commit_kernel, B, 128, 0, st, rows, B, spare, tok, lp, experts, n_moe, topk, s_tok,
             s_pos, s_done, s_nout, s_maxnew, s_stop, nstop, out_tok, out_lp, max_new, out_exp,
             s_rec, max_len);
 }

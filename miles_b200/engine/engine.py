@@ -140,7 +140,7 @@ def _commit_ref(ds: DecodeState, st: dict, tok, lp, experts):
     p = ds.s_pos[r].long()
     if experts is not None and ds.out_exp is not None:
         rec = (ds.s_rec[r] != 0) & (p < ds.max_len)
-        ds.out_exp[r[rec], p[rec]] = experts[live][rec].to(torch.uint8)
+        ds.out_exp[r[rec], p[rec]] = experts.permute(1, 0, 2)[live][rec].to(torch.uint8)
     ok = n < ds.max_len
     ds.out_tok[r[ok], n[ok]] = t[ok]
     ds.out_lp[r[ok], n[ok]] = lp[live][ok].float()
@@ -264,7 +264,8 @@ class RolloutEngine:
             "pt": torch.zeros(B, self.max_pages_per_seq, dtype=torch.int32, device=dev),
             "inv_t": torch.ones(B, dtype=torch.float32, device=dev),
             "seeds": torch.zeros(B, dtype=torch.int64, device=dev),
-            "experts": torch.zeros(B, max(self.n_moe, 1), max(self.cfg.topk, 1), dtype=torch.int32, device=dev),
+            # routing of each batch row, layer-major [L_moe, B, k] (each layer's slice contiguous)
+            "experts": torch.zeros(max(self.n_moe, 1), B, max(self.cfg.topk, 1), dtype=torch.int32, device=dev),
             # linear-attention state row of every batch row (= its slot; padding: the spare row)
             "state_rows": torch.full((B,), self.max_batch, dtype=torch.int64, device=dev),
         }
@@ -280,12 +281,9 @@ class RolloutEngine:
                                    st["state_rows"], ds.S)
         else:
             _prep_ref(ds, st)
-        rec = []
         h = self.model.forward_decode(st["tokens"], st["positions"], self.cache, st["pt"], st["ctx"],
-                                      st["slots"], record=rec if rec_on else None,
+                                      st["slots"], record=st["experts"] if rec_on else None,
                                       state_rows=st["state_rows"])
-        for j, idx in enumerate(rec):
-            st["experts"][:, j].copy_(idx)
         # the sampled token sits at position `positions + 1`
         tok, lp = sample_from_hidden(h, self.model.lm_head_weight(), st["inv_t"], st["seeds"],
                                      st["positions"] + 1)

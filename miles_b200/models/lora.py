@@ -47,7 +47,9 @@ def resolve_targets(targets) -> set[str]:
 
 class LoRA:
     def __init__(self, model, rank: int, alpha: float, targets=None, dropout: float = 0.0,
-                 seed: int = 0):
+                 seed: int = 0, exclude=None):
+        """exclude: module names (e.g. "o_proj", "layers.0.") whose weights get no adapter
+        even when a target matches (--exclude-modules)."""
         self.rank = rank
         self.scale = alpha / rank
         self.dropout = dropout
@@ -57,6 +59,8 @@ class LoRA:
         self.B: dict[str, torch.nn.Parameter] = {}
         for name, p in model.params.items():
             if p.dim() != 2 or not any(name.endswith(sfx) for sfx in suffixes):
+                continue
+            if exclude and any(e in name for e in exclude):
                 continue
             out_f, in_f = p.shape
             bound = 1.0 / math.sqrt(in_f)  # kaiming-uniform(a=sqrt(5)) bound for A

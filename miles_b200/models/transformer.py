@@ -28,7 +28,7 @@ from torch.utils.checkpoint import checkpoint
 from miles_b200.models.config import ModelConfig
 from miles_b200.ops import gemm as G
 from miles_b200.ops.attention import PAGE, VarlenMeta, decode_attention, varlen_attention
-from miles_b200.ops.moe import RouterCfg, moe_experts
+from miles_b200.ops.moe import RouterCfg, emit_record, moe_experts
 from miles_b200.ops.norm import (add_rms_norm, qk_norm_rope, qk_norm_rope_to_cache, rms_norm,
                                  rope_tables, swiglu)
 from miles_b200.parallel.tp import (copy_to_tp, reduce_from_tp, row_parallel_rs, sp_gather,
@@ -463,8 +463,8 @@ class Transformer(torch.nn.Module):
             buf[:hi - lo] = idx
             parts = [torch.empty_like(buf) for _ in range(tp.size)]
             dist.all_gather(parts, buf, group=tp.group)
-            record(torch.cat([p[:(T * (r + 1) // tp.size) - (T * r // tp.size)]
-                              for r, p in enumerate(parts)], 0))
+            emit_record(record, torch.cat([p[:(T * (r + 1) // tp.size) - (T * r // tp.size)]
+                                           for r, p in enumerate(parts)], 0))
         return F.pad(y, (0, 0, lo, T - hi))
 
     def _layer_train(self, i, m_prev, r_prev, meta, replay):
@@ -879,7 +879,10 @@ class Transformer(torch.nn.Module):
                 o = decode_attention(q, cache.k[i], cache.v[i], page_table, ctx_lens)
                 a = self._pending_out(o.reshape(B, -1), pre + "o_proj.weight")
             x2, r = self._add_norm(self._sw_pend(i, "post_self_attn_layernorm", a), r, post)
-            rec = record.append if (record is not None and i in self.router_cfgs) else None
+            rec = None
+            if record is not None and i in self.router_cfgs:
+                # a [L_moe, B, k] buffer: the router writes layer i's routing straight into it
+                rec = record[self.moe_index[i]] if isinstance(record, torch.Tensor) else record.append
             pend = self._mlp_partial(i, x2, record=rec) if rec is not None else self._pending_mlp(i, x2)
             pend = self._sw_pend(i, "post_mlp_layernorm", pend)
         y, _ = self._add_norm(pend, r, self.params["norm.weight"])

@@ -82,9 +82,9 @@ class MoEPlan:
     """Device-side dispatch plan for one batch: dest rows, padded offsets and counts."""
 
     @classmethod
-    def fused(cls, logits, bias, replay_idx, x, cfg: "RouterCfg"):
+    def fused(cls, logits, bias, replay_idx, x, cfg: "RouterCfg", idx_out=None):
         """Routing + plan + gather in one kernel (small batches, no backward). Returns
-        (plan, idx, w, xs)."""
+        (plan, idx, w, xs); idx_out: optional contiguous int32 [T, k] that receives idx."""
         T = logits.shape[0]
         k, E = cfg.k, cfg.E
         n = T * k
@@ -95,7 +95,7 @@ class MoEPlan:
         self.counts = torch.empty(E, dtype=torch.int32, device=dev)
         self.offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
         self.dest = torch.empty(n, dtype=torch.int32, device=dev)
-        idx = torch.empty(T, k, dtype=torch.int32, device=dev)
+        idx = idx_out if idx_out is not None else torch.empty(T, k, dtype=torch.int32, device=dev)
         w = torch.empty(T, k, dtype=torch.float32, device=dev)
         xs = torch.empty(self.rows, x.shape[1], dtype=x.dtype, device=dev)
         lib().moe_route_dispatch(logits, bias, replay_idx, x, idx, w, self.counts, self.offsets,
@@ -159,17 +159,17 @@ class _MoE(torch.autograd.Function):
         logits = G.matmul_nt(x, router_w, out_dtype=torch.float32)
         if not need_bwd and T * cfg.k <= FUSED_DISPATCH_MAX_ROWS:
             # decode-sized batch: one kernel for routing, plan and gather
+            into = record if isinstance(record, torch.Tensor) else None
             plan, idx, w, xs = MoEPlan.fused(logits, bias, replay_idx.contiguous().view(T, cfg.k)
-                                             if replay_idx is not None else None, x, cfg)
-            if record is not None:
+                                             if replay_idx is not None else None, x, cfg, idx_out=into)
+            if record is not None and into is None:
                 record(idx)
         else:
             idx = torch.empty(T, cfg.k, dtype=torch.int32, device=x.device)
             w = torch.empty(T, cfg.k, dtype=torch.float32, device=x.device)
             lib().router_fwd(logits, bias, replay_idx, idx, w, cfg.k, cfg.score_fn, cfg.renorm,
                              cfg.n_group, cfg.topk_group, cfg.scale)
-            if record is not None:
-                record(idx)
+            emit_record(record, idx)
             plan = MoEPlan(idx, cfg.E)
             xs = plan.gather(x, zero_pad=need_bwd)
         gu, a, ys = experts_forward(xs, w1, w2, plan, save_gu=need_bwd)
@@ -205,13 +205,25 @@ class _MoE(torch.autograd.Function):
         return dx, dwr, dw1, dw2, None, None, None, None, None
 
 
+def emit_record(record, idx: torch.Tensor) -> None:
+    """Hand a layer's routing to its recorder: a callable, or an int32 [T, k] tensor that
+    receives a copy (the decode path passes its record buffer so that the fused router kernel
+    writes into it directly)."""
+    if record is None:
+        return
+    if isinstance(record, torch.Tensor):
+        if record.data_ptr() != idx.data_ptr():
+            record.copy_(idx)
+    else:
+        record(idx)
+
+
 def moe_experts(x, router_w, w1, w2, cfg: RouterCfg, bias=None, replay_idx=None, record=None):
     """Routed-expert output for x [T,H]. w1 [E, 2I, H] ([gate|up]), w2 [E, H, I].
-    replay_idx: int32 [T,k] replays a recorded routing (R3); record(idx) receives the routing
-    actually used (R3 capture)."""
+    replay_idx: int32 [T,k] replays a recorded routing (R3); `record` receives the routing
+    actually used (R3 capture): a callable record(idx) or an int32 [T, k] output tensor."""
     if not use_native(x):
         y, idx = moe_ref(x, router_w, w1, w2, cfg, bias, replay_idx)
-        if record is not None:
-            record(idx)
+        emit_record(record, idx)
         return y
     return _MoE.apply(x, router_w, w1, w2, bias, cfg, replay_idx, record, torch.is_grad_enabled())

@@ -34,11 +34,28 @@ class PolicyLossCfg:
     use_opsm: bool = False
     opsm_delta: float = 1e-4
     gspo: bool = False
+    unbiased_kl: bool = False        # --use-unbiased-kl: KL term weighted by exp(logp - old_logp)
+    custom_pg_loss_reducer_path: str | None = None
+
+
+def kl_terms(logp, ref_logp, kl_type: str):
+    """Per-token KL estimator of log(pi / pi_ref) (k1 / k2 / k3 = low_var_kl, clamped)."""
+    kt = KL_TYPES[kl_type]
+    if not kt:
+        return torch.zeros_like(logp)
+    lr = logp - ref_logp
+    if kt == 1:
+        return lr
+    if kt == 2:
+        return 0.5 * lr * lr
+    return ((-lr).exp() + lr - 1).clamp(-10, 10)
 
 
 def policy_loss_ref(logp, old_logp, adv, weight, cfg: PolicyLossCfg, rollout_logp=None,
-                    ref_logp=None):
-    """Returns (loss, metrics dict) with autograd through logp."""
+                    ref_logp=None, pg_reducer=None):
+    """Returns (loss, metrics dict) with autograd through logp. pg_reducer: optional callable
+    mapping the per-token policy-gradient loss to its scalar (a custom reducer replaces the
+    weighted sum for the pg term)."""
     ppo_kl = old_logp - logp
     ratio = (-ppo_kl).exp()
     pg1 = -adv * ratio
@@ -59,20 +76,14 @@ def policy_loss_ref(logp, old_logp, adv, weight, cfg: PolicyLossCfg, rollout_log
             tis = raw.clamp(cfg.tis_clip_low, cfg.tis_clip)
         tis_clip = (tis != raw).to(logp.dtype)
         pg = pg * tis.detach()
-    kl = torch.zeros_like(logp)
-    kt = KL_TYPES[cfg.kl_type]
-    if kt:
-        lr = logp - ref_logp
-        if kt == 1:
-            kl = lr
-        elif kt == 2:
-            kl = 0.5 * lr * lr
-        else:
-            kl = ((-lr).exp() + lr - 1).clamp(-10, 10)
-    loss = (weight * (pg + cfg.kl_coef * kl)).sum()
+    kl = kl_terms(logp, ref_logp, cfg.kl_type)
+    if cfg.unbiased_kl and KL_TYPES[cfg.kl_type]:
+        kl = kl * (logp - old_logp).exp()  # importance ratio pi / pi_old (reference loss.py:669)
+    pg_term = pg_reducer(pg) if pg_reducer is not None else (weight * pg).sum()
+    loss = pg_term + (weight * cfg.kl_coef * kl).sum()
     w = weight.detach()
     m = {
-        "pg_loss": (w * pg).sum().item(),
+        "pg_loss": float(pg_term.detach()) if pg_reducer is not None else (w * pg).sum().item(),
         "pg_clipfrac": (w * clipfrac).sum().item(),
         "ppo_kl": (w * ppo_kl).sum().item(),
         "kl_loss": (w * kl).sum().item(),
@@ -110,12 +121,25 @@ class _PolicyLoss(torch.autograd.Function):
         return dlogp * gloss, None, None, None, None, None, None
 
 
-def policy_loss(logp, old_logp, adv, weight, cfg: PolicyLossCfg, rollout_logp=None, ref_logp=None):
+def policy_loss(logp, old_logp, adv, weight, cfg: PolicyLossCfg, rollout_logp=None, ref_logp=None,
+                pg_reducer=None):
     """Fused clipped policy loss. `weight` carries mask and reduction normaliser.
-    Returns (loss scalar tensor, metrics tensor [7] of weighted sums in METRIC_NAMES order)."""
-    if not use_native(logp):
-        loss, m = policy_loss_ref(logp, old_logp, adv, weight, cfg, rollout_logp, ref_logp)
-        return loss, torch.tensor([m[k] for k in METRIC_NAMES])
+    Returns (loss scalar tensor, metrics tensor [7] of weighted sums in METRIC_NAMES order).
+    The unbiased KL (KL x pi / pi_old, with its gradient) and a custom pg reducer run as PyTorch
+    ops around the fused kernel."""
+    if not use_native(logp) or pg_reducer is not None:
+        loss, m = policy_loss_ref(logp, old_logp, adv, weight, cfg, rollout_logp, ref_logp, pg_reducer)
+        return loss, torch.tensor([m[k] for k in METRIC_NAMES], device=logp.device)
+    if cfg.unbiased_kl and KL_TYPES[cfg.kl_type]:
+        import dataclasses
+
+        loss, m = _PolicyLoss.apply(logp, old_logp, adv, weight, rollout_logp, None,
+                                    dataclasses.replace(cfg, kl_coef=0.0, kl_type="none"))
+        kl = kl_terms(logp, ref_logp, cfg.kl_type) * (logp - old_logp).exp()
+        loss = loss + cfg.kl_coef * (weight * kl).sum()
+        m = m.clone()
+        m[METRIC_NAMES.index("kl_loss")] = (weight.detach() * kl.detach()).sum()
+        return loss, m
     return _PolicyLoss.apply(logp, old_logp, adv, weight, rollout_logp, ref_logp, cfg)
 
 

@@ -70,6 +70,13 @@ class RolloutManager:
         self.custom_reward_post = (load_function(args.custom_reward_post_process_path)
                                    if args.custom_reward_post_process_path else None)
         self.last_metrics: dict = {}
+        # --custom-rollout-log-function-path / --custom-eval-rollout-log-function-path: called
+        # with the rollout's samples (eval: its per-dataset data); returning True skips the
+        # default metrics (reference miles/ray/rollout.py:1145-1186)
+        self.custom_rollout_log = (load_function(args.custom_rollout_log_function_path)
+                                   if args.custom_rollout_log_function_path else None)
+        self.custom_eval_log = (load_function(args.custom_eval_rollout_log_function_path)
+                                if args.custom_eval_rollout_log_function_path else None)
 
     # ------------------------------------------------------------------ generation
     def _local_args(self):
@@ -105,7 +112,11 @@ class RolloutManager:
                 pickle.dump({"rollout_id": rollout_id, "samples": groups}, f)
         samples = [s for g in groups for s in g]
         dt = time.perf_counter() - t0
-        metrics.update(self.rollout_metrics(samples, dt))
+        if self.custom_rollout_log is not None and self.custom_rollout_log(rollout_id, self.args, samples,
+                                                                          metrics, dt):
+            pass  # the custom logger replaced the default rollout metrics
+        else:
+            metrics.update(self.rollout_metrics(samples, dt))
         data = self.convert_samples_to_train_data(groups)
         self.last_metrics = metrics
         data["metrics"] = metrics
@@ -113,7 +124,12 @@ class RolloutManager:
 
     def eval(self, rollout_id: int) -> dict:
         out = self.eval_fn(self.args, rollout_id, self.data_source, evaluation=True)
-        return getattr(out, "metrics", {}) if not isinstance(out, dict) else out
+        metrics = getattr(out, "metrics", {}) if not isinstance(out, dict) else out
+        if self.custom_eval_log is not None:
+            data = out if isinstance(out, dict) else getattr(out, "data", None)
+            if self.custom_eval_log(rollout_id, self.args, data, metrics):
+                return {}
+        return metrics
 
     # ------------------------------------------------------------------ rewards / conversion
     def post_process_rewards(self, groups: list[list[Sample]]) -> tuple[list[float], list[float]]:

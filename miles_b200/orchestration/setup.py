@@ -21,6 +21,7 @@ from miles_b200.ops.rl import PolicyLossCfg
 from miles_b200.parallel.reloadable import REGISTRY as _RG
 from miles_b200.trainer.actor import Actor, ActorConfig
 from miles_b200.trainer.lr_scheduler import schedule_from_args
+from miles_b200.utils.misc import load_function
 
 
 @dataclass
@@ -191,9 +192,20 @@ def load_tokenizer(args):
 
 
 def build_model(args, ctx: ProcessContext) -> Transformer:
+    if getattr(args, "custom_megatron_init_path", None):
+        # user initialisation after the process groups exist (reference initialize.py:106-110)
+        load_function(args.custom_megatron_init_path)(args)
     cfg = model_config(args)
     dtype = torch.bfloat16 if ctx.device.type == "cuda" else torch.float32
-    model = Transformer(cfg, device=ctx.device, dtype=dtype, seed=args.seed, tp_group=ctx.tp_group,
+    provider = None
+    if getattr(args, "custom_model_provider_path", None):
+        # custom model provider: fn(args, cfg) returning a ModelConfig to build, or a built
+        # Transformer (the role of the reference's Megatron model_provider hook)
+        provider = load_function(args.custom_model_provider_path)(args, cfg)
+        if isinstance(provider, ModelConfig):
+            cfg, provider = provider, None
+    model = provider if provider is not None else Transformer(
+                        cfg, device=ctx.device, dtype=dtype, seed=args.seed, tp_group=ctx.tp_group,
                         ep_group=ctx.ep_group, cp_group=ctx.cp_group, pp_group=ctx.pp_group,
                         vpp=getattr(args, "virtual_pipeline_model_parallel_size", None) or 1,
                         pp_first_layers=getattr(args, "decoder_first_pipeline_num_layers", None),
@@ -220,7 +232,7 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
         from miles_b200.models.lora import LoRA
 
         model.lora = LoRA(model, args.lora_rank, args.lora_alpha, args.target_modules,
-                          args.lora_dropout, seed=args.seed)
+                          args.lora_dropout, seed=args.seed, exclude=args.exclude_modules)
         if args.lora_adapter_path:
             model.lora.load(args.lora_adapter_path)
     return model
@@ -237,6 +249,8 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                          tis_mode=tis_mode,
                          custom_tis_path=None if tis_path in KERNEL_MODES or not tis_path else tis_path,
                          loss_type=args.loss_type, custom_loss_path=args.custom_loss_function_path,
+                         unbiased_kl=args.use_unbiased_kl,
+                         custom_pg_loss_reducer_path=args.custom_pg_loss_reducer_function_path,
                          use_opsm=args.use_opsm, opsm_delta=args.opsm_delta,
                          gspo=args.advantage_estimator == "gspo",
                          kl_coef=args.kl_loss_coef if args.use_kl_loss else 0.0,
@@ -254,7 +268,7 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                       logprob_chunk=args.log_probs_chunk_size if args.log_probs_chunk_size > 0 else 4096,
                       mtp_loss_scale=(args.mtp_loss_scaling_factor
                                       if getattr(args, "enable_mtp_training", False) else 0.0),
-                      adam_eps=args.adam_eps, lr_schedule=schedule_from_args(args),
+                      adam_eps=args.adam_eps, lr_schedule=schedule_from_args(args), tis_args=args,
                       micro_batching="balanced" if args.use_dynamic_batch_size else "fixed",
                       micro_batch_size=args.micro_batch_size,
                       log_probs_max_tokens_per_gpu=args.log_probs_max_tokens_per_gpu)

@@ -32,7 +32,7 @@ import torch.distributed as dist
 
 from miles_b200.ops import gemm as G
 from miles_b200.ops._lib import lib
-from miles_b200.ops.moe import ALIGN, MoEPlan, RouterCfg, _accum_grouped_wgrad
+from miles_b200.ops.moe import ALIGN, MoEPlan, RouterCfg, _accum_grouped_wgrad, emit_record
 
 
 class EPContext:
@@ -126,8 +126,7 @@ class _MoEEPPeer(torch.autograd.Function):
         w = torch.empty(T, k, dtype=torch.float32, device=dev)
         C.router_fwd(logits, bias, replay_idx, idx, w, k, cfg.score_fn, cfg.renorm,
                      cfg.n_group, cfg.topk_group, cfg.scale)
-        if record is not None:
-            record(idx)
+        emit_record(record, idx)
         if T > ep.cap_tokens:
             raise ValueError(f"{T} tokens exceed the EP buffers ({ep.cap_tokens})")
         n = T * k
@@ -222,8 +221,7 @@ class _MoEEP(torch.autograd.Function):
         w = torch.empty(T, k, dtype=torch.float32, device=x.device)
         lib().router_fwd(logits, bias, replay_idx, idx, w, k, cfg.score_fn, cfg.renorm,
                          cfg.n_group, cfg.topk_group, cfg.scale)
-        if record is not None:
-            record(idx)
+        emit_record(record, idx)
         # send plan: groups = destination ranks, no padding
         dest_rank = torch.div(idx, ep.E_local, rounding_mode="floor").to(torch.int32)
         n = T * k
@@ -319,8 +317,7 @@ def moe_ep_ref(x, router_w, w1_local, w2_local, cfg: RouterCfg, ep: EPContext, b
     T, H = x.shape
     logits = x.float() @ router_w.float().t()
     idx, w = route_ref(logits, cfg, bias, replay_idx)
-    if record is not None:
-        record(idx)
+    emit_record(record, idx)
     dest = torch.div(idx.long(), ep.E_local, rounding_mode="floor").view(-1)
     # stable sort by destination keeps (token, slot) order inside each destination
     order = torch.sort(dest, stable=True).indices

@@ -252,17 +252,42 @@ async def eval_rollout(args, rollout_id: int) -> RolloutFnEvalOutput:
         datasets = [{"name": n, "path": p} for n, p in zip(it, it)]
     for ds in datasets:
         d = Dataset(ds["path"], state.tokenizer, prompt_key=args.eval_input_key or args.input_key,
-                    label_key=args.eval_label_key or args.label_key)
+                    label_key=args.eval_label_key or args.label_key,
+                    tool_key=getattr(args, "eval_tool_key", None) or getattr(args, "tool_key", None))
         sp = dict(state.sampling_params, temperature=args.eval_temperature,
                   max_new_tokens=args.eval_max_response_len)
+        if getattr(args, "eval_top_p", None) is not None:
+            sp["top_p"] = args.eval_top_p
+        if getattr(args, "eval_top_k", None) is not None:
+            sp["top_k"] = args.eval_top_k
+        if getattr(args, "eval_min_new_tokens", None):
+            sp["min_new_tokens"] = args.eval_min_new_tokens
+        max_prompt = getattr(args, "eval_max_prompt_len", None)
+        max_ctx = getattr(args, "eval_max_context_len", None)
         tasks = []
         for s in d.samples:
+            if max_prompt and len(s.tokens) > max_prompt:
+                continue  # --eval-max-prompt-len drops longer prompts
+            spp = sp
+            if max_ctx:  # --eval-max-context-len caps prompt + response
+                spp = dict(sp, max_new_tokens=max(0, min(sp["max_new_tokens"] or max_ctx,
+                                                         max_ctx - len(s.tokens))))
             for k in range(args.n_samples_per_eval_prompt):
                 c = copy.deepcopy(s)
                 c.index = (s.index or 0) * args.n_samples_per_eval_prompt + k
-                tasks.append(generate_and_rm(args, c, sp, evaluation=True))
+                tasks.append(generate_and_rm(args, c, spp, evaluation=True))
         samples = await asyncio.gather(*tasks)
-        rewards = [s.get_reward_value(args) if s.reward is not None else 0.0 for s in samples]
-        out[ds["name"]] = {"rewards": rewards, "samples": samples}
+        key = getattr(args, "eval_reward_key", None)
+        rewards = [(s.reward.get(key, 0.0) if key and isinstance(s.reward, dict) else
+                    s.get_reward_value(args)) if s.reward is not None else 0.0 for s in samples]
+        out[ds["name"]] = {"rewards": rewards, "samples": samples,
+                           "truncated": [int(s.status == Sample.Status.TRUNCATED) for s in samples]}
         metrics[f"eval/{ds['name']}"] = float(np.mean(rewards)) if rewards else 0.0
+        if out[ds["name"]]["truncated"]:
+            metrics[f"eval/{ds['name']}-truncated_ratio"] = float(np.mean(out[ds["name"]]["truncated"]))
+        if getattr(args, "log_passrate", False):
+            from miles_b200.utils.metric_utils import compute_pass_rate
+
+            for k, v in compute_pass_rate(rewards, args.n_samples_per_eval_prompt).items():
+                metrics[f"eval/{ds['name']}-{k}"] = v
     return RolloutFnEvalOutput(out, metrics)

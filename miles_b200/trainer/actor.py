@@ -77,6 +77,7 @@ class ActorConfig:
     micro_batch_size: int = 1
     log_probs_max_tokens_per_gpu: int | None = None
     lr_schedule: "LRSchedule | None" = None   # None: constant `lr`
+    tis_args: object = None   # namespace handed to a custom TIS function (e.g. MIS settings)
 
 
 def pack_microbatches(lengths: list[int], max_tokens: int) -> list[list[int]]:
@@ -128,6 +129,7 @@ class Actor:
         self.timers: dict[str, float] = {}
         self._custom_loss = None
         self._custom_tis = None
+        self._pg_reducer = None
         self._host_state = self._prefetch_host_state()
 
     # ------------------------------------------------------------------ memory
@@ -397,6 +399,7 @@ class Actor:
 
     def _mb_loss(self, prep: dict, lp, ent, metrics: torch.Tensor):
         cfg = self.cfg
+        self._cur_total_lens = [b - a for a, b in zip(prep["meta"].cu_list[:-1], prep["meta"].cu_list[1:])]
         loss, m = self._loss(lp, ent, prep["seg"], prep["n"], prep["old"], prep["adv"], prep["wgt"],
                              prep["roll"], prep["ref"])
         if cfg.entropy_coef:
@@ -476,16 +479,32 @@ class Actor:
             if self._custom_tis is None:
                 self._custom_tis = load_function(lc.custom_tis_path)
             # reference hook signature: scales pg_loss; applied to the (detached) weights
-            scaled, _, _ = self._custom_tis(lc, pg_loss=torch.ones_like(lp), train_log_probs=[old],
-                                            rollout_log_probs=[roll], loss_masks=[mask])
+            sizes = torch.bincount(seg, minlength=nseq).tolist()
+            sp = lambda x: list(torch.split(x, sizes))  # noqa: E731  (per-sample tensors)
+            scaled, masks, _ = self._custom_tis(cfg.tis_args if cfg.tis_args is not None else lc,
+                                                pg_loss=torch.ones_like(lp), train_log_probs=sp(old),
+                                                rollout_log_probs=sp(roll), loss_masks=sp(mask))
             w = w * scaled.detach()
+            if masks is not None:  # rejection (mask mode / rejection sampling) drops tokens
+                w = w * torch.cat([mm.float() for mm in masks]).to(w.device)
             lc = dataclasses.replace(lc, use_tis=False)
         lp_in, old_in = lp, old
         if lc.gspo:
             # GSPO: sequence-level importance ratio exp(mean_t(logp - old)) on every token
             lp_in = _seg_mean(lp * mask, mask, seg, nseq)
             old_in = _seg_mean(old * mask, mask, seg, nseq)
-        return policy_loss(lp_in, old_in, adv, w, lc, roll if lc.use_tis else None, ref)
+        reducer = None
+        if lc.custom_pg_loss_reducer_path:
+            # custom reducer: fn(total_lengths, response_lengths, loss_masks, per_token_loss)
+            # returns a callable over the concatenated per-token pg loss (reference
+            # training_utils/loss.py:644-652)
+            if self._pg_reducer is None:
+                self._pg_reducer = load_function(lc.custom_pg_loss_reducer_path)
+            rl = torch.bincount(seg, minlength=nseq).tolist()
+            masks = list(torch.split(mask, rl))
+            tl = getattr(self, "_cur_total_lens", None) or rl
+            reducer = self._pg_reducer(tl, rl, masks, cfg.per_token_loss)
+        return policy_loss(lp_in, old_in, adv, w, lc, roll if lc.use_tis else None, ref, reducer)
 
     def _reduce_grads(self):
         """Sum gradients over data-parallel ranks (replicated region) and expert-data-parallel

@@ -16,6 +16,7 @@ training_utils/ci_utils.py:12-24, training_utils/log_utils.py:171-200.
 """
 from __future__ import annotations
 
+import os
 import time
 
 import numpy as np
@@ -68,6 +69,19 @@ class TrainActor:
         self.backuper = TensorBackuper(self.model, enabled=not args.disable_weights_backuper)
         self.need_ref = bool(args.use_kl_loss or args.kl_coef)
         self.metrics: dict = {}
+        from miles_b200.utils.misc import load_function
+
+        hook = lambda name: (load_function(getattr(args, name)) if getattr(args, name, None)  # noqa: E731
+                             else None)
+        # user hooks (reference megatron_utils/model.py:279-283, :354-358; actor.py:187-190)
+        self._hook_before_lp = hook("custom_megatron_before_log_prob_hook_path")
+        self._hook_before_step = hook("custom_megatron_before_train_step_hook_path")
+        self._postprocess = hook("rollout_data_postprocess_path")
+
+    def _rank(self) -> int:
+        import torch.distributed as dist
+
+        return dist.get_rank() if dist.is_initialized() else 0
 
     def init_ref(self):
         """Reference policy for the KL terms: the weights of --ref-load (torch_dist iteration
@@ -128,6 +142,15 @@ class TrainActor:
 
             data = rebalance_over_dp(data, self.dp_group)
         items = data_to_items(data)
+        if getattr(a, "save_debug_train_data", None):
+            import pickle
+
+            path = a.save_debug_train_data.format(rollout_id=rollout_id, rank=self._rank())
+            os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
+            with open(path, "wb") as f:
+                pickle.dump({k: v for k, v in data.items() if k != "metrics"}, f)
+        if self._hook_before_lp is not None:
+            self._hook_before_lp(a, self.model, "")
         old = None
         if not a.use_rollout_logprobs:
             old_actor = getattr(a, "keep_old_actor", False) and "old_actor" in self.backuper.backups
@@ -154,6 +177,8 @@ class TrainActor:
                                             values=values, dp_group=self.dp_group)
             for it, adv in zip(items, advs):
                 it.advantage = adv
+        if self._postprocess is not None:
+            self._postprocess(a)  # reference hook signature: fn(args), after the advantages
         m = {}
         world = self.data_world
         if self.critic is not None and rets is not None:
@@ -168,11 +193,25 @@ class TrainActor:
             m["train/train_rollout_logprob_abs_diff"] = float(d.mean()) if d.size else 0.0
         steps = a.num_steps_per_rollout or 1
         per = (len(items) + steps - 1) // steps
+        if getattr(a, "get_mismatch_metrics", False) and items and items[0].rollout_logp is not None:
+            from miles_b200.trainer.mis import mismatch_metrics
+
+            m.update(mismatch_metrics([it.old_logp if it.old_logp is not None else it.rollout_logp
+                                       for it in items],
+                                      [it.rollout_logp for it in items],
+                                      [it.loss_mask for it in items]))
         for s in range(steps):
             sub = items[s * per:(s + 1) * per]
             if not sub:
                 continue
+            if self._hook_before_step is not None:
+                self._hook_before_step(a, rollout_id, s, self.model, self.actor.opt,
+                                       getattr(self.actor.cfg, "lr_schedule", None))
             out = self.actor.train_step(sub, global_num_samples=len(sub) * self.data_world)
+            if getattr(a, "ci_save_grad_norm", None) or getattr(a, "ci_load_grad_norm", None):
+                from miles_b200.utils.ci_utils import check_grad_norm
+
+                check_grad_norm(a, out["grad_norm"], rollout_id, s, rank=self._rank())
             for k, v in out.items():
                 m[f"train/{k}" if "/" not in k else k] = v
         t2 = time.perf_counter()

@@ -343,7 +343,6 @@ def add_reward_args(p):
     g = p.add_argument_group("reward")
     g.add_argument("--rm-type", default=None)
     g.add_argument("--reward-key", default=None)
-    g.add_argument("--eval-reward-key-dup", dest="_unused_eval_reward_key", default=None, help=argparse.SUPPRESS)
     g.add_argument("--group-rm", action="store_true", default=False)
     g.add_argument("--rm-url", default=None)
     g.add_argument("--custom-rm-path", default=None)

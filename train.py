@@ -60,6 +60,9 @@ def setup(args):
         actor._ensure_grads()
         info = load_checkpoint(args.load, model, actor.opt, load_optim=not args.no_load_optim)
         restore_schedule(actor, info)
+        from miles_b200.utils.ci_utils import check_model_hashes
+
+        check_model_hashes(args, model, info["iteration"], ctx.rank)
         start = info.get("extra", {}).get("rollout_id", info["iteration"]) + 1
         data_source.load(start - 1)
     if args.start_rollout_id is not None:
@@ -114,6 +117,9 @@ def train(args):
             save_checkpoint(args.save, rollout_id, model, actor.opt, extra={"rollout_id": rollout_id, **schedule_state(actor)},
                             save_optim=not args.no_save_optim, async_save=args.async_save)
             data_source.save(rollout_id)
+            from miles_b200.utils.ci_utils import save_model_hashes
+
+            save_model_hashes(args, model, rollout_id, ctx.rank)
             if args.save_hf:
                 from miles_b200.checkpoint.hf import save_hf
 
