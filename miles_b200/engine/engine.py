@@ -19,6 +19,7 @@ torch_memory_saver release/resume of KV memory (E15).
 from __future__ import annotations
 
 import math
+import threading
 import time
 from dataclasses import dataclass, field
 
@@ -172,6 +173,10 @@ class RolloutEngine:
         self.graph_launches: dict[int, int] = {}
         self.pool = None
         self.aborted = False
+        self.dead = False            # set by a failed health check / injected crash
+        self._lock = threading.Lock()
+        self._inbox: list = []       # (GenRequest, callback) submitted while generate() runs
+        self._serving = False
         self.stats = {}
         self.n_moe = sum(1 for i in range(self.cfg.num_layers) if self.cfg.layer_is_moe(i))
         self.native = _lib.use_native(torch.empty(0, device=self.dev))
@@ -328,23 +333,45 @@ class RolloutEngine:
     def abort(self):
         self.aborted = True
 
-    def generate(self, reqs: list[GenRequest], stop_when=None) -> list[GenResult]:
+    def submit(self, items: list) -> bool:
+        """Hand [(GenRequest, callback(GenResult))] to a generate() call that is running in
+        another thread: they join its batch at its next host visit (continuous batching across
+        callers). Returns False when no call is running (the caller starts one)."""
+        with self._lock:
+            if not self._serving:
+                return False
+            self._inbox.extend(items)
+            return True
+
+    def health_check(self) -> bool:
+        """Liveness probe: not marked dead, and no kernel has reported a failed bounded wait."""
+        if self.dead:
+            return False
+        if self.dev.type == "cuda" and self.native:
+            code = _lib.peek_device_error()
+            if code:
+                return False
+        return True
+
+    def generate(self, reqs: list[GenRequest], stop_when=None, callbacks=None) -> list[GenResult]:
         """Continuous batching with the decode loop on the device: requests are admitted whenever
         a slot and enough KV pages are free (prefilled as a packed batch; their slots join the
         running batch), the batch runs `steps_per_sync` decode steps per host visit (finished
         sequences freeze on the device), and finished sequences leave at the next visit.
+        Requests that other threads `submit()` while the call runs join it the same way.
 
         stop_when(results): checked at every host visit with the finished results so far (rid ->
         GenResult); when it returns True the call aborts the rest (partial rollout: unfinished
-        sequences return their tokens so far with finish_reason "abort")."""
+        sequences return their tokens so far with finish_reason "abort").
+        callbacks: {rid: fn(GenResult)} for requests whose result is delivered by callback (as
+        it finishes) instead of in the returned list."""
+        if self.dead:
+            raise RuntimeError("rollout engine is marked dead (recover it first)")
         self.resume_memory()
         ds = self.ds
-        if self.n_moe and any(r.return_routed_experts for r in reqs):
-            if self.cfg.num_experts > 256:
-                raise ValueError("routed-expert recording stores expert ids as uint8 (<= 256 experts)")
-            ds.ensure_exp()
         self.aborted = False
         results: dict[int, GenResult] = {}
+        cbs = dict(callbacks or {})
         pending = list(reqs)
         live: dict[int, _Seq] = {}           # slot -> sequence
         free_slots = list(range(self.max_batch - 1, -1, -1))
@@ -352,7 +379,29 @@ class RolloutEngine:
         n_decode_steps = n_prefills = n_syncs = 0
         cur_rows: tuple | None = None
         cur_key = None
-        while (pending or live) and not self.aborted:
+
+        def finish(res: GenResult):
+            cb = cbs.pop(res.rid, None)
+            if cb is not None:
+                cb(res)
+            else:
+                results[res.rid] = res
+
+        with self._lock:
+            self._serving = True
+        while True:
+            with self._lock:
+                for r, cb in self._inbox:
+                    pending.append(r)
+                    cbs[r.rid] = cb
+                self._inbox = []
+                if self.aborted or not (pending or live):
+                    self._serving = False
+                    break
+            if self.n_moe and any(r.return_routed_experts for r in pending) and ds.out_exp is None:
+                if self.cfg.num_experts > 256:
+                    raise ValueError("routed-expert recording stores expert ids as uint8 (<= 256 experts)")
+                ds.ensure_exp()
             if pending and free_slots:
                 new, pending = self._admit(pending, len(free_slots))
                 if new:
@@ -387,7 +436,7 @@ class RolloutEngine:
                 if done[sl]:
                     sq = live.pop(sl)
                     sq.done = True
-                    results[sq.req.rid] = self._result(sq, int(nout[sl]))
+                    finish(self._result(sq, int(nout[sl])))
                     self.free_pages.extend(sq.pages)
                     free_slots.append(sl)
             if stop_when is not None and stop_when(results):
@@ -395,14 +444,14 @@ class RolloutEngine:
         if self.aborted:
             done, nout = self._read_flags()
             for sl, sq in list(live.items()):
-                results[sq.req.rid] = self._result(sq, int(nout[sl]), reason="abort")
+                finish(self._result(sq, int(nout[sl]), reason="abort"))
                 self.free_pages.extend(sq.pages)
                 ds.s_done[sl] = 1
             for r in pending:
-                results[r.rid] = GenResult(r.rid, [], [], "abort", None, self.model.weight_version)
+                finish(GenResult(r.rid, [], [], "abort", None, self.model.weight_version))
         self.stats = {"wall_s": time.perf_counter() - t0, "decode_steps": n_decode_steps,
                       "prefills": n_prefills, "host_syncs": n_syncs}
-        return [results[r.rid] for r in reqs]
+        return [results[r.rid] for r in reqs if r.rid in results]
 
     def _read_flags(self):
         """Done flags and generated counts of every slot (one small device->host copy)."""

@@ -116,3 +116,9 @@ def check_device_error(device: torch.device | None = None, clear: bool = True) -
         if clear:
             t.zero_()
         raise DeviceKernelError(f"device kernel error {code}: {_ERR_NAMES.get(code, 'unknown')}")
+
+
+def peek_device_error(device: torch.device | None = None) -> int:
+    """The device error word of `device` (0 = none) without clearing it or raising."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    return int(err_word(device).item())

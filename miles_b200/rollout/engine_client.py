@@ -50,6 +50,8 @@ class LocalEngineClient:
         self._pending: list[tuple[GenRequest, asyncio.Future]] = []
         self._lock = threading.Lock()
         self._runner: asyncio.Task | None = None
+        self._serve = None  # executor future of the running engine.generate call
+        self._outstanding = 0
         self._rid = 0
         self.num_requests = 0
 
@@ -69,25 +71,45 @@ class LocalEngineClient:
         self.num_requests += 1
         if self._runner is None or self._runner.done():
             self._runner = asyncio.ensure_future(self._run())
-        res = await fut
+        self._outstanding += 1
+        try:
+            res = await fut
+        finally:
+            self._outstanding -= 1
+            if (self._outstanding == 0 and not self._pending and self._runner is not None
+                    and not self._runner.done() and (self._serve is None or self._serve.done())):
+                self._runner.cancel()  # nothing left to feed: stop the feeder task
+        if isinstance(res, Exception):
+            raise res
         return _result_dict(res, self.tokenizer)
 
     async def _run(self):
+        """Feed queued requests to the engine: into the running generate() call when there is
+        one (they join its batch at its next host visit), else into a new call on a worker
+        thread. Results come back per request as each finishes."""
         loop = asyncio.get_running_loop()
-        while self._pending:
+        while self._pending or (self._serve is not None and not self._serve.done()):
             await asyncio.sleep(self.max_wait_s)
-            batch, self._pending = self._pending[: self.max_batch], self._pending[self.max_batch:]
-            reqs = [r for r, _ in batch]
-            try:
-                results = await loop.run_in_executor(None, self.engine.generate, reqs)
-            except Exception as e:  # propagate to every waiter
-                for _, f in batch:
-                    if not f.done():
-                        f.set_exception(e)
+            batch, self._pending = self._pending, []
+            if not batch:
                 continue
-            for (_, f), r in zip(batch, results):
-                if not f.done():
-                    f.set_result(r)
+            items = [(req, self._deliver(loop, fut)) for req, fut in batch]
+            if not self.engine.submit(items):
+                self._serve = loop.run_in_executor(None, self._serve_items, items)
+
+    @staticmethod
+    def _deliver(loop, fut):
+        def cb(res):
+            loop.call_soon_threadsafe(lambda: fut.done() or fut.set_result(res))
+        return cb
+
+    def _serve_items(self, items):
+        futs = {req.rid: cb for req, cb in items}
+        try:
+            self.engine.generate([r for r, _ in items], callbacks=futs)
+        except Exception as e:  # propagate to every waiter of this call
+            for req, cb in items:
+                cb(e)
 
     def abort(self):
         """Abort in-flight generations (they finish with finish_reason 'abort')."""
@@ -99,7 +121,7 @@ class LocalEngineClient:
         self._pending = []
 
     async def health(self) -> bool:
-        return True
+        return self.engine.health_check()
 
 
 class HttpEngineClient:

@@ -87,3 +87,32 @@ def test_rank_departure_detected(tmp_path):
                         "--master-addr", "127.0.0.1", "--master-port", str(free_port()), str(p)],
                        env=env, capture_output=True, text=True, timeout=110)
     assert "DETECTED rank 1 left the job" in r.stdout, r.stdout + r.stderr[-2000:]
+
+
+def test_train_recovers_engine_after_injected_crash(tmp_path, monkeypatch):
+    """--use-fault-tolerance with --ci-test: a host-side crash is injected into the rollout
+    engine at rollout 1; the supervisor rebuilds it before that rollout and training goes on."""
+    monkeypatch.setenv("MILES_B200_FORCE_CPU", "1")
+    import json
+
+    import numpy as np
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    rng = np.random.default_rng(0)
+    with open(tmp_path / "d.jsonl", "w") as f:
+        for _ in range(8):
+            f.write(json.dumps({"input": rng.integers(0, 4096, 32).tolist(), "label": "1"}) + "\n")
+    sys.path.insert(0, root)
+    import train as T
+    from miles_b200.rollout.default import GenerateState
+    from miles_b200.utils.arguments import parse_args
+
+    GenerateState._inst = None
+    args = parse_args(["--model-name", "tiny", "--prompt-data", str(tmp_path / "d.jsonl"),
+                       "--label-key", "label", "--rollout-batch-size", "2", "--n-samples-per-prompt", "2",
+                       "--rollout-max-response-len", "8", "--rm-type", "random", "--num-rollout", "3",
+                       "--actor-num-gpus-per-node", "1", "--ci-test", "--use-fault-tolerance",
+                       "--rollout-health-check-interval", "0.2", "--rollout-health-check-timeout", "5"])
+    hist = T.train(args)
+    assert len(hist) == 3
+    assert [h["fault_tolerance/recoveries"] for h in hist] == [0, 1, 1]

@@ -98,3 +98,27 @@ def test_partial_rollout_over_sampling_cpu():
                                        rid=0)])[0]
         assert ref.tokens == s.tokens[plen:]
         assert np.allclose(ref.logprobs, s.rollout_log_probs, atol=1e-5)
+
+
+def test_engine_client_joins_running_batch_cpu():
+    """Requests that arrive while a generate() call runs join its batch (engine.submit) instead
+    of waiting for the whole wave; results equal standalone generation (same seeds)."""
+    import asyncio
+
+    from miles_b200.rollout.engine_client import LocalEngineClient
+
+    m = _model()
+    eng = RolloutEngine(m, max_batch=8, num_pages=128, use_cuda_graph=False, steps_per_sync=2)
+    client = LocalEngineClient(eng)
+    p1, p2 = list(range(5, 25)), list(range(40, 52))
+
+    async def run():
+        t1 = asyncio.ensure_future(client.generate(p1, {"max_new_tokens": 40, "sampling_seed": 1}))
+        await asyncio.sleep(0.3)  # the first call is decoding by now
+        t2 = asyncio.ensure_future(client.generate(p2, {"max_new_tokens": 6, "sampling_seed": 2}))
+        return await t1, await t2
+
+    r1, r2 = asyncio.run(run())
+    assert eng.stats["prefills"] >= 1
+    ref = eng.generate([GenRequest(p1, 40, seed=1, rid=0), GenRequest(p2, 6, seed=2, rid=1)])
+    assert r1["output_ids"] == ref[0].tokens and r2["output_ids"] == ref[1].tokens

@@ -69,6 +69,10 @@ def setup(args):
         start = args.start_rollout_id
     trainer.init_ref()
     tracker = Tracker(args, ctx.rank)
+    from miles_b200.orchestration.fault_tolerance import EngineSupervisor, default_store
+
+    manager.supervisor = EngineSupervisor(args, engine, lambda: build_engine(args, engine_model, ctx),
+                                          client, ctx.rank, ctx.world, default_store())
     return ctx, model, actor, engine, manager, trainer, tracker, start, data_source
 
 
@@ -90,7 +94,9 @@ def train(args):
             from miles_b200.parallel.reloadable import REGISTRY
 
             REGISTRY.destroy()
+        engine = manager.supervisor.before_rollout(rollout_id)  # recovers a dead engine
         data = manager.generate(rollout_id)
+        manager.supervisor.after_rollout()
         engine.release_memory()
         if reload_groups:
             REGISTRY.reload([ctx, model, actor, trainer, _pp._TIED_GROUPS])
@@ -135,10 +141,13 @@ def train(args):
                     save_hf(model, args.save_hf.format(rollout_id=rollout_id))
         # colocated refit: the engine reads the trainer's parameter buffer in place
         m["rollout/weight_version"] = model.weight_version
+        if manager.supervisor.enabled:
+            m["fault_tolerance/recoveries"] = manager.supervisor.recoveries
         if should_run_periodic_action(rollout_id, args.eval_interval, num_rollout):
             m.update(manager.eval(rollout_id))
         tracker.log(m, rollout_id)
     wait_async_save()
+    manager.supervisor.close()
     if args.ci_metric_checker_key:
         from miles_b200.utils.metric_checker import check_metric
 
