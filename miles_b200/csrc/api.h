@@ -97,7 +97,7 @@ int mb_logprob_bwd(const float* logits, long long ld, const int* target, int n, 
                    const float* ent, void* dlogits, long long ldd, cudaStream_t st);
 int mb_sample(const float* logits, long long ld, int n, int V, const float* inv_temps,
               const unsigned long long* seeds, const int* positions, int* tokens, float* logp,
-              cudaStream_t st);
+              const float* thr, cudaStream_t st);
 int mb_policy_loss(const float* logp, const float* old_logp, const float* adv, const float* weight,
                    const float* rollout_logp, const float* ref_logp, float* dlogp, float* pg_out,
                    float* part, float* metrics, int n, float eps, float eps_hi, float eps_c,

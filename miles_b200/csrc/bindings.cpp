@@ -259,11 +259,12 @@ int64_t logprob_bwd(torch::Tensor logits, torch::Tensor target, double inv_temp,
                           cur_stream());
 }
 int64_t sample(torch::Tensor logits, torch::Tensor inv_temps, torch::Tensor seeds,
-            torch::Tensor positions, torch::Tensor tokens, OT logp) {
+            torch::Tensor positions, torch::Tensor tokens, OT logp, OT thr) {
   CHECK_DT(logits, at::kFloat);
+  if (thr.has_value()) CHECK_DT(thr.value(), at::kFloat);
   return mb_sample(PT<float>(logits), logits.stride(0), logits.size(0), logits.size(1),
                      PT<float>(inv_temps), PT<unsigned long long>(seeds), PT<int>(positions),
-                     PT<int>(tokens), PT<float>(logp), cur_stream());
+                     PT<int>(tokens), PT<float>(logp), PT<float>(thr), cur_stream());
 }
 int64_t policy_loss(torch::Tensor logp, torch::Tensor old_logp, torch::Tensor adv,
                  torch::Tensor weight, OT rollout_logp, OT ref_logp, torch::Tensor dlogp,

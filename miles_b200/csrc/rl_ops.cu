@@ -117,11 +117,14 @@ MB_DEVICE uint64_t splitmix64(uint64_t x) {
 __global__ void __launch_bounds__(LS_THREADS) sample_kernel(
     const float* __restrict__ logits, long long ld, int V, const float* __restrict__ inv_temps,
     const unsigned long long* __restrict__ seeds, const int* __restrict__ positions,
-    int* __restrict__ tokens, float* __restrict__ logp) {
+    int* __restrict__ tokens, float* __restrict__ logp, const float* __restrict__ thr) {
   pdl_trigger();
   pdl_wait();
   const long long r = blockIdx.x;
   const float* z = logits + r * ld;
+  // top-k / top-p: only logits >= thr[r] take part in the draw (the reported log-prob stays the
+  // full-distribution one, which is what the trainer computes)
+  const float cut = thr ? thr[r] : -INFINITY;
   const float itemp = inv_temps[r];
   const bool greedy = itemp <= 0.f;
   const float it = greedy ? 1.f : itemp;
@@ -131,6 +134,7 @@ __global__ void __launch_bounds__(LS_THREADS) sample_kernel(
   float best = -INFINITY;
   int besti = 0x7fffffff;
   for (int i = threadIdx.x; i < V; i += LS_THREADS) {
+    if (z[i] < cut) continue;
     float score = z[i] * it;
     if (!greedy) {
       const uint64_t h = splitmix64(key ^ (uint64_t)i);
@@ -450,9 +454,10 @@ extern "C" int mb_logprob_bwd(const float* logits, long long ld, const int* targ
 
 extern "C" int mb_sample(const float* logits, long long ld, int n, int V, const float* inv_temps,
                          const unsigned long long* seeds, const int* positions, int* tokens,
-                         float* logp, cudaStream_t st) {
+                         float* logp, const float* thr, cudaStream_t st) {
   if (n == 0) return 0;
-  mb_launch(sample_kernel, n, LS_THREADS, 0, st, logits, ld, V, inv_temps, seeds, positions, tokens, logp);
+  mb_launch(sample_kernel, n, LS_THREADS, 0, st, logits, ld, V, inv_temps, seeds, positions, tokens,
+            logp, thr);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

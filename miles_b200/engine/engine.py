@@ -43,6 +43,8 @@ class GenRequest:
     stop_token_ids: tuple = ()
     return_routed_experts: bool = False
     rid: int = 0
+    top_k: int = 0          # <= 0: off
+    top_p: float = 1.0      # >= 1: off
 
 
 @dataclass
@@ -94,6 +96,8 @@ class DecodeState:
         self.s_seed = torch.zeros(S + 1, dtype=torch.int64, device=dev)
         self.s_stop = torch.full((S + 1, _NSTOP), -1, **i32)
         self.s_rec = torch.zeros(S + 1, **i32)
+        self.s_topk = torch.zeros(S + 1, **i32)
+        self.s_topp = torch.ones(S + 1, dtype=torch.float32, device=dev)
         self.out_tok = torch.zeros(S + 1, self.max_len, **i32)
         self.out_lp = torch.zeros(S + 1, self.max_len, dtype=torch.float32, device=dev)
         self.n_moe, self.topk = n_moe, topk
@@ -156,7 +160,7 @@ def _commit_ref(ds: DecodeState, st: dict, tok, lp, experts):
 class RolloutEngine:
     def __init__(self, model: Transformer, max_batch: int = 64, num_pages: int | None = None,
                  mem_fraction: float = 0.9, use_cuda_graph: bool = True, max_pages_per_seq: int = 160,
-                 steps_per_sync: int = 8, persistent_kv: bool = True):
+                 steps_per_sync: int = 8, persistent_kv: bool = True, prefill_tokens: int = 32768):
         self.model = model
         self.cfg = model.cfg
         self.dev = model.device
@@ -165,6 +169,7 @@ class RolloutEngine:
         self.max_pages_per_seq = max_pages_per_seq
         # decode steps run back to back on the device between two host visits (one graph)
         self.steps_per_sync = max(1, steps_per_sync)
+        self.prefill_tokens = prefill_tokens   # token budget of one packed prefill
         self._num_pages_req = num_pages
         self._mem_fraction = mem_fraction
         self.cache: KVCache | None = None
@@ -180,6 +185,7 @@ class RolloutEngine:
         self.stats = {}
         self.n_moe = sum(1 for i in range(self.cfg.num_layers) if self.cfg.layer_is_moe(i))
         self.native = _lib.use_native(torch.empty(0, device=self.dev))
+        self._filt = (0, False)      # sampler restriction of the running batch (graph variant)
         # fixed-address KV cache: graphs survive release / resume (GPU only)
         self.use_arena = persistent_kv and self.use_graph and self.native
         self.arena = None
@@ -215,7 +221,9 @@ class RolloutEngine:
                 free, _ = torch.cuda.mem_get_info(self.dev)
                 # the routed-expert record buffer is allocated on first use: leave room for it
                 reserve = (self.max_batch + 1) * self.ds.max_len * self.n_moe * max(self.cfg.topk, 1)
-                n = int(max(free - reserve, 0) * self._mem_fraction) // self.kv_bytes_per_page()
+                # headroom for prefill activations and the decode graphs' memory pool
+                headroom = 8 << 30
+                n = int(max(free - reserve - headroom, 0) * self._mem_fraction) // self.kv_bytes_per_page()
             else:
                 n = 1024
         n = max(n, 2)
@@ -290,8 +298,12 @@ class RolloutEngine:
                                       st["slots"], record=st["experts"] if rec_on else None,
                                       state_rows=st["state_rows"])
         # the sampled token sits at position `positions + 1`
+        kmax, use_p = self._filt
+        rows = st["rows"].long()
         tok, lp = sample_from_hidden(h, self.model.lm_head_weight(), st["inv_t"], st["seeds"],
-                                     st["positions"] + 1)
+                                     st["positions"] + 1,
+                                     top_k=ds.s_topk[rows] if kmax else None,
+                                     top_p=ds.s_topp[rows] if use_p else None, k_max=kmax)
         if self.native:
             _lib.lib().decode_commit(st["rows"], ds.S, tok, lp, st["experts"] if rec_on else None,
                                      ds.s_tok, ds.s_pos, ds.s_done, ds.s_nout, ds.s_maxnew,
@@ -302,7 +314,7 @@ class RolloutEngine:
 
     def _get_steps(self, B: int):
         """(graph or None, static inputs) running `steps_per_sync` decode steps of bucket B."""
-        key = (B, self.ds.out_exp is not None)
+        key = (B, self.ds.out_exp is not None) + self._filt
         if key in self.graphs:
             return self.graphs[key]
         st = self._static(B)
@@ -408,17 +420,30 @@ class RolloutEngine:
                     for sq in new:
                         sq.slot = free_slots.pop()
                         live[sq.slot] = sq
-                    self._prefill(new)
+                    # packed prefill in chunks of at most `prefill_tokens` tokens (a longer
+                    # prompt goes alone): bounds the activation memory next to the KV cache
+                    chunk, ntok = [], 0
+                    for sq in new:
+                        L = len(sq.req.prompt)
+                        if chunk and ntok + L > self.prefill_tokens:
+                            self._prefill(chunk)
+                            n_prefills += 1
+                            chunk, ntok = [], 0
+                        chunk.append(sq)
+                        ntok += L
+                    self._prefill(chunk)
                     n_prefills += 1
                 elif not live:
                     raise RuntimeError("KV cache too small for a single request")
             slots = sorted(live)
+            self._filt = self._filter_mode(live.values())
             Bb = self._bucket(len(slots))
             g, st = self._get_steps(Bb)
             rows = tuple(slots) + (self.max_batch,) * (Bb - len(slots))
-            if rows != cur_rows or (Bb, ds.out_exp is not None) != cur_key:
+            key = (Bb, ds.out_exp is not None) + self._filt
+            if rows != cur_rows or key != cur_key:
                 st["rows"].copy_(torch.tensor(rows, dtype=torch.int32), non_blocking=False)
-                cur_rows, cur_key = rows, (Bb, ds.out_exp is not None)
+                cur_rows, cur_key = rows, key
             if self.dev.type == "cuda":
                 torch.cuda.nvtx.range_push("decode_steps")
             if g is not None:
@@ -452,6 +477,15 @@ class RolloutEngine:
         self.stats = {"wall_s": time.perf_counter() - t0, "decode_steps": n_decode_steps,
                       "prefills": n_prefills, "host_syncs": n_syncs}
         return [results[r.rid] for r in reqs if r.rid in results]
+
+    @staticmethod
+    def _filter_mode(seqs) -> tuple:
+        """(k_max, top_p on) of the sampler for these sequences: k_max is the largest top_k
+        rounded up to a power of two (few graph variants), 0 when no row restricts."""
+        k = max((s.req.top_k for s in seqs), default=0)
+        use_p = any(s.req.top_p < 1.0 for s in seqs)
+        kmax = 1 << (int(k) - 1).bit_length() if k > 0 else 0
+        return (kmax, use_p)
 
     def _read_flags(self):
         """Done flags and generated counts of every slot (one small device->host copy)."""
@@ -505,8 +539,12 @@ class RolloutEngine:
         inv_t = torch.tensor(invt_h, dtype=torch.float32, device=dev)
         seeds = torch.tensor(seed_h, dtype=torch.int64, device=dev)
         posn = torch.tensor(plen_h, dtype=torch.int32, device=dev)
+        kmax, use_p = self._filter_mode(wave)
+        topk = torch.tensor([s.req.top_k for s in wave], dtype=torch.int32, device=dev)
+        topp = torch.tensor([float(s.req.top_p) for s in wave], dtype=torch.float32, device=dev)
         tok, lp = sample_from_hidden(h.index_select(0, last).contiguous(), self.model.lm_head_weight(),
-                                     inv_t, seeds, posn)
+                                     inv_t, seeds, posn, top_k=topk if kmax else None,
+                                     top_p=topp if use_p else None, k_max=kmax)
         n = len(wave)
         pt = np.zeros((n, self.max_pages_per_seq), np.int32)
         stop = np.full((n, _NSTOP), -1, np.int32)
@@ -522,6 +560,8 @@ class RolloutEngine:
         ds.s_stop[sl] = stop_d
         ds.s_invt[sl] = inv_t
         ds.s_seed[sl] = seeds
+        ds.s_topk[sl] = topk
+        ds.s_topp[sl] = topp
         ds.s_maxnew[sl] = maxnew
         ds.s_rec[sl] = torch.tensor([int(s.req.return_routed_experts) for s in wave],
                                     dtype=torch.int32, device=dev)

@@ -154,6 +154,10 @@ class LoRAOptimizer:
         self.opt.step()
         self.opt.zero_grad(set_to_none=True)
 
+    def reset_state(self) -> None:
+        self.step_id = 0
+        self.opt.state.clear()
+
     def state_dict(self) -> dict:
         return {"step": self.step_id, "adam": self.opt.state_dict()}
 

@@ -486,7 +486,8 @@ class Transformer(torch.nn.Module):
         activation recompute when training. `replay_experts` [T, L_moe, k] is sliced to layer i's
         MoE column (and to `rows`, a slice of this rank's rows, if given)."""
         m = None
-        for i in (self.layer_ids if layers is None else layers):
+        rc_limit = getattr(self, "recompute_layers", None)  # recompute only the first N (block)
+        for li, i in enumerate(self.layer_ids if layers is None else layers):
             replay = None
             if i in self.router_cfgs and replay_experts is not None:
                 col = replay_experts[:, self.moe_index[i]]
@@ -494,7 +495,8 @@ class Transformer(torch.nn.Module):
             # layers that exchange point-to-point messages in their forward (linear attention
             # under CP) are not recomputed: a recompute would send the messages twice
             p2p = self.cp is not None and self.cfg.layer_is_linear(i)
-            if self.recompute and torch.is_grad_enabled() and not p2p:
+            if (self.recompute and torch.is_grad_enabled() and not p2p
+                    and (rc_limit is None or li < rc_limit)):
                 if m is None:
                     m, r = checkpoint(lambda rr, i=i, rp=replay: layer_fn(i, None, rr, rp), r,
                                       use_reentrant=False)

@@ -88,26 +88,56 @@ def lm_head_logprob(h: torch.Tensor, W: torch.Tensor, targets: torch.Tensor,
     return _LMHeadLogProb.apply(h, W, targets.int().contiguous(), 1.0 / temperature, chunk)
 
 
+def sampling_threshold(z: torch.Tensor, inv_temps: torch.Tensor, top_k: torch.Tensor | None,
+                       top_p: torch.Tensor | None, k_max: int) -> torch.Tensor:
+    """Per-row logit threshold of top-k / top-p sampling: tokens with z >= thr are kept.
+    top_k int32 [B] (<= 0: off; at most k_max), top_p fp32 [B] (>= 1: off). The nucleus is the
+    smallest prefix of the tokens sorted by probability (at the row's temperature) whose mass
+    reaches top_p. Runs without host synchronisation (capturable in a CUDA graph)."""
+    B = z.shape[0]
+    thr = torch.full((B,), float("-inf"), dtype=torch.float32, device=z.device)
+    if top_k is not None and k_max > 0:
+        vals = torch.topk(z, k_max, dim=1).values                     # [B, k_max] descending
+        k = top_k.long().clamp(1, k_max) - 1
+        tk = vals.gather(1, k[:, None])[:, 0]
+        thr = torch.where(top_k > 0, torch.maximum(thr, tk), thr)
+    if top_p is not None:
+        it = torch.where(inv_temps > 0, inv_temps, torch.ones_like(inv_temps))
+        srt, _ = torch.sort(z, dim=1, descending=True)
+        p = torch.softmax(srt * it[:, None], dim=1)
+        before = torch.cumsum(p, dim=1) - p                              # mass of the better tokens
+        n_keep = (before < top_p[:, None]).sum(1).clamp_min(1)
+        tp = srt.gather(1, (n_keep - 1)[:, None])[:, 0]
+        thr = torch.where(top_p < 1.0, torch.maximum(thr, tp), thr)
+    return thr
+
+
 def sample_from_hidden(h: torch.Tensor, W: torch.Tensor, inv_temps: torch.Tensor,
                        seeds: torch.Tensor, positions: torch.Tensor,
-                       logits_buf: torch.Tensor | None = None):
+                       logits_buf: torch.Tensor | None = None, top_k: torch.Tensor | None = None,
+                       top_p: torch.Tensor | None = None, k_max: int = 0):
     """Sample one token per row of h [B,H]. inv_temps fp32 [B] (<=0 => greedy), seeds int64 [B],
-    positions int32 [B] (position of the sampled token). Returns (tokens int32, logp fp32)."""
+    positions int32 [B] (position of the sampled token); optional per-row top_k / top_p
+    (see sampling_threshold). Returns (tokens int32, logp fp32): logp is the log-prob of the
+    sampled token under the full temperature-scaled distribution (the trainer's log-prob)."""
     B = h.shape[0]
     V = W.shape[0]
+    filt = top_k is not None or top_p is not None
     if not use_native(h):
         z = h.float() @ W.float().t()
         it = inv_temps.float()
         greedy = it <= 0
         zz = z * torch.where(greedy, torch.ones_like(it), it)[:, None]
+        thr = sampling_threshold(z, it, top_k, top_p, k_max) if filt else None
         gen = torch.Generator(device=h.device)
         toks = []
         for b in range(B):
+            row = zz[b] if thr is None else torch.where(z[b] >= thr[b], zz[b], torch.full_like(zz[b], float("-inf")))
             if bool(greedy[b]):
-                toks.append(int(zz[b].argmax()))
+                toks.append(int(row.argmax()))
             else:
                 gen.manual_seed(int(seeds[b]) * 1000003 + int(positions[b]))
-                toks.append(int(torch.multinomial(zz[b].softmax(-1), 1, generator=gen)))
+                toks.append(int(torch.multinomial(row.softmax(-1), 1, generator=gen)))
         tok = torch.tensor(toks, dtype=torch.int32, device=h.device)
         lp = zz.log_softmax(-1).gather(1, tok.long()[:, None])[:, 0]
         return tok, lp
@@ -115,5 +145,6 @@ def sample_from_hidden(h: torch.Tensor, W: torch.Tensor, inv_temps: torch.Tensor
     G.matmul_nt(h, W, out=z)
     tok = torch.empty(B, dtype=torch.int32, device=h.device)
     lp = torch.empty(B, dtype=torch.float32, device=h.device)
-    lib().sample(z, inv_temps, seeds, positions, tok, lp)
+    thr = sampling_threshold(z, inv_temps, top_k, top_p, k_max).contiguous() if filt else None
+    lib().sample(z, inv_temps, seeds, positions, tok, lp, thr)
     return tok, lp

@@ -96,6 +96,10 @@ class RolloutManager:
         if self.args.load_debug_rollout_data:
             with open(self.args.load_debug_rollout_data.format(rollout_id=rollout_id), "rb") as f:
                 groups = pickle.load(f)["samples"]
+            frac = getattr(self.args, "load_debug_rollout_data_subsample", None)
+            if frac is not None and 0 < frac < 1:  # keep a deterministic fraction of the groups
+                keep = max(1, int(round(len(groups) * frac)))
+                groups = groups[:keep]
             metrics = {}
         else:
             la = self._local_args()
@@ -110,6 +114,7 @@ class RolloutManager:
             os.makedirs(os.path.dirname(path) or ".", exist_ok=True)
             with open(path, "wb") as f:
                 pickle.dump({"rollout_id": rollout_id, "samples": groups}, f)
+        groups = self._trim(groups)
         samples = [s for g in groups for s in g]
         dt = time.perf_counter() - t0
         if self.custom_rollout_log is not None and self.custom_rollout_log(rollout_id, self.args, samples,
@@ -121,6 +126,26 @@ class RolloutManager:
         self.last_metrics = metrics
         data["metrics"] = metrics
         return data
+
+    def _trim(self, groups):
+        """Drop trailing groups so this rank's sample count is a multiple of its share of
+        --global-batch-size (dynamic filtering can return more); --disable-rollout-trim-samples
+        keeps them all."""
+        a = self.args
+        if getattr(a, "disable_rollout_trim_samples", False) or not groups or not a.global_batch_size:
+            return groups
+        per_rank = max(1, a.global_batch_size // self.world)
+        n = sum(len(g) for g in groups)
+        if n <= per_rank or n % per_rank == 0:
+            return groups
+        target = n // per_rank * per_rank
+        out, c = [], 0
+        for g in groups:
+            if c + len(g) > target:
+                break
+            out.append(g)
+            c += len(g)
+        return out or groups
 
     def eval(self, rollout_id: int) -> dict:
         out = self.eval_fn(self.args, rollout_id, self.data_source, evaluation=True)
@@ -199,6 +224,23 @@ class RolloutManager:
                 m["rollout/zero_std/count"] = int((g.std(1) == 0).sum())
         except Exception:
             pass
+        a = self.args
+        if getattr(a, "log_correct_samples", False):
+            ok = [s for s in samples if (s.get_reward_value(a) or 0) > 0]
+            m["rollout/correct_samples"] = len(ok)
+            if ok:
+                m["rollout/correct_response_len/mean"] = float(np.mean([s.response_length for s in ok]))
+        if getattr(a, "log_multi_turn", False):
+            turns = [s.metadata.get("num_turns", s.metadata.get("turn", 1)) for s in samples]
+            m["rollout/multi_turn/turns_mean"] = float(np.mean(turns))
+            m["rollout/multi_turn/turns_max"] = int(np.max(turns))
+        cat_key = getattr(a, "log_reward_category", None)
+        if cat_key:  # mean reward per value of sample.metadata[<key>] (e.g. the task / source)
+            by: dict = {}
+            for s in samples:
+                by.setdefault(str(s.metadata.get(cat_key, "none")), []).append(s.get_reward_value(a))
+            for k, v in by.items():
+                m[f"rollout/reward_category/{k}"] = float(np.mean(v))
         wv = [s.weight_versions[-1] for s in samples if s.weight_versions]
         if wv:
             m["rollout/weight_version"] = max(int(v) for v in wv)

@@ -49,6 +49,10 @@ def _groups(world: int, size: int):
 
 
 def init_distributed(args) -> ProcessContext:
+    # --train-env-vars: JSON object of environment variables for the training process
+    env = getattr(args, "train_env_vars", None)
+    if env and env != "{}":
+        os.environ.update({k: str(v) for k, v in json.loads(env).items()})
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -186,9 +190,14 @@ def load_tokenizer(args):
     try:
         from transformers import AutoTokenizer
 
-        return AutoTokenizer.from_pretrained(args.hf_checkpoint, trust_remote_code=True)
+        tok = AutoTokenizer.from_pretrained(args.hf_checkpoint, trust_remote_code=True)
     except Exception:
         return None
+    if getattr(args, "chat_template_path", None):
+        # --chat-template-path: a Jinja chat template file replacing the tokenizer's own
+        with open(args.chat_template_path) as f:
+            tok.chat_template = f.read()
+    return tok
 
 
 def build_model(args, ctx: ProcessContext) -> Transformer:
@@ -213,6 +222,15 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
                         etp=getattr(args, "expert_tensor_parallel_size", None),
                         tp_cap_rows=max(4096, getattr(args, "max_tokens_per_gpu", 0) or 0))
     model.mtp_train = bool(getattr(args, "enable_mtp_training", False))
+    # activation recompute (Megatron flags): granularity "full" recomputes whole layers; method
+    # "block" limits it to the first --recompute-num-layers layers of this rank ("uniform"
+    # recomputes every layer, one checkpoint per layer); granularity "none" stores activations
+    gran = getattr(args, "recompute_granularity", "full") or "none"
+    if gran not in ("full", "selective", "none"):
+        raise ValueError(f"unknown --recompute-granularity {gran}")
+    model.recompute = gran != "none"
+    if gran != "none" and getattr(args, "recompute_method", "uniform") == "block":
+        model.recompute_layers = int(args.recompute_num_layers)
     if getattr(args, "sequence_parallel", False) and model.tp is not None:
         model.sequence_parallel = True
     if getattr(args, "vocab_parallel_logprob", False) and model.tp is not None:
@@ -271,7 +289,8 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                       adam_eps=args.adam_eps, lr_schedule=schedule_from_args(args), tis_args=args,
                       micro_batching="balanced" if args.use_dynamic_batch_size else "fixed",
                       micro_batch_size=args.micro_batch_size,
-                      log_probs_max_tokens_per_gpu=args.log_probs_max_tokens_per_gpu)
+                      log_probs_max_tokens_per_gpu=args.log_probs_max_tokens_per_gpu,
+                      memory_margin_bytes=args.train_memory_margin_bytes)
     if getattr(args, "train_backend", "b200") == "fsdp":
         # HF model under FSDP2 (trainer/fsdp_actor.py); `model` is then the engine's Transformer,
         # refreshed from the gathered HF state after every step

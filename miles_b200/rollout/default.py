@@ -251,17 +251,23 @@ async def eval_rollout(args, rollout_id: int) -> RolloutFnEvalOutput:
         it = iter(args.eval_prompt_data)
         datasets = [{"name": n, "path": p} for n, p in zip(it, it)]
     for ds in datasets:
-        d = Dataset(ds["path"], state.tokenizer, prompt_key=args.eval_input_key or args.input_key,
-                    label_key=args.eval_label_key or args.label_key,
-                    tool_key=getattr(args, "eval_tool_key", None) or getattr(args, "tool_key", None))
-        sp = dict(state.sampling_params, temperature=args.eval_temperature,
-                  max_new_tokens=args.eval_max_response_len)
-        if getattr(args, "eval_top_p", None) is not None:
-            sp["top_p"] = args.eval_top_p
-        if getattr(args, "eval_top_k", None) is not None:
-            sp["top_k"] = args.eval_top_k
-        if getattr(args, "eval_min_new_tokens", None):
-            sp["min_new_tokens"] = args.eval_min_new_tokens
+        # per-dataset settings (--eval-config) fall back to the eval flags
+        opt = lambda key, flag: ds.get(key) if ds.get(key) is not None else getattr(args, flag, None)  # noqa: E731
+        d = Dataset(ds["path"], state.tokenizer, prompt_key=opt("input_key", "eval_input_key") or args.input_key,
+                    label_key=opt("label_key", "eval_label_key") or args.label_key,
+                    tool_key=opt("tool_key", "eval_tool_key") or getattr(args, "tool_key", None))
+        sp = dict(state.sampling_params, temperature=opt("temperature", "eval_temperature"),
+                  max_new_tokens=opt("max_response_len", "eval_max_response_len"))
+        for key, flag in (("top_p", "eval_top_p"), ("top_k", "eval_top_k"),
+                          ("min_new_tokens", "eval_min_new_tokens"), ("stop_token_ids", None)):
+            v = ds.get(key) if ds.get(key) is not None else (getattr(args, flag, None) if flag else None)
+            if v is not None:
+                sp[key] = v
+        n_per = int(opt("n_samples_per_eval_prompt", "n_samples_per_eval_prompt") or 1)
+        dargs = args
+        if ds.get("rm_type"):
+            dargs = copy.copy(args)
+            dargs.rm_type = ds["rm_type"]
         max_prompt = getattr(args, "eval_max_prompt_len", None)
         max_ctx = getattr(args, "eval_max_context_len", None)
         tasks = []
@@ -272,14 +278,14 @@ async def eval_rollout(args, rollout_id: int) -> RolloutFnEvalOutput:
             if max_ctx:  # --eval-max-context-len caps prompt + response
                 spp = dict(sp, max_new_tokens=max(0, min(sp["max_new_tokens"] or max_ctx,
                                                          max_ctx - len(s.tokens))))
-            for k in range(args.n_samples_per_eval_prompt):
+            for k in range(n_per):
                 c = copy.deepcopy(s)
-                c.index = (s.index or 0) * args.n_samples_per_eval_prompt + k
-                tasks.append(generate_and_rm(args, c, spp, evaluation=True))
+                c.index = (s.index or 0) * n_per + k
+                tasks.append(generate_and_rm(dargs, c, spp, evaluation=True))
         samples = await asyncio.gather(*tasks)
         key = getattr(args, "eval_reward_key", None)
         rewards = [(s.reward.get(key, 0.0) if key and isinstance(s.reward, dict) else
-                    s.get_reward_value(args)) if s.reward is not None else 0.0 for s in samples]
+                    s.get_reward_value(dargs)) if s.reward is not None else 0.0 for s in samples]
         out[ds["name"]] = {"rewards": rewards, "samples": samples,
                            "truncated": [int(s.status == Sample.Status.TRUNCATED) for s in samples]}
         metrics[f"eval/{ds['name']}"] = float(np.mean(rewards)) if rewards else 0.0
@@ -288,6 +294,6 @@ async def eval_rollout(args, rollout_id: int) -> RolloutFnEvalOutput:
         if getattr(args, "log_passrate", False):
             from miles_b200.utils.metric_utils import compute_pass_rate
 
-            for k, v in compute_pass_rate(rewards, args.n_samples_per_eval_prompt).items():
+            for k, v in compute_pass_rate(rewards, n_per).items():
                 metrics[f"eval/{ds['name']}-{k}"] = v
     return RolloutFnEvalOutput(out, metrics)

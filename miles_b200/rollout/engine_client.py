@@ -40,6 +40,24 @@ def _result_dict(res, tokenizer=None) -> dict:
     return {"output_ids": res.tokens, "text": text, "meta_info": meta}
 
 
+def _truncate_at_stop(res, stops: list[str], tokenizer):
+    """Stop strings: cut the response after the first token whose decoded prefix contains a stop
+    string (tokens, log-probs and routing cut alike; finish reason "stop"). The engine stops on
+    token ids on the device; strings are matched here on the text."""
+    text = ""
+    for i in range(len(res.tokens)):
+        text = tokenizer.decode(res.tokens[: i + 1])
+        if any(s and s in text for s in stops):
+            import dataclasses
+
+            ex = res.routed_experts
+            if ex is not None:
+                ex = ex[: len(ex) - (len(res.tokens) - (i + 1))]
+            return dataclasses.replace(res, tokens=res.tokens[: i + 1], logprobs=res.logprobs[: i + 1],
+                                       finish_reason="stop", routed_experts=ex)
+    return res
+
+
 class LocalEngineClient:
     def __init__(self, engine: RolloutEngine, tokenizer=None, max_wait_s: float = 0.002,
                  max_batch: int | None = None):
@@ -66,7 +84,8 @@ class LocalEngineClient:
                          max_new_tokens=int(sampling_params.get("max_new_tokens", 128)),
                          temperature=temp, seed=int(sampling_params.get("sampling_seed", self._rid)),
                          stop_token_ids=stop, return_routed_experts=return_routed_experts,
-                         rid=self._rid)
+                         rid=self._rid, top_k=int(sampling_params.get("top_k", 0) or 0),
+                         top_p=float(sampling_params.get("top_p", 1.0) or 1.0))
         self._pending.append((req, fut))
         self.num_requests += 1
         if self._runner is None or self._runner.done():
@@ -81,6 +100,10 @@ class LocalEngineClient:
                 self._runner.cancel()  # nothing left to feed: stop the feeder task
         if isinstance(res, Exception):
             raise res
+        stops = sampling_params.get("stop")
+        if stops and self.tokenizer is not None:
+            res = _truncate_at_stop(res, [stops] if isinstance(stops, str) else list(stops),
+                                    self.tokenizer)
         return _result_dict(res, self.tokenizer)
 
     async def _run(self):

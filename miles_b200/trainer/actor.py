@@ -78,6 +78,7 @@ class ActorConfig:
     log_probs_max_tokens_per_gpu: int | None = None
     lr_schedule: "LRSchedule | None" = None   # None: constant `lr`
     tis_args: object = None   # namespace handed to a custom TIS function (e.g. MIS settings)
+    memory_margin_bytes: int = 0   # device memory kept free when placing the optimizer state
 
 
 def pack_microbatches(lengths: list[int], max_tokens: int) -> list[list[int]]:
@@ -159,6 +160,7 @@ class Actor:
                                 weight_decay=self.cfg.weight_decay,
                                 clip_grad=self.cfg.clip_grad, placement=self.cfg.optimizer_placement,
                                 host_state=self._host_state,
+                                memory_margin=self.cfg.memory_margin_bytes,
                                 dp_group=self.dp_group if self._sharded() else None,
                                 **self._norm_scope())
 
@@ -174,6 +176,7 @@ class Actor:
         ns = n // world
         if cfg.optimizer_placement == "auto":
             free, _ = torch.cuda.mem_get_info(m.device)
+            free -= cfg.memory_margin_bytes
             grad_bytes = n * torch.empty((), dtype=cfg.grad_dtype).element_size()
             if not 12 * ns > 0.8 * (free - grad_bytes):
                 return None

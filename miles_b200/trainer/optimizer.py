@@ -42,7 +42,7 @@ class FlatAdam:
                  betas=(0.9, 0.98), eps: float = 1e-8, weight_decay: float = 0.0,
                  clip_grad: float = 1.0, placement: str = "auto", chunk: int = 1 << 28,
                  seed: int = 1234, dp_group=None, norm_group=None, norm_exclude=None,
-                 expert_norm=None, host_state=None):
+                 expert_norm=None, host_state=None, memory_margin: int = 0):
         """norm_group / norm_exclude: under model parallelism (TP, PP) every rank runs its own
         optimizer over its part of the model; the gradient norm sums the squares over
         `norm_group`, leaving out this rank's flat ranges `norm_exclude` (parameters another
@@ -78,7 +78,7 @@ class FlatAdam:
             placement = "device"
             if dev.type == "cuda":
                 free, _ = torch.cuda.mem_get_info(dev)
-                if 12 * ns > 0.8 * free:
+                if 12 * ns > 0.8 * (free - memory_margin):
                     placement = "host"
         self.placement = placement
         if placement == "device":
@@ -201,6 +201,14 @@ class FlatAdam:
                 back.record(self.d2h)
             backs.append(back)
         cur.wait_stream(self.d2h)
+
+    def reset_state(self) -> None:
+        """--reset-optimizer-states: zero the moments and the step count (master copy kept)."""
+        for b in getattr(self, "_pinning", ()):
+            b.wait()
+        self.step_id = 0
+        self.m.zero_()
+        self.v.zero_()
 
     def state_dict(self) -> dict:
         return {"step": self.step_id, "m": self.m, "v": self.v, "master": self.master,

@@ -214,6 +214,8 @@ class TrainActor:
                 check_grad_norm(a, out["grad_norm"], rollout_id, s, rank=self._rank())
             for k, v in out.items():
                 m[f"train/{k}" if "/" not in k else k] = v
+        if getattr(a, "reset_optimizer_states", False) and hasattr(self.actor.opt, "reset_state"):
+            self.actor.opt.reset_state()  # fresh Adam moments for every rollout
         t2 = time.perf_counter()
         m["perf/log_probs_time"] = t1 - t0
         m["perf/actor_train_time"] = t2 - t1

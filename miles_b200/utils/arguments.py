@@ -508,6 +508,8 @@ def validate_args(args) -> None:
         args.global_batch_size = args.rollout_batch_size * args.n_samples_per_prompt
     if args.eval_temperature is None:
         args.eval_temperature = args.rollout_temperature
+    if args.eval_config:
+        args.eval_datasets = load_eval_config(args.eval_config)
     if args.eval_top_p is None:
         args.eval_top_p = args.rollout_top_p
     if args.eval_top_k is None:
@@ -538,6 +540,31 @@ def validate_args(args) -> None:
             or (args.virtual_pipeline_model_parallel_size or 1) > 1):
         raise ValueError("--decoder-first/last-pipeline-num-layers and "
                          "--virtual-pipeline-model-parallel-size need --pipeline-model-parallel-size > 1")
+
+
+def load_eval_config(path: str) -> list[dict]:
+    """--eval-config YAML: an `eval` mapping (or the root) with optional `defaults` and
+    `datasets` (a list of entries with `name`, or a mapping keyed by name). Each dataset entry
+    (path, n_samples_per_eval_prompt, temperature, top_p, top_k, max_response_len, input_key,
+    label_key, tool_key, rm_type, stop_token_ids, min_new_tokens) falls back to `defaults`,
+    then to the eval flags (reference miles/utils/eval_config.py)."""
+    with open(path) as f:
+        cfg = yaml.safe_load(f) or {}
+    if not isinstance(cfg, dict):
+        raise ValueError("--eval-config must contain a mapping at the root")
+    ev = cfg.get("eval", cfg)
+    defaults = dict(ev.get("defaults") or {})
+    ds = ev.get("datasets")
+    if isinstance(ds, dict):
+        ds = [dict(v or {}, name=v.get("name", k) if isinstance(v, dict) else k) for k, v in ds.items()]
+    if not ds:
+        raise ValueError("--eval-config defines no datasets under `eval.datasets`")
+    out = []
+    for d in ds:
+        if "name" not in d or "path" not in {**defaults, **d}:
+            raise ValueError("each eval dataset needs a `name` and a `path`")
+        out.append({**defaults, **d})
+    return out
 
 
 def reset_arg(parser: argparse.ArgumentParser, name: str, **kwargs) -> None:
