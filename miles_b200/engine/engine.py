@@ -243,17 +243,22 @@ class RolloutEngine:
             self._free_pages = list(range(self._num_pages - 1, 0, -1))  # page 0 = trash page
         return self._free_pages
 
-    def release_memory(self):
-        """Free the KV cache (mirrors release_memory_occupation(kv_cache, cuda_graph)). With the
-        arena its physical memory is unmapped and the decode graphs, their pool and the decode
-        state are kept (they are small and their addresses stay valid); otherwise the graphs
-        go too."""
+    def release_memory(self, levels=("kv_cache",)):
+        """Free the engine's memory (mirrors release_memory_occupation with the reference's
+        --offload-rollout-level tags). "kv_cache": the KV cache (with the arena its physical
+        memory is unmapped and the addresses kept); "cuda_graph": the decode graphs, their
+        memory pool and the decode state too (they are re-captured on the next rollout;
+        without this tag they stay, since the arena keeps their addresses valid). "weight" has
+        nothing to free: the colocated engine reads the trainer's parameter buffer."""
+        levels = set(levels or ())
         self.cache = None
         self._free_pages = None
+        drop_graphs = "cuda_graph" in levels or self.arena is None
         if self.arena is not None:
             self.arena.unmap()
-        else:
+        if drop_graphs:
             self.graphs.clear()
+            self.graph_launches.clear()
             self.pool = None
             self.ds = None
         if self.dev.type == "cuda":
@@ -379,6 +384,12 @@ class RolloutEngine:
         it finishes) instead of in the returned list."""
         if self.dead:
             raise RuntimeError("rollout engine is marked dead (recover it first)")
+        from miles_b200.utils import dumper
+
+        with dumper.phase("inference"):
+            return self._generate(reqs, stop_when, callbacks)
+
+    def _generate(self, reqs, stop_when, callbacks) -> list[GenResult]:
         self.resume_memory()
         ds = self.ds
         self.aborted = False

@@ -27,6 +27,7 @@ from torch.utils.checkpoint import checkpoint
 
 from miles_b200.models.config import ModelConfig
 from miles_b200.ops import gemm as G
+from miles_b200.utils import dumper as _dumper
 from miles_b200.ops.attention import PAGE, VarlenMeta, decode_attention, varlen_attention
 from miles_b200.ops.moe import RouterCfg, emit_record, moe_experts
 from miles_b200.ops.norm import (add_rms_norm, qk_norm_rope, qk_norm_rope_to_cache, rms_norm,
@@ -746,12 +747,17 @@ class Transformer(torch.nn.Module):
                 a = self._attn_train(i, x, meta)
                 x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
                 return self._mlp(i, x2, replay=replay, record=record_experts.append), r
-            return self._layer_train(i, m, r, meta, replay)
+            out = self._layer_train(i, m, r, meta, replay)
+            if _dumper.enabled():  # per-layer residual stream (--dumper-enable)
+                _dumper.dump(f"layer{i:03d}_residual", out[1])
+            return out
 
         m, r = self._run_layers(layer, r, replay_experts, layers=layers)
         if not last:
             return r if m is None else m + r
         y, _ = add_rms_norm(m, r, self.params["norm.weight"], cfg.rms_eps)
+        if _dumper.enabled():
+            _dumper.dump("final_hidden", y)
         return y
 
     # -------------------------------------------------------------------------------- inference
@@ -847,7 +853,11 @@ class Transformer(torch.nn.Module):
             rec = record.append if (record is not None and i in self.router_cfgs) else None
             pend = self._mlp_partial(i, x2, record=rec) if rec is not None else self._pending_mlp(i, x2)
             pend = self._sw_pend(i, "post_mlp_layernorm", pend)
+            if _dumper.enabled():
+                _dumper.dump(f"layer{i:03d}_residual", r)
         y, _ = self._add_norm(pend, r, self.params["norm.weight"])
+        if _dumper.enabled():
+            _dumper.dump("final_hidden", y)
         return y
 
     @torch.no_grad()

@@ -49,6 +49,9 @@ def _groups(world: int, size: int):
 
 
 def init_distributed(args) -> ProcessContext:
+    if getattr(args, "http_proxy", None):  # proxy for the HTTP clients (reward models, routers)
+        os.environ.setdefault("http_proxy", args.http_proxy)
+        os.environ.setdefault("https_proxy", args.http_proxy)
     # --train-env-vars: JSON object of environment variables for the training process
     env = getattr(args, "train_env_vars", None)
     if env and env != "{}":
@@ -347,7 +350,16 @@ def build_critic(args, ctx: ProcessContext):
                        optimizer_placement="host" if args.optimizer_cpu_offload else "auto",
                        micro_batching="balanced" if args.use_dynamic_batch_size else "fixed",
                        micro_batch_size=args.micro_batch_size)
-    return Critic(body, acfg, value_clip=args.value_clip, dp_group=ctx.dp_group)
+    critic = Critic(body, acfg, value_clip=args.value_clip, dp_group=ctx.dp_group)
+    if args.critic_load:
+        from miles_b200.checkpoint.torch_dist import get_checkpoint_iteration
+
+        it = get_checkpoint_iteration(args.critic_load)
+        head = os.path.join(args.critic_load, f"iter_{it:07d}", "value_head.pt") if it is not None else ""
+        if head and os.path.exists(head):
+            with torch.no_grad():
+                critic.head.copy_(torch.load(head, weights_only=True).to(critic.head.device))
+    return critic
 
 
 def build_engine_model(args, model: Transformer, ctx: ProcessContext) -> Transformer:

@@ -375,3 +375,25 @@ def make_refit(model: Transformer, group, src: int, bucket_bytes: int, mode: str
     if transport == "peer":
         return PeerRefit(model, group, src, bucket_bytes, mode)
     return WeightRefit(model, group, src, bucket_bytes, mode)
+
+
+def verify_weights_equal(model, group, src: int, exact: bool = True) -> dict:
+    """--check-weight-update-equal: after a refit every member of `group` (the source trainer
+    and the engines) reduces its flat parameter buffer to a checksum (the bf16 bit patterns
+    summed as integers, so equal bits give equal sums); with `exact` (bf16 refit) every engine
+    must match the source, otherwise (fp8 refit: engines hold dequantised weights) the engines
+    must match each other. Raises AssertionError on a mismatch; every member must call it."""
+    flat = model.flat
+    csum = flat.view(torch.int16).to(torch.int64).sum().reshape(1)
+    world = dist.get_world_size(group)
+    got = [torch.zeros_like(csum) for _ in range(world)]
+    dist.all_gather(got, csum, group=group)
+    vals = [int(g.item()) for g in got]
+    ranks = dist.get_process_group_ranks(group) if hasattr(dist, "get_process_group_ranks") else list(range(world))
+    src_i = ranks.index(src) if src in ranks else 0
+    engines = [v for i, v in enumerate(vals) if i != src_i]
+    if exact and any(v != vals[src_i] for v in engines):
+        raise AssertionError(f"engine weights differ from the trainer's after refit: {vals}")
+    if not exact and len(set(engines)) > 1:
+        raise AssertionError(f"engine weights differ from each other after refit: {vals}")
+    return {"update_weights/checksum": vals[src_i]}

@@ -65,8 +65,11 @@ class Session:
     def head(self) -> Checkpoint | None:
         return self.checkpoints[-1] if self.checkpoints else None
 
-    def prepare(self, tok, request_messages: list[dict], tools=None) -> tuple[list[int], list[int], list[float]]:
-        """(input_ids, loss mask so far, log-probs so far) for the next completion."""
+    def prepare(self, tok, request_messages: list[dict], tools=None,
+                allowed_roles=None) -> tuple[list[int], list[int], list[float]]:
+        """(input_ids, loss mask so far, log-probs so far) for the next completion.
+        allowed_roles: roles that may be appended after the last assistant turn
+        (--tito-allowed-append-roles; None = any)."""
         # roll back one assistant step if the agent retries from the previous checkpoint
         if len(self.checkpoints) >= 2 and len(request_messages) < len(self.messages) and \
                 len(request_messages) >= self.checkpoints[-2].num_messages:
@@ -79,6 +82,10 @@ class Session:
         n = head.num_messages
         if request_messages[:n] != self.messages[:n]:
             raise SessionError("request rewrites earlier messages; sessions are linear")
+        if allowed_roles is not None:
+            bad = [m.get("role") for m in request_messages[n:] if m.get("role") not in allowed_roles]
+            if bad:
+                raise SessionError(f"appending role(s) {bad} is not allowed (allowed: {sorted(allowed_roles)})")
         old = _render(tok, self.messages[:n], False, tools)
         new = _render(tok, request_messages, True, tools)
         if new[:len(old)] != old:
@@ -107,7 +114,10 @@ class Session:
 
 
 class SessionRegistry:
-    def __init__(self, tokenizer, client, default_max_tokens: int = 1024):
+    def __init__(self, tokenizer, client, default_max_tokens: int = 1024, allowed_append_roles=None,
+                 model_name: str | None = None):
+        self.allowed_roles = set(allowed_append_roles) if allowed_append_roles else None
+        self.model_name = model_name
         self.tok = tokenizer
         self.client = client  # .generate(input_ids, sampling_params, return_logprob) -> dict
         self.sessions: dict[str, Session] = {}
@@ -135,7 +145,7 @@ class SessionRegistry:
         msgs = body.get("messages", [])
         tools = body.get("tools")
         async with sess.lock:
-            ids, mask, lps = sess.prepare(self.tok, msgs, tools)
+            ids, mask, lps = sess.prepare(self.tok, msgs, tools, self.allowed_roles)
             nmsg = len(sess.checkpoints)
         sp = {"temperature": body.get("temperature", 1.0),
               "max_new_tokens": body.get("max_tokens") or body.get("max_completion_tokens")
@@ -153,7 +163,7 @@ class SessionRegistry:
         finish = out["meta_info"].get("finish_reason", {}).get("type", "stop")
         resp = {
             "id": f"chatcmpl-{sid}-{nmsg}", "object": "chat.completion", "created": int(time.time()),
-            "model": body.get("model", "miles-b200"),
+            "model": body.get("model", self.model_name or "miles-b200"),
             "choices": [{"index": 0, "message": reply,
                          "finish_reason": "length" if finish == "length" else "stop",
                          "prompt_token_ids": ids,
@@ -206,3 +216,33 @@ def build_session_app(registry: SessionRegistry):
             raise HTTPException(400, str(e))
 
     return app
+
+
+def launch_session_server(args, tokenizer, client, background: bool = True):
+    """--use-session-server: the OpenAI-style session endpoint on --session-server-ip /
+    --session-server-port (a free port when unset), backed by this rank's engine client.
+    Returns (registry, url)."""
+    import socket
+    import threading
+
+    import uvicorn
+
+    host = getattr(args, "session_server_ip", None) or "127.0.0.1"
+    port = getattr(args, "session_server_port", None)
+    if not port:
+        with socket.socket() as sk:
+            sk.bind((host, 0))
+            port = sk.getsockname()[1]
+    reg = SessionRegistry(tokenizer, client,
+                          default_max_tokens=getattr(args, "rollout_max_response_len", None) or 1024,
+                          allowed_append_roles=getattr(args, "tito_allowed_append_roles", None),
+                          model_name=getattr(args, "tito_model", None))
+    server = uvicorn.Server(uvicorn.Config(build_session_app(reg), host=host, port=int(port),
+                                           log_level="warning"))
+    if background:
+        threading.Thread(target=server.run, daemon=True).start()
+    else:
+        server.run()
+    url = f"http://{host}:{port}"
+    args.session_server_url = url
+    return reg, url

@@ -256,6 +256,12 @@ class Actor:
     @torch.no_grad()
     def compute_logprobs(self, items: list[TrainItem]) -> list[np.ndarray]:
         """Forward-only response log-probs of every item (old / ref log-probs)."""
+        from miles_b200.utils import dumper
+
+        with dumper.phase("fwd_only"):
+            return self._compute_logprobs(items)
+
+    def _compute_logprobs(self, items: list[TrainItem]) -> list[np.ndarray]:
         out: list[np.ndarray | None] = [None] * len(items)
         if self.model.pp is not None:
             return self._logprobs_pp(items)
@@ -314,6 +320,13 @@ class Actor:
     # ------------------------------------------------------------------ train
     def train_step(self, items: list[TrainItem], global_num_samples: int | None = None,
                    global_num_tokens: int | None = None) -> dict:
+        from miles_b200.utils import dumper
+
+        with dumper.phase("fwd_bwd"):
+            return self._train_step(items, global_num_samples, global_num_tokens)
+
+    def _train_step(self, items: list[TrainItem], global_num_samples: int | None = None,
+                    global_num_tokens: int | None = None) -> dict:
         cfg = self.cfg
         self._ensure_grads()
         model = self.model

@@ -465,6 +465,14 @@ def parse_args(argv: list[str] | None = None, add_custom_arguments: Callable | N
 
 def validate_args(args) -> None:
     """Cross-flag rules of the reference (miles_validate_args, arguments.py:1805-2096)."""
+    reject_unsupported(args)
+    if getattr(args, "dump_details", None):
+        # --dump-details DIR: rollout and train data of every rollout under DIR
+        d = args.dump_details
+        if not args.save_debug_rollout_data:
+            args.save_debug_rollout_data = os.path.join(d, "rollout_data", "{rollout_id}.pkl")
+        if not getattr(args, "save_debug_train_data", None):
+            args.save_debug_train_data = os.path.join(d, "train_data", "{rollout_id}_{rank}.pkl")
     if args.hf_checkpoint is None and getattr(args, "hf_checkpoint_alias", None):
         args.hf_checkpoint = args.hf_checkpoint_alias
     if args.eps_clip_high is None:
@@ -565,6 +573,57 @@ def load_eval_config(path: str) -> list[dict]:
             raise ValueError("each eval dataset needs a `name` and a `path`")
         out.append({**defaults, **d})
     return out
+
+
+# ------------------------------------------------------------------------------------------------
+# Flags of the reference that need no action here, and flags whose non-default values are not
+# supported. Every other flag is read by the code it configures (tests/test_flag_registry_cpu.py
+# checks that each flag is in exactly one of the three groups).
+# ------------------------------------------------------------------------------------------------
+NO_EFFECT = {
+    "num_gpus_per_node": "torchrun starts one process per GPU; the node size comes from it",
+    "distributed_backend": "NCCL on GPUs and gloo on CPU are chosen per device",
+    "pin_rollout_manager_to_head": "no Ray placement: the rollout manager runs in every rank",
+    "miles_router_max_connections": "the router keeps one HTTP session with no connection cap",
+    "use_miles_router": "router/router.py is the only router",
+    "megatron_to_hf_mode": "one converter (checkpoint/hf.py) serves both modes",
+    "qkv_format": "training always packs sequences (thd); bshd is rejected below",
+    "seq_length": "packed variable-length batches have no fixed sequence length",
+    "padded_vocab_size": "the vocabulary is not padded",
+    "data_pad_size_multiplier": "packed (thd) micro-batches carry no padding",
+    "allgather_cp": "the DSA indexer inputs are always all-gathered over context parallelism",
+    "recompute_loss_function": "LM-head logits are never stored: the backward always recomputes them",
+    "p2p_transfer_num_workers": "peer-memory refit runs as device kernels, without a worker pool",
+    "p2p_transfer_timeout": "peer-memory refit waits are bounded inside the kernels",
+    "use_distributed_post": "requests go to the in-process engine, not over HTTP",
+    "lora_sync_from_tensor": "the colocated engine reads the adapters in place",
+    "low_memory_resume": "resume loads straight into the flat parameter buffers",
+    "loss_mask_type": "multi-turn loss masks come from the chat-template rendering (any family)",
+    "pause_generation_mode": "the engine server takes the mode per /pause_generation request",
+}
+
+UNSUPPORTED = {  # flag -> default; a different value is rejected at parse time
+    "rollout_external": False,
+    "rollout_external_engine_addrs": None,
+    "rollout_buffer_url": None,
+    "fetch_trajectory_retry_times": -1,
+    "rollout_task_type": None,
+    "min_batch_collection_ratio": 1.0,
+    "use_dynamic_global_batch_size": False,
+    "use_rollout_entropy": False,
+    "lora_type": "lora",
+    "dumper_source_patcher_config_train": None,
+    "dumper_source_patcher_config_inference": None,
+    "memory_recorder": "torch",
+}
+
+
+def reject_unsupported(args) -> None:
+    bad = [f"--{k.replace('_', '-')}" for k, d in UNSUPPORTED.items() if getattr(args, k, d) != d]
+    if getattr(args, "qkv_format", "thd") != "thd":
+        bad.append("--qkv-format bshd")
+    if bad:
+        raise ValueError(f"not supported by this framework: {', '.join(bad)}")
 
 
 def reset_arg(parser: argparse.ArgumentParser, name: str, **kwargs) -> None:

@@ -24,6 +24,11 @@ def configure(args=None, rank: int = 0):
     if args is not None:
         _STATE["enabled"] = bool(getattr(args, "dumper_enable", False)) or _STATE["enabled"]
         _STATE["dir"] = getattr(args, "dumper_dir", _STATE["dir"])
+        # which phases dump: inference (rollout engine), fwd_only (log-prob passes), fwd_bwd
+        # (training); none selected = all of them
+        sel = {p for p, flag in (("inference", "dumper_inference"), ("fwd_only", "dumper_fwd_only"),
+                                 ("fwd_bwd", "dumper_fwd_bwd")) if getattr(args, flag, False)}
+        _STATE["phases"] = sel or None
     _STATE["rank"] = rank
 
 
@@ -45,6 +50,9 @@ def phase(name: str, step: int | None = None):
 
 def dump(name: str, t: torch.Tensor):
     if not _STATE["enabled"]:
+        return
+    phases = _STATE.get("phases")
+    if phases is not None and _STATE["phase"] not in phases:
         return
     d = os.path.join(_STATE["dir"], _STATE["phase"], f"rank{_STATE['rank']}")
     os.makedirs(d, exist_ok=True)

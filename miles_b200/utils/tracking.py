@@ -37,7 +37,8 @@ class Tracker:
             try:
                 from torch.utils.tensorboard import SummaryWriter
 
-                d = args.tensorboard_dir or os.path.join(out or ".", "tb", args.tb_experiment_name or "run")
+                d = args.tensorboard_dir or os.path.join(out or ".", "tb", getattr(args, "tb_project_name", None) or "",
+                                                         args.tb_experiment_name or "run")
                 self.tb = SummaryWriter(d)
             except Exception as e:
                 logger.warning("tensorboard unavailable: %s", e)
@@ -45,9 +46,19 @@ class Tracker:
             try:
                 import wandb
 
-                self.wandb = wandb.init(project=args.wandb_project, group=args.wandb_group,
+                if getattr(args, "wandb_key", None) or getattr(args, "wandb_host", None):
+                    wandb.login(key=args.wandb_key, host=args.wandb_host)
+                name = args.wandb_group
+                if name and not getattr(args, "disable_wandb_random_suffix", False):
+                    import uuid
+
+                    name = f"{name}_{uuid.uuid4().hex[:6]}"
+                self.wandb = wandb.init(project=args.wandb_project, group=args.wandb_group, name=name,
                                         entity=args.wandb_team, dir=args.wandb_dir, mode=args.wandb_mode,
                                         id=args.wandb_run_id, resume="allow", config=vars(args))
+                if getattr(args, "wandb_always_use_train_step", False):
+                    # every metric on the train-step axis (the logged `step`)
+                    self.wandb.define_metric("*", step_metric="train/step")
             except Exception as e:
                 logger.warning("wandb unavailable: %s", e)
         if getattr(args, "use_prometheus", False):
@@ -81,7 +92,10 @@ class Tracker:
                     self.prom["gauges"][k] = g
                 g.labels(run=self.args.prometheus_run_name or "run").set(v)
         if self.wandb:
-            self.wandb.log(rec, step=step)
+            if getattr(self.args, "wandb_always_use_train_step", False):
+                self.wandb.log({**rec, "train/step": step})
+            else:
+                self.wandb.log(rec, step=step)
 
     def finish(self):
         if self.jsonl:

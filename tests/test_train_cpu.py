@@ -91,14 +91,14 @@ def _async_run(tmp_path, extra, port):
 @pytest.mark.timeout(600)
 def test_train_async_disaggregated(tmp_path):
     """1 trainer + 1 rollout rank: one-step-ahead pipeline with bf16 broadcast refits."""
-    _async_run(tmp_path, [], free_port())
+    _async_run(tmp_path, ["--check-weight-update-equal"], free_port())
 
 
 @pytest.mark.timeout(600)
 def test_train_async_fully_async_fp8_refit(tmp_path):
     """Continuous generation worker (partial rollout, staleness filter) and fp8 refits."""
     _async_run(tmp_path, ["--fully-async", "--partial-rollout", "--max-weight-staleness", "4",
-                          "--update-weight-quant", "fp8"], free_port())
+                          "--update-weight-quant", "fp8", "--check-weight-update-equal"], free_port())
 
 
 def test_train_ppo_with_critic(tmp_path, monkeypatch):

@@ -53,6 +53,11 @@ def setup(args):
     # prompts are sharded over data-parallel replicas: the ranks of one tensor-parallel group
     # generate (and train on) the same samples
     manager = RolloutManager(args, data_source, client, tok, ctx.dp_rank, ctx.dp_size)
+    if args.use_session_server:
+        # OpenAI-style session endpoint for agent rollouts (token-in / token-out trajectories)
+        from miles_b200.rollout.session import launch_session_server
+
+        manager.session_registry, _ = launch_session_server(args, tok, client)
     trainer = TrainActor(args, actor, ctx.dp_group, critic=build_critic(args, ctx),
                          data_parallel_size=ctx.dp_size)
     start = 0
@@ -97,7 +102,7 @@ def train(args):
         engine = manager.supervisor.before_rollout(rollout_id)  # recovers a dead engine
         data = manager.generate(rollout_id)
         manager.supervisor.after_rollout()
-        engine.release_memory()
+        engine.release_memory(args.offload_rollout_level)
         if reload_groups:
             REGISTRY.reload([ctx, model, actor, trainer, _pp._TIED_GROUPS])
         if args.debug_rollout_only:
@@ -123,6 +128,13 @@ def train(args):
             save_checkpoint(args.save, rollout_id, model, actor.opt, extra={"rollout_id": rollout_id, **schedule_state(actor)},
                             save_optim=not args.no_save_optim, async_save=args.async_save)
             data_source.save(rollout_id)
+            if args.critic_save and trainer.critic is not None:
+                # the PPO critic: body in torch_dist layout plus its value head
+                cr = trainer.critic
+                save_checkpoint(args.critic_save, rollout_id, cr.model, cr.body.opt,
+                                extra={"rollout_id": rollout_id}, save_optim=not args.no_save_optim)
+                torch.save(cr.head.detach().cpu(), os.path.join(
+                    args.critic_save, f"iter_{rollout_id:07d}", "value_head.pt"))
             from miles_b200.utils.ci_utils import save_model_hashes
 
             save_model_hashes(args, model, rollout_id, ctx.rank)

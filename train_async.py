@@ -143,6 +143,10 @@ def run_trainer(args, ctx, T, train_gloo, refit_group, data_gloo):
         if _refit_due(j, args, N, start):
             if ctx.rank == 0:
                 m.update(refit.sync())
+                if args.check_weight_update_equal:
+                    from miles_b200.parallel.refit import verify_weights_equal
+
+                    m.update(verify_weights_equal(model, refit_group, 0, args.update_weight_quant != "fp8"))
         m["rollout/weight_version"] = model.weight_version
         if should_run_periodic_action(j, args.save_interval, N) and args.save:
             from miles_b200.checkpoint.torch_dist import save_checkpoint
@@ -179,6 +183,10 @@ def run_engine(args, ctx, T, R, refit_group, data_gloo):
             if worker is not None:
                 worker.pause()
             refit.sync()
+            if args.check_weight_update_equal:
+                from miles_b200.parallel.refit import verify_weights_equal
+
+                verify_weights_equal(model, refit_group, 0, args.update_weight_quant != "fp8")
             if worker is not None:
                 worker.resume()
         if worker is None:
