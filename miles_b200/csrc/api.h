@@ -55,7 +55,7 @@ int mb_moe_route_dispatch(const float* logits, const float* bias, const int* idx
                           int topk_group, float scale, int align, int* idx_out, float* w_out,
                           int* counts, int* offsets, int* dest, void* xs, cudaStream_t st);
 int mb_moe_zero_pad(const int* counts, const int* offsets, void* buf, int E, int H, cudaStream_t st);
-int mb_moe_gather(const void* x, const int* dest, int n, int k, int H, void* xs, cudaStream_t st);
+int mb_moe_gather(const void* x, const int* dest, int n, int k, int H, void* xs, int rows, cudaStream_t st);
 int mb_moe_gather_bwd(const void* dxs, const int* dest, int T, int k, int H, void* dx,
                       cudaStream_t st);
 int mb_moe_combine(const void* ys, const int* dest, const float* w, const void* add, int T, int k,
@@ -268,6 +268,16 @@ int mb_vmm_map(unsigned long long ptr, size_t bytes, int device, unsigned long l
 int mb_vmm_unmap(unsigned long long ptr, size_t bytes, unsigned long long handle);
 int mb_host_register(void* ptr, size_t bytes);
 int mb_host_unregister(void* ptr);
+#ifdef __cplusplus
+}
+#endif
+
+// Checked-build guard words (MB_GUARD in common.cuh; always 0 in the regular build).
+#ifdef __cplusplus
+extern "C" {
+#endif
+int mb_checks_moe(int* out, int clear);
+int mb_checks_engine(int* out, int clear);
 #ifdef __cplusplus
 }
 #endif

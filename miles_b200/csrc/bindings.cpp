@@ -189,7 +189,8 @@ int64_t moe_zero_pad(torch::Tensor counts, torch::Tensor offsets, torch::Tensor 
                            cur_stream());
 }
 int64_t moe_gather(torch::Tensor x, torch::Tensor dest, int64_t k, torch::Tensor xs) {
-  return mb_moe_gather(P(x), PT<int>(dest), dest.numel(), k, x.size(1), P(xs), cur_stream());
+  return mb_moe_gather(P(x), PT<int>(dest), dest.numel(), k, x.size(1), P(xs), (int)xs.size(0),
+                       cur_stream());
 }
 int64_t moe_gather_bwd(torch::Tensor dxs, torch::Tensor dest, int64_t k, torch::Tensor dx) {
   return mb_moe_gather_bwd(P(dxs), PT<int>(dest), dx.size(0), k, dx.size(1), P(dx), cur_stream());
@@ -605,6 +606,14 @@ int64_t host_unregister(torch::Tensor t, int64_t offset) {
   return mb_host_unregister(static_cast<char*>(t.data_ptr()) + offset);
 }
 
+// Guard words of the checked build: {moe, engine_step} (zeros in the regular build).
+std::vector<int64_t> check_words(bool clear) {
+  int a = 0, b = 0;
+  mb_checks_moe(&a, clear);
+  mb_checks_engine(&b, clear);
+  return {a, b};
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_decode", &mla_decode, "absorbed MLA decode over the paged latent cache");
   m.def("gdn_decode", &gdn_decode, "Gated DeltaNet decode step (state updated in place)");
@@ -665,6 +674,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nonfinite", &nonfinite);
   m.def("adam", &adam);
   m.def("decode_prep", &decode_prep);
+  m.def("check_words", &check_words);
   m.def("vmm_granularity", &vmm_granularity);
   m.def("vmm_reserve", &vmm_reserve);
   m.def("vmm_free", &vmm_free);

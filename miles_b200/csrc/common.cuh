@@ -64,6 +64,36 @@ MB_DEVICE void report_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// Checked builds (-DMB_CHECKS=1, the miles_b200._C_checked extension): MB_GUARD(cond, code)
+// evaluates `cond`; when it is false the code is recorded in this translation unit's check word
+// (the first code sticks) and the caller skips the guarded access instead of faulting. In the
+// regular build MB_GUARD is the constant `true` and `cond` is not evaluated. MB_CHECK_GETTER
+// defines the C function that copies (and optionally clears) this unit's check word.
+#ifdef MB_CHECKS
+static __device__ int mb_check_word;
+MB_DEVICE bool mb_guard(bool ok, int code) {
+  if (!ok) atomicCAS(&mb_check_word, 0, code);
+  return ok;
+}
+#define MB_GUARD(cond, code) ::mb::mb_guard((cond), (code))
+#define MB_CHECK_GETTER(fn)                                                                      \
+  extern "C" int fn(int* out, int clear) {                                                       \
+    if (cudaMemcpyFromSymbol(out, ::mb::mb_check_word, sizeof(int)) != cudaSuccess) return -1;   \
+    const int zero = 0;                                                                          \
+    if (clear && cudaMemcpyToSymbol(::mb::mb_check_word, &zero, sizeof(int)) != cudaSuccess)     \
+      return -1;                                                                                 \
+    return 0;                                                                                    \
+  }
+#else
+#define MB_GUARD(cond, code) true
+#define MB_CHECK_GETTER(fn)                \
+  extern "C" int fn(int* out, int clear) { \
+    (void)clear;                           \
+    *out = 0;                              \
+    return 0;                              \
+  }
+#endif
+
 // Spin limit for mbarrier waits: with the suspend hint of mbar_try_wait, 1<<22 polls is about
 // 2 s of wall time, far beyond any legitimate stall.
 constexpr uint32_t kSpinLimit = 1u << 22;

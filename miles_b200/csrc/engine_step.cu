@@ -38,6 +38,7 @@ __global__ void decode_prep_kernel(const int* __restrict__ rows, int B, int spar
   const int j = blockIdx.x;
   if (j >= B) return;
   const int s = rows[j];
+  if (!MB_GUARD(s >= 0 && s <= spare, 51)) return;  // batch row mapped to no slot
   const bool live = s != spare && !s_done[s];
   int p = live ? s_pos[s] : 0;
   // a position past the page table would index outside the row: treat the row as padding
@@ -75,6 +76,7 @@ __global__ void decode_commit_kernel(const int* __restrict__ rows, int B, int sp
   const int j = blockIdx.x;
   if (j >= B) return;
   const int s = rows[j];
+  if (!MB_GUARD(s >= 0 && s <= spare, 52)) return;
   if (s == spare) return;
   __shared__ int live_sh, pos_sh;
   if (threadIdx.x == 0) {
@@ -133,3 +135,5 @@ extern "C" int mb_decode_commit(const int* rows, int B, int spare, const int* to
             s_pos, s_done, s_nout, s_maxnew, s_stop, nstop, out_tok, out_lp, max_new, out_exp,
             s_rec, max_len);
 }
+
+MB_CHECK_GETTER(mb_checks_engine)

@@ -254,7 +254,7 @@ __global__ void moe_hist_kernel(const int* __restrict__ idx, int n, int E, int* 
   for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
   __syncthreads();
   const int i = blockIdx.x * kChunk + threadIdx.x;
-  if (i < n) atomicAdd(&h[idx[i]], 1);
+  if (i < n && MB_GUARD(idx[i] >= 0 && idx[i] < E, 42)) atomicAdd(&h[idx[i]], 1);
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[blockIdx.x * E + e] = h[e];
 }
@@ -329,12 +329,13 @@ __global__ void moe_zero_pad_kernel(const int* __restrict__ counts, const int* _
 
 // x_sorted[dest[t*k+j]] = x[t]; one warp per entry.
 __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ dest,
-                                  int n, int k, int H, __nv_bfloat16* __restrict__ xs) {
+                                  int n, int k, int H, __nv_bfloat16* __restrict__ xs, int rows) {
   pdl_trigger();
   pdl_wait();
   const long long w = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (w >= n) return;
+  if (!MB_GUARD(dest[w] >= 0 && dest[w] < rows, 41)) return;  // destination row outside xs
   const int t = (int)(w / k);
   const uint4* src = reinterpret_cast<const uint4*>(x + (long long)t * H);
   uint4* dst = reinterpret_cast<uint4*>(xs + (long long)dest[w] * H);
@@ -595,11 +596,11 @@ extern "C" int mb_moe_zero_pad(const int* counts, const int* offsets, void* buf,
 }
 
 extern "C" int mb_moe_gather(const void* x, const int* dest, int n, int k, int H, void* xs,
-                             cudaStream_t st) {
+                             int rows, cudaStream_t st) {
   if (n == 0) return 0;
   if (H % 8) return -1;
   mb_launch(moe_gather_kernel, (n + 7) / 8, 256, 0, st, (const __nv_bfloat16*)x, dest, n, k, H,
-                                                 (__nv_bfloat16*)xs);
+                                                 (__nv_bfloat16*)xs, rows);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -670,3 +671,5 @@ extern "C" int mb_moe_route_dispatch(const float* logits, const float* bias, con
             align, idx_out, w_out, counts, offsets, dest, (__nv_bfloat16*)xs);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
+
+MB_CHECK_GETTER(mb_checks_moe)
