@@ -288,7 +288,7 @@ def preset(name: str) -> ModelConfig:
                            v_head_dim=32, qk_norm=False, routed_scaling_factor=2.5,
                            index_n_heads=4, index_head_dim=32, index_topk=16, max_position=4096)
     if n in ("dsv3-small", "deepseek-v3-small"):
-        # BASELINE config 5 shape: MLA + MoE, sigmoid grouped routing, shared experts
+        # DeepSeek-V3-style shape (27 layers): MLA + MoE, sigmoid grouped routing, shared experts
         return ModelConfig(arch="deepseek_v3", vocab_size=163840, hidden_size=2048, num_layers=27,
                            num_heads=16, num_kv_heads=16, head_dim=128, intermediate_size=11264,
                            num_experts=64, topk=6, moe_intermediate_size=1408, num_shared_experts=2,

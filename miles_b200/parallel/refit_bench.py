@@ -10,7 +10,7 @@ bf16; for fp8 against the 128x128 block quantisation of the source). Rank 0 prin
 line per transport.
 
 Reference: the refit path of update_weight_from_distributed.py (bucketed NCCL broadcast) that
-BASELINE's weight-sync metric times.
+the weight-sync metric times (seconds per refit and GB/s).
 """
 from __future__ import annotations
 

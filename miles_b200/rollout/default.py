@@ -137,7 +137,14 @@ async def generate_and_rm(args, sample: Sample, sampling_params: dict, evaluatio
         t0 = time.perf_counter()
         gen = load_function(args.custom_generate_function_path) if args.custom_generate_function_path else generate
         sample = await gen(args, sample, sampling_params)
-        sample.metadata.setdefault("gen_time", time.perf_counter() - t0)
+        for s in (sample if isinstance(sample, list) else [sample]):
+            s.metadata.setdefault("gen_time", time.perf_counter() - t0)
+    if isinstance(sample, list):  # a generate function that returns several samples
+        if not args.group_rm:
+            for s in sample:
+                if s.status != Sample.Status.ABORTED and s.reward is None:
+                    s.reward = await async_rm(args, s)
+        return sample
     if sample.status == Sample.Status.ABORTED or args.group_rm:
         return sample
     if sample.reward is None:
@@ -150,7 +157,8 @@ async def generate_and_rm_group(args, group: list[Sample], sampling_params: dict
     state = GenerateState.get(args)
     if state.aborted:
         return group
-    group = list(await asyncio.gather(*[generate_and_rm(args, s, sampling_params, evaluation) for s in group]))
+    out = await asyncio.gather(*[generate_and_rm(args, s, sampling_params, evaluation) for s in group])
+    group = [x for o in out for x in (o if isinstance(o, list) else [o])]
     if args.group_rm and not state.aborted and all(s.status != Sample.Status.ABORTED for s in group):
         await batched_async_rm(args, group, inplace_set_reward_field=True)
     return group

@@ -24,13 +24,16 @@ def _default(o):
 
 
 async def _session():
+    """One client session per event loop (a session is bound to the loop that created it; each
+    asyncio.run() starts a new loop)."""
     import aiohttp
 
     global _SESSION
-    if _SESSION is None or _SESSION.closed:
-        _SESSION = aiohttp.ClientSession(timeout=aiohttp.ClientTimeout(total=None),
-                                         json_serialize=lambda x: json.dumps(x, default=_default))
-    return _SESSION
+    loop = asyncio.get_running_loop()
+    if _SESSION is None or _SESSION[1].closed or _SESSION[0] is not loop:
+        _SESSION = (loop, aiohttp.ClientSession(timeout=aiohttp.ClientTimeout(total=None),
+                                                json_serialize=lambda x: json.dumps(x, default=_default)))
+    return _SESSION[1]
 
 
 async def post(url: str, payload: dict, max_retries: int = 10, retry_wait: float = 1.0):

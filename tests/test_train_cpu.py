@@ -1,4 +1,4 @@
-"""CPU end-to-end of train.py (BASELINE config 1 plumbing): tiny Qwen3-style model, GRPO,
+"""CPU end-to-end of train.py (the plumbing configuration): tiny Qwen3-style model, GRPO,
 single process and a 2-rank gloo world; checkpoint save/resume round trip."""
 import json
 import os
