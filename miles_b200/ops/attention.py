@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import math
 
+import numpy as np
 import torch
 
 from miles_b200.ops._lib import err_word, lib, use_native
@@ -20,35 +21,50 @@ PAGE = 64  # KV-cache page size (tokens); equals the attention key block
 CHUNK_PAGES = 16  # keys are merged in canonical 1024-key chunks (csrc/attention.cu)
 
 
+def to_device(a: np.ndarray, device) -> torch.Tensor:
+    """Host array -> device tensor through a pinned staging buffer with an asynchronous copy
+    (a pageable source would make the copy wait for the stream, stalling the host)."""
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if torch.device(device).type != "cuda":
+        return t.to(device)
+    staged = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    staged.copy_(t)
+    return staged.to(device, non_blocking=True)
+
+
+def _block_table_np(cu: np.ndarray, rows: int) -> tuple[np.ndarray, np.ndarray]:
+    lens = np.diff(cu)
+    n = (lens + rows - 1) // rows
+    seq = np.repeat(np.arange(len(lens), dtype=np.int32), n)
+    starts = np.repeat(np.cumsum(n) - n, n)
+    idx = (np.arange(int(n.sum())) - starts).astype(np.int32)
+    order = np.argsort(-idx, kind="stable")
+    return seq[order], idx[order]
+
+
 def block_table(cu_seqlens: list[int], device, rows: int = 64) -> tuple[torch.Tensor, torch.Tensor]:
     """(seq index, block index) of every `rows`-row block of every sequence, longest-work first
     (64-row blocks for the backward kernels, 128-row tiles for the forward)."""
-    seq, idx = [], []
-    for b in range(len(cu_seqlens) - 1):
-        n = (cu_seqlens[b + 1] - cu_seqlens[b] + rows - 1) // rows
-        seq.extend([b] * n)
-        idx.extend(range(n))
-    t_seq = torch.tensor(seq, dtype=torch.int32)
-    t_idx = torch.tensor(idx, dtype=torch.int32)
-    order = torch.argsort(-t_idx, stable=True)
-    return t_seq[order].to(device), t_idx[order].to(device)
+    seq, idx = _block_table_np(np.asarray(cu_seqlens, dtype=np.int64), rows)
+    return to_device(seq, device), to_device(idx, device)
 
 
 class VarlenMeta:
     """Host-built metadata of a packed batch (built once per micro-batch, reused by layers)."""
 
     def __init__(self, cu_seqlens: list[int], device):
-        self.cu_list = list(cu_seqlens)
-        self.cu = torch.tensor(cu_seqlens, dtype=torch.int32, device=device)
-        self.blk_seq, self.blk_idx = block_table(cu_seqlens, device)
-        self.tile_seq, self.tile_idx = block_table(cu_seqlens, device, FWD_TILE)
-        self.total = cu_seqlens[-1]
-        if len(cu_seqlens) > 1:
-            pos = torch.cat([torch.arange(cu_seqlens[b + 1] - cu_seqlens[b], dtype=torch.int32)
-                             for b in range(len(cu_seqlens) - 1)])
+        self.cu_list = [int(c) for c in cu_seqlens]
+        cu = np.asarray(self.cu_list, dtype=np.int64)
+        self.cu = to_device(cu.astype(np.int32), device)
+        self.blk_seq, self.blk_idx = block_table(self.cu_list, device)
+        self.tile_seq, self.tile_idx = block_table(self.cu_list, device, FWD_TILE)
+        self.total = self.cu_list[-1]
+        if len(cu) > 1:
+            lens = np.diff(cu)
+            pos = (np.arange(int(cu[-1]), dtype=np.int64) - np.repeat(cu[:-1], lens)).astype(np.int32)
         else:
-            pos = torch.zeros(0, dtype=torch.int32)
-        self.positions = pos.to(device)
+            pos = np.zeros(0, dtype=np.int32)
+        self.positions = to_device(pos, device)
 
 
 def attention_ref(q, k, v, cu_seqlens: list[int], scale: float | None = None):

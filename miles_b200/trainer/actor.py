@@ -29,7 +29,7 @@ import torch.distributed as dist
 from miles_b200.models.transformer import Transformer
 from miles_b200.ops.gemm import clear_main_grads, register_main_grad
 from miles_b200.parallel.tp import tp_partial_param_names, tp_replicated_ranges
-from miles_b200.ops.attention import VarlenMeta
+from miles_b200.ops.attention import VarlenMeta, to_device
 from miles_b200.ops.rl import METRIC_NAMES, PolicyLossCfg, policy_loss
 from miles_b200.trainer.lr_scheduler import LRSchedule
 from miles_b200.trainer.optimizer import FlatAdam
@@ -227,19 +227,18 @@ class Actor:
 
     # ------------------------------------------------------------------ batching
     def _mb_inputs(self, items: list[TrainItem]):
-        toks, cu, sel, tgt = [], [0], [], []
-        for it in items:
-            base = len(toks)
-            toks.extend(it.tokens)
-            cu.append(len(toks))
-            # hidden at position p predicts token p+1: response tokens P..L-1 <- rows P-1..L-2
-            sel.extend(range(base + it.prompt_len - 1, base + len(it.tokens) - 1))
-            tgt.extend(it.tokens[it.prompt_len:])
+        toks = [np.asarray(it.tokens, dtype=np.int32) for it in items]
+        lens = np.array([len(t) for t in toks], dtype=np.int64)
+        cu = np.concatenate([[0], np.cumsum(lens)])
+        # hidden at position p predicts token p+1: response tokens P..L-1 <- rows P-1..L-2
+        sel = np.concatenate([np.arange(cu[i] + it.prompt_len - 1, cu[i + 1] - 1, dtype=np.int64)
+                              for i, it in enumerate(items)]) if items else np.zeros(0, np.int64)
+        tgt = np.concatenate([t[it.prompt_len:] for t, it in zip(toks, items)]) if items else \
+            np.zeros(0, np.int32)
         dev = self.dev
-        meta = VarlenMeta(cu, dev)
-        return (torch.tensor(toks, dtype=torch.int32, device=dev), meta,
-                torch.tensor(sel, dtype=torch.long, device=dev),
-                torch.tensor(tgt, dtype=torch.int32, device=dev))
+        meta = VarlenMeta(cu.tolist(), dev)
+        return (to_device(np.concatenate(toks) if toks else np.zeros(0, np.int32), dev), meta,
+                to_device(sel, dev), to_device(tgt.astype(np.int32), dev))
 
     def _replay(self, items: list[TrainItem]):
         if not self.cfg.use_routing_replay or not items or items[0].routed_experts is None:
@@ -250,7 +249,7 @@ class Actor:
             # the last token never went through the model during rollout; repeat its predecessor
             ex = np.concatenate([ex, ex[-1:]], 0)[: len(it.tokens)]
             parts.append(ex)
-        return torch.from_numpy(np.concatenate(parts, 0)).to(self.dev, non_blocking=True)
+        return to_device(np.concatenate(parts, 0), self.dev)
 
     # ------------------------------------------------------------------ log-probs
     @torch.no_grad()
@@ -265,18 +264,24 @@ class Actor:
         out: list[np.ndarray | None] = [None] * len(items)
         if self.model.pp is not None:
             return self._logprobs_pp(items)
+        pending = []
         for mb in make_micro_batches([len(it.tokens) for it in items], self.cfg,
                                      self.cfg.log_probs_max_tokens_per_gpu):
             sub = [items[i] for i in mb]
             tok, meta, sel, tgt = self._mb_inputs(sub)
             lp, _ = self.model.selected_logprob(tok, meta, sel, tgt, self.cfg.temperature,
                                                 self.cfg.logprob_chunk, self._replay(sub))
-            lp = lp.cpu().numpy()
+            pending.append((mb, lp.float()))
+        # one device -> host copy at the end (a copy per micro-batch would stall the host on
+        # every one while the next micro-batch's inputs could already be queued)
+        if pending:
+            flat = torch.cat([lp for _, lp in pending]).cpu().numpy()
             o = 0
-            for i in mb:
-                n = items[i].resp_len
-                out[i] = lp[o:o + n]
-                o += n
+            for mb, _ in pending:
+                for i in mb:
+                    n = items[i].resp_len
+                    out[i] = flat[o:o + n]
+                    o += n
         return out
 
     @torch.no_grad()
@@ -406,8 +411,8 @@ class Actor:
                 wgt.append(mask / max(n_tokens, 1))
             else:
                 wgt.append(mask / max(mask.sum(), 1.0) / n_samples)
-        T = lambda xs: torch.from_numpy(np.concatenate(xs)).to(self.dev, non_blocking=True)
-        seg = torch.from_numpy(np.repeat(np.arange(len(sub)), [it.resp_len for it in sub])).to(self.dev)
+        T = lambda xs: to_device(np.concatenate(xs), self.dev)  # noqa: E731
+        seg = to_device(np.repeat(np.arange(len(sub)), [it.resp_len for it in sub]), self.dev)
         return {"tok": tok, "meta": meta, "sel": sel, "tgt": tgt, "n": len(sub), "seg": seg,
                 "old": T(old), "adv": T(adv), "wgt": T(wgt),
                 "roll": T(roll) if any(r is not None for r in roll) else None,

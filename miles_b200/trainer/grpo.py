@@ -20,6 +20,7 @@ import torch
 from miles_b200.engine.engine import GenRequest, RolloutEngine
 from miles_b200.ops.rl import grpo_advantages
 from miles_b200.trainer.actor import Actor, ActorConfig, TrainItem
+from miles_b200.utils.flops import train_tflops
 from miles_b200.utils.types import Sample
 
 
@@ -192,6 +193,8 @@ class ColocatedRL:
             "rollout/generated_tokens": self.generated_tokens,
             "rollout/buffered_groups": len(self.buffer),
             "perf/actor_train_tok_per_s": n_tok / max(t_train - t_lp, 1e-9),
+            "perf/actor_train_tflops": train_tflops(self.actor.model.cfg, [len(s.tokens) for s in samples],
+                                                    t_train - t_lp),
             "tokens_total": n_tok,
             "response_tokens": n_resp,
         })
