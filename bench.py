@@ -10,9 +10,9 @@ Rollout Routing Replay (routing recorded in rollout, replayed in training), Adam
 At N GPUs the global batch is N x 64 samples (N x 8 prompts), i.e. the headline workload's
 64 prompts x 8 samples at N = 8.
 
-Rollout (default): the reference's partial rollout with 2x over-sampling (--partial-rollout,
---over-sampling-batch-size): 16 groups per GPU are in flight, each step trains the first 8 that
-complete, and the others keep their partial responses for the next step. Every trained sample
+Rollout (default): the reference's partial rollout with over-sampling (--partial-rollout,
+--over-sampling-batch-size, here 4x): 32 groups per GPU are in flight, each step trains the first
+8 that complete, and the others keep their partial responses for the next step. Every trained sample
 is generated to its full sampled length; in steady state each step generates as many tokens as
 it trains. `--partial-rollout 0` generates every step's 8 groups to the end instead.
 
@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--partial-rollout", type=int, default=1,
                     help="1: reference --partial-rollout with over-sampling (unfinished groups "
                          "continue next step); 0: every step generates its groups to the end")
-    ap.add_argument("--over-sampling", type=int, default=2,
+    ap.add_argument("--over-sampling", type=int, default=4,
                     help="groups in flight per trained group under partial rollout")
     ap.add_argument("--steps-per-sync", type=int, default=8)
     return ap.parse_args()

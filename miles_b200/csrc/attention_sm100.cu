@@ -50,13 +50,17 @@ constexpr int CHUNK = 8;     // blocks per canonical chunk (1024 keys)
 constexpr int SUB = 128 * 64 * 2;   // one [128][64] bf16 SW128 sub-tile = 16 KB
 constexpr int TILE = 2 * SUB;       // [128][128] bf16 = 32 KB
 // shared memory map (offsets from a 1024-aligned base)
+constexpr int NST = 3;       // K/V pipeline stages (decode is bound by the K/V stream)
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = TILE;            // 2 stages
-constexpr int OFF_V = 3 * TILE;        // 2 stages
-constexpr int OFF_RED = 5 * TILE;          // softmax row max / sum exchange, 2 x [2][128] f32
+constexpr int OFF_K = TILE;                  // NST stages
+constexpr int OFF_V = OFF_K + NST * TILE;    // NST stages
+constexpr int OFF_RED = OFF_V + NST * TILE;  // softmax row max / sum exchange, 2 x [2][128] f32
 constexpr int OFF_BAR = OFF_RED + 2048;
 constexpr int NTHREADS = 320;              // producer, MMA, 8 softmax warps
-constexpr int SMEM_BYTES = OFF_BAR + 256 /*barriers*/ + 1024 /*align*/;
+// The dynamic shared memory of this kernel starts 1024-aligned (it has no static shared
+// memory); the kernel checks that and exits with error 2 otherwise, so no slack is requested.
+constexpr int SMEM_BYTES = OFF_BAR + 256 /*barriers*/;
+static_assert(SMEM_BYTES <= 232448, "fa_fwd_kernel shared memory exceeds the 227 KB limit");
 
 struct Params {
   // mode 0
@@ -204,16 +208,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;  // [2] one per S/P buffer
-  uint64_t* q_empty = bars + 13;
-  uint64_t* o_full = bars + 14;
-  uint64_t* o_empty = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* k_full = bars + 1;                // [NST]
+  uint64_t* k_empty = k_full + NST;           // [NST]
+  uint64_t* v_full = k_empty + NST;           // [NST]
+  uint64_t* v_empty = v_full + NST;           // [NST]
+  uint64_t* s_full = v_empty + NST;           // [2]
+  uint64_t* p_full = s_full + 2;              // [2] one per S/P buffer
+  uint64_t* q_empty = p_full + 2;
+  uint64_t* o_full = q_empty + 1;
+  uint64_t* o_empty = o_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 1);
+  if (smem != smem_raw) {  // not 1024-aligned: the shared-memory budget has no slack for it
+    if (threadIdx.x == 0) report_error(p.err, 2);
+    return;
+  }
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.nq / p.nkv;
@@ -221,11 +229,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(k_full + s, 1);
       mbar_init(k_empty + s, 1);
       mbar_init(v_full + s, 1);
       mbar_init(v_empty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(s_full + s, 1);
       mbar_init(p_full + s, 8);
     }
@@ -268,8 +278,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         }
         ++n;
         for (int j = 0; j < it.nblk; ++j, ++g) {
-          const int s = g & 1;
-          const uint32_t ph = ((g >> 1) & 1) ^ 1;
+          const int s = g % NST;  // K/V stage
+          const uint32_t ph = ((g / NST) & 1) ^ 1;
           const int jj = it.jbeg + j;
           int y0, y1;  // rows of the two 64-key halves of the block
           if (MODE == 0) {
@@ -309,10 +319,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     auto issue_pv = [&](int i) -> bool {
       if (!wait_bar(p_full + (i & 1), (i >> 1) & 1, p.err)) return false;
       if (!wait_bar(o_empty, (i & 1) ^ 1, p.err)) return false;
-      if (!wait_bar(v_full + (i & 1), (i >> 1) & 1, p.err)) return false;
+      if (!wait_bar(v_full + i % NST, (i / NST) & 1, p.err)) return false;
       tc_fence_after();
       if (elect_one()) {
-        const uint32_t sv = smem_u32(smem + OFF_V + (i & 1) * TILE);
+        const uint32_t sv = smem_u32(smem + OFF_V + (i % NST) * TILE);
         const uint32_t pa = tmem_base + (i & 1) * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
@@ -322,7 +332,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
                       kk > 0 ? 1u : 0u);
         }
         umma_commit(o_full);
-        umma_commit(v_empty + (i & 1));
+        umma_commit(v_empty + i % NST);
       }
       __syncwarp();
       return true;
@@ -335,13 +345,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
       if (!wait_bar(q_full, n & 1, p.err)) break;
       ++n;
       for (int j = 0; j < it.nblk; ++j, ++g) {
-        const int s = g & 1;
-        if (!wait_bar(k_full + s, (g >> 1) & 1, p.err)) { ok = false; break; }
+        const int s = g & 1;     // S / P buffer in tensor memory
+        const int ks = g % NST;  // K stage in shared memory
+        if (!wait_bar(k_full + ks, (g / NST) & 1, p.err)) { ok = false; break; }
         // S buffer s last held P_{g-2}: wait until PV_{g-2} has consumed it
         if (g >= 2 && !wait_bar(o_full, (g - 2) & 1, p.err)) { ok = false; break; }
         tc_fence_after();
         if (elect_one()) {
-          const uint32_t sk = smem_u32(smem + OFF_K + s * TILE);
+          const uint32_t sk = smem_u32(smem + OFF_K + ks * TILE);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t ad = make_sdesc_sw128(sq + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
@@ -349,7 +360,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
             umma_f16(tmem_base + s * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
           }
           umma_commit(s_full + s);
-          umma_commit(k_empty + s);
+          umma_commit(k_empty + ks);
           if (j == it.nblk - 1) umma_commit(q_empty);  // last S of the item: Q may be reloaded
         }
         __syncwarp();
