@@ -154,6 +154,7 @@ int64_t router_fwd(torch::Tensor logits, OT bias, OT idx_in, torch::Tensor idx_o
                 torch::Tensor w_out, int64_t k, int64_t score_fn, bool renorm, int64_t n_group,
                 int64_t topk_group, double scale) {
   CHECK_DT(logits, at::kFloat); TORCH_CHECK(logits.is_contiguous());
+  if (bias.has_value()) CHECK_DT(bias.value(), at::kFloat);
   return mb_router_fwd(PT<float>(logits), PT<float>(bias), PT<int>(idx_in), PT<int>(idx_out),
                          PT<float>(w_out), logits.size(0), logits.size(1), k, score_fn, renorm,
                          n_group, topk_group, (float)scale, cur_stream());
@@ -164,6 +165,7 @@ int64_t moe_route_dispatch(torch::Tensor logits, OT bias, OT idx_in, torch::Tens
                            int64_t score_fn, bool renorm, int64_t n_group, int64_t topk_group,
                            double scale, int64_t align) {
   CHECK_DT(logits, at::kFloat); TORCH_CHECK(logits.is_contiguous() && x.is_contiguous());
+  if (bias.has_value()) CHECK_DT(bias.value(), at::kFloat);
   return mb_moe_route_dispatch(PT<float>(logits), PT<float>(bias), PT<int>(idx_in), P(x),
                                logits.size(0), logits.size(1), k, x.size(1), score_fn, renorm,
                                n_group, topk_group, (float)scale, align, PT<int>(idx_out),

@@ -151,10 +151,19 @@ def experts_forward(xs, w1, w2, plan: MoEPlan, save_gu: bool = True):
     return gu, a, ys
 
 
+def router_bias(bias):
+    """The routing-score bias as the fp32 vector the router kernels read (parameters may be
+    stored in the model dtype)."""
+    if bias is None or bias.dtype == torch.float32:
+        return bias
+    return bias.float().contiguous()
+
+
 class _MoE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, router_w, w1, w2, bias, cfg: RouterCfg, replay_idx, record, need_bwd):
         T, H = x.shape
+        bias = router_bias(bias)
         x = x.contiguous()
         logits = G.matmul_nt(x, router_w, out_dtype=torch.float32)
         if not need_bwd and T * cfg.k <= FUSED_DISPATCH_MAX_ROWS:

@@ -32,7 +32,7 @@ import torch.distributed as dist
 
 from miles_b200.ops import gemm as G
 from miles_b200.ops._lib import lib
-from miles_b200.ops.moe import ALIGN, MoEPlan, RouterCfg, _accum_grouped_wgrad, emit_record
+from miles_b200.ops.moe import ALIGN, MoEPlan, RouterCfg, _accum_grouped_wgrad, emit_record, router_bias
 
 
 class EPContext:
@@ -124,7 +124,7 @@ class _MoEEPPeer(torch.autograd.Function):
         logits = G.matmul_nt(x, router_w, out_dtype=torch.float32)
         idx = torch.empty(T, k, dtype=torch.int32, device=dev)
         w = torch.empty(T, k, dtype=torch.float32, device=dev)
-        C.router_fwd(logits, bias, replay_idx, idx, w, k, cfg.score_fn, cfg.renorm,
+        C.router_fwd(logits, router_bias(bias), replay_idx, idx, w, k, cfg.score_fn, cfg.renorm,
                      cfg.n_group, cfg.topk_group, cfg.scale)
         emit_record(record, idx)
         if T > ep.cap_tokens:
@@ -219,7 +219,7 @@ class _MoEEP(torch.autograd.Function):
         logits = G.matmul_nt(x, router_w, out_dtype=torch.float32)
         idx = torch.empty(T, k, dtype=torch.int32, device=x.device)
         w = torch.empty(T, k, dtype=torch.float32, device=x.device)
-        lib().router_fwd(logits, bias, replay_idx, idx, w, k, cfg.score_fn, cfg.renorm,
+        lib().router_fwd(logits, router_bias(bias), replay_idx, idx, w, k, cfg.score_fn, cfg.renorm,
                          cfg.n_group, cfg.topk_group, cfg.scale)
         emit_record(record, idx)
         # send plan: groups = destination ranks, no padding

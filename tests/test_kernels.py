@@ -324,3 +324,24 @@ def test_fused_route_dispatch_matches_multi_kernel(score_fn, T):
     assert torch.equal(ref.dest, plan.dest)
     rows = ref.dest.long()
     assert torch.equal(xs[rows], xs_ref[rows])
+
+
+def test_moe_layer_bf16_router_bias_matches_reference():
+    """A routing bias stored in bf16 (a model parameter) is widened to fp32 before the router
+    kernels read it: the layer's routing equals the fp32 reference's."""
+    from miles_b200.ops.moe import RouterCfg, moe_experts, route_ref
+
+    torch.manual_seed(3)
+    T, H, E, k, F = 64, 256, 16, 4, 128
+    x = torch.randn(T, H, device=DEV, dtype=torch.bfloat16)
+    wr = (torch.randn(E, H, device=DEV) * 0.05).to(torch.bfloat16)
+    w1 = (torch.randn(E, 2 * F, H, device=DEV) * 0.05).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, F, device=DEV) * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(E, device=DEV) * 0.5).to(torch.bfloat16)
+    cfg = RouterCfg(E, k, score_fn="sigmoid", renorm=True, n_group=4, topk_group=2, scale=1.0)
+    got = []
+    with torch.no_grad():
+        moe_experts(x, wr, w1, w2, cfg, bias, None, got.append)
+    logits = x.float() @ wr.float().t()
+    ref, _ = route_ref(logits, cfg, bias)
+    assert torch.equal(got[0].sort(1).values, ref.int().sort(1).values)
