@@ -77,6 +77,7 @@ struct Params {
   float* ws_o;             // [B, nq, nsplit_max, 128]
   float* ws_ml;            // [B, nq, nsplit_max, 2]
   int nsplit_max;
+  int q_rows;              // query rows loaded per item (the G valid heads, rounded up to 8)
   // common
   __nv_bfloat16* o;
   int nq, nkv;
@@ -180,7 +181,7 @@ MB_DEVICE Item get_item(const Params& p, int t) {
     const int r = t - it.b * per_b;
     it.hk = r / p.nsplit_max;
     it.split = r - it.hk * p.nsplit_max;
-    const int ctx = p.ctx_lens[it.b];
+    const int ctx = __ldg(p.ctx_lens + it.b);
     it.nblk = 0;
     it.nsplit = 1;
     if (ctx > 0) {
@@ -267,7 +268,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         if (it.nblk == 0) continue;
         uint8_t* sq = smem + OFF_Q;
         if (!wait_bar(q_empty, (n & 1) ^ 1, p.err)) break;
-        mbar_arrive_expect_tx(q_full, TILE);
+        // decode loads only the G query heads of the item (rows past them stay stale; every row
+        // of S, P and O depends only on its own query row, and those rows are discarded)
+        mbar_arrive_expect_tx(q_full, MODE == 0 ? TILE : 2 * p.q_rows * 128);
         if (MODE == 0) {
           tma_load_2d(sq, &tmQ, q_full, it.h * D, it.seq_start + it.m0);
           tma_load_2d(sq + SUB, &tmQ, q_full, it.h * D + 64, it.seq_start + it.m0);
@@ -277,6 +280,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
           tma_load_2d(sq + SUB, &tmQ, q_full, 64, row);
         }
         ++n;
+        // decode: the item's page-table entries (at most 2 * CHUNK pages) are fetched up front
+        // as independent loads, instead of two dependent global loads before every block
+        int pgs[2 * CHUNK];
+        if (MODE == 1) {
+          const int* pt = p.page_table + (long long)it.b * p.max_pages;
+#pragma unroll
+          for (int c = 0; c < 2 * CHUNK; ++c) {
+            const int pg = 2 * it.jbeg + c;
+            pgs[c] = (c < 2 * it.nblk && pg < p.max_pages) ? __ldg(pt + pg) : 0;
+          }
+        }
         for (int j = 0; j < it.nblk; ++j, ++g) {
           const int s = g % NST;  // K/V stage
           const uint32_t ph = ((g / NST) & 1) ^ 1;
@@ -286,10 +300,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
             y0 = it.seq_start + jj * BN;
             y1 = y0 + 64;
           } else {
-            const int* pt = p.page_table + (long long)it.b * p.max_pages;
-            const int pg1 = 2 * jj + 1;
-            y0 = pt[2 * jj] * 64;
-            y1 = (pg1 < p.max_pages ? pt[pg1] : 0) * 64;
+            y0 = pgs[2 * j] * 64;
+            y1 = pgs[2 * j + 1] * 64;
           }
           // K block: K-major sub-tiles [128 keys][64 dims]; key half at +8KB
           if (!wait_bar(k_empty + s, ph, p.err)) { ok = false; break; }
@@ -1138,7 +1150,8 @@ extern "C" int mb_fa_decode(const void* q, const void* kc, const void* vc, void*
   if (nsplit_max > 1 && (!ws_o || !ws_ml)) return -3;
   if (int rc = current_ctx()) return rc;
   CUtensorMap tq, tk, tv;
-  int rc = make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)B * nq, D, D, 64, 128);
+  const int q_rows = ((nq / nkv + 7) / 8) * 8;
+  int rc = make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)B * nq, D, D, 64, q_rows);
   if (rc) return rc;
   rc = make_map(&tk, kc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, (uint64_t)nkv * D,
                 (uint64_t)nkv * D, 64, 64);
@@ -1153,6 +1166,7 @@ extern "C" int mb_fa_decode(const void* q, const void* kc, const void* vc, void*
   p.ws_o = ws_o;
   p.ws_ml = ws_ml;
   p.nsplit_max = nsplit_max;
+  p.q_rows = q_rows;
   p.o = (__nv_bfloat16*)o;
   p.nq = nq;
   p.nkv = nkv;
