@@ -180,7 +180,10 @@ def main():
     acfg = ActorConfig(lr=1e-6, max_tokens_per_gpu=args.max_tokens_per_gpu,
                        loss=PolicyLossCfg(eps_clip=0.2, eps_clip_high=0.2, use_tis=True,
                                           tis_clip=2.0),
-                       use_routing_replay=cfg.is_moe)
+                       use_routing_replay=cfg.is_moe,
+                       # old log-probs from the training forward (bitwise those of a separate
+                       # no-grad pass; one optimizer step per rollout)
+                       old_logp_from_forward=True)
     actor = Actor(model, acfg, dp_group=group)
     rl = ColocatedRL(engine, actor, RLConfig(n_samples_per_prompt=args.samples_per_prompt,
                                              routing_replay=cfg.is_moe, seed=rank,

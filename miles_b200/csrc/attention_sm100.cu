@@ -50,11 +50,12 @@ constexpr int CHUNK = 8;     // blocks per canonical chunk (1024 keys)
 constexpr int SUB = 128 * 64 * 2;   // one [128][64] bf16 SW128 sub-tile = 16 KB
 constexpr int TILE = 2 * SUB;       // [128][128] bf16 = 32 KB
 // shared memory map (offsets from a 1024-aligned base)
-constexpr int NST = 3;       // K/V pipeline stages (decode is bound by the K/V stream)
+constexpr int NST = 2;       // K/V pipeline stages
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = TILE;                  // NST stages
 constexpr int OFF_V = OFF_K + NST * TILE;    // NST stages
-constexpr int OFF_RED = OFF_V + NST * TILE;  // softmax row max / sum exchange, 2 x [2][128] f32
+constexpr int OFF_P = OFF_V + NST * TILE;    // fast decode (mode 2): two P tiles (SS P.V)
+constexpr int OFF_RED = OFF_P + 2 * TILE;    // softmax row max / sum exchange, 2 x [2][128] f32
 constexpr int OFF_BAR = OFF_RED + 2048;
 constexpr int NTHREADS = 320;              // producer, MMA, 8 softmax warps
 // The dynamic shared memory of this kernel starts 1024-aligned (it has no static shared
@@ -238,10 +239,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(s_full + s, 1);
-      mbar_init(p_full + s, 8);
+      mbar_init(p_full + s, MODE == 2 ? 1 : 8);
     }
     mbar_init(o_full, 1);
-    mbar_init(o_empty, 8);
+    mbar_init(o_empty, MODE == 2 ? 1 : 8);
     fence_barrier_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
@@ -270,10 +271,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         if (!wait_bar(q_empty, (n & 1) ^ 1, p.err)) break;
         // decode loads only the G query heads of the item (rows past them stay stale; every row
         // of S, P and O depends only on its own query row, and those rows are discarded)
-        mbar_arrive_expect_tx(q_full, MODE == 0 ? TILE : 2 * p.q_rows * 128);
+        mbar_arrive_expect_tx(q_full, MODE == 0 ? TILE : MODE == 2 ? 8 * 1024 : 2 * p.q_rows * 128);
         if (MODE == 0) {
           tma_load_2d(sq, &tmQ, q_full, it.h * D, it.seq_start + it.m0);
           tma_load_2d(sq + SUB, &tmQ, q_full, it.h * D + 64, it.seq_start + it.m0);
+        } else if (MODE == 2) {
+          // fast decode: the G (<= 8) heads four times, in tile rows 8c + h (c = 0..3): row
+          // 8c + h of S is head h's scores, read by lane 8c + h for keys 32c .. 32c + 31
+          const int row = it.b * p.nq + it.hk * G;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            tma_load_2d(sq + c * 1024, &tmQ, q_full, 0, row);
+            tma_load_2d(sq + SUB + c * 1024, &tmQ, q_full, 64, row);
+          }
         } else {
           const int row = it.b * p.nq + it.hk * G;
           tma_load_2d(sq, &tmQ, q_full, 0, row);
@@ -283,7 +293,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         // decode: the item's page-table entries (at most 2 * CHUNK pages) are fetched up front
         // as independent loads, instead of two dependent global loads before every block
         int pgs[2 * CHUNK];
-        if (MODE == 1) {
+        if (MODE != 0) {
           const int* pt = p.page_table + (long long)it.b * p.max_pages;
 #pragma unroll
           for (int c = 0; c < 2 * CHUNK; ++c) {
@@ -336,12 +346,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
       if (elect_one()) {
         const uint32_t sv = smem_u32(smem + OFF_V + (i % NST) * TILE);
         const uint32_t pa = tmem_base + (i & 1) * 128;
+        const uint32_t ps = smem_u32(smem + OFF_P + (i & 1) * TILE);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          // keys 16kk..16kk+15: packed P columns (kk>>2)*64 + (kk&3)*8 of the S buffer
           const uint64_t bd = make_sdesc_sw128(sv + (kk >> 2) * SUB + (kk & 3) * 2048, 8192, 1024);
-          umma_f16_ts(tmem_base + 256, pa + (kk >> 2) * 64 + (kk & 3) * 8, bd, idesc_o,
-                      kk > 0 ? 1u : 0u);
+          if (MODE == 2) {
+            // keys 16kk..16kk+15 of the P tile in shared memory (K-major SW128, like Q)
+            const uint64_t ad = make_sdesc_sw128(ps + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
+            umma_f16(tmem_base + 256, ad, bd, idesc_o, kk > 0 ? 1u : 0u);
+          } else {
+            // keys 16kk..16kk+15: packed P columns (kk>>2)*64 + (kk&3)*8 of the S buffer
+            umma_f16_ts(tmem_base + 256, pa + (kk >> 2) * 64 + (kk & 3) * 8, bd, idesc_o,
+                        kk > 0 ? 1u : 0u);
+          }
         }
         umma_commit(o_full);
         umma_commit(v_empty + i % NST);
@@ -360,8 +377,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         const int s = g & 1;     // S / P buffer in tensor memory
         const int ks = g % NST;  // K stage in shared memory
         if (!wait_bar(k_full + ks, (g / NST) & 1, p.err)) { ok = false; break; }
-        // S buffer s last held P_{g-2}: wait until PV_{g-2} has consumed it
-        if (g >= 2 && !wait_bar(o_full, (g - 2) & 1, p.err)) { ok = false; break; }
+        // S buffer s last held P_{g-2}: wait until PV_{g-2} has consumed it (fast decode keeps
+        // P in shared memory: the softmax finished reading S_{g-2} before PV_{g-2} was issued)
+        if (MODE != 2 && g >= 2 && !wait_bar(o_full, (g - 2) & 1, p.err)) { ok = false; break; }
         tc_fence_after();
         if (elect_one()) {
           const uint32_t sk = smem_u32(smem + OFF_K + ks * TILE);
@@ -380,6 +398,159 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
       }
     }
     if (ok && g > 0) issue_pv(g - 1);
+  } else if (MODE == 2) {
+    // ================= fast decode softmax / output (one warp) =================
+    // Warp 4 (TMEM lanes 0..31). Lane t = 8c + h handles head h (< G) and keys 32c .. 32c+31 of
+    // every block: S row t holds head h's scores (Q was loaded four times). Row maximum and
+    // sum combine the four lanes of a head with shuffles, in the same order as the two-thread
+    // rows of the other modes: rs = (cs0 + cs1) + (cs2 + cs3), so the results are bitwise
+    // those of the prefill kernel. P (bf16) goes to the shared-memory P tile of the block's
+    // buffer (rows h, K-major SW128) for an SS P.V; lanes 0..G-1 keep the running output in
+    // TMEM columns 384..511 (unused in this mode).
+    if (warp == 4) {
+      const int c4 = lane >> 3, h = lane & 7;
+      const bool live_row = h < G;
+      int g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < n_items; t += gridDim.x) {
+        const Item it = get_item<MODE>(p, t);
+        if (it.nblk == 0) continue;
+        const int qpos = it.qpos;
+        float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+        bool first_fold = true;
+        // Otot <- fma(Otot, alpha_prev, O_i) (Otot = 0 before the item's first fold)
+        auto fold_pv = [&](int i) -> bool {
+          if (!wait_warp(o_full, i & 1, p.err, 2)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t oj[32], ot[32];
+            tmem_ld_32x32b_x32(tmem_base + 256 + c * 32, oj);
+            if (!first_fold) tmem_ld_32x32b_x32(tmem_base + 384 + c * 32, ot);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              ot[e] = __float_as_uint(__fmaf_rn(first_fold ? 0.f : __uint_as_float(ot[e]),
+                                                alpha_prev, __uint_as_float(oj[e])));
+            tmem_st_32x32b_x32(tmem_base + 384 + c * 32, ot);
+          }
+          tmem_st_wait();
+          first_fold = false;
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(o_empty);
+          return true;
+        };
+        for (int j = 0; j < it.nblk; ++j, ++g) {
+          const int s = g & 1;
+          ok = ok && wait_warp(s_full + s, (g >> 1) & 1, p.err, 2);
+          if (!ok) break;
+          tc_fence_after();
+          const int kbase = (it.jbeg + j) * BN + c4 * 32;
+          const bool masked = j == it.nblk - 1;
+          // this lane's 32 scores: the warp reads columns 32c for c = 0..3 (one per lane group)
+          float sv[32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + s * 128 + c * 32, r);
+            tmem_ld_wait();
+            if (c == c4) {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) sv[e] = __uint_as_float(r[e]);
+            }
+          }
+          float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float v = masked && kbase + e > qpos ? -INFINITY : sv[e];
+            mx4[e & 3] = fmaxf(mx4[e & 3], v);
+          }
+          float raw = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+          raw = fmaxf(raw, __shfl_xor_sync(0xffffffff, raw, 8));
+          raw = fmaxf(raw, __shfl_xor_sync(0xffffffff, raw, 16));
+          const float mnew = fmaxf(m, raw == -INFINITY ? -INFINITY : __fmul_rn(raw, p.scale_log2));
+          const float sub = mnew == -INFINITY ? 0.f : mnew;
+          const float alpha = exp2f(__fsub_rn(m == -INFINITY ? sub : m, sub));
+          const float nsub = -sub;
+          float a4[4] = {0.f, 0.f, 0.f, 0.f};
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float p0 = ex2_approx(__fmaf_rn(sv[e], p.scale_log2, nsub));
+            float p1 = ex2_approx(__fmaf_rn(sv[e + 1], p.scale_log2, nsub));
+            if (masked) {
+              p0 = kbase + e > qpos ? 0.f : p0;
+              p1 = kbase + e + 1 > qpos ? 0.f : p1;
+            }
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+            a4[e & 3] = __fadd_rn(a4[e & 3], __low2float(h2));
+            a4[(e + 1) & 3] = __fadd_rn(a4[(e + 1) & 3], __high2float(h2));
+            pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          // P tile row h, keys 32c4 .. 32c4+31: sub-tile c4 >> 1, 16-byte chunks (c4 & 1) * 4 + q
+          // of the 128-byte row, SW128-swizzled (chunk ^ (row & 7))
+          uint8_t* prow = smem + OFF_P + s * TILE + (c4 >> 1) * SUB + h * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = ((c4 & 1) * 4 + q) ^ (h & 7);
+            *reinterpret_cast<uint4*>(prow + chunk * 16) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
+          fence_proxy_async_smem();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(p_full + s);
+          float cs = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
+          cs = __fadd_rn(cs, __shfl_xor_sync(0xffffffff, cs, 8));    // (g0 + g1) | (g2 + g3)
+          cs = __fadd_rn(cs, __shfl_xor_sync(0xffffffff, cs, 16));   // (g0 + g1) + (g2 + g3)
+          l = __fmaf_rn(l, alpha, cs);
+          m = mnew;
+          if (j >= 1) ok = ok && fold_pv(g - 1);
+          alpha_prev = alpha;
+        }
+        ok = ok && fold_pv(g - 1);
+        if (!ok) break;
+        // lanes 0..G-1 (one per head, all 128 dims) write the item's output
+        float o[32];
+        const long long w = (long long)it.b * p.nq + (long long)it.hk * G + h;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + 384 + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(r[e]);
+          if (c4 == 0 && live_row) {
+            if (it.nsplit == 1) {
+              const float inv = l > 0.f ? __frcp_rn(l) : 0.f;
+              __nv_bfloat16* out = p.o + w * D + c * 32;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint4 v;
+                v.x = pack_bf16x2(__fmul_rn(o[q * 8 + 0], inv), __fmul_rn(o[q * 8 + 1], inv));
+                v.y = pack_bf16x2(__fmul_rn(o[q * 8 + 2], inv), __fmul_rn(o[q * 8 + 3], inv));
+                v.z = pack_bf16x2(__fmul_rn(o[q * 8 + 4], inv), __fmul_rn(o[q * 8 + 5], inv));
+                v.w = pack_bf16x2(__fmul_rn(o[q * 8 + 6], inv), __fmul_rn(o[q * 8 + 7], inv));
+                reinterpret_cast<uint4*>(out)[q] = v;
+              }
+            } else {
+              const long long base = w * p.nsplit_max + it.split;
+              float4* wo = reinterpret_cast<float4*>(p.ws_o + base * D + c * 32);
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                wo[q] = make_float4(o[q * 4], o[q * 4 + 1], o[q * 4 + 2], o[q * 4 + 3]);
+              if (c == 0) {
+                p.ws_ml[base * 2] = m;
+                p.ws_ml[base * 2 + 1] = l;
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+      }
+    }
   } else {
     // ================= softmax / output =================
     // 8 warps: thread (quad, half) owns row quad*32+lane and columns [64*half, 64*half+64) of
@@ -1150,7 +1321,9 @@ extern "C" int mb_fa_decode(const void* q, const void* kc, const void* vc, void*
   if (nsplit_max > 1 && (!ws_o || !ws_ml)) return -3;
   if (int rc = current_ctx()) return rc;
   CUtensorMap tq, tk, tv;
-  const int q_rows = ((nq / nkv + 7) / 8) * 8;
+  // G <= 8 query heads per KV head: the one-warp softmax path (mode 2); larger groups: mode 1
+  const bool fast = nq / nkv <= 8;
+  const int q_rows = fast ? 8 : ((nq / nkv + 7) / 8) * 8;
   int rc = make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)B * nq, D, D, 64, q_rows);
   if (rc) return rc;
   rc = make_map(&tk, kc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, num_slots, (uint64_t)nkv * D,
@@ -1172,7 +1345,8 @@ extern "C" int mb_fa_decode(const void* q, const void* kc, const void* vc, void*
   p.nkv = nkv;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.err = err;
-  return launch_fa<1>(tq, tk, tv, p, B * nkv * nsplit_max, st);
+  return fast ? launch_fa<2>(tq, tk, tv, p, B * nkv * nsplit_max, st)
+              : launch_fa<1>(tq, tk, tv, p, B * nkv * nsplit_max, st);
 }
 
 // Backward of mb_fa_fwd: dq [T, nq, 128], dk / dv [T, nkv, 128] (row strides given; every row

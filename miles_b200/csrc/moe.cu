@@ -342,7 +342,10 @@ __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, const int
   for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
 }
 
-// dx[t] = sum_j dxs[dest[t*k+j]] (slot order), one warp per (token, 256-column chunk).
+// dx[t] = sum_j dxs[dest[t*k+j]] (slot order), one warp per (token, 256-column chunk). The k
+// row indices and then the k rows are loaded before the sum (independent loads in flight
+// instead of a dependent index -> row chain per slot); the sum order is unchanged.
+constexpr int kGatherMaxK = 8;
 __global__ void moe_gather_bwd_kernel(const __nv_bfloat16* __restrict__ dxs,
                                       const int* __restrict__ dest, int T, int k, int H,
                                       __nv_bfloat16* __restrict__ dx) {
@@ -355,11 +358,22 @@ __global__ void moe_gather_bwd_kernel(const __nv_bfloat16* __restrict__ dxs,
   const int t = (int)(gw / nch);
   const int c = (int)(gw % nch) * 256 + lane * 8;
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int j = 0; j < k; ++j) {
-    const uint4 v = *reinterpret_cast<const uint4*>(dxs + (long long)dest[t * k + j] * H + c);
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
+  for (int j0 = 0; j0 < k; j0 += kGatherMaxK) {
+    long long row[kGatherMaxK];
+    uint4 v[kGatherMaxK];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(b[q]);
+    for (int j = 0; j < kGatherMaxK; ++j)
+      if (j0 + j < k) row[j] = __ldg(dest + (long long)t * k + j0 + j);
+#pragma unroll
+    for (int j = 0; j < kGatherMaxK; ++j)
+      if (j0 + j < k) v[j] = *reinterpret_cast<const uint4*>(dxs + row[j] * H + c);
+#pragma unroll
+    for (int j = 0; j < kGatherMaxK; ++j) {
+      if (j0 + j >= k) break;
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v[j]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(b[q]);
+    }
   }
   uint4 o;
   __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
@@ -382,12 +396,27 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ ys, const i
   const int t = (int)(gw / nch);
   const int c = (int)(gw % nch) * 256 + lane * 8;
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int j = 0; j < k; ++j) {
-    const float wj = w[t * k + j];
-    const uint4 v = *reinterpret_cast<const uint4*>(ys + (long long)dest[t * k + j] * H + c);
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v);
+  // indices and weights, then rows, all in flight before the slot-ordered sum
+  for (int j0 = 0; j0 < k; j0 += kGatherMaxK) {
+    long long row[kGatherMaxK];
+    float wj[kGatherMaxK];
+    uint4 v[kGatherMaxK];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) acc[q] += wj * __bfloat162float(b[q]);
+    for (int j = 0; j < kGatherMaxK; ++j)
+      if (j0 + j < k) {
+        row[j] = __ldg(dest + (long long)t * k + j0 + j);
+        wj[j] = __ldg(w + (long long)t * k + j0 + j);
+      }
+#pragma unroll
+    for (int j = 0; j < kGatherMaxK; ++j)
+      if (j0 + j < k) v[j] = *reinterpret_cast<const uint4*>(ys + row[j] * H + c);
+#pragma unroll
+    for (int j = 0; j < kGatherMaxK; ++j) {
+      if (j0 + j >= k) break;
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&v[j]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += wj[j] * __bfloat162float(b[q]);
+    }
   }
   if (add) {
     const uint4 v = *reinterpret_cast<const uint4*>(add + (long long)t * H + c);

@@ -293,7 +293,8 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                       micro_batching="balanced" if args.use_dynamic_batch_size else "fixed",
                       micro_batch_size=args.micro_batch_size,
                       log_probs_max_tokens_per_gpu=args.log_probs_max_tokens_per_gpu,
-                      memory_margin_bytes=args.train_memory_margin_bytes)
+                      memory_margin_bytes=args.train_memory_margin_bytes,
+                      old_logp_from_forward=_old_logp_from_forward(args))
     if getattr(args, "train_backend", "b200") == "fsdp":
         # HF model under FSDP2 (trainer/fsdp_actor.py); `model` is then the engine's Transformer,
         # refreshed from the gathered HF state after every step
@@ -312,6 +313,18 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
     actor = Actor(model, cfg, dp_group=ctx.dp_group)
     actor.expert_dp_group = ctx.expert_dp_group
     return actor
+
+
+def _old_logp_from_forward(args) -> bool:
+    """Take the old log-probs from the training forward instead of a separate pass when nothing
+    needs them before the update: one optimizer step per rollout, an estimator that does not
+    use them (GRPO / GSPO), no KL-shaped rewards, no old-actor weights, no mismatch report. The
+    values are bitwise those of the separate pass (same weights, batch-invariant kernels)."""
+    return (getattr(args, "num_steps_per_rollout", None) in (None, 1)
+            and args.advantage_estimator in ("grpo", "gspo") and not args.kl_coef
+            and not getattr(args, "keep_old_actor", False)
+            and not getattr(args, "get_mismatch_metrics", False)
+            and getattr(args, "train_backend", "b200") != "fsdp")
 
 
 def build_engine(args, model: Transformer, ctx: ProcessContext) -> RolloutEngine:

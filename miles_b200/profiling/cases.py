@@ -7,7 +7,11 @@ cases: gemm_dense (8192x6144x2048 bf16 tcgen05 GEMM), gemm_grouped_decode (gate_
 (same, backward), attn_decode (64 sequences x 4096 keys, paged), symm_ar_norm (one-rank group:
 GEMM storing into the symmetric staging + reduce/residual/RMSNorm kernel, 4096 x 2048 output),
 ep_dispatch_combine (one-rank expert-parallel layer through the peer-memory dispatch / combine
-kernels: 4096 tokens, top-8 of 128 experts, forward and backward).
+kernels: 4096 tokens, top-8 of 128 experts, forward and backward), rl_step (Qwen3-30B-A3B widths
+with 2 layers: one training step of 8192 packed tokens -- norms, RoPE, router, MoE permute /
+combine, SwiGLU, log-prob, policy loss, Adam -- and 8 engine decode steps of 64 sequences --
+decode-state prep / commit, fused route + dispatch, sampler; the small-kernel profiles use it),
+rl_math (GRPO advantages and chunked GAE over 64k tokens).
 """
 import sys
 
@@ -54,6 +58,37 @@ elif case == "attn_decode":
     q = torch.randn(B, nq, 128, device='cuda', dtype=torch.bfloat16)
     lens = torch.full((B,), ctx, dtype=torch.int32, device='cuda')
     for _ in range(4): decode_attention(q, kc, vc, pt, lens)
+elif case == "rl_step":
+    import dataclasses
+
+    import numpy as np
+
+    from miles_b200.engine.engine import GenRequest, RolloutEngine
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops.rl import PolicyLossCfg
+    from miles_b200.trainer.actor import Actor, ActorConfig, TrainItem
+    cfg = dataclasses.replace(preset("qwen3-30b-a3b"), num_layers=2)
+    m = Transformer(cfg, device="cuda", seed=0)
+    rng = np.random.default_rng(0)
+    items = [TrainItem(rng.integers(0, cfg.vocab_size, 1024).tolist(), 256, advantage=1.0,
+                       rollout_logp=(-rng.random(768)).tolist()) for _ in range(8)]
+    a = Actor(m, ActorConfig(max_tokens_per_gpu=8192, optimizer_placement="device",
+                             loss=PolicyLossCfg(use_tis=True, tis_clip=2.0)))
+    for _ in range(2):
+        a.train_step(items)
+    eng = RolloutEngine(m, max_batch=64, num_pages=64 * 24, max_pages_per_seq=24, use_cuda_graph=False)
+    eng.generate([GenRequest(rng.integers(0, cfg.vocab_size, 1024).tolist(), 8, seed=i, rid=i,
+                             return_routed_experts=True) for i in range(64)])
+elif case == "rl_math":
+    from miles_b200.ops.rl import gae, grpo_advantages
+    r = torch.rand(4096, device="cuda")
+    n = 1 << 16
+    rew, val = torch.randn(n, device="cuda"), torch.randn(n, device="cuda")
+    cu = list(range(0, n + 1, 1024))
+    for _ in range(3):
+        grpo_advantages(r, 8)
+        gae(rew, val, cu, 1.0, 0.95)
 elif case in ("symm_ar_norm", "ep_dispatch_combine"):
     import torch.distributed as dist
     dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29731", rank=0, world_size=1)

@@ -65,6 +65,10 @@ class ActorConfig:
     mtp_loss_scale: float = 0.0      # weight of the multi-token prediction loss (model.mtp_train)
     temperature: float = 1.0
     use_rollout_logprobs: bool = False
+    # old log-probs from the training forward itself (one optimizer step per rollout): the
+    # separate no-grad pass would recompute the same values bit for bit (batch-invariant
+    # kernels, unchanged weights), so the training forward's detached log-probs are used
+    old_logp_from_forward: bool = False
     use_routing_replay: bool = False
     grad_dtype: torch.dtype = torch.bfloat16
     optimizer_placement: str = "auto"
@@ -342,6 +346,7 @@ class Actor:
         n_tokens = global_num_tokens or sum(
             (sum(it.loss_mask) if it.loss_mask is not None else it.resp_len) for it in items)
         metrics = torch.zeros(len(METRIC_NAMES) + 1, dtype=torch.float64, device=self.dev)
+        self._parity = torch.zeros(2, dtype=torch.float64, device=self.dev)  # sum |old - rollout|, count
         mbs = make_micro_batches([len(it.tokens) for it in items], cfg)
         mtp_total = torch.zeros((), dtype=torch.float32, device=self.dev)
         if model.pp is not None:
@@ -378,6 +383,9 @@ class Actor:
         self.opt.step()  # sharded: reduce-scatter + shard update + all-gather inside
         model.weight_version += 1
         out = {k: float(v) for k, v in zip(METRIC_NAMES + ["entropy"], metrics.tolist())}
+        if cfg.old_logp_from_forward:
+            s_, n_ = self._parity.tolist()
+            out["train_rollout_logprob_abs_diff"] = s_ / max(n_, 1.0)
         out["grad_norm"] = float(self.opt.grad_norm())
         out["lr"] = float(self.opt.lr)
         if model.mtp_train and cfg.mtp_loss_scale:
@@ -420,6 +428,12 @@ class Actor:
 
     def _mb_loss(self, prep: dict, lp, ent, metrics: torch.Tensor):
         cfg = self.cfg
+        if cfg.old_logp_from_forward:
+            prep = dict(prep, old=lp.detach().float())
+            if prep["roll"] is not None:
+                mask = (prep["wgt"] > 0).double()
+                self._parity[0] += ((prep["old"] - prep["roll"]).abs().double() * mask).sum()
+                self._parity[1] += mask.sum()
         self._cur_total_lens = [b - a for a, b in zip(prep["meta"].cu_list[:-1], prep["meta"].cu_list[1:])]
         loss, m = self._loss(lp, ent, prep["seg"], prep["n"], prep["old"], prep["adv"], prep["wgt"],
                              prep["roll"], prep["ref"])

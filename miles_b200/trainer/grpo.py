@@ -163,7 +163,7 @@ class ColocatedRL:
                  for s, a in zip(samples, adv)]
         # old log-probs (forward pass); bitwise equal to the rollout's under colocated weights
         diff = 0.0
-        if not self.actor.cfg.use_rollout_logprobs:
+        if not self.actor.cfg.use_rollout_logprobs and not self.actor.cfg.old_logp_from_forward:
             olds = self.actor.compute_logprobs(items)
             num = 0
             for it, o in zip(items, olds):
@@ -177,6 +177,8 @@ class ColocatedRL:
         world = torch.distributed.get_world_size(dp) if dp is not None else 1
         # loss weights are 1 / (global sample count); gradients are summed over DP ranks
         m = self.actor.train_step(items, global_num_samples=len(items) * world)
+        if self.actor.cfg.old_logp_from_forward:
+            diff = m.pop("train_rollout_logprob_abs_diff", 0.0)
         t_train = time.perf_counter()
         self.rollout_id += 1
         n_resp = sum(s.response_length for s in samples)

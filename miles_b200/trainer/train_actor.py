@@ -152,7 +152,7 @@ class TrainActor:
         if self._hook_before_lp is not None:
             self._hook_before_lp(a, self.model, "")
         old = None
-        if not a.use_rollout_logprobs:
+        if not a.use_rollout_logprobs and not self.actor.cfg.old_logp_from_forward:
             old_actor = getattr(a, "keep_old_actor", False) and "old_actor" in self.backuper.backups
             if old_actor:  # old log-probs under the weights that generated this rollout
                 self._switch("old_actor")
@@ -208,6 +208,8 @@ class TrainActor:
                 self._hook_before_step(a, rollout_id, s, self.model, self.actor.opt,
                                        getattr(self.actor.cfg, "lr_schedule", None))
             out = self.actor.train_step(sub, global_num_samples=len(sub) * self.data_world)
+            if "train_rollout_logprob_abs_diff" in out:  # old log-probs from the training forward
+                m["train/train_rollout_logprob_abs_diff"] = out.pop("train_rollout_logprob_abs_diff")
             if getattr(a, "ci_save_grad_norm", None) or getattr(a, "ci_load_grad_norm", None):
                 from miles_b200.utils.ci_utils import check_grad_norm
 

@@ -122,3 +122,21 @@ def test_engine_client_joins_running_batch_cpu():
     assert eng.stats["prefills"] >= 1
     ref = eng.generate([GenRequest(p1, 40, seed=1, rid=0), GenRequest(p2, 6, seed=2, rid=1)])
     assert r1["output_ids"] == ref[0].tokens and r2["output_ids"] == ref[1].tokens
+
+
+def test_old_logprobs_from_training_forward_cpu():
+    """With one optimizer step per rollout, old log-probs taken from the training forward give
+    the same update as a separate no-grad pass (same weights, same kernels)."""
+    results = []
+    for from_fwd in (False, True):
+        m = _model()
+        eng = RolloutEngine(m, max_batch=16, num_pages=256, use_cuda_graph=False)
+        actor = Actor(m, ActorConfig(lr=1e-3, max_tokens_per_gpu=512, grad_dtype=torch.float32,
+                                     old_logp_from_forward=from_fwd))
+        rl = ColocatedRL(eng, actor, RLConfig(n_samples_per_prompt=4, max_new_tokens=8))
+        rng = np.random.default_rng(1)
+        prompts = [rng.integers(0, 4096, 16).tolist() for _ in range(2)]
+        met = rl.step(prompts, rewards=[1.0, 0.0, 1.0, 0.0, 0.0, 1.0, 1.0, 0.0])
+        results.append((m.flat.clone(), met))
+    assert torch.allclose(results[0][0], results[1][0], atol=1e-6)
+    assert results[1][1]["train/train_rollout_logprob_abs_diff"] < 1e-4
