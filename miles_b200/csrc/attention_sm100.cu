@@ -1239,7 +1239,7 @@ using namespace mb;
 using namespace mb::fa;
 
 namespace {
-int fwd_attr_set[2] = {0, 0};
+int fwd_attr_set[3] = {0, 0, 0};  // one flag per MODE (0 prefill, 1 decode, 2 fast decode)
 int g_sms = 0;
 template <int MODE>
 int launch_fa(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
