@@ -225,7 +225,9 @@ class TrainActor:
         m["perf/actor_train_tok_per_s"] = n_tok / max(t2 - t1, 1e-9)
         from miles_b200.utils.flops import train_tflops
 
-        m["perf/actor_train_tflops"] = train_tflops(self.model.cfg, [len(t) for t in data["tokens"]], t2 - t1)
+        if getattr(self.model, "cfg", None) is not None:  # the FSDP backend trains an HF module
+            m["perf/actor_train_tflops"] = train_tflops(self.model.cfg, [len(t) for t in data["tokens"]],
+                                                        t2 - t1)
         if a.ci_test:
             self.ci_checks(rollout_id, m)
         self.metrics = m
