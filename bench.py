@@ -55,6 +55,10 @@ def parse():
     ap.add_argument("--over-sampling", type=int, default=4,
                     help="groups in flight per trained group under partial rollout")
     ap.add_argument("--steps-per-sync", type=int, default=8)
+    ap.add_argument("--fp8", type=int, default=1,
+                    help="1: unified block-scaled fp8 (e4m3, 1x128 activation / 128x128 weight "
+                         "scales) forward GEMMs in rollout and training (the headline config); "
+                         "0: bf16")
     return ap.parse_args()
 
 
@@ -173,6 +177,8 @@ def main():
 
     cfg = preset(args.model)
     model = Transformer(cfg, device=dev, seed=1234)
+    if args.fp8:
+        model.enable_fp8()
     inflight = args.prompts_per_gpu * (args.over_sampling if args.partial_rollout else 1)
     engine = RolloutEngine(model, max_batch=inflight * args.samples_per_prompt,
                            use_cuda_graph=not args.no_graph, steps_per_sync=args.steps_per_sync,
@@ -211,8 +217,9 @@ def main():
     def progress(tag, m):
         if rank == 0:
             keys = ("perf/rollout_time", "perf/log_probs_time", "perf/actor_train_time",
-                    "perf/step_time", "response_tokens", "train/train_rollout_logprob_abs_diff",
-                    "grad_norm")
+                    "perf/step_time", "response_tokens", "rollout/generated_tokens",
+                    "train/train_rollout_logprob_abs_diff",
+                    "train/train_rollout_logprob_abs_diff_current_weights", "grad_norm")
             print(tag, json.dumps({k: m.get(k) for k in keys}), file=sys.stderr, flush=True)
 
     for i in range(args.warmup):
@@ -226,6 +233,7 @@ def main():
     ev1 = torch.cuda.Event(enable_timing=True)
     tokens = resp = 0
     rollout_s = train_s = lp_s = 0.0
+    model.fp8_sync_events.clear()
     t_host0 = time.perf_counter()
     ev0.record()
     h2d = d2h = 0
@@ -256,6 +264,7 @@ def main():
         sm = vals[5:].clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         vals = torch.cat([mx, sm])
+    sync_s = sum(a.elapsed_time(b) for a, b in model.fp8_sync_events) / 1e3 / args.steps
     ms, host_ms, rollout_s, lp_s, train_s, tokens, resp = vals.tolist()
     step_s = ms / 1e3
     value = tokens / args.steps / step_s
@@ -268,7 +277,10 @@ def main():
             "unit": "tokens/s (GRPO step throughput: prompt+response tokens rolled out and trained per second, whole job)",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16",
+            "vs_baseline": None,
+            "dtype": ("fp8-block (e4m3 forward GEMMs: 1x128 activation / 128x128 weight scales, "
+                      "rollout and training; bf16 backward, attention, LM head, router; fp32 accum)"
+                      if args.fp8 else "bf16"),
             "data": "synthetic (uniform-random prompt tokens, Bernoulli(0.5) rewards, random-init weights)",
             "config": {"model": "Qwen3-30B-A3B" if args.model == "qwen3-30b-a3b" else args.model,
                        "global_batch": nsamp * world, "prompts": args.prompts_per_gpu * world,
@@ -285,13 +297,21 @@ def main():
             "grpo_step_s": step_s,
             "rollout_tok_s": resp / args.steps / (rollout_s / args.steps),
             "rollout_s": rollout_s / args.steps, "log_probs_s": lp_s / args.steps,
-            "train_s": train_s / args.steps, "weight_sync_s": 0.0,
-            "weight_sync_note": "colocated engine shares the trainer's parameter buffer: refit is a weight-version bump",
+            "train_s": train_s / args.steps, "weight_sync_s": sync_s,
+            "weight_sync_note": ("colocated engine shares the trainer's parameter buffer; with fp8 the "
+                                 "refit is the in-place 128x128 block re-quantisation of every GEMM "
+                                 "weight after the optimizer step (device-timed)" if args.fp8 else
+                                 "colocated engine shares the trainer's parameter buffer: refit is a "
+                                 "weight-version bump"),
             "clocks": clocks,
             "e2e": {"value": tokens / (host_ms / 1e3 * args.steps), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "train_rollout_logprob_abs_diff": rl.last_metrics.get("train/train_rollout_logprob_abs_diff"),
+            # over the tokens sampled under the weights being trained (partial rollout resumes
+            # samples whose earlier tokens came from older weights): 0.0 = bitwise parity
+            "train_rollout_logprob_abs_diff_current_weights":
+                rl.last_metrics.get("train/train_rollout_logprob_abs_diff_current_weights"),
         }
         print(json.dumps(out), flush=True)
     if world > 1:

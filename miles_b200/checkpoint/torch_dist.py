@@ -223,6 +223,7 @@ def load_checkpoint(load: str, model: Transformer, optimizer=None, load_optim: b
         raise FileNotFoundError(f"no torch_dist checkpoint under {load}")
     d = os.path.join(load, f"iter_{it:07d}")
     cfg = model.cfg
+    model._fp8_version = None  # new weights: the fp8 copies (if any) re-quantise on next use
     sd = {"model": {k: torch.empty_like(v) for k, v in model_state_dict(model).items()}}
     lora = getattr(model, "lora", None)
     if lora is not None:

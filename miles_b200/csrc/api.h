@@ -12,6 +12,14 @@ int mb_gemm_bf16(const void* a, long long a_rows, long long a_cols, long long ld
                  void* c, long long ldc, int M, int N, int K, int mode, const int* group_offsets,
                  int num_groups, int b_rows_per_group, long long c_group_stride, int epi,
                  float alpha, int bn, const int* group_counts, int* err, cudaStream_t stream);
+// Block-scaled fp8 GEMM and 1 x 128 activation quantisation (gemm_fp8_sm100.cu).
+int mb_fp8_act_quant(const void* x, long long ldx, int M, int K, void* q, float* s, long long lds,
+                     const int* offsets, const int* counts, int E, cudaStream_t st);
+int mb_gemm_fp8(const void* a, long long a_rows, long long lda, const float* sa, long long lds,
+                const void* b, long long b_rows, long long ldb, const float* sb, void* c,
+                long long ldc, int M, int N, int K, int mode, const int* group_offsets,
+                const int* group_counts, int num_groups, int b_rows_per_group, int epi,
+                int swiglu_f, void* c2, long long ldc2, int bn, int* err, cudaStream_t stream);
 int mb_gemm_bf16_swiglu(const void* a, long long a_rows, long long lda, const void* b,
                         long long b_rows, long long ldb, void* out, long long ldo, void* gu,
                         long long ldgu, int M, int F, int K, int mode, const int* group_offsets,

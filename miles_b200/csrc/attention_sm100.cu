@@ -219,7 +219,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
   uint64_t* q_empty = p_full + 2;
   uint64_t* o_full = q_empty + 1;
   uint64_t* o_empty = o_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 1);
+  uint64_t* red_bar = o_empty + 1;            // [2] fast decode: max / sum exchange of 4 warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 2);
   if (smem != smem_raw) {  // not 1024-aligned: the shared-memory budget has no slack for it
     if (threadIdx.x == 0) report_error(p.err, 2);
     return;
@@ -239,10 +240,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(s_full + s, 1);
-      mbar_init(p_full + s, MODE == 2 ? 1 : 8);
+      mbar_init(p_full + s, MODE == 2 ? 4 : 8);
     }
     mbar_init(o_full, 1);
-    mbar_init(o_empty, MODE == 2 ? 1 : 8);
+    mbar_init(o_empty, MODE == 2 ? 4 : 8);
+    mbar_init(red_bar, 4);
+    mbar_init(red_bar + 1, 4);
     fence_barrier_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
@@ -276,13 +279,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
           tma_load_2d(sq, &tmQ, q_full, it.h * D, it.seq_start + it.m0);
           tma_load_2d(sq + SUB, &tmQ, q_full, it.h * D + 64, it.seq_start + it.m0);
         } else if (MODE == 2) {
-          // fast decode: the G (<= 8) heads four times, in tile rows 8c + h (c = 0..3): row
-          // 8c + h of S is head h's scores, read by lane 8c + h for keys 32c .. 32c + 31
+          // fast decode: the G (<= 8) heads four times, in tile rows 32q + h (q = 0..3): row
+          // 32q + h of S is head h's scores, read by lane h of softmax warp 4 + q
           const int row = it.b * p.nq + it.hk * G;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            tma_load_2d(sq + c * 1024, &tmQ, q_full, 0, row);
-            tma_load_2d(sq + SUB + c * 1024, &tmQ, q_full, 64, row);
+            tma_load_2d(sq + c * 4096, &tmQ, q_full, 0, row);
+            tma_load_2d(sq + SUB + c * 4096, &tmQ, q_full, 64, row);
           }
         } else {
           const int row = it.b * p.nq + it.hk * G;
@@ -399,17 +402,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     }
     if (ok && g > 0) issue_pv(g - 1);
   } else if (MODE == 2) {
-    // ================= fast decode softmax / output (one warp) =================
-    // Warp 4 (TMEM lanes 0..31). Lane t = 8c + h handles head h (< G) and keys 32c .. 32c+31 of
-    // every block: S row t holds head h's scores (Q was loaded four times). Row maximum and
-    // sum combine the four lanes of a head with shuffles, in the same order as the two-thread
-    // rows of the other modes: rs = (cs0 + cs1) + (cs2 + cs3), so the results are bitwise
-    // those of the prefill kernel. P (bf16) goes to the shared-memory P tile of the block's
-    // buffer (rows h, K-major SW128) for an SS P.V; lanes 0..G-1 keep the running output in
-    // TMEM columns 384..511 (unused in this mode).
-    if (warp == 4) {
-      const int c4 = lane >> 3, h = lane & 7;
-      const bool live_row = h < G;
+    // ================= fast decode softmax / output (four warps) =================
+    // Warps 4..7, warp 4 + q reading TMEM lanes 32q..32q+31. Q was loaded four times, at tile
+    // rows 32q + h (h < G <= 8), so every warp finds head h's scores in its own lane h. Warp q
+    // handles keys 32q .. 32q+31 of every block and output columns 32q .. 32q+31. The row
+    // maximum and sum combine the four key groups through shared memory (bounded mbarrier
+    // exchange) in the same order as the two-thread rows of the other modes:
+    // rs = (g0 + g1) + (g2 + g3), so the results are bitwise those of the prefill kernel. Each
+    // warp writes its 32 P values (bf16) into all four row copies 32q' + h of the block's
+    // shared-memory P tile, so the SS P.V leaves head h's output in lane h of every lane
+    // quarter; warp q folds its 32 output columns into registers.
+    if (warp >= 4 && warp < 8) {
+      const int q = warp & 3;
+      const int h = lane & 7;
+      const bool live_row = lane < G;
+      const uint32_t lane_off = (uint32_t)(32 * q) << 16;
+      float* red_max = reinterpret_cast<float*>(smem + OFF_RED);  // [4 groups][8 heads]
+      float* red_sum = red_max + 32;                              // [4 groups][8 heads]
       int g = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < n_items; t += gridDim.x) {
@@ -418,23 +427,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         const int qpos = it.qpos;
         float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
         bool first_fold = true;
-        // Otot <- fma(Otot, alpha_prev, O_i) (Otot = 0 before the item's first fold)
+        float ot[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ot[e] = 0.f;
+        // Otot <- fma(Otot, alpha_prev, O_i) over this warp's 32 columns (Otot = 0 at first)
         auto fold_pv = [&](int i) -> bool {
           if (!wait_warp(o_full, i & 1, p.err, 2)) return false;
           tc_fence_after();
+          uint32_t oj[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_off + 256 + 32 * q, oj);
+          tmem_ld_wait();
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t oj[32], ot[32];
-            tmem_ld_32x32b_x32(tmem_base + 256 + c * 32, oj);
-            if (!first_fold) tmem_ld_32x32b_x32(tmem_base + 384 + c * 32, ot);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              ot[e] = __float_as_uint(__fmaf_rn(first_fold ? 0.f : __uint_as_float(ot[e]),
-                                                alpha_prev, __uint_as_float(oj[e])));
-            tmem_st_32x32b_x32(tmem_base + 384 + c * 32, ot);
-          }
-          tmem_st_wait();
+          for (int e = 0; e < 32; ++e)
+            ot[e] = __fmaf_rn(first_fold ? 0.f : ot[e], alpha_prev, __uint_as_float(oj[e]));
           first_fold = false;
           tc_fence_before();
           __syncwarp();
@@ -446,19 +451,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
           ok = ok && wait_warp(s_full + s, (g >> 1) & 1, p.err, 2);
           if (!ok) break;
           tc_fence_after();
-          const int kbase = (it.jbeg + j) * BN + c4 * 32;
+          const int kbase = (it.jbeg + j) * BN + q * 32;
           const bool masked = j == it.nblk - 1;
-          // this lane's 32 scores: the warp reads columns 32c for c = 0..3 (one per lane group)
           float sv[32];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          {
             uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem_base + s * 128 + c * 32, r);
+            tmem_ld_32x32b_x32(tmem_base + lane_off + s * 128 + q * 32, r);
             tmem_ld_wait();
-            if (c == c4) {
 #pragma unroll
-              for (int e = 0; e < 32; ++e) sv[e] = __uint_as_float(r[e]);
-            }
+            for (int e = 0; e < 32; ++e) sv[e] = __uint_as_float(r[e]);
           }
           float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
@@ -466,9 +467,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
             const float v = masked && kbase + e > qpos ? -INFINITY : sv[e];
             mx4[e & 3] = fmaxf(mx4[e & 3], v);
           }
-          float raw = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-          raw = fmaxf(raw, __shfl_xor_sync(0xffffffff, raw, 8));
-          raw = fmaxf(raw, __shfl_xor_sync(0xffffffff, raw, 16));
+          if (lane < 8) red_max[q * 8 + lane] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(red_bar);
+          ok = ok && wait_warp(red_bar, g & 1, p.err, 2);
+          if (!ok) break;
+          const float raw = fmaxf(fmaxf(red_max[h], red_max[8 + h]), fmaxf(red_max[16 + h], red_max[24 + h]));
           const float mnew = fmaxf(m, raw == -INFINITY ? -INFINITY : __fmul_rn(raw, p.scale_log2));
           const float sub = mnew == -INFINITY ? 0.f : mnew;
           const float alpha = exp2f(__fsub_rn(m == -INFINITY ? sub : m, sub));
@@ -488,22 +492,31 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
             a4[(e + 1) & 3] = __fadd_rn(a4[(e + 1) & 3], __high2float(h2));
             pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
           }
-          // P tile row h, keys 32c4 .. 32c4+31: sub-tile c4 >> 1, 16-byte chunks (c4 & 1) * 4 + q
-          // of the 128-byte row, SW128-swizzled (chunk ^ (row & 7))
-          uint8_t* prow = smem + OFF_P + s * TILE + (c4 >> 1) * SUB + h * 128;
+          // P rows 32q' + h (q' = 0..3), keys 32q .. 32q+31: sub-tile q >> 1, 16-byte chunks
+          // (q & 1) * 4 + c of the 128-byte row, SW128-swizzled (chunk ^ (row & 7) = chunk ^ h)
+          if (lane < 8) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = ((c4 & 1) * 4 + q) ^ (h & 7);
-            *reinterpret_cast<uint4*>(prow + chunk * 16) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+            for (int qq = 0; qq < 4; ++qq) {
+              uint8_t* prow = smem + OFF_P + s * TILE + (q >> 1) * SUB + (32 * qq + h) * 128;
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                const int chunk = ((q & 1) * 4 + c) ^ h;
+                *reinterpret_cast<uint4*>(prow + chunk * 16) =
+                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+              }
+            }
           }
           fence_proxy_async_smem();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(p_full + s);
-          float cs = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
-          cs = __fadd_rn(cs, __shfl_xor_sync(0xffffffff, cs, 8));    // (g0 + g1) | (g2 + g3)
-          cs = __fadd_rn(cs, __shfl_xor_sync(0xffffffff, cs, 16));   // (g0 + g1) + (g2 + g3)
+          if (lane < 8) red_sum[q * 8 + lane] = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(red_bar + 1);
+          ok = ok && wait_warp(red_bar + 1, g & 1, p.err, 2);
+          if (!ok) break;
+          const float cs = __fadd_rn(__fadd_rn(red_sum[h], red_sum[8 + h]),
+                                     __fadd_rn(red_sum[16 + h], red_sum[24 + h]));
           l = __fmaf_rn(l, alpha, cs);
           m = mnew;
           if (j >= 1) ok = ok && fold_pv(g - 1);
@@ -511,39 +524,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         }
         ok = ok && fold_pv(g - 1);
         if (!ok) break;
-        // lanes 0..G-1 (one per head, all 128 dims) write the item's output
-        float o[32];
-        const long long w = (long long)it.b * p.nq + (long long)it.hk * G + h;
+        // lanes 0..G-1 (one per head) write this warp's 32 output columns
+        if (live_row) {
+          const long long w = (long long)it.b * p.nq + (long long)it.hk * G + h;
+          if (it.nsplit == 1) {
+            const float inv = l > 0.f ? __frcp_rn(l) : 0.f;
+            __nv_bfloat16* out = p.o + w * D + q * 32;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + 384 + c * 32, r);
-          tmem_ld_wait();
+            for (int c = 0; c < 4; ++c) {
+              uint4 v;
+              v.x = pack_bf16x2(__fmul_rn(ot[c * 8 + 0], inv), __fmul_rn(ot[c * 8 + 1], inv));
+              v.y = pack_bf16x2(__fmul_rn(ot[c * 8 + 2], inv), __fmul_rn(ot[c * 8 + 3], inv));
+              v.z = pack_bf16x2(__fmul_rn(ot[c * 8 + 4], inv), __fmul_rn(ot[c * 8 + 5], inv));
+              v.w = pack_bf16x2(__fmul_rn(ot[c * 8 + 6], inv), __fmul_rn(ot[c * 8 + 7], inv));
+              reinterpret_cast<uint4*>(out)[c] = v;
+            }
+          } else {
+            const long long base = w * p.nsplit_max + it.split;
+            float4* wo = reinterpret_cast<float4*>(p.ws_o + base * D + q * 32);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(r[e]);
-          if (c4 == 0 && live_row) {
-            if (it.nsplit == 1) {
-              const float inv = l > 0.f ? __frcp_rn(l) : 0.f;
-              __nv_bfloat16* out = p.o + w * D + c * 32;
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 v;
-                v.x = pack_bf16x2(__fmul_rn(o[q * 8 + 0], inv), __fmul_rn(o[q * 8 + 1], inv));
-                v.y = pack_bf16x2(__fmul_rn(o[q * 8 + 2], inv), __fmul_rn(o[q * 8 + 3], inv));
-                v.z = pack_bf16x2(__fmul_rn(o[q * 8 + 4], inv), __fmul_rn(o[q * 8 + 5], inv));
-                v.w = pack_bf16x2(__fmul_rn(o[q * 8 + 6], inv), __fmul_rn(o[q * 8 + 7], inv));
-                reinterpret_cast<uint4*>(out)[q] = v;
-              }
-            } else {
-              const long long base = w * p.nsplit_max + it.split;
-              float4* wo = reinterpret_cast<float4*>(p.ws_o + base * D + c * 32);
-#pragma unroll
-              for (int q = 0; q < 8; ++q)
-                wo[q] = make_float4(o[q * 4], o[q * 4 + 1], o[q * 4 + 2], o[q * 4 + 3]);
-              if (c == 0) {
-                p.ws_ml[base * 2] = m;
-                p.ws_ml[base * 2 + 1] = l;
-              }
+            for (int c = 0; c < 8; ++c)
+              wo[c] = make_float4(ot[c * 4], ot[c * 4 + 1], ot[c * 4 + 2], ot[c * 4 + 3]);
+            if (q == 0) {
+              p.ws_ml[base * 2] = m;
+              p.ws_ml[base * 2 + 1] = l;
             }
           }
         }

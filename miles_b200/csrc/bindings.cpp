@@ -50,6 +50,87 @@ int64_t gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
   return rc;
 }
 
+// Block-scaled fp8: x bf16 [M, K] -> q (uint8 view of e4m3) [M, K], s fp32 [K/128, lds].
+int64_t fp8_act_quant(torch::Tensor x, torch::Tensor q, torch::Tensor s,
+                      c10::optional<torch::Tensor> offsets, c10::optional<torch::Tensor> counts) {
+  CHECK_CUDA(x); CHECK_CUDA(q); CHECK_CUDA(s);
+  CHECK_DT(x, at::kBFloat16); CHECK_DT(q, at::kByte); CHECK_DT(s, at::kFloat);
+  TORCH_CHECK(x.dim() == 2 && q.dim() == 2 && s.dim() == 2, "fp8_act_quant operands must be 2-D");
+  CHECK_ROWMAJOR(x); CHECK_ROWMAJOR(s);
+  TORCH_CHECK(q.is_contiguous(), "q must be contiguous");
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(q.size(0) == M && q.size(1) == K, "q shape");
+  TORCH_CHECK(K % 128 == 0 && s.size(0) == K / 128 && s.size(1) >= M, "s shape");
+  TORCH_CHECK(x.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 8 == 0, "x misaligned");
+  const int* op = nullptr;
+  const int* cp = nullptr;
+  int E = 0;
+  if (offsets.has_value()) {
+    CHECK_DT(offsets.value(), at::kInt);
+    op = offsets.value().data_ptr<int>();
+    E = (int)offsets.value().numel() - 1;
+    if (counts.has_value()) {
+      CHECK_DT(counts.value(), at::kInt);
+      TORCH_CHECK(counts.value().numel() == E, "counts must have E entries");
+      cp = counts.value().data_ptr<int>();
+    }
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  return mb_fp8_act_quant(x.data_ptr(), x.stride(0), (int)M, (int)K, q.data_ptr(), s.data_ptr<float>(),
+                          s.stride(0), op, cp, E, cur_stream());
+}
+
+// Block-scaled fp8 GEMM: a [a_rows, K] e4m3 (uint8) with sa [K/128, >= a_rows]; b [b_rows, K]
+// with sb [b_rows/128, K/128]; c bf16. epi 0: c [M, N]; epi 4: SwiGLU, N = 2F, c [M, F],
+// optional gu [M, 2F].
+int64_t gemm_fp8(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb,
+                 torch::Tensor c, c10::optional<torch::Tensor> gu, int64_t M, int64_t N, int64_t K,
+                 int64_t mode, c10::optional<torch::Tensor> group_offsets,
+                 c10::optional<torch::Tensor> group_counts, int64_t num_groups,
+                 int64_t b_rows_per_group, int64_t epi, int64_t swiglu_f, int64_t bn,
+                 torch::Tensor err) {
+  CHECK_CUDA(a); CHECK_CUDA(b); CHECK_CUDA(c); CHECK_CUDA(sa); CHECK_CUDA(sb);
+  CHECK_DT(a, at::kByte); CHECK_DT(b, at::kByte); CHECK_DT(c, at::kBFloat16);
+  CHECK_DT(sa, at::kFloat); CHECK_DT(sb, at::kFloat);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm_fp8 operands must be 2-D");
+  CHECK_ROWMAJOR(a); CHECK_ROWMAJOR(b); CHECK_ROWMAJOR(c);
+  TORCH_CHECK(sa.is_contiguous() && sb.is_contiguous(), "scales must be contiguous");
+  TORCH_CHECK(a.size(1) == K && b.size(1) == K && K % 128 == 0, "K mismatch / K % 128");
+  TORCH_CHECK(sa.dim() == 2 && sa.size(0) == K / 128 && sa.size(1) >= std::min<int64_t>(M, a.size(0)),
+              "sa shape");
+  TORCH_CHECK(sb.numel() == (b.size(0) / 128) * (K / 128) && b.size(0) % 128 == 0, "sb shape");
+  TORCH_CHECK(a.stride(0) % 16 == 0 && b.stride(0) % 16 == 0, "row strides must be 16-byte multiples");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0, "operands must be 16-byte aligned");
+  TORCH_CHECK(c.stride(0) % 8 == 0, "ldc must be a multiple of 8");
+  TORCH_CHECK(mode == 0 ? (M <= a.size(0) && N <= b.size(0)) : (M <= a.size(0)), "M / N out of range");
+  const int* go = nullptr;
+  const int* gc = nullptr;
+  if (mode != 0) {
+    TORCH_CHECK(group_offsets.has_value(), "grouped mode needs group_offsets");
+    CHECK_DT(group_offsets.value(), at::kInt);
+    go = group_offsets.value().data_ptr<int>();
+    TORCH_CHECK(b.size(0) == num_groups * b_rows_per_group, "b rows != groups * rows per group");
+    if (group_counts.has_value()) {
+      CHECK_DT(group_counts.value(), at::kInt);
+      gc = group_counts.value().data_ptr<int>();
+    }
+  }
+  void* gup = nullptr;
+  int64_t ldgu = 0;
+  if (gu.has_value()) {
+    CHECK_CUDA(gu.value()); CHECK_DT(gu.value(), at::kBFloat16); CHECK_ROWMAJOR(gu.value());
+    gup = gu.value().data_ptr();
+    ldgu = gu.value().stride(0);
+  }
+  c10::cuda::CUDAGuard g(a.device());
+  return mb_gemm_fp8(a.data_ptr(), a.size(0), a.stride(0), sa.data_ptr<float>(), sa.size(1),
+                     b.data_ptr(), b.size(0), b.stride(0), sb.data_ptr<float>(), c.data_ptr(),
+                     c.stride(0), (int)M, (int)N, (int)K, (int)mode, go, gc, (int)num_groups,
+                     (int)b_rows_per_group, (int)epi, (int)swiglu_f, gup, ldgu, (int)bn,
+                     err.data_ptr<int>(), cur_stream());
+}
+
 // out[M, F] = silu(a @ b_gate^T) * (a @ b_up^T), b: [groups * 2F, K] ([gate; up] per group);
 // gu (optional) receives the [M, 2F] product.
 int64_t gemm_swiglu(torch::Tensor a, torch::Tensor b, torch::Tensor out,
@@ -646,6 +727,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvfp4_quant", &nvfp4_quant);
   m.def("mxfp8_quant", &mxfp8_quant);
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM (dense / grouped)");
+  m.def("fp8_act_quant", &fp8_act_quant, "1 x 128 fp8 activation quantisation (K-block-major scales)");
+  m.def("gemm_fp8", &gemm_fp8, "tcgen05 block-scaled fp8 GEMM (dense / grouped, SwiGLU epilogue)");
   m.def("gemm_swiglu", &gemm_swiglu, "tcgen05 bf16 GEMM with fused SwiGLU epilogue");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);

@@ -269,6 +269,14 @@ MB_DEVICE void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
+// 32 lanes x 8 consecutive 32-bit columns.
+MB_DEVICE void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
 // ---------------------------------------------------------------------------------------------
 // UMMA descriptors
 // ---------------------------------------------------------------------------------------------

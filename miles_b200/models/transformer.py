@@ -17,6 +17,8 @@ Reference: the GPT/MoE layer specs the reference builds through Megatron + TE
 """
 from __future__ import annotations
 
+import collections
+
 import math
 from dataclasses import dataclass
 
@@ -332,6 +334,9 @@ class Transformer(torch.nn.Module):
         self.moe_index = {i: j for j, i in enumerate(i for i in range(cfg.num_layers) if cfg.layer_is_moe(i))}
         self.recompute = True
         self.weight_version = 0
+        self.fp8: dict = {}  # name -> Fp8Weight (block-scaled fp8 copies, see enable_fp8)
+        self._fp8_version = None
+        self.fp8_sync_events = collections.deque(maxlen=256)
         self.lora = None  # miles_b200.models.lora.LoRA when adapters are attached
         self.gdn = None
         if cfg.linear_attn_interval:
@@ -360,6 +365,60 @@ class Transformer(torch.nn.Module):
         if self.lora is not None and name in self.lora:
             return swiglu(self._lin(x, name))
         return G.linear_swiglu(x, self.params[name])
+
+    # -------------------------------------------------------------------------------- fp8
+    FP8_SUFFIXES = ("qkv_proj.weight", "o_proj.weight", "gate_up_proj.weight", "down_proj.weight",
+                    "q_proj.weight", "k_proj.weight", "v_proj.weight", "experts.w1", "experts.w2")
+
+    def enable_fp8(self) -> None:
+        """Unified block-scaled fp8 (the reference's `--fp8-format e4m3 --fp8-recipe
+        blockwise` training with fp8 rollout): every linear / grouped-expert weight gets an e4m3
+        copy with 128 x 128 block scales, and the forward GEMMs of training, prefill and decode
+        run on it (activations quantised 1 x 128 on the fly). Training and rollout use the same
+        copy and the same kernels, so their log-probs stay bitwise equal. The bf16 parameters
+        stay the master copy: the backward uses them and the optimizer updates them; the fp8
+        copy is re-quantised in place (same addresses, so decode graphs stay valid) whenever the
+        weight version changes. Embeddings, the LM head, the router and norms stay bf16, as in
+        the reference."""
+        from miles_b200.ops.fp8 import Fp8Weight, register_fp8
+
+        if self.tp is not None or self.lora is not None:
+            raise ValueError("block-scaled fp8 GEMMs run without tensor parallelism and LoRA")
+        for name, p in self.params.items():
+            if not name.endswith(self.FP8_SUFFIXES) or p.dim() < 2:
+                continue
+            if p.shape[-1] % 128 or (p.numel() // p.shape[-1]) % 128:
+                continue
+            w8 = Fp8Weight.empty_like(p)
+            register_fp8(p, w8)
+            self.fp8[name] = w8
+        self.sync_fp8(force=True)
+
+    def disable_fp8(self) -> None:
+        from miles_b200.ops.fp8 import unregister_fp8
+
+        for name in self.fp8:
+            unregister_fp8(self.params[name])
+        self.fp8 = {}
+
+    @torch.no_grad()
+    def sync_fp8(self, force: bool = False) -> None:
+        """Re-quantise the fp8 copies when the bf16 weights changed (new weight version); not
+        inside a CUDA graph capture (the captured kernels read the copies in place)."""
+        if not self.fp8 or (not force and self._fp8_version == self.weight_version):
+            return
+        if self.device.type == "cuda" and torch.cuda.is_current_stream_capturing():
+            return
+        ev = None
+        if self.device.type == "cuda":
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        for name, w8 in self.fp8.items():
+            w8.requant_(self.params[name])
+        if ev is not None:
+            ev[1].record()
+            self.fp8_sync_events.append(ev)  # device time of each re-quantisation (refit)
+        self._fp8_version = self.weight_version
 
     # -------------------------------------------------------------------------------- params
     @torch.no_grad()
@@ -725,6 +784,7 @@ class Transformer(torch.nn.Module):
         model chunk to run: the embedding belongs to chunk 0 of the first rank, the final norm to
         the last chunk of the last rank."""
         cfg = self.cfg
+        self.sync_fp8()
         if self.tp is not None and self.sequence_parallel and record_experts is None and self.cp is None:
             return self._forward_train_sp(tokens, meta, replay_experts)
         if self.cp is not None:
@@ -824,6 +884,7 @@ class Transformer(torch.nn.Module):
         (linear-attention layers: the final states of sequence b to row state_rows[b]).
         Returns the final hidden of every token [T, H]."""
         cfg = self.cfg
+        self.sync_fp8()
         r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
         pend = None
         for i in range(cfg.num_layers):
@@ -868,6 +929,7 @@ class Transformer(torch.nn.Module):
         (cache row of the new token); ctx_lens int32 [B] = positions + 1. Returns hidden [B,H]."""
         cfg = self.cfg
         B = tokens.shape[0]
+        self.sync_fp8()
         r = F.embedding(tokens.long(), self.params["embed_tokens.weight"])
         pend = None
         for i in range(cfg.num_layers):

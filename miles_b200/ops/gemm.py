@@ -175,8 +175,46 @@ class _Linear(torch.autograd.Function):
         return dx, dw
 
 
+class _Fp8Linear(_Linear):
+    """Forward on the weight's registered fp8 copy (block-scaled fp8 GEMM, x quantised 1 x 128
+    on the fly); the backward of the bf16 linear (data-grad with the bf16 weight, weight-grad
+    into the bf16 parameter's gradient)."""
+
+    @staticmethod
+    def forward(ctx, x, w, w8):
+        from miles_b200.ops.fp8 import fp8_linear
+
+        shp = x.shape
+        y = fp8_linear(x.reshape(-1, shp[-1]).contiguous(), w8)
+        ctx.save_for_backward(x, w)
+        return y.view(*shp[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        if not use_native(dy):
+            x, w = ctx.saved_tensors
+            x2 = x.reshape(-1, x.shape[-1])
+            dy2 = dy.reshape(-1, dy.shape[-1])
+            dx = (dy2 @ w).view(x.shape) if ctx.needs_input_grad[0] else None
+            dw = (dy2.t() @ x2) if ctx.needs_input_grad[1] else None
+            return dx, dw, None
+        dx, dw = _Linear.backward(ctx, dy)
+        return dx, dw, None
+
+
 def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """y = x @ w.T  (w: [out, in], bf16)."""
+    """y = x @ w.T  (w: [out, in], bf16). A weight with a registered fp8 copy
+    (miles_b200.ops.fp8.register_fp8) runs its forward in block-scaled fp8."""
+    from miles_b200.ops.fp8 import fp8_of
+
+    w8 = fp8_of(w)
+    if w8 is not None:
+        if not (torch.is_grad_enabled() and (x.requires_grad or w.requires_grad)):
+            from miles_b200.ops.fp8 import fp8_linear
+
+            shp = x.shape
+            return fp8_linear(x.reshape(-1, shp[-1]).contiguous(), w8).view(*shp[:-1], w.shape[0])
+        return _Fp8Linear.apply(x, w, w8)
     if not use_native(x):
         return torch.nn.functional.linear(x, w)
     return _Linear.apply(x, w)
@@ -232,8 +270,60 @@ class _LinearSwiGLU(torch.autograd.Function):
         return dx, dw
 
 
+class _Fp8LinearSwiGLU(_LinearSwiGLU):
+    """SwiGLU projection with its forward on the registered fp8 copy (SwiGLU fused into the fp8
+    GEMM epilogue); backward of the bf16 form."""
+
+    @staticmethod
+    def forward(ctx, x, w, w8):
+        shp = x.shape
+        a, gu = _fp8_swiglu(x.reshape(-1, shp[-1]).contiguous(), w8, w.shape[0] // 2, True)
+        ctx.save_for_backward(x, w, gu)
+        return a.view(*shp[:-1], w.shape[0] // 2)
+
+    @staticmethod
+    def backward(ctx, da):
+        if not use_native(da):
+            from miles_b200.ops.norm import swiglu_bwd_raw
+
+            x, w, gu = ctx.saved_tensors
+            dgu = swiglu_bwd_raw(gu, da.reshape(-1, da.shape[-1]))
+            x2 = x.reshape(-1, x.shape[-1])
+            dx = (dgu @ w).view(x.shape) if ctx.needs_input_grad[0] else None
+            dw = (dgu.t() @ x2) if ctx.needs_input_grad[1] else None
+            return dx, dw, None
+        dx, dw = _LinearSwiGLU.backward(ctx, da)
+        return dx, dw, None
+
+
+def _fp8_swiglu(x2: torch.Tensor, w8, F: int, save_gu: bool):
+    from miles_b200.ops import fp8 as F8
+
+    M = x2.shape[0]
+    if not use_native(x2):
+        q, s = F8.quant_act(x2)
+        offs = torch.tensor([0, M], dtype=torch.int32)
+        cnt = torch.tensor([M], dtype=torch.int32)
+        a, gu = F8.fp8_gemm_grouped_ref(q, s, w8, offs, cnt, 2 * F, swiglu_f=F, out_dtype=x2.dtype)
+        return a, (gu if save_gu else None)
+    q, s = F8.quant_act(x2)
+    a = torch.empty(M, F, dtype=torch.bfloat16, device=x2.device)
+    gu = torch.empty(M, 2 * F, dtype=torch.bfloat16, device=x2.device) if save_gu else None
+    F8.fp8_gemm(q, s, w8, a, M, 2 * F, swiglu_f=F, gu=gu)
+    return a, gu
+
+
 def linear_swiglu(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """swiglu(x @ w.T) with w = [gate; up] ([2F, in]); one kernel on the GPU."""
+    from miles_b200.ops.fp8 import fp8_of
+
+    w8 = fp8_of(w)
+    if w8 is not None:
+        if not (torch.is_grad_enabled() and (x.requires_grad or w.requires_grad)):
+            shp = x.shape
+            a, _ = _fp8_swiglu(x.reshape(-1, shp[-1]).contiguous(), w8, w.shape[0] // 2, False)
+            return a.view(*shp[:-1], w.shape[0] // 2)
+        return _Fp8LinearSwiGLU.apply(x, w, w8)
     if not use_native(x):
         from miles_b200.ops.norm import swiglu_ref
 

@@ -61,9 +61,25 @@ def route_ref(logits: torch.Tensor, cfg: RouterCfg, bias=None, replay_idx=None):
 
 def moe_ref(x, router_w, w1, w2, cfg: RouterCfg, bias=None, replay_idx=None):
     """fp32 reference of the whole expert layer."""
+    from miles_b200.ops.fp8 import fp8_of, quant_act_ref
+
     logits = x.float() @ router_w.float().t()
     idx, w = route_ref(logits, cfg, bias, replay_idx)
     T, H = x.shape
+    w1q, w2q = fp8_of(w1), fp8_of(w2)
+    if w1q is not None and w2q is not None:
+        # block-scaled fp8 experts: quantise-dequantise both operands of each expert GEMM
+        # (the fp8 values in the forward; gradients pass straight through to the bf16 operands)
+        def qdq(a):
+            q, s = quant_act_ref(a.detach())
+            K = a.shape[1]
+            return a + ((q.float().view(-1, K // 128, 128) * s.t()[..., None]).view(-1, K) - a).detach()
+
+        w1 = w1 + (w1q.dequant().view(w1.shape) - w1).detach()
+        w2 = w2 + (w2q.dequant().view(w2.shape) - w2).detach()
+    else:
+        def qdq(a):
+            return a
     y = torch.zeros(T, H, dtype=torch.float32, device=x.device)
     for e in range(cfg.E):
         tok, slot = (idx == e).nonzero(as_tuple=True)
@@ -71,9 +87,9 @@ def moe_ref(x, router_w, w1, w2, cfg: RouterCfg, bias=None, replay_idx=None):
             continue
         # intermediate roundings follow the activation dtype (bf16 on the kernel path)
         rd = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
-        gu = (x[tok].float() @ w1[e].float().t()).to(rd)
+        gu = (qdq(x[tok].float()) @ w1[e].float().t()).to(rd)
         a = swiglu_ref(gu)
-        o = (a.float() @ w2[e].float().t()).to(rd)
+        o = (qdq(a.float()) @ w2[e].float().t()).to(rd)
         y.index_add_(0, tok, w[tok, slot][:, None] * o.float())
     return y.to(x.dtype), idx
 
@@ -143,6 +159,12 @@ def _accum_grouped_wgrad(w: torch.Tensor, dy: torch.Tensor, x: torch.Tensor, pla
 def experts_forward(xs, w1, w2, plan: MoEPlan, save_gu: bool = True):
     """gate_up GEMM with the SwiGLU fused into its epilogue, then the down GEMM. The
     pre-activation gu is kept only when a backward follows."""
+    from miles_b200.ops.fp8 import fp8_experts, fp8_of
+
+    w1q, w2q = fp8_of(w1), fp8_of(w2)
+    if w1q is not None and w2q is not None:
+        E, N2, H = w1.shape
+        return fp8_experts(xs, w1q, w2q, plan.offsets, plan.counts, E, N2 // 2, H, save_gu)
     n = plan.T * plan.k
     # without a backward the padding rows are never read: skip writing them
     cnt = None if save_gu else plan.counts

@@ -249,6 +249,13 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
         from miles_b200.checkpoint.hf import load_hf
 
         load_hf(model, args.hf_checkpoint)
+    fmt, recipe = getattr(args, "fp8_format", None), getattr(args, "fp8_recipe", "blockwise")
+    if fmt:
+        # unified block-scaled fp8 training + rollout (the reference's --fp8-format e4m3
+        # --fp8-recipe blockwise with fp8 rollout engines)
+        if fmt != "e4m3" or recipe != "blockwise":
+            raise ValueError(f"fp8 supports --fp8-format e4m3 --fp8-recipe blockwise (got {fmt} / {recipe})")
+        model.enable_fp8()
     if getattr(args, "lora_rank", 0):
         from miles_b200.models.lora import LoRA
 

@@ -11,7 +11,9 @@ kernels: 4096 tokens, top-8 of 128 experts, forward and backward), rl_step (Qwen
 with 2 layers: one training step of 8192 packed tokens -- norms, RoPE, router, MoE permute /
 combine, SwiGLU, log-prob, policy loss, Adam -- and 8 engine decode steps of 64 sequences --
 decode-state prep / commit, fused route + dispatch, sampler; the small-kernel profiles use it),
-rl_math (GRPO advantages and chunked GAE over 64k tokens).
+rl_math (GRPO advantages and chunked GAE over 64k tokens), fp8_gemm_dense (block-scaled fp8
+GEMM 8192x6144x2048 with its 1 x 128 activation quantisation), fp8_grouped_decode (the
+gemm_grouped_decode step on fp8 expert weights), attn_decode256 (256 sequences x 4096 keys).
 """
 import sys
 
@@ -23,6 +25,26 @@ if case == "gemm_dense":
     a = torch.randn(8192, 2048, device="cuda", dtype=torch.bfloat16)
     b = torch.randn(6144, 2048, device="cuda", dtype=torch.bfloat16)
     for _ in range(4): G.matmul_nt(a, b)
+elif case == "fp8_gemm_dense":
+    from miles_b200.ops import fp8 as F8
+    a = torch.randn(8192, 2048, device="cuda", dtype=torch.bfloat16)
+    w = F8.Fp8Weight.from_bf16(torch.randn(6144, 2048, device="cuda", dtype=torch.bfloat16))
+    out = torch.empty(8192, 6144, device="cuda", dtype=torch.bfloat16)
+    for _ in range(4):
+        aq, sa = F8.quant_act(a)
+        F8.fp8_gemm(aq, sa, w, out, 8192, 6144)
+elif case == "fp8_grouped_decode":
+    from miles_b200.ops import fp8 as F8
+    from miles_b200.ops.moe import MoEPlan
+    E, K, F, k, T = 128, 2048, 768, 8, 64
+    idx = torch.stack([torch.randperm(E, device='cuda')[:k] for _ in range(T)]).int()
+    plan = MoEPlan(idx, E)
+    x = torch.randn(T, K, device='cuda', dtype=torch.bfloat16)
+    xs = plan.gather(x)
+    w1 = F8.Fp8Weight.from_bf16(torch.randn(E * 2 * F, K, device='cuda', dtype=torch.bfloat16))
+    w2 = F8.Fp8Weight.from_bf16(torch.randn(E * K, F, device='cuda', dtype=torch.bfloat16))
+    for _ in range(4):
+        F8.fp8_experts(xs, w1, w2, plan.offsets, plan.counts, E, F, K, save_gu=False)
 elif case == "gemm_grouped_decode":
     from miles_b200.ops import gemm as G
     from miles_b200.ops.moe import MoEPlan
@@ -48,9 +70,9 @@ elif case in ("attn_fwd", "attn_bwd"):
         o = varlen_attention(q, k_, v, meta)
         if case == "attn_bwd":
             o.backward(torch.ones_like(o))
-elif case == "attn_decode":
+elif case in ("attn_decode", "attn_decode256"):
     from miles_b200.ops.attention import decode_attention
-    B, nq, nkv, ctx, P = 64, 32, 4, 4096, 64
+    B, nq, nkv, ctx, P = 64 if case == "attn_decode" else 256, 32, 4, 4096, 64
     pages = B * ctx // P
     kc = torch.randn(pages * P, nkv, 128, device='cuda', dtype=torch.bfloat16)
     vc = torch.randn(pages * P, nkv, 128, device='cuda', dtype=torch.bfloat16)

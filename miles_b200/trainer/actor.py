@@ -46,6 +46,9 @@ class TrainItem:
     old_logp: list[float] | None = None
     ref_logp: list[float] | None = None
     routed_experts: np.ndarray | None = None    # [len(tokens)-1, L_moe, k] int32
+    # response index from which rollout_logp was produced by the current weights (partial
+    # rollout resumes a sample under newer weights; earlier tokens are off-policy)
+    fresh_from: int = 0
 
     @property
     def resp_len(self) -> int:
@@ -346,7 +349,8 @@ class Actor:
         n_tokens = global_num_tokens or sum(
             (sum(it.loss_mask) if it.loss_mask is not None else it.resp_len) for it in items)
         metrics = torch.zeros(len(METRIC_NAMES) + 1, dtype=torch.float64, device=self.dev)
-        self._parity = torch.zeros(2, dtype=torch.float64, device=self.dev)  # sum |old - rollout|, count
+        # sum |old - rollout|, count; the same over tokens sampled under the current weights
+        self._parity = torch.zeros(4, dtype=torch.float64, device=self.dev)
         mbs = make_micro_batches([len(it.tokens) for it in items], cfg)
         mtp_total = torch.zeros((), dtype=torch.float32, device=self.dev)
         if model.pp is not None:
@@ -384,8 +388,10 @@ class Actor:
         model.weight_version += 1
         out = {k: float(v) for k, v in zip(METRIC_NAMES + ["entropy"], metrics.tolist())}
         if cfg.old_logp_from_forward:
-            s_, n_ = self._parity.tolist()
+            s_, n_, sf, nf = self._parity.tolist()
             out["train_rollout_logprob_abs_diff"] = s_ / max(n_, 1.0)
+            out["train_rollout_logprob_abs_diff_current_weights"] = sf / max(nf, 1.0)
+            out["train_rollout_logprob_current_weight_tokens"] = nf
         out["grad_norm"] = float(self.opt.grad_norm())
         out["lr"] = float(self.opt.lr)
         if model.mtp_train and cfg.mtp_loss_scale:
@@ -400,9 +406,10 @@ class Actor:
         """Host-built inputs and per-token loss terms of one micro-batch."""
         cfg = self.cfg
         tok, meta, sel, tgt = self._mb_inputs(sub)
-        adv, old, roll, ref, wgt = [], [], [], [], []
+        adv, old, roll, ref, wgt, fresh = [], [], [], [], [], []
         for it in sub:
             n = it.resp_len
+            fresh.append((np.arange(n) >= it.fresh_from).astype(np.float32))
             mask = np.asarray(it.loss_mask if it.loss_mask is not None else [1] * n, np.float32)
             a = it.advantage
             adv.append(np.full(n, a, np.float32) if np.isscalar(a) else np.asarray(a, np.float32))
@@ -422,7 +429,7 @@ class Actor:
         T = lambda xs: to_device(np.concatenate(xs), self.dev)  # noqa: E731
         seg = to_device(np.repeat(np.arange(len(sub)), [it.resp_len for it in sub]), self.dev)
         return {"tok": tok, "meta": meta, "sel": sel, "tgt": tgt, "n": len(sub), "seg": seg,
-                "old": T(old), "adv": T(adv), "wgt": T(wgt),
+                "old": T(old), "adv": T(adv), "wgt": T(wgt), "fresh": T(fresh),
                 "roll": T(roll) if any(r is not None for r in roll) else None,
                 "ref": T(ref) if ref and cfg.loss.kl_type != "none" else None}
 
@@ -432,8 +439,12 @@ class Actor:
             prep = dict(prep, old=lp.detach().float())
             if prep["roll"] is not None:
                 mask = (prep["wgt"] > 0).double()
-                self._parity[0] += ((prep["old"] - prep["roll"]).abs().double() * mask).sum()
+                d = (prep["old"] - prep["roll"]).abs().double()
+                self._parity[0] += (d * mask).sum()
                 self._parity[1] += mask.sum()
+                fm = mask * prep["fresh"].double()
+                self._parity[2] += (d * fm).sum()
+                self._parity[3] += fm.sum()
         self._cur_total_lens = [b - a for a, b in zip(prep["meta"].cu_list[:-1], prep["meta"].cu_list[1:])]
         loss, m = self._loss(lp, ent, prep["seg"], prep["n"], prep["old"], prep["adv"], prep["wgt"],
                              prep["roll"], prep["ref"])

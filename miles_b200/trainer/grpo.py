@@ -96,6 +96,7 @@ class ColocatedRL:
         for g in groups:
             for s in g:
                 md = s.metadata
+                md["fresh_from"] = s.response_length  # tokens from here on: current weights
                 left = md["max_new"] - s.response_length
                 if left <= 0 or md.get("finished"):
                     continue
@@ -159,7 +160,8 @@ class ColocatedRL:
         adv = grpo_advantages(r, cfg.n_samples_per_prompt, cfg.normalize_std).cpu().numpy()
         items = [TrainItem(tokens=s.tokens, prompt_len=s.prompt_length, advantage=float(a),
                            loss_mask=s.loss_mask, rollout_logp=s.rollout_log_probs,
-                           routed_experts=s.rollout_routed_experts)
+                           routed_experts=s.rollout_routed_experts,
+                           fresh_from=s.metadata.get("fresh_from", 0))
                  for s, a in zip(samples, adv)]
         # old log-probs (forward pass); bitwise equal to the rollout's under colocated weights
         diff = 0.0
@@ -179,6 +181,10 @@ class ColocatedRL:
         m = self.actor.train_step(items, global_num_samples=len(items) * world)
         if self.actor.cfg.old_logp_from_forward:
             diff = m.pop("train_rollout_logprob_abs_diff", 0.0)
+            m["train/train_rollout_logprob_abs_diff_current_weights"] = m.pop(
+                "train_rollout_logprob_abs_diff_current_weights", 0.0)
+            m["train/train_rollout_logprob_current_weight_tokens"] = m.pop(
+                "train_rollout_logprob_current_weight_tokens", 0.0)
         t_train = time.perf_counter()
         self.rollout_id += 1
         n_resp = sum(s.response_length for s in samples)

@@ -146,6 +146,11 @@ def add_rollout_args(p):
     g.add_argument("--update-weight-transport", choices=["auto", "peer", "nccl"], default="auto",
                    help="trainer -> engine refit: kernels storing into the engines' IPC-mapped "
                         "staging over NVLink (peer), or NCCL broadcast")
+    g.add_argument("--fp8-format", choices=["e4m3", "hybrid"], default=None,
+                   help="block-scaled fp8 forward GEMMs in training and rollout (e4m3 only)")
+    g.add_argument("--fp8-recipe", choices=["blockwise", "mxfp8", "delayed", "tensorwise"],
+                   default="blockwise", help="fp8 scaling recipe (blockwise: 1x128 activation "
+                   "and 128x128 weight scales)")
     g.add_argument("--update-weight-quant", choices=["none", "fp8"], default="none",
                    help="quantise weights at refit (fp8: 128x128 block-scaled e4m3 broadcast)")
     g.add_argument("--fully-async", action="store_true", default=False,
