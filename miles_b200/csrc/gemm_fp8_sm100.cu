@@ -64,7 +64,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES_RAW = (196 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
-  static constexpr int NBUF = 4;  // TMEM buffers of BN columns (K blocks in flight)
+  static constexpr int NBUF = BN >= 128 ? 4 : 8;  // TMEM buffers of BN columns (K blocks in flight)
   static constexpr int TMEM_COLS = NBUF * BN <= 32 ? 32 : NBUF * BN <= 64 ? 64 : NBUF * BN <= 128 ? 128
                                  : NBUF * BN <= 256 ? 256 : 512;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
@@ -285,29 +285,51 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
       float acc0[Q], acc1[Q];
 #pragma unroll
       for (int i = 0; i < Q; ++i) acc0[i] = acc1[i] = 0.f;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const float sav = row_in ? __ldg(p.sa + (long long)kb * p.lds + row) : 0.f;
-        const float s0 = sav * __ldg(sb0 + kb);
-        const float s1 = sav * __ldg(sb1 + kb);
-        if (!__all_sync(0xffffffff, wait_or_abort(tfull_bar + buf, bphase, abort_flag, p.err))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t r0[Q], r1[Q];
-        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * BN;
-        tld<Q>(taddr + c0, r0);
-        tld<Q>(taddr + c1, r1);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(tempty_bar + buf);
+      // The three scales of K block kb are loaded PF blocks ahead (a ring of registers indexed
+      // by kb % PF after unrolling), so the global-load latency overlaps the previous blocks'
+      // TMEM reads instead of stalling every block's FMAs.
+      constexpr int PF = 4;
+      float pa[PF], pb0[PF], pb1[PF];
 #pragma unroll
-        for (int i = 0; i < Q; ++i) {
-          acc0[i] = fmaf(__uint_as_float(r0[i]), s0, acc0[i]);
-          acc1[i] = fmaf(__uint_as_float(r1[i]), s1, acc1[i]);
+      for (int u = 0; u < PF; ++u) {
+        const bool in = u < nkb;
+        pa[u] = in && row_in ? __ldg(p.sa + (long long)u * p.lds + row) : 0.f;
+        pb0[u] = in ? __ldg(sb0 + u) : 0.f;
+        pb1[u] = in ? __ldg(sb1 + u) : 0.f;
+      }
+      for (int kb0 = 0; kb0 < nkb && ok; kb0 += PF) {
+#pragma unroll
+        for (int u = 0; u < PF; ++u) {
+          const int kb = kb0 + u;
+          if (kb >= nkb) break;
+          const float s0 = pa[u] * pb0[u];
+          const float s1 = pa[u] * pb1[u];
+          const int nk = kb + PF;  // refill this slot
+          if (nk < nkb) {
+            pa[u] = row_in ? __ldg(p.sa + (long long)nk * p.lds + row) : 0.f;
+            pb0[u] = __ldg(sb0 + nk);
+            pb1[u] = __ldg(sb1 + nk);
+          }
+          if (!__all_sync(0xffffffff, wait_or_abort(tfull_bar + buf, bphase, abort_flag, p.err))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t r0[Q], r1[Q];
+          const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * BN;
+          tld<Q>(taddr + c0, r0);
+          tld<Q>(taddr + c1, r1);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty_bar + buf);
+#pragma unroll
+          for (int i = 0; i < Q; ++i) {
+            acc0[i] = fmaf(__uint_as_float(r0[i]), s0, acc0[i]);
+            acc1[i] = fmaf(__uint_as_float(r1[i]), s1, acc1[i]);
+          }
+          if (++buf == NBUF) { buf = 0; bphase ^= 1; }
         }
-        if (++buf == NBUF) { buf = 0; bphase ^= 1; }
       }
       if (!ok || !row_ok) continue;
       if (p.epi == 4) {
