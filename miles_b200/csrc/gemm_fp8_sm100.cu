@@ -8,7 +8,7 @@
 //
 // Because the scales change with every 128-wide K block, the tensor cores cannot accumulate
 // the whole K range in one TMEM accumulator. Each K block is instead a fresh 128 x BN x 128
-// product (4 kind::f8f6f4 UMMAs of K = 32) written into one of NBUF TMEM buffers; eight
+// product (4 kind::f8f6f4 UMMAs of K = 32) written into one of NBUF TMEM buffers; the
 // epilogue warps read the buffer back (tcgen05.ld), release it to the MMA warp at once, and
 // fold it into fp32 register accumulators with the block's combined scale. The MMA of K block
 // j+1..j+NBUF-1 runs while the epilogue scales K block j. Rows and columns are independent and
@@ -21,9 +21,10 @@
 // 4 SwiGLU (B = [gate; up] per group, output silu(gate) * up, optionally the [gate | up]
 // product for the backward), both with the bf16 rounding points of the bf16 kernels.
 //
-// Roles (320 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer, warps 2..9
-// epilogue. Warp w may only read TMEM lanes 32*(w%4)..+31, so warps 2..5 and 6..9 cover the
-// 128 rows twice; the two sets split the columns.
+// Roles: warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer, then NSETS sets of four
+// epilogue warps (NSETS = 4 for BN >= 64: 576 threads). Warp w may only read TMEM lanes
+// 32*(w%4)..+31, so every set covers the 128 rows once; the sets split the columns. Several
+// warps per SM sub-partition hide the TMEM-load and scale-load latency of each K block.
 //
 // Reference roles replaced: the blockwise fp8 GEMMs of TransformerEngine (--fp8-recipe
 // blockwise, examples/low_precision/README.md:17-18) and of DeepGEMM in the rollout engine
@@ -68,7 +69,9 @@ struct Cfg {
   static constexpr int TMEM_COLS = NBUF * BN <= 32 ? 32 : NBUF * BN <= 64 ? 64 : NBUF * BN <= 128 ? 128
                                  : NBUF * BN <= 256 ? 256 : 512;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
-  static constexpr int Q = BN / 4;  // columns per epilogue warp and range (two ranges per warp)
+  static constexpr int NSETS = BN >= 64 ? 4 : 2;  // sets of four epilogue warps
+  static constexpr int THREADS = 64 + 128 * NSETS;
+  static constexpr int Q = BN / (2 * NSETS);  // columns per epilogue warp and range (two ranges)
 };
 
 struct Tile {
@@ -149,7 +152,7 @@ MB_DEVICE void store_row(__nv_bfloat16* out, const float* v, int valid_cols) {
 }
 
 template <int BN, int MODE>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
 gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const Params p) {
   using C = Cfg<BN>;
@@ -175,7 +178,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     }
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(tfull_bar + b, 1);
-      mbar_init(tempty_bar + b, 8);
+      mbar_init(tempty_bar + b, 4 * C::NSETS);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -257,7 +260,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
   } else {
     // ---------------- Epilogue / scale-and-accumulate (warps 2..9) ----------------
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = (warp - 2) >> 2;  // epilogue set
     const int c0 = half * Q;           // first range: tile columns [c0, c0 + Q)
     const int c1 = BN / 2 + half * Q;  // second range: [c1, c1 + Q)
     int buf = 0;
@@ -388,7 +391,7 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   if (tiles == 0) return 0;
   const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-  mb_launch(kern, grid, 320, C::SMEM_BYTES, st, ta, tb, p);
+  mb_launch(kern, grid, C::THREADS, C::SMEM_BYTES, st, ta, tb, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 

@@ -13,7 +13,11 @@ combine, SwiGLU, log-prob, policy loss, Adam -- and 8 engine decode steps of 64 
 decode-state prep / commit, fused route + dispatch, sampler; the small-kernel profiles use it),
 rl_math (GRPO advantages and chunked GAE over 64k tokens), fp8_gemm_dense (block-scaled fp8
 GEMM 8192x6144x2048 with its 1 x 128 activation quantisation), fp8_grouped_decode (the
-gemm_grouped_decode step on fp8 expert weights), attn_decode256 (256 sequences x 4096 keys).
+gemm_grouped_decode step on fp8 expert weights), attn_decode256 (256 sequences x 4096 keys),
+small_kernels (the memory-bound kernels of a training / decode step on inputs larger than L2, a
+few GB in total: RMSNorm fwd / bwd, QK-norm + RoPE fwd / bwd, SwiGLU fwd / bwd, router fwd / bwd,
+MoE permute plan / gather / combine, LM-head log-prob / entropy, sampler, policy loss, Adam,
+fp8 activation and block quantisation).
 """
 import sys
 
@@ -45,6 +49,52 @@ elif case == "fp8_grouped_decode":
     w2 = F8.Fp8Weight.from_bf16(torch.randn(E * K, F, device='cuda', dtype=torch.bfloat16))
     for _ in range(4):
         F8.fp8_experts(xs, w1, w2, plan.offsets, plan.counts, E, F, K, save_gu=False)
+elif case == "small_kernels":
+    from miles_b200.ops import fp8 as F8
+    from miles_b200.ops.logprob import lm_head_logprob, sample_from_hidden
+    from miles_b200.ops.moe import RouterCfg, moe_experts
+    from miles_b200.ops.norm import qk_norm_rope, rms_norm, rope_tables, swiglu
+    from miles_b200.ops.optim import adam_
+    from miles_b200.ops.quant import fp8_block_quant
+    from miles_b200.ops.rl import PolicyLossCfg, policy_loss
+    T, H, E, F = 32768, 2048, 128, 768
+    for _ in range(2):
+        x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        w = torch.ones(H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        rms_norm(x, w).sum().backward()
+        qkv = torch.randn(T, 5120, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        cos, sin = rope_tables(8192, 128, 1e6, "cuda")
+        pos = (torch.arange(T, device="cuda") % 8192).int()
+        qw = torch.ones(128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        q, k, v = qk_norm_rope(qkv, qw, qw, pos, cos, sin, 32, 4)
+        (q.float().sum() + k.float().sum() + v.float().sum()).backward()
+        gu = torch.randn(T, 2 * F, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        swiglu(gu).sum().backward()
+        xm = torch.randn(8192, H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        rw = torch.randn(E, H, device="cuda", dtype=torch.bfloat16, requires_grad=True) * 0.02
+        w1 = torch.randn(E, 2 * F, H, device="cuda", dtype=torch.bfloat16) * 0.02
+        w2 = torch.randn(E, H, F, device="cuda", dtype=torch.bfloat16) * 0.02
+        moe_experts(xm, rw, w1, w2, RouterCfg(E, 8)).float().sum().backward()
+        hh = torch.randn(2048, H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        Wv = torch.randn(151936, H, device="cuda", dtype=torch.bfloat16) * 0.02
+        tg = torch.randint(0, 151936, (2048,), device="cuda", dtype=torch.int32)
+        lp, ent = lm_head_logprob(hh, Wv, tg)
+        n = lp.numel()
+        loss, _ = policy_loss(lp, lp.detach(), torch.randn(n, device="cuda"),
+                              torch.full((n,), 1.0 / n, device="cuda"), PolicyLossCfg(use_tis=True))
+        loss.backward()
+        hs = torch.randn(256, H, device="cuda", dtype=torch.bfloat16)
+        sample_from_hidden(hs, Wv, torch.ones(256, device="cuda"),
+                           torch.arange(256, device="cuda", dtype=torch.int64),
+                           torch.zeros(256, device="cuda", dtype=torch.int32))
+        N = 1 << 26
+        prm = torch.randn(N, device="cuda").bfloat16()
+        adam_(prm, torch.randn(N, device="cuda").bfloat16(), torch.zeros(N, device="cuda"),
+              torch.zeros(N, device="cuda"), master=torch.zeros(N, device="cuda"), lr=1e-6)
+        F8.quant_act(torch.randn(T, H, device="cuda", dtype=torch.bfloat16))
+        fp8_block_quant(torch.randn(6144, H, device="cuda", dtype=torch.bfloat16))
+        del x, qkv, gu, xm, Wv
+        torch.cuda.synchronize()
 elif case == "gemm_grouped_decode":
     from miles_b200.ops import gemm as G
     from miles_b200.ops.moe import MoEPlan

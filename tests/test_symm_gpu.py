@@ -308,9 +308,9 @@ def test_peer_refit_matches_nccl_refit(tmp_path):
     assert r["bf16_equal"] and r["fp8_equal"] and r["bf16_nonzero"]
 
 
-def _two_rank_ep(rank, port, out):
+def _two_rank_ep(rank, port, out, world=2):
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             device_id=torch.device("cuda", rank))
     from miles_b200.models.config import preset
     from miles_b200.models.transformer import Transformer
@@ -358,3 +358,86 @@ def test_ep_peer_transport_matches_nccl(tmp_path):
     r = torch.load(out)
     print(r)
     assert r["fwd_equal"] and r["grad_equal"] and r["nograd_equal"]
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_ep_peer_transport_matches_nccl_n_ranks(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = str(tmp_path / "ep.pt")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    mp.spawn(_two_rank_ep, args=(free_port(), out, world), nprocs=world, join=True)
+    r = torch.load(out)
+    assert r["fwd_equal"] and r["grad_equal"] and r["nograd_equal"]
+
+
+def _n_rank_collectives(rank, port, out, world):
+    """Symmetric collectives at `world` ranks against a rank-ordered reference: every rank's
+    part gathered with NCCL and summed in rank order in fp32, rounded once (the symmetric
+    kernels' arithmetic; NCCL's own all-reduce order differs above two ranks)."""
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=torch.device("cuda", rank))
+    from miles_b200.ops import check_device_error
+    from miles_b200.ops import gemm as G
+    from miles_b200.ops.norm import add_rms_norm
+    from miles_b200.parallel.symm import SymmComm
+
+    H = 2048
+    comm = SymmComm(dist.group.WORLD, hidden=H, cap_rows=1024)
+    torch.manual_seed(300 + rank)
+
+    def ordered_sum(x):
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x.contiguous())
+        acc = torch.zeros_like(x, dtype=torch.float32)
+        for p_ in parts:
+            acc += p_.float()
+        return acc.to(x.dtype)
+
+    ok = {}
+    for M in (1, 64, 512):
+        a = torch.randn(M, 1024, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(H, 1024, device="cuda", dtype=torch.bfloat16) * 0.03
+        r = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
+        dist.broadcast(r, 0)
+        nw = torch.rand(H, device="cuda", dtype=torch.bfloat16) + 0.5
+        dist.broadcast(nw, 0)
+        part = G.linear(a, w)
+        ref = ordered_sum(part)
+        ok[f"ar{M}"] = bool(torch.equal(comm.all_reduce(part), ref))
+        ok[f"gemm_ar{M}"] = bool(torch.equal(comm.gemm_all_reduce(a, w), ref))
+        y_ref, h_ref = add_rms_norm(ref, r, nw, 1e-6)
+        y, h = comm.gemm_all_reduce(a, w, res=r, norm_w=nw, eps=1e-6)
+        ok[f"gemm_ar_norm{M}"] = bool(torch.equal(y, y_ref) and torch.equal(h, h_ref))
+    rows = 128 * world
+    x = torch.randn(rows, H, device="cuda", dtype=torch.bfloat16)
+    ref = ordered_sum(x)
+    ok["rs"] = bool(torch.equal(comm.reduce_scatter(x), ref[rank * 128:(rank + 1) * 128]))
+    parts = [torch.empty(100, H, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    dist.all_gather(parts, x[:100].contiguous())
+    ok["ag"] = bool(torch.equal(comm.all_gather(x[:100]), torch.cat(parts)))
+    a = torch.randn(rows, 1024, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(H, 1024, device="cuda", dtype=torch.bfloat16) * 0.03
+    ref = ordered_sum(G.linear(a, w))
+    ok["gemm_rs"] = bool(torch.equal(comm.gemm_reduce_scatter(a, w), ref[rank * 128:(rank + 1) * 128]))
+    check_device_error()
+    flags = torch.tensor([int(all(ok.values()))], device="cuda")
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    comm.close()
+    if rank == 0:
+        torch.save({"ok": bool(flags.item()), "detail": ok}, out)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_symm_collectives_n_ranks(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = str(tmp_path / "c.pt")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    mp.spawn(_n_rank_collectives, args=(free_port(), out, world), nprocs=world, join=True)
+    r = torch.load(out)
+    print(r)
+    assert r["ok"], r["detail"]
