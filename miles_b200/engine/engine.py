@@ -18,6 +18,7 @@ torch_memory_saver release/resume of KV memory (E15).
 """
 from __future__ import annotations
 
+import dataclasses
 import math
 import threading
 import time
@@ -59,11 +60,14 @@ class GenResult:
 
 
 class _Seq:
-    __slots__ = ("req", "pages", "slot", "done", "reason", "prompt_experts")
+    __slots__ = ("req", "pages", "slot", "done", "reason", "prompt_experts", "order")
+    _count = 0
 
     def __init__(self, req: GenRequest, pages: list[int]):
         self.req = req
         self.pages = pages
+        _Seq._count += 1
+        self.order = _Seq._count  # admission order (the latest admitted is preempted first)
         self.slot = -1           # sequence slot: row of the device decode state (and GDN state)
         self.done = False
         self.reason = ""
@@ -160,7 +164,8 @@ def _commit_ref(ds: DecodeState, st: dict, tok, lp, experts):
 class RolloutEngine:
     def __init__(self, model: Transformer, max_batch: int = 64, num_pages: int | None = None,
                  mem_fraction: float = 0.9, use_cuda_graph: bool = True, max_pages_per_seq: int = 160,
-                 steps_per_sync: int = 8, persistent_kv: bool = True, prefill_tokens: int = 32768):
+                 steps_per_sync: int = 8, persistent_kv: bool = True, prefill_tokens: int = 32768,
+                 lazy_pages: bool = True):
         self.model = model
         self.cfg = model.cfg
         self.dev = model.device
@@ -170,6 +175,11 @@ class RolloutEngine:
         # decode steps run back to back on the device between two host visits (one graph)
         self.steps_per_sync = max(1, steps_per_sync)
         self.prefill_tokens = prefill_tokens   # token budget of one packed prefill
+        # KV pages on demand: a sequence holds pages for its prompt and the next host visit's
+        # decode steps only, and gets more as it grows; when the pool runs dry the latest
+        # admitted sequence is preempted (its tokens kept, resumed later by re-prefill).
+        # Otherwise every request reserves pages for prompt + max_new_tokens at admission.
+        self.lazy_pages = lazy_pages
         self._num_pages_req = num_pages
         self._mem_fraction = mem_fraction
         self.cache: KVCache | None = None
@@ -402,8 +412,15 @@ class RolloutEngine:
         n_decode_steps = n_prefills = n_syncs = 0
         cur_rows: tuple | None = None
         cur_key = None
+        carry: dict[int, tuple] = {}  # rid -> (tokens, logprobs, routed experts) before preemption
+        n_preempt = 0
 
         def finish(res: GenResult):
+            if res.rid in carry:
+                toks, lps, ex = carry.pop(res.rid)
+                res = dataclasses.replace(res, tokens=toks + res.tokens, logprobs=lps + res.logprobs,
+                                          routed_experts=res.routed_experts if res.routed_experts is not None
+                                          else ex)
             cb = cbs.pop(res.rid, None)
             if cb is not None:
                 cb(res)
@@ -426,7 +443,7 @@ class RolloutEngine:
                     raise ValueError("routed-expert recording stores expert ids as uint8 (<= 256 experts)")
                 ds.ensure_exp()
             if pending and free_slots:
-                new, pending = self._admit(pending, len(free_slots))
+                new, pending = self._admit(pending, len(free_slots), len(live))
                 if new:
                     for sq in new:
                         sq.slot = free_slots.pop()
@@ -477,6 +494,8 @@ class RolloutEngine:
                     free_slots.append(sl)
             if stop_when is not None and stop_when(results):
                 self.aborted = True
+            elif self.lazy_pages and live:
+                n_preempt += self._grow(live, nout, pending, carry, free_slots)
         if self.aborted:
             done, nout = self._read_flags()
             for sl, sq in list(live.items()):
@@ -486,7 +505,7 @@ class RolloutEngine:
             for r in pending:
                 finish(GenResult(r.rid, [], [], "abort", None, self.model.weight_version))
         self.stats = {"wall_s": time.perf_counter() - t0, "decode_steps": n_decode_steps,
-                      "prefills": n_prefills, "host_syncs": n_syncs}
+                      "prefills": n_prefills, "host_syncs": n_syncs, "preemptions": n_preempt}
         return [results[r.rid] for r in reqs if r.rid in results]
 
     @staticmethod
@@ -508,14 +527,71 @@ class RolloutEngine:
             torch.cuda.current_stream(self.dev).synchronize()
         return hf[0].numpy(), hf[1].numpy()
 
-    def _admit(self, pending, room: int):
-        """Take requests in order while batch slots (`room`) and KV pages last."""
+    def _cover(self, plen: int, nout: int, max_new: int) -> int:
+        """Pages a sequence must hold before the next graph replay (lazy pages): its fed
+        positions plus the replay's steps, capped at its full length."""
+        return math.ceil(min(plen + nout + self.steps_per_sync + 1, plen + max_new) / PAGE)
+
+    def _grow(self, live: dict, nout, pending: list, carry: dict, free_slots: list) -> int:
+        """Give every live sequence the pages its next `steps_per_sync` decode steps write
+        (oldest first); when the pool is empty, preempt the latest admitted sequence: its
+        tokens, log-probs and routing so far are kept and it is queued first, to resume by
+        re-prefilling prompt + tokens (sampling is keyed by position, so the continuation is the
+        same). Returns the number of preemptions."""
+        ds = self.ds
+        n_pre = 0
+        upd_s, upd_i, upd_p = [], [], []
+        for sq in sorted(live.values(), key=lambda q: q.order):
+            if sq.slot not in live or live[sq.slot] is not sq:
+                continue
+            want = self._cover(len(sq.req.prompt), int(nout[sq.slot]), sq.req.max_new_tokens)
+            while len(sq.pages) < want:
+                if self.free_pages:
+                    pg = self.free_pages.pop()
+                    upd_s.append(sq.slot)
+                    upd_i.append(len(sq.pages))
+                    upd_p.append(pg)
+                    sq.pages.append(pg)
+                    continue
+                victim = max(live.values(), key=lambda q: q.order)
+                n = int(nout[victim.slot])
+                res = self._result(victim, n, reason="abort")
+                prev = carry.get(victim.req.rid, ([], [], None))
+                carry[victim.req.rid] = (prev[0] + res.tokens, prev[1] + res.logprobs,
+                                         res.routed_experts if res.routed_experts is not None else prev[2])
+                ds.s_done[victim.slot] = 1
+                live.pop(victim.slot)
+                free_slots.append(victim.slot)
+                self.free_pages.extend(victim.pages)
+                victim.pages = []
+                pending.insert(0, dataclasses.replace(
+                    victim.req, prompt=list(victim.req.prompt) + res.tokens,
+                    max_new_tokens=victim.req.max_new_tokens - n))
+                n_pre += 1
+                if victim is sq:
+                    break
+        if upd_s:
+            keep = [j for j, sl in enumerate(upd_s) if sl in live]
+            if keep:
+                ds.s_pt[torch.tensor([upd_s[j] for j in keep], dtype=torch.long, device=self.dev),
+                        torch.tensor([upd_i[j] for j in keep], dtype=torch.long, device=self.dev)] = \
+                    torch.tensor([upd_p[j] for j in keep], dtype=torch.int32, device=self.dev)
+        return n_pre
+
+    def _admit(self, pending, room: int, n_live: int = 0):
+        """Take requests in order while batch slots (`room`) and KV pages last. With lazy pages
+        a page per running sequence stays in reserve for growth, so that admitting does not
+        immediately force a preemption."""
         wave, rest = [], []
         for r in pending:
             need = math.ceil((len(r.prompt) + r.max_new_tokens) / PAGE)
             if need > self.max_pages_per_seq:
                 raise ValueError(f"request needs {need} pages > max_pages_per_seq")
-            if not rest and len(wave) < room and need <= len(self.free_pages):
+            reserve = 0
+            if self.lazy_pages:
+                need = self._cover(len(r.prompt), 1, r.max_new_tokens)
+                reserve = n_live + len(wave) if (n_live or wave) else 0
+            if not rest and len(wave) < room and need + reserve <= len(self.free_pages):
                 wave.append(_Seq(r, [self.free_pages.pop() for _ in range(need)]))
             else:
                 rest.append(r)  # keep arrival order: no request overtakes an earlier one
