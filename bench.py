@@ -218,6 +218,7 @@ def main():
         if rank == 0:
             keys = ("perf/rollout_time", "perf/log_probs_time", "perf/actor_train_time",
                     "perf/step_time", "response_tokens", "rollout/generated_tokens",
+                    "rollout/decode_steps", "rollout/preemptions",
                     "train/train_rollout_logprob_abs_diff",
                     "train/train_rollout_logprob_abs_diff_current_weights", "grad_norm")
             print(tag, json.dumps({k: m.get(k) for k in keys}), file=sys.stderr, flush=True)

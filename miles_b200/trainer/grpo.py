@@ -200,6 +200,8 @@ class ColocatedRL:
             "perf/tokens_per_gpu_per_sec": self.generated_tokens / max(t_gen - t0, 1e-9),
             "rollout/generated_tokens": self.generated_tokens,
             "rollout/buffered_groups": len(self.buffer),
+            "rollout/decode_steps": self.engine.stats.get("decode_steps", 0),
+            "rollout/preemptions": self.engine.stats.get("preemptions", 0),
             "perf/actor_train_tok_per_s": n_tok / max(t_train - t_lp, 1e-9),
             "perf/actor_train_tflops": train_tflops(self.actor.model.cfg, [len(s.tokens) for s in samples],
                                                     t_train - t_lp),
