@@ -355,6 +355,15 @@ int64_t policy_loss(torch::Tensor logp, torch::Tensor old_logp, torch::Tensor ad
                  OT pg_out, torch::Tensor part, torch::Tensor metrics, double eps, double eps_hi,
                  double eps_c, double tis_lo, double tis_hi, double kl_coef, int64_t kl_type,
                  int64_t use_tis) {
+  // the kernel reads the rollout log-probs under TIS / IcePop and the reference log-probs under
+  // a KL term: reject the call on the host when they are missing (a null read would fault)
+  TORCH_CHECK(use_tis == 0 || rollout_logp.has_value(), "policy_loss: TIS needs rollout_logp");
+  TORCH_CHECK(kl_type == 0 || ref_logp.has_value(), "policy_loss: a KL term needs ref_logp");
+  const int64_t n = logp.numel();
+  for (const torch::Tensor* t : {&old_logp, &adv, &weight, &dlogp})
+    TORCH_CHECK(t->numel() == n, "policy_loss: operand sizes differ");
+  if (rollout_logp.has_value()) TORCH_CHECK(rollout_logp.value().numel() == n, "rollout_logp size");
+  if (ref_logp.has_value()) TORCH_CHECK(ref_logp.value().numel() == n, "ref_logp size");
   return mb_policy_loss(PT<float>(logp), PT<float>(old_logp), PT<float>(adv), PT<float>(weight),
                           PT<float>(rollout_logp), PT<float>(ref_logp), PT<float>(dlogp),
                           PT<float>(pg_out), PT<float>(part), PT<float>(metrics), logp.numel(),

@@ -97,6 +97,10 @@ def policy_loss_ref(logp, old_logp, adv, weight, cfg: PolicyLossCfg, rollout_log
 class _PolicyLoss(torch.autograd.Function):
     @staticmethod
     def forward(ctx, logp, old_logp, adv, weight, rollout_logp, ref_logp, cfg: PolicyLossCfg):
+        if cfg.use_tis and rollout_logp is None:
+            raise ValueError("policy_loss: TIS / IcePop needs the rollout log-probs")
+        if cfg.kl_type != "none" and ref_logp is None:
+            raise ValueError("policy_loss: a KL term needs the reference log-probs")
         n = logp.numel()
         dev = logp.device
         dlogp = torch.empty(n, dtype=torch.float32, device=dev)

@@ -58,40 +58,53 @@ elif case == "small_kernels":
     from miles_b200.ops.quant import fp8_block_quant
     from miles_b200.ops.rl import PolicyLossCfg, policy_loss
     T, H, E, F = 32768, 2048, 128, 768
+
+    def mark(name):
+        torch.cuda.synchronize()
+        print("ok", name, flush=True)
     for _ in range(2):
         x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
         w = torch.ones(H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
         rms_norm(x, w).sum().backward()
+        mark("rmsnorm")
         qkv = torch.randn(T, 5120, device="cuda", dtype=torch.bfloat16, requires_grad=True)
         cos, sin = rope_tables(8192, 128, 1e6, "cuda")
         pos = (torch.arange(T, device="cuda") % 8192).int()
         qw = torch.ones(128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
         q, k, v = qk_norm_rope(qkv, qw, qw, pos, cos, sin, 32, 4)
         (q.float().sum() + k.float().sum() + v.float().sum()).backward()
+        mark("qk_norm_rope")
         gu = torch.randn(T, 2 * F, device="cuda", dtype=torch.bfloat16, requires_grad=True)
         swiglu(gu).sum().backward()
+        mark("swiglu")
         xm = torch.randn(8192, H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
         rw = torch.randn(E, H, device="cuda", dtype=torch.bfloat16, requires_grad=True) * 0.02
         w1 = torch.randn(E, 2 * F, H, device="cuda", dtype=torch.bfloat16) * 0.02
         w2 = torch.randn(E, H, F, device="cuda", dtype=torch.bfloat16) * 0.02
         moe_experts(xm, rw, w1, w2, RouterCfg(E, 8)).float().sum().backward()
+        mark("moe")
         hh = torch.randn(2048, H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
         Wv = torch.randn(151936, H, device="cuda", dtype=torch.bfloat16) * 0.02
         tg = torch.randint(0, 151936, (2048,), device="cuda", dtype=torch.int32)
         lp, ent = lm_head_logprob(hh, Wv, tg)
         n = lp.numel()
         loss, _ = policy_loss(lp, lp.detach(), torch.randn(n, device="cuda"),
-                              torch.full((n,), 1.0 / n, device="cuda"), PolicyLossCfg(use_tis=True))
+                              torch.full((n,), 1.0 / n, device="cuda"), PolicyLossCfg(use_tis=True),
+                              rollout_logp=lp.detach() - 0.01)
         loss.backward()
+        mark("logprob+policy_loss")
         hs = torch.randn(256, H, device="cuda", dtype=torch.bfloat16)
         sample_from_hidden(hs, Wv, torch.ones(256, device="cuda"),
                            torch.arange(256, device="cuda", dtype=torch.int64),
                            torch.zeros(256, device="cuda", dtype=torch.int32))
+        mark("sample")
         N = 1 << 26
         prm = torch.randn(N, device="cuda").bfloat16()
         adam_(prm, torch.randn(N, device="cuda").bfloat16(), torch.zeros(N, device="cuda"),
               torch.zeros(N, device="cuda"), master=torch.zeros(N, device="cuda"), lr=1e-6)
+        mark("adam")
         F8.quant_act(torch.randn(T, H, device="cuda", dtype=torch.bfloat16))
+        mark("act_quant")
         fp8_block_quant(torch.randn(6144, H, device="cuda", dtype=torch.bfloat16))
         del x, qkv, gu, xm, Wv
         torch.cuda.synchronize()
