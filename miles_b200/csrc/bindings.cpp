@@ -201,6 +201,13 @@ int64_t qk_norm_rope_fwd(torch::Tensor qkv, OT qw, OT kw, torch::Tensor pos, tor
                       torch::Tensor v_out, OT slot, int64_t ld_kv, OT rstd, int64_t nq,
                       int64_t nkv, double eps, bool use_norm) {
   TORCH_CHECK(qkv.stride(-1) == 1);
+  // the kernel reads cos / sin as float2 pairs of a [positions, 64] table
+  TORCH_CHECK(cos_t.is_contiguous() && sin_t.is_contiguous() && cos_t.size(-1) == 64 &&
+                  sin_t.size(-1) == 64 && reinterpret_cast<uintptr_t>(cos_t.data_ptr()) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(sin_t.data_ptr()) % 8 == 0,
+              "qk_norm_rope: cos / sin must be contiguous [positions, 64] fp32 tables");
+  TORCH_CHECK(qkv.stride(0) % 2 == 0 && reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 4 == 0,
+              "qk_norm_rope: qkv rows must be 4-byte aligned");
   const int T = qkv.size(0);
   return mb_qk_norm_rope_fwd(P(qkv), qkv.stride(0), P(qw), P(kw), PT<int>(pos),
                                PT<float>(cos_t), PT<float>(sin_t), P(q_out), P(k_out), P(v_out),

@@ -425,42 +425,66 @@ __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, long long 
   const int lane = threadIdx.x & 31;
   int rows = M;
   if (offsets) rows = min(rows, __ldg(offsets + E));
-  const long long items = (long long)rows * nkb;
-  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long item = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < items;
-       item += nwarps) {
-    const int kb = (int)(item % nkb);
-    const long long row = item / nkb;
-    if (offsets && counts) {
-      int lo = 0, hi = E - 1;  // segment of this row: largest g with offsets[g] <= row
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (__ldg(offsets + mid) <= row) lo = mid; else hi = mid - 1;
+  const int items = rows * nkb;  // < 2^31 (checked on the host)
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  // U consecutive items (row-major over (row, kb)) per warp and iteration, all loaded before any
+  // is reduced; one 32-bit division per iteration locates the first of them
+  constexpr int U = 4;
+  for (int base = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * U; base < items;
+       base += nwarps * U) {
+    int row[U], kb[U];
+    row[0] = base / nkb;
+    kb[0] = base - row[0] * nkb;
+#pragma unroll
+    for (int u = 1; u < U; ++u) {
+      kb[u] = kb[u - 1] + 1;
+      row[u] = row[u - 1];
+      if (kb[u] == nkb) { kb[u] = 0; ++row[u]; }
+    }
+    uint2 raw[U];
+    bool use[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      use[u] = base + u < items;
+      if (use[u] && offsets && counts) {
+        int lo = 0, hi = E - 1;  // segment of this row: largest g with offsets[g] <= row
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (__ldg(offsets + mid) <= row[u]) lo = mid; else hi = mid - 1;
+        }
+        use[u] = row[u] - __ldg(offsets + lo) < __ldg(counts + lo);  // warp-uniform
       }
-      if (row - __ldg(offsets + lo) >= __ldg(counts + lo)) continue;  // warp-uniform
+      if (use[u])
+        raw[u] = *reinterpret_cast<const uint2*>(x + (long long)row[u] * ldx + kb[u] * 128 + lane * 4);
     }
-    const uint2 raw = *reinterpret_cast<const uint2*>(x + row * ldx + kb * 128 + lane * 4);
-    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
-    float v[4];
-    float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      v[i] = __bfloat162float(h[i]);
-      amax = fmaxf(amax, fabsf(v[i]));
-    }
-    amax = warp_max(amax);
-    const float sc = fmaxf(amax, 1e-12f) / 448.f;
-    const float inv = 1.f / sc;
-    uint32_t packed = 0;
+    for (int u = 0; u < U; ++u) {
+      if (!use[u]) continue;
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw[u]);
+      float v[4];
+      float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __nv_fp8_e4m3 e(fminf(fmaxf(v[i] * inv, -448.f), 448.f));
-      packed |= (uint32_t)(*reinterpret_cast<const uint8_t*>(&e)) << (8 * i);
+      for (int i = 0; i < 4; ++i) {
+        v[i] = __bfloat162float(h[i]);
+        amax = fmaxf(amax, fabsf(v[i]));
+      }
+      amax = warp_max(amax);
+      const float sc = fmaxf(amax, 1e-12f) / 448.f;
+      const float inv = 1.f / sc;
+      uint32_t packed = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_fp8_e4m3 e(fminf(fmaxf(v[i] * inv, -448.f), 448.f));
+        packed |= (uint32_t)(*reinterpret_cast<const uint8_t*>(&e)) << (8 * i);
+      }
+      *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(q) + (long long)row[u] * K + kb[u] * 128 +
+                                   lane * 4) = packed;
+      if (lane == 0) s[(long long)kb[u] * lds + row[u]] = sc;
     }
-    *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(q) + row * K + kb * 128 + lane * 4) = packed;
-    if (lane == 0) s[(long long)kb * lds + row] = sc;
   }
 }
+
+
 
 }  // namespace f8
 }  // namespace mb
@@ -474,10 +498,11 @@ extern "C" int mb_fp8_act_quant(const void* x, long long ldx, int M, int K, void
                                 long long lds, const int* offsets, const int* counts, int E,
                                 cudaStream_t st) {
   if (K % 128 || ldx % 4 || lds < M || (offsets && E < 1)) return -1;
+  if ((long long)M * (K / 128) >= (1ll << 31)) return -1;
   if (M == 0) return 0;
   const long long items = (long long)M * (K / 128);
   const int per_block = 8;
-  long long blocks = (items + per_block - 1) / per_block;
+  long long blocks = (items + 4 * per_block - 1) / (4 * per_block);
   if (blocks > 148 * 16) blocks = 148 * 16;  // grid-stride beyond 16 blocks per SM
   mb::mb_launch(mb::f8::act_quant_kernel, dim3((unsigned)blocks), dim3(per_block * 32), 0, st,
                 reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, K,

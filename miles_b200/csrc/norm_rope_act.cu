@@ -184,6 +184,10 @@ __global__ void reduce_parts_kernel(const float* __restrict__ parts, int nparts,
 // cos/sin tables: [max_pos, D/2] fp32. One warp per (token, head); lane owns 4 dims:
 // d = lane*2 + {0,1} in the first half and the same + D/2 in the second half.
 // ----------------------------------------------------------------------------------------------
+// One warp handles R consecutive heads of one token (R divides the head count): the R rows
+// are loaded before any of them is processed (more loads in flight per warp) and the token's
+// position / cos / sin are read once. Per element the arithmetic is that of one row at a time.
+template <int R>
 __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, long long ld_in,
                                         const __nv_bfloat16* __restrict__ qw,
                                         const __nv_bfloat16* __restrict__ kw,
@@ -202,45 +206,55 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, l
   const int nh = nq + 2 * nkv;
   const long long gw = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  if (gw >= (long long)T * nh) return;
-  const int t = (int)(gw / nh), h = (int)(gw % nh);
-  const __nv_bfloat16* src = qkv + (long long)t * ld_in + (long long)h * D;
+  if (gw * R >= (long long)T * nh) return;
+  const int t = (int)(gw * R / nh), h0 = (int)(gw * R % nh);
+  const __nv_bfloat16* src = qkv + (long long)t * ld_in + (long long)h0 * D;
   const int d0 = lane * 2;
-  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(src + d0);
-  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(src + HALF + d0);
-  float x0 = __low2float(a), x1 = __high2float(a), y0 = __low2float(b), y1 = __high2float(b);
+  __nv_bfloat162 a[R], b[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    a[r] = *reinterpret_cast<const __nv_bfloat162*>(src + r * D + d0);
+    b[r] = *reinterpret_cast<const __nv_bfloat162*>(src + r * D + HALF + d0);
+  }
   const long long dst_row = slot ? slot[t] : (long long)t;
-  if (h >= nq + nkv) {  // V: plain copy into the cache / v buffer
-    __nv_bfloat16* dst = v_out + dst_row * ld_kv + (long long)(h - nq - nkv) * D;
-    *reinterpret_cast<__nv_bfloat162*>(dst + d0) = a;
-    *reinterpret_cast<__nv_bfloat162*>(dst + HALF + d0) = b;
-    return;
-  }
-  const bool isq = h < nq;
-  if (use_norm) {
-    float ss = x0 * x0 + x1 * x1 + y0 * y0 + y1 * y1;
-    ss = warp_sum(ss);
-    const float rs = rsqrtf(ss / (float)D + eps);
-    if (lane == 0 && rstd_out) rstd_out[(long long)t * (nq + nkv) + h] = rs;
-    const __nv_bfloat16* nw = isq ? qw : kw;
-    x0 = __bfloat162float(__float2bfloat16(x0 * rs)) * __bfloat162float(nw[d0]);
-    x1 = __bfloat162float(__float2bfloat16(x1 * rs)) * __bfloat162float(nw[d0 + 1]);
-    y0 = __bfloat162float(__float2bfloat16(y0 * rs)) * __bfloat162float(nw[HALF + d0]);
-    y1 = __bfloat162float(__float2bfloat16(y1 * rs)) * __bfloat162float(nw[HALF + d0 + 1]);
-    x0 = __bfloat162float(__float2bfloat16(x0));
-    x1 = __bfloat162float(__float2bfloat16(x1));
-    y0 = __bfloat162float(__float2bfloat16(y0));
-    y1 = __bfloat162float(__float2bfloat16(y1));
-  }
   const int p = pos[t];
-  const float c0 = cos_t[(long long)p * HALF + d0], c1 = cos_t[(long long)p * HALF + d0 + 1];
-  const float s0 = sin_t[(long long)p * HALF + d0], s1 = sin_t[(long long)p * HALF + d0 + 1];
-  const float o0 = x0 * c0 - y0 * s0, o1 = x1 * c1 - y1 * s1;
-  const float p0 = y0 * c0 + x0 * s0, p1 = y1 * c1 + x1 * s1;
-  __nv_bfloat16* dst = isq ? q_out + ((long long)t * nq + h) * D
-                           : k_out + dst_row * ld_kv + (long long)(h - nq) * D;
-  *reinterpret_cast<__nv_bfloat162*>(dst + d0) = __floats2bfloat162_rn(o0, o1);
-  *reinterpret_cast<__nv_bfloat162*>(dst + HALF + d0) = __floats2bfloat162_rn(p0, p1);
+  const float2 cs = *reinterpret_cast<const float2*>(cos_t + (long long)p * HALF + d0);
+  const float2 sn = *reinterpret_cast<const float2*>(sin_t + (long long)p * HALF + d0);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int h = h0 + r;
+    if (h >= nq + nkv) {  // V: plain copy into the cache / v buffer
+      __nv_bfloat16* dst = v_out + dst_row * ld_kv + (long long)(h - nq - nkv) * D;
+      *reinterpret_cast<__nv_bfloat162*>(dst + d0) = a[r];
+      *reinterpret_cast<__nv_bfloat162*>(dst + HALF + d0) = b[r];
+      continue;
+    }
+    float x0 = __low2float(a[r]), x1 = __high2float(a[r]);
+    float y0 = __low2float(b[r]), y1 = __high2float(b[r]);
+    const bool isq = h < nq;
+    if (use_norm) {
+      float ss = x0 * x0 + x1 * x1 + y0 * y0 + y1 * y1;
+      ss = warp_sum(ss);
+      const float rs = rsqrtf(ss / (float)D + eps);
+      if (lane == 0 && rstd_out) rstd_out[(long long)t * (nq + nkv) + h] = rs;
+      const __nv_bfloat16* nw = isq ? qw : kw;
+      x0 = __bfloat162float(__float2bfloat16(x0 * rs)) * __bfloat162float(nw[d0]);
+      x1 = __bfloat162float(__float2bfloat16(x1 * rs)) * __bfloat162float(nw[d0 + 1]);
+      y0 = __bfloat162float(__float2bfloat16(y0 * rs)) * __bfloat162float(nw[HALF + d0]);
+      y1 = __bfloat162float(__float2bfloat16(y1 * rs)) * __bfloat162float(nw[HALF + d0 + 1]);
+      x0 = __bfloat162float(__float2bfloat16(x0));
+      x1 = __bfloat162float(__float2bfloat16(x1));
+      y0 = __bfloat162float(__float2bfloat16(y0));
+      y1 = __bfloat162float(__float2bfloat16(y1));
+    }
+    const float c0 = cs.x, c1 = cs.y, s0 = sn.x, s1 = sn.y;
+    const float o0 = x0 * c0 - y0 * s0, o1 = x1 * c1 - y1 * s1;
+    const float p0 = y0 * c0 + x0 * s0, p1 = y1 * c1 + x1 * s1;
+    __nv_bfloat16* dst = isq ? q_out + ((long long)t * nq + h) * D
+                             : k_out + dst_row * ld_kv + (long long)(h - nq) * D;
+    *reinterpret_cast<__nv_bfloat162*>(dst + d0) = __floats2bfloat162_rn(o0, o1);
+    *reinterpret_cast<__nv_bfloat162*>(dst + HALF + d0) = __floats2bfloat162_rn(p0, p1);
+  }
 }
 
 // Backward of the above for q and k heads; dv is copied through. Produces d(qkv) and per-block
@@ -466,10 +480,14 @@ extern "C" int mb_qk_norm_rope_fwd(const void* qkv, long long ld_in, const void*
                                    long long ld_kv, float* rstd, int T, int nq, int nkv, float eps,
                                    int use_norm, cudaStream_t st) {
   if (T == 0) return 0;
-  const long long warps = (long long)T * (nq + 2 * nkv);
+  const int nh = nq + 2 * nkv;
+  const int R = nh % 4 == 0 ? 4 : nh % 2 == 0 ? 2 : 1;  // heads per warp
+  const long long warps = (long long)T * nh / R;
   const int block = 256;
   const long long grid = (warps + 7) / 8;
-  mb_launch(qk_norm_rope_fwd_kernel, (unsigned)grid, block, 0, st, 
+  auto kern = R == 4 ? qk_norm_rope_fwd_kernel<4> : R == 2 ? qk_norm_rope_fwd_kernel<2>
+                                                            : qk_norm_rope_fwd_kernel<1>;
+  mb_launch(kern, (unsigned)grid, block, 0, st, 
       (const __nv_bfloat16*)qkv, ld_in, (const __nv_bfloat16*)qw, (const __nv_bfloat16*)kw, pos,
       cos_t, sin_t, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out, slot,
       ld_kv, rstd, T, nq, nkv, eps, use_norm);

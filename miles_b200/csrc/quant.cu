@@ -65,6 +65,53 @@ __global__ void fp8_block_cast_kernel(const __nv_bfloat16* __restrict__ x, int M
   }
 }
 
+// Fast path of the 128 x 128 block cast (full blocks, 16-byte aligned rows): thread t of the
+// CTA holds row t / 2, columns (t & 1) * 64 .. +63 of the block in registers (eight 16-byte
+// loads), so the block is read once; same scale and conversion as fp8_block_cast_kernel.
+__global__ void __launch_bounds__(256) fp8_block_cast128_kernel(
+    const __nv_bfloat16* __restrict__ x, int N, __nv_fp8_e4m3* __restrict__ y,
+    float* __restrict__ scale_inv, int ue8m0) {
+  const int br = blockIdx.y, bc = blockIdx.x;
+  const int r = threadIdx.x >> 1, c0 = (threadIdx.x & 1) * 64;
+  const long long base = (long long)(br * 128 + r) * N + bc * 128 + c0;
+  uint4 raw[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) raw[i] = reinterpret_cast<const uint4*>(x + base)[i];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(__bfloat162float(h[j])));
+  }
+  __shared__ float red[8];
+  amax = warp_max(amax);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+  amax = fmaxf(m, 1e-12f);
+  float sc = amax / FP8_MAX;
+  if (ue8m0) sc = ue8m0_round_up(sc);
+  if (threadIdx.x == 0) scale_inv[br * gridDim.x + bc] = sc;
+  const float inv = 1.f / sc;
+  uint4 out[4];
+  uint8_t* ob = reinterpret_cast<uint8_t*>(out);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const __nv_fp8_e4m3 e(fminf(fmaxf(__bfloat162float(h[j]) * inv, -FP8_MAX), FP8_MAX));
+      ob[i * 8 + j] = *reinterpret_cast<const uint8_t*>(&e);
+    }
+  }
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(y) + base);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = out[i];
+}
+
 // 1 x group activation quantization: one warp per (row, group).
 __global__ void fp8_group_cast_kernel(const __nv_bfloat16* __restrict__ x, long long M, int N,
                                       int group, __nv_fp8_e4m3* __restrict__ y,
@@ -196,6 +243,12 @@ extern "C" int mb_fp8_block_cast(const void* x, int M, int N, int bm, int bn, vo
                                  float* scale_inv, int ue8m0, cudaStream_t st) {
   if (M == 0 || N == 0) return 0;
   dim3 grid((N + bn - 1) / bn, (M + bm - 1) / bm);
+  if (bm == 128 && bn == 128 && M % 128 == 0 && N % 128 == 0 &&
+      reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0) {
+    fp8_block_cast128_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, N, (__nv_fp8_e4m3*)y,
+                                                    scale_inv, ue8m0);
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  }
   fp8_block_cast_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, M, N, bm, bn,
                                                (__nv_fp8_e4m3*)y, scale_inv, ue8m0);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
