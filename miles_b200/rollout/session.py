@@ -86,11 +86,24 @@ class Session:
             bad = [m.get("role") for m in request_messages[n:] if m.get("role") not in allowed_roles]
             if bad:
                 raise SessionError(f"appending role(s) {bad} is not allowed (allowed: {sorted(allowed_roles)})")
+        from miles_b200.rollout.tito import IncrementalTokenizer
+
+        tito = IncrementalTokenizer(tok, tools)
         old = _render(tok, self.messages[:n], False, tools)
         new = _render(tok, request_messages, True, tools)
-        if new[:len(old)] != old:
-            raise SessionError("chat template is not prefix-stable for the appended messages")
-        delta = new[len(old):]
+        try:
+            # the generated turn ends where the engine stopped: add what the template renders
+            # after an assistant turn that the generation did not emit (e.g. the newline after
+            # the end-of-turn token)
+            join = tito.junction(head.token_ids)
+            if new[:len(old)] == old:
+                delta = join + new[len(old):]
+            else:
+                # not prefix-stable (e.g. a thinking template dropping earlier reasoning):
+                # tokenize the appended messages incrementally
+                delta = join + tito.suffix(request_messages[n:])
+        except ValueError as e:
+            raise SessionError(str(e)) from e
         return (head.token_ids + delta, head.loss_mask + [0] * len(delta),
                 head.logprobs + [0.0] * len(delta))
 
