@@ -17,7 +17,9 @@ gemm_grouped_decode step on fp8 expert weights), attn_decode256 (256 sequences x
 small_kernels (the memory-bound kernels of a training / decode step on inputs larger than L2, a
 few GB in total: RMSNorm fwd / bwd, QK-norm + RoPE fwd / bwd, SwiGLU fwd / bwd, router fwd / bwd,
 MoE permute plan / gather / combine, LM-head log-prob / entropy, sampler, policy loss, Adam,
-fp8 activation and block quantisation).
+fp8 activation and block quantisation), family_decode (engine decode of 64 sequences on a
+2-layer DeepSeek-V3-width MLA model and the tiny Gated DeltaNet hybrid: the absorbed-MLA and
+GDN decode kernels; plus the fp8 block dequantisation and the RL advantage kernels).
 """
 import sys
 
@@ -108,6 +110,34 @@ elif case == "small_kernels":
         fp8_block_quant(torch.randn(6144, H, device="cuda", dtype=torch.bfloat16))
         del x, qkv, gu, xm, Wv
         torch.cuda.synchronize()
+elif case == "family_decode":
+    import dataclasses
+
+    import numpy as np
+
+    from miles_b200.engine.engine import GenRequest, RolloutEngine
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+    from miles_b200.ops.quant import fp8_block_dequant, fp8_block_quant
+    from miles_b200.ops.rl import gae, grpo_advantages
+    dev = sys.argv[2] if len(sys.argv) > 2 else "cuda"
+    dt = torch.bfloat16 if dev == "cuda" else torch.float32
+    rng = np.random.default_rng(0)
+    for name, layers, ctx in (("dsv3-small", 2, 1024), ("tiny-gdn", None, 512)):
+        cfg = preset(name)
+        if layers:
+            cfg = dataclasses.replace(cfg, num_layers=layers)
+        m = Transformer(cfg, device=dev, dtype=dt, seed=0)
+        eng = RolloutEngine(m, max_batch=64, num_pages=64 * (ctx // 64 + 2), max_pages_per_seq=ctx // 64 + 2,
+                            use_cuda_graph=False)
+        eng.generate([GenRequest(rng.integers(0, cfg.vocab_size, ctx).tolist(), 8, seed=i, rid=i)
+                      for i in range(64)])
+        del eng, m
+    q, sc = fp8_block_quant(torch.randn(6144, 2048, device=dev).to(dt))
+    fp8_block_dequant(q, sc)
+    n = 1 << 16
+    grpo_advantages(torch.rand(4096, device=dev), 8)
+    gae(torch.randn(n, device=dev), torch.randn(n, device=dev), list(range(0, n + 1, 1024)), 1.0, 0.95)
 elif case == "gemm_grouped_decode":
     from miles_b200.ops import gemm as G
     from miles_b200.ops.moe import MoEPlan
