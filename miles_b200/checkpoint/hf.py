@@ -356,6 +356,7 @@ def load_hf_tensors(model: Transformer, tensors: dict[str, torch.Tensor]) -> Non
 def _load(model: Transformer, wmap, get, path: str) -> None:
     cfg = model.cfg
     model._fp8_version = None  # new weights: the fp8 copies (if any) re-quantise on next use
+    model._qat_version = None
 
     targets = dict(to_hf_tensors(model))  # views into model.flat
     missing_mtp: list[str] = []

@@ -224,6 +224,7 @@ def load_checkpoint(load: str, model: Transformer, optimizer=None, load_optim: b
     d = os.path.join(load, f"iter_{it:07d}")
     cfg = model.cfg
     model._fp8_version = None  # new weights: the fp8 copies (if any) re-quantise on next use
+    model._qat_version = None
     sd = {"model": {k: torch.empty_like(v) for k, v in model_state_dict(model).items()}}
     lora = getattr(model, "lora", None)
     if lora is not None:

@@ -337,6 +337,9 @@ class Transformer(torch.nn.Module):
         self.fp8: dict = {}  # name -> Fp8Weight (block-scaled fp8 copies, see enable_fp8)
         self._fp8_version = None
         self.fp8_sync_events = collections.deque(maxlen=256)
+        self.qat: dict = {}  # name -> fake-int4 weight value (int4 quantisation-aware training)
+        self.qat_group = 128
+        self._qat_version = None
         self.lora = None  # miles_b200.models.lora.LoRA when adapters are attached
         self.gdn = None
         if cfg.linear_attn_interval:
@@ -394,6 +397,39 @@ class Transformer(torch.nn.Module):
             self.fp8[name] = w8
         self.sync_fp8(force=True)
 
+    def enable_int4_qat(self, group: int = 128) -> None:
+        """Int4 quantisation-aware training of the routed experts (the reference's
+        OPEN_TRAINING_INT4_FAKE_QAT_FLAG / OPEN_TRAINING_INT4_GROUP_SIZE): the expert GEMMs of
+        training, prefill and decode use the fake-int4 value of each expert weight (symmetric
+        int4 in groups of `group` along K, re-computed whenever the weight version changes),
+        the data-gradient uses it too, and the weight-gradient goes straight through to the bf16
+        weight (straight-through estimator). The rollout engine therefore runs the int4-rounded
+        experts the training forward sees, like an int4 (W4A16) rollout."""
+        if self.fp8:
+            raise ValueError("int4 QAT and block fp8 are exclusive")
+        self.qat_group = group
+        for name, p in self.params.items():
+            if name.endswith(("experts.w1", "experts.w2")):
+                self.qat[name] = torch.empty_like(p.data)
+        self._qat_version = None
+        self.sync_fp8()
+
+    def expert_weight(self, name: str) -> torch.Tensor:
+        """The tensor the expert GEMMs use for parameter `name` (its fake-int4 value under QAT).
+        On the kernel path the fake-int4 copy shares the parameter's gradient buffer, so the
+        weight-gradient GEMM accumulates into it (straight-through); the PyTorch path builds the
+        same estimator with autograd."""
+        p = self.params[name]
+        q = self.qat.get(name)
+        if q is None:
+            return p
+        if not G.use_native(q):
+            return p + (q - p).detach()
+        g = G.main_grad_of(p)
+        if g is not None:
+            G.register_main_grad(q, g)
+        return q
+
     def disable_fp8(self) -> None:
         from miles_b200.ops.fp8 import unregister_fp8
 
@@ -405,6 +441,13 @@ class Transformer(torch.nn.Module):
     def sync_fp8(self, force: bool = False) -> None:
         """Re-quantise the fp8 copies when the bf16 weights changed (new weight version); not
         inside a CUDA graph capture (the captured kernels read the copies in place)."""
+        if self.qat and self._qat_version != self.weight_version and not (
+                self.device.type == "cuda" and torch.cuda.is_current_stream_capturing()):
+            from miles_b200.ops.quant import int4_qat_weight
+
+            for name, q in self.qat.items():
+                int4_qat_weight(self.params[name].data, self.qat_group, out=q)
+            self._qat_version = self.weight_version
         if not self.fp8 or (not force and self._fp8_version == self.weight_version):
             return
         if self.device.type == "cuda" and torch.cuda.is_current_stream_capturing():
@@ -498,8 +541,8 @@ class Transformer(torch.nn.Module):
         zero-filled [T, H] block, so the TP all-reduce that follows completes the output (and
         the backward of the TP copy sums the row gradients)."""
         pre = f"layers.{i}.mlp."
-        args = (self.params[pre + "gate.weight"], self.params[pre + "experts.w1"],
-                self.params[pre + "experts.w2"], self.router_cfgs[i])
+        args = (self.params[pre + "gate.weight"], self.expert_weight(pre + "experts.w1"),
+                self.expert_weight(pre + "experts.w2"), self.router_cfgs[i])
         bias = self.params.get(pre + "gate.e_score_correction_bias")
 
         def run(xr, rp, rec):

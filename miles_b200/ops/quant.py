@@ -101,6 +101,27 @@ def int4_fake_quant(w: torch.Tensor, group: int = 128, sym: bool = True):
     return q, s, z
 
 
+@torch.no_grad()
+def int4_qat_weight(w: torch.Tensor, group: int = 128, out: torch.Tensor | None = None,
+                    rows_per_chunk: int = 1 << 16) -> torch.Tensor:
+    """The value an int4 quantisation-aware-training forward uses for a weight: symmetric int4 in
+    groups of `group` along the last dim, scale = max(|w| over the group / 7, 1e-5) in fp32,
+    q = clamp(round(w / scale), -7, 7), result q * scale in the weight's dtype. Processed in row
+    chunks (bounded fp32 temporaries). Reference: the fake-int4 STE of the grouped expert linear
+    (docker/patch/latest/megatron.patch, _FakeInt4QuantizationSTE)."""
+    K = w.shape[-1]
+    if K % group:
+        raise ValueError(f"int4 QAT needs the input dim ({K}) to be a multiple of {group}")
+    w2 = w.reshape(-1, K)
+    out = out if out is not None else torch.empty_like(w)
+    o2 = out.view(-1, K)
+    for a in range(0, w2.shape[0], rows_per_chunk):
+        g = w2[a:a + rows_per_chunk].float().view(-1, K // group, group)
+        sc = (g.abs().amax(-1, keepdim=True) / 7).clamp_min(1e-5)
+        o2[a:a + rows_per_chunk] = (torch.round(g / sc).clamp(-7, 7) * sc).view(-1, K).to(w.dtype)
+    return out
+
+
 def int4_dequant(q, s, z, group: int = 128, sym: bool = True):
     M, N = q.shape
     qf = q.float().view(M, N // group, group)

@@ -256,6 +256,9 @@ def build_model(args, ctx: ProcessContext) -> Transformer:
         if fmt != "e4m3" or recipe != "blockwise":
             raise ValueError(f"fp8 supports --fp8-format e4m3 --fp8-recipe blockwise (got {fmt} / {recipe})")
         model.enable_fp8()
+    if os.environ.get("OPEN_TRAINING_INT4_FAKE_QAT_FLAG", "0") == "1":
+        # int4 quantisation-aware training of the routed experts (the reference's switch)
+        model.enable_int4_qat(int(os.environ.get("OPEN_TRAINING_INT4_GROUP_SIZE", "128")))
     if getattr(args, "lora_rank", 0):
         from miles_b200.models.lora import LoRA
 
