@@ -59,8 +59,37 @@ class GenResult:
     meta: dict = field(default_factory=dict)
 
 
+@dataclass
+class PrefillHandoff:
+    """A request prefilled by a prefill engine, on its way to a decode engine (prefill / decode
+    disaggregation): the prompt's K/V cache rows of every attention layer, the first sampled
+    token with its log-prob, and the prompt's routing (R3)."""
+    req: GenRequest
+    k: list                       # per attention layer: [P, nkv, head_dim]
+    v: list
+    token: int
+    logprob: float
+    experts: np.ndarray | None = None  # [P, L_moe, k] uint8
+
+    @property
+    def rid(self):
+        return self.req.rid
+
+    @property
+    def prompt(self):
+        return self.req.prompt
+
+    @property
+    def max_new_tokens(self):
+        return self.req.max_new_tokens
+
+    @property
+    def return_routed_experts(self):
+        return self.req.return_routed_experts
+
+
 class _Seq:
-    __slots__ = ("req", "pages", "slot", "done", "reason", "prompt_experts", "order")
+    __slots__ = ("req", "pages", "slot", "done", "reason", "prompt_experts", "order", "handoff")
     _count = 0
 
     def __init__(self, req: GenRequest, pages: list[int]):
@@ -68,6 +97,7 @@ class _Seq:
         self.pages = pages
         _Seq._count += 1
         self.order = _Seq._count  # admission order (the latest admitted is preempted first)
+        self.handoff = None
         self.slot = -1           # sequence slot: row of the device decode state (and GDN state)
         self.done = False
         self.reason = ""
@@ -448,6 +478,10 @@ class RolloutEngine:
                     for sq in new:
                         sq.slot = free_slots.pop()
                         live[sq.slot] = sq
+                    imported = [sq for sq in new if sq.handoff is not None]
+                    if imported:  # prefilled elsewhere: copy in the K/V rows and the state
+                        self._import(imported)
+                    new = [sq for sq in new if sq.handoff is None]
                     # packed prefill in chunks of at most `prefill_tokens` tokens (a longer
                     # prompt goes alone): bounds the activation memory next to the KV cache
                     chunk, ntok = [], 0
@@ -459,8 +493,9 @@ class RolloutEngine:
                             chunk, ntok = [], 0
                         chunk.append(sq)
                         ntok += L
-                    self._prefill(chunk)
-                    n_prefills += 1
+                    if chunk:
+                        self._prefill(chunk)
+                        n_prefills += 1
                 elif not live:
                     raise RuntimeError("KV cache too small for a single request")
             slots = sorted(live)
@@ -592,7 +627,10 @@ class RolloutEngine:
                 need = self._cover(len(r.prompt), 1, r.max_new_tokens)
                 reserve = n_live + len(wave) if (n_live or wave) else 0
             if not rest and len(wave) < room and need + reserve <= len(self.free_pages):
-                wave.append(_Seq(r, [self.free_pages.pop() for _ in range(need)]))
+                sq = _Seq(getattr(r, "req", r), [self.free_pages.pop() for _ in range(need)])
+                if isinstance(r, PrefillHandoff):
+                    sq.handoff = r
+                wave.append(sq)
             else:
                 rest.append(r)  # keep arrival order: no request overtakes an earlier one
         return wave, rest
@@ -632,6 +670,97 @@ class RolloutEngine:
         tok, lp = sample_from_hidden(h.index_select(0, last).contiguous(), self.model.lm_head_weight(),
                                      inv_t, seeds, posn, top_k=topk if kmax else None,
                                      top_p=topp if use_p else None, k_max=kmax)
+        self._set_slots(wave, tok, lp, inv_t, seeds, posn, topk, topp)
+        if rec:
+            ex = torch.stack(rec, 1).to(torch.uint8)  # [T, L_moe, k]
+            for b, s in enumerate(wave):
+                if s.req.return_routed_experts:
+                    ds.out_exp[s.slot, :plen_h[b]] = ex[cu[b]:cu[b + 1]]
+        if nvtx:
+            torch.cuda.nvtx.range_pop()
+
+    def _sampling_params(self, wave: list[_Seq]):
+        dev = self.dev
+        inv_t = torch.tensor([1.0 / s.req.temperature if s.req.temperature > 0 else 0.0 for s in wave],
+                             dtype=torch.float32, device=dev)
+        seeds = torch.tensor([s.req.seed for s in wave], dtype=torch.int64, device=dev)
+        posn = torch.tensor([len(s.req.prompt) for s in wave], dtype=torch.int32, device=dev)
+        topk = torch.tensor([s.req.top_k for s in wave], dtype=torch.int32, device=dev)
+        topp = torch.tensor([float(s.req.top_p) for s in wave], dtype=torch.float32, device=dev)
+        return inv_t, seeds, posn, topk, topp
+
+    def _check_pd(self) -> None:
+        c = self.cfg
+        if c.kv_lora_rank or c.linear_attn_interval:
+            raise ValueError("prefill / decode hand-off supports standard K/V caches only "
+                             "(not MLA latents or Gated DeltaNet states)")
+
+    def _import(self, wave: list[_Seq]) -> None:
+        """Admit sequences prefilled by another engine: their prompt K/V rows are written into
+        this engine's pages and their slots get the state `_prefill` would have set."""
+        self._check_pd()
+        dev, ds, cache = self.dev, self.ds, self.cache
+        for s in wave:
+            h = s.handoff
+            P = len(s.req.prompt)
+            rows = torch.tensor([self._slot(s, p) for p in range(P)], dtype=torch.int64, device=dev)
+            j = 0
+            for i in range(self.cfg.num_layers):
+                cache.k[i].index_copy_(0, rows, h.k[j].to(dev, cache.k[i].dtype))
+                cache.v[i].index_copy_(0, rows, h.v[j].to(dev, cache.v[i].dtype))
+                j += 1
+            if h.experts is not None and s.req.return_routed_experts and ds.out_exp is not None:
+                ds.out_exp[s.slot, :P] = torch.from_numpy(np.asarray(h.experts)).to(dev, torch.uint8)
+        tok = torch.tensor([s.handoff.token for s in wave], dtype=torch.int32, device=dev)
+        lp = torch.tensor([s.handoff.logprob for s in wave], dtype=torch.float32, device=dev)
+        self._set_slots(wave, tok, lp, *self._sampling_params(wave))
+
+    def prefill_handoffs(self, reqs: list[GenRequest]) -> list[PrefillHandoff]:
+        """Prefill role of prefill / decode disaggregation: prefill every request (packed, as
+        many at a time as slots and pages allow), sample its first token and return the
+        hand-offs; this engine keeps nothing. A decode engine continues them with
+        `generate(handoffs)` (the same tokens a single engine would produce)."""
+        self._check_pd()
+        self.resume_memory()
+        ds = self.ds
+        if self.n_moe and any(r.return_routed_experts for r in reqs):
+            ds.ensure_exp()
+        out: dict[int, PrefillHandoff] = {}
+        pending = list(reqs)
+        while pending:
+            new, pending = self._admit(pending, self.max_batch)
+            if not new:
+                raise RuntimeError("KV cache too small for a single request")
+            for j, sq in enumerate(new):
+                sq.slot = j
+            chunk, ntok = [], 0
+            for sq in new:
+                if chunk and ntok + len(sq.req.prompt) > self.prefill_tokens:
+                    self._prefill(chunk)
+                    chunk, ntok = [], 0
+                chunk.append(sq)
+                ntok += len(sq.req.prompt)
+            self._prefill(chunk)
+            for sq in new:
+                P = len(sq.req.prompt)
+                rows = torch.tensor([self._slot(sq, p) for p in range(P)], dtype=torch.int64,
+                                    device=self.dev)
+                k = [self.cache.k[i].index_select(0, rows) for i in range(self.cfg.num_layers)]
+                v = [self.cache.v[i].index_select(0, rows) for i in range(self.cfg.num_layers)]
+                ex = None
+                if sq.req.return_routed_experts and ds.out_exp is not None:
+                    ex = ds.out_exp[sq.slot, :P].clone().cpu().numpy()  # the slot is reused
+                out[sq.req.rid] = PrefillHandoff(sq.req, k, v, int(ds.s_tok[sq.slot]),
+                                                 float(ds.out_lp[sq.slot, 0].detach()), ex)
+                ds.s_done[sq.slot] = 1
+                self.free_pages.extend(sq.pages)
+        return [out[r.rid] for r in reqs]
+
+    def _set_slots(self, wave: list[_Seq], tok, lp, inv_t, seeds, posn, topk, topp) -> None:
+        """Device state of freshly prefilled (or imported) sequences: page-table rows, sampling
+        parameters, the first sampled token and its log-prob, done flags."""
+        dev, ds = self.dev, self.ds
+        sl = torch.tensor([s.slot for s in wave], dtype=torch.int64, device=dev)
         n = len(wave)
         pt = np.zeros((n, self.max_pages_per_seq), np.int32)
         stop = np.full((n, _NSTOP), -1, np.int32)
@@ -659,13 +788,6 @@ class RolloutEngine:
         ds.out_lp[sl, 0] = lp
         first_done = (maxnew <= 1) | (stop_d == tok[:, None]).any(1)
         ds.s_done[sl] = first_done.int()
-        if rec:
-            ex = torch.stack(rec, 1).to(torch.uint8)  # [T, L_moe, k]
-            for b, s in enumerate(wave):
-                if s.req.return_routed_experts:
-                    ds.out_exp[s.slot, :plen_h[b]] = ex[cu[b]:cu[b + 1]]
-        if nvtx:
-            torch.cuda.nvtx.range_pop()
 
     def _result(self, s: _Seq, n: int, reason: str | None = None) -> GenResult:
         ds = self.ds
