@@ -59,6 +59,10 @@ def _truncate_at_stop(res, stops: list[str], tokenizer):
 
 
 class LocalEngineClient:
+    # prefill / decode disaggregation: a miles_b200.rollout.pd.RemotePrefill that prefills the
+    # requests on a paired prefill rank (this engine then only decodes); None: prefill here
+    remote_prefill = None
+
     def __init__(self, engine: RolloutEngine, tokenizer=None, max_wait_s: float = 0.002,
                  max_batch: int | None = None):
         self.engine = engine
@@ -117,6 +121,10 @@ class LocalEngineClient:
             if not batch:
                 continue
             items = [(req, self._deliver(loop, fut)) for req, fut in batch]
+            if self.remote_prefill is not None:
+                # the paired prefill rank computes the prompts; this engine admits the hand-offs
+                hs = await loop.run_in_executor(None, self.remote_prefill.prefill, [r for r, _ in items])
+                items = [(h, cb) for h, (_, cb) in zip(hs, items)]
             if not self.engine.submit(items):
                 self._serve = loop.run_in_executor(None, self._serve_items, items)
 

@@ -65,3 +65,39 @@ def recv_handoffs(src: int, device, group=None) -> list[PrefillHandoff]:
                 off += n
         out.append(PrefillHandoff(req, ks, vs, tok, lp, ex))
     return out
+
+
+_STEP_END = "__step_end__"
+
+
+class RemotePrefill:
+    """Decode-side stub of a paired prefill rank: `prefill(requests)` sends them and returns the
+    hand-offs; `end_step()` tells the prefill rank that this rollout step has no more requests."""
+
+    def __init__(self, peer: int, device, group=None):
+        self.peer, self.device, self.group = peer, torch.device(device), group
+
+    def prefill(self, reqs) -> list[PrefillHandoff]:
+        dev = self.device if self.device.type == "cuda" else None
+        dist.send_object_list([list(reqs)], dst=self.peer, group=self.group, device=dev)
+        return recv_handoffs(self.peer, self.device, self.group)
+
+    def end_step(self) -> None:
+        dev = self.device if self.device.type == "cuda" else None
+        dist.send_object_list([_STEP_END], dst=self.peer, group=self.group, device=dev)
+
+
+def serve_prefill_step(engine, peer: int, group=None) -> int:
+    """Prefill-rank loop of one rollout step: prefill every request batch the paired decode rank
+    sends and return the hand-offs, until it ends the step. Returns the requests served."""
+    dev = engine.dev if engine.dev.type == "cuda" else None
+    served = 0
+    while True:
+        box = [None]
+        dist.recv_object_list(box, src=peer, group=group, device=dev)
+        msg = box[0]
+        if isinstance(msg, str) and msg == _STEP_END:
+            return served
+        hs = engine.prefill_handoffs(msg) if msg else []
+        send_handoffs(hs, peer, group)
+        served += len(hs)

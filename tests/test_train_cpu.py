@@ -75,13 +75,14 @@ def test_train_tp2(tmp_path):
     assert os.path.exists(tmp_path / "hf_2" / "model.safetensors.index.json")
 
 
-def _async_run(tmp_path, extra, port):
+def _async_run(tmp_path, extra, port, rollout_gpus: int = 1):
     _dataset(tmp_path / "d.jsonl")
     env = dict(os.environ, MILES_B200_FORCE_CPU="1", PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={1 + rollout_gpus}",
            "--master-addr", "127.0.0.1", "--master-port", str(port),
            os.path.join(ROOT, "train_async.py"),
-           *_argv(tmp_path, ["--actor-num-gpus-per-node", "1", "--rollout-num-gpus", "1",
+           *_argv(tmp_path, ["--actor-num-gpus-per-node", "1", "--rollout-num-gpus", str(rollout_gpus),
                              "--num-rollout", "3", "--save-interval", "100", *extra])]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=580)
     assert r.returncode == 0, r.stderr[-3000:]
@@ -92,6 +93,18 @@ def _async_run(tmp_path, extra, port):
 def test_train_async_disaggregated(tmp_path):
     """1 trainer + 1 rollout rank: one-step-ahead pipeline with bf16 broadcast refits."""
     _async_run(tmp_path, ["--check-weight-update-equal"], free_port())
+
+
+@pytest.mark.timeout(600)
+def test_train_async_prefill_decode_disaggregation(tmp_path):
+    """1 trainer + 1 prefill rank + 1 decode rank (--prefill-num-servers 1): the decode rank's
+    requests are prefilled on its paired rank and decoded from the hand-offs; both engine ranks
+    take the refits."""
+    r = _async_run(tmp_path, ["--prefill-num-servers", "1", "--check-weight-update-equal"], free_port(),
+                   rollout_gpus=2)
+    served = [int(line.split("prefilled ")[1].split()[0]) for line in r.stdout.splitlines()
+              if "prefilled" in line]
+    assert len(served) == 3 and all(n > 0 for n in served), r.stdout[-2000:]
 
 
 @pytest.mark.timeout(600)

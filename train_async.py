@@ -81,6 +81,7 @@ def _init(args):
 
 
 def _merge(parts: list[dict]) -> dict:
+    parts = [p for p in parts if p is not None]  # prefill ranks contribute no samples
     out: dict = {}
     for p in parts:
         for k, v in p.items():
@@ -158,13 +159,67 @@ def run_trainer(args, ctx, T, train_gloo, refit_group, data_gloo):
     return tracker.history
 
 
+def _pd_roles(args, T: int, R: int):
+    """Prefill / decode disaggregation (--prefill-num-servers K): the first K engine ranks
+    prefill, the other R - K decode; decode rank j is paired with prefill rank j (K = R - K).
+    Returns (prefill ranks, decode ranks) or None."""
+    K = getattr(args, "prefill_num_servers", None) or 0
+    if not K:
+        return None
+    if 2 * K != R:
+        raise ValueError(f"--prefill-num-servers {K}: pairs one prefill rank with one decode rank, "
+                         f"so it must be half of the {R} rollout GPUs")
+    if args.fully_async:
+        raise ValueError("--prefill-num-servers is not supported with --fully-async")
+    eng = list(range(T, T + R))
+    return eng[:K], eng[K:]
+
+
+def run_prefill(args, ctx, T, R, refit_group, data_gloo, pre: list[int], dec: list[int]):
+    """A prefill rank: per rollout step, prefill the requests of its paired decode rank until it
+    ends the step; take part in the refits like every engine rank; contribute no samples."""
+    from miles_b200.rollout.pd import serve_prefill_step
+
+    model = build_model(args, ctx)
+    engine = build_engine(args, model, ctx)
+    peer = dec[pre.index(ctx.rank)]
+    refit = make_refit(model, refit_group, src=0, bucket_bytes=args.update_weight_buffer_size,
+                       mode="fp8" if args.update_weight_quant == "fp8" else "bf16",
+                       transport=args.update_weight_transport)
+    refit.sync()
+    start, N = 0, args.num_rollout
+    for r in range(start, N):
+        if r >= start + 2 and _refit_due(r - 2, args, N, start):
+            refit.sync()
+            if args.check_weight_update_equal:
+                from miles_b200.parallel.refit import verify_weights_equal
+
+                verify_weights_equal(model, refit_group, 0, args.update_weight_quant != "fp8")
+        n = serve_prefill_step(engine, peer)
+        print(f"[prefill rank {ctx.rank}] rollout {r}: prefilled {n} requests for rank {peer}", flush=True)
+        engine.release_memory()
+        dist.gather_object(None, None, dst=0, group=data_gloo)
+    return []
+
+
 def run_engine(args, ctx, T, R, refit_group, data_gloo):
+    roles = _pd_roles(args, T, R)
+    if roles is not None and ctx.rank in roles[0]:
+        return run_prefill(args, ctx, T, R, refit_group, data_gloo, *roles)
     model = build_model(args, ctx)
     engine = build_engine(args, model, ctx)
     tok = load_tokenizer(args)
     client = LocalEngineClient(engine, tok)
     ds_cls = load_function(args.data_source_path)
-    manager = RolloutManager(args, ds_cls(args, tok), client, tok, ctx.rank - T, R)
+    if roles is not None:  # a decode rank: its paired prefill rank computes the prompts
+        from miles_b200.rollout.pd import RemotePrefill
+
+        pre, dec = roles
+        j = dec.index(ctx.rank)
+        client.remote_prefill = RemotePrefill(pre[j], ctx.device)
+        manager = RolloutManager(args, ds_cls(args, tok), client, tok, j, len(dec))
+    else:
+        manager = RolloutManager(args, ds_cls(args, tok), client, tok, ctx.rank - T, R)
     refit = make_refit(model, refit_group, src=0, bucket_bytes=args.update_weight_buffer_size,
                        mode="fp8" if args.update_weight_quant == "fp8" else "bf16",
                        transport=args.update_weight_transport)
@@ -191,6 +246,8 @@ def run_engine(args, ctx, T, R, refit_group, data_gloo):
                 worker.resume()
         if worker is None:
             data = manager.generate(r)
+            if client.remote_prefill is not None:
+                client.remote_prefill.end_step()
         else:
             groups = worker.get_batch(manager._local_args().rollout_batch_size)
             data = manager.convert_samples_to_train_data(groups)
