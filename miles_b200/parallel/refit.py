@@ -56,6 +56,8 @@ class WeightRefit:
     def _broadcast_fp8(self, is_src: bool):
         sent = 0
         dev = self.model.flat.device
+        fp8 = getattr(self.model, "fp8", {}) or {}
+        self._filled = set()
         for s in self.model.specs:
             p = self.model.params[s.name].data
             if p.dim() == 2 and p.shape[0] >= 128 and p.shape[1] >= 128:
@@ -77,6 +79,13 @@ class WeightRefit:
             sent += q.numel() + sc.numel() * 4
             if not is_src:
                 w.copy_(fp8_block_dequant(q, sc, dtype=w.dtype))
+                w8 = fp8.get(s.name)
+                if w8 is not None and tuple(w8.q.shape) == (M, N):
+                    # an engine serving block fp8: keep the trainer's e4m3 values and scales as
+                    # they are (no dequantise / re-quantise round trip)
+                    w8.q.copy_(q.view(torch.uint8))
+                    w8.s.copy_(sc)
+                    self._filled.add(s.name)
         return sent
 
     # ------------------------------------------------------------------ API
@@ -106,6 +115,9 @@ class WeightRefit:
             dt = time.perf_counter() - t0
         if not is_src:
             self.model.weight_version = int(ver.item())
+            fp8 = getattr(self.model, "fp8", {}) or {}
+            if self.mode == "fp8" and fp8 and set(fp8) <= getattr(self, "_filled", set()):
+                self.model._fp8_version = self.model.weight_version  # copies already current
         self.last_stats = {"perf/update_weights_time": dt, "update_weights/bytes": nbytes,
                            "update_weights/GBps": nbytes / dt / 1e9 if dt > 0 else 0.0}
         return self.last_stats
@@ -293,6 +305,9 @@ class PeerRefit:
         nbytes = int(nb)
         if not is_src:
             self.model.weight_version = int(ver.item())
+            fp8 = getattr(self.model, "fp8", {}) or {}
+            if self.mode == "fp8" and fp8 and set(fp8) <= getattr(self, "_filled", set()):
+                self.model._fp8_version = self.model.weight_version  # copies already current
         self.last_stats = {"perf/update_weights_time": dt, "update_weights/bytes": nbytes,
                            "update_weights/GBps": nbytes / dt / 1e9 if dt > 0 else 0.0}
         return self.last_stats
