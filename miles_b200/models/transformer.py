@@ -633,6 +633,8 @@ class Transformer(torch.nn.Module):
                                    self.rope_cos, self.rope_sin, self.nq, self.nkv, cfg.rms_eps, cfg.qk_norm)
             o = varlen_attention(q, k, v, meta)
             a = self._row_rs(o.reshape(xf.shape[0], -1), pre + "o_proj.weight")
+        # GLM-4 sandwich norms act row by row: on this rank's rows after the reduce-scatter
+        a = self._sw(i, "post_self_attn_layernorm", a)
         x2, r = add_rms_norm(a, r, self.params[f"layers.{i}.post_attention_layernorm.weight"], cfg.rms_eps)
         x2f = sp_gather(x2, tp)
         if i in self.router_cfgs:
@@ -640,7 +642,7 @@ class Transformer(torch.nn.Module):
         else:
             pm = f"layers.{i}.mlp."
             m = self._row_rs(self._lin_swiglu(x2f, pm + "gate_up_proj.weight"), pm + "down_proj.weight")
-        return m, r
+        return self._sw(i, "post_mlp_layernorm", m), r
 
     def _row_rs(self, a: torch.Tensor, name: str) -> torch.Tensor:
         if self.lora is not None and name in self.lora:
@@ -651,8 +653,8 @@ class Transformer(torch.nn.Module):
         from miles_b200.ops.attention import VarlenMeta
 
         cfg, tp = self.cfg, self.tp
-        if self.gdn is not None or cfg.sandwich_norm:
-            raise NotImplementedError("sequence parallelism with linear-attention layers or sandwich norms")
+        if self.gdn is not None:
+            raise NotImplementedError("sequence parallelism with linear-attention layers")
         T = tokens.shape[0]
         pad = (-T) % tp.size
         if pad:

@@ -247,7 +247,8 @@ def tp_partial_param_names(model) -> list[str]:
     out = []
     # under SP these see only this rank's rows: the norms, and MLA's replicated down projections
     sp_norms = ("input_layernorm.weight", "post_attention_layernorm.weight", "q_a_proj.weight",
-                "q_a_layernorm.weight", "kv_a_proj_with_mqa.weight", "kv_a_layernorm.weight")
+                "q_a_layernorm.weight", "kv_a_proj_with_mqa.weight", "kv_a_layernorm.weight",
+                "post_self_attn_layernorm.weight", "post_mlp_layernorm.weight")
     for name in model.params:
         if name.endswith(("self_attn.q_norm.weight", "self_attn.k_norm.weight", "linear_attn.norm.weight")):
             out.append(name)

@@ -67,7 +67,7 @@ def _run(rank, world, port, preset_name, ckpt, out_dir):
         grads[name] = gr
     # sequence parallel: same forward, same gradients (37 rows: exercises the padding)
     sp = {}
-    if not cfg.linear_attn_interval and not cfg.sandwich_norm:  # no SP for these
+    if not cfg.linear_attn_interval:  # no SP for Gated DeltaNet layers
         for p in m.params.values():
             p.grad = None
         m.sequence_parallel = True
