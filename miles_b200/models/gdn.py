@@ -87,11 +87,12 @@ class GDN:
     def _p(self, i, name):
         return self.m.params[f"layers.{i}.linear_attn.{name}"]
 
-    def _project(self, i, x):
+    def _project(self, i, x, tp_copy: bool = True):
         from miles_b200.parallel.tp import copy_to_tp
 
         nk, nv, dk, dv = self.nk, self.nv, self.dk, self.dv
-        x = copy_to_tp(x, self.m.tp)
+        if tp_copy:  # (under sequence parallelism the row all-gather's backward reduces instead)
+            x = copy_to_tp(x, self.m.tp)
         qkvz = self.m._lin(x, f"layers.{i}.linear_attn.in_proj_qkvz.weight").float()
         mixed, z = qkvz.split([2 * nk * dk + nv * dv, nv * dv], -1)
         ba = self.m._lin(x, f"layers.{i}.linear_attn.in_proj_ba.weight").float()
@@ -163,7 +164,7 @@ class GDN:
                 "hjd,hjv->hdv", kc * torch.exp(last[:, None] - gam)[:, :, None], u)
         return torch.cat(outs, 0), S
 
-    def _out(self, i, o, z, dtype, pending: bool = False):
+    def _out(self, i, o, z, dtype, pending: bool = False, scatter: bool = False):
         """Gated norm + out_proj (row parallel under TP): reduced, or (pending) what the
         caller's residual add + norm reduces."""
         from miles_b200.parallel.tp import reduce_from_tp
@@ -174,6 +175,8 @@ class GDN:
         o, name = o.reshape(T, -1).to(dtype), f"layers.{i}.linear_attn.out_proj.weight"
         if pending:
             return self.m._pending_out(o, name)
+        if scatter:  # sequence parallel: reduce-scatter the rows instead of all-reducing them
+            return self.m._row_rs(o, name)
         return reduce_from_tp(self.m._lin(o, name), self.m.tp)
 
     def _zero_states(self, device):
@@ -182,11 +185,19 @@ class GDN:
                 torch.zeros(nv, dk, dv, dtype=torch.float32, device=device))
 
     # ------------------------------------------------------------------ training / prefill
+    def attn_sp(self, i: int, x: torch.Tensor, meta) -> torch.Tensor:
+        """Sequence parallel: x holds this TP rank's rows; the recurrence runs on the
+        all-gathered rows (whole sequences, this rank's heads) and out_proj ends in a
+        reduce-scatter back to the rank's rows."""
+        from miles_b200.parallel.tp import sp_gather
+
+        return self.attn(i, sp_gather(x, self.m.tp), meta, _sp=True)
+
     def attn(self, i: int, x: torch.Tensor, meta, cache=None, state_rows=None,
-             pending: bool = False) -> torch.Tensor:
+             pending: bool = False, _sp: bool = False) -> torch.Tensor:
         """Packed sequences from zero states; with `cache` the final states of sequence b are
         written to row state_rows[b]."""
-        mixed, z, beta, g = self._project(i, x)
+        mixed, z, beta, g = self._project(i, x, tp_copy=not _sp)
         outs = []
         cu = meta.cu_list
         for b in range(len(cu) - 1):
@@ -203,7 +214,7 @@ class GDN:
                 cache.lin_conv[i][row].copy_(cst)
                 cache.lin_state[i][row].copy_(S)
         o = torch.cat(outs, 0)
-        return self._out(i, o, z, x.dtype, pending)
+        return self._out(i, o, z, x.dtype, pending, scatter=_sp)
 
     # ------------------------------------------------------------------ decode
     def decode(self, i: int, x: torch.Tensor, cache, state_rows: torch.Tensor,

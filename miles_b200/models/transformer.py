@@ -621,7 +621,9 @@ class Transformer(torch.nn.Module):
         else:
             x, r = add_rms_norm(m_prev, r_prev, ln1, cfg.rms_eps)
         pre = f"layers.{i}.self_attn."
-        if self.mla is not None:  # latents gathered instead of the hidden rows (models/mla.py)
+        if self.gdn is not None and cfg.layer_is_linear(i):  # Gated DeltaNet (models/gdn.py)
+            a = self.gdn.attn_sp(i, x, meta)
+        elif self.mla is not None:  # latents gathered instead of the hidden rows (models/mla.py)
             a = self.mla.attn_sp(i, x, meta)
         elif self.gattn is not None:  # separate q / k / v (models/qwen3_next.py)
             a = self.gattn.attn_sp(i, x, meta)
@@ -653,8 +655,6 @@ class Transformer(torch.nn.Module):
         from miles_b200.ops.attention import VarlenMeta
 
         cfg, tp = self.cfg, self.tp
-        if self.gdn is not None:
-            raise NotImplementedError("sequence parallelism with linear-attention layers")
         T = tokens.shape[0]
         pad = (-T) % tp.size
         if pad:

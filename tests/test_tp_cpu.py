@@ -67,7 +67,7 @@ def _run(rank, world, port, preset_name, ckpt, out_dir):
         grads[name] = gr
     # sequence parallel: same forward, same gradients (37 rows: exercises the padding)
     sp = {}
-    if not cfg.linear_attn_interval:  # no SP for Gated DeltaNet layers
+    if True:  # sequence parallel for every family
         for p in m.params.values():
             p.grad = None
         m.sequence_parallel = True
