@@ -257,8 +257,6 @@ class Transformer(torch.nn.Module):
             self.cp = CPContext(cp_group)
             if self.cp.size == 1:
                 self.cp = None
-            elif self.tp is not None and cfg.linear_attn_interval:
-                raise ValueError("linear-attention (Gated DeltaNet) layers run without TP")
             elif (cfg.num_kv_heads // self.tp_size) % self.cp.size:
                 raise ValueError(f"{cfg.num_kv_heads // self.tp_size} KV heads per TP rank do not "
                                  f"split over CP {self.cp.size}")

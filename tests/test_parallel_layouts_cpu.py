@@ -1,5 +1,6 @@
 """Model-parallel layouts on CPU (gloo): EP alone, TP x EP with TP-split experts, TP x EP and TP
-alone with whole experts (expert-tensor-parallel size 1), TP x CP. Each layout's groups come from
+alone with whole experts (expert-tensor-parallel size 1), TP x CP (also for MLA / DSA and the
+Gated DeltaNet hybrid). Each layout's groups come from
 `init_distributed`; one actor step over data-parallel shards of a batch, then `save_hf`, gives
 the same HF tensors as one process stepping on the whole batch; the gradient norm is the
 global one on every rank."""
@@ -27,6 +28,8 @@ def _cfg(variant="moe"):
         return dataclasses.replace(base, attention_bias=True, partial_rotary_factor=0.5)
     if variant == "mla":
         return preset("tiny-dsa")
+    if variant == "gdn":  # Gated DeltaNet hybrid: states handed over along each TP rank's CP group
+        return dataclasses.replace(preset("tiny-gdn"), num_heads=8, num_kv_heads=4)
     return base
 
 
@@ -91,6 +94,7 @@ def _run(rank, world, port, layout, ckpt, out, variant):
     ((2, 1, None, 2), 4, 29695),     # TP2 x CP2
     ((2, 1, None, 2, "biased"), 4, 29696),   # TP2 x CP2, separate biased q / k / v
     ((2, 1, None, 2, "mla"), 4, 29698),      # TP2 x CP2, MLA + DSA
+    ((2, 1, None, 2, "gdn"), 4, 29699),      # TP2 x CP2, Gated DeltaNet hybrid
 ])
 def test_layouts_match_single(tmp_path, layout, world, port):
     from safetensors import safe_open
@@ -107,7 +111,10 @@ def test_layouts_match_single(tmp_path, layout, world, port):
     save_hf(m, ckpt)
     a = Actor(m, _actor_cfg())
     met = a.train_step(_items(cfg))
-    ref = {k: v.detach().clone() for k, v in to_hf_tensors(m)}
+    from miles_b200.checkpoint.hf import to_hf_layout
+
+    # compared in the saved (HF) layout: zero-centred norms and the conv weight differ from ours
+    ref = {k: to_hf_layout(cfg, k, v.detach()).clone() for k, v in to_hf_tensors(m)}
     out = str(tmp_path / "out")
     mp.spawn(_run, args=(world, free_port(), layout, ckpt, out, variant), nprocs=world, join=True)
     import json
