@@ -6,7 +6,9 @@ Endpoints (request / response shapes follow the SGLang server the reference driv
   GET  /health, /health_generate, /model_info, /get_weight_version
   POST /flush_cache, /abort_request, /pause_generation {mode}, /continue_generation,
        /release_memory_occupation {tags}, /resume_memory_occupation {tags},
-       /update_weight_version {new_version}, /start_profile, /stop_profile, /shutdown
+       /update_weight_version {new_version}, /start_profile, /stop_profile, /shutdown,
+       /load_lora_adapter {lora_path}, /unload_lora_adapter, /weights_checker {action},
+       /simulate_crash
 
 Reference: backends/sglang_utils/sglang_engine.py (server launch :55-108, control RPCs
 :111-587), sglang.patch (pause modes, weight version, routed experts).
@@ -124,6 +126,57 @@ def build_app(engine: RolloutEngine, tokenizer=None):
             os.makedirs(d, exist_ok=True)
             p.export_chrome_trace(os.path.join(d, "trace.json"))
             state["profiler"] = None
+        return {"success": True}
+
+    @app.post("/load_lora_adapter")
+    async def load_lora(req: Request):
+        """Load adapter tensors saved by `LoRA.save` into the engine's attached adapters."""
+        body = await req.json()
+        lora = getattr(engine.model, "lora", None)
+        if lora is None:
+            return JSONResponse({"success": False, "message": "the engine has no LoRA adapters"}, 400)
+        lora.load(body["lora_path"])
+        return {"success": True}
+
+    @app.post("/unload_lora_adapter")
+    async def unload_lora(req: Request):
+        """Serve the base weights: the adapters' B matrices are zeroed (reload with
+        /load_lora_adapter)."""
+        import torch
+
+        lora = getattr(engine.model, "lora", None)
+        if lora is None:
+            return JSONResponse({"success": False, "message": "the engine has no LoRA adapters"}, 400)
+        with torch.no_grad():
+            for b in lora.B.values():
+                b.zero_()
+        return {"success": True}
+
+    @app.post("/weights_checker")
+    async def weights_checker(req: Request):
+        """action "snapshot": remember a checksum of the weights; "compare": report whether the
+        weights still match the snapshot; "checksum": return the current checksum (the bf16 bit
+        patterns summed as integers, so equal bits give equal sums)."""
+        import torch
+
+        body = await req.json() if (await req.body()) else {}
+        flat = engine.model.flat
+        csum = int(flat.view(torch.int16).to(torch.int64).sum().item()) if flat.element_size() == 2 else \
+            int(flat.view(torch.int32).to(torch.int64).sum().item())
+        action = body.get("action", "checksum")
+        out = {"success": True, "checksum": csum, "weight_version": str(engine.model.weight_version)}
+        if action == "snapshot":
+            state["weights_snapshot"] = csum
+        elif action == "compare":
+            snap = state.get("weights_snapshot")
+            out["equal"] = snap is not None and snap == csum
+        return out
+
+    @app.post("/simulate_crash")
+    async def simulate_crash():
+        """Fault injection on the host: the engine is marked dead (health checks fail, generate
+        raises) without touching the GPU, so the recovery path can be exercised."""
+        engine.dead = True
         return {"success": True}
 
     @app.post("/shutdown")
