@@ -337,15 +337,44 @@ def _old_logp_from_forward(args) -> bool:
             and getattr(args, "train_backend", "b200") != "fsdp")
 
 
+def sglang_engine_kwargs(sg: dict) -> dict:
+    """RolloutEngine arguments from the forwarded `--sglang-*` flags that have a counterpart in
+    this engine (SGLang server argument names): mem_fraction_static -> KV pool share,
+    max_running_requests -> batch slots, chunked_prefill_size -> packed-prefill token budget,
+    disable_cuda_graph -> no decode graphs, context_length -> longest sequence,
+    num_continuous_decode_steps -> decode steps per host visit. Other SGLang flags (kernels,
+    schedulers and servers this engine does not have) are accepted and ignored."""
+
+    def flag(v):
+        return v in (True, "true", "True", "1", 1, None, "")
+
+    out = {}
+    if "mem_fraction_static" in sg:
+        out["mem_fraction"] = float(sg["mem_fraction_static"])
+    if "max_running_requests" in sg:
+        out["max_batch"] = int(sg["max_running_requests"])
+    if "chunked_prefill_size" in sg and int(sg["chunked_prefill_size"]) > 0:
+        out["prefill_tokens"] = int(sg["chunked_prefill_size"])
+    if "disable_cuda_graph" in sg and flag(sg["disable_cuda_graph"]):
+        out["use_cuda_graph"] = False
+    if "context_length" in sg:
+        out["context_length"] = int(sg["context_length"])
+    if "num_continuous_decode_steps" in sg:
+        out["steps_per_sync"] = int(sg["num_continuous_decode_steps"])
+    return out
+
+
 def build_engine(args, model: Transformer, ctx: ProcessContext) -> RolloutEngine:
-    mem = float(args.sglang_args.get("mem_fraction_static", 0.85)) if hasattr(args, "sglang_args") else 0.85
+    sg = sglang_engine_kwargs(getattr(args, "sglang_args", {}) or {})
     max_len = (args.rollout_max_prompt_len or 1024) + (args.rollout_max_response_len or 1024)
     if args.rollout_max_context_len:
         max_len = max(max_len, args.rollout_max_context_len)
-    return RolloutEngine(model, max_batch=args.rollout_max_batch,
-                         num_pages=None if ctx.device.type == "cuda" else 4096,
-                         mem_fraction=mem, use_cuda_graph=not args.no_cuda_graph,
-                         max_pages_per_seq=(max_len + 63) // 64 + 1)
+    max_len = max(max_len, sg.pop("context_length", 0))
+    kw = dict(max_batch=args.rollout_max_batch, mem_fraction=0.85,
+              use_cuda_graph=not args.no_cuda_graph)
+    kw.update(sg)
+    return RolloutEngine(model, num_pages=None if ctx.device.type == "cuda" else 4096,
+                         max_pages_per_seq=(max_len + 63) // 64 + 1, **kw)
 
 
 def build_critic(args, ctx: ProcessContext):

@@ -78,3 +78,15 @@ def test_dynamic_filter():
     assert not check_reward_nonzero_std(a, g).keep
     g[1].reward = 0.0
     assert check_reward_nonzero_std(a, g).keep
+
+
+def test_sglang_flags_reach_the_engine():
+    from miles_b200.orchestration.setup import sglang_engine_kwargs
+
+    kw = sglang_engine_kwargs({"mem_fraction_static": "0.7", "max_running_requests": "96",
+                               "chunked_prefill_size": "8192", "disable_cuda_graph": None,
+                               "context_length": "32768", "num_continuous_decode_steps": "4",
+                               "attention_backend": "fa3"})
+    assert kw == {"mem_fraction": 0.7, "max_batch": 96, "prefill_tokens": 8192,
+                  "use_cuda_graph": False, "context_length": 32768, "steps_per_sync": 4}
+    assert sglang_engine_kwargs({"chunked_prefill_size": "-1"}) == {}
