@@ -272,6 +272,9 @@ def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> No
         ep_first = 0 in dist.get_process_group_ranks(ep.group)  # the EP group rank 0 is in
     for name, t in to_hf_tensors(model):
         tpc = model_tp(model, name)
+        internal = name[len("model."):] if name.startswith("model.") else name
+        if internal in getattr(model, "fp32", {}):  # fp32-pinned: export the fp32 value
+            t = model.fp32[internal]
         t = tp_gather_for(model, name, t.detach())
         if name in skip:
             continue
@@ -380,6 +383,9 @@ def _load(model: Transformer, wmap, get, path: str) -> None:
             raise KeyError(f"{name} missing from {path}")
         src = from_hf_layout(cfg, name, get(src_name))
         dst.copy_(tp_slice_for(model, name, src).to(dst.dtype))
+        internal = name[len("model."):] if name.startswith("model.") else name
+        if internal in getattr(model, "fp32", {}):  # keep the checkpoint's full precision
+            model.set_fp32_value(internal, tp_slice_for(model, name, src))
     if missing_mtp:
         warnings.warn(f"{path} has no multi-token prediction weights ({len(missing_mtp)} tensors, "
                       f"e.g. {missing_mtp[0]}); keeping the initialised MTP layers")

@@ -98,7 +98,9 @@ class GDN:
         ba = self.m._lin(x, f"layers.{i}.linear_attn.in_proj_ba.weight").float()
         b, a = ba.split([nv, nv], -1)
         beta = torch.sigmoid(b)
-        g = -torch.exp(self._p(i, "A_log").float()) * F.softplus(a + self._p(i, "dt_bias").float())
+        pin = self.m.pinned_param
+        g = -torch.exp(pin(f"layers.{i}.linear_attn.A_log").float()) * F.softplus(
+            a + pin(f"layers.{i}.linear_attn.dt_bias").float())
         return mixed, z, beta, g
 
     def _conv(self, i, mixed, state):

@@ -335,6 +335,12 @@ class Transformer(torch.nn.Module):
         self.fp8: dict = {}  # name -> Fp8Weight (block-scaled fp8 copies, see enable_fp8)
         self._fp8_version = None
         self.fp8_sync_events = collections.deque(maxlen=256)
+        # fp32 pinning (the reference's mark_param_dtype): parameters whose runtime value stays
+        # fp32 although the flat buffer is bf16 (see pinned_param)
+        self.fp32 = {n: p.detach().float().clone() for n, p in self.params.items()
+                     if n.endswith(self.FP32_PINNED)}
+        self._fp32_snap = {n: p.detach().clone() for n, p in self.params.items() if n in self.fp32}
+        self._fp32_version = self.weight_version
         self.qat: dict = {}  # name -> fake-int4 weight value (int4 quantisation-aware training)
         self.qat_group = 128
         self._qat_version = None
@@ -366,6 +372,44 @@ class Transformer(torch.nn.Module):
         if self.lora is not None and name in self.lora:
             return swiglu(self._lin(x, name))
         return G.linear_swiglu(x, self.params[name])
+
+    # -------------------------------------------------------------------------------- fp32 pinning
+    FP32_PINNED = ("mlp.gate.e_score_correction_bias", "linear_attn.A_log", "linear_attn.dt_bias")
+
+    def pinned_param(self, name: str):
+        """The runtime value of parameter `name`: for the fp32-pinned parameters (the router's
+        expert-score bias, Gated DeltaNet's A_log / dt_bias) the fp32 copy, which keeps what a
+        checkpoint stored in fp32; gradients still reach the bf16 parameter (straight through)."""
+        p = self.params.get(name)
+        f = self.fp32.get(name)
+        if p is None or f is None:
+            return p
+        if torch.is_grad_enabled() and p.requires_grad:
+            return f + (p - p.detach()).float()
+        return f
+
+    @torch.no_grad()
+    def _sync_fp32(self) -> None:
+        """After a weight update (new version) a pinned parameter whose bf16 value changed takes
+        that value; unchanged ones keep their fp32 value. Not inside a CUDA graph capture."""
+        if not self.fp32 or self._fp32_version == self.weight_version:
+            return
+        if self.device.type == "cuda" and torch.cuda.is_current_stream_capturing():
+            return
+        for n, f in self.fp32.items():
+            p = self.params[n].data
+            if not torch.equal(p, self._fp32_snap[n]):
+                f.copy_(p.float())
+                self._fp32_snap[n].copy_(p)
+        self._fp32_version = self.weight_version
+
+    @torch.no_grad()
+    def set_fp32_value(self, name: str, value: torch.Tensor) -> None:
+        """Load a full-precision value for a pinned parameter (checkpoint loaders)."""
+        if name in self.fp32:
+            self.fp32[name].copy_(value.float())
+            self.params[name].data.copy_(value.to(self.params[name].dtype))
+            self._fp32_snap[name].copy_(self.params[name].data)
 
     # -------------------------------------------------------------------------------- fp8
     FP8_SUFFIXES = ("qkv_proj.weight", "o_proj.weight", "gate_up_proj.weight", "down_proj.weight",
@@ -438,7 +482,9 @@ class Transformer(torch.nn.Module):
     @torch.no_grad()
     def sync_fp8(self, force: bool = False) -> None:
         """Re-quantise the fp8 copies when the bf16 weights changed (new weight version); not
-        inside a CUDA graph capture (the captured kernels read the copies in place)."""
+        inside a CUDA graph capture (the captured kernels read the copies in place). Also
+        refreshes the int4-QAT values and the fp32-pinned parameters."""
+        self._sync_fp32()
         if self.qat and self._qat_version != self.weight_version and not (
                 self.device.type == "cuda" and torch.cuda.is_current_stream_capturing()):
             from miles_b200.ops.quant import int4_qat_weight
@@ -541,7 +587,7 @@ class Transformer(torch.nn.Module):
         pre = f"layers.{i}.mlp."
         args = (self.params[pre + "gate.weight"], self.expert_weight(pre + "experts.w1"),
                 self.expert_weight(pre + "experts.w2"), self.router_cfgs[i])
-        bias = self.params.get(pre + "gate.e_score_correction_bias")
+        bias = self.pinned_param(pre + "gate.e_score_correction_bias")
 
         def run(xr, rp, rec):
             if self.ep is not None:
