@@ -304,7 +304,9 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                       micro_batch_size=args.micro_batch_size,
                       log_probs_max_tokens_per_gpu=args.log_probs_max_tokens_per_gpu,
                       memory_margin_bytes=args.train_memory_margin_bytes,
-                      old_logp_from_forward=_old_logp_from_forward(args))
+                      old_logp_from_forward=_old_logp_from_forward(args),
+                      offload_optimizer=bool(getattr(args, "offload_train", False)
+                                             and getattr(args, "colocate", False)))
     if getattr(args, "train_backend", "b200") == "fsdp":
         # HF model under FSDP2 (trainer/fsdp_actor.py); `model` is then the engine's Transformer,
         # refreshed from the gathered HF state after every step

@@ -86,6 +86,9 @@ class ActorConfig:
     lr_schedule: "LRSchedule | None" = None   # None: constant `lr`
     tis_args: object = None   # namespace handed to a custom TIS function (e.g. MIS settings)
     memory_margin_bytes: int = 0   # device memory kept free when placing the optimizer state
+    # colocated: park device-placed optimizer state in pinned host memory while rolling out
+    # (released with the gradients, back before the optimizer step)
+    offload_optimizer: bool = False
 
 
 def pack_microbatches(lengths: list[int], max_tokens: int) -> list[list[int]]:
@@ -229,6 +232,8 @@ class Actor:
         self.grad_flat = None
         if self.opt is not None:
             self.opt.g = None
+            if self.cfg.offload_optimizer and hasattr(self.opt, "offload"):
+                self.opt.offload()
         if self.dev.type == "cuda":
             torch.cuda.empty_cache()
 

@@ -126,9 +126,53 @@ class FlatAdam:
             for dst, src in zip(parts, gathered):
                 dst.copy_(src)
 
+    # ------------------------------------------------------------------ offload
+    @torch.no_grad()
+    def offload(self, force: bool = False) -> None:
+        """Move device-placed state (fp32 master, m, v) into pinned host buffers and free the
+        device copies: colocated training gives that memory to the rollout's KV cache (the
+        reference's torch_memory_saver offload of the optimizer). The next step() brings it
+        back first. `force` also runs the copy for CPU state (tests)."""
+        if self.placement != "device" or getattr(self, "_parked", None) is not None:
+            return
+        if self.m.device.type != "cuda" and not force:
+            return
+        pin = self.m.device.type == "cuda"
+        keep = {}
+        for k in ("master", "m", "v"):
+            t = getattr(self, k)
+            if t is None:
+                continue
+            buf = getattr(self, "_pinned", {}).get(k)
+            if buf is None or buf.shape != t.shape:
+                buf = torch.empty(t.shape, dtype=t.dtype, pin_memory=pin)
+            buf.copy_(t, non_blocking=pin)
+            keep[k] = buf
+        if pin:
+            torch.cuda.current_stream(self.m.device).synchronize()
+        self._dev = self.m.device
+        self._pinned = keep
+        self._parked = keep
+        for k in keep:
+            setattr(self, k, None)
+        if pin:
+            torch.cuda.empty_cache()
+
+    @torch.no_grad()
+    def onload(self) -> None:
+        """Bring offloaded state back to the device (no-op when it is there)."""
+        parked = getattr(self, "_parked", None)
+        if parked is None:
+            return
+        pin = self._dev.type == "cuda"
+        for k, buf in parked.items():
+            setattr(self, k, buf.to(self._dev, non_blocking=pin) if pin else buf.clone())
+        self._parked = None
+
     # ------------------------------------------------------------------ step
     @torch.no_grad()
     def step(self) -> None:
+        self.onload()
         self.step_id += 1
         if self.world > 1:
             self._reduce_scatter_grads()
@@ -204,6 +248,7 @@ class FlatAdam:
 
     def reset_state(self) -> None:
         """--reset-optimizer-states: zero the moments and the step count (master copy kept)."""
+        self.onload()
         for b in getattr(self, "_pinning", ()):
             b.wait()
         self.step_id = 0
@@ -211,10 +256,12 @@ class FlatAdam:
         self.v.zero_()
 
     def state_dict(self) -> dict:
+        self.onload()
         return {"step": self.step_id, "m": self.m, "v": self.v, "master": self.master,
                 "placement": self.placement, "shard": (self.rank, self.world)}
 
     def load_state_dict(self, sd: dict) -> None:
+        self.onload()
         self.step_id = sd["step"]
         self.m.copy_(sd["m"])
         self.v.copy_(sd["v"])
