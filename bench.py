@@ -20,6 +20,8 @@ Timing: W untimed warm-up steps, then K steps bracketed by barrier + synchronize
 with CUDA events; the max over ranks is reported. Inputs are larger than L2 every step (the
 model itself is ~61 GB). `e2e` times the same public API call (ColocatedRL.step) on the host
 clock, including the host->device copy of the prompts and the device->host read of the result.
+A run that would outlast `--time-limit` (wall clock from process start) times fewer steps than
+asked and reports both counts (`steps`, `steps_requested`, `stopped_early`).
 """
 from __future__ import annotations
 
@@ -33,6 +35,8 @@ import threading
 import time
 
 import numpy as np
+
+T_START = time.perf_counter()
 
 
 def parse():
@@ -55,6 +59,11 @@ def parse():
     ap.add_argument("--over-sampling", type=int, default=4,
                     help="groups in flight per trained group under partial rollout")
     ap.add_argument("--steps-per-sync", type=int, default=8)
+    ap.add_argument("--time-limit", type=float, default=None,
+                    help="wall-clock seconds (from process start) the whole run must fit in: the "
+                         "timed loop ends early, and says so in the JSON line (steps = the steps "
+                         "actually timed, steps_requested = K), when one more step would not fit. "
+                         "Default 1700 s at one GPU, 820 s per run at several; 0 disables")
     ap.add_argument("--fp8", type=int, default=1,
                     help="1: unified block-scaled fp8 (e4m3, 1x128 activation / 128x128 weight "
                          "scales) forward GEMMs in rollout and training (the headline config); "
@@ -238,7 +247,20 @@ def main():
     t_host0 = time.perf_counter()
     ev0.record()
     h2d = d2h = 0
+    limit = args.time_limit if args.time_limit is not None else (1700.0 if world == 1 else 820.0)
+    done, slowest, t_prev = 0, 0.0, time.perf_counter()
     for _ in range(args.steps):
+        if done and limit > 0:
+            # one more step must fit (with 15 % slack on the slowest so far); every rank
+            # decides the same way (max over ranks)
+            now = time.perf_counter()
+            slowest = max(slowest, now - t_prev)
+            t_prev = now
+            over = torch.tensor([float(now - T_START + 1.15 * slowest > limit)], device=dev)
+            if world > 1:
+                dist.all_reduce(over, op=dist.ReduceOp.MAX)
+            if over.item() > 0:
+                break
         prompts, lens, rewards = workload()
         # host -> device: this step's prompt ids from pinned memory; device -> host inside the
         # step: generated tokens / log-probs / routing and the step's metrics
@@ -251,13 +273,14 @@ def main():
         rollout_s += m["perf/rollout_time"]
         lp_s += m["perf/log_probs_time"]
         train_s += m["perf/actor_train_time"]
+        done += 1
     ev1.record()
     barrier()
     t_host = time.perf_counter() - t_host0
     clocks = sampler.stop()
     launches = _lib.launch_count() - n0
-    ms = ev0.elapsed_time(ev1) / args.steps
-    vals = torch.tensor([ms, t_host / args.steps * 1e3, rollout_s, lp_s, train_s,
+    ms = ev0.elapsed_time(ev1) / done
+    vals = torch.tensor([ms, t_host / done * 1e3, rollout_s, lp_s, train_s,
                          float(tokens), float(resp)], dtype=torch.float64, device=dev)
     if world > 1:
         mx = vals[:5].clone()
@@ -265,18 +288,21 @@ def main():
         sm = vals[5:].clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         vals = torch.cat([mx, sm])
-    sync_s = sum(a.elapsed_time(b) for a, b in model.fp8_sync_events) / 1e3 / args.steps
+    sync_s = sum(a.elapsed_time(b) for a, b in model.fp8_sync_events) / 1e3 / done
     ms, host_ms, rollout_s, lp_s, train_s, tokens, resp = vals.tolist()
     step_s = ms / 1e3
-    value = tokens / args.steps / step_s
+    value = tokens / done / step_s
     if rank == 0:
-        h2d = h2d // args.steps * world
-        d2h = d2h // args.steps * world
+        h2d = h2d // done * world
+        d2h = d2h // done * world
         out = {
             "metric": METRIC,
             "value": value,
             "unit": "tokens/s (GRPO step throughput: prompt+response tokens rolled out and trained per second, whole job)",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "n_gpus": world, "steps": done, "warmup": args.warmup,
+            **({"steps_requested": args.steps,
+                "stopped_early": f"time limit {limit:.0f} s (--time-limit): {args.steps} steps "
+                                 f"would not fit; {done} timed"} if done < args.steps else {}),
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
             "dtype": ("fp8-block (e4m3 forward GEMMs: 1x128 activation / 128x128 weight scales, "
@@ -296,16 +322,16 @@ def main():
                                    if args.partial_rollout else {"partial_rollout": False}),
                        "l2": "inputs larger than L2 (61 GB of weights streamed every step)"},
             "grpo_step_s": step_s,
-            "rollout_tok_s": resp / args.steps / (rollout_s / args.steps),
-            "rollout_s": rollout_s / args.steps, "log_probs_s": lp_s / args.steps,
-            "train_s": train_s / args.steps, "weight_sync_s": sync_s,
+            "rollout_tok_s": resp / done / (rollout_s / done),
+            "rollout_s": rollout_s / done, "log_probs_s": lp_s / done,
+            "train_s": train_s / done, "weight_sync_s": sync_s,
             "weight_sync_note": ("colocated engine shares the trainer's parameter buffer; with fp8 the "
                                  "refit is the in-place 128x128 block re-quantisation of every GEMM "
                                  "weight after the optimizer step (device-timed)" if args.fp8 else
                                  "colocated engine shares the trainer's parameter buffer: refit is a "
                                  "weight-version bump"),
             "clocks": clocks,
-            "e2e": {"value": tokens / (host_ms / 1e3 * args.steps), "unit": "tokens/s",
+            "e2e": {"value": tokens / (host_ms / 1e3 * done), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "train_rollout_logprob_abs_diff": rl.last_metrics.get("train/train_rollout_logprob_abs_diff"),
