@@ -183,6 +183,11 @@ int mb_symm_allreduce(const long long* flag_ptrs, const long long* stage_ptrs, i
                       float eps, void* out, void* h_out, float* rstd, long long timeout_ns,
                       int* err, cudaStream_t st);
 int mb_symm_copy(const void* src, void* dst, long long bytes, cudaStream_t st);
+// Fused gradient reduce-scatter + cast/scale + squared norm over peer memory: out[0, n) =
+// bf16(scale * sum_r g_r[lo, lo + n)), *sq_out = sum of the squares of out. n, lo multiples of 8,
+// pointers 16-byte aligned, partial >= 592 floats, counter one zeroed int.
+int mb_grad_rs(const long long* g_ptrs, int world, long long lo, long long n, float scale,
+               void* out, float* partial, int* counter, float* sq_out, cudaStream_t st);
 int mb_fp8_block_dequant(const void* q, const float* s, int M, int N, int bm, int bn, void* out,
                          cudaStream_t st);
 int mb_gemm_bf16_peer(const void* a, long long a_rows, long long a_cols, long long lda, bool a_mn,

@@ -512,6 +512,20 @@ int64_t symm_copy_ptr(int64_t src_ptr, int64_t dst_ptr, int64_t bytes) {
   return mb_symm_copy(reinterpret_cast<void*>(src_ptr), reinterpret_cast<void*>(dst_ptr), bytes,
                       cur_stream());
 }
+// Fused gradient reduce-scatter over peer memory (symm.cu grad_rs_kernel).
+int64_t grad_rs(std::vector<int64_t> g_ptrs, int64_t lo, int64_t n, double scale, torch::Tensor out,
+                torch::Tensor partial, torch::Tensor counter, torch::Tensor sq) {
+  CHECK_DT(out, at::kBFloat16);
+  CHECK_DT(partial, at::kFloat);
+  CHECK_DT(counter, at::kInt);
+  CHECK_DT(sq, at::kFloat);
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() >= n, "grad_rs: out");
+  TORCH_CHECK(partial.is_cuda() && partial.numel() >= 148 * 4, "grad_rs: partial needs 592 floats");
+  TORCH_CHECK(counter.is_cuda() && counter.numel() >= 1 && sq.is_cuda() && sq.numel() >= 1);
+  TORCH_CHECK(!g_ptrs.empty() && g_ptrs.size() <= 8, "grad_rs: 1..8 ranks");
+  return mb_grad_rs((const long long*)g_ptrs.data(), (int)g_ptrs.size(), lo, n, (float)scale,
+                    P(out), PT<float>(partial), PT<int>(counter), PT<float>(sq), cur_stream());
+}
 // Refit: quantise a local bf16 weight into (possibly peer) fp8 + scale buffers, and dequantise
 // from (possibly peer) buffers into a local bf16 weight.
 int64_t fp8_block_cast_ptr(torch::Tensor x, int64_t bm, int64_t bn, int64_t y_ptr, int64_t s_ptr,
@@ -734,6 +748,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_collective", &symm_collective);
   m.def("symm_copy", &symm_copy);
   m.def("symm_copy_ptr", &symm_copy_ptr);
+  m.def("grad_rs", &grad_rs);
   m.def("fp8_block_cast_ptr", &fp8_block_cast_ptr);
   m.def("fp8_block_dequant_ptr", &fp8_block_dequant_ptr);
   m.def("gemm_peer", &gemm_peer, "tcgen05 GEMM storing its tiles into peer staging areas");

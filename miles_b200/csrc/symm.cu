@@ -361,6 +361,72 @@ __global__ void fp8_block_dequant_kernel(const uint8_t* q, const float* s, int M
   }
 }
 
+// Gradient reduce-scatter fused with the cast / scale and the squared norm of the result: this
+// rank's shard [lo, lo + 8 * n8) of the flat bf16 gradient is summed over every rank's copy,
+// read straight from the peers' memory (rank order, fp32, one rounding: bitwise the same on
+// every run), scaled, rounded to bf16 and stored in place into this rank's own copy (a range no
+// peer reads); the squared norm of the stored values goes to *sq_out (per-CTA partials reduced
+// in CTA order by the last CTA: deterministic). All loads of a chunk are issued before the
+// accumulation, so `world` 16-byte loads per thread are in flight. The caller orders the call
+// after every rank's backward (a barrier) and keeps its own gradient buffer unchanged until
+// every rank's call has finished (the parameter all-gather that follows).
+__global__ void __launch_bounds__(256) grad_rs_kernel(Peers g, long long lo, long long n8,
+                                                      float scale, int world, __nv_bfloat16* out,
+                                                      float* partial, int* counter, float* sq_out) {
+  pdl_trigger();
+  pdl_wait();
+  float sq = 0.f;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+       i += (long long)gridDim.x * blockDim.x) {
+    uint4 v[kMaxPeers];
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+      if (r < world) v[r] = ld_volatile_v4(reinterpret_cast<const __nv_bfloat16*>(g.p[r]) + lo + i * 8);
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+      if (r < world) {
+        const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&v[r]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] += __bfloat162float(vb[k]);
+      }
+    }
+    uint4 o;
+    __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      ob[k] = __float2bfloat16(acc[k] * scale);
+      const float f = __bfloat162float(ob[k]);
+      sq += f * f;
+    }
+    *reinterpret_cast<uint4*>(out + i * 8) = o;
+  }
+  // CTA sum in a fixed tree, then the last CTA adds the partials in CTA order
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, d);
+  __shared__ float ws[8];
+  __shared__ int last;
+  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += ws[w];
+    partial[blockIdx.x] = t;
+    __threadfence();
+    last = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    float t = 0.f;
+    for (int b = 0; b < (int)gridDim.x; ++b) t += *reinterpret_cast<volatile float*>(partial + b);
+    *sq_out = t;
+    *counter = 0;
+  }
+}
+
 }  // namespace mb
 
 using namespace mb;
@@ -550,6 +616,23 @@ int mb_fp8_block_dequant(const void* q, const float* s, int M, int N, int bm, in
   if (g > 148 * 8) g = 148 * 8;
   mb_launch(fp8_block_dequant_kernel, (int)g, 256, 0, st, (const uint8_t*)q, s, M, N, bm, bn,
             (__nv_bfloat16*)out);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// Fused gradient reduce-scatter (grad_rs_kernel). g_ptrs: every rank's flat gradient base
+// (this rank's own at index rank); out = this rank's base + lo. partial: >= 148 * 4 floats.
+int mb_grad_rs(const long long* g_ptrs, int world, long long lo, long long n, float scale,
+               void* out, float* partial, int* counter, float* sq_out, cudaStream_t st) {
+  if (world < 1 || world > kMaxPeers || n % 8 || lo % 8) return -1;
+  for (int r = 0; r < world; ++r)
+    if (g_ptrs[r] % 16) return -1;
+  if (reinterpret_cast<uintptr_t>(out) % 16) return -1;
+  const long long n8 = n / 8;
+  long long grid = (n8 + 255) / 256;
+  if (grid > 148 * 4) grid = 148 * 4;
+  if (grid < 1) grid = 1;
+  mb_launch(grad_rs_kernel, (int)grid, 256, 0, st, to_peers(g_ptrs, world), lo, n8, scale, world,
+            (__nv_bfloat16*)out, partial, counter, sq_out);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

@@ -305,6 +305,7 @@ def build_actor(args, model: Transformer, ctx: ProcessContext) -> Actor:
                       log_probs_max_tokens_per_gpu=args.log_probs_max_tokens_per_gpu,
                       memory_margin_bytes=args.train_memory_margin_bytes,
                       old_logp_from_forward=_old_logp_from_forward(args),
+                      grad_reduce=getattr(args, "grad_reduce", "nccl"),
                       offload_optimizer=bool(getattr(args, "offload_train", False)
                                              and getattr(args, "colocate", False)))
     if getattr(args, "train_backend", "b200") == "fsdp":

@@ -115,6 +115,52 @@ class PeerTensor:
         self._bases = []
 
 
+class PeerGradBuffer:
+    """The flat bf16 gradient buffer of a data-parallel group in symmetric memory, and the fused
+    reduce-scatter over it (csrc/symm.cu grad_rs_kernel): each rank reads its shard of every
+    peer's gradient straight over NVLink, sums in rank order in fp32, scales, rounds to bf16
+    into its own copy and produces the shard's squared norm, in one kernel. The buffer is
+    allocated once (cudaMalloc + IPC handles exchanged once) and stays resident, so a step
+    pays no handle exchange.
+
+    Replaces the NCCL reduce-scatter of Megatron's distributed optimizer (reference:
+    megatron_utils/model.py:537-612) for the DP gradient."""
+
+    def __init__(self, numel: int, group=None, device: torch.device | None = None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("PeerGradBuffer supports up to 8 ranks (one NVSwitch domain)")
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.numel = numel
+        self.buf = SymmBuffer(max(16, (numel * 2 + 15) // 16 * 16), group, self.device)
+        self.tensor = self.buf.view(0, (numel,), torch.bfloat16)
+        self.partial = torch.zeros(148 * 4, dtype=torch.float32, device=self.device)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._token = torch.zeros(1, dtype=torch.float32, device=self.device)
+
+    def reduce_scatter(self, lo: int, n: int, sq: torch.Tensor, scale: float = 1.0) -> None:
+        """tensor[lo, lo + n) = bf16(scale * sum over ranks), sq[0] = its squared norm. Every
+        rank's backward must be complete before any rank reads: a one-element all-reduce on
+        the stream orders the kernel after every rank's earlier work. The caller must not
+        write the buffer again before every rank's call has finished (the optimizer's
+        parameter all-gather that follows is such a point)."""
+        if lo % 8 or n % 8:
+            raise ValueError(f"fused gradient reduce-scatter needs 8-aligned shards (lo={lo}, n={n})")
+        if self.world > 1:
+            dist.all_reduce(self._token, group=self.group)
+        rc = lib().grad_rs(self.buf.peers, lo, n, scale, self.tensor[lo:lo + n], self.partial,
+                           self.counter, sq)
+        if rc != 0:
+            raise RuntimeError(f"grad_rs launch failed ({rc})")
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self.buf.close()
+
+
 class SymmComm:
     def __init__(self, group=None, hidden: int = 4096, cap_rows: int = 256,
                  device: torch.device | None = None, timeout_s: float = 2.0):

@@ -89,6 +89,9 @@ class ActorConfig:
     # colocated: park device-placed optimizer state in pinned host memory while rolling out
     # (released with the gradients, back before the optimizer step)
     offload_optimizer: bool = False
+    # DP gradient reduce-scatter: "nccl", or "peer" (fused kernel over a resident symmetric
+    # gradient buffer; sharded bf16 gradients on CUDA)
+    grad_reduce: str = "nccl"
 
 
 def pack_microbatches(lengths: list[int], max_tokens: int) -> list[list[int]]:
@@ -141,6 +144,7 @@ class Actor:
         self._custom_loss = None
         self._custom_tis = None
         self._pg_reducer = None
+        self._peer_grads = None
         self._host_state = self._prefetch_host_state()
 
     # ------------------------------------------------------------------ memory
@@ -156,8 +160,16 @@ class Actor:
                                          self.cfg.weight_decay, self.cfg.clip_grad, self.dp_group)
             return
         if self.grad_flat is None:
-            self.grad_flat = torch.zeros(self.model.flat.numel(), dtype=self.cfg.grad_dtype,
-                                         device=self.dev)
+            n = self.model.flat.numel()
+            if self._use_peer_grads():
+                if self._peer_grads is None:
+                    from miles_b200.parallel.symm import PeerGradBuffer
+
+                    self._peer_grads = PeerGradBuffer(n, self.dp_group, self.dev)
+                self.grad_flat = self._peer_grads.tensor
+                self.grad_flat.zero_()
+            else:
+                self.grad_flat = torch.zeros(n, dtype=self.cfg.grad_dtype, device=self.dev)
             for s in self.model.specs:
                 g = self.grad_flat[s.offset:s.offset + s.numel].view(s.shape)
                 self.model.params[s.name].main_grad = g
@@ -172,6 +184,7 @@ class Actor:
                                 host_state=self._host_state,
                                 memory_margin=self.cfg.memory_margin_bytes,
                                 dp_group=self.dp_group if self._sharded() else None,
+                                peer_grads=self._peer_grads,
                                 **self._norm_scope())
 
     def _prefetch_host_state(self):
@@ -215,6 +228,10 @@ class Actor:
                 ex.append((sp.offset, sp.offset + sp.numel))
             return {"norm_group": m.pp.group, "norm_exclude": ex}
         return {}
+
+    def _use_peer_grads(self) -> bool:
+        return (self.cfg.grad_reduce == "peer" and self._sharded() and self.dev.type == "cuda"
+                and self.cfg.grad_dtype == torch.bfloat16)
 
     def _sharded(self) -> bool:
         """Optimizer sharded over the data-parallel group (ZeRO-1): every rank holds the whole

@@ -42,20 +42,24 @@ class FlatAdam:
                  betas=(0.9, 0.98), eps: float = 1e-8, weight_decay: float = 0.0,
                  clip_grad: float = 1.0, placement: str = "auto", chunk: int = 1 << 28,
                  seed: int = 1234, dp_group=None, norm_group=None, norm_exclude=None,
-                 expert_norm=None, host_state=None, memory_margin: int = 0):
+                 expert_norm=None, host_state=None, memory_margin: int = 0, peer_grads=None):
         """norm_group / norm_exclude: under model parallelism (TP, PP) every rank runs its own
         optimizer over its part of the model; the gradient norm sums the squares over
         `norm_group`, leaving out this rank's flat ranges `norm_exclude` (parameters another
         rank of the group already counts: TP-replicated ones on TP ranks > 0, the last pipeline
         stage's copy of tied embeddings). expert_norm = (offset, groups): under expert
         parallelism the flat tail from `offset` (this rank's experts) is summed over each of
-        `groups` in turn (TP when experts are TP-split, then EP) instead of `norm_group`."""
+        `groups` in turn (TP when experts are TP-split, then EP) instead of `norm_group`.
+        peer_grads: a `parallel.symm.PeerGradBuffer` whose tensor is `grads_flat`; the gradient
+        reduce-scatter then runs as the fused peer-memory kernel (sum, cast and shard norm in one
+        pass) instead of NCCL."""
         self.p = params_flat
         self.expert_norm = expert_norm
         self.norm_group = norm_group
         self.norm_world = dist.get_world_size(norm_group) if norm_group is not None else 1
         self.norm_exclude = list(norm_exclude or [])
         self.g = grads_flat
+        self.peer_grads = peer_grads
         self.lr = lr
         self.betas = betas
         self.eps = eps
@@ -108,12 +112,20 @@ class FlatAdam:
         return self.sq.sqrt()
 
     # ------------------------------------------------------------------ collectives
-    def _reduce_scatter_grads(self) -> None:
+    def _reduce_scatter_grads(self) -> bool:
+        """Reduce-scatter the gradient into this rank's shard; True when the fused peer kernel
+        ran (it also leaves the shard's squared norm in self.sq)."""
+        pg = self.peer_grads
+        if (pg is not None and self.g.data_ptr() == pg.tensor.data_ptr()
+                and self.lo % 8 == 0 and self.shard % 8 == 0):
+            pg.reduce_scatter(self.lo, self.shard, self.sq)
+            return True
         mine = self.g[self.lo:self.lo + self.shard]
         if _is_nccl(self.group):
             dist.reduce_scatter_tensor(mine, self.g, group=self.group)  # in place
         else:  # gloo has no reduce-scatter: sum everything, keep the shard
             dist.all_reduce(self.g, group=self.group)
+        return False
 
     def _all_gather_params(self) -> None:
         mine = self.p[self.lo:self.lo + self.shard]
@@ -174,13 +186,13 @@ class FlatAdam:
     def step(self) -> None:
         self.onload()
         self.step_id += 1
-        if self.world > 1:
-            self._reduce_scatter_grads()
+        fused = self._reduce_scatter_grads() if self.world > 1 else False
         lo, hi = self.lo, self.lo + self.shard
         p, g = self.p[lo:hi], self.g[lo:hi]
-        self.sq.zero_()
         self.skip.zero_()
-        sqnorm_(g, self.sq)
+        if not fused:
+            self.sq.zero_()
+            sqnorm_(g, self.sq)
         if self.norm_world > 1 and self.norm_exclude:
             sq_x = torch.zeros_like(self.sq)
             for a, b in self.norm_exclude:

@@ -146,6 +146,10 @@ def add_rollout_args(p):
     g.add_argument("--update-weight-transport", choices=["auto", "peer", "nccl"], default="auto",
                    help="trainer -> engine refit: kernels storing into the engines' IPC-mapped "
                         "staging over NVLink (peer), or NCCL broadcast")
+    g.add_argument("--grad-reduce", choices=["nccl", "peer"], default="nccl",
+                   help="data-parallel gradient reduce-scatter: NCCL, or the fused peer-memory "
+                        "kernel (sum + cast + shard norm in one pass over a resident symmetric "
+                        "gradient buffer; the buffer is not released during rollout)")
     g.add_argument("--fp8-format", choices=["e4m3", "hybrid"], default=None,
                    help="block-scaled fp8 forward GEMMs in training and rollout (e4m3 only)")
     g.add_argument("--fp8-recipe", choices=["blockwise", "mxfp8", "delayed", "tensorwise"],
