@@ -100,6 +100,13 @@ int mb_fa_bwd(const void* q, const void* k, const void* v, const void* dout, con
               float softmax_scale, int* err, cudaStream_t st);
 int mb_logprob_fwd(const float* logits, long long ld, const int* target, int n, int V,
                    float inv_temp, float* logp, float* ent, float* lse, cudaStream_t st);
+// Vocabulary-parallel log-prob: per-slice softmax statistics part [4][n] = {m, s, sz, target
+// logit or 0} of logits [n, V] holding vocabulary ids [lo, lo + V); then the rank-order combine of
+// `world` parts [world][4][n] into logp / ent / lse.
+int mb_logprob_part(const float* logits, long long ld, const int* target, int lo, int n, int V,
+                    float inv_temp, float* part, cudaStream_t st);
+int mb_logprob_combine(const float* parts, int world, int n, float* logp, float* ent, float* lse,
+                       cudaStream_t st);
 int mb_logprob_bwd(const float* logits, long long ld, const int* target, int n, int V,
                    float inv_temp, const float* lse, const float* g_lp, const float* g_ent,
                    const float* ent, void* dlogits, long long ldd, cudaStream_t st);

@@ -342,6 +342,29 @@ int64_t logprob_fwd(torch::Tensor logits, torch::Tensor target, double inv_temp,
                           logits.size(1), (float)inv_temp, PT<float>(logp), PT<float>(ent),
                           PT<float>(lse), cur_stream());
 }
+int64_t logprob_part(torch::Tensor logits, torch::Tensor target, int64_t lo, double inv_temp,
+                     torch::Tensor part) {
+  CHECK_DT(logits, at::kFloat); TORCH_CHECK(logits.stride(-1) == 1);
+  CHECK_DT(target, at::kInt); CHECK_DT(part, at::kFloat);
+  const int64_t n = logits.size(0);
+  TORCH_CHECK(target.is_contiguous() && target.numel() >= n, "logprob_part: target");
+  TORCH_CHECK(part.is_contiguous() && part.numel() >= 4 * n, "logprob_part: part needs [4, n]");
+  return mb_logprob_part(PT<float>(logits), logits.stride(0), PT<int>(target), lo, n,
+                         logits.size(1), (float)inv_temp, PT<float>(part), cur_stream());
+}
+int64_t logprob_combine(torch::Tensor parts, int64_t world, OT logp, OT ent, OT lse) {
+  CHECK_DT(parts, at::kFloat);
+  TORCH_CHECK(parts.is_contiguous() && world >= 1 && parts.numel() % (4 * world) == 0,
+              "logprob_combine: parts must be [world, 4, n]");
+  const int64_t n = parts.numel() / (4 * world);
+  for (const OT* o : {&logp, &ent, &lse})
+    if (o->has_value()) {
+      CHECK_DT(o->value(), at::kFloat);
+      TORCH_CHECK(o->value().is_contiguous() && o->value().numel() >= n, "logprob_combine: output");
+    }
+  return mb_logprob_combine(PT<float>(parts), world, n, PT<float>(logp), PT<float>(ent),
+                            PT<float>(lse), cur_stream());
+}
 int64_t logprob_bwd(torch::Tensor logits, torch::Tensor target, double inv_temp, torch::Tensor lse,
                  OT g_lp, OT g_ent, OT ent, torch::Tensor dlogits) {
   return mb_logprob_bwd(PT<float>(logits), logits.stride(0), PT<int>(target), logits.size(0),
@@ -782,6 +805,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &attn_bwd);
   m.def("logprob_fwd", &logprob_fwd);
   m.def("logprob_bwd", &logprob_bwd);
+  m.def("logprob_part", &logprob_part);
+  m.def("logprob_combine", &logprob_combine);
   m.def("sample", &sample);
   m.def("policy_loss", &policy_loss);
   m.def("gae", &gae);

@@ -77,6 +77,50 @@ __global__ void __launch_bounds__(LS_THREADS) logprob_fwd_kernel(
   }
 }
 
+// Vocabulary-parallel log-prob, part 1: the softmax statistics of this rank's vocabulary slice
+// [lo, lo + V) of every row (row_stats, the same reduction as logprob_fwd_kernel) and the
+// target's scaled logit when the target falls in the slice (0 otherwise).
+// part = [4][n]: {m, s, sz, tz}. The ranks' parts are then exchanged and combined.
+__global__ void __launch_bounds__(LS_THREADS) logprob_part_kernel(
+    const float* __restrict__ logits, long long ld, const int* __restrict__ target, int lo, int V,
+    float inv_temp, float* __restrict__ part, int n) {
+  pdl_trigger();
+  pdl_wait();
+  const long long r = blockIdx.x;
+  const float* z = logits + r * ld;
+  const SoftStats st = row_stats(z, V, inv_temp);
+  if (threadIdx.x == 0) {
+    const int t = target[r] - lo;
+    part[r] = st.m;
+    part[n + r] = st.s;
+    part[2LL * n + r] = st.sz;
+    part[3LL * n + r] = (t >= 0 && t < V) ? z[t] * inv_temp : 0.f;
+  }
+}
+
+// Part 2: combine the parts of `world` slices ([world][4][n], in rank order, the same order on
+// every rank, so every rank gets the same bits) into lse, the target log-prob and the entropy.
+// With one slice this reproduces logprob_fwd_kernel exactly.
+__global__ void logprob_combine_kernel(const float* __restrict__ parts, int world, int n,
+                                       float* __restrict__ logp, float* __restrict__ ent,
+                                       float* __restrict__ lse) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  SoftStats a{-INFINITY, 0.f, 0.f};
+  float tz = 0.f;
+  for (int w = 0; w < world; ++w) {
+    const float* p = parts + (long long)w * 4 * n;
+    a = combine(a, SoftStats{p[r], p[n + r], p[2LL * n + r]});
+    tz += p[3LL * n + r];
+  }
+  const float l = a.m + logf(a.s);
+  if (lse) lse[r] = l;
+  if (logp) logp[r] = tz - l;
+  if (ent) ent[r] = l - a.sz / a.s;
+}
+
 // dz_i = inv_temp * [ g_lp (1[i==t] - p_i) - g_ent p_i (z'_i - E_p z') ]  (bf16 output)
 __global__ void __launch_bounds__(LS_THREADS) logprob_bwd_kernel(
     const float* __restrict__ logits, long long ld, const int* __restrict__ target, int V,
@@ -439,6 +483,21 @@ extern "C" int mb_logprob_fwd(const float* logits, long long ld, const int* targ
                               float inv_temp, float* logp, float* ent, float* lse, cudaStream_t st) {
   if (n == 0) return 0;
   mb_launch(logprob_fwd_kernel, n, LS_THREADS, 0, st, logits, ld, target, V, inv_temp, logp, ent, lse);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+extern "C" int mb_logprob_part(const float* logits, long long ld, const int* target, int lo, int n,
+                               int V, float inv_temp, float* part, cudaStream_t st) {
+  if (n == 0) return 0;
+  mb_launch(logprob_part_kernel, n, LS_THREADS, 0, st, logits, ld, target, lo, V, inv_temp, part, n);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+extern "C" int mb_logprob_combine(const float* parts, int world, int n, float* logp, float* ent,
+                                  float* lse, cudaStream_t st) {
+  if (n == 0) return 0;
+  if (world < 1) return -1;
+  mb_launch(logprob_combine_kernel, (n + 255) / 256, 256, 0, st, parts, world, n, logp, ent, lse);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

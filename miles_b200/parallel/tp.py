@@ -29,6 +29,8 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
+from miles_b200.ops._lib import use_native
+
 
 class TPContext:
     def __init__(self, group, backend: str = "auto", hidden: int = 0, cap_rows: int = 16384):
@@ -438,6 +440,11 @@ class _VocabParallelLogProb(torch.autograd.Function):
         ent = torch.empty_like(lp)
         lse = torch.empty_like(lp)
         Wl = W[lo:hi]
+        ctx.save_for_backward(h, W, targets, lse, ent)
+        ctx.cfg = (inv_temp, lo, hi, chunk)
+        if use_native(h):
+            _vp_logprob_fwd(h, Wl, targets, inv_temp, tp, lo, chunk, lp, ent, lse)
+            return lp, ent
         for s in range(0, n, chunk):
             e = min(n, s + chunk)
             z = G.matmul_nt(h[s:e].contiguous(), Wl, out_dtype=torch.float32) * inv_temp
@@ -456,8 +463,6 @@ class _VocabParallelLogProb(torch.autograd.Function):
             lse[s:e] = l
             lp[s:e] = red[1] - l
             ent[s:e] = l - red[2] / red[0]
-        ctx.save_for_backward(h, W, targets, lse, ent)
-        ctx.cfg = (inv_temp, lo, hi, chunk)
         return lp, ent
 
     @staticmethod
@@ -468,6 +473,10 @@ class _VocabParallelLogProb(torch.autograd.Function):
         inv_temp, lo, hi, chunk = ctx.cfg
         n = h.shape[0]
         Wl = W[lo:hi]
+        if use_native(h):
+            dh, dW = _vp_logprob_bwd(h, W, targets, inv_temp, lo, hi, chunk, lse, ent, g_lp, g_ent,
+                                     ctx.needs_input_grad[1])
+            return dh, dW, None, None, None, None, None, None
         dh = torch.empty(h.shape, dtype=torch.float32, device=h.device)
         dW = torch.zeros(W.shape, dtype=torch.float32, device=h.device) if ctx.needs_input_grad[1] else None
         for s in range(0, n, chunk):
@@ -490,6 +499,66 @@ class _VocabParallelLogProb(torch.autograd.Function):
             if dW is not None:
                 dW[lo:hi] += dz.t() @ hs.float()
         return dh.to(h.dtype), (dW.to(W.dtype) if dW is not None else None), None, None, None, None, None, None
+
+
+def _vp_logprob_fwd(h, Wl, targets, inv_temp, tp, lo, chunk, lp, ent, lse):
+    """Kernel path of the vocabulary-parallel forward, per row chunk: the tcgen05 GEMM writes this
+    rank's fp32 logit slice, one kernel reduces it to the slice's softmax statistics
+    {max, sum exp, sum exp * z, target logit} (csrc/rl_ops.cu logprob_part_kernel), ONE
+    all-gather exchanges those 4 floats per row, and a second kernel combines the ranks' parts in
+    rank order into lse / log-prob / entropy (logprob_combine_kernel: every rank gets the same
+    bits; with one rank it is exactly the single-GPU log-prob kernel)."""
+    from miles_b200.ops import gemm as G
+    from miles_b200.ops._lib import lib
+
+    n = h.shape[0]
+    V = Wl.shape[0]
+    world = tp.size
+    cs = min(chunk, max(n, 1))
+    zbuf = torch.empty(cs, V, dtype=torch.float32, device=h.device)
+    part = torch.empty(4, cs, dtype=torch.float32, device=h.device)
+    parts = torch.empty(world, 4, cs, dtype=torch.float32, device=h.device)
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        k = e - s
+        z = zbuf[:k]
+        G.matmul_nt(h[s:e].contiguous(), Wl, out=z)
+        pk = part[:, :k] if k == cs else torch.empty(4, k, dtype=torch.float32, device=h.device)
+        lib().logprob_part(z, targets[s:e], lo, inv_temp, pk)
+        pa = parts if k == cs else torch.empty(world, 4, k, dtype=torch.float32, device=h.device)
+        dist.all_gather_into_tensor(pa, pk, group=tp.group)
+        lib().logprob_combine(pa, world, lp[s:e], ent[s:e], lse[s:e])
+
+
+def _vp_logprob_bwd(h, W, targets, inv_temp, lo, hi, chunk, lse, ent, g_lp, g_ent, need_dw):
+    """Kernel path of the vocabulary-parallel backward: the logit gradient of this rank's slice
+    (csrc/rl_ops.cu logprob_bwd_kernel with the global lse / entropy and slice-relative targets,
+    bf16), then the GEMMs for the partial hidden-state gradient and this slice's LM-head rows."""
+    from miles_b200.ops import gemm as G
+    from miles_b200.ops._lib import lib
+
+    n, H = h.shape
+    Wl = W[lo:hi]
+    V = hi - lo
+    cs = min(chunk, max(n, 1))
+    dh = torch.empty_like(h)
+    dW = torch.zeros(W.shape, dtype=torch.float32, device=h.device) if need_dw else None
+    zbuf = torch.empty(cs, V, dtype=torch.float32, device=h.device)
+    dbuf = torch.empty(cs, V, dtype=torch.bfloat16, device=h.device)
+    tl = (targets - lo).int().contiguous()  # outside the slice: never equal to a slice index
+    g_lp = g_lp.contiguous() if g_lp is not None else None
+    g_ent = g_ent.contiguous() if g_ent is not None else None
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        hs = h[s:e].contiguous()
+        z, d = zbuf[:e - s], dbuf[:e - s]
+        G.matmul_nt(hs, Wl, out=z)
+        lib().logprob_bwd(z, tl[s:e], inv_temp, lse[s:e], None if g_lp is None else g_lp[s:e],
+                          None if g_ent is None else g_ent[s:e], ent[s:e], d)
+        G.matmul_nn(d, Wl, out=dh[s:e])
+        if dW is not None:
+            G.matmul_tn(d, hs, out=dW[lo:hi], accumulate=True)
+    return dh, (dW.to(W.dtype) if dW is not None else None)
 
 
 def vocab_parallel_logprob(h, W, targets, temperature: float, tp: TPContext, chunk: int = 4096):
