@@ -107,7 +107,7 @@ class GatedAttention:
         return reduce_from_tp(self.m._lin(o, name), self.m.tp)
 
     def _sdpa(self, q, k, v, cu):
-        rep = self.m.nq // self.m.nkv
+        rep = q.shape[1] // k.shape[1]  # the heads passed in (a CP head slice may hold one KV head)
         outs = []
         for b in range(len(cu) - 1):
             s, e = cu[b], cu[b + 1]

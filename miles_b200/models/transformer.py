@@ -257,9 +257,11 @@ class Transformer(torch.nn.Module):
             self.cp = CPContext(cp_group)
             if self.cp.size == 1:
                 self.cp = None
-            elif (cfg.num_kv_heads // self.tp_size) % self.cp.size:
-                raise ValueError(f"{cfg.num_kv_heads // self.tp_size} KV heads per TP rank do not "
-                                 f"split over CP {self.cp.size}")
+            else:
+                nq_l, nkv_l, c = cfg.num_heads // self.tp_size, cfg.num_kv_heads // self.tp_size, self.cp.size
+                if nq_l % c or (nkv_l % c and c % nkv_l):
+                    raise ValueError(f"{nq_l} q / {nkv_l} KV heads per TP rank do not split over "
+                                     f"CP {c} (KV heads must split over it or divide it)")
         self.nq = cfg.num_heads // self.tp_size      # this rank's query heads
         self.nkv = cfg.num_kv_heads // self.tp_size  # this rank's KV heads
         self.ep = None
@@ -716,7 +718,7 @@ class Transformer(torch.nn.Module):
     # -------------------------------------------------------------------------------- context parallel
     def _layer_train_cp(self, i, m_prev, r_prev, meta, pos, replay):
         cfg, cp = self.cfg, self.cp
-        from miles_b200.parallel.cp import heads_to_tokens, tokens_to_heads
+        from miles_b200.parallel.cp import heads_to_tokens, kv_tokens_to_heads, tokens_to_heads
 
         ln1 = self.params[f"layers.{i}.input_layernorm.weight"]
         if m_prev is None:
@@ -740,7 +742,7 @@ class Transformer(torch.nn.Module):
             return self._mlp(i, x2, replay=replay), r
         if self.gattn is not None:  # gated attention (Qwen3-Next): same head exchange
             q, k, v, gate = self.gattn._qkv(i, x, pos)
-            qh, kh, vh = tokens_to_heads(q, cp), tokens_to_heads(k, cp), tokens_to_heads(v, cp)
+            qh, kh, vh = tokens_to_heads(q, cp), kv_tokens_to_heads(k, cp), kv_tokens_to_heads(v, cp)
             if self.gattn._native(x):
                 oh = varlen_attention(qh, kh, vh, meta)
             else:
@@ -754,7 +756,7 @@ class Transformer(torch.nn.Module):
         q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
                                self.params.get(pre + "k_norm.weight"), pos,
                                self.rope_cos, self.rope_sin, self.nq, self.nkv, cfg.rms_eps, cfg.qk_norm)
-        o = varlen_attention(tokens_to_heads(q, cp), tokens_to_heads(k, cp), tokens_to_heads(v, cp), meta)
+        o = varlen_attention(tokens_to_heads(q, cp), kv_tokens_to_heads(k, cp), kv_tokens_to_heads(v, cp), meta)
         a = reduce_from_tp(self._lin(heads_to_tokens(o, cp).reshape(x.shape[0], -1), pre + "o_proj.weight"),
                            self.tp)
         x2, r = add_rms_norm(self._sw(i, "post_self_attn_layernorm", a), r,

@@ -9,7 +9,11 @@ second all-to-all turns the output back. The per-head arithmetic is unchanged, s
 is bitwise the forward without CP (and the rollout engine's log-probs stay exact).
 
 The exchange moves 4 x T x heads x D elements per layer in the forward (q, k, v, o), which on
-NVLink is small next to the attention itself; it needs the KV heads to split over c.
+NVLink is small next to the attention itself. With fewer KV heads than ranks (c a multiple of
+the KV-head count, GQA), each KV head is replicated c / nkv times before the exchange, so every
+rank receives the one KV head that its query heads attend to; the forward arithmetic is still
+that of the run without CP, and the backward of the replication sums the replicas' gradients.
+So CP is not capped at the KV-head count (4 KV heads of Qwen3-30B-A3B, CP 8).
 
 Gradients: each rank's parameter gradients cover its own rows, so the optimizer reduces them
 over data-parallel x context-parallel ranks. The per-token log-probs are computed on the rows
@@ -84,6 +88,19 @@ def _heads_to_tokens(x, cp):
     send = x.reshape(c, R, hl, D).contiguous()                        # [c (dest rows), R, hl, D]
     recv = _a2a(send, cp.group)                                       # [c (source heads), R, hl, D]
     return recv.transpose(0, 1).reshape(R, c * hl, D)
+
+
+def kv_tokens_to_heads(x, cp):
+    """tokens_to_heads for K / V: with fewer KV heads than ranks (cp.size a multiple of them),
+    replicate each KV head cp.size / nkv times first, so rank r gets KV head r // (cp.size / nkv),
+    the one its query heads [r * nq / c, (r + 1) * nq / c) use."""
+    nh = x.shape[1]
+    c = cp.size
+    if nh % c == 0:
+        return tokens_to_heads(x, cp)
+    if c % nh:
+        raise ValueError(f"{nh} KV heads neither split over nor divide CP {c}")
+    return tokens_to_heads(x.repeat_interleave(c // nh, dim=1), cp)
 
 
 def tokens_to_heads(x, cp):

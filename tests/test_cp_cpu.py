@@ -75,6 +75,29 @@ def test_cp2_matches_single(tmp_path, name, port):
         assert torch.allclose(g, m.params[n].grad, atol=tol, rtol=1e-3), (n, (g - m.params[n].grad).abs().max())
 
 
+@pytest.mark.parametrize("name", ["tiny", "tiny-gdn"])
+def test_cp4_more_ranks_than_kv_heads(tmp_path, name):
+    """CP 4 over 2 KV heads: each KV head is replicated to the two ranks whose query heads use
+    it; log-probs equal the single-rank ones and the gradients sum to the single-rank ones."""
+    from miles_b200.models.config import preset
+    from miles_b200.models.transformer import Transformer
+
+    cfg = preset(name)
+    assert cfg.num_kv_heads < 4 <= cfg.num_heads
+    m = Transformer(cfg, device="cpu", dtype=torch.float32, seed=3)
+    toks, meta, sel, tgt = _inputs(cfg)
+    lp, ent = m.selected_logprob(toks, meta, sel, tgt, 1.0, 4096)
+    (lp.sum() + 0.1 * ent.sum()).backward()
+    out = str(tmp_path / "cp4.pt")
+    mp.spawn(_run, args=(4, free_port(), name, out), nprocs=4, join=True)
+    r = torch.load(out)
+    assert torch.allclose(r["lp"], lp.detach(), atol=1e-5), (r["lp"] - lp).abs().max()
+    assert torch.allclose(r["ent"], ent.detach(), atol=1e-5)
+    tol = 1e-4 if name == "tiny-gdn" else 1e-5
+    for n, g in r["grads"].items():
+        assert torch.allclose(g, m.params[n].grad, atol=tol, rtol=1e-3), (n, (g - m.params[n].grad).abs().max())
+
+
 @pytest.mark.timeout(600)
 def test_train_cp2(tmp_path):
     import json
