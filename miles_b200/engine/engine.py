@@ -195,7 +195,7 @@ class RolloutEngine:
     def __init__(self, model: Transformer, max_batch: int = 64, num_pages: int | None = None,
                  mem_fraction: float = 0.9, use_cuda_graph: bool = True, max_pages_per_seq: int = 160,
                  steps_per_sync: int = 8, persistent_kv: bool = True, prefill_tokens: int = 32768,
-                 lazy_pages: bool = True):
+                 lazy_pages: bool = True, speculative: str | None = None):
         self.model = model
         self.cfg = model.cfg
         self.dev = model.device
@@ -232,6 +232,20 @@ class RolloutEngine:
         self._arena_pages = 0
         self._num_pages = 0
         self._free_pages: list[int] | None = None
+        # speculative rollout with the model's MTP layer as the draft (engine/speculative.py)
+        self.speculative = None
+        if speculative:
+            self.enable_speculative(speculative)
+
+    def enable_speculative(self, algo: str = "mtp"):
+        """Route `generate` through speculative decoding: "mtp" (aliases "nextn", "eagle") drafts
+        one token per step with the model's first MTP layer and verifies it in one main-model
+        decode pass (engine/speculative.py)."""
+        if str(algo).lower() not in ("mtp", "nextn", "eagle"):
+            raise ValueError(f"unknown speculative algorithm {algo!r}")
+        from miles_b200.engine.speculative import MTPSpeculativeDecoder
+
+        self.speculative = MTPSpeculativeDecoder(self)
 
     # ------------------------------------------------------------------ memory
     def kv_bytes_per_page(self) -> int:
@@ -426,6 +440,12 @@ class RolloutEngine:
             raise RuntimeError("rollout engine is marked dead (recover it first)")
         from miles_b200.utils import dumper
 
+        if self.speculative is not None:
+            if stop_when is not None or callbacks:
+                raise ValueError("speculative decoding returns whole results: no stop_when / "
+                                 "callbacks (partial rollout) on this path")
+            with dumper.phase("inference"):
+                return self.speculative.generate(reqs)
         with dumper.phase("inference"):
             return self._generate(reqs, stop_when, callbacks)
 

@@ -1053,6 +1053,46 @@ class Transformer(torch.nn.Module):
         y, _ = self._add_norm(pend, r, self.params["norm.weight"])
         return y
 
+    @torch.no_grad()
+    def mtp_infer(self, j: int, h: torch.Tensor, next_tokens: torch.Tensor, positions: torch.Tensor,
+                  kc: torch.Tensor, vc: torch.Tensor, slots: torch.Tensor, meta: VarlenMeta | None = None,
+                  page_table: torch.Tensor | None = None, ctx_lens: torch.Tensor | None = None):
+        """Inference form of MTP layer j (the training form is in `mtp_loss`): row t combines the
+        main model's final hidden h[t] (position t) with the embedding of token t + 1, runs layer
+        j with its own paged K/V cache (kc / vc, rows `slots`), and returns (the layer output
+        before the head norm, shared_head.norm of it) — the hidden whose LM-head distribution
+        drafts token t + 2. With `meta` the rows are a packed prefill (varlen attention over the
+        rows themselves); otherwise decode rows attending to the cache through `page_table` /
+        `ctx_lens`. Standard softmax-attention layers only."""
+        cfg = self.cfg
+        p = f"layers.{j}."
+        e = F.embedding(next_tokens.long(), self.params["embed_tokens.weight"])
+        x = torch.cat([rms_norm(e, self.params[p + "enorm.weight"], cfg.rms_eps),
+                       rms_norm(h.to(e.dtype), self.params[p + "hnorm.weight"], cfg.rms_eps)], -1)
+        r = self._lin(x, p + "eh_proj.weight")
+        xn = rms_norm(r, self.params[p + "input_layernorm.weight"], cfg.rms_eps)
+        pre = p + "self_attn."
+        qkv = self._lin(xn, pre + "qkv_proj.weight")
+        T = xn.shape[0]
+        if meta is not None:
+            q, k, v = qk_norm_rope(qkv, self.params.get(pre + "q_norm.weight"),
+                                   self.params.get(pre + "k_norm.weight"), positions,
+                                   self.rope_cos, self.rope_sin, self.nq, self.nkv,
+                                   cfg.rms_eps, cfg.qk_norm)
+            kc.index_copy_(0, slots, k.to(kc.dtype))
+            vc.index_copy_(0, slots, v.to(vc.dtype))
+            o = varlen_attention(q, k, v, meta)
+        else:
+            q = qk_norm_rope_to_cache(qkv, self.params.get(pre + "q_norm.weight"),
+                                      self.params.get(pre + "k_norm.weight"), positions,
+                                      self.rope_cos, self.rope_sin, self.nq, self.nkv, kc, vc,
+                                      slots, cfg.rms_eps, cfg.qk_norm)
+            o = decode_attention(q, kc, vc, page_table, ctx_lens)
+        x2, r = self._add_norm(self._pending_out(o.reshape(T, -1), pre + "o_proj.weight"), r,
+                               self.params[p + "post_attention_layernorm.weight"])
+        y, prev = self._add_norm(self._pending_mlp(j, x2), r, self.params[p + "shared_head.norm.weight"])
+        return prev, y
+
     def flops_per_token(self, ctx: float) -> float:
         """Forward FLOPs per token (matmuls + attention at average context `ctx`)."""
         c = self.cfg

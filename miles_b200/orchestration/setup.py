@@ -345,7 +345,8 @@ def sglang_engine_kwargs(sg: dict) -> dict:
     this engine (SGLang server argument names): mem_fraction_static -> KV pool share,
     max_running_requests -> batch slots, chunked_prefill_size -> packed-prefill token budget,
     disable_cuda_graph -> no decode graphs, context_length -> longest sequence,
-    num_continuous_decode_steps -> decode steps per host visit. Other SGLang flags (kernels,
+    num_continuous_decode_steps -> decode steps per host visit, speculative_algorithm
+    (NEXTN / EAGLE / MTP) -> speculative rollout with the MTP draft. Other SGLang flags (kernels,
     schedulers and servers this engine does not have) are accepted and ignored."""
 
     def flag(v):
@@ -364,6 +365,8 @@ def sglang_engine_kwargs(sg: dict) -> dict:
         out["context_length"] = int(sg["context_length"])
     if "num_continuous_decode_steps" in sg:
         out["steps_per_sync"] = int(sg["num_continuous_decode_steps"])
+    if sg.get("speculative_algorithm"):
+        out["speculative"] = str(sg["speculative_algorithm"]).lower()
     return out
 
 
