@@ -18,8 +18,13 @@ layout-free currency of the HF tensors instead:
      slicing an HF checkpoint load uses) into its flat parameter buffer, and bumps its weight
      version.
 
-Every rank of the job calls `ReshardRefit(...)` (it creates the stage groups) and then
-`update()` with the same arguments. Expert parallelism on the trainer is not handled here.
+Expert-parallel trainers: every (stage, EP rank) has its own source (its TP rank 0; the lowest
+global rank among expert-data-parallel replicas): EP rank 0 sends the dense tensors and its
+experts, the other EP ranks only their experts (global expert ids in the HF names), so every
+expert crosses once. Engines hold every expert (no EP on the engine side).
+
+Every rank of the job calls `ReshardRefit(...)` (it creates the source groups) and then
+`update()` with the same arguments.
 
 Reference: miles/backends/megatron_utils/update_weight/common.py:50-134 (TP all-gather of the
 shards, GLU stride fix, PP / EP broadcasts), hf_weight_iterator_direct.py:19-215 (HF-named
@@ -45,6 +50,14 @@ def _tp_rank(model) -> int:
     return model.tp.rank if getattr(model, "tp", None) is not None else 0
 
 
+def _ep_rank(model) -> int:
+    return model.ep.rank if getattr(model, "ep", None) is not None else 0
+
+
+def _is_expert(name: str) -> bool:
+    return ".mlp.experts." in name
+
+
 class ReshardRefit:
     def __init__(self, train_model, engine_model, trainer_ranks: list[int], engine_ranks: list[int],
                  bucket_bytes: int = 512 << 20, mode: str = "bf16"):
@@ -54,8 +67,8 @@ class ReshardRefit:
         ranks, the same lists on every rank."""
         if mode not in ("bf16", "fp8"):
             raise ValueError(f"unknown refit mode {mode}")
-        if train_model is not None and getattr(train_model, "ep", None) is not None:
-            raise ValueError("resharding refit: expert-parallel trainers are not supported")
+        if engine_model is not None and getattr(engine_model, "ep", None) is not None:
+            raise ValueError("resharding refit: engines hold every expert (no expert parallelism)")
         if engine_model is not None and getattr(engine_model, "pp", None) is not None:
             raise ValueError("resharding refit: engines hold every layer (no pipeline stages)")
         self.train, self.engine, self.mode = train_model, engine_model, mode
@@ -65,17 +78,19 @@ class ReshardRefit:
         self.wire = ref.flat.dtype  # bf16 on GPUs (fp32 in CPU runs)
         self.esize = ref.flat.element_size()
         me = dist.get_rank()
-        # (stage, tp rank) of every trainer rank: each stage's TP rank 0 is its source
-        info = None if train_model is None else (_stage_of(train_model), _tp_rank(train_model))
+        # (stage, EP rank, TP rank) of every trainer rank: each (stage, EP rank)'s TP rank 0 with
+        # the lowest global rank is its source
+        info = None if train_model is None else (_stage_of(train_model), _ep_rank(train_model),
+                                                 _tp_rank(train_model))
         allinfo: list = [None] * dist.get_world_size()
         dist.all_gather_object(allinfo, (me, info))
-        self.leaders: dict[int, int] = {}      # stage -> global rank of its TP rank 0
-        for r, inf in allinfo:
-            if inf is not None and inf[1] == 0 and r in trainer_ranks:
-                self.leaders[inf[0]] = r
+        self.leaders: dict[tuple, int] = {}    # (stage, ep rank) -> global rank of the source
+        for r, inf in sorted(allinfo, key=lambda x: x[0]):
+            if inf is not None and inf[2] == 0 and r in trainer_ranks:
+                self.leaders.setdefault((inf[0], inf[1]), r)
         self.stages = sorted(self.leaders)
-        # one broadcast group per stage: its leader + the engines (created by every rank, in
-        # the same order)
+        # one broadcast group per source: it + the engines (created by every rank, in the same
+        # order)
         self.groups = {s: dist.new_group(sorted({self.leaders[s]} | set(self.engines)))
                        for s in self.stages}
         self.last_stats: dict = {}
@@ -154,7 +169,7 @@ class ReshardRefit:
         ref = self.engine if self.engine is not None else self.train
         dev = ref.flat.device
         sent = 0
-        my_stage = None if self.train is None else _stage_of(self.train)
+        my_stage = None if self.train is None else (_stage_of(self.train), _ep_rank(self.train))
         targets = dict(to_hf_tensors(self.engine)) if self.engine is not None else None
         for s in self.stages:
             leader, grp = self.leaders[s], self.groups[s]
@@ -163,6 +178,8 @@ class ReshardRefit:
                 pending: list[tuple[str, torch.Tensor]] = []
                 size = 0
                 for name, local in to_hf_tensors(self.train):
+                    if s[1] != 0 and not _is_expert(name):
+                        continue  # dense tensors come from EP rank 0 (same on every TP peer)
                     g = tp_gather_for(self.train, name, local.detach())
                     if me != leader:
                         continue

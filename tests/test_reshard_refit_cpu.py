@@ -34,6 +34,8 @@ def _rank(rank, world, port, layout, mode, out):
     if rank in trainers:
         if layout["train"] == "tp2":
             model = Transformer(cfg, seed=3, tp_group=tgrp, **kw)
+        elif layout["train"] == "ep2":
+            model = Transformer(cfg, seed=3, ep_group=tgrp, **kw)
         else:
             model = Transformer(cfg, seed=3, pp_group=tgrp, **kw)
     else:
@@ -65,8 +67,8 @@ def _rank(rank, world, port, layout, mode, out):
     else:
         stage = model.pp.stage if model.pp is not None else 0
         lead = model.tp is None or model.tp.rank == 0
-        if lead:
-            torch.save(full, f"{out}/t{stage}.pt")
+        if lead:  # EP ranks hold different experts: one file each
+            torch.save(full, f"{out}/t{stage}_{rank}.pt")
     dist.barrier()
     dist.destroy_process_group()
 
@@ -74,6 +76,8 @@ def _rank(rank, world, port, layout, mode, out):
 LAYOUTS = {
     "tp2_to_tp1": dict(train="tp2", trainers=[0, 1], engines=[2], engine_tp=1),
     "pp2_to_tp2": dict(train="pp2", trainers=[0, 1], engines=[2, 3], engine_tp=2),
+    # expert-parallel trainer: each EP rank sends its own experts, EP rank 0 the dense tensors
+    "ep2_to_tp2": dict(train="ep2", trainers=[0, 1], engines=[2, 3], engine_tp=2),
     # colocated: the same two ranks hold the trainer (PP2) and the engine (TP2)
     "colocated_pp2_to_tp2": dict(train="pp2", trainers=[0, 1], engines=[0, 1], engine_tp=2,
                                  colocated=True),
@@ -82,6 +86,7 @@ LAYOUTS = {
 
 @pytest.mark.timeout(300)
 @pytest.mark.parametrize("name,mode", [("tp2_to_tp1", "bf16"), ("pp2_to_tp2", "bf16"), ("tp2_to_tp1", "fp8"),
+                                       ("ep2_to_tp2", "bf16"), ("ep2_to_tp2", "fp8"),
                                        ("colocated_pp2_to_tp2", "bf16")])
 def test_reshard_refit(tmp_path, name, mode):
     from miles_b200.ops.quant import fp8_block_dequant, fp8_block_quant
@@ -95,6 +100,11 @@ def test_reshard_refit(tmp_path, name, mode):
             trainer.update(torch.load(tmp_path / f))
     engines = [torch.load(tmp_path / f) for f in os.listdir(tmp_path) if f.startswith("e")]
     assert engines
+    if lay["train"] == "ep2":  # both EP ranks' experts arrived
+        E = 0
+        while any(f".mlp.experts.{E}." in n for n in trainer):
+            E += 1
+        assert all(any(f".mlp.experts.{e}." in n for n in engines[0]) for e in range(E)) and E > 1
     for eng in engines:
         assert set(eng) <= set(trainer) | {"lm_head.weight"}
         for n, t in eng.items():
