@@ -370,8 +370,11 @@ def sglang_engine_kwargs(sg: dict) -> dict:
     return out
 
 
-def build_engine(args, model: Transformer, ctx: ProcessContext) -> RolloutEngine:
-    sg = sglang_engine_kwargs(getattr(args, "sglang_args", {}) or {})
+def build_engine(args, model: Transformer, ctx: ProcessContext,
+                 overrides: dict | None = None) -> RolloutEngine:
+    """The rank's rollout engine; `overrides`: SGLang flags of its `--sglang-config` group,
+    applied over the forwarded `--sglang-*` ones."""
+    sg = sglang_engine_kwargs({**(getattr(args, "sglang_args", {}) or {}), **(overrides or {})})
     max_len = (args.rollout_max_prompt_len or 1024) + (args.rollout_max_response_len or 1024)
     if args.rollout_max_context_len:
         max_len = max(max_len, args.rollout_max_context_len)

@@ -16,8 +16,11 @@ The schema is the reference's, so existing deployment files load unchanged (`eng
 is accepted for `server_groups`). `plan()` turns it into concrete engine instances over the
 rollout ranks: one engine per `num_gpus_per_engine` GPUs, in file order, `placeholder`
 groups reserving GPUs without an engine. Engines here run one GPU each (tensor-parallel
-engines are not built), and prefill / decode groups run as regular engines (every engine
-does both phases), which `plan()` reports.
+engines are not built). `load_deployment` is what the drivers use: one deployed model (the
+actor being trained), each engine's `overrides` applied as forwarded SGLang flags, and under
+train_async.py the prefill / decode groups run disaggregated (`pd_pairs`: the i-th prefill
+engine serves the i-th decode engine's prompts); `plan()` itself still reports prefill /
+decode groups as regular engines for callers that do not pair them.
 
 Reference: miles/backends/sglang_utils/sglang_config.py (ServerGroupConfig :11-36,
 ModelConfig :39-100, SglangConfig.from_yaml / from_prefill_num_servers :103-190).
@@ -148,3 +151,42 @@ class DeploymentConfig:
                     engines.append(EngineInstance(m.name, gi, g.worker_type, [r],
                                                   bool(m.update_weights), dict(g.overrides)))
         return engines, notes
+
+
+def load_deployment(args, rollout_ranks: list[int]) -> tuple[list[EngineInstance], list[str]]:
+    """The `--sglang-config` deployment over `rollout_ranks`, as the drivers run it: exactly one
+    model (the trained actor, refitted), no placeholder groups, GPUs matching the rollout ranks."""
+    dep = DeploymentConfig.from_yaml(args.sglang_config)
+    if len(dep.models) != 1:
+        raise ValueError("--sglang-config: one deployed model (the trained actor) is supported; "
+                         f"got {[m.name for m in dep.models]}")
+    if any(g.worker_type == "placeholder" for g in dep.models[0].server_groups):
+        raise ValueError("--sglang-config: placeholder groups are not supported by the drivers")
+    if dep.total_num_gpus != len(rollout_ranks):
+        raise ValueError(f"--sglang-config uses {dep.total_num_gpus} GPUs, the job has "
+                         f"{len(rollout_ranks)} rollout GPUs")
+    engines, notes = dep.plan(args, rollout_ranks)
+    if dep.models[0].update_weights is False:
+        raise ValueError("--sglang-config: the deployed actor must take weight updates")
+    return engines, notes
+
+
+def overrides_for(engines: list[EngineInstance], rank: int) -> dict:
+    """The SGLang-flag overrides of the engine that runs on `rank` ({} if none)."""
+    for e in engines:
+        if rank in e.ranks:
+            return {k: v for k, v in e.overrides.items() if k != "model_path"}
+    return {}
+
+
+def pd_pairs(engines: list[EngineInstance]) -> tuple[list[int], list[int]] | None:
+    """(prefill ranks, decode ranks), paired by position, or None without prefill / decode
+    groups."""
+    pre = [e.ranks[0] for e in engines if e.worker_type == "prefill"]
+    dec = [e.ranks[0] for e in engines if e.worker_type == "decode"]
+    if not pre and not dec:
+        return None
+    if len(pre) != len(dec):
+        raise ValueError(f"--sglang-config: {len(pre)} prefill and {len(dec)} decode engines; "
+                         "each decode engine needs its own prefill engine")
+    return pre, dec

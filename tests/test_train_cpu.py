@@ -108,6 +108,41 @@ def test_train_async_prefill_decode_disaggregation(tmp_path):
 
 
 @pytest.mark.timeout(600)
+def test_train_async_deployment_yaml_prefill_decode(tmp_path):
+    """--sglang-config with a prefill and a decode group (and engine overrides): the same
+    disaggregated loop as --prefill-num-servers, set up from the deployment file."""
+    (tmp_path / "dep.yaml").write_text(
+        "sglang:\n  - name: actor\n    update_weights: true\n    server_groups:\n"
+        "      - {worker_type: prefill, num_gpus: 1, overrides: {max_running_requests: 16}}\n"
+        "      - {worker_type: decode, num_gpus: 1}\n")
+    r = _async_run(tmp_path, ["--sglang-config", str(tmp_path / "dep.yaml")], free_port(),
+                   rollout_gpus=2)
+    served = [int(line.split("prefilled ")[1].split()[0]) for line in r.stdout.splitlines()
+              if "prefilled" in line]
+    assert len(served) == 3 and all(n > 0 for n in served), r.stdout[-2000:]
+
+
+def test_deployment_helpers(tmp_path):
+    import types
+
+    import pytest as _pt
+
+    from miles_b200.rollout.sglang_config import load_deployment, overrides_for, pd_pairs
+
+    (tmp_path / "a.yaml").write_text(
+        "sglang:\n  - name: actor\n    server_groups:\n"
+        "      - {worker_type: regular, num_gpus: 2, overrides: {mem_fraction_static: 0.5}}\n"
+        "      - {worker_type: prefill, num_gpus: 1}\n      - {worker_type: decode, num_gpus: 1}\n")
+    args = types.SimpleNamespace(sglang_config=str(tmp_path / "a.yaml"), hf_checkpoint=None,
+                                 rollout_num_gpus_per_engine=1)
+    engines, _ = load_deployment(args, [4, 5, 6, 7])
+    assert overrides_for(engines, 5) == {"mem_fraction_static": 0.5} and overrides_for(engines, 6) == {}
+    assert pd_pairs(engines) == ([6], [7])
+    with _pt.raises(ValueError):
+        load_deployment(args, [0, 1, 2])
+
+
+@pytest.mark.timeout(600)
 def test_train_async_fully_async_fp8_refit(tmp_path):
     """Continuous generation worker (partial rollout, staleness filter) and fp8 refits."""
     _async_run(tmp_path, ["--fully-async", "--partial-rollout", "--max-weight-staleness", "4",

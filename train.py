@@ -45,7 +45,16 @@ def setup(args):
     model = build_model(args, ctx)
     actor = build_actor(args, model, ctx)
     engine_model = build_engine_model(args, model, ctx)
-    engine = build_engine(args, engine_model, ctx)
+    overrides = None
+    if getattr(args, "sglang_config", None):
+        from miles_b200.rollout.sglang_config import load_deployment, overrides_for, pd_pairs
+
+        engines, _ = load_deployment(args, list(range(ctx.world)))
+        if pd_pairs(engines) is not None:
+            raise ValueError("--sglang-config prefill / decode groups need disaggregated engines "
+                             "(train_async.py); colocated engines run both phases")
+        overrides = overrides_for(engines, ctx.rank)
+    engine = build_engine(args, engine_model, ctx, overrides)
     tok = load_tokenizer(args)
     client = LocalEngineClient(engine, tok)
     ds_cls = load_function(args.data_source_path)
@@ -76,7 +85,7 @@ def setup(args):
     tracker = Tracker(args, ctx.rank)
     from miles_b200.orchestration.fault_tolerance import EngineSupervisor, default_store
 
-    manager.supervisor = EngineSupervisor(args, engine, lambda: build_engine(args, engine_model, ctx),
+    manager.supervisor = EngineSupervisor(args, engine, lambda: build_engine(args, engine_model, ctx, overrides),
                                           client, ctx.rank, ctx.world, default_store())
     return ctx, model, actor, engine, manager, trainer, tracker, start, data_source
 

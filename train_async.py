@@ -164,6 +164,15 @@ def _pd_roles(args, T: int, R: int):
     prefill, the other R - K decode; decode rank j is paired with prefill rank j (K = R - K).
     Returns (prefill ranks, decode ranks) or None."""
     K = getattr(args, "prefill_num_servers", None) or 0
+    if getattr(args, "sglang_config", None):
+        from miles_b200.rollout.sglang_config import load_deployment, pd_pairs
+
+        if K:
+            raise ValueError("--sglang-config and --prefill-num-servers are exclusive")
+        roles = pd_pairs(load_deployment(args, list(range(T, T + R)))[0])
+        if roles is not None and args.fully_async:
+            raise ValueError("prefill / decode groups are not supported with --fully-async")
+        return roles
     if not K:
         return None
     if 2 * K != R:
@@ -175,13 +184,22 @@ def _pd_roles(args, T: int, R: int):
     return eng[:K], eng[K:]
 
 
+def _overrides(args, ctx, T: int, R: int) -> dict | None:
+    """SGLang-flag overrides of this rank's `--sglang-config` engine group."""
+    if not getattr(args, "sglang_config", None):
+        return None
+    from miles_b200.rollout.sglang_config import load_deployment, overrides_for
+
+    return overrides_for(load_deployment(args, list(range(T, T + R)))[0], ctx.rank)
+
+
 def run_prefill(args, ctx, T, R, refit_group, data_gloo, pre: list[int], dec: list[int]):
     """A prefill rank: per rollout step, prefill the requests of its paired decode rank until it
     ends the step; take part in the refits like every engine rank; contribute no samples."""
     from miles_b200.rollout.pd import serve_prefill_step
 
     model = build_model(args, ctx)
-    engine = build_engine(args, model, ctx)
+    engine = build_engine(args, model, ctx, _overrides(args, ctx, T, R))
     peer = dec[pre.index(ctx.rank)]
     refit = make_refit(model, refit_group, src=0, bucket_bytes=args.update_weight_buffer_size,
                        mode="fp8" if args.update_weight_quant == "fp8" else "bf16",
@@ -207,19 +225,19 @@ def run_engine(args, ctx, T, R, refit_group, data_gloo):
     if roles is not None and ctx.rank in roles[0]:
         return run_prefill(args, ctx, T, R, refit_group, data_gloo, *roles)
     model = build_model(args, ctx)
-    engine = build_engine(args, model, ctx)
+    engine = build_engine(args, model, ctx, _overrides(args, ctx, T, R))
     tok = load_tokenizer(args)
     client = LocalEngineClient(engine, tok)
     ds_cls = load_function(args.data_source_path)
-    if roles is not None:  # a decode rank: its paired prefill rank computes the prompts
+    # sample-producing ranks: every engine rank but the prefill ones
+    producers = [r for r in range(T, T + R) if roles is None or r not in roles[0]]
+    if roles is not None and ctx.rank in roles[1]:  # its paired prefill rank computes the prompts
         from miles_b200.rollout.pd import RemotePrefill
 
         pre, dec = roles
-        j = dec.index(ctx.rank)
-        client.remote_prefill = RemotePrefill(pre[j], ctx.device)
-        manager = RolloutManager(args, ds_cls(args, tok), client, tok, j, len(dec))
-    else:
-        manager = RolloutManager(args, ds_cls(args, tok), client, tok, ctx.rank - T, R)
+        client.remote_prefill = RemotePrefill(pre[dec.index(ctx.rank)], ctx.device)
+    manager = RolloutManager(args, ds_cls(args, tok), client, tok, producers.index(ctx.rank),
+                             len(producers))
     refit = make_refit(model, refit_group, src=0, bucket_bytes=args.update_weight_buffer_size,
                        mode="fp8" if args.update_weight_quant == "fp8" else "bf16",
                        transport=args.update_weight_transport)
