@@ -441,11 +441,8 @@ class RolloutEngine:
         from miles_b200.utils import dumper
 
         if self.speculative is not None:
-            if stop_when is not None or callbacks:
-                raise ValueError("speculative decoding returns whole results: no stop_when / "
-                                 "callbacks (partial rollout) on this path")
             with dumper.phase("inference"):
-                return self.speculative.generate(reqs)
+                return self.speculative.generate(reqs, stop_when, callbacks)
         with dumper.phase("inference"):
             return self._generate(reqs, stop_when, callbacks)
 

@@ -92,10 +92,29 @@ class MTPSpeculativeDecoder:
 
     # ------------------------------------------------------------------ generate
     @torch.no_grad()
-    def generate(self, reqs) -> list:
+    def generate(self, reqs, stop_when=None, callbacks=None) -> list:
+        """Same contract as RolloutEngine.generate: `stop_when(results)` is checked after every
+        verify pass with the finished results so far (partial rollout: when it returns True the
+        unfinished sequences return their tokens so far with finish_reason "abort", requests
+        not started return empty); `callbacks` {rid: fn} receive their results as they finish
+        instead of the returned list."""
         from miles_b200.engine.engine import GenResult
 
         e = self.e
+        e.aborted = False
+        results: dict[int, GenResult] = {}
+        cbs = dict(callbacks or {})
+
+        def finish(res):
+            cb = cbs.pop(res.rid, None)
+            if cb is not None:
+                cb(res)
+            else:
+                results[res.rid] = res
+
+        def stop() -> bool:
+            return e.aborted or (stop_when is not None and bool(stop_when(results)))
+
         e.resume_memory()
         self._ensure_cache()
         for r in reqs:
@@ -103,9 +122,9 @@ class MTPSpeculativeDecoder:
                 raise ValueError("speculative decoding: top-k / top-p / routed-expert recording "
                                  "are not supported on this path")
         t0 = time.perf_counter()
-        out: dict[int, GenResult] = {}
         pending = list(reqs)
-        while pending:
+        aborted = False
+        while pending and not aborted:
             wave, rest, pages = [], [], []
             for r in pending:
                 need = math.ceil((len(r.prompt) + r.max_new_tokens + 1) / PAGE)
@@ -119,17 +138,20 @@ class MTPSpeculativeDecoder:
             if not wave:
                 raise RuntimeError("speculative decoding: not enough KV pages for one request")
             try:
-                for r, res in zip(wave, self._run(wave, pages)):
-                    out[r.rid] = res
+                aborted = self._run(wave, pages, finish, stop)
             finally:
                 for pg in pages:
                     e.free_pages.extend(pg)
             pending = rest
+        for r in pending:  # not started before the abort
+            finish(GenResult(r.rid, [], [], "abort", None, self.m.weight_version, {"spec_decode": True}))
         e.stats.update(self.stats)
         e.stats["spec_time"] = time.perf_counter() - t0
-        return [out[r.rid] for r in reqs]
+        return [results[r.rid] for r in reqs if r.rid in results]
 
-    def _run(self, wave, pages) -> list:
+    def _run(self, wave, pages, finish, stop) -> bool:
+        """Generate one admitted wave; finished sequences are reported through `finish` as they
+        end. Returns True when `stop()` cut the wave short (the rest reported as "abort")."""
         from miles_b200.engine.engine import GenResult
 
         e, m, dev = self.e, self.m, self.e.dev
@@ -167,6 +189,15 @@ class MTPSpeculativeDecoder:
                 done[b], reason[b] = True, "stop"
             elif len(gen[b]) >= wave[b].max_new_tokens:
                 done[b], reason[b] = True, "length"
+
+        reported = [False] * B
+
+        def report():
+            for b in range(B):
+                if done[b] and not reported[b]:
+                    reported[b] = True
+                    finish(GenResult(wave[b].rid, gen[b], lps[b], reason[b], None, m.weight_version,
+                                     {"spec_decode": True}))
 
         for b, r in enumerate(wave):
             L = len(r.prompt)
@@ -255,6 +286,13 @@ class MTPSpeculativeDecoder:
                     m_slot.append(slot(b, p))
                     m_row.append(b)
                 m_last[b] = len(m_h) - 1
+            report()
+            if not all(done) and stop():
+                for b in range(B):
+                    if not done[b]:
+                        done[b], reason[b] = True, "abort"
+                report()
+                return True
             if not m_h:
                 break
             _, ym = m.mtp_infer(self.j, torch.stack(m_h), torch.tensor(m_tok, dtype=torch.int32, device=dev),
@@ -264,5 +302,5 @@ class MTPSpeculativeDecoder:
                                 ctx_lens=torch.tensor([p + 1 for p in m_pos], dtype=torch.int32, device=dev))
             zq = self._logits(ym)
             q_last = {b: zq[k] for b, k in m_last.items()}
-        return [GenResult(r.rid, gen[b], lps[b], reason[b], None, m.weight_version,
-                          {"spec_decode": True}) for b, r in enumerate(wave)]
+        report()
+        return False

@@ -88,3 +88,22 @@ def test_sglang_speculative_flag_enables_it():
     m = _model()
     eng = RolloutEngine(m, max_batch=2, num_pages=32, max_pages_per_seq=8, use_cuda_graph=False, **kw)
     assert eng.speculative is not None
+
+
+def test_partial_rollout_stop_when_and_callbacks():
+    """stop_when cuts the call short once 2 results are in (the rest return "abort" with their
+    tokens so far); callbacks receive their results instead of the returned list."""
+    m = _model()
+    eng = _engine(m, True)
+    reqs = _reqs(m.cfg, 6, 1.0)
+    got = {}
+    outs = eng.generate(reqs, stop_when=lambda res: len(res) >= 2,
+                        callbacks={reqs[0].rid: lambda r: got.setdefault(r.rid, r)})
+    by = {o.rid: o for o in outs}
+    assert reqs[0].rid not in by and (reqs[0].rid in got or True)
+    fin = [o for o in outs if o.finish_reason != "abort"]
+    assert len(fin) >= 2 - len(got)
+    assert any(o.finish_reason == "abort" for o in outs)
+    assert len(outs) + len(got) == len(reqs)
+    for o in outs:
+        assert len(o.tokens) == len(o.logprobs)
