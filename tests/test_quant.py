@@ -22,6 +22,18 @@ def test_refs_roundtrip_cpu():
     assert (Q.mxfp8_dequant(y, e, torch.float32) - w[:, :512]).abs().max() / w.abs().max() < 0.07
 
 
+def test_int4_all_zero_group_pinned_cpu():
+    """The int4 fake quantiser's scale floor (1e-8) on an all-zero group: codes 0, zero-point 0,
+    scale 1e-8, in both modes, so the group dequantises to exact zeros."""
+    w = torch.randn(2, 256)
+    w[0, :128] = 0
+    for sym in (True, False):
+        q, s, z = Q.int4_fake_quant_ref(w, 128, sym)
+        assert torch.all(q[0, :128] == (0 if sym else z[0, 0]))
+        assert float(s[0, 0]) == pytest.approx(1e-8) and float(z[0, 0]) == 0.0
+        assert torch.all(Q.int4_dequant(q, s, z, 128, sym)[0, :128] == 0)
+
+
 @pytest.mark.gpu
 def test_kernels_match_refs():
     torch.manual_seed(1)
