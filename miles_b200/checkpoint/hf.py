@@ -238,6 +238,8 @@ def hf_config_dict(cfg: ModelConfig) -> dict:
 
 def save_hf(model: Transformer, path: str, max_shard_bytes: int = 5 << 30) -> None:
     os.makedirs(path, exist_ok=True)
+    if hasattr(model, "_sync_fp32"):  # fp32-pinned copies take the latest update first
+        model._sync_fp32()
     with open(os.path.join(path, "config.json"), "w") as f:
         json.dump(hf_config_dict(model.cfg), f, indent=2)
     shard, size, idx, weight_map = {}, 0, 0, {}
