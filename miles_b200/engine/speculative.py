@@ -102,6 +102,7 @@ class MTPSpeculativeDecoder:
 
         e = self.e
         e.aborted = False
+        self.stats = {"spec_steps": 0, "spec_drafts": 0, "spec_accepted": 0}  # this call's
         results: dict[int, GenResult] = {}
         cbs = dict(callbacks or {})
 

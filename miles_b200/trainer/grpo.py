@@ -202,6 +202,9 @@ class ColocatedRL:
             "rollout/buffered_groups": len(self.buffer),
             "rollout/decode_steps": self.engine.stats.get("decode_steps", 0),
             "rollout/preemptions": self.engine.stats.get("preemptions", 0),
+            # speculative rollout (MTP draft): accepted drafts / drafts of the step's generate
+            "rollout/spec_accept_rate": (self.engine.stats.get("spec_accepted", 0)
+                                         / max(self.engine.stats.get("spec_drafts", 0), 1)),
             "perf/actor_train_tok_per_s": n_tok / max(t_train - t_lp, 1e-9),
             "perf/actor_train_tflops": train_tflops(self.actor.model.cfg, [len(s.tokens) for s in samples],
                                                     t_train - t_lp),

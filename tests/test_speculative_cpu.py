@@ -52,7 +52,7 @@ def test_oracle_drafts_all_accepted():
     out = {o.rid: o.tokens for o in eng.generate(_reqs(m.cfg, 5, 0.0))}
     assert out == ref
     st = eng.stats
-    assert st["spec_accepted"] == st["spec_drafts"]
+    assert st["spec_accepted"] == st["spec_drafts"] > 0
     total = sum(len(t) for t in ref.values())
     assert st["spec_steps"] < 0.6 * total  # about two tokens per verify pass
 
